@@ -1,0 +1,157 @@
+/* om_cuda.h -- B200 (sm_100a) mixture-of-experts block, C ABI.
+ *
+ * This is the device-side replacement for the MoE layer of the overhang C
+ * engines.  Routing, token->expert dispatch, the int8-dequant expert SwiGLU
+ * products and the weighted combine all run on the GPU; the caller hands in
+ * the post-norm activations x[T,D] and receives out[T,D].
+ *
+ * Reference interfaces this header replaces:
+ *   - moe()       engines/olmoe.c:344-402  (router + top-k + experts + combine)
+ *   - moe_step()  engines/qwen.c:453-495   (shared expert + router + experts)
+ *   - the GPU seam metal/om_metal.h:14-46 (omm_*), whose prototypes are
+ *     mirrored one-for-one by om_metal.h in this directory.
+ *
+ * Conventions
+ *   - Plain C types only: pointers, sizes, ints.  No CUDA or torch types.
+ *   - Every entry point returns an OMC_* status (0 = OK, < 0 = error); there
+ *     is no CPU fallback.  omc_strerror() names a status; omc_last_error()
+ *     returns the detail string of the last failure on this thread.
+ *   - One process drives one GPU (omc_init(device, ...)); expert parallelism
+ *     across GPUs is joined with omc_ep_init().
+ *   - Calls are made from one host thread, as the engines do
+ *     (engines/olmoe.c:405-427).
+ */
+#ifndef OM_CUDA_H
+#define OM_CUDA_H
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ---------------------------------------------------- */
+#define OMC_OK          0
+#define OMC_EINVAL     -1   /* bad argument / descriptor / shape          */
+#define OMC_ENOMEM     -2   /* device, pinned or slab allocation failed   */
+#define OMC_ENOINIT    -3   /* omc_init / omc_layer_init not called        */
+#define OMC_ECUDA      -4   /* CUDA runtime error                          */
+#define OMC_EDEVICE    -5   /* a kernel reported an error (bounds, wait)   */
+#define OMC_ETIMEOUT   -6   /* a bounded wait expired (device or NCCL)     */
+#define OMC_ENCCL      -7   /* NCCL error or NCCL unavailable              */
+#define OMC_EUNSUPPORTED -8 /* valid request this build does not handle    */
+
+/* ---- layer descriptor ------------------------------------------------ */
+/* Model family fixes the reference's arithmetic: the router's softmax sum
+ * precision, the SwiGLU form and the combine order.
+ *   OLMOE: softmax_row float sum (engines/olmoe.c:170-174), silu as
+ *          g/(1+exp(-g)) (olmoe.c:393), out = sum_k w_k*y_k (olmoe.c:395-397)
+ *   QWEN : softmax_ double sum (engines/qwen.c:161-165), silu as
+ *          g*sigmoid(g) (qwen.c:158-159), renormalised top-k, out =
+ *          sigmoid(sh_gate.x)*shared(x) + sum_k w_k*y_k (qwen.c:455-492) */
+#define OMC_FAMILY_OLMOE 0
+#define OMC_FAMILY_QWEN  1
+
+#define OMC_ROUTER_F32 0    /* router weights f32 [E,D]                       */
+#define OMC_ROUTER_I8  1    /* int8 [E,D] + f32 scale [E] (qwen.c:284 stream)  */
+
+typedef struct omc_moe_desc {
+    int family;        /* OMC_FAMILY_*                                          */
+    int D;             /* hidden size (multiple of 64)                          */
+    int I;             /* routed-expert FFN width (multiple of 64)              */
+    int E;             /* routed experts (<= 1024)                              */
+    int k;             /* experts per token (<= 32)                             */
+    int renorm;        /* 1: top-k weights divided by their sum (forced for QWEN) */
+    int router_dtype;  /* OMC_ROUTER_*                                          */
+    int has_shared;    /* 1: always-on shared expert behind a sigmoid gate (QWEN) */
+    int Is;            /* shared-expert FFN width (multiple of 64)               */
+} omc_moe_desc;
+
+/* ---- lifetime ------------------------------------------------------- */
+
+/* Bind this process to CUDA `device` and reserve the HBM expert slab.
+ * slab_bytes = 0: use free HBM minus a 4 GiB reserve.  Replaces omm_init
+ * (metal/om_metal.h:13-14). */
+int omc_init(int device, size_t slab_bytes);
+
+/* Free every device and pinned resource (and the NCCL communicator). */
+void omc_shutdown(void);
+
+/* Describe layer `layer` and upload its router.  router_w is f32 [E,D] or
+ * int8 [E,D] with router_s f32 [E].  Replaces the router weights the engines
+ * keep resident (engines/olmoe.c:226, engines/qwen.c:278,284). */
+int omc_layer_init(int layer, const omc_moe_desc *desc,
+                   const void *router_w, const float *router_s);
+
+/* Upload routed expert e of a layer into the HBM slab (re-tiled for the
+ * kernels).  Row-major int8 container tensors as written by the converters
+ * (tools/convert_olmoe.py:93-99): g,u [I,D], d [D,I], per-row f32 scales
+ * gs,us [I], ds [D].  Replaces expert_get's disk fill
+ * (engines/olmoe.c:250-272, engines/qwen.c:428-450). */
+int omc_expert_set(int layer, int e,
+                   const int8_t *g, const float *gs, const int8_t *u, const float *us,
+                   const int8_t *d, const float *ds);
+
+/* The same for all E experts at once from expert-major packed arrays:
+ * g,u [E,I,D], d [E,D,I], gs,us [E,I], ds [E,D]. */
+int omc_experts_set_packed(int layer,
+                           const int8_t *g, const float *gs, const int8_t *u, const float *us,
+                           const int8_t *d, const float *ds);
+
+/* QWEN shared expert: g,u int8 [Is,D], d int8 [D,Is], their row scales, and
+ * the f32 gate vector sh_gate [D] (engines/qwen.c:279-287). */
+int omc_shared_set(int layer,
+                   const int8_t *g, const float *gs, const int8_t *u, const float *us,
+                   const int8_t *d, const float *ds, const float *sh_gate);
+
+/* ---- forward -------------------------------------------------------- */
+
+/* out[T,D] = MoE_layer(x[T,D]) with HOST pointers (blocking).  topk_idx and
+ * topk_w (nullable, [T,k]) receive the routing in selection order.
+ * Drop-in for moe(m, l, layer, x, S, out) (engines/olmoe.c:344). */
+int omc_moe_forward(int layer, const float *x, int T, float *out,
+                    int32_t *topk_idx, float *topk_w);
+
+/* The same with DEVICE pointers, enqueued on `stream` (a cudaStream_t; NULL
+ * = the library's stream).  Returns once enqueued; the caller synchronises. */
+int omc_moe_forward_dev(int layer, const float *x, int T, float *out,
+                        int32_t *topk_idx, float *topk_w, void *stream);
+
+/* Wait for all work of the library; reports a pending device error. */
+int omc_sync(void);
+
+/* ---- expert parallelism (1 process per GPU) ------------------------- */
+
+/* Join an expert-parallel group of `world` ranks.  unique_id is the 128-byte
+ * ncclUniqueId made by rank 0 and shared by the caller.  Layers initialised
+ * afterwards keep only experts [rank*E/world, (rank+1)*E/world) in the slab;
+ * omc_moe_forward[_dev] then routes the caller's tokens, dispatches them to
+ * their experts' ranks and combines the results (NCCL over NVLink). */
+int omc_ep_init(int rank, int world, const void *unique_id);
+
+/* Write a fresh 128-byte ncclUniqueId into buf (rank 0 only). */
+int omc_ep_unique_id(void *buf, size_t len);
+
+/* ---- introspection -------------------------------------------------- */
+
+const char *omc_strerror(int status);
+const char *omc_last_error(void);
+
+/* Per-stage device time of the last forward (milliseconds, CUDA events on
+ * the launching stream) when profiling is on: stages are router, dispatch,
+ * expert gate/up, expert down, combine, exchange.  Returns the number of
+ * stages written. */
+int omc_set_profiling(int on);
+int omc_stage_times(float *ms, int n);
+
+/* Number of kernels the library launched since the last reset (a count of
+ * its own launches, not of library calls it makes). */
+long long omc_launch_count(int reset);
+
+/* Build and version string. */
+const char *omc_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

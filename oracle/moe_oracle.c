@@ -1,0 +1,248 @@
+/* moe_oracle.c -- CPU oracle for the overhang MoE block (TEST INFRASTRUCTURE
+ * ONLY; see moe_oracle.h).  Every function below restates a reference
+ * function operation for operation; the citation is on each one.
+ *
+ * Build: gcc -O3 -fPIC -ffp-contract=off (no -ffast-math, no -march): the
+ * same x86-64 SSE2 scalar arithmetic the reference engines get from
+ * `gcc -O3 -fopenmp` (Makefile:5-11 with gcc in place of clang).
+ */
+#include "moe_oracle.h"
+
+#include <math.h>
+#include <stdlib.h>
+#include <string.h>
+
+/* ---- reference arithmetic kernels ------------------------------------ */
+
+/* engines/olmoe.c:74-85 (matmul) and engines/qwen.c:70-77 (matvec):
+ * y[o] = sum_i x[i]*W[o,i], one sequential fp32 chain per output. */
+static void ref_matvec_f32(float *y, const float *x, const float *W, int I, int O) {
+    for (int o = 0; o < O; o++) {
+        const float *w = W + (int64_t)o * I;
+        float acc = 0.f;
+        for (int i = 0; i < I; i++) acc += x[i] * w[i];
+        y[o] = acc;
+    }
+}
+
+/* engines/olmoe.c:134-140, engines/qwen.c:116-121 (x86 scalar matmul_q):
+ * y[o] = (sum_i x[i]*(float)q[o,i]) * scale[o]. */
+static void ref_matmul_q(float *y, const float *x, const int8_t *q, const float *scale, int I, int O) {
+    for (int o = 0; o < O; o++) {
+        const int8_t *w = q + (int64_t)o * I;
+        float acc = 0.f;
+        for (int i = 0; i < I; i++) acc += x[i] * (float)w[i];
+        y[o] = acc * scale[o];
+    }
+}
+
+/* engines/olmoe.c:170-174 softmax_row: float running sum. */
+static void ref_softmax_f32sum(float *x, int n) {
+    float m = -1e30f;
+    for (int i = 0; i < n; i++) if (x[i] > m) m = x[i];
+    float s = 0;
+    for (int i = 0; i < n; i++) { x[i] = expf(x[i] - m); s += x[i]; }
+    for (int i = 0; i < n; i++) x[i] /= s;
+}
+
+/* engines/qwen.c:161-165 softmax_: double running sum, divide by (float)sum. */
+static void ref_softmax_f64sum(float *x, int n) {
+    float m = -1e30f;
+    for (int i = 0; i < n; i++) if (x[i] > m) m = x[i];
+    double s = 0;
+    for (int i = 0; i < n; i++) { x[i] = expf(x[i] - m); s += x[i]; }
+    for (int i = 0; i < n; i++) x[i] /= (float)s;
+}
+
+/* engines/olmoe.c:355-362, engines/qwen.c:468-475: k passes of argmax over the
+ * probabilities with strict '>' from bv=-1e30 and taken ids skipped, so an
+ * equal probability keeps the lower expert id. */
+static void ref_topk(const float *pr, int E, int K, int *idx, float *val) {
+    for (int kk = 0; kk < K; kk++) {
+        int best = -1; float bv = -1e30f;
+        for (int e = 0; e < E; e++) {
+            int taken = 0;
+            for (int j = 0; j < kk; j++) if (idx[j] == e) { taken = 1; break; }
+            if (!taken && pr[e] > bv) { bv = pr[e]; best = e; }
+        }
+        idx[kk] = best; val[kk] = bv;
+    }
+}
+
+/* engines/olmoe.c:363 and engines/qwen.c:476-477: float sum, then divide. */
+static void ref_renorm(float *val, int K) {
+    float sm = 0;
+    for (int kk = 0; kk < K; kk++) sm += val[kk];
+    for (int kk = 0; kk < K; kk++) val[kk] /= sm;
+}
+
+/* engines/qwen.c:158-159 */
+static float ref_sigmoidf(float z) { return 1.f / (1.f + expf(-z)); }
+static float ref_siluf(float z) { return z * ref_sigmoidf(z); }
+
+/* ---- routing ------------------------------------------------------- */
+
+static int desc_ok(const orc_desc *d) {
+    if (!d || d->D <= 0 || d->I <= 0 || d->E <= 0 || d->k <= 0 || d->k > d->E || d->k > 64) return 0;
+    if (d->family != ORC_FAMILY_OLMOE && d->family != ORC_FAMILY_QWEN) return 0;
+    if (d->has_shared && (d->family != ORC_FAMILY_QWEN || d->Is <= 0)) return 0;
+    return 1;
+}
+
+/* Routes one token: logits -> softmax -> top-k -> renorm.
+ * olmoe: engines/olmoe.c:347 (logits), :351-364 (softmax_row, top-k, renorm)
+ * qwen : engines/qwen.c:465-477 (DM router, softmax_, top-k, renorm) */
+static void route_one(const orc_desc *d, const orc_weights *w, const float *xs, float *pr,
+                      int *idx, float *val) {
+    if (d->router_i8) ref_matmul_q(pr, xs, (const int8_t *)w->router, w->router_s, d->D, d->E);
+    else              ref_matvec_f32(pr, xs, (const float *)w->router, d->D, d->E);
+    if (d->family == ORC_FAMILY_QWEN) ref_softmax_f64sum(pr, d->E);
+    else                              ref_softmax_f32sum(pr, d->E);
+    ref_topk(pr, d->E, d->k, idx, val);
+    if (d->family == ORC_FAMILY_QWEN || d->renorm) ref_renorm(val, d->k);
+}
+
+int orc_route(const orc_desc *d, const orc_weights *w, const float *x, int T,
+              int32_t *topk_idx, float *topk_w) {
+    if (!desc_ok(d) || T < 0) return -1;
+    #pragma omp parallel
+    {
+        float *pr = malloc(sizeof(float) * d->E);
+        int idx[64]; float val[64];
+        #pragma omp for schedule(static)
+        for (int s = 0; s < T; s++) {
+            route_one(d, w, x + (int64_t)s * d->D, pr, idx, val);
+            for (int kk = 0; kk < d->k; kk++) {
+                if (topk_idx) topk_idx[(int64_t)s * d->k + kk] = idx[kk];
+                if (topk_w)   topk_w[(int64_t)s * d->k + kk] = val[kk];
+            }
+        }
+        free(pr);
+    }
+    return 0;
+}
+
+/* ---- the block ------------------------------------------------------ */
+
+/* Tokens are independent in the reference (every buffer below is per token),
+ * so they are spread over OpenMP threads; each token's arithmetic is the
+ * reference's, in the reference's order. */
+int orc_moe(const orc_desc *d, const orc_weights *w, const float *x, int T,
+            float *out, int32_t *topk_idx, float *topk_w) {
+    if (!desc_ok(d) || T < 0) return -1;
+    const int D = d->D, I = d->I, E = d->E, K = d->k;
+    const int Wmax = (d->has_shared && d->Is > I) ? d->Is : I;
+    #pragma omp parallel
+    {
+        float *pr = malloc(sizeof(float) * E);
+        float *g = malloc(sizeof(float) * Wmax), *u = malloc(sizeof(float) * Wmax);
+        float *hh = malloc(sizeof(float) * D);
+        int idx[64]; float val[64];
+        #pragma omp for schedule(dynamic, 1)
+        for (int s = 0; s < T; s++) {
+            const float *xs = x + (int64_t)s * D;
+            float *os = out + (int64_t)s * D;
+            if (d->family == ORC_FAMILY_QWEN && d->has_shared) {
+                /* engines/qwen.c:455-462: shared expert, then x sigmoid gate */
+                const int SI = d->Is;
+                ref_matmul_q(g, xs, w->sh_g, w->sh_gs, D, SI);
+                ref_matmul_q(u, xs, w->sh_u, w->sh_us, D, SI);
+                for (int i = 0; i < SI; i++) g[i] = ref_siluf(g[i]) * u[i];
+                ref_matmul_q(os, g, w->sh_d, w->sh_ds, SI, D);
+                float sg = 0;
+                for (int i = 0; i < D; i++) sg += w->sh_gate[i] * xs[i];
+                sg = ref_sigmoidf(sg);
+                for (int i = 0; i < D; i++) os[i] *= sg;
+            } else {
+                memset(os, 0, sizeof(float) * D);        /* engines/olmoe.c:348 */
+            }
+            route_one(d, w, xs, pr, idx, val);
+            for (int kk = 0; kk < K; kk++) {
+                const int e = idx[kk];
+                const int8_t *qg = w->g + (int64_t)e * I * D, *qu = w->u + (int64_t)e * I * D;
+                const int8_t *qd = w->d + (int64_t)e * D * I;
+                ref_matmul_q(g, xs, qg, w->gs + (int64_t)e * I, D, I);
+                ref_matmul_q(u, xs, qu, w->us + (int64_t)e * I, D, I);
+                if (d->family == ORC_FAMILY_QWEN) {
+                    for (int i = 0; i < I; i++) g[i] = ref_siluf(g[i]) * u[i];          /* qwen.c:485 */
+                } else {
+                    for (int i = 0; i < I; i++) { float gv = g[i]; g[i] = (gv / (1.f + expf(-gv))) * u[i]; } /* olmoe.c:393 */
+                }
+                ref_matmul_q(hh, g, qd, w->ds + (int64_t)e * D, I, D);
+                const float wk = val[kk];
+                for (int i = 0; i < D; i++) os[i] += wk * hh[i];   /* olmoe.c:395-397, qwen.c:492 */
+                if (topk_idx) topk_idx[(int64_t)s * K + kk] = e;
+                if (topk_w)   topk_w[(int64_t)s * K + kk] = wk;
+            }
+        }
+        free(pr); free(g); free(u); free(hh);
+    }
+    return 0;
+}
+
+/* ---- quantisers and inputs ----------------------------------------- */
+
+/* tools/convert_olmoe.py:32-38 (same rule in convert_qwen.py / convert_gemma.py) */
+void orc_quantize_rows_py(const float *w, int O, int I, int8_t *q, float *s) {
+    for (int o = 0; o < O; o++) {
+        const float *wr = w + (int64_t)o * I;
+        float amax = 0.f;
+        for (int i = 0; i < I; i++) { float a = fabsf(wr[i]); if (a > amax) amax = a; }
+        if (amax < 1e-12f) amax = 1e-12f;
+        const float sc = amax / 127.0f;
+        s[o] = sc;
+        for (int i = 0; i < I; i++) {
+            float v = nearbyintf(wr[i] / sc);              /* torch.round: half to even */
+            if (v > 127.f) v = 127.f;
+            if (v < -128.f) v = -128.f;
+            q[(int64_t)o * I + i] = (int8_t)v;
+        }
+    }
+}
+
+/* engines/qwen.c:124-138 */
+void orc_quantize_rows_c(const float *w, int O, int I, int8_t *q, float *s) {
+    for (int o = 0; o < O; o++) {
+        const float *wr = w + (int64_t)o * I;
+        float am = 0.f;
+        for (int i = 0; i < I; i++) { float a = fabsf(wr[i]); if (a > am) am = a; }
+        float sc = am / 127.f;
+        if (sc < 1e-8f) sc = 1e-8f;
+        s[o] = sc;
+        for (int i = 0; i < I; i++) {
+            int v = (int)lrintf(wr[i] / sc);
+            if (v > 127) v = 127;
+            if (v < -128) v = -128;
+            q[(int64_t)o * I + i] = (int8_t)v;
+        }
+    }
+}
+
+static uint64_t splitmix64(uint64_t *st) {
+    uint64_t z = (*st += 0x9E3779B97F4A7C15ULL);
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ULL;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBULL;
+    return z ^ (z >> 31);
+}
+
+/* Blocks of 65536 values, each block seeded from (seed, block index), so the
+ * stream is the same whatever the thread count. */
+void orc_fill_normal(uint64_t seed, float *dst, int64_t n, float sigma) {
+    const int64_t BLK = 65536;
+    const int64_t nb = (n + BLK - 1) / BLK;
+    #pragma omp parallel for schedule(static)
+    for (int64_t b = 0; b < nb; b++) {
+        uint64_t st = seed ^ (0xD1B54A32D192ED03ULL * (uint64_t)(b + 1));
+        splitmix64(&st);
+        const int64_t lo = b * BLK, hi = (lo + BLK < n) ? lo + BLK : n;
+        for (int64_t i = lo; i < hi; i += 2) {
+            double u1 = ((splitmix64(&st) >> 11) + 1.0) * 0x1.0p-53;   /* (0,1] */
+            double u2 = (splitmix64(&st) >> 11) * 0x1.0p-53;
+            double r = sqrt(-2.0 * log(u1)), th = 6.283185307179586 * u2;
+            dst[i] = (float)(sigma * r * cos(th));
+            if (i + 1 < hi) dst[i + 1] = (float)(sigma * r * sin(th));
+        }
+    }
+}
+
+float orc_expf(float x) { return expf(x); }

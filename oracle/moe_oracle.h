@@ -1,0 +1,82 @@
+/* moe_oracle.h -- CPU oracle for the overhang MoE block.
+ *
+ * TEST INFRASTRUCTURE ONLY.  Only tests/, __graft_entry__.smoke() and the
+ * cpu_baseline leg of bench.py may load this code, and only as the checker.
+ * The product (libomc.so) never links, loads or calls it.
+ *
+ * It restates, operation for operation, the reference C engines' MoE math:
+ *   - OLMoE  moe()       engines/olmoe.c:344-402
+ *   - Qwen   moe_step()  engines/qwen.c:453-495   (stream mode: int8 router,
+ *                                                  int8 shared expert)
+ * in the same floating-point order (sequential fp32 sums, no FMA
+ * contraction, glibc expf), so that on identical inputs its outputs are
+ * bit-identical to the reference built with gcc -O3 on x86-64.  That
+ * bit-identity is checked against the reference itself (oracle/_ref) and
+ * against golden vectors generated from it (tests/golden/).
+ */
+#ifndef MOE_ORACLE_H
+#define MOE_ORACLE_H
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Model family: fixes the reference's arithmetic for routing, the SwiGLU
+ * form and the combine order.  Same values as OMC_FAMILY_* in om_cuda.h. */
+enum { ORC_FAMILY_OLMOE = 0, ORC_FAMILY_QWEN = 1 };
+
+typedef struct {
+    int family;        /* ORC_FAMILY_* */
+    int D, I, E, k;    /* hidden, expert FFN width, experts, top-k */
+    int renorm;        /* olmoe: config norm_topk_prob (olmoe.c:194,363); qwen: always 1 (qwen.c:476-477) */
+    int router_i8;     /* 0: f32 router [E,D] (olmoe.c:74-85); 1: int8 [E,D] + f32 scale[E] (qwen.c:284,465) */
+    int has_shared;    /* qwen shared expert (qwen.c:455-462) */
+    int Is;            /* shared expert FFN width */
+} orc_desc;
+
+/* Expert weights, packed expert-major (the int8 container layout of
+ * tools/convert_olmoe.py:32-38 per expert, concatenated):
+ *   g, u : int8 [E][I][D]   gs, us : f32 [E][I]
+ *   d    : int8 [E][D][I]   ds     : f32 [E][D]
+ * Shared expert (qwen): sh_g, sh_u int8 [Is][D], sh_d int8 [D][Is], their
+ * f32 row scales, and sh_gate f32 [D] (kept f32 by qwen.c:282,460). */
+typedef struct {
+    const void   *router;   const float *router_s;
+    const int8_t *g, *u, *d;
+    const float  *gs, *us, *ds;
+    const int8_t *sh_g, *sh_u, *sh_d;
+    const float  *sh_gs, *sh_us, *sh_ds, *sh_gate;
+} orc_weights;
+
+/* out[T,D] = MoE(x[T,D]).  topk_idx/topk_w [T,k] (nullable) receive the
+ * routing in selection order.  Returns 0, or -1 on a bad descriptor. */
+int orc_moe(const orc_desc *dsc, const orc_weights *w, const float *x, int T,
+            float *out, int32_t *topk_idx, float *topk_w);
+
+/* Routing only (router GEMV + softmax + top-k + optional renorm), same rules. */
+int orc_route(const orc_desc *dsc, const orc_weights *w, const float *x, int T,
+              int32_t *topk_idx, float *topk_w);
+
+/* Per-row symmetric int8 quantiser of the container converters
+ * (tools/convert_olmoe.py:32-38): s = max(amax,1e-12)/127,
+ * q = clamp(round_half_even(w/s), -128, 127). */
+void orc_quantize_rows_py(const float *w, int O, int I, int8_t *q, float *s);
+
+/* The engines' load-time quantiser (qwen.c:124-138, olmoe.c:145-161 with
+ * bits=8): s = max(amax/127, 1e-8), q = clamp(lrintf(w/s), -128, 127).
+ * qwen.c uses it for the router and the shared expert in stream mode. */
+void orc_quantize_rows_c(const float *w, int O, int I, int8_t *q, float *s);
+
+/* SplitMix64 + Box-Muller generator shared by tests and bench so that CPU
+ * and GPU legs see identical seeded inputs.  fills n floats ~ N(0, sigma). */
+void orc_fill_normal(uint64_t seed, float *dst, int64_t n, float sigma);
+
+/* glibc expf as called by the reference (exposed so tests can compare the
+ * device restatement of the same function against it). */
+float orc_expf(float x);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,234 @@
+"""ctypes access to the CPU oracle (TEST INFRASTRUCTURE ONLY).
+
+Only tests/, ``__graft_entry__.smoke()`` and the cpu_baseline / reference leg
+of ``bench.py`` import this module, and only as the checker or the timed CPU
+baseline.  The product library (``overhang_b200/libomc.so``) never loads it.
+
+Two checkers live here:
+
+* ``liboracle.so``: the C restatement in ``moe_oracle.c`` (always built);
+* ``_ref/libref_olmoe.so`` / ``_ref/libref_qwen.so``: the reference engines'
+  own ``moe()`` (engines/olmoe.c:344-402) and ``moe_step()``
+  (engines/qwen.c:453-495), compiled from the reference sources by
+  ``oracle/Makefile`` (present wherever they were built and shipped).
+
+It also generates the seeded synthetic layers used by tests and bench: weights
+N(0, 0.02) through the converters' per-row int8 rule
+(tools/convert_olmoe.py:32-38), activations N(0, 1).
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+from dataclasses import dataclass, field
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+FAMILY_OLMOE, FAMILY_QWEN = 0, 1
+
+_f32p = np.ctypeslib.ndpointer(np.float32, flags="C_CONTIGUOUS")
+_i8p = np.ctypeslib.ndpointer(np.int8, flags="C_CONTIGUOUS")
+_i32p = np.ctypeslib.ndpointer(np.int32, flags="C_CONTIGUOUS")
+
+
+class OrcDesc(C.Structure):
+    _fields_ = [(n, C.c_int) for n in
+                ("family", "D", "I", "E", "k", "renorm", "router_i8", "has_shared", "Is")]
+
+
+class OrcWeights(C.Structure):
+    _fields_ = [(n, C.c_void_p) for n in
+                ("router", "router_s", "g", "u", "d", "gs", "us", "ds",
+                 "sh_g", "sh_u", "sh_d", "sh_gs", "sh_us", "sh_ds", "sh_gate")]
+
+
+_lib = None
+_ref = {}
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        path = os.path.join(HERE, "liboracle.so")
+        if not os.path.exists(path):
+            raise RuntimeError(f"oracle not built: {path} (run make -C oracle)")
+        L = C.CDLL(path)
+        L.orc_moe.restype = C.c_int
+        L.orc_moe.argtypes = [C.POINTER(OrcDesc), C.POINTER(OrcWeights), _f32p, C.c_int,
+                              _f32p, C.c_void_p, C.c_void_p]
+        L.orc_route.restype = C.c_int
+        L.orc_route.argtypes = [C.POINTER(OrcDesc), C.POINTER(OrcWeights), _f32p, C.c_int,
+                                C.c_void_p, C.c_void_p]
+        L.orc_quantize_rows_py.argtypes = [_f32p, C.c_int, C.c_int, _i8p, _f32p]
+        L.orc_quantize_rows_c.argtypes = [_f32p, C.c_int, C.c_int, _i8p, _f32p]
+        L.orc_fill_normal.argtypes = [C.c_uint64, _f32p, C.c_int64, C.c_float]
+        L.orc_expf.restype = C.c_float
+        L.orc_expf.argtypes = [C.c_float]
+        _lib = L
+    return _lib
+
+
+def ref_lib(name: str):
+    """The compiled reference (``olmoe`` or ``qwen``), or None if not built."""
+    if name not in _ref:
+        path = os.path.join(HERE, "_ref", f"libref_{name}.so")
+        _ref[name] = C.CDLL(path) if os.path.exists(path) else None
+    return _ref[name]
+
+
+def ref_available() -> bool:
+    return ref_lib("olmoe") is not None and ref_lib("qwen") is not None
+
+
+def normal(seed: int, shape, sigma: float = 1.0) -> np.ndarray:
+    a = np.empty(int(np.prod(shape)), np.float32)
+    lib().orc_fill_normal(seed & 0xFFFFFFFFFFFFFFFF, a, a.size, sigma)
+    return a.reshape(shape)
+
+
+def quantize_py(w: np.ndarray):
+    w = np.ascontiguousarray(w, np.float32)
+    O, I = w.shape
+    q = np.empty((O, I), np.int8)
+    s = np.empty(O, np.float32)
+    lib().orc_quantize_rows_py(w, O, I, q, s)
+    return q, s
+
+
+def quantize_c(w: np.ndarray):
+    w = np.ascontiguousarray(w, np.float32)
+    O, I = w.shape
+    q = np.empty((O, I), np.int8)
+    s = np.empty(O, np.float32)
+    lib().orc_quantize_rows_c(w, O, I, q, s)
+    return q, s
+
+
+@dataclass
+class Layer:
+    """One seeded MoE layer in the packed expert-major layout."""
+    family: int
+    D: int
+    I: int
+    E: int
+    k: int
+    renorm: int = 0
+    router_i8: int = 0
+    has_shared: int = 0
+    Is: int = 0
+    arrays: dict = field(default_factory=dict)
+
+    def desc(self) -> OrcDesc:
+        return OrcDesc(self.family, self.D, self.I, self.E, self.k, self.renorm,
+                       self.router_i8, self.has_shared, self.Is)
+
+    def weights(self) -> OrcWeights:
+        a = self.arrays
+
+        def p(n):
+            v = a.get(n)
+            return None if v is None else v.ctypes.data
+
+        return OrcWeights(p("router"), p("router_s"), p("g"), p("u"), p("d"), p("gs"),
+                          p("us"), p("ds"), p("sh_g"), p("sh_u"), p("sh_d"), p("sh_gs"),
+                          p("sh_us"), p("sh_ds"), p("sh_gate"))
+
+
+def make_layer(family: int, D: int, I: int, E: int, k: int, seed: int, *, renorm: int = 0,
+               router_i8: int = 0, has_shared: int = 0, Is: int = 0,
+               sigma: float = 0.02, router_bias=None) -> Layer:
+    """Seeded random layer.  Experts: N(0, sigma) quantised per row with the
+    converter rule.  Router: f32 N(0, sigma), or (router_i8) quantised with the
+    engine's load-time rule as qwen.c does in stream mode (qwen.c:283-288).
+    The shared expert is quantised the same way (qwen.c:285-287); sh_gate
+    stays f32 (qwen.c:282)."""
+    L = Layer(family, D, I, E, k, renorm, router_i8, has_shared, Is)
+    a = L.arrays
+    g = np.empty((E, I, D), np.int8); u = np.empty((E, I, D), np.int8)
+    d = np.empty((E, D, I), np.int8)
+    gs = np.empty((E, I), np.float32); us = np.empty((E, I), np.float32)
+    ds = np.empty((E, D), np.float32)
+    base = seed * 1000003
+    for e in range(E):
+        g[e], gs[e] = quantize_py(normal(base + 3 * e + 1, (I, D), sigma))
+        u[e], us[e] = quantize_py(normal(base + 3 * e + 2, (I, D), sigma))
+        d[e], ds[e] = quantize_py(normal(base + 3 * e + 3, (D, I), sigma))
+    a.update(g=g, u=u, d=d, gs=gs, us=us, ds=ds)
+    rw = normal(base + 7, (E, D), sigma)
+    if router_i8:
+        a["router"], a["router_s"] = quantize_c(rw)
+    else:
+        a["router"] = rw
+    if has_shared:
+        a["sh_g"], a["sh_gs"] = quantize_c(normal(base + 11, (Is, D), sigma))
+        a["sh_u"], a["sh_us"] = quantize_c(normal(base + 12, (Is, D), sigma))
+        a["sh_d"], a["sh_ds"] = quantize_c(normal(base + 13, (D, Is), sigma))
+        a["sh_gate"] = normal(base + 14, (D,), sigma)
+    return L
+
+
+def olmoe_layer(seed: int = 1, D=2048, I=1024, E=64, k=8, renorm=0) -> Layer:
+    return make_layer(FAMILY_OLMOE, D, I, E, k, seed, renorm=renorm)
+
+
+def qwen_layer(seed: int = 2, D=2048, I=512, E=256, k=8, Is=512, router_i8=1) -> Layer:
+    return make_layer(FAMILY_QWEN, D, I, E, k, seed, renorm=1, router_i8=router_i8,
+                      has_shared=1, Is=Is)
+
+
+def oracle_moe(L: Layer, x: np.ndarray):
+    """(out [T,D], topk_idx [T,k], topk_w [T,k]) from the C restatement."""
+    x = np.ascontiguousarray(x, np.float32)
+    T = x.shape[0]
+    out = np.empty((T, L.D), np.float32)
+    idx = np.empty((T, L.k), np.int32)
+    w = np.empty((T, L.k), np.float32)
+    d, ww = L.desc(), L.weights()
+    rc = lib().orc_moe(C.byref(d), C.byref(ww), x, T, out, idx.ctypes.data, w.ctypes.data)
+    if rc:
+        raise ValueError("orc_moe rejected the descriptor")
+    return out, idx, w
+
+
+def oracle_route(L: Layer, x: np.ndarray):
+    x = np.ascontiguousarray(x, np.float32)
+    T = x.shape[0]
+    idx = np.empty((T, L.k), np.int32)
+    w = np.empty((T, L.k), np.float32)
+    d, ww = L.desc(), L.weights()
+    if lib().orc_route(C.byref(d), C.byref(ww), x, T, idx.ctypes.data, w.ctypes.data):
+        raise ValueError("orc_route rejected the descriptor")
+    return idx, w
+
+
+def reference_moe(L: Layer, x: np.ndarray) -> np.ndarray:
+    """out [T,D] from the reference's own compiled moe()/moe_step()."""
+    x = np.ascontiguousarray(x, np.float32)
+    T = x.shape[0]
+    out = np.zeros((T, L.D), np.float32)
+    a = L.arrays
+    vp = lambda n: a[n].ctypes.data_as(C.c_void_p)  # noqa: E731
+    if L.family == FAMILY_OLMOE:
+        R = ref_lib("olmoe")
+        if R is None:
+            raise RuntimeError("oracle/_ref not built")
+        assert not L.router_i8
+        rc = R.ref_olmoe_moe(C.c_int(L.D), C.c_int(L.E), C.c_int(L.k), C.c_int(L.I),
+                             C.c_int(L.renorm), x.ctypes.data_as(C.c_void_p), C.c_int(T),
+                             vp("router"), vp("g"), vp("gs"), vp("u"), vp("us"), vp("d"),
+                             vp("ds"), out.ctypes.data_as(C.c_void_p))
+    else:
+        R = ref_lib("qwen")
+        if R is None:
+            raise RuntimeError("oracle/_ref not built")
+        assert L.router_i8 and L.has_shared
+        rc = R.ref_qwen_moe(C.c_int(L.D), C.c_int(L.E), C.c_int(L.k), C.c_int(L.I),
+                            C.c_int(L.Is), vp("router"), vp("router_s"), vp("sh_g"),
+                            vp("sh_gs"), vp("sh_u"), vp("sh_us"), vp("sh_d"), vp("sh_ds"),
+                            vp("sh_gate"), vp("g"), vp("gs"), vp("u"), vp("us"), vp("d"),
+                            vp("ds"), x.ctypes.data_as(C.c_void_p), C.c_int(T),
+                            out.ctypes.data_as(C.c_void_p))
+    if rc:
+        raise RuntimeError("reference harness failed")
+    return out

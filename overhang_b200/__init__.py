@@ -1,0 +1,191 @@
+"""overhang_b200 -- B200-native MoE block for the overhang engines.
+
+The product is the C-ABI library ``libomc.so`` (include/om_cuda.h, and the
+engines' own GPU seam include/om_metal.h).  This module is its Python face:
+ctypes prototypes plus a small ``MoELayer`` wrapper mirroring the engines'
+per-layer MoE call (``moe()`` in engines/olmoe.c:344, ``moe_step()`` in
+engines/qwen.c:453).  There is no Python or CPU fallback: if the library is
+missing or a call fails, an ``OmcError`` is raised.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+import numpy as np
+
+PKG = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(PKG, "libomc.so")
+
+FAMILY_OLMOE, FAMILY_QWEN = 0, 1
+ROUTER_F32, ROUTER_I8 = 0, 1
+
+OK, EINVAL, ENOMEM, ENOINIT, ECUDA, EDEVICE, ETIMEOUT, ENCCL, EUNSUPPORTED = 0, -1, -2, -3, -4, -5, -6, -7, -8
+
+
+class OmcError(RuntimeError):
+    def __init__(self, status: int, msg: str):
+        super().__init__(msg)
+        self.status = status
+
+
+class MoEDesc(C.Structure):
+    """omc_moe_desc (include/om_cuda.h)."""
+    _fields_ = [(n, C.c_int) for n in
+                ("family", "D", "I", "E", "k", "renorm", "router_dtype", "has_shared", "Is")]
+
+
+class OmmJob(C.Structure):
+    """omm_job (include/om_metal.h; same layout as metal/om_metal.h:21-27)."""
+    _fields_ = [("g", C.c_void_p), ("u", C.c_void_p), ("d", C.c_void_p),
+                ("gs", C.c_void_p), ("us", C.c_void_p), ("ds", C.c_void_p),
+                ("mpos", C.c_int), ("pos", C.c_void_p), ("w", C.c_void_p)]
+
+
+# every symbol include/*.h declares, with its ctypes signature
+_vp, _i, _sz = C.c_void_p, C.c_int, C.c_size_t
+SIGNATURES = {
+    "omc_init": (_i, [_i, _sz]),
+    "omc_shutdown": (None, []),
+    "omc_layer_init": (_i, [_i, C.POINTER(MoEDesc), _vp, _vp]),
+    "omc_expert_set": (_i, [_i, _i, _vp, _vp, _vp, _vp, _vp, _vp]),
+    "omc_experts_set_packed": (_i, [_i, _vp, _vp, _vp, _vp, _vp, _vp]),
+    "omc_shared_set": (_i, [_i, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
+    "omc_moe_forward": (_i, [_i, _vp, _i, _vp, _vp, _vp]),
+    "omc_moe_forward_dev": (_i, [_i, _vp, _i, _vp, _vp, _vp, _vp]),
+    "omc_sync": (_i, []),
+    "omc_ep_init": (_i, [_i, _i, _vp]),
+    "omc_ep_unique_id": (_i, [_vp, _sz]),
+    "omc_strerror": (C.c_char_p, [_i]),
+    "omc_last_error": (C.c_char_p, []),
+    "omc_set_profiling": (_i, [_i]),
+    "omc_stage_times": (_i, [C.POINTER(C.c_float), _i]),
+    "omc_launch_count": (C.c_longlong, [_i]),
+    "omc_version": (C.c_char_p, []),
+    "omm_init": (_i, []),
+    "omm_alloc": (_vp, [_sz]),
+    "omm_moe": (_i, [C.POINTER(OmmJob), _i, _vp, _i, _i, _i, _vp]),
+    "omm_moe_act": (_i, [C.POINTER(OmmJob), _i, _vp, _i, _i, _i, _vp, _i]),
+    "omm_dense_q": (_i, [_vp, _vp, _i, _i, _vp, _i, _vp]),
+    "omm_dense": (_i, [_vp, _i, _i, _vp, _i, _vp]),
+    # not in the public headers: failure-detection test hook
+    "omc_debug_wait_timeout": (_i, []),
+}
+
+_lib = None
+
+
+def lib() -> C.CDLL:
+    """Load the in-tree libomc.so (raises if it was not built)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise OmcError(ENOINIT, f"{LIB_PATH} missing: run `python -m overhang_b200.build`")
+        L = C.CDLL(LIB_PATH)
+        for name, (res, args) in SIGNATURES.items():
+            f = getattr(L, name)
+            f.restype = res
+            f.argtypes = args
+        _lib = L
+    return _lib
+
+
+def last_error() -> str:
+    return lib().omc_last_error().decode()
+
+
+def check(rc: int, what: str) -> None:
+    if rc != OK:
+        raise OmcError(rc, f"{what}: {lib().omc_strerror(rc).decode()}: {last_error()}")
+
+
+def _p(a):
+    return None if a is None else a.ctypes.data_as(C.c_void_p)
+
+
+def init(device: int = 0, slab_bytes: int = 0) -> None:
+    check(lib().omc_init(device, slab_bytes), "omc_init")
+
+
+def shutdown() -> None:
+    lib().omc_shutdown()
+
+
+def sync() -> None:
+    check(lib().omc_sync(), "omc_sync")
+
+
+def launch_count(reset: bool = False) -> int:
+    return int(lib().omc_launch_count(1 if reset else 0))
+
+
+def stage_times(n: int = 8):
+    buf = (C.c_float * n)()
+    k = lib().omc_stage_times(buf, n)
+    return [buf[i] for i in range(k)]
+
+
+def set_profiling(on: bool) -> None:
+    lib().omc_set_profiling(1 if on else 0)
+
+
+class MoELayer:
+    """One MoE layer resident on the GPU.
+
+    ``forward(x)`` is the drop-in for the engines' per-layer MoE call: x is
+    the post-norm activation [T, D] f32, the result is out [T, D] f32 plus the
+    routing (topk_idx [T, k] int32, topk_w [T, k] f32) in selection order.
+    """
+
+    def __init__(self, layer: int, family: int, D: int, I: int, E: int, k: int, router,
+                 router_s=None, renorm: int = 0, has_shared: int = 0, Is: int = 0):
+        self.layer = layer
+        r_i8 = router.dtype == np.int8
+        self.desc = MoEDesc(family, D, I, E, k, renorm, ROUTER_I8 if r_i8 else ROUTER_F32,
+                            has_shared, Is)
+        self._keep = [np.ascontiguousarray(router)]
+        rs = None if router_s is None else np.ascontiguousarray(router_s, np.float32)
+        check(lib().omc_layer_init(layer, C.byref(self.desc), _p(self._keep[0]), _p(rs)),
+              "omc_layer_init")
+
+    @classmethod
+    def from_oracle_layer(cls, layer: int, L) -> "MoELayer":
+        """Upload a seeded layer built by oracle.pyoracle.make_layer (tests/bench)."""
+        a = L.arrays
+        m = cls(layer, L.family, L.D, L.I, L.E, L.k, a["router"], a.get("router_s"),
+                L.renorm, L.has_shared, L.Is)
+        m.set_experts_packed(a["g"], a["gs"], a["u"], a["us"], a["d"], a["ds"])
+        if L.has_shared:
+            m.set_shared(a["sh_g"], a["sh_gs"], a["sh_u"], a["sh_us"], a["sh_d"], a["sh_ds"],
+                         a["sh_gate"])
+        return m
+
+    def set_experts_packed(self, g, gs, u, us, d, ds) -> None:
+        arrs = [np.ascontiguousarray(v) for v in (g, gs, u, us, d, ds)]
+        check(lib().omc_experts_set_packed(self.layer, *[_p(v) for v in arrs]),
+              "omc_experts_set_packed")
+
+    def set_expert(self, e: int, g, gs, u, us, d, ds) -> None:
+        arrs = [np.ascontiguousarray(v) for v in (g, gs, u, us, d, ds)]
+        check(lib().omc_expert_set(self.layer, e, *[_p(v) for v in arrs]), "omc_expert_set")
+
+    def set_shared(self, g, gs, u, us, d, ds, sh_gate) -> None:
+        arrs = [np.ascontiguousarray(v) for v in (g, gs, u, us, d, ds, sh_gate)]
+        check(lib().omc_shared_set(self.layer, *[_p(v) for v in arrs]), "omc_shared_set")
+
+    def forward(self, x: np.ndarray):
+        x = np.ascontiguousarray(x, np.float32)
+        T = x.shape[0]
+        out = np.empty((T, self.desc.D), np.float32)
+        idx = np.empty((T, self.desc.k), np.int32)
+        w = np.empty((T, self.desc.k), np.float32)
+        check(lib().omc_moe_forward(self.layer, _p(x), T, _p(out), _p(idx), _p(w)),
+              "omc_moe_forward")
+        return out, idx, w
+
+    def forward_dev(self, x_ptr: int, T: int, out_ptr: int, idx_ptr: int = 0, w_ptr: int = 0,
+                    stream: int = 0) -> None:
+        check(lib().omc_moe_forward_dev(self.layer, C.c_void_p(x_ptr), T, C.c_void_p(out_ptr),
+                                        C.c_void_p(idx_ptr or None), C.c_void_p(w_ptr or None),
+                                        C.c_void_p(stream or None)),
+              "omc_moe_forward_dev")

@@ -1,0 +1,565 @@
+/* omc_host.c -- host runtime of the B200 MoE block (C, CUDA runtime API).
+ *
+ * Owns the device, the library stream, the HBM expert slab, the per-layer
+ * weights and the per-forward workspace, and sequences the kernels of one
+ * MoE forward:
+ *
+ *   router (logits -> softmax -> top-k)            engines/olmoe.c:346-364
+ *   expert FFN  (tensor-core grouped GEMMs, or      engines/olmoe.c:386-399
+ *                CUDA-core GEMV for few tokens)      engines/qwen.c:455-493
+ *   weighted combine (fused into the down pass)     engines/olmoe.c:395-397
+ *
+ * It replaces, in the engines, the per-layer LRU of int8 expert slots
+ * (engines/olmoe.c:48-53,250-272) with one HBM slab filled at load time, and
+ * the Metal backend's arena (metal/om_metal.mm:14-48) with cudaHostAlloc'd
+ * memory for the omm_* seam (omm_shim.c).
+ */
+#include <stdarg.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include <cuda_runtime.h>
+
+#include "om_cuda.h"
+#include "omc_internal.h"
+#include "omc_host.h"
+
+long long omc_g_launches = 0;
+
+omc_state omc_G;
+#define G omc_G
+
+static char g_errbuf[512];
+
+int omc_fail(int code, const char *fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_errbuf, sizeof(g_errbuf), fmt, ap);
+    va_end(ap);
+    return code;
+}
+
+#define CK(call)                                                                                       \
+    do {                                                                                               \
+        cudaError_t e_ = (call);                                                                       \
+        if (e_ != cudaSuccess)                                                                         \
+            return omc_fail(e_ == cudaErrorMemoryAllocation ? OMC_ENOMEM : OMC_ECUDA, "%s: %s (%s:%d)", \
+                            #call, cudaGetErrorString(e_), __FILE__, __LINE__);                        \
+    } while (0)
+
+const char *omc_last_error(void) { return g_errbuf; }
+
+const char *omc_strerror(int st) {
+    switch (st) {
+    case OMC_OK: return "ok";
+    case OMC_EINVAL: return "invalid argument";
+    case OMC_ENOMEM: return "out of memory";
+    case OMC_ENOINIT: return "not initialised";
+    case OMC_ECUDA: return "CUDA error";
+    case OMC_EDEVICE: return "device-side error";
+    case OMC_ETIMEOUT: return "timeout";
+    case OMC_ENCCL: return "NCCL error";
+    case OMC_EUNSUPPORTED: return "unsupported";
+    default: return "unknown status";
+    }
+}
+
+const char *omc_version(void) { return "overhang_b200 omc 0.1 (sm_100a)"; }
+
+long long omc_launch_count(int reset) {
+    long long n = omc_g_launches;
+    if (reset) omc_g_launches = 0;
+    return n;
+}
+
+/* ---------------------------------------------------------------- slab -- */
+/* One budget of HBM for expert weights, handed out in 256-byte aligned
+ * pieces from 1 GiB chunks cudaMalloc'd on demand.  Past the budget,
+ * weights go to mapped pinned host memory, which the kernels read over the
+ * host link (slower, but the layer still runs). */
+#define SLAB_CHUNK ((size_t)1 << 30)
+
+void *omc_slab_alloc(size_t n, int *on_host) {
+    n = (n + 255) & ~(size_t)255;
+    *on_host = 0;
+    if (G.slab_used + n <= G.slab_budget) {
+        if (!G.nchunk || G.chunk_used + n > G.chunk_size[G.nchunk - 1]) {
+            if (G.nchunk == OMC_MAX_CHUNKS) goto host;
+            size_t sz = n > SLAB_CHUNK ? n : SLAB_CHUNK;
+            if (sz > G.slab_budget - G.slab_used) sz = G.slab_budget - G.slab_used;
+            if (sz < n) goto host;
+            void *p = NULL;
+            if (cudaMalloc(&p, sz) != cudaSuccess) {
+                cudaGetLastError();
+                goto host;
+            }
+            G.chunk[G.nchunk] = p;
+            G.chunk_size[G.nchunk] = sz;
+            G.nchunk++;
+            G.chunk_used = 0;
+        }
+        void *p = (char *)G.chunk[G.nchunk - 1] + G.chunk_used;
+        G.chunk_used += n;
+        G.slab_used += n;
+        return p;
+    }
+host:
+    if (G.nhost == OMC_MAX_HOST_BLOCKS) return NULL;
+    {
+        void *h = NULL;
+        if (cudaHostAlloc(&h, n, cudaHostAllocMapped | cudaHostAllocPortable) != cudaSuccess) {
+            cudaGetLastError();
+            return NULL;
+        }
+        G.host_blocks[G.nhost++] = h;
+        G.host_bytes += n;
+        *on_host = 1;
+        return h;   /* UVA: the host pointer is valid in kernels */
+    }
+}
+
+static void slab_release(void) {
+    for (int i = 0; i < G.nchunk; ++i) cudaFree(G.chunk[i]);
+    for (int i = 0; i < G.nhost; ++i) cudaFreeHost(G.host_blocks[i]);
+    G.nchunk = G.nhost = 0;
+    G.slab_used = G.chunk_used = G.host_bytes = 0;
+}
+
+/* ---------------------------------------------------------------- init -- */
+int omc_init(int device, size_t slab_bytes) {
+    if (G.init) {
+        if (device != G.device) return omc_fail(OMC_EINVAL, "omc_init: already bound to device %d", G.device);
+        return OMC_OK;
+    }
+    int n = 0;
+    CK(cudaGetDeviceCount(&n));
+    if (device < 0 || device >= n) return omc_fail(OMC_EINVAL, "omc_init: device %d of %d", device, n);
+    CK(cudaSetDevice(device));
+    struct cudaDeviceProp prop;
+    CK(cudaGetDeviceProperties(&prop, device));
+    if (prop.major != 10) return omc_fail(OMC_EUNSUPPORTED, "omc_init: %s is sm_%d%d; this build is sm_100a",
+                                          prop.name, prop.major, prop.minor);
+    G.num_sms = prop.multiProcessorCount;
+    CK(cudaStreamCreateWithFlags(&G.stream, cudaStreamNonBlocking));
+    CK(cudaMalloc((void **)&G.d_err, 16 * sizeof(int)));
+    CK(cudaMemset(G.d_err, 0, 16 * sizeof(int)));
+    for (int i = 0; i < OMC_NSTAGE_EV; ++i) CK(cudaEventCreate(&G.ev[i]));
+    if (slab_bytes == 0) {
+        size_t fr = 0, tot = 0;
+        CK(cudaMemGetInfo(&fr, &tot));
+        const size_t reserve = (size_t)4 << 30;
+        slab_bytes = fr > 2 * reserve ? fr - reserve : fr / 2;
+    }
+    G.slab_budget = slab_bytes;
+    G.device = device;
+    G.init = 1;
+    const char *p = getenv("OMC_FFN_PATH");
+    G.path_override = !p ? 0 : (!strcmp(p, "gemv") ? 1 : (!strcmp(p, "mma") ? 2 : 0));
+    return OMC_OK;
+}
+
+static void ws_free(void);
+
+void omc_shutdown(void) {
+    if (!G.init) return;
+    cudaSetDevice(G.device);
+    cudaDeviceSynchronize();
+    omc_ep_release();
+    for (int i = 0; i < G.nlayers; ++i) {
+        free(G.layers[i].h_experts);
+        cudaFree(G.layers[i].d_experts_tab);
+    }
+    free(G.layers);
+    G.layers = NULL;
+    G.nlayers = 0;
+    ws_free();
+    slab_release();
+    cudaFree(G.staging);
+    G.staging = NULL;
+    G.staging_bytes = 0;
+    for (int i = 0; i < OMC_NSTAGE_EV; ++i) cudaEventDestroy(G.ev[i]);
+    cudaFree(G.d_err);
+    cudaStreamDestroy(G.stream);
+    memset(&G, 0, sizeof(G));
+}
+
+/* ---------------------------------------------------------------- layers -- */
+omc_layer *omc_get_layer(int layer) {
+    if (layer < 0 || layer >= G.nlayers || !G.layers[layer].used) return NULL;
+    return &G.layers[layer];
+}
+
+static int staging_ensure(size_t n) {
+    if (n <= G.staging_bytes) return OMC_OK;
+    cudaStreamSynchronize(G.stream);
+    cudaFree(G.staging);
+    G.staging = NULL;
+    G.staging_bytes = 0;
+    CK(cudaMalloc(&G.staging, n));
+    G.staging_bytes = n;
+    return OMC_OK;
+}
+
+int omc_layer_init(int layer, const omc_moe_desc *d, const void *router_w, const float *router_s) {
+    if (!G.init) return omc_fail(OMC_ENOINIT, "omc_layer_init: omc_init not called");
+    if (layer < 0 || layer > 4096 || !d || !router_w) return omc_fail(OMC_EINVAL, "omc_layer_init: bad arguments");
+    if (d->family != OMC_FAMILY_OLMOE && d->family != OMC_FAMILY_QWEN)
+        return omc_fail(OMC_EINVAL, "omc_layer_init: unknown family %d", d->family);
+    if (d->D <= 0 || d->I <= 0 || d->E <= 0 || d->k <= 0 || d->k > d->E || d->k > OMC_MAX_K || d->E > OMC_MAX_E ||
+        (d->D % 64) || (d->I % 32))
+        return omc_fail(OMC_EINVAL, "omc_layer_init: shape D=%d I=%d E=%d k=%d (D%%64, I%%32, k<=%d, E<=%d)", d->D,
+                        d->I, d->E, d->k, OMC_MAX_K, OMC_MAX_E);
+    if (d->has_shared && (d->family != OMC_FAMILY_QWEN || d->Is <= 0 || (d->Is % 32)))
+        return omc_fail(OMC_EINVAL, "omc_layer_init: shared expert needs QWEN family and Is%%32==0");
+    if (d->router_dtype == OMC_ROUTER_I8 && !router_s)
+        return omc_fail(OMC_EINVAL, "omc_layer_init: int8 router needs scales");
+    if (layer >= G.nlayers) {
+        int nn = layer + 1;
+        omc_layer *nl = realloc(G.layers, sizeof(omc_layer) * nn);
+        if (!nl) return omc_fail(OMC_ENOMEM, "omc_layer_init: host alloc");
+        memset(nl + G.nlayers, 0, sizeof(omc_layer) * (nn - G.nlayers));
+        G.layers = nl;
+        G.nlayers = nn;
+    }
+    omc_layer *L = &G.layers[layer];
+    if (L->used) {
+        free(L->h_experts);
+        cudaFree(L->d_experts_tab);
+        /* slab space of a re-initialised layer is not reclaimed (bump allocator) */
+    }
+    memset(L, 0, sizeof(*L));
+    L->desc = *d;
+    if (d->family == OMC_FAMILY_QWEN) L->desc.renorm = 1;
+    omc_layer_dev *P = &L->dev;
+    P->family = d->family; P->D = d->D; P->I = d->I; P->E = d->E; P->k = d->k;
+    P->renorm = L->desc.renorm; P->router_i8 = d->router_dtype == OMC_ROUTER_I8;
+    P->has_shared = d->has_shared; P->Is = d->has_shared ? d->Is : 0;
+    P->D_pad = omc_round_up(d->D, OMC_KB);
+    P->I_pad = omc_round_up(d->I, OMC_KB);
+    P->Is_pad = d->has_shared ? omc_round_up(d->Is, OMC_KB) : 0;
+    P->D_rows = omc_round_up(d->D, OMC_TM);
+    P->I_rows = omc_round_up(d->I, OMC_TM);
+    P->Is_rows = d->has_shared ? omc_round_up(d->Is, OMC_TM) : 0;
+    /* EP: the experts this rank owns */
+    L->e0 = 0;
+    L->ne = d->E;
+    if (G.ep_world > 1) {
+        if (d->E % G.ep_world) return omc_fail(OMC_EINVAL, "omc_layer_init: E=%d not divisible by EP world %d",
+                                                d->E, G.ep_world);
+        L->ne = d->E / G.ep_world;
+        L->e0 = G.ep_rank * L->ne;
+    }
+    int on_host;
+    const size_t rbytes = (size_t)d->E * d->D * sizeof(float);
+    float *router = omc_slab_alloc(rbytes, &on_host);
+    if (!router) return omc_fail(OMC_ENOMEM, "omc_layer_init: router");
+    if (P->router_i8) {
+        int rc = staging_ensure((size_t)d->E * d->D);
+        if (rc) return rc;
+        CK(cudaMemcpy(G.staging, router_w, (size_t)d->E * d->D, cudaMemcpyHostToDevice));
+        rc = omc_launch_i8_to_f32((const int8_t *)G.staging, router, (long long)d->E * d->D, G.stream);
+        if (rc) return omc_fail(rc, "omc_layer_init: router conversion launch");
+        float *rs = omc_slab_alloc((size_t)d->E * sizeof(float), &on_host);
+        if (!rs) return omc_fail(OMC_ENOMEM, "omc_layer_init: router scales");
+        CK(cudaMemcpyAsync(rs, router_s, (size_t)d->E * sizeof(float), cudaMemcpyHostToDevice, G.stream));
+        P->router_s = rs;
+    } else {
+        CK(cudaMemcpyAsync(router, router_w, rbytes, cudaMemcpyHostToDevice, G.stream));
+    }
+    P->router = router;
+    L->h_experts = calloc((size_t)d->E + 1, sizeof(omc_expert_ptrs));
+    L->have = calloc((size_t)d->E + 1, 1);
+    if (!L->h_experts || !L->have) return omc_fail(OMC_ENOMEM, "omc_layer_init: host alloc");
+    CK(cudaMalloc((void **)&L->d_experts_tab, sizeof(omc_expert_ptrs) * ((size_t)d->E + 1)));
+    CK(cudaMemsetAsync(L->d_experts_tab, 0, sizeof(omc_expert_ptrs) * ((size_t)d->E + 1), G.stream));
+    P->experts = L->d_experts_tab;
+    L->used = 1;
+    CK(cudaStreamSynchronize(G.stream));
+    return OMC_OK;
+}
+
+/* Upload one row-major int8 matrix [O][K] + scales [O] into slab tiles. */
+static int upload_matrix(const int8_t *q, const float *s, int O, int K, int O_pad, int K_pad, const int8_t **wq,
+                         const float **ws) {
+    int on_host;
+    int8_t *dq = omc_slab_alloc((size_t)O_pad * K_pad, &on_host);
+    float *dsc = omc_slab_alloc((size_t)O_pad * sizeof(float), &on_host);
+    if (!dq || !dsc) return omc_fail(OMC_ENOMEM, "expert upload: slab and host overflow exhausted");
+    int rc = staging_ensure((size_t)O * K);
+    if (rc) return rc;
+    CK(cudaMemcpyAsync(G.staging, q, (size_t)O * K, cudaMemcpyHostToDevice, G.stream));
+    rc = omc_launch_relayout((const int8_t *)G.staging, O, K, dq, O_pad, K_pad, G.stream);
+    if (rc) return omc_fail(rc, "expert upload: relayout launch");
+    CK(cudaMemsetAsync(dsc, 0, (size_t)O_pad * sizeof(float), G.stream));
+    CK(cudaMemcpyAsync(dsc, s, (size_t)O * sizeof(float), cudaMemcpyHostToDevice, G.stream));
+    /* the staging buffer is reused by the next matrix */
+    CK(cudaStreamSynchronize(G.stream));
+    *wq = dq;
+    *ws = dsc;
+    return OMC_OK;
+}
+
+static int set_expert_slot(omc_layer *L, int slot, int I_, int I_pad, int I_rows, const int8_t *g, const float *gs,
+                           const int8_t *u, const float *us, const int8_t *d, const float *ds) {
+    const omc_layer_dev *P = &L->dev;
+    omc_expert_ptrs ep;
+    int rc;
+    if ((rc = upload_matrix(g, gs, I_, P->D, I_rows, P->D_pad, &ep.g, &ep.gs))) return rc;
+    if ((rc = upload_matrix(u, us, I_, P->D, I_rows, P->D_pad, &ep.u, &ep.us))) return rc;
+    if ((rc = upload_matrix(d, ds, P->D, I_, P->D_rows, I_pad, &ep.d, &ep.ds))) return rc;
+    L->h_experts[slot] = ep;
+    L->have[slot] = 1;
+    CK(cudaMemcpy(L->d_experts_tab + slot, &ep, sizeof(ep), cudaMemcpyHostToDevice));
+    return OMC_OK;
+}
+
+int omc_expert_set(int layer, int e, const int8_t *g, const float *gs, const int8_t *u, const float *us,
+                   const int8_t *d, const float *ds) {
+    omc_layer *L = omc_get_layer(layer);
+    if (!L) return omc_fail(OMC_ENOINIT, "omc_expert_set: layer %d not initialised", layer);
+    if (e < 0 || e >= L->desc.E || !g || !gs || !u || !us || !d || !ds)
+        return omc_fail(OMC_EINVAL, "omc_expert_set: bad expert %d or null pointer", e);
+    if (e < L->e0 || e >= L->e0 + L->ne) return OMC_OK;   /* owned by another EP rank */
+    return set_expert_slot(L, e, L->desc.I, L->dev.I_pad, L->dev.I_rows, g, gs, u, us, d, ds);
+}
+
+int omc_experts_set_packed(int layer, const int8_t *g, const float *gs, const int8_t *u, const float *us,
+                           const int8_t *d, const float *ds) {
+    omc_layer *L = omc_get_layer(layer);
+    if (!L) return omc_fail(OMC_ENOINIT, "omc_experts_set_packed: layer %d not initialised", layer);
+    const size_t D = L->desc.D, I = L->desc.I;
+    for (int e = 0; e < L->desc.E; ++e) {
+        int rc = omc_expert_set(layer, e, g + e * I * D, gs + e * I, u + e * I * D, us + e * I, d + e * D * I,
+                                ds + e * D);
+        if (rc) return rc;
+    }
+    return OMC_OK;
+}
+
+int omc_shared_set(int layer, const int8_t *g, const float *gs, const int8_t *u, const float *us, const int8_t *d,
+                   const float *ds, const float *sh_gate) {
+    omc_layer *L = omc_get_layer(layer);
+    if (!L) return omc_fail(OMC_ENOINIT, "omc_shared_set: layer %d not initialised", layer);
+    if (!L->desc.has_shared) return omc_fail(OMC_EINVAL, "omc_shared_set: layer %d has no shared expert", layer);
+    if (!g || !gs || !u || !us || !d || !ds || !sh_gate) return omc_fail(OMC_EINVAL, "omc_shared_set: null pointer");
+    int on_host;
+    float *sgv = omc_slab_alloc((size_t)L->desc.D * sizeof(float), &on_host);
+    if (!sgv) return omc_fail(OMC_ENOMEM, "omc_shared_set: gate vector");
+    CK(cudaMemcpy(sgv, sh_gate, (size_t)L->desc.D * sizeof(float), cudaMemcpyHostToDevice));
+    L->dev.sh_gate = sgv;
+    return set_expert_slot(L, L->desc.E, L->desc.Is, L->dev.Is_pad, L->dev.Is_rows, g, gs, u, us, d, ds);
+}
+
+/* ---------------------------------------------------------------- workspace -- */
+static void ws_free(void) {
+    void **p = (void **)&G.ws_ptrs;
+    for (size_t i = 0; i < sizeof(G.ws_ptrs) / sizeof(void *); ++i) {
+        cudaFree(p[i]);
+        p[i] = NULL;
+    }
+    memset(&G.ws, 0, sizeof(G.ws));
+    memset(G.ws_bytes, 0, sizeof(G.ws_bytes));
+}
+
+/* grow-only buffer */
+static int ws_buf(int slot, void **ptr, size_t need) {
+    if (need == 0) need = 256;
+    if (G.ws_bytes[slot] >= need && *ptr) return OMC_OK;
+    cudaStreamSynchronize(G.stream);
+    cudaDeviceSynchronize();
+    cudaFree(*ptr);
+    *ptr = NULL;
+    size_t n = need + need / 4;
+    cudaError_t e = cudaMalloc(ptr, n);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        G.ws_bytes[slot] = 0;
+        return omc_fail(OMC_ENOMEM, "workspace: cudaMalloc(%zu) failed", n);
+    }
+    G.ws_bytes[slot] = n;
+    return OMC_OK;
+}
+
+int omc_ws_ensure(const omc_layer *L, int T, int host_io) {
+    const omc_layer_dev *P = &L->dev;
+    const size_t Tz = (size_t)T, D = (size_t)P->D, E = (size_t)P->E, K = (size_t)P->k;
+    const size_t Imax_rows = (size_t)(P->Is_rows > P->I_rows ? P->Is_rows : P->I_rows);
+    const size_t Imax_pad = (size_t)(P->Is_pad > P->I_pad ? P->Is_pad : P->I_pad);
+    /* activation rows: every routed slot + shared rows + 16-row padding per expert */
+    const size_t R = omc_round_up((int)(Tz * K + (P->has_shared ? Tz : 0) + (E + 1) * OMC_ROW_ALIGN), 128);
+    int rc = 0;
+    omc_ws_ptrs *W = &G.ws_ptrs;
+    if (host_io) {
+        if ((rc = ws_buf(0, (void **)&W->x, Tz * D * 4))) return rc;
+        if ((rc = ws_buf(1, (void **)&W->out, Tz * D * 4))) return rc;
+    }
+    if ((rc = ws_buf(2, (void **)&W->logits, Tz * (E + 1) * 4))) return rc;
+    if ((rc = ws_buf(3, (void **)&W->topk_idx, Tz * K * 4))) return rc;
+    if ((rc = ws_buf(4, (void **)&W->topk_w, Tz * K * 4))) return rc;
+    if ((rc = ws_buf(5, (void **)&W->sg, Tz * 4))) return rc;
+    if ((rc = ws_buf(6, (void **)&W->counts, (E + 4) * 4 * 3 + 64))) return rc;
+    if ((rc = ws_buf(7, (void **)&W->rowinfo, R * 4))) return rc;
+    if ((rc = ws_buf(8, (void **)&W->work, (size_t)64 << 20 > R * 64 ? R * 64 : (size_t)64 << 20))) return rc;
+    if ((rc = ws_buf(9, (void **)&W->xp, (size_t)P->D_pad * R * 2))) return rc;
+    if ((rc = ws_buf(10, (void **)&W->hp, Imax_pad * R * 2))) return rc;
+    if ((rc = ws_buf(11, (void **)&W->ypart, Tz * (K + 1) * D * 4))) return rc;
+    if ((rc = ws_buf(12, (void **)&W->hbuf, (Tz * K + Tz) * Imax_rows * 4))) return rc;
+    omc_ws *ws = &G.ws;
+    ws->T_cap = T;
+    ws->R_cap = (int)R;
+    ws->x = W->x;
+    ws->out = W->out;
+    ws->logits = W->logits;
+    ws->topk_idx = W->topk_idx;
+    ws->topk_w = W->topk_w;
+    ws->sg = W->sg;
+    ws->counts = W->counts;
+    ws->offsets = W->counts + (E + 4);
+    ws->fill = W->counts + 2 * (E + 4);
+    ws->nwork = W->counts + 3 * (E + 4);
+    ws->rowinfo = W->rowinfo;
+    ws->work = W->work;
+    ws->xp = W->xp;
+    ws->hp = W->hp;
+    ws->ypart = W->ypart;
+    ws->hbuf = W->hbuf;
+    ws->err = G.d_err;
+    return OMC_OK;
+}
+
+/* ---------------------------------------------------------------- errors -- */
+int omc_check_device_error(void) {
+    int h[4] = {0, 0, 0, 0};
+    cudaError_t e = cudaMemcpy(h, G.d_err, sizeof(h), cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return omc_fail(OMC_ECUDA, "reading device error word: %s", cudaGetErrorString(e));
+    if (!h[0]) return OMC_OK;
+    cudaMemset(G.d_err, 0, sizeof(h));
+    const int st = h[0] == OMC_DEVERR_TIMEOUT ? OMC_ETIMEOUT : OMC_EDEVICE;
+    return omc_fail(st, "device error code %d at site %d (detail %d)", h[0], h[1], h[2]);
+}
+
+int omc_sync(void) {
+    if (!G.init) return omc_fail(OMC_ENOINIT, "omc_sync: omc_init not called");
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) return omc_fail(OMC_ECUDA, "omc_sync: %s", cudaGetErrorString(e));
+    return omc_check_device_error();
+}
+
+/* ---------------------------------------------------------------- profiling -- */
+int omc_set_profiling(int on) {
+    G.profiling = on ? 1 : 0;
+    return OMC_OK;
+}
+
+int omc_stage_times(float *ms, int n) {
+    if (!G.init || !G.prof_valid) return 0;
+    int k = 0;
+    for (int i = 0; i + 1 < G.prof_nev && k < n; ++i, ++k) {
+        float t = 0.f;
+        if (cudaEventElapsedTime(&t, G.ev[i], G.ev[i + 1]) != cudaSuccess) {
+            cudaGetLastError();
+            t = -1.f;
+        }
+        ms[k] = t;
+    }
+    return k;
+}
+
+void omc_prof_mark(cudaStream_t s, int i) {
+    if (G.profiling && i < OMC_NSTAGE_EV) {
+        cudaEventRecord(G.ev[i], s);
+        G.prof_nev = i + 1;
+    }
+}
+
+/* ---------------------------------------------------------------- forward -- */
+static int layer_ready(const omc_layer *L) {
+    for (int e = L->e0; e < L->e0 + L->ne; ++e)
+        if (!L->have[e]) return omc_fail(OMC_ENOINIT, "forward: expert %d of layer not uploaded", e);
+    if (L->desc.has_shared && !L->have[L->desc.E])
+        return omc_fail(OMC_ENOINIT, "forward: shared expert not uploaded");
+    return OMC_OK;
+}
+
+/* Choose the expert path: tensor-core grouped GEMM when experts see enough
+ * tokens to fill an MMA N of 16, CUDA-core GEMV otherwise. */
+static int use_mma(const omc_layer *L, int T) {
+    if (G.path_override == 1) return 0;
+    if (G.path_override == 2) return 1;
+    const long long slots = (long long)T * L->desc.k;
+    return slots >= 4LL * L->desc.E;   /* >= 4 tokens per expert on average */
+}
+
+int omc_forward_device(omc_layer *L, const float *x, int T, float *out, int32_t *topk_idx, float *topk_w,
+                       cudaStream_t s) {
+    int rc;
+    if ((rc = layer_ready(L))) return rc;
+    if ((rc = omc_ws_ensure(L, T, 0))) return rc;
+    if (G.ep_world > 1) return omc_ep_forward(L, x, T, out, topk_idx, topk_w, s);
+    const omc_ws *ws = &G.ws;
+    int32_t *idx = topk_idx ? topk_idx : ws->topk_idx;
+    float *w = topk_w ? topk_w : ws->topk_w;
+    G.prof_valid = 0;
+    omc_prof_mark(s, 0);
+    CK(cudaMemsetAsync(ws->counts, 0, sizeof(int) * (size_t)(L->desc.E + 4) * 3, s));
+    if ((rc = omc_launch_router(&L->dev, x, T, ws, idx, w, s))) return omc_fail(rc, "router launch failed");
+    omc_prof_mark(s, 1);
+    if (use_mma(L, T)) {
+        rc = omc_launch_mma_ffn(&L->dev, x, T, ws, idx, w, out, s);
+        if (rc == OMC_EUNSUPPORTED && G.path_override != 2) rc = omc_launch_gemv_ffn(&L->dev, x, T, ws, idx, w, out, s);
+    } else {
+        rc = omc_launch_gemv_ffn(&L->dev, x, T, ws, idx, w, out, s);
+    }
+    if (rc) return omc_fail(rc, "expert FFN launch failed (%s)", omc_strerror(rc));
+    omc_prof_mark(s, 2);
+    G.prof_valid = G.profiling;
+    return OMC_OK;
+}
+
+int omc_moe_forward_dev(int layer, const float *x, int T, float *out, int32_t *topk_idx, float *topk_w,
+                        void *stream) {
+    if (!G.init) return omc_fail(OMC_ENOINIT, "omc_moe_forward_dev: omc_init not called");
+    omc_layer *L = omc_get_layer(layer);
+    if (!L) return omc_fail(OMC_ENOINIT, "omc_moe_forward_dev: layer %d not initialised", layer);
+    if (T < 0 || (T > 0 && (!x || !out))) return omc_fail(OMC_EINVAL, "omc_moe_forward_dev: bad T or pointers");
+    if (T == 0 && G.ep_world <= 1) return OMC_OK;
+    cudaStream_t s = stream ? (cudaStream_t)stream : G.stream;
+    return omc_forward_device(L, x, T, out, topk_idx, topk_w, s);
+}
+
+int omc_moe_forward(int layer, const float *x, int T, float *out, int32_t *topk_idx, float *topk_w) {
+    if (!G.init) return omc_fail(OMC_ENOINIT, "omc_moe_forward: omc_init not called");
+    omc_layer *L = omc_get_layer(layer);
+    if (!L) return omc_fail(OMC_ENOINIT, "omc_moe_forward: layer %d not initialised", layer);
+    if (T < 0 || (T > 0 && (!x || !out))) return omc_fail(OMC_EINVAL, "omc_moe_forward: bad T or pointers");
+    if (T == 0 && G.ep_world <= 1) return OMC_OK;
+    int rc;
+    if ((rc = omc_ws_ensure(L, T > 0 ? T : 1, 1))) return rc;
+    const size_t D = (size_t)L->desc.D, K = (size_t)L->desc.k;
+    cudaStream_t s = G.stream;
+    if (T > 0) CK(cudaMemcpyAsync(G.ws.x, x, (size_t)T * D * 4, cudaMemcpyHostToDevice, s));
+    if ((rc = omc_forward_device(L, G.ws.x, T, G.ws.out, G.ws.topk_idx, G.ws.topk_w, s))) {
+        cudaStreamSynchronize(s);
+        return rc;
+    }
+    if (T > 0) {
+        CK(cudaMemcpyAsync(out, G.ws.out, (size_t)T * D * 4, cudaMemcpyDeviceToHost, s));
+        if (topk_idx) CK(cudaMemcpyAsync(topk_idx, G.ws.topk_idx, (size_t)T * K * 4, cudaMemcpyDeviceToHost, s));
+        if (topk_w) CK(cudaMemcpyAsync(topk_w, G.ws.topk_w, (size_t)T * K * 4, cudaMemcpyDeviceToHost, s));
+    }
+    CK(cudaStreamSynchronize(s));
+    return omc_check_device_error();
+}
+
+/* ---------------------------------------------------------------- debug -- */
+/* Runs a kernel whose bounded wait can never complete and returns the status
+ * the library reports for it (OMC_ETIMEOUT expected), leaving the context
+ * usable.  Used by the failure-detection test. */
+int omc_debug_wait_timeout(void) {
+    if (!G.init) return omc_fail(OMC_ENOINIT, "omc_debug_wait_timeout: omc_init not called");
+    int rc = omc_launch_test_wait(G.d_err, G.stream);
+    if (rc) return rc;
+    CK(cudaStreamSynchronize(G.stream));
+    return omc_check_device_error();
+}

@@ -1,0 +1,86 @@
+/* omc_host.h -- host-side state of the runtime (internal). */
+#ifndef OMC_HOST_H
+#define OMC_HOST_H
+#include <cuda_runtime.h>
+
+#include "om_cuda.h"
+#include "omc_internal.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define OMC_MAX_CHUNKS 512
+#define OMC_MAX_HOST_BLOCKS 65536
+#define OMC_NSTAGE_EV 8
+
+typedef struct {
+    int used;
+    omc_moe_desc desc;
+    omc_layer_dev dev;              /* what kernels receive                 */
+    omc_expert_ptrs *h_experts;     /* host copy of the pointer table [E+1] */
+    omc_expert_ptrs *d_experts_tab; /* device pointer table [E+1]           */
+    unsigned char *have;            /* uploaded flags [E+1]                 */
+    int e0, ne;                     /* experts owned by this rank (EP)      */
+} omc_layer;
+
+typedef struct {
+    float *x, *out, *logits;
+    int32_t *topk_idx;
+    float *topk_w, *sg;
+    int *counts, *rowinfo, *work;
+    uint16_t *xp, *hp;
+    float *ypart, *hbuf;
+} omc_ws_ptrs;
+
+typedef struct {
+    int init, device, num_sms;
+    cudaStream_t stream;
+    int *d_err;
+    /* slab */
+    size_t slab_budget, slab_used, chunk_used, host_bytes;
+    void *chunk[OMC_MAX_CHUNKS];
+    size_t chunk_size[OMC_MAX_CHUNKS];
+    int nchunk;
+    void *host_blocks[OMC_MAX_HOST_BLOCKS];
+    int nhost;
+    void *staging;
+    size_t staging_bytes;
+    /* layers */
+    omc_layer *layers;
+    int nlayers;
+    /* workspace */
+    omc_ws ws;
+    omc_ws_ptrs ws_ptrs;
+    size_t ws_bytes[16];
+    /* profiling */
+    int profiling, prof_valid, prof_nev;
+    cudaEvent_t ev[OMC_NSTAGE_EV];
+    int path_override;              /* 0 auto, 1 gemv, 2 mma (OMC_FFN_PATH) */
+    /* expert parallelism */
+    int ep_rank, ep_world;
+    void *ep;                       /* omc_ep_state (omc_ep.c)              */
+} omc_state;
+
+extern omc_state omc_G;
+
+int omc_fail(int code, const char *fmt, ...);
+void *omc_slab_alloc(size_t n, int *on_host);
+omc_layer *omc_get_layer(int layer);
+int omc_ws_ensure(const omc_layer *L, int T, int host_io);
+int omc_check_device_error(void);
+void omc_prof_mark(cudaStream_t s, int i);
+int omc_forward_device(omc_layer *L, const float *x, int T, float *out, int32_t *topk_idx, float *topk_w,
+                       cudaStream_t s);
+
+/* expert parallelism (omc_ep.c) */
+int omc_ep_forward(omc_layer *L, const float *x, int T, float *out, int32_t *topk_idx, float *topk_w,
+                   cudaStream_t s);
+void omc_ep_release(void);
+
+int omc_debug_wait_timeout(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

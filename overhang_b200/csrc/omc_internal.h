@@ -1,0 +1,115 @@
+/* omc_internal.h -- internal types shared by the C host runtime (omc_host.c)
+ * and the CUDA kernel files.  Not part of the public ABI (include/om_cuda.h).
+ *
+ * Expert weight layout in HBM ("tiled int8"): a row-major int8 matrix
+ * W[O][K] is padded to O_pad = roundup(O,128), K_pad = roundup(K,64) with
+ * zeros and stored as blocks of 128 rows x 64 columns (8 KiB each), blocks
+ * ordered [row tile][K block]; inside a block the 16-byte chunk c (columns
+ * 16c..16c+15) of row r sits at byte (c*128 + r)*16.  A warp reading 32
+ * consecutive rows' chunk c reads 512 contiguous bytes, and one K block of a
+ * row tile is one contiguous 8 KiB bulk copy.  Row scales are f32 padded with
+ * zeros to O_pad.
+ *
+ * Activation operands of the tensor-core path ("AOL"): f16 rows of 64
+ * elements (128 B) per K block, 8-row atoms of 1024 B with the 128-byte
+ * swizzle (16-byte chunk c of row r stored at chunk c ^ (r & 7)), K blocks
+ * outermost: element (row, k) of a [R][K_pad] operand lives at
+ *   (k/64)*R*128 + row*128 + ((((k%64)/8) ^ (row&7)) * 16) + (k%8)*2.
+ * A contiguous run of rows of one K block is a valid K-major SWIZZLE_128B
+ * UMMA operand once copied 1024-byte aligned into shared memory.
+ */
+#ifndef OMC_INTERNAL_H
+#define OMC_INTERNAL_H
+#include <stdint.h>
+#include <stddef.h>
+#include <cuda_runtime.h>
+
+#include "om_cuda.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define OMC_TM 128          /* rows per weight tile                       */
+#define OMC_KB 64           /* int8 columns per K block                   */
+#define OMC_BLK_BYTES (OMC_TM * OMC_KB)
+#define OMC_ROW_ALIGN 16    /* expert row groups padded to 16 rows (UMMA N) */
+#define OMC_MAX_K 32
+#define OMC_MAX_E 1024
+
+/* device error codes written into the error word */
+#define OMC_DEVERR_TIMEOUT 1
+#define OMC_DEVERR_BOUNDS  2
+#define OMC_DEVERR_ROUTE   3
+#define OMC_DEVERR_CONFIG  4
+
+/* error sites (err[1]) */
+#define OMC_SITE_GEMM_PRODUCER 10
+#define OMC_SITE_GEMM_DEQUANT  11
+#define OMC_SITE_GEMM_MMA      12
+#define OMC_SITE_GEMM_EPILOGUE 13
+#define OMC_SITE_ROUTER        20
+#define OMC_SITE_DISPATCH      21
+#define OMC_SITE_GEMV          22
+#define OMC_SITE_COMBINE       23
+#define OMC_SITE_TEST_WAIT     90
+
+static inline int omc_round_up(int x, int m) { return (x + m - 1) / m * m; }
+
+/* One expert's three tiled matrices and padded scales. */
+typedef struct {
+    const int8_t *g, *u, *d;
+    const float *gs, *us, *ds;
+} omc_expert_ptrs;
+
+/* Layer parameters handed to kernels by value. */
+typedef struct {
+    int family, D, I, E, k, renorm, router_i8, has_shared, Is;
+    int D_pad, I_pad, Is_pad;     /* roundup(.., 64): K extent of a tiled matrix   */
+    int D_rows, I_rows, Is_rows;  /* roundup(.., 128): row extent of a tiled matrix */
+    const float *router;          /* f32 [E][D] (int8 routers stored as their exact f32 values) */
+    const float *router_s;        /* [E] for int8 routers, else NULL */
+    const float *sh_gate;         /* [D] or NULL */
+    const omc_expert_ptrs *experts;  /* device table [E + 1]; entry E = shared expert */
+} omc_layer_dev;
+
+/* Per-forward workspace (device pointers, grow-only). */
+typedef struct {
+    int T_cap, R_cap;             /* capacity in tokens and activation rows */
+    float *x;                     /* [T][D] staging for host inputs       */
+    float *out;                   /* [T][D] staging for host outputs      */
+    float *logits;                /* [T][E + 1]                           */
+    int32_t *topk_idx;            /* [T][k]                               */
+    float *topk_w;                /* [T][k]                               */
+    float *sg;                    /* [T] shared-gate sigmoid              */
+    int *counts;                  /* [E + 2] rows per expert (+ shared)   */
+    int *offsets;                 /* [E + 3] padded row offsets           */
+    int *fill;                    /* [E + 2]                              */
+    int *rowinfo;                 /* [R]: routed slot t*k+kk, T*k+t shared, -1 pad */
+    int *work;                    /* tile work list                       */
+    int *nwork;                   /* [4] work counts                      */
+    uint16_t *xp;                 /* AOL f16 [D_pad/64][R][64]            */
+    uint16_t *hp;                 /* AOL f16 [Imax_pad/64][R][64]         */
+    float *ypart;                 /* [T][k + 1][D]                        */
+    float *hbuf;                  /* [T*k + T][Imax_pad] (GEMV path)      */
+    int *err;                     /* [4] device error word                */
+} omc_ws;
+
+/* ---- launchers (CUDA files), all enqueue on `s` ---------------------- */
+int omc_launch_relayout(const int8_t *src, int O, int K, int8_t *dst, int O_pad, int K_pad, cudaStream_t s);
+int omc_launch_i8_to_f32(const int8_t *src, float *dst, long long n, cudaStream_t s);
+int omc_launch_router(const omc_layer_dev *L, const float *x, int T, const omc_ws *ws,
+                      int32_t *topk_idx, float *topk_w, cudaStream_t s);
+int omc_launch_gemv_ffn(const omc_layer_dev *L, const float *x, int T, const omc_ws *ws,
+                        const int32_t *topk_idx, const float *topk_w, float *out, cudaStream_t s);
+int omc_launch_mma_ffn(const omc_layer_dev *L, const float *x, int T, const omc_ws *ws,
+                       const int32_t *topk_idx, const float *topk_w, float *out, cudaStream_t s);
+int omc_launch_test_wait(int *err, cudaStream_t s);
+
+/* number of kernels launched by this library (launchers add to it) */
+extern long long omc_g_launches;
+
+#ifdef __cplusplus
+}
+#endif
+#endif
