@@ -1,0 +1,337 @@
+#!/usr/bin/env python3
+"""MoE-block benchmark (one JSON line on rank 0).
+
+Workload: one OLMoE-shaped MoE layer, prefill --
+D=2048, 64 experts, top-8 softmax routing (no renorm), SwiGLU FFN 1024, int8
+per-row weights with f32 scales, T=512 tokens of f32 activations ~N(0,1),
+router and experts N(0,0.02) from a fixed seed.  A step is one pass of the
+MoE block over the 512 tokens.
+
+  python bench.py [--gpus N --steps K --warmup W] [--impl reference]
+
+Arms
+  ours (default): libomc.so.  `value` = tokens/s with inputs resident in HBM
+      (device entry omc_moe_forward_dev), timed with CUDA events on the
+      launching stream, max over ranks; `e2e` = the same through the host
+      entry omc_moe_forward (pinned host x in, host out/top-k back every
+      step).  N>1: each rank runs its own copy of the workload (weak
+      scaling, no data-path collective).
+  reference: the reference's own CPU MoE (engines/olmoe.c moe(), compiled from
+      its sources into oracle/_ref by oracle/Makefile) on all host cores, each
+      step a bounded token sample; rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+D, I, E, K, T = 2048, 1024, 64, 8, 512
+SEED_W, SEED_X = 1, 4242
+METRIC, UNIT = "MoE-block tokens/s", "tokens/s"
+WORKLOAD = "olmoe_layer_prefill_T512"
+EXPERT_BYTES = 3 * D * I + 4 * (2 * I + D)          # int8 g,u,d + f32 scales
+CONFIG = {"workload": WORKLOAD, "D": D, "I": I, "E": E, "k": K, "T": T,
+          "weights": "int8 per-row + f32 scales, N(0,0.02) seed 1",
+          "x": "f32 N(0,1) seed 4242, 8 rotating batches",
+          "l2": "expert weights 403 MB > 126 MB L2 stream from HBM every step"}
+
+
+def env_rank():
+    return (int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)),
+            int(os.environ.get("LOCAL_RANK", 0)))
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        j = json.load(open(p))
+        return j["hbm_gbs"], j.get("bf16_tflops"), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index, self.proc, self.lines = index, None, []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "50"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.t.join(timeout=2)
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [v.strip() for v in ln.split(",")]
+            if len(f) < 7:
+                continue
+            try:
+                sm.append(float(f[0]))
+                mx = float(f[1])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[3:7]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def make_layer():
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import pyoracle
+    return pyoracle, pyoracle.olmoe_layer(SEED_W, D=D, I=I, E=E, k=K)
+
+
+def cpu_reference_tokens_per_s(pyoracle, L, budget_s, kind_pref="reference"):
+    """Time the reference's CPU MoE on a bounded token sample; returns
+    (tokens/s, sample tokens, kind, cores, seconds)."""
+    cores = os.cpu_count() or 1
+    os.environ.setdefault("OMP_NUM_THREADS", str(cores))
+    fn, kind = None, "port"
+    if kind_pref == "reference" and pyoracle.ref_lib("olmoe") is not None:
+        fn, kind = (lambda xx: pyoracle.reference_moe(L, xx)), "reference"
+    else:
+        fn = lambda xx: pyoracle.oracle_moe(L, xx)[0]  # noqa: E731
+    x = pyoracle.normal(SEED_X, (T, D))
+    t0 = time.perf_counter()
+    fn(x[:16])
+    probe = max(time.perf_counter() - t0, 1e-3)
+    n = int(min(T, max(16, 16 * budget_s / probe)))
+    reps, tot, t0 = 0, 0, time.perf_counter()
+    while True:
+        fn(x[:n])
+        reps += 1
+        tot += n
+        if time.perf_counter() - t0 >= budget_s:
+            break
+    dt = time.perf_counter() - t0
+    return tot / dt, n, kind, cores, dt
+
+
+def run_reference(args):
+    rank, world, _ = env_rank()
+    if rank != 0:
+        return
+    pyoracle, L = make_layer()
+    cores = os.cpu_count() or 1
+    os.environ.setdefault("OMP_NUM_THREADS", str(cores))
+    if pyoracle.ref_lib("olmoe") is not None:
+        kind, fn = "reference", (lambda xx: pyoracle.reference_moe(L, xx))
+    else:
+        kind, fn = "port", (lambda xx: pyoracle.oracle_moe(L, xx)[0])
+    x = pyoracle.normal(SEED_X, (T, D))
+    # size each step so the whole run stays within ~150 s of CPU time
+    per_step = max(0.25, min(10.0, 150.0 / max(args.steps + args.warmup, 1)))
+    t0 = time.perf_counter()
+    fn(x[:16])
+    probe = max(time.perf_counter() - t0, 1e-3)
+    n = int(min(T, max(8, 16 * per_step / probe)))
+    for _ in range(args.warmup):
+        fn(x[:n])
+    samples = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        fn(x[:n])
+        samples.append(time.perf_counter() - t0)
+    step_s = sum(samples) / len(samples)
+    value = n / step_s
+    line = {"metric": METRIC, "value": value, "unit": UNIT, "impl": "reference", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_s * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic", "config": dict(CONFIG, sample_tokens_per_step=n),
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": kind,
+                             "sample": f"{n} of {T} tokens per step, engines/olmoe.c moe() "
+                                       f"OpenMP on {cores} threads"},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args):
+    import torch
+    rank, world, local = env_rank()
+    dist = None
+    if world > 1:
+        import torch.distributed as dist  # noqa: F811
+        from datetime import timedelta
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120))
+    dev = local
+    torch.cuda.set_device(dev)
+    import overhang_b200 as ob
+    ob.init(dev, 8 << 30)
+    pyoracle, L = make_layer()
+    layer = ob.MoELayer.from_oracle_layer(0, L)
+    nbuf = 8
+    xs = [torch.from_numpy(pyoracle.normal(SEED_X + i, (T, D))).to(f"cuda:{dev}") for i in range(nbuf)]
+    out = torch.empty((T, D), dtype=torch.float32, device=f"cuda:{dev}")
+    idx = torch.empty((T, K), dtype=torch.int32, device=f"cuda:{dev}")
+    wts = torch.empty((T, K), dtype=torch.float32, device=f"cuda:{dev}")
+    # a dedicated stream: the library enqueues on it and the events time it
+    stream = torch.cuda.Stream(device=dev)
+    torch.cuda.set_stream(stream)
+    sptr = stream.cuda_stream
+
+    def step(i):
+        layer.forward_dev(xs[i % nbuf].data_ptr(), T, out.data_ptr(), idx.data_ptr(), wts.data_ptr(),
+                          sptr)
+
+    def barrier():
+        torch.cuda.synchronize()
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for i in range(args.warmup):
+        step(i)
+    ob.sync()
+    barrier()
+    clk = ClockSampler(dev)
+    clk.start()
+    ob.launch_count(reset=True)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(args.steps):
+        step(i)
+    e1.record(stream)
+    barrier()
+    launches = ob.launch_count()
+    clocks = clk.stop()
+    ob.sync()
+    ms = e0.elapsed_time(e1)
+    t_max = ms
+    if dist:
+        tt = torch.tensor([ms], device=f"cuda:{dev}")
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        t_max = float(tt.item())
+    value = world * T * args.steps / (t_max / 1e3)
+
+    # per-stage device time (profiling events on the launching stream)
+    ob.set_profiling(True)
+    st = []
+    for i in range(max(3, min(args.steps, 20))):
+        step(i)
+        torch.cuda.synchronize()
+        st.append(ob.stage_times())
+    ob.set_profiling(False)
+    stage_names = [n for n, _ in st[-1]] if st and st[-1] else []
+    stage_ms = np.array([[v for _, v in row] for row in st]).mean(axis=0).tolist() if stage_names else []
+
+    # end to end through the host entry: pinned x in, out + routing back
+    hx = [torch.from_numpy(pyoracle.normal(SEED_X + i, (T, D))).pin_memory() for i in range(nbuf)]
+    hout = torch.empty((T, D), dtype=torch.float32).pin_memory()
+    hidx = torch.empty((T, K), dtype=torch.int32).pin_memory()
+    hw = torch.empty((T, K), dtype=torch.float32).pin_memory()
+    lib = ob.lib()
+
+    def step_e2e(i):
+        rc = lib.omc_moe_forward(0, C.c_void_p(hx[i % nbuf].data_ptr()), T, C.c_void_p(hout.data_ptr()),
+                                 C.c_void_p(hidx.data_ptr()), C.c_void_p(hw.data_ptr()))
+        ob.check(rc, "omc_moe_forward")
+
+    for i in range(args.warmup):
+        step_e2e(i)
+    barrier()
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        step_e2e(i)
+    e2e_s = time.perf_counter() - t0
+    if dist:
+        tt = torch.tensor([e2e_s], device=f"cuda:{dev}")
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        e2e_s = float(tt.item())
+    e2e = world * T * args.steps / e2e_s
+
+    hbm, tf, src = peaks()
+    # dominant kernel: the gate/up expert GEMM (2/3 of the weight bytes).
+    # algorithmic bytes per launch = every active expert's int8 gate+up rows +
+    # their scales + the f16 token operand it reads + the f16 h it writes.
+    n_active = int(len(np.unique(idx.cpu().numpy())))
+    stages = dict(zip(stage_names, stage_ms))
+    if "gemm_gateup" in stages:
+        dom, dom_ms = "gemm_gateup", stages["gemm_gateup"]
+        alg_bytes = n_active * (2 * I * D + 2 * I * 4) + T * K * D * 2 + T * K * I * 2
+    else:
+        dom = "gemv_gateup" if "gemv_gateup" in stages else "expert pass"
+        dom_ms = stages.get("gemv_gateup", ms / args.steps)
+        alg_bytes = n_active * (2 * I * D + 2 * I * 4) + T * D * 4 + T * K * I * 4
+    achieved = alg_bytes / (dom_ms / 1e3) / 1e9
+    line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": t_max / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f16xint8->f32",
+            "data": "synthetic", "config": dict(CONFIG, parallelism=f"replica{world}"),
+            "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": T * D * 4,
+                    "d2h_bytes_per_step": T * D * 4 + T * K * 8},
+            "gpu_launches": launches,
+            "stage_ms": stages,
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                         "frac": achieved / hbm, "traffic": None,
+                         "kernel": dom, "peak_source": src,
+                         "alg_bytes_per_launch": alg_bytes},
+            "clocks": clocks}
+    if rank == 0 and world == 1 and not args.no_cpu:
+        tps, n, kind, cores, dt = cpu_reference_tokens_per_s(pyoracle, L, args.cpu_seconds)
+        line["cpu_baseline"] = {"value": tps, "unit": UNIT, "cores": cores, "kind": kind,
+                                "sample": f"{n} of {T} tokens per call for {dt:.1f} s, "
+                                          f"engines/olmoe.c moe() OpenMP"}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    ob.shutdown()
+    if dist:
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

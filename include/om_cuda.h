@@ -144,6 +144,10 @@ const char *omc_last_error(void);
 int omc_set_profiling(int on);
 int omc_stage_times(float *ms, int n);
 
+/* Name of stage i of the last profiled forward ("router", "dispatch",
+ * "gemm_gateup", "gemm_down", "combine", "gemv_gateup", ...), or NULL. */
+const char *omc_stage_name(int i);
+
 /* Number of kernels the library launched since the last reset (a count of
  * its own launches, not of library calls it makes). */
 long long omc_launch_count(int reset);

@@ -246,3 +246,8 @@ void orc_fill_normal(uint64_t seed, float *dst, int64_t n, float sigma) {
 }
 
 float orc_expf(float x) { return expf(x); }
+
+void orc_expf_array(const float *x, float *y, int64_t n) {
+    #pragma omp parallel for schedule(static)
+    for (int64_t i = 0; i < n; i++) y[i] = expf(x[i]);
+}

@@ -75,6 +75,7 @@ void orc_fill_normal(uint64_t seed, float *dst, int64_t n, float sigma);
 /* glibc expf as called by the reference (exposed so tests can compare the
  * device restatement of the same function against it). */
 float orc_expf(float x);
+void orc_expf_array(const float *x, float *y, int64_t n);
 
 #ifdef __cplusplus
 }

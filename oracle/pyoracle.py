@@ -65,6 +65,7 @@ def lib():
         L.orc_fill_normal.argtypes = [C.c_uint64, _f32p, C.c_int64, C.c_float]
         L.orc_expf.restype = C.c_float
         L.orc_expf.argtypes = [C.c_float]
+        L.orc_expf_array.argtypes = [_f32p, _f32p, C.c_int64]
         _lib = L
     return _lib
 
@@ -85,6 +86,14 @@ def normal(seed: int, shape, sigma: float = 1.0) -> np.ndarray:
     a = np.empty(int(np.prod(shape)), np.float32)
     lib().orc_fill_normal(seed & 0xFFFFFFFFFFFFFFFF, a, a.size, sigma)
     return a.reshape(shape)
+
+
+def glibc_expf(x: np.ndarray) -> np.ndarray:
+    """The host's glibc expf, elementwise (what the reference's softmax calls)."""
+    x = np.ascontiguousarray(x, np.float32)
+    y = np.empty_like(x)
+    lib().orc_expf_array(x.ravel(), y.ravel(), x.size)
+    return y
 
 
 def quantize_py(w: np.ndarray):

@@ -60,6 +60,7 @@ SIGNATURES = {
     "omc_last_error": (C.c_char_p, []),
     "omc_set_profiling": (_i, [_i]),
     "omc_stage_times": (_i, [C.POINTER(C.c_float), _i]),
+    "omc_stage_name": (C.c_char_p, [_i]),
     "omc_launch_count": (C.c_longlong, [_i]),
     "omc_version": (C.c_char_p, []),
     "omm_init": (_i, []),
@@ -70,7 +71,17 @@ SIGNATURES = {
     "omm_dense": (_i, [_vp, _i, _i, _vp, _i, _vp]),
     # not in the public headers: failure-detection test hook
     "omc_debug_wait_timeout": (_i, []),
+    "omc_debug_expf": (_i, [_vp, _vp, C.c_longlong]),
+    "omc_debug_set_path": (_i, [_i]),
+    "omc_debug_ws_copy": (_i, [_i, _vp, _sz]),
 }
+
+PATH_AUTO, PATH_GEMV, PATH_MMA = 0, 1, 2
+
+
+def set_path(path: int) -> None:
+    """Force the expert path (tests): PATH_AUTO, PATH_GEMV or PATH_MMA."""
+    check(lib().omc_debug_set_path(path), "omc_debug_set_path")
 
 _lib = None
 
@@ -119,10 +130,11 @@ def launch_count(reset: bool = False) -> int:
     return int(lib().omc_launch_count(1 if reset else 0))
 
 
-def stage_times(n: int = 8):
+def stage_times(n: int = 12):
+    """[(stage name, ms)] of the last forward run with profiling on."""
     buf = (C.c_float * n)()
     k = lib().omc_stage_times(buf, n)
-    return [buf[i] for i in range(k)]
+    return [(lib().omc_stage_name(i).decode(), buf[i]) for i in range(k)]
 
 
 def set_profiling(on: bool) -> None:

@@ -181,8 +181,10 @@ extern "C" int omc_launch_gemv_ffn(const omc_layer_dev *L, const float *x, int T
     }
     dim3 g1(nslots, Imax_rows / OMC_TM);
     gemv_gateup_kernel<<<g1, 128, smem1, s>>>(*L, x, T, topk_idx, ws->hbuf, ldh, ws->err);
+    omc_prof_mark(s, "gemv_gateup");
     dim3 g2(T, L->D_rows / OMC_TM);
     gemv_down_combine_kernel<<<g2, 128, smem2, s>>>(*L, T, topk_idx, topk_w, ws->sg, ws->hbuf, ldh, out, ws->err);
+    omc_prof_mark(s, "gemv_down_combine");
     omc_g_launches += 2;
     return cudaGetLastError() == cudaSuccess ? 0 : OMC_ECUDA;
 }

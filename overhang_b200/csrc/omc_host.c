@@ -400,7 +400,7 @@ int omc_ws_ensure(const omc_layer *L, int T, int host_io) {
     if ((rc = ws_buf(5, (void **)&W->sg, Tz * 4))) return rc;
     if ((rc = ws_buf(6, (void **)&W->counts, (E + 4) * 4 * 3 + 64))) return rc;
     if ((rc = ws_buf(7, (void **)&W->rowinfo, R * 4))) return rc;
-    if ((rc = ws_buf(8, (void **)&W->work, (size_t)64 << 20 > R * 64 ? R * 64 : (size_t)64 << 20))) return rc;
+    if ((rc = ws_buf(8, (void **)&W->work, (size_t)omc_mma_work_items(P, (int)R) * 16))) return rc;
     if ((rc = ws_buf(9, (void **)&W->xp, (size_t)P->D_pad * R * 2))) return rc;
     if ((rc = ws_buf(10, (void **)&W->hp, Imax_pad * R * 2))) return rc;
     if ((rc = ws_buf(11, (void **)&W->ypart, Tz * (K + 1) * D * 4))) return rc;
@@ -454,6 +454,7 @@ int omc_set_profiling(int on) {
 
 int omc_stage_times(float *ms, int n) {
     if (!G.init || !G.prof_valid) return 0;
+    cudaEventSynchronize(G.ev[G.prof_nev - 1]);
     int k = 0;
     for (int i = 0; i + 1 < G.prof_nev && k < n; ++i, ++k) {
         float t = 0.f;
@@ -466,10 +467,25 @@ int omc_stage_times(float *ms, int n) {
     return k;
 }
 
-void omc_prof_mark(cudaStream_t s, int i) {
-    if (G.profiling && i < OMC_NSTAGE_EV) {
-        cudaEventRecord(G.ev[i], s);
-        G.prof_nev = i + 1;
+const char *omc_stage_name(int i) {
+    if (!G.init || i < 0 || i + 1 >= G.prof_nev) return NULL;
+    return G.prof_names[i];
+}
+
+static void prof_begin(cudaStream_t s) {
+    G.prof_nev = 0;
+    if (G.profiling) {
+        cudaEventRecord(G.ev[0], s);
+        G.prof_nev = 1;
+    }
+}
+
+/* Ends the stage `name` on stream s (profiling mode only). */
+void omc_prof_mark(cudaStream_t s, const char *name) {
+    if (G.profiling && G.prof_nev > 0 && G.prof_nev < OMC_NSTAGE_EV) {
+        cudaEventRecord(G.ev[G.prof_nev], s);
+        G.prof_names[G.prof_nev - 1] = name;
+        G.prof_nev++;
     }
 }
 
@@ -501,10 +517,10 @@ int omc_forward_device(omc_layer *L, const float *x, int T, float *out, int32_t 
     int32_t *idx = topk_idx ? topk_idx : ws->topk_idx;
     float *w = topk_w ? topk_w : ws->topk_w;
     G.prof_valid = 0;
-    omc_prof_mark(s, 0);
+    prof_begin(s);
     CK(cudaMemsetAsync(ws->counts, 0, sizeof(int) * (size_t)(L->desc.E + 4) * 3, s));
     if ((rc = omc_launch_router(&L->dev, x, T, ws, idx, w, s))) return omc_fail(rc, "router launch failed");
-    omc_prof_mark(s, 1);
+    omc_prof_mark(s, "router");
     if (use_mma(L, T)) {
         rc = omc_launch_mma_ffn(&L->dev, x, T, ws, idx, w, out, s);
         if (rc == OMC_EUNSUPPORTED && G.path_override != 2) rc = omc_launch_gemv_ffn(&L->dev, x, T, ws, idx, w, out, s);
@@ -512,7 +528,6 @@ int omc_forward_device(omc_layer *L, const float *x, int T, float *out, int32_t 
         rc = omc_launch_gemv_ffn(&L->dev, x, T, ws, idx, w, out, s);
     }
     if (rc) return omc_fail(rc, "expert FFN launch failed (%s)", omc_strerror(rc));
-    omc_prof_mark(s, 2);
     G.prof_valid = G.profiling;
     return OMC_OK;
 }
@@ -562,4 +577,47 @@ int omc_debug_wait_timeout(void) {
     if (rc) return rc;
     CK(cudaStreamSynchronize(G.stream));
     return omc_check_device_error();
+}
+
+/* Forces the expert path (0 auto, 1 CUDA-core GEMV, 2 tensor-core grouped
+ * GEMM); tests use it to run both paths on the same inputs. */
+int omc_debug_set_path(int path) {
+    if (path < 0 || path > 2) return omc_fail(OMC_EINVAL, "omc_debug_set_path: %d", path);
+    G.path_override = path;
+    return OMC_OK;
+}
+
+/* Device expf on n host inputs (test hook for the glibc-equality check). */
+int omc_debug_expf(const float *x, float *y, long long n) {
+    if (!G.init) return omc_fail(OMC_ENOINIT, "omc_debug_expf: omc_init not called");
+    if (n <= 0) return OMC_OK;
+    float *d = NULL;
+    CK(cudaMalloc((void **)&d, (size_t)n * 8));
+    CK(cudaMemcpy(d, x, (size_t)n * 4, cudaMemcpyHostToDevice));
+    int rc = omc_launch_expf_probe(d, d + n, n, G.stream);
+    if (!rc) rc = cudaStreamSynchronize(G.stream) == cudaSuccess ? OMC_OK : OMC_ECUDA;
+    if (!rc) rc = cudaMemcpy(y, d + n, (size_t)n * 4, cudaMemcpyDeviceToHost) == cudaSuccess ? OMC_OK : OMC_ECUDA;
+    cudaFree(d);
+    return rc ? omc_fail(rc, "omc_debug_expf failed") : OMC_OK;
+}
+
+/* Copies a workspace buffer of the last forward to host memory (debugging):
+ * 0 xp, 1 hp, 2 ypart, 3 rowinfo, 4 counts/offsets/fill/nwork, 5 logits. */
+int omc_debug_ws_copy(int which, void *dst, size_t bytes) {
+    if (!G.init) return omc_fail(OMC_ENOINIT, "omc_debug_ws_copy: omc_init not called");
+    const void *src = NULL;
+    switch (which) {
+    case 0: src = G.ws.xp; break;
+    case 1: src = G.ws.hp; break;
+    case 2: src = G.ws.ypart; break;
+    case 3: src = G.ws.rowinfo; break;
+    case 4: src = G.ws.counts; break;
+    case 5: src = G.ws.logits; break;
+    default: return omc_fail(OMC_EINVAL, "omc_debug_ws_copy: buffer %d", which);
+    }
+    if (!src || bytes > G.ws_bytes[which == 0 ? 9 : which == 1 ? 10 : which == 2 ? 11 : which == 3 ? 7 : which == 4 ? 6 : 2])
+        return omc_fail(OMC_EINVAL, "omc_debug_ws_copy: %zu bytes too many", bytes);
+    CK(cudaDeviceSynchronize());
+    CK(cudaMemcpy(dst, src, bytes, cudaMemcpyDeviceToHost));
+    return OMC_OK;
 }

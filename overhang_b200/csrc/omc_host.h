@@ -12,7 +12,7 @@ extern "C" {
 
 #define OMC_MAX_CHUNKS 512
 #define OMC_MAX_HOST_BLOCKS 65536
-#define OMC_NSTAGE_EV 8
+#define OMC_NSTAGE_EV 12
 
 typedef struct {
     int used;
@@ -56,6 +56,7 @@ typedef struct {
     /* profiling */
     int profiling, prof_valid, prof_nev;
     cudaEvent_t ev[OMC_NSTAGE_EV];
+    const char *prof_names[OMC_NSTAGE_EV];
     int path_override;              /* 0 auto, 1 gemv, 2 mma (OMC_FFN_PATH) */
     /* expert parallelism */
     int ep_rank, ep_world;
@@ -69,7 +70,6 @@ void *omc_slab_alloc(size_t n, int *on_host);
 omc_layer *omc_get_layer(int layer);
 int omc_ws_ensure(const omc_layer *L, int T, int host_io);
 int omc_check_device_error(void);
-void omc_prof_mark(cudaStream_t s, int i);
 int omc_forward_device(omc_layer *L, const float *x, int T, float *out, int32_t *topk_idx, float *topk_w,
                        cudaStream_t s);
 
@@ -79,6 +79,9 @@ int omc_ep_forward(omc_layer *L, const float *x, int T, float *out, int32_t *top
 void omc_ep_release(void);
 
 int omc_debug_wait_timeout(void);
+int omc_debug_expf(const float *x, float *y, long long n);
+int omc_debug_set_path(int path);
+int omc_debug_ws_copy(int which, void *dst, size_t bytes);
 
 #ifdef __cplusplus
 }

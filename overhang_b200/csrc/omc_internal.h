@@ -105,6 +105,11 @@ int omc_launch_gemv_ffn(const omc_layer_dev *L, const float *x, int T, const omc
 int omc_launch_mma_ffn(const omc_layer_dev *L, const float *x, int T, const omc_ws *ws,
                        const int32_t *topk_idx, const float *topk_w, float *out, cudaStream_t s);
 int omc_launch_test_wait(int *err, cudaStream_t s);
+long long omc_mma_work_items(const omc_layer_dev *L, int R);
+int omc_launch_expf_probe(const float *x, float *y, long long n, cudaStream_t s);
+
+/* profiling: ends the named stage on stream s (no-op unless profiling) */
+void omc_prof_mark(cudaStream_t s, const char *name);
 
 /* number of kernels launched by this library (launchers add to it) */
 extern long long omc_g_launches;

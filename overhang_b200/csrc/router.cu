@@ -200,3 +200,18 @@ extern "C" int omc_launch_router(const omc_layer_dev *L, const float *x, int T, 
     omc_g_launches += 2;
     return cudaGetLastError() == cudaSuccess ? 0 : OMC_ECUDA;
 }
+
+// Evaluates omc_expf_glibc on n inputs: lets the tests compare the device
+// restatement with the host's glibc expf bit for bit.
+namespace {
+__global__ void expf_probe_kernel(const float *__restrict__ x, float *__restrict__ y, long long n) {
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
+        y[i] = omc_expf_glibc(x[i]);
+}
+}  // namespace
+
+extern "C" int omc_launch_expf_probe(const float *x, float *y, long long n, cudaStream_t s) {
+    expf_probe_kernel<<<1184, 256, 0, s>>>(x, y, n);
+    omc_g_launches += 1;
+    return cudaGetLastError() == cudaSuccess ? 0 : OMC_ECUDA;
+}

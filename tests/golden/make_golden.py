@@ -1,0 +1,128 @@
+"""Generate the golden MoE fixtures from the REFERENCE itself.
+
+Run in a container that has the reference sources (oracle/_ref built by
+``make -C oracle``; the tiny fixture model under REF_ROOT/oracle/qwen_tiny):
+
+    python tests/golden/make_golden.py
+
+Each ``golden_*.npz`` holds the layer (int8 experts + scales, router,
+shared expert), the input x, and ``out_ref`` -- the output of the reference's
+own compiled moe() (engines/olmoe.c:344-402) or moe_step()
+(engines/qwen.c:453-495) on those inputs.  ``idx_ref``/``w_ref`` are the
+routing of the C restatement (oracle/moe_oracle.c), recorded only after its
+out matched out_ref bit for bit.  The fixtures pin the oracle where the
+reference cannot be built, and the GPU path against the reference directly.
+
+Cases:
+  olmoe_small   D=128 I=64 E=8 k=2, softmax top-k, no renorm
+  olmoe_renorm  D=128 I=96 E=12 k=3, norm_topk_prob=1
+  olmoe_ties    D=128 I=64 E=8 k=3, router rows duplicated -> exactly tied
+                probabilities, which the reference breaks by lower expert id
+  qwen_small    D=128 I=64 E=16 k=4 Is=64, int8 router, shared expert
+  qwen_tiny_l0 / qwen_tiny_l3
+                the reference's own test model (oracle/qwen_tiny,
+                tools/make_qwen_oracle.py) layers 0 and 3, quantised the way
+                stream mode runs it: experts with the converter rule
+                (tools/convert_qwen.py:23-27), router and shared expert with
+                the engine's load-time rule (engines/qwen.c:124-138,283-288)
+"""
+import ctypes as C
+import os
+import sys
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(os.path.dirname(HERE))
+sys.path.insert(0, os.path.join(ROOT, "oracle"))
+import pyoracle as P  # noqa: E402
+
+REF_ROOT = os.environ.get("REF_ROOT", "/root/reference")
+
+
+def bits_equal(a, b):
+    return a.shape == b.shape and np.array_equal(a.view(np.uint32), b.view(np.uint32))
+
+
+def save(name, L, x, out_ref, extra=None):
+    o, idx, w = P.oracle_moe(L, x)
+    assert bits_equal(o, out_ref), f"{name}: oracle differs from the reference"
+    meta = np.array([L.family, L.D, L.I, L.E, L.k, L.renorm, L.router_i8, L.has_shared, L.Is],
+                    np.int32)
+    arrays = {k: v for k, v in L.arrays.items()}
+    arrays.update(meta=meta, x=x, out_ref=out_ref, idx_ref=idx, w_ref=w)
+    if extra:
+        arrays.update(extra)
+    np.savez_compressed(os.path.join(HERE, f"golden_{name}.npz"), **arrays)
+    print(f"{name}: T={x.shape[0]} max|out|={np.abs(out_ref).max():.4f} idx[0]={idx[0]}")
+
+
+def tiny_layer(li):
+    R = P.ref_lib("qwen")
+    snap = os.path.join(REF_ROOT, "oracle", "qwen_tiny").encode()
+    R.ref_qwen_tiny_load(C.c_char_p(snap))
+    dims = (C.c_int * 7)()
+    R.ref_qwen_tiny_dims(dims)
+    D, E, K, MI, SI = dims[0], dims[1], dims[2], dims[3], dims[4]
+    f = lambda *s: np.zeros(s, np.float32)  # noqa: E731
+    gate, shg, shu, shd, shgate = f(E, D), f(SI, D), f(SI, D), f(D, SI), f(D)
+    eg, eu, ed = f(E, MI, D), f(E, MI, D), f(E, D, MI)
+    vp = lambda a: a.ctypes.data_as(C.c_void_p)  # noqa: E731
+    rc = R.ref_qwen_tiny_weights(C.c_int(li), vp(gate), vp(shg), vp(shu), vp(shd), vp(shgate),
+                                 vp(eg), vp(eu), vp(ed))
+    assert rc == 0
+    L = P.Layer(P.FAMILY_QWEN, D, MI, E, K, 1, 1, 1, SI)
+    a = L.arrays
+    a["router"], a["router_s"] = P.quantize_c(gate)
+    a["sh_g"], a["sh_gs"] = P.quantize_c(shg)
+    a["sh_u"], a["sh_us"] = P.quantize_c(shu)
+    a["sh_d"], a["sh_ds"] = P.quantize_c(shd)
+    a["sh_gate"] = shgate
+    q = [P.quantize_py(m) for m in eg]
+    a["g"], a["gs"] = np.stack([t[0] for t in q]), np.stack([t[1] for t in q])
+    q = [P.quantize_py(m) for m in eu]
+    a["u"], a["us"] = np.stack([t[0] for t in q]), np.stack([t[1] for t in q])
+    q = [P.quantize_py(m) for m in ed]
+    a["d"], a["ds"] = np.stack([t[0] for t in q]), np.stack([t[1] for t in q])
+    # the reference's own f32-resident moe_step on the same x (information only)
+    return L, R
+
+
+def main():
+    assert P.ref_available(), "build oracle/_ref first (make -C oracle)"
+    L = P.make_layer(P.FAMILY_OLMOE, 128, 64, 8, 2, seed=101)
+    x = P.normal(1001, (12, 128))
+    save("olmoe_small", L, x, P.reference_moe(L, x))
+
+    L = P.make_layer(P.FAMILY_OLMOE, 128, 96, 12, 3, seed=102, renorm=1)
+    x = P.normal(1002, (9, 128))
+    save("olmoe_renorm", L, x, P.reference_moe(L, x))
+
+    L = P.make_layer(P.FAMILY_OLMOE, 128, 64, 8, 3, seed=103)
+    r = L.arrays["router"]
+    r[5] = r[2]
+    r[6] = r[1]
+    x = P.normal(1003, (16, 128))
+    out = P.reference_moe(L, x)
+    _, idx, w = P.oracle_moe(L, x)
+    ties = sum(int(w[t, j] == w[t, j + 1]) for t in range(16) for j in range(2))
+    assert ties > 0, "tie case produced no tied selections"
+    save("olmoe_ties", L, x, out)
+
+    L = P.make_layer(P.FAMILY_QWEN, 128, 64, 16, 4, seed=104, renorm=1, router_i8=1,
+                     has_shared=1, Is=64)
+    x = P.normal(1004, (10, 128))
+    save("qwen_small", L, x, P.reference_moe(L, x))
+
+    for li in (0, 3):
+        L, R = tiny_layer(li)
+        x = P.normal(1100 + li, (8, L.D))
+        out = P.reference_moe(L, x)
+        f32 = np.zeros_like(out)
+        R.ref_qwen_tiny_moe(C.c_int(li), x.ctypes.data_as(C.c_void_p), C.c_int(x.shape[0]),
+                            f32.ctypes.data_as(C.c_void_p))
+        save(f"qwen_tiny_l{li}", L, x, out, {"out_ref_f32_resident": f32})
+
+
+if __name__ == "__main__":
+    main()
