@@ -117,6 +117,30 @@ int omc_moe_forward(int layer, const float *x, int T, float *out,
 int omc_moe_forward_dev(int layer, const float *x, int T, float *out,
                         int32_t *topk_idx, float *topk_w, void *stream);
 
+/* The same as omc_moe_forward_dev, but it allocates nothing: no cudaMalloc,
+ * cudaFree or other allocating call, on any call.  This entry has no
+ * counterpart in the reference.
+ *
+ * It is for callers that must not allocate device memory per call: an engine
+ * that has reserved its whole HBM budget up front (expert slab, KV cache) and
+ * must keep a fixed footprint, or a serving loop that may not stall in the
+ * driver's allocator between tokens.  The other forward entries grow their
+ * workspace with cudaMalloc when T grows; this one takes it from a fixed
+ * 32 MiB device array that the library holds on every GPU it is loaded on
+ * until the process exits (its address is looked up once, in omc_init).
+ *
+ * Limit: a forward whose workspace does not fit those 32 MiB is rejected with
+ * OMC_EINVAL and a message giving the largest T for the layer (for the
+ * OLMoE-shaped layer, D=2048 E=64 k=8 I=1024, T=167; for the Qwen-shaped
+ * one, E=256 I=512 with its shared expert, T=84).  The caller still
+ * passes x, out and the optional top-k buffers as device pointers.  Every call
+ * uses the same array, which keeps the previous call's contents; the counters
+ * that must start at zero are cleared on `stream` by each call.  Two calls
+ * that can run at the same time on the GPU (different streams with no
+ * ordering between them) race on the array: order them on one stream. */
+int omc_moe_forward_noalloc(int layer, const float *x, int T, float *out,
+                            int32_t *topk_idx, float *topk_w, void *stream);
+
 /* Wait for all work of the library; reports a pending device error. */
 int omc_sync(void);
 

@@ -53,6 +53,7 @@ SIGNATURES = {
     "omc_shared_set": (_i, [_i, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "omc_moe_forward": (_i, [_i, _vp, _i, _vp, _vp, _vp]),
     "omc_moe_forward_dev": (_i, [_i, _vp, _i, _vp, _vp, _vp, _vp]),
+    "omc_moe_forward_noalloc": (_i, [_i, _vp, _i, _vp, _vp, _vp, _vp]),
     "omc_sync": (_i, []),
     "omc_ep_init": (_i, [_i, _i, _vp]),
     "omc_ep_unique_id": (_i, [_vp, _sz]),

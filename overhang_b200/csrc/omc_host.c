@@ -152,6 +152,10 @@ int omc_init(int device, size_t slab_bytes) {
         slab_bytes = fr > 2 * reserve ? fr - reserve : fr / 2;
     }
     G.slab_budget = slab_bytes;
+    {
+        const int rc = omc_noalloc_setup(device);   /* static scratch address, this device */
+        if (rc) return omc_fail(rc, "omc_init: cudaGetSymbolAddress of the no-alloc scratch failed");
+    }
     G.device = device;
     G.init = 1;
     const char *p = getenv("OMC_FFN_PATH");
@@ -507,13 +511,10 @@ static int use_mma(const omc_layer *L, int T) {
     return slots >= 4LL * L->desc.E;   /* >= 4 tokens per expert on average */
 }
 
-int omc_forward_device(omc_layer *L, const float *x, int T, float *out, int32_t *topk_idx, float *topk_w,
-                       cudaStream_t s) {
+/* One forward on workspace `ws` (kernels only: no allocation here). */
+static int forward_on_ws(omc_layer *L, const omc_ws *ws, const float *x, int T, float *out, int32_t *topk_idx,
+                         float *topk_w, cudaStream_t s) {
     int rc;
-    if ((rc = layer_ready(L))) return rc;
-    if ((rc = omc_ws_ensure(L, T, 0))) return rc;
-    if (G.ep_world > 1) return omc_ep_forward(L, x, T, out, topk_idx, topk_w, s);
-    const omc_ws *ws = &G.ws;
     int32_t *idx = topk_idx ? topk_idx : ws->topk_idx;
     float *w = topk_w ? topk_w : ws->topk_w;
     G.prof_valid = 0;
@@ -530,6 +531,86 @@ int omc_forward_device(omc_layer *L, const float *x, int T, float *out, int32_t 
     if (rc) return omc_fail(rc, "expert FFN launch failed (%s)", omc_strerror(rc));
     G.prof_valid = G.profiling;
     return OMC_OK;
+}
+
+int omc_forward_device(omc_layer *L, const float *x, int T, float *out, int32_t *topk_idx, float *topk_w,
+                       cudaStream_t s) {
+    int rc;
+    if ((rc = layer_ready(L))) return rc;
+    if ((rc = omc_ws_ensure(L, T, 0))) return rc;
+    if (G.ep_world > 1) return omc_ep_forward(L, x, T, out, topk_idx, topk_w, s);
+    return forward_on_ws(L, &G.ws, x, T, out, topk_idx, topk_w, s);
+}
+
+/* ---------------------------------------------------- no-alloc forward -- */
+/* Lays out one forward's workspace inside the static device scratch
+ * (noalloc.cu).  Returns the bytes needed; fills *ws when base is given. */
+static size_t noalloc_layout(const omc_layer_dev *P, int T, char *base, omc_ws *ws) {
+    const size_t Tz = (size_t)T, D = (size_t)P->D, E = (size_t)P->E, K = (size_t)P->k;
+    const size_t Imax_rows = (size_t)(P->Is_rows > P->I_rows ? P->Is_rows : P->I_rows);
+    const size_t Imax_pad = (size_t)(P->Is_pad > P->I_pad ? P->Is_pad : P->I_pad);
+    const size_t R = (size_t)omc_round_up((int)(Tz * K + (P->has_shared ? Tz : 0) + (E + 1) * OMC_ROW_ALIGN), 128);
+    size_t off = 0;
+#define TAKE(field, type, bytes)                                     \
+    do {                                                             \
+        if (base) ws->field = (type)(base + off);                    \
+        off += ((size_t)(bytes) + 255) & ~(size_t)255;               \
+    } while (0)
+    TAKE(logits, float *, Tz * (E + 1) * 4);
+    TAKE(topk_idx, int32_t *, Tz * K * 4);
+    TAKE(topk_w, float *, Tz * K * 4);
+    TAKE(sg, float *, Tz * 4);
+    TAKE(counts, int *, (E + 4) * 4 * 3 + 64);
+    TAKE(rowinfo, int *, R * 4);
+    TAKE(work, int *, (size_t)omc_mma_work_items(P, (int)R) * 16);
+    TAKE(xp, uint16_t *, (size_t)P->D_pad * R * 2);
+    TAKE(hp, uint16_t *, Imax_pad * R * 2);
+    TAKE(ypart, float *, Tz * (K + 1) * D * 4);
+    TAKE(hbuf, float *, (Tz * K + Tz) * Imax_rows * 4);
+#undef TAKE
+    if (base) {
+        ws->offsets = ws->counts + (E + 4);
+        ws->fill = ws->counts + 2 * (E + 4);
+        ws->nwork = ws->counts + 3 * (E + 4);
+        ws->x = ws->out = NULL;
+        ws->T_cap = T;
+        ws->R_cap = (int)R;
+        ws->err = G.d_err;
+    }
+    return off;
+}
+
+int omc_moe_forward_noalloc(int layer, const float *x, int T, float *out, int32_t *topk_idx, float *topk_w,
+                            void *stream) {
+    if (!G.init) return omc_fail(OMC_ENOINIT, "omc_moe_forward_noalloc: omc_init not called");
+    omc_layer *L = omc_get_layer(layer);
+    if (!L) return omc_fail(OMC_ENOINIT, "omc_moe_forward_noalloc: layer %d not initialised", layer);
+    if (T < 0 || (T > 0 && (!x || !out))) return omc_fail(OMC_EINVAL, "omc_moe_forward_noalloc: bad T or pointers");
+    if (G.ep_world > 1)
+        return omc_fail(OMC_EUNSUPPORTED, "omc_moe_forward_noalloc: not available with expert parallelism");
+    if (T == 0) return OMC_OK;
+    int rc;
+    if ((rc = layer_ready(L))) return rc;
+    const size_t need = noalloc_layout(&L->dev, T, NULL, NULL);
+    if (need > OMC_NOALLOC_SCRATCH_BYTES) {
+        int lo = 0, hi = T;   /* largest T that fits, for the message */
+        while (lo < hi) {
+            const int mid = (lo + hi + 1) / 2;
+            if (noalloc_layout(&L->dev, mid, NULL, NULL) <= OMC_NOALLOC_SCRATCH_BYTES) lo = mid;
+            else hi = mid - 1;
+        }
+        return omc_fail(OMC_EINVAL,
+                        "omc_moe_forward_noalloc: T=%d needs %zu bytes of scratch, the static scratch holds %u; "
+                        "at most T=%d for this layer",
+                        T, need, (unsigned)OMC_NOALLOC_SCRATCH_BYTES, lo);
+    }
+    char *base = (char *)omc_noalloc_scratch_ptr(G.device);
+    if (!base) return omc_fail(OMC_ENOINIT, "omc_moe_forward_noalloc: scratch address not set up");
+    omc_ws ws;
+    memset(&ws, 0, sizeof(ws));
+    noalloc_layout(&L->dev, T, base, &ws);
+    cudaStream_t s = stream ? (cudaStream_t)stream : G.stream;
+    return forward_on_ws(L, &ws, x, T, out, topk_idx, topk_w, s);
 }
 
 int omc_moe_forward_dev(int layer, const float *x, int T, float *out, int32_t *topk_idx, float *topk_w,

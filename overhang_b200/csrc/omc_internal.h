@@ -36,6 +36,10 @@ extern "C" {
 #define OMC_ROW_ALIGN 16    /* expert row groups padded to 16 rows (UMMA N) */
 #define OMC_MAX_K 32
 #define OMC_MAX_E 1024
+#define OMC_MAX_DEVICES 64
+
+/* Size of the static device scratch behind omc_moe_forward_noalloc(). */
+#define OMC_NOALLOC_SCRATCH_BYTES (32u << 20)
 
 /* device error codes written into the error word */
 #define OMC_DEVERR_TIMEOUT 1
@@ -106,6 +110,8 @@ int omc_launch_mma_ffn(const omc_layer_dev *L, const float *x, int T, const omc_
                        const int32_t *topk_idx, const float *topk_w, float *out, cudaStream_t s);
 int omc_launch_test_wait(int *err, cudaStream_t s);
 long long omc_mma_work_items(const omc_layer_dev *L, int R);
+int omc_noalloc_setup(int device);
+void *omc_noalloc_scratch_ptr(int device);
 int omc_launch_expf_probe(const float *x, float *y, long long n, cudaStream_t s);
 
 /* profiling: ends the named stage on stream s (no-op unless profiling) */
