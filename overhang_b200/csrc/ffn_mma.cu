@@ -17,18 +17,26 @@
 //   combine out = [sigmoid gate * shared] + sum_k partial_k, in the reference's
 //           order (engines/olmoe.c:395-397, engines/qwen.c:459-462,492)
 //
-// GEMM design (one persistent CTA per SM, warp-specialised, 320 threads):
-//   warp 0      bulk-copy producer: the int8 weight K-block(s) (8 KiB per
-//               matrix, contiguous in the tiled slab) and the f16 token tile
-//               (n rows x 128 B, contiguous in the operand) into a smem ring;
-//   warp 1      TMEM allocator + single-thread tcgen05.mma issuer;
-//   warps 2..9  dequant: int8 -> f16 (exact) in registers, written straight
-//               into TMEM as the MMA's A operand (tcgen05.st), so the f16
-//               weights never round-trip through shared memory; the same
-//               warps run the epilogue (tcgen05.ld of the f32 accumulators).
-// The weight rows are the MMA's M (=128) and the tokens its N (16..128):
-// few tokens per expert still fill the tensor core's M dimension, and the
-// per-row int8 scale is one register per epilogue thread.
+// GEMM design (one persistent CTA per SM, warp-specialised, 864 threads).
+// The expert weights are the MMA's N operand (256 rows per instruction:
+// 128 gate + 128 up rows, or two 128-row tiles of the down matrix) and the
+// tokens its M (128 rows, padded): a tcgen05.mma costs ~140 cycles whatever
+// its N, so N=256 puts 4 KiB of weights through each instruction.
+//   warp 26      int8 producer: bulk-copies (no multicast) the two 8 KiB int8
+//                weight blocks of each K block into a 6-deep smem ring; the
+//                depth covers ~2 us of HBM latency at the streaming rate;
+//   warp 0       token producer: bulk-copies the f16 token tile (n rows x
+//                128 B, contiguous in the AOL operand) into a 3-deep ring;
+//   warps 2..17  dequant, two groups of 256 threads taking alternate K
+//                blocks: thread t owns weight row t, converts its 64 int8
+//                exactly to f16 and writes them 128B-swizzled into the
+//                group's f16 B tile (2-deep ring, one tile per group);
+//   warp 1       TMEM allocator + single-thread tcgen05.mma issuer
+//                (kind::f16, M=128, N=256, K=16; both operands from smem);
+//   warps 18..25 epilogue, one token row per thread (TMEM lane), two warps
+//                per lane quarter splitting the 256 columns: SwiGLU or the
+//                routing weight, from a double-buffered f32 accumulator
+//                ([128 tokens] x [256 weight rows] per buffer, 512 columns).
 //
 // Every mbarrier wait is bounded (~1 s); on expiry the CTA records
 // OMC_DEVERR_TIMEOUT, raises a shared abort flag, and all roles unwind.
@@ -36,19 +44,30 @@
 
 namespace {
 
-constexpr int NMAX = 128;                 // tokens per work item (MMA N)
-constexpr int SW = 4;                     // smem ring stages
-constexpr int SA = 4;                     // TMEM A stages
-constexpr int NTHREADS = 320;
-constexpr int W_BYTES = OMC_BLK_BYTES;    // 8 KiB int8 per matrix per stage
-constexpr int B_BYTES = NMAX * 128;       // 16 KiB f16 token tile per stage
-constexpr uint32_t TMEM_COLS = 512;
+constexpr int NMAX = 128;                 // tokens per work item (MMA M)
+constexpr int NGRP = 2;                   // dequant groups (alternate K blocks)
+constexpr int NDQ = 8;                    // warps per dequant group (256 threads = 256 weight rows)
+constexpr int NEPI = 8;                   // epilogue warps: two per TMEM lane quarter
+constexpr int SA = 3;                     // token-tile ring
+constexpr int SB = NGRP;                  // f16 weight-tile ring: one tile per dequant group
+constexpr int SI = 6;                     // int8 ring
+constexpr int WARP_DQ0 = 2;
+constexpr int WARP_EPI0 = WARP_DQ0 + NGRP * NDQ;              // 18
+constexpr int WARP_I8 = WARP_EPI0 + NEPI;                     // 26
+constexpr int NTHREADS = (WARP_I8 + 1) * 32;                  // 864
+constexpr int W_BYTES = OMC_BLK_BYTES;    // 8 KiB int8 per 128-row weight block per K block
+constexpr int A_BYTES = NMAX * 128;       // 16 KiB f16 token tile
+constexpr int B_BYTES = 256 * 128;        // 32 KiB f16 weight tile
+constexpr uint32_t TMEM_COLS = 512;       // two accumulator buffers of 256 columns
 
 // smem layout (bytes, from a 1024-aligned base)
-constexpr int OFF_B = 0;                                  // SW x B_BYTES
-constexpr int OFF_W = OFF_B + SW * B_BYTES;               // SW x 2 x W_BYTES
-constexpr int OFF_BAR = OFF_W + SW * 2 * W_BYTES;         // barriers
-constexpr int SMEM_BYTES = OFF_BAR + 256 + 1024;          // + alignment slack
+constexpr int OFF_A = 0;
+constexpr int OFF_B = OFF_A + SA * A_BYTES;
+constexpr int OFF_I8 = OFF_B + SB * B_BYTES;
+constexpr int OFF_SC = OFF_I8 + SI * 2 * W_BYTES;         // [2][256] f32 row scales of the item
+constexpr int OFF_BAR = OFF_SC + 2 * 256 * 4;
+constexpr int SMEM_BYTES = OFF_BAR + 512 + 1024;
+static_assert(SMEM_BYTES <= 227 * 1024, "smem budget");
 
 struct WorkItem {
     int g, mt, n0, n;
@@ -58,7 +77,7 @@ struct GemmArgs {
     omc_layer_dev L;
     const int4 *work;
     const int *nwork;
-    const uint16_t *act;       // B operand rows (AOL): x (gemm1) or h (gemm2)
+    const uint16_t *act;       // A operand rows (AOL): x (gemm1) or h (gemm2)
     uint16_t *hout;            // gemm1: h operand out
     float *ypart;              // gemm2: per-slot partials [T][k+1][D]
     const int *rowinfo;        // gemm2: row -> slot
@@ -83,13 +102,9 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t *bar, uint32_t parity, in
     }
 }
 
-__device__ __forceinline__ void tmem_st_32x32b_x16(uint32_t taddr, const uint32_t *v) {
-    asm volatile(
-        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
-        "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
-        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]),
-        "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
-        : "memory");
+__device__ __forceinline__ bool warp_wait(uint64_t *bar, uint32_t parity, int *err, int site,
+                                          volatile int *abort_flag) {
+    return __all_sync(0xffffffffu, wait_or_abort(bar, parity, err, site, abort_flag));
 }
 
 __device__ __forceinline__ uint32_t f32x2_to_f16x2_sat(float lo, float hi) {
@@ -104,36 +119,129 @@ __device__ __forceinline__ float swiglu_f(int family, float g, float u) {
     return __fdividef(g, 1.f + e) * u;
 }
 
-// Byte offset of element (row, k) in an AOL operand with R rows.
-__device__ __forceinline__ size_t aol_off(int R, int row, int k) {
-    return (size_t)(k >> 6) * R * 128 + (size_t)row * 128 + ((((k & 63) >> 3) ^ (row & 7)) << 4) + ((k & 7) << 1);
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
+
+// D[tmem] (+)= A[smem desc] * B[smem desc]^T, kind::f16, f32 accumulate.
+__device__ __forceinline__ void tc_mma_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                          uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// The 128-row weight blocks an item multiplies: phase 1 = gate tile mt and up
+// tile mt; phase 2 = down tiles 2*mt and 2*mt+1 (the second absent past D_rows).
+template <int PHASE>
+__device__ __forceinline__ int item_nmat(const omc_layer_dev &L, const WorkItem &it) {
+    if (PHASE == 1) return 2;
+    return (2 * it.mt + 1) * OMC_TM < L.D_rows ? 2 : 1;
+}
+
+template <int PHASE>
+struct Ctx {
+    const GemmArgs &a;
+    __device__ WorkItem item(int idx) const {
+        const int4 v = a.work[idx];
+        return WorkItem{v.x, v.y, v.z, v.w};
+    }
+    __device__ bool ok(const WorkItem &it) const {
+        const omc_layer_dev &L = a.L;
+        if (it.g < 0 || it.g > L.E || (it.g == L.E && !L.has_shared)) return false;
+        if (it.n <= 0 || it.n > NMAX || (it.n & 15) || it.n0 < 0 || it.n0 + it.n > a.R || (it.n0 & 15)) return false;
+        if (PHASE == 1) return it.mt >= 0 && it.mt * OMC_TM < (it.g == L.E ? L.Is_rows : L.I_rows);
+        return it.mt >= 0 && 2 * it.mt * OMC_TM < L.D_rows;
+    }
+    __device__ int nkb(const WorkItem &it) const {
+        if (PHASE == 1) return a.L.D_pad / OMC_KB;
+        return (it.g == a.L.E ? a.L.Is_pad : a.L.I_pad) / OMC_KB;
+    }
+    // first int8 byte of weight block `mat` (0/1) of the item, K block 0
+    __device__ const int8_t *wbase(const WorkItem &it, int mat) const {
+        const omc_expert_ptrs P = a.L.experts[it.g];
+        const int n = nkb(it);
+        if (PHASE == 1) return (mat ? P.u : P.g) + (size_t)it.mt * n * W_BYTES;
+        return P.d + (size_t)(2 * it.mt + mat) * n * W_BYTES;
+    }
+};
+
+// Walks this CTA's (item, K block) stages in order.
+template <int PHASE>
+struct StageIter {
+    int idx, kb, nkb, nmat, nitems, stride;
+    const int8_t *w0, *w1;
+    bool valid;
+    __device__ void load_item(const Ctx<PHASE> &c) {
+        valid = idx < nitems;
+        if (!valid) return;
+        const WorkItem it = c.item(idx);
+        if (!c.ok(it)) {
+            valid = false;
+            return;
+        }
+        nkb = c.nkb(it);
+        nmat = item_nmat<PHASE>(c.a.L, it);
+        w0 = c.wbase(it, 0);
+        w1 = nmat > 1 ? c.wbase(it, 1) : w0;
+    }
+    __device__ void init(const Ctx<PHASE> &c, int first, int n, int cta_stride) {
+        idx = first;
+        nitems = n;
+        stride = cta_stride;
+        kb = 0;
+        load_item(c);
+    }
+    __device__ void step(const Ctx<PHASE> &c) {
+        if (!valid) return;
+        if (++kb >= nkb) {
+            kb = 0;
+            idx += stride;
+            load_item(c);
+        }
+    }
+};
 
 template <int PHASE>   // 1: gate/up + SwiGLU, 2: down + weighting
 __global__ void __launch_bounds__(NTHREADS, 1) moe_gemm_kernel(const GemmArgs a) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint64_t *full_w = reinterpret_cast<uint64_t *>(smem + OFF_BAR);   // [SW]
-    uint64_t *empty_w = full_w + SW;                                   // [SW]
-    uint64_t *afull = empty_w + SW;                                    // [SA]
-    uint64_t *aempty = afull + SA;                                     // [SA]
-    uint64_t *accfull = aempty + SA;                                   // [1]
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(accfull + 1);
+    uint64_t *fullA = reinterpret_cast<uint64_t *>(smem + OFF_BAR);   // [SA] token tile landed
+    uint64_t *emptyA = fullA + SA;                                    // [SA] its MMAs done
+    uint64_t *fullB = emptyA + SA;                                    // [SB] f16 weight tile written
+    uint64_t *emptyB = fullB + SB;                                    // [SB] its MMAs done
+    uint64_t *fullI = emptyB + SB;                                    // [SI] int8 blocks landed
+    uint64_t *emptyI = fullI + SI;                                    // [SI] int8 slot read
+    uint64_t *accfull = emptyI + SI;                                  // [2]
+    uint64_t *accempty = accfull + 2;                                 // [2]
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(accempty + 2);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    constexpr int NDQ = 8;   // dequant warps
+    const Ctx<PHASE> c{a};
+    const omc_layer_dev &L = a.L;
+    const int nitems = a.nwork[PHASE - 1];
 
     if (threadIdx.x == 0) {
-        for (int i = 0; i < SW; ++i) {
-            mbar_init(&full_w[i], 1);
-            mbar_init(&empty_w[i], NDQ + 1);
-        }
         for (int i = 0; i < SA; ++i) {
-            mbar_init(&afull[i], NDQ);
-            mbar_init(&aempty[i], 1);
+            mbar_init(&fullA[i], 1);
+            mbar_init(&emptyA[i], 1);
         }
-        mbar_init(accfull, 1);
+        for (int i = 0; i < SB; ++i) {
+            mbar_init(&fullB[i], NDQ);
+            mbar_init(&emptyB[i], 1);
+        }
+        for (int i = 0; i < SI; ++i) {
+            mbar_init(&fullI[i], 1);
+            mbar_init(&emptyI[i], NDQ);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&accfull[i], 1);
+            mbar_init(&accempty[i], NEPI);
+        }
         *abort_flag = 0;
         fence_barrier_init();
     }
@@ -143,214 +251,227 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_gemm_kernel(const GemmArgs a)
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
-    const int nitems = a.nwork[PHASE - 1];
-    const omc_layer_dev &L = a.L;
-    constexpr int NMAT = PHASE == 1 ? 2 : 1;
-    // TMEM columns: accumulators at 0 (gate) and NMAX (up) / 0 (down); A stages from 256
-    constexpr uint32_t ACOL0 = 256;
-    constexpr uint32_t ACOLS_PER_STAGE = 32 * NMAT;
-
-    auto item_at = [&](int idx) -> WorkItem {
-        const int4 v = a.work[idx];
-        return WorkItem{v.x, v.y, v.z, v.w};
-    };
-    auto item_ok = [&](const WorkItem &it) -> bool {
-        if (it.g < 0 || it.g > L.E || (it.g == L.E && !L.has_shared)) return false;
-        if (it.n <= 0 || it.n > NMAX || (it.n & 15) || it.n0 < 0 || it.n0 + it.n > a.R || (it.n0 & 15)) return false;
-        const int rows = PHASE == 1 ? (it.g == L.E ? L.Is_rows : L.I_rows) : L.D_rows;
-        return it.mt >= 0 && it.mt * OMC_TM < rows;
-    };
-    auto nkb_of = [&](const WorkItem &it) -> int {
-        if (PHASE == 1) return L.D_pad / OMC_KB;
-        return (it.g == L.E ? L.Is_pad : L.I_pad) / OMC_KB;
-    };
-
     if (warp == 0) {
-        // ------------------------------------------------ producer
+        // ------------------------------------------------ token-tile producer
         if (lane == 0) {
-            uint32_t it_count = 0;
+            uint32_t i = 0;
             for (int idx = blockIdx.x; idx < nitems && !*abort_flag; idx += gridDim.x) {
-                const WorkItem it = item_at(idx);
-                if (!item_ok(it)) {
+                const WorkItem it = c.item(idx);
+                if (!c.ok(it)) {
                     omc_dev_error(a.err, OMC_DEVERR_BOUNDS, OMC_SITE_GEMM_PRODUCER, idx);
                     *abort_flag = 1;
                     break;
                 }
-                const omc_expert_ptrs P = L.experts[it.g];
-                const int nkb = nkb_of(it);
-                const int8_t *w0 = PHASE == 1 ? P.g : P.d;
-                const int8_t *w1 = P.u;
-                const size_t tile = (size_t)it.mt * nkb * W_BYTES;
-                const uint32_t bbytes = (uint32_t)it.n * 128;
-                for (int kb = 0; kb < nkb; ++kb, ++it_count) {
-                    const int s = it_count % SW;
-                    const uint32_t ph = (it_count / SW) & 1;
-                    if (!wait_or_abort(&empty_w[s], ph ^ 1, a.err, OMC_SITE_GEMM_PRODUCER, abort_flag)) break;
-                    mbar_arrive_expect_tx(&full_w[s], NMAT * W_BYTES + bbytes);
-                    uint8_t *sw = smem + OFF_W + s * 2 * W_BYTES;
-                    bulk_g2s(sw, w0 + tile + (size_t)kb * W_BYTES, W_BYTES, &full_w[s]);
-                    if (NMAT == 2) bulk_g2s(sw + W_BYTES, w1 + tile + (size_t)kb * W_BYTES, W_BYTES, &full_w[s]);
+                const int nkb = c.nkb(it);
+                const uint32_t bytes = (uint32_t)it.n * 128;
+                for (int kb = 0; kb < nkb; ++kb, ++i) {
+                    const int sa = i % SA;
+                    if (!wait_or_abort(&emptyA[sa], ((i / SA) & 1) ^ 1, a.err, OMC_SITE_GEMM_PRODUCER, abort_flag))
+                        break;
+                    mbar_arrive_expect_tx(&fullA[sa], bytes);
                     const uint8_t *src = reinterpret_cast<const uint8_t *>(a.act) + (size_t)kb * a.R * 128 +
                                          (size_t)it.n0 * 128;
-                    bulk_g2s(smem + OFF_B + s * B_BYTES, src, bbytes, &full_w[s]);
+                    bulk_g2s(smem + OFF_A + sa * A_BYTES, src, bytes, &fullA[sa]);
                 }
+            }
+        }
+    } else if (warp == WARP_I8) {
+        // ------------------------------------------------ int8 weight producer
+        if (lane == 0) {
+            StageIter<PHASE> it;
+            it.init(c, blockIdx.x, nitems, gridDim.x);
+            for (uint32_t i = 0; it.valid && !*abort_flag; ++i) {
+                const int si = i % SI;
+                if (!wait_or_abort(&emptyI[si], ((i / SI) & 1) ^ 1, a.err, OMC_SITE_GEMM_PRODUCER, abort_flag))
+                    break;
+                mbar_arrive_expect_tx(&fullI[si], it.nmat * W_BYTES);
+                uint8_t *dst = smem + OFF_I8 + si * 2 * W_BYTES;
+                bulk_g2s(dst, it.w0 + (size_t)it.kb * W_BYTES, W_BYTES, &fullI[si]);
+                if (it.nmat > 1) bulk_g2s(dst + W_BYTES, it.w1 + (size_t)it.kb * W_BYTES, W_BYTES, &fullI[si]);
+                it.step(c);
             }
         }
     } else if (warp == 1) {
         // ------------------------------------------------ MMA issuer
         if (lane == 0) {
-            uint32_t it_count = 0, a_count = 0, item_count = 0;
-            for (int idx = blockIdx.x; idx < nitems && !*abort_flag; idx += gridDim.x, ++item_count) {
-                const WorkItem it = item_at(idx);
-                if (!item_ok(it)) break;
-                const int nkb = nkb_of(it);
-                const uint32_t idesc = tc_idesc_f16(128, it.n);
+            uint32_t i = 0, ci = 0;
+            for (int idx = blockIdx.x; idx < nitems && !*abort_flag; idx += gridDim.x, ++ci) {
+                const WorkItem it = c.item(idx);
+                if (!c.ok(it)) break;
+                const int nkb = c.nkb(it);
+                const uint32_t idesc = tc_idesc_f16(NMAX, 128 * item_nmat<PHASE>(L, it));
+                const int b = ci & 1;
+                if (!wait_or_abort(&accempty[b], ((ci >> 1) & 1) ^ 1, a.err, OMC_SITE_GEMM_MMA, abort_flag)) break;
+                tc_fence_after();
+                const uint32_t dcol = (uint32_t)b * 256;
                 bool ok = true;
-                for (int kb = 0; kb < nkb && ok; ++kb, ++it_count, ++a_count) {
-                    const int s = it_count % SW;
-                    const uint32_t ph = (it_count / SW) & 1;
-                    const int as = a_count % SA;
-                    const uint32_t aph = (a_count / SA) & 1;
-                    ok = wait_or_abort(&full_w[s], ph, a.err, OMC_SITE_GEMM_MMA, abort_flag) &&
-                         wait_or_abort(&afull[as], aph, a.err, OMC_SITE_GEMM_MMA, abort_flag);
+                for (int kb = 0; kb < nkb; ++kb, ++i) {
+                    const int sa = i % SA, sb = i % SB;
+                    ok = wait_or_abort(&fullA[sa], (i / SA) & 1, a.err, OMC_SITE_GEMM_MMA, abort_flag) &&
+                         wait_or_abort(&fullB[sb], (i / SB) & 1, a.err, OMC_SITE_GEMM_MMA, abort_flag);
                     if (!ok) break;
                     tc_fence_after();
-                    const uint32_t bsm = smem_u32(smem + OFF_B + s * B_BYTES);
+                    const uint64_t ad = tc_sdesc_k_sw128(smem_u32(smem + OFF_A + sa * A_BYTES));
+                    const uint64_t bd = tc_sdesc_k_sw128(smem_u32(smem + OFF_B + sb * B_BYTES));
 #pragma unroll
-                    for (int k16 = 0; k16 < 4; ++k16) {
-                        const uint64_t bd = tc_sdesc_k_sw128(bsm + k16 * 32);
-                        const uint32_t acc = (kb > 0 || k16 > 0) ? 1u : 0u;
-                        const uint32_t acol = ACOL0 + as * ACOLS_PER_STAGE + k16 * 8;
-                        tc_mma_ts(tmem + 0, tmem + acol, bd, idesc, acc);
-                        if (NMAT == 2) tc_mma_ts(tmem + NMAX, tmem + acol + 32, bd, idesc, acc);
-                    }
-                    tc_commit(&empty_w[s]);
-                    tc_commit(&aempty[as]);
+                    for (int k16 = 0; k16 < 4; ++k16)   // +32 B along K = +2 in the descriptor's 16-byte units
+                        tc_mma_ss(tmem + dcol, ad + 2 * k16, bd + 2 * k16, idesc, (kb > 0 || k16 > 0) ? 1u : 0u);
+                    tc_commit(&emptyA[sa]);
+                    tc_commit(&emptyB[sb]);
                 }
                 if (!ok) break;
-                tc_commit(accfull);
+                tc_commit(&accfull[b]);
             }
         }
-    } else {
-        // ------------------------------------------------ dequant + epilogue (warps 2..9)
-        const int dq = warp - 2;                 // 0..7
-        const int q = warp & 3;                  // TMEM lane quarter this warp may access
-        const int half = dq >> 2;                // 0/1: gate/up (phase 1) or K half (phase 2)
-        const int row = q * 32 + lane;           // weight row within the 128-row tile
-        const uint32_t lane_bits = (uint32_t)(q * 32) << 16;
-        uint32_t it_count = 0, a_count = 0, item_count = 0;
-        for (int idx = blockIdx.x; idx < nitems && !*abort_flag; idx += gridDim.x, ++item_count) {
-            const WorkItem it = item_at(idx);
-            if (!item_ok(it)) break;
-            const int nkb = nkb_of(it);
-            bool ok = true;
-            for (int kb = 0; kb < nkb; ++kb, ++it_count, ++a_count) {
-                const int s = it_count % SW;
-                const uint32_t ph = (it_count / SW) & 1;
-                const int as = a_count % SA;
-                const uint32_t aph = (a_count / SA) & 1;
-                ok = __all_sync(0xffffffffu, wait_or_abort(&full_w[s], ph, a.err, OMC_SITE_GEMM_DEQUANT, abort_flag));
-                if (!ok) break;
-                const uint8_t *sw = smem + OFF_W + s * 2 * W_BYTES;
-                uint4 raw[4];
-                if (PHASE == 1) {
-                    const uint8_t *m = sw + half * W_BYTES;
+    } else if (warp < WARP_EPI0) {
+        // ------------------------------------------------ dequant: int8 ring -> f16 B tile
+        const int dq = warp - WARP_DQ0;
+        const int grp = dq / NDQ;                // K blocks i with i % NGRP == grp, B tile `grp`
+        const int t = (dq % NDQ) * 32 + lane;    // weight row of the B tile, 0..255
+        const int mat = t >> 7, r = t & 127;
+        uint8_t *brow = smem + OFF_B + grp * B_BYTES + (uint32_t)(t >> 3) * 1024 + (uint32_t)(t & 7) * 128;
+        StageIter<PHASE> pr;
+        pr.init(c, blockIdx.x, nitems, gridDim.x);
+        for (int j = 0; j < grp; ++j) pr.step(c);
+        for (uint32_t i = grp; pr.valid && !*abort_flag; i += NGRP) {
+            const int si = i % SI;
+            if (!warp_wait(&fullI[si], (i / SI) & 1, a.err, OMC_SITE_GEMM_DEQUANT, abort_flag)) break;
+            uint4 f[8];
+            const bool active = mat < pr.nmat;
+            if (active) {
+                const uint8_t *m = smem + OFF_I8 + si * 2 * W_BYTES + mat * W_BYTES;
 #pragma unroll
-                    for (int c = 0; c < 4; ++c) raw[c] = *reinterpret_cast<const uint4 *>(m + (c * 128 + row) * 16);
-                } else {
-#pragma unroll
-                    for (int c = 0; c < 2; ++c)
-                        raw[c] = *reinterpret_cast<const uint4 *>(sw + ((2 * half + c) * 128 + row) * 16);
+                for (int cc = 0; cc < 4; ++cc) {
+                    const uint4 q = *reinterpret_cast<const uint4 *>(m + (cc * 128 + r) * 16);
+                    i8x4_to_f16x4(q.x, f[2 * cc].x, f[2 * cc].y);
+                    i8x4_to_f16x4(q.y, f[2 * cc].z, f[2 * cc].w);
+                    i8x4_to_f16x4(q.z, f[2 * cc + 1].x, f[2 * cc + 1].y);
+                    i8x4_to_f16x4(q.w, f[2 * cc + 1].z, f[2 * cc + 1].w);
                 }
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&empty_w[s]);
-                ok = __all_sync(0xffffffffu, wait_or_abort(&aempty[as], aph ^ 1, a.err, OMC_SITE_GEMM_DEQUANT, abort_flag));
-                if (!ok) break;
-                uint32_t v[32];
-                const int nchunk = PHASE == 1 ? 4 : 2;
-#pragma unroll
-                for (int c = 0; c < nchunk; ++c) {
-                    i8x4_to_f16x4(raw[c].x, v[8 * c + 0], v[8 * c + 1]);
-                    i8x4_to_f16x4(raw[c].y, v[8 * c + 2], v[8 * c + 3]);
-                    i8x4_to_f16x4(raw[c].z, v[8 * c + 4], v[8 * c + 5]);
-                    i8x4_to_f16x4(raw[c].w, v[8 * c + 6], v[8 * c + 7]);
-                }
-                const uint32_t acol = ACOL0 + as * ACOLS_PER_STAGE;
-                if (PHASE == 1) {
-                    tmem_st_32x32b_x32(tmem + lane_bits + acol + half * 32, *reinterpret_cast<uint32_t(*)[32]>(v));
-                } else {
-                    tmem_st_32x32b_x16(tmem + lane_bits + acol + half * 16, v);
-                }
-                tc_wait_st();
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&afull[as]);
             }
-            if (!ok) break;
-            // ---- epilogue of this item
-            if (!__all_sync(0xffffffffu, wait_or_abort(accfull, item_count & 1, a.err, OMC_SITE_GEMM_EPILOGUE, abort_flag)))
-                break;
+            // The slot is released only after the converted values exist: an
+            // arrive issued while the ld.shared above is still in flight does
+            // not keep the next bulk copy (async proxy) from overwriting the
+            // bytes before they are read.
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&emptyI[si]);
+            if (!warp_wait(&emptyB[grp], ((i / NGRP) & 1) ^ 1, a.err, OMC_SITE_GEMM_DEQUANT, abort_flag)) break;
+            if (active) {
+#pragma unroll
+                for (int j = 0; j < 8; ++j) *reinterpret_cast<uint4 *>(brow + ((j ^ (t & 7)) << 4)) = f[j];
+            }
+            fence_proxy_async_smem();      // generic stores -> visible to the tensor core
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&fullB[grp]);
+            for (int j = 0; j < NGRP; ++j) pr.step(c);
+        }
+    } else {
+        // ------------------------------------------------ epilogue: one token row per thread
+        const int e = warp - WARP_EPI0;          // 0..7
+        const int q = warp & 3;                  // TMEM lane quarter
+        const int half = e >> 2;                 // which half of the 256 columns
+        const int trow = q * 32 + lane;          // token row within the item = TMEM lane
+        const uint32_t lane_bits = (uint32_t)(q * 32) << 16;
+        uint32_t ci = 0;
+        for (int idx = blockIdx.x; idx < nitems && !*abort_flag; idx += gridDim.x, ++ci) {
+            const WorkItem it = c.item(idx);
+            if (!c.ok(it)) break;
+            const int b = ci & 1;
+            if (!warp_wait(&accfull[b], (ci >> 1) & 1, a.err, OMC_SITE_GEMM_EPILOGUE, abort_flag)) break;
             tc_fence_after();
+            const uint32_t acc = tmem + lane_bits + (uint32_t)b * 256;
             const omc_expert_ptrs P = L.experts[it.g];
-            const int grow = it.mt * OMC_TM + row;            // weight row (I or D index)
+            const bool live = trow < it.n;
+            const int row = it.n0 + trow;        // operand row of this token slot
+            // the item's 256 weight-row scales -> smem (one load round trip per item)
+            float *sc = reinterpret_cast<float *>(smem + OFF_SC) + b * 256;
+            {
+                const int j = e * 32 + lane;     // 0..255
+                float v = 0.f;
+                if (PHASE == 1) {
+                    const int Iw = it.g == L.E ? L.Is : L.I;
+                    const int f = it.mt * OMC_TM + (j & 127);
+                    if (f < Iw) v = j < 128 ? P.gs[f] : P.us[f];
+                } else {
+                    const int d = 2 * it.mt * OMC_TM + j;
+                    if (d < L.D) v = P.ds[d];
+                }
+                sc[j] = v;
+                asm volatile("bar.sync 1, %0;" ::"n"(NEPI * 32) : "memory");
+            }
             if (PHASE == 1) {
-                // rows in [Iw, K-extent of the down GEMM) are written as zeros so
-                // the padded K columns of the h operand are finite
                 const int Iw = it.g == L.E ? L.Is : L.I;
                 const int Iw_pad = it.g == L.E ? L.Is_pad : L.I_pad;
-                const float gsc = grow < Iw ? P.gs[grow] : 0.f;
-                const float usc = grow < Iw ? P.us[grow] : 0.f;
-                for (int c16 = half; c16 < it.n / 16; c16 += 2) {
+                uint8_t *hrow = reinterpret_cast<uint8_t *>(a.hout) + (size_t)row * 128;
+#pragma unroll 1
+                for (int j0 = half * 64; j0 < half * 64 + 64; j0 += 16) {
+                    const int f0 = it.mt * OMC_TM + j0;              // first feature of the chunk
                     uint32_t gv[16], uv[16];
-                    tmem_ld_32x32b_x16(tmem + lane_bits + 0 + c16 * 16, gv);
-                    tmem_ld_32x32b_x16(tmem + lane_bits + NMAX + c16 * 16, uv);
+                    tmem_ld_32x32b_x16(acc + j0, gv);
+                    tmem_ld_32x32b_x16(acc + 128 + j0, uv);
                     tc_wait_ld();
-                    if (grow < Iw_pad) {
+                    uint32_t hv[8];
 #pragma unroll
-                        for (int j = 0; j < 16; ++j) {
-                            float h = 0.f;
-                            if (grow < Iw) {
-                                const float g = __uint_as_float(gv[j]) * gsc;
-                                const float u = __uint_as_float(uv[j]) * usc;
-                                h = swiglu_f(L.family, g, u);
-                            }
-                            const int r = it.n0 + c16 * 16 + j;
-                            const uint32_t hb = f32x2_to_f16x2_sat(h, 0.f) & 0xFFFFu;
-                            *reinterpret_cast<uint16_t *>(reinterpret_cast<uint8_t *>(a.hout) + aol_off(a.R, r, grow)) =
-                                (uint16_t)hb;
-                        }
+                    for (int jj = 0; jj < 16; jj += 2) {
+                        const float h0 = f0 + jj < Iw ? swiglu_f(L.family, __uint_as_float(gv[jj]) * sc[j0 + jj],
+                                                                  __uint_as_float(uv[jj]) * sc[128 + j0 + jj])
+                                                       : 0.f;
+                        const float h1 = f0 + jj + 1 < Iw
+                                             ? swiglu_f(L.family, __uint_as_float(gv[jj + 1]) * sc[j0 + jj + 1],
+                                                        __uint_as_float(uv[jj + 1]) * sc[128 + j0 + jj + 1])
+                                             : 0.f;
+                        hv[jj >> 1] = f32x2_to_f16x2_sat(h0, h1);
+                    }
+                    if (live && f0 < Iw_pad) {
+                        uint8_t *kbase = hrow + (size_t)(f0 >> 6) * a.R * 128;
+                        const int cb = (f0 & 63) >> 3;
+                        *reinterpret_cast<uint4 *>(kbase + ((cb ^ (row & 7)) << 4)) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
+                        *reinterpret_cast<uint4 *>(kbase + (((cb + 1) ^ (row & 7)) << 4)) =
+                            make_uint4(hv[4], hv[5], hv[6], hv[7]);
                     }
                 }
             } else {
-                const float dsc = grow < L.D ? P.ds[grow] : 0.f;
                 const int K = L.k;
-                for (int c16 = half; c16 < it.n / 16; c16 += 2) {
-                    uint32_t yv[16];
-                    tmem_ld_32x32b_x16(tmem + lane_bits + c16 * 16, yv);
-                    tc_wait_ld();
-                    if (grow < L.D) {
+                const int nmat = item_nmat<PHASE>(L, it);
+                int slot = -1;
+                float w = 1.f;
+                if (live) {
+                    slot = a.rowinfo[row];
+                    if (slot >= 0 && slot < a.T * K) w = a.topk_w[slot];
+                }
+                float *dst = nullptr;
+                if (slot >= 0) {
+                    const int tk = slot < a.T * K ? slot / K : slot - a.T * K;
+                    const int kk = slot < a.T * K ? slot - tk * K : K;
+                    dst = a.ypart + ((size_t)tk * (K + 1) + kk) * L.D;
+                }
+                const bool shared_row = slot >= a.T * K;
+                if (half < nmat) {
+#pragma unroll 1
+                    for (int j0 = half * 128; j0 < half * 128 + 128; j0 += 16) {
+                        const int d0 = 2 * it.mt * OMC_TM + j0;      // first output row of the chunk
+                        uint32_t yv[16];
+                        tmem_ld_32x32b_x16(acc + j0, yv);
+                        tc_wait_ld();
+                        float o[16];
 #pragma unroll
-                        for (int j = 0; j < 16; ++j) {
-                            const int slot = a.rowinfo[it.n0 + c16 * 16 + j];
-                            if (slot < 0) continue;
-                            const float y = __fmul_rn(__uint_as_float(yv[j]), dsc);   // matmul_q: acc * scale
-                            size_t dst;
-                            float p;
-                            if (slot < a.T * K) {
-                                const int t = slot / K, kk = slot - t * K;
-                                p = __fmul_rn(a.topk_w[slot], y);                    // w * hh
-                                dst = ((size_t)t * (K + 1) + kk) * L.D + grow;
-                            } else {
-                                const int t = slot - a.T * K;
-                                p = y;
-                                dst = ((size_t)t * (K + 1) + K) * L.D + grow;
-                            }
-                            a.ypart[dst] = p;
+                        for (int jj = 0; jj < 16; ++jj) {
+                            const float y = __fmul_rn(__uint_as_float(yv[jj]), sc[j0 + jj]);   // matmul_q: acc * scale
+                            o[jj] = shared_row ? y : __fmul_rn(w, y);                         // w * hh
+                        }
+                        if (dst && d0 < L.D) {
+#pragma unroll
+                            for (int jj = 0; jj < 16; jj += 4)
+                                if (d0 + jj < L.D)
+                                    *reinterpret_cast<float4 *>(dst + d0 + jj) =
+                                        make_float4(o[jj], o[jj + 1], o[jj + 2], o[jj + 3]);
                         }
                     }
                 }
             }
             tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&accempty[b]);
         }
     }
 
@@ -381,7 +502,7 @@ __global__ void __launch_bounds__(1024) plan_kernel(const int *__restrict__ coun
         const int nch = (pad + NMAX - 1) / NMAX;
         const int mt1 = (g < E ? I_rows : Is_rows) / OMC_TM;
         s_w1[g] = nch * mt1;
-        s_w2[g] = nch * (D_rows / OMC_TM);
+        s_w2[g] = nch * ((D_rows / OMC_TM + 1) / 2);
         fill[g] = 0;
     }
     __syncthreads();
@@ -416,7 +537,7 @@ __global__ void __launch_bounds__(1024) plan_kernel(const int *__restrict__ coun
         const int pad = s_pad[g];
         if (!pad) continue;
         const int nch = (pad + NMAX - 1) / NMAX;
-        const int mt1 = (g < E ? I_rows : Is_rows) / OMC_TM, mt2 = D_rows / OMC_TM;
+        const int mt1 = (g < E ? I_rows : Is_rows) / OMC_TM, mt2 = (D_rows / OMC_TM + 1) / 2;
         int p1 = s_w1[g], p2 = s_w2[g];
         for (int c = 0; c < nch; ++c) {
             const int n0 = s_off[g] + c * NMAX;
@@ -519,7 +640,7 @@ extern "C" long long omc_mma_work_items(const omc_layer_dev *L, int R) {
     const int G = L->E + (L->has_shared ? 1 : 0);
     const int Imax_rows = L->has_shared && L->Is_rows > L->I_rows ? L->Is_rows : L->I_rows;
     const long long chunks_max = R / NMAX + G;
-    return chunks_max * (Imax_rows / OMC_TM) + chunks_max * (L->D_rows / OMC_TM);
+    return chunks_max * (Imax_rows / OMC_TM) + chunks_max * ((L->D_rows / OMC_TM + 1) / 2);
 }
 
 extern "C" int omc_launch_mma_ffn(const omc_layer_dev *L, const float *x, int T, const omc_ws *ws,
@@ -543,7 +664,7 @@ extern "C" int omc_launch_mma_ffn(const omc_layer_dev *L, const float *x, int T,
     const int Imax_rows = L->has_shared && L->Is_rows > L->I_rows ? L->Is_rows : L->I_rows;
     const int chunks_max = R / NMAX + G;
     const int cap1 = chunks_max * (Imax_rows / OMC_TM);
-    const int cap2 = chunks_max * (L->D_rows / OMC_TM);
+    const int cap2 = chunks_max * ((L->D_rows / OMC_TM + 1) / 2);
     int4 *work1 = reinterpret_cast<int4 *>(ws->work);
     int4 *work2 = work1 + cap1;
     plan_kernel<<<1, 1024, 0, s>>>(ws->counts, E, L->has_shared, T, L->I_rows, L->Is_rows, L->D_rows, R, cap1, cap2,

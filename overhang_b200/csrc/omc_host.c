@@ -521,7 +521,7 @@ static int forward_on_ws(omc_layer *L, const omc_ws *ws, const float *x, int T, 
     prof_begin(s);
     CK(cudaMemsetAsync(ws->counts, 0, sizeof(int) * (size_t)(L->desc.E + 4) * 3, s));
     if ((rc = omc_launch_router(&L->dev, x, T, ws, idx, w, s))) return omc_fail(rc, "router launch failed");
-    omc_prof_mark(s, "router");
+    omc_prof_mark(s, "router_select");
     if (use_mma(L, T)) {
         rc = omc_launch_mma_ffn(&L->dev, x, T, ws, idx, w, out, s);
         if (rc == OMC_EUNSUPPORTED && G.path_override != 2) rc = omc_launch_gemv_ffn(&L->dev, x, T, ws, idx, w, out, s);

@@ -52,6 +52,20 @@ def test_olmoe_full_shape_parity(gpu, oracle, path, T):
     assert_close(out, ro, what=f"olmoe T={T}/{path}")
 
 
+@pytest.mark.parametrize("T", [1, 5, 200])
+def test_repeat_is_bit_identical(gpu, oracle, path, T):
+    """Eight forwards of the same input give bit-identical outputs.  A race
+    between the pipeline's producer and consumer roles shows up here first:
+    at small T each CTA streams many K blocks through the rings while the
+    epilogue has little to do."""
+    L = olmoe_full()
+    m = gpu.MoELayer.from_oracle_layer(next_layer_id(), L)
+    x = oracle.normal(7300 + T, (T, L.D))
+    first = m.forward(x)[0]
+    for _ in range(7):
+        assert np.array_equal(m.forward(x)[0].view(np.uint32), first.view(np.uint32)), "not deterministic"
+
+
 @pytest.mark.parametrize("T", [1, 48])
 def test_qwen_full_shape_parity(gpu, oracle, path, T):
     L = qwen_full()
