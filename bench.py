@@ -62,54 +62,119 @@ def peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
-    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
-              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-              "clocks_event_reasons.sw_power_cap")
+    """SM clocks and throttle reasons sampled every ~5 ms during the timed
+    region, read through NVML in a thread (reading only; nothing is set).
+    Falls back to `nvidia-smi -lms` when NVML cannot be loaded."""
+    REASONS = (("hw_slowdown", "nvmlClocksEventReasonHwSlowdown"),
+               ("hw_thermal_slowdown", "nvmlClocksEventReasonHwThermalSlowdown"),
+               ("sw_thermal_slowdown", "nvmlClocksEventReasonSwThermalSlowdown"),
+               ("sw_power_cap", "nvmlClocksEventReasonSwPowerCap"),
+               ("hw_power_brake", "nvmlClocksEventReasonHwPowerBrakeSlowdown"))
+    SMI_FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+                  "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+                  "clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, index):
-        self.index, self.proc, self.lines = index, None, []
+    def __init__(self, cuda_index, period_s=0.005):
+        self.cuda_index, self.period = cuda_index, period_s
+        self.sm, self.power, self.reasons, self.max_mhz = [], [], set(), None
+        self.stop_ev = threading.Event()
+        self.thread, self.proc, self.source = None, None, None
+
+    def _nvml_handle(self):
+        import pynvml
+        import torch
+        pynvml.nvmlInit()
+        p = torch.cuda.get_device_properties(self.cuda_index)
+        bus = f"{p.pci_domain_id:08x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0"
+        try:
+            return pynvml, pynvml.nvmlDeviceGetHandleByPciBusId(bus.encode())
+        except pynvml.NVMLError:
+            return pynvml, pynvml.nvmlDeviceGetHandleByIndex(self.cuda_index)
 
     def start(self):
         try:
+            nv, h = self._nvml_handle()
+        except Exception:  # noqa: BLE001 - any NVML failure selects the fallback
+            return self._start_smi()
+        self.source = "nvml"
+        self.max_mhz = float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
+        masks = [(n, getattr(nv, a)) for n, a in self.REASONS]
+
+        def run():
+            while not self.stop_ev.is_set():
+                try:
+                    self.sm.append(float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)))
+                    self.power.append(nv.nvmlDeviceGetPowerUsage(h) / 1000.0)
+                    r = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                    self.reasons.update(n for n, m in masks if r & m)
+                except nv.NVMLError:
+                    pass
+                self.stop_ev.wait(self.period)
+
+        self.thread = threading.Thread(target=run, daemon=True)
+        self.thread.start()
+
+    def _start_smi(self):
+        self.source = "nvidia-smi"
+        try:
             self.proc = subprocess.Popen(
-                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
+                ["nvidia-smi", "-i", str(self.cuda_index), f"--query-gpu={self.SMI_FIELDS}",
                  "--format=csv,noheader,nounits", "-lms", "50"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.t = threading.Thread(target=self._read, daemon=True)
-            self.t.start()
         except OSError:
             self.proc = None
+            return
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
+        def read():
+            names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+            for ln in self.proc.stdout:
+                f = [v.strip() for v in ln.split(",")]
+                if len(f) < 7:
+                    continue
+                try:
+                    self.sm.append(float(f[0]))
+                    self.max_mhz = float(f[1])
+                except ValueError:
+                    continue
+                self.reasons.update(n for n, v in zip(names, f[3:7]) if v.lower() == "active")
+
+        self.thread = threading.Thread(target=read, daemon=True)
+        self.thread.start()
 
     def stop(self):
-        if not self.proc:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except subprocess.TimeoutExpired:
-            self.proc.kill()
-        self.t.join(timeout=2)
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
-            f = [v.strip() for v in ln.split(",")]
-            if len(f) < 7:
-                continue
+        self.stop_ev.set()
+        if self.proc:
+            self.proc.terminate()
             try:
-                sm.append(float(f[0]))
-                mx = float(f[1])
-            except ValueError:
-                continue
-            for n, v in zip(names, f[3:7]):
-                if v.lower() == "active":
-                    reasons.add(n)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
-                "reasons": sorted(reasons), "samples": len(sm)}
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+        if self.thread:
+            self.thread.join(timeout=2)
+        if not self.sm:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["no clock samples"],
+                    "samples": 0, "source": self.source}
+        out = {"sm_mhz": statistics.median(self.sm), "sm_max_mhz": self.max_mhz,
+               "reasons": sorted(self.reasons), "samples": len(self.sm), "source": self.source}
+        if self.power:
+            out["power_w_median"] = statistics.median(self.power)
+        return out
+
+
+def profiled_traffic(kernel):
+    """DRAM bytes (read + write) per launch of `kernel`, from the committed
+    ncu summary profiles/<kernel>_olmoe_T512.md (its `traffic_bytes:` line),
+    or None."""
+    p = os.path.join(ROOT, "profiles", f"{kernel}_olmoe_T512.md")
+    if not os.path.exists(p):
+        return None
+    for ln in open(p):
+        if ln.strip().startswith("traffic_bytes:"):
+            try:
+                return float(ln.split(":", 1)[1].strip().split()[0])
+            except (ValueError, IndexError):
+                return None
+    return None
 
 
 def make_layer():
@@ -194,7 +259,7 @@ def run_ours(args):
     dev = local
     torch.cuda.set_device(dev)
     import overhang_b200 as ob
-    ob.init(dev, 8 << 30)
+    ob.init(dev, 1 << 30)      # one layer: 403 MB of experts + router
     pyoracle, L = make_layer()
     layer = ob.MoELayer.from_oracle_layer(0, L)
     nbuf = 8
@@ -220,10 +285,27 @@ def run_ours(args):
     for i in range(args.warmup):
         step(i)
     ob.sync()
+
+    # per-stage device time, a diagnostic pass before the timed region
+    # (profiling events between kernels, one synchronised forward at a time)
+    ob.set_profiling(True)
+    st = []
+    for i in range(5):
+        step(i)
+        torch.cuda.synchronize()
+        st.append(ob.stage_times())
+    ob.set_profiling(False)
+    stage_names = [n for n, _ in st[-1]] if st and st[-1] else []
+    stage_ms = np.array([[v for _, v in row] for row in st]).mean(axis=0).tolist() if stage_names else []
+    stages = dict(zip(stage_names, stage_ms))
+    # the dominant kernel: the gate/up expert pass (2/3 of the weight bytes)
+    dom = "gemm_gateup" if "gemm_gateup" in stages else "gemv_gateup"
+
     barrier()
     clk = ClockSampler(dev)
     clk.start()
     ob.launch_count(reset=True)
+    ob.time_stage(dom)          # one event pair around `dom` per step, on the launching stream
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for i in range(args.steps):
@@ -232,6 +314,8 @@ def run_ours(args):
     barrier()
     launches = ob.launch_count()
     clocks = clk.stop()
+    dom_ms, dom_n = ob.stage_timer()
+    ob.time_stage(None)
     ob.sync()
     ms = e0.elapsed_time(e1)
     t_max = ms
@@ -240,17 +324,6 @@ def run_ours(args):
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
         t_max = float(tt.item())
     value = world * T * args.steps / (t_max / 1e3)
-
-    # per-stage device time (profiling events on the launching stream)
-    ob.set_profiling(True)
-    st = []
-    for i in range(max(3, min(args.steps, 20))):
-        step(i)
-        torch.cuda.synchronize()
-        st.append(ob.stage_times())
-    ob.set_profiling(False)
-    stage_names = [n for n, _ in st[-1]] if st and st[-1] else []
-    stage_ms = np.array([[v for _, v in row] for row in st]).mean(axis=0).tolist() if stage_names else []
 
     # end to end through the host entry: pinned x in, out + routing back
     hx = [torch.from_numpy(pyoracle.normal(SEED_X + i, (T, D))).pin_memory() for i in range(nbuf)]
@@ -278,19 +351,16 @@ def run_ours(args):
     e2e = world * T * args.steps / e2e_s
 
     hbm, tf, src = peaks()
-    # dominant kernel: the gate/up expert GEMM (2/3 of the weight bytes).
-    # algorithmic bytes per launch = every active expert's int8 gate+up rows +
-    # their scales + the f16 token operand it reads + the f16 h it writes.
+    # algorithmic bytes of one launch of the dominant kernel: every active
+    # expert's int8 gate+up rows and their scales, the f16 token operand it
+    # reads (one row per routed slot) and the f16 h it writes.
     n_active = int(len(np.unique(idx.cpu().numpy())))
-    stages = dict(zip(stage_names, stage_ms))
-    if "gemm_gateup" in stages:
-        dom, dom_ms = "gemm_gateup", stages["gemm_gateup"]
+    if dom == "gemm_gateup":
         alg_bytes = n_active * (2 * I * D + 2 * I * 4) + T * K * D * 2 + T * K * I * 2
     else:
-        dom = "gemv_gateup" if "gemv_gateup" in stages else "expert pass"
-        dom_ms = stages.get("gemv_gateup", ms / args.steps)
         alg_bytes = n_active * (2 * I * D + 2 * I * 4) + T * D * 4 + T * K * I * 4
-    achieved = alg_bytes / (dom_ms / 1e3) / 1e9
+    achieved = alg_bytes / (dom_ms / 1e3) / 1e9 if dom_ms > 0 else None
+    traffic = profiled_traffic(dom)
     line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": t_max / args.steps, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f16xint8->f32",
@@ -300,9 +370,9 @@ def run_ours(args):
             "gpu_launches": launches,
             "stage_ms": stages,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
-                         "frac": achieved / hbm, "traffic": None,
-                         "kernel": dom, "peak_source": src,
-                         "alg_bytes_per_launch": alg_bytes},
+                         "frac": achieved / hbm if achieved else None, "traffic": traffic,
+                         "kernel": dom, "peak_source": src, "alg_bytes_per_launch": alg_bytes,
+                         "launch_ms": dom_ms, "launches_timed": dom_n},
             "clocks": clocks}
     if rank == 0 and world == 1 and not args.no_cpu:
         tps, n, kind, cores, dt = cpu_reference_tokens_per_s(pyoracle, L, args.cpu_seconds)
@@ -319,8 +389,8 @@ def run_ours(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
-    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=1000)
+    ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu", action="store_true")

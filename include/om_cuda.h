@@ -172,6 +172,16 @@ int omc_stage_times(float *ms, int n);
  * "gemm_gateup", "gemm_down", "combine", "gemv_gateup", ...), or NULL. */
 const char *omc_stage_name(int i);
 
+/* Stage timer for benchmarks: from this call on, every forward records one
+ * pair of CUDA events on its launching stream, at the boundaries just before
+ * and just after the stage called `name` (a name omc_stage_name reports, e.g.
+ * "gemm_gateup"); no other event is kept and nothing is synchronised, so the
+ * forwards run as they do untimed.  name = NULL stops.  omc_stage_timer
+ * returns the mean duration of that stage over the timed forwards (the last
+ * 1023 when more ran) and how many it averaged. */
+int omc_time_stage(const char *name);
+int omc_stage_timer(float *mean_ms, int *count);
+
 /* Number of kernels the library launched since the last reset (a count of
  * its own launches, not of library calls it makes). */
 long long omc_launch_count(int reset);

@@ -62,6 +62,8 @@ SIGNATURES = {
     "omc_set_profiling": (_i, [_i]),
     "omc_stage_times": (_i, [C.POINTER(C.c_float), _i]),
     "omc_stage_name": (C.c_char_p, [_i]),
+    "omc_time_stage": (_i, [C.c_char_p]),
+    "omc_stage_timer": (_i, [C.POINTER(C.c_float), C.POINTER(_i)]),
     "omc_launch_count": (C.c_longlong, [_i]),
     "omc_version": (C.c_char_p, []),
     "omm_init": (_i, []),
@@ -140,6 +142,19 @@ def stage_times(n: int = 12):
 
 def set_profiling(on: bool) -> None:
     lib().omc_set_profiling(1 if on else 0)
+
+
+def time_stage(name) -> None:
+    """Time stage `name` ("gemm_gateup", ...) in every following forward with
+    one CUDA-event pair on its stream; None stops."""
+    check(lib().omc_time_stage(None if name is None else name.encode()), "omc_time_stage")
+
+
+def stage_timer():
+    """(mean ms, forwards averaged) of the stage given to time_stage."""
+    ms, n = C.c_float(0.0), C.c_int(0)
+    check(lib().omc_stage_timer(C.byref(ms), C.byref(n)), "omc_stage_timer")
+    return float(ms.value), int(n.value)
 
 
 class MoELayer:

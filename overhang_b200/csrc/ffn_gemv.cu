@@ -82,7 +82,7 @@ __global__ void __launch_bounds__(128) gemv_gateup_kernel(omc_layer_dev L, const
     __syncthreads();
     const omc_expert_ptrs P = L.experts[e];
     const int nkb = L.D_pad / OMC_KB;
-    const size_t tile = (size_t)ot * nkb * OMC_BLK_BYTES + (size_t)r * 16;
+    const size_t tile = (size_t)ot * nkb * OMC_PAIR_STRIDE + (size_t)r * 16;   // pair ot: g member 0, u member 1
     const int8_t *gp = P.g + tile, *up = P.u + tile;
     float ag = 0.f, au = 0.f;
 #pragma unroll 2
@@ -90,8 +90,8 @@ __global__ void __launch_bounds__(128) gemv_gateup_kernel(omc_layer_dev L, const
         int4 wg[4], wu[4];
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
-            wg[c] = ldg_nc_v4(gp + (size_t)kb * OMC_BLK_BYTES + c * 2048);
-            wu[c] = ldg_nc_v4(up + (size_t)kb * OMC_BLK_BYTES + c * 2048);
+            wg[c] = ldg_nc_v4(gp + (size_t)kb * OMC_PAIR_STRIDE + c * 2048);
+            wu[c] = ldg_nc_v4(up + (size_t)kb * OMC_PAIR_STRIDE + c * 2048);
         }
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
@@ -115,7 +115,7 @@ __device__ __forceinline__ float down_dot(const int8_t *dp, const float *h, int 
     for (int kb = 0; kb < nkb; ++kb) {
         int4 w[4];
 #pragma unroll
-        for (int c = 0; c < 4; ++c) w[c] = ldg_nc_v4(dp + (size_t)kb * OMC_BLK_BYTES + c * 2048);
+        for (int c = 0; c < 4; ++c) w[c] = ldg_nc_v4(dp + (size_t)kb * OMC_PAIR_STRIDE + c * 2048);
 #pragma unroll
         for (int c = 0; c < 4; ++c) a = dot16(a, w[c], h + kb * OMC_KB + c * 16);
     }
@@ -143,7 +143,7 @@ __global__ void __launch_bounds__(128) gemv_down_combine_kernel(omc_layer_dev L,
     if (L.has_shared) {
         const omc_expert_ptrs P = L.experts[L.E];
         const int nkb_s = L.Is_pad / OMC_KB;
-        const int8_t *dp = P.d + (size_t)dt * nkb_s * OMC_BLK_BYTES + (size_t)r * 16;
+        const int8_t *dp = P.d + omc_dblk(dt, 0, nkb_s) + (size_t)r * 16;
         const float y = __fmul_rn(down_dot(dp, hs + (size_t)K * ldh, nkb_s), P.ds[d]);
         acc = __fmul_rn(y, sg[t]);                       // out = shared; out *= sigmoid(gate)
     }
@@ -155,7 +155,7 @@ __global__ void __launch_bounds__(128) gemv_down_combine_kernel(omc_layer_dev L,
             return;
         }
         const omc_expert_ptrs P = L.experts[e];
-        const int8_t *dp = P.d + (size_t)dt * nkb * OMC_BLK_BYTES + (size_t)r * 16;
+        const int8_t *dp = P.d + omc_dblk(dt, 0, nkb) + (size_t)r * 16;
         const float y = __fmul_rn(down_dot(dp, hs + (size_t)kk * ldh, nkb), P.ds[d]);
         acc = __fadd_rn(acc, __fmul_rn(topk_w[(size_t)t * K + kk], y));   // out += w * y
     }

@@ -18,25 +18,42 @@
 //           order (engines/olmoe.c:395-397, engines/qwen.c:459-462,492)
 //
 // GEMM design (one persistent CTA per SM, warp-specialised, 864 threads).
-// The expert weights are the MMA's N operand (256 rows per instruction:
-// 128 gate + 128 up rows, or two 128-row tiles of the down matrix) and the
-// tokens its M (128 rows, padded): a tcgen05.mma costs ~140 cycles whatever
-// its N, so N=256 puts 4 KiB of weights through each instruction.
-//   warp 26      int8 producer: bulk-copies (no multicast) the two 8 KiB int8
-//                weight blocks of each K block into a 6-deep smem ring; the
-//                depth covers ~2 us of HBM latency at the streaming rate;
-//   warp 0       token producer: bulk-copies the f16 token tile (n rows x
-//                128 B, contiguous in the AOL operand) into a 3-deep ring;
-//   warps 2..17  dequant, two groups of 256 threads taking alternate K
-//                blocks: thread t owns weight row t, converts its 64 int8
-//                exactly to f16 and writes them 128B-swizzled into the
-//                group's f16 B tile (2-deep ring, one tile per group);
-//   warp 1       TMEM allocator + single-thread tcgen05.mma issuer
-//                (kind::f16, M=128, N=256, K=16; both operands from smem);
-//   warps 18..25 epilogue, one token row per thread (TMEM lane), two warps
-//                per lane quarter splitting the 256 columns: SwiGLU or the
-//                routing weight, from a double-buffered f32 accumulator
-//                ([128 tokens] x [256 weight rows] per buffer, 512 columns).
+// The dequantised expert weights are the MMA's A operand, held in tensor
+// memory (M = 128 weight rows per instruction); the tokens are its B operand
+// in shared memory (N = the item's 16..128 token rows).  Weights therefore
+// never pass through shared memory as f16: per 16 KiB int8 K block the SM's
+// shared-memory traffic is the int8 landing + its read (32 KiB), the token
+// tile (<= 16 KiB) and the MMA's token reads, instead of also writing and
+// re-reading a 32 KiB f16 weight tile.  (tcgen05.mma reads its shared-memory
+// operands through the same 128 B/cycle as every other access; with weights
+// in TMEM an M=128 N=64 K=16 MMA runs at the full 32-cycle tensor rate.)
+//   warp 26      int8 producer: one bulk copy (no multicast) per K block of
+//                the item's tile pair, 16 KiB contiguous in the slab's paired
+//                layout, into a 6-deep ring, L2 evict-first (every weight
+//                byte is read once per forward).  One thread issuing 8 KiB
+//                copies tops out near 5.3 TB/s on B200; 16 KiB ones reach
+//                ~6.9 TB/s;
+//   warps 2..17  dequant, two groups of 8 warps taking alternate K blocks.
+//                A group first starts its K block's f16 token tile (n rows
+//                x 128 B, contiguous in the AOL operand) into a 4-deep smem
+//                ring with per-lane cp.async, L2 evict-last (bulk copies of
+//                one SM share a queue: one issued behind the int8 stream
+//                waits ~4k cycles even on an L2 hit); then,
+//                within a group warp w writes weight rows 32*(w%4)..+31 (its
+//                TMEM lane quarter) of tile (gate/up or down 2mt / 2mt+1):
+//                64 int8 -> exact f16 -> tcgen05.st into a 3-deep ring of
+//                TMEM A stages (64 columns each: 2 tiles x 32);
+//   warp 1       TMEM allocator + tcgen05.mma issuer: the warp runs the
+//                loop, an elected lane issues (kind::f16, A from TMEM,
+//                M=128, N=n, K=16; 8 per K block);
+//   warps 18..25 epilogue, one weight row (= TMEM lane) per thread, two
+//                warps per lane quarter: SwiGLU into an smem tile that two
+//                bulk stores write out as the h operand, or scale x routing
+//                weight straight into the per-slot partials.
+// Accumulators: two 160-column TMEM slots.  An item of <= 80 tokens uses one
+// slot (gate at +0, up at +80), so consecutive items double-buffer; a larger
+// item takes both slots.  The epilogue fetches what it needs of an item
+// (scales, routing of its rows) before it waits for the accumulator.
 //
 // Every mbarrier wait is bounded (~1 s); on expiry the CTA records
 // OMC_DEVERR_TIMEOUT, raises a shared abort flag, and all roles unwind.
@@ -44,30 +61,34 @@
 
 namespace {
 
-constexpr int NMAX = 128;                 // tokens per work item (MMA M)
+constexpr int NMAX = 128;                 // tokens per work item (MMA N)
 constexpr int NGRP = 2;                   // dequant groups (alternate K blocks)
-constexpr int NDQ = 8;                    // warps per dequant group (256 threads = 256 weight rows)
+constexpr int NDQ = 8;                    // warps per dequant group: 2 tiles x 4 lane quarters
 constexpr int NEPI = 8;                   // epilogue warps: two per TMEM lane quarter
-constexpr int SA = 3;                     // token-tile ring
-constexpr int SB = NGRP;                  // f16 weight-tile ring: one tile per dequant group
-constexpr int SI = 6;                     // int8 ring
+constexpr int SA = 4;                     // token-tile ring (smem)
+constexpr int ST = 3;                     // weight A stages (TMEM)
+constexpr int SI = 6;                     // int8 ring (smem)
 constexpr int WARP_DQ0 = 2;
 constexpr int WARP_EPI0 = WARP_DQ0 + NGRP * NDQ;              // 18
 constexpr int WARP_I8 = WARP_EPI0 + NEPI;                     // 26
 constexpr int NTHREADS = (WARP_I8 + 1) * 32;                  // 864
 constexpr int W_BYTES = OMC_BLK_BYTES;    // 8 KiB int8 per 128-row weight block per K block
 constexpr int A_BYTES = NMAX * 128;       // 16 KiB f16 token tile
-constexpr int B_BYTES = 256 * 128;        // 32 KiB f16 weight tile
-constexpr uint32_t TMEM_COLS = 512;       // two accumulator buffers of 256 columns
+constexpr uint32_t TMEM_COLS = 512;
+constexpr uint32_t ACC_SLOT_COLS = 160;   // accumulator slots at columns 0 and 160
+constexpr uint32_t TCOL_A = 320;          // A stages: 320 + 64*stage + 32*tile
+constexpr int SMALL_N = 80;               // items up to this many tokens take one slot
+static_assert(TCOL_A + ST * 64 <= TMEM_COLS && 2 * ACC_SLOT_COLS <= TCOL_A, "TMEM columns");
 
 // smem layout (bytes, from a 1024-aligned base)
 constexpr int OFF_A = 0;
-constexpr int OFF_B = OFF_A + SA * A_BYTES;
-constexpr int OFF_I8 = OFF_B + SB * B_BYTES;
-constexpr int OFF_SC = OFF_I8 + SI * 2 * W_BYTES;         // [2][256] f32 row scales of the item
-constexpr int OFF_BAR = OFF_SC + 2 * 256 * 4;
+constexpr int OFF_I8 = OFF_A + SA * A_BYTES;
+constexpr int OFF_STG = OFF_I8 + SI * 2 * W_BYTES;         // [2 K halves][NMAX rows][128 B] h staging
+constexpr int OFF_TAB = OFF_STG + 2 * NMAX * 128;        // [NEPI][NMAX] (ypart row, weight) per epilogue warp
+constexpr int OFF_BAR = OFF_TAB + NEPI * NMAX * 8;
 constexpr int SMEM_BYTES = OFF_BAR + 512 + 1024;
 static_assert(SMEM_BYTES <= 227 * 1024, "smem budget");
+static_assert(OFF_I8 % 1024 == 0 && OFF_STG % 1024 == 0, "alignment");
 
 struct WorkItem {
     int g, mt, n0, n;
@@ -81,7 +102,7 @@ struct GemmArgs {
     uint16_t *hout;            // gemm1: h operand out
     float *ypart;              // gemm2: per-slot partials [T][k+1][D]
     const int *rowinfo;        // gemm2: row -> slot
-    const float *topk_w;       // gemm2: routing weights [T][k]
+    const float *roww;         // gemm2: row -> routing weight (1 for the shared expert)
     int T, R;                  // tokens, operand rows
     int *err;
 };
@@ -123,17 +144,6 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
-// D[tmem] (+)= A[smem desc] * B[smem desc]^T, kind::f16, f32 accumulate.
-__device__ __forceinline__ void tc_mma_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
-                                          uint32_t accumulate) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
-        : "memory");
-}
-
 // The 128-row weight blocks an item multiplies: phase 1 = gate tile mt and up
 // tile mt; phase 2 = down tiles 2*mt and 2*mt+1 (the second absent past D_rows).
 template <int PHASE>
@@ -160,20 +170,20 @@ struct Ctx {
         if (PHASE == 1) return a.L.D_pad / OMC_KB;
         return (it.g == a.L.E ? a.L.Is_pad : a.L.I_pad) / OMC_KB;
     }
-    // first int8 byte of weight block `mat` (0/1) of the item, K block 0
-    __device__ const int8_t *wbase(const WorkItem &it, int mat) const {
+    // first int8 byte of the item's tile pair (gate/up of tile mt, or down
+    // tiles 2mt and 2mt+1), K block 0; K block kb is OMC_PAIR_STRIDE further
+    __device__ const int8_t *pair_base(const WorkItem &it) const {
         const omc_expert_ptrs P = a.L.experts[it.g];
-        const int n = nkb(it);
-        if (PHASE == 1) return (mat ? P.u : P.g) + (size_t)it.mt * n * W_BYTES;
-        return P.d + (size_t)(2 * it.mt + mat) * n * W_BYTES;
+        const size_t off = (size_t)it.mt * nkb(it) * OMC_PAIR_STRIDE;
+        return (PHASE == 1 ? P.g : P.d) + off;
     }
 };
 
 // Walks this CTA's (item, K block) stages in order.
 template <int PHASE>
 struct StageIter {
-    int idx, kb, nkb, nmat, nitems, stride;
-    const int8_t *w0, *w1;
+    int idx, kb, nkb, nmat, nitems, stride, n0, n;
+    const int8_t *w;
     bool valid;
     __device__ void load_item(const Ctx<PHASE> &c) {
         valid = idx < nitems;
@@ -185,8 +195,9 @@ struct StageIter {
         }
         nkb = c.nkb(it);
         nmat = item_nmat<PHASE>(c.a.L, it);
-        w0 = c.wbase(it, 0);
-        w1 = nmat > 1 ? c.wbase(it, 1) : w0;
+        w = c.pair_base(it);
+        n0 = it.n0;
+        n = it.n;
     }
     __device__ void init(const Ctx<PHASE> &c, int first, int n, int cta_stride) {
         idx = first;
@@ -205,19 +216,74 @@ struct StageIter {
     }
 };
 
+// 16-byte cp.async global -> shared with an L2 cache policy (LSU path).
+__device__ __forceinline__ void cp_async16_hint(void *smem_dst, const void *gsrc, uint64_t policy) {
+    asm volatile("cp.async.cg.shared.global.L2::cache_hint [%0], [%1], 16, %2;" ::"r"(smem_u32(smem_dst)), "l"(gsrc),
+                 "l"(policy)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
+// 16-byte-aligned bulk store shared -> global, tracked by this thread's bulk group.
+__device__ __forceinline__ void bulk_s2g(void *gdst, const void *ssrc, uint32_t bytes) {
+    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(gdst), "r"(smem_u32(ssrc)),
+                 "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+// One lane of the (converged) warp, the same each call.
+__device__ __forceinline__ bool elect_one() {
+    uint32_t pred = 0;
+    asm volatile("{\n\t.reg .pred P1;\n\telect.sync _|P1, 0xffffffff;\n\tselp.b32 %0, 1, 0, P1;\n\t}" : "=r"(pred));
+    return pred != 0;
+}
+
+// TMEM accumulator columns of an item's weight tile t (both roles agree):
+// one slot for <= SMALL_N tokens (tile t at +64t), else one slot per tile.
+struct AccSlots {
+    uint32_t ctr = 0, u0 = 0, u1 = 0;   // slots taken so far; uses of slot 0 and slot 1
+    int nslots = 1, p0 = 0;             // this item: slot count, first slot (second = p0 ^ 1)
+    __device__ void begin(int n) {
+        nslots = n > SMALL_N ? 2 : 1;
+        p0 = (int)(ctr & 1u);
+    }
+    __device__ int slot(int j) const { return p0 ^ j; }
+    __device__ uint32_t col(int t) const {
+        return nslots == 1 ? (uint32_t)p0 * ACC_SLOT_COLS + (uint32_t)t * (uint32_t)SMALL_N
+                           : (uint32_t)(p0 ^ t) * ACC_SLOT_COLS;
+    }
+    __device__ uint32_t parity(int j) const { return (slot(j) ? u1 : u0) & 1u; }
+    __device__ void end() {
+        if (nslots == 2) {
+            ++u0;
+            ++u1;
+        } else if (p0) {
+            ++u1;
+        } else {
+            ++u0;
+        }
+        ctr += (uint32_t)nslots;
+    }
+};
+
 template <int PHASE>   // 1: gate/up + SwiGLU, 2: down + weighting
 __global__ void __launch_bounds__(NTHREADS, 1) moe_gemm_kernel(const GemmArgs a) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint64_t *fullA = reinterpret_cast<uint64_t *>(smem + OFF_BAR);   // [SA] token tile landed
-    uint64_t *emptyA = fullA + SA;                                    // [SA] its MMAs done
-    uint64_t *fullB = emptyA + SA;                                    // [SB] f16 weight tile written
-    uint64_t *emptyB = fullB + SB;                                    // [SB] its MMAs done
-    uint64_t *fullI = emptyB + SB;                                    // [SI] int8 blocks landed
-    uint64_t *emptyI = fullI + SI;                                    // [SI] int8 slot read
-    uint64_t *accfull = emptyI + SI;                                  // [2]
-    uint64_t *accempty = accfull + 2;                                 // [2]
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(accempty + 2);
+    uint64_t *emptyA = reinterpret_cast<uint64_t *>(smem + OFF_BAR);  // [SA] token slot's MMAs done
+    uint64_t *fullI = emptyA + SA;                                    // [SI] int8 blocks landed
+    uint64_t *emptyI = fullI + SI;                                    // [SI] int8 slot converted
+    uint64_t *fullT = emptyI + SI;                                    // [ST] TMEM weight stage + token tile ready
+    uint64_t *emptyT = fullT + ST;                                    // [ST] its MMAs done
+    uint64_t *accfull = emptyT + ST;                                  // [2] accumulator slot ready
+    uint64_t *accempty = accfull + 2;                                 // [2] accumulator slot drained
+    uint64_t *stgfull = accempty + 2;                                 // h staging written (phase 1)
+    uint64_t *stgfree = stgfull + 1;                                  // h staging read by its bulk store
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(stgfree + 1);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -226,22 +292,21 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_gemm_kernel(const GemmArgs a)
     const int nitems = a.nwork[PHASE - 1];
 
     if (threadIdx.x == 0) {
-        for (int i = 0; i < SA; ++i) {
-            mbar_init(&fullA[i], 1);
-            mbar_init(&emptyA[i], 1);
-        }
-        for (int i = 0; i < SB; ++i) {
-            mbar_init(&fullB[i], NDQ);
-            mbar_init(&emptyB[i], 1);
-        }
+        for (int i = 0; i < SA; ++i) mbar_init(&emptyA[i], 1);
         for (int i = 0; i < SI; ++i) {
             mbar_init(&fullI[i], 1);
             mbar_init(&emptyI[i], NDQ);
+        }
+        for (int i = 0; i < ST; ++i) {
+            mbar_init(&fullT[i], NDQ);
+            mbar_init(&emptyT[i], 1);
         }
         for (int i = 0; i < 2; ++i) {
             mbar_init(&accfull[i], 1);
             mbar_init(&accempty[i], NEPI);
         }
+        mbar_init(stgfull, NEPI);
+        mbar_init(stgfree, 1);
         *abort_flag = 0;
         fence_barrier_init();
     }
@@ -252,227 +317,259 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_gemm_kernel(const GemmArgs a)
     const uint32_t tmem = *tmem_slot;
 
     if (warp == 0) {
-        // ------------------------------------------------ token-tile producer
-        if (lane == 0) {
-            uint32_t i = 0;
-            for (int idx = blockIdx.x; idx < nitems && !*abort_flag; idx += gridDim.x) {
-                const WorkItem it = c.item(idx);
-                if (!c.ok(it)) {
-                    omc_dev_error(a.err, OMC_DEVERR_BOUNDS, OMC_SITE_GEMM_PRODUCER, idx);
-                    *abort_flag = 1;
-                    break;
-                }
-                const int nkb = c.nkb(it);
-                const uint32_t bytes = (uint32_t)it.n * 128;
-                for (int kb = 0; kb < nkb; ++kb, ++i) {
-                    const int sa = i % SA;
-                    if (!wait_or_abort(&emptyA[sa], ((i / SA) & 1) ^ 1, a.err, OMC_SITE_GEMM_PRODUCER, abort_flag))
-                        break;
-                    mbar_arrive_expect_tx(&fullA[sa], bytes);
-                    const uint8_t *src = reinterpret_cast<const uint8_t *>(a.act) + (size_t)kb * a.R * 128 +
-                                         (size_t)it.n0 * 128;
-                    bulk_g2s(smem + OFF_A + sa * A_BYTES, src, bytes, &fullA[sa]);
-                }
-            }
-        }
+        // no role: the token tiles are loaded by the dequant group of their K block
     } else if (warp == WARP_I8) {
         // ------------------------------------------------ int8 weight producer
         if (lane == 0) {
             StageIter<PHASE> it;
             it.init(c, blockIdx.x, nitems, gridDim.x);
+            const uint64_t stream = l2_policy_evict_first();
             for (uint32_t i = 0; it.valid && !*abort_flag; ++i) {
                 const int si = i % SI;
                 if (!wait_or_abort(&emptyI[si], ((i / SI) & 1) ^ 1, a.err, OMC_SITE_GEMM_PRODUCER, abort_flag))
                     break;
-                mbar_arrive_expect_tx(&fullI[si], it.nmat * W_BYTES);
-                uint8_t *dst = smem + OFF_I8 + si * 2 * W_BYTES;
-                bulk_g2s(dst, it.w0 + (size_t)it.kb * W_BYTES, W_BYTES, &fullI[si]);
-                if (it.nmat > 1) bulk_g2s(dst + W_BYTES, it.w1 + (size_t)it.kb * W_BYTES, W_BYTES, &fullI[si]);
+                // the pair's K block is one contiguous 16 KiB (8 KiB when the pair has one tile)
+                const uint32_t bytes = (uint32_t)it.nmat * W_BYTES;
+                mbar_arrive_expect_tx(&fullI[si], bytes);
+                bulk_g2s_hint(smem + OFF_I8 + si * 2 * W_BYTES, it.w + (size_t)it.kb * OMC_PAIR_STRIDE, bytes,
+                              &fullI[si], stream);
                 it.step(c);
             }
         }
     } else if (warp == 1) {
         // ------------------------------------------------ MMA issuer
-        if (lane == 0) {
-            uint32_t i = 0, ci = 0;
-            for (int idx = blockIdx.x; idx < nitems && !*abort_flag; idx += gridDim.x, ++ci) {
-                const WorkItem it = c.item(idx);
-                if (!c.ok(it)) break;
-                const int nkb = c.nkb(it);
-                const uint32_t idesc = tc_idesc_f16(NMAX, 128 * item_nmat<PHASE>(L, it));
-                const int b = ci & 1;
-                if (!wait_or_abort(&accempty[b], ((ci >> 1) & 1) ^ 1, a.err, OMC_SITE_GEMM_MMA, abort_flag)) break;
-                tc_fence_after();
-                const uint32_t dcol = (uint32_t)b * 256;
-                bool ok = true;
-                for (int kb = 0; kb < nkb; ++kb, ++i) {
-                    const int sa = i % SA, sb = i % SB;
-                    ok = wait_or_abort(&fullA[sa], (i / SA) & 1, a.err, OMC_SITE_GEMM_MMA, abort_flag) &&
-                         wait_or_abort(&fullB[sb], (i / SB) & 1, a.err, OMC_SITE_GEMM_MMA, abort_flag);
-                    if (!ok) break;
-                    tc_fence_after();
-                    const uint64_t ad = tc_sdesc_k_sw128(smem_u32(smem + OFF_A + sa * A_BYTES));
-                    const uint64_t bd = tc_sdesc_k_sw128(smem_u32(smem + OFF_B + sb * B_BYTES));
-#pragma unroll
-                    for (int k16 = 0; k16 < 4; ++k16)   // +32 B along K = +2 in the descriptor's 16-byte units
-                        tc_mma_ss(tmem + dcol, ad + 2 * k16, bd + 2 * k16, idesc, (kb > 0 || k16 > 0) ? 1u : 0u);
-                    tc_commit(&emptyA[sa]);
-                    tc_commit(&emptyB[sb]);
+        // The whole warp runs the loop (operands warp-uniform) and one elected
+        // lane issues each instruction: issued from a lane-0-only branch,
+        // every tcgen05.mma cost the issuing thread ~110 cycles, against the
+        // 40 cycles an M=128 N=80 MMA takes on the tensor core.
+        uint32_t i = 0;
+        AccSlots acc;
+        for (int idx = blockIdx.x; idx < nitems && !*abort_flag; idx += gridDim.x) {
+            const WorkItem it = c.item(idx);
+            if (!c.ok(it)) break;
+            const int nkb = c.nkb(it);
+            const int nmat = item_nmat<PHASE>(L, it);
+            acc.begin(it.n);
+            bool ok = true;
+            for (int j = 0; j < acc.nslots && ok; ++j)
+                ok = warp_wait(&accempty[acc.slot(j)], acc.parity(j) ^ 1u, a.err, OMC_SITE_GEMM_MMA, abort_flag);
+            if (!ok) break;
+            tc_fence_after();
+            const uint32_t idesc = tc_idesc_f16(128, it.n);     // M = weight rows, N = tokens
+            const uint32_t d0 = tmem + acc.col(0), d1 = tmem + acc.col(1);
+            for (int kb = 0; kb < nkb; ++kb, ++i) {
+                const int sa = i % SA, st = i % ST;
+                if (!warp_wait(&fullT[st], (i / ST) & 1, a.err, OMC_SITE_GEMM_MMA, abort_flag)) {
+                    ok = false;
+                    break;
                 }
-                if (!ok) break;
-                tc_commit(&accfull[b]);
+                tc_fence_after();
+                const uint64_t bd = tc_sdesc_k_sw128(smem_u32(smem + OFF_A + sa * A_BYTES));
+                const uint32_t acol = tmem + TCOL_A + (uint32_t)st * 64u;
+#pragma unroll
+                for (int k16 = 0; k16 < 4; ++k16) {   // +32 B along K: +2 in the smem descriptor, +8 TMEM columns
+                    const uint32_t accum = (kb > 0 || k16 > 0) ? 1u : 0u;
+                    if (elect_one()) tc_mma_ts(d0, acol + 8u * k16, bd + 2 * k16, idesc, accum);
+                    __syncwarp();
+                    if (nmat > 1) {
+                        if (elect_one()) tc_mma_ts(d1, acol + 32u + 8u * k16, bd + 2 * k16, idesc, accum);
+                        __syncwarp();
+                    }
+                }
+                if (elect_one()) {
+                    tc_commit(&emptyA[sa]);
+                    tc_commit(&emptyT[st]);
+                }
+                __syncwarp();
             }
+            if (!ok) break;
+            if (elect_one())
+                for (int j = 0; j < acc.nslots; ++j) tc_commit(&accfull[acc.slot(j)]);
+            __syncwarp();
+            acc.end();
         }
     } else if (warp < WARP_EPI0) {
-        // ------------------------------------------------ dequant: int8 ring -> f16 B tile
+        // ------------------------------------------------ dequant: int8 ring -> TMEM A stage
         const int dq = warp - WARP_DQ0;
-        const int grp = dq / NDQ;                // K blocks i with i % NGRP == grp, B tile `grp`
-        const int t = (dq % NDQ) * 32 + lane;    // weight row of the B tile, 0..255
-        const int mat = t >> 7, r = t & 127;
-        uint8_t *brow = smem + OFF_B + grp * B_BYTES + (uint32_t)(t >> 3) * 1024 + (uint32_t)(t & 7) * 128;
+        const int grp = dq / NDQ;                // K blocks i with i % NGRP == grp
+        const int tile = (dq % NDQ) / 4;         // 0: gate / down 2mt, 1: up / down 2mt+1
+        const int q = warp & 3;                  // this warp's TMEM lane quarter
+        const int r = q * 32 + lane;             // weight row within the 128-row tile
+        const uint32_t lane_bits = (uint32_t)(q * 32) << 16;
         StageIter<PHASE> pr;
         pr.init(c, blockIdx.x, nitems, gridDim.x);
         for (int j = 0; j < grp; ++j) pr.step(c);
+        const int gt = (dq % NDQ) * 32 + lane;   // thread index within the group, 0..255
+        const uint64_t keep = l2_policy_evict_last();
         for (uint32_t i = grp; pr.valid && !*abort_flag; i += NGRP) {
-            const int si = i % SI;
+            const int si = i % SI, st = i % ST, sa = i % SA;
+            // token tile of this K block: per-lane cp.async (not a bulk copy, which would queue
+            // behind the int8 stream's in the SM's copy engine), issued first so that its L2
+            // latency overlaps the int8 wait and the conversion
+            if (!warp_wait(&emptyA[sa], ((i / SA) & 1) ^ 1, a.err, OMC_SITE_GEMM_DEQUANT, abort_flag)) break;
+            {
+                const uint8_t *src = reinterpret_cast<const uint8_t *>(a.act) + (size_t)pr.kb * a.R * 128 +
+                                     (size_t)pr.n0 * 128;
+                uint8_t *dst = smem + OFF_A + sa * A_BYTES;
+                for (int ch = gt; ch < pr.n * 8; ch += NDQ * 32) cp_async16_hint(dst + ch * 16, src + ch * 16, keep);
+                cp_async_commit();
+            }
             if (!warp_wait(&fullI[si], (i / SI) & 1, a.err, OMC_SITE_GEMM_DEQUANT, abort_flag)) break;
-            uint4 f[8];
-            const bool active = mat < pr.nmat;
+            const bool active = tile < pr.nmat;  // warp-uniform
+            uint32_t v[32];
             if (active) {
-                const uint8_t *m = smem + OFF_I8 + si * 2 * W_BYTES + mat * W_BYTES;
+                const uint8_t *m = smem + OFF_I8 + si * 2 * W_BYTES + tile * W_BYTES;
 #pragma unroll
-                for (int cc = 0; cc < 4; ++cc) {
-                    const uint4 q = *reinterpret_cast<const uint4 *>(m + (cc * 128 + r) * 16);
-                    i8x4_to_f16x4(q.x, f[2 * cc].x, f[2 * cc].y);
-                    i8x4_to_f16x4(q.y, f[2 * cc].z, f[2 * cc].w);
-                    i8x4_to_f16x4(q.z, f[2 * cc + 1].x, f[2 * cc + 1].y);
-                    i8x4_to_f16x4(q.w, f[2 * cc + 1].z, f[2 * cc + 1].w);
+                for (int cc = 0; cc < 4; ++cc) {   // 16 int8 of K per chunk -> TMEM columns 8cc..8cc+7
+                    const uint4 qv = *reinterpret_cast<const uint4 *>(m + (cc * 128 + r) * 16);
+                    i8x4_to_f16x4(qv.x, v[8 * cc + 0], v[8 * cc + 1]);
+                    i8x4_to_f16x4(qv.y, v[8 * cc + 2], v[8 * cc + 3]);
+                    i8x4_to_f16x4(qv.z, v[8 * cc + 4], v[8 * cc + 5]);
+                    i8x4_to_f16x4(qv.w, v[8 * cc + 6], v[8 * cc + 7]);
                 }
             }
-            // The slot is released only after the converted values exist: an
-            // arrive issued while the ld.shared above is still in flight does
-            // not keep the next bulk copy (async proxy) from overwriting the
-            // bytes before they are read.
+            // release the int8 slot only once its bytes are in registers as
+            // f16 (an arrive with the ld.shared still in flight would let the
+            // next bulk copy overwrite them)
             __syncwarp();
             if (lane == 0) mbar_arrive(&emptyI[si]);
-            if (!warp_wait(&emptyB[grp], ((i / NGRP) & 1) ^ 1, a.err, OMC_SITE_GEMM_DEQUANT, abort_flag)) break;
+            if (!warp_wait(&emptyT[st], ((i / ST) & 1) ^ 1, a.err, OMC_SITE_GEMM_DEQUANT, abort_flag)) break;
+            tc_fence_after();
             if (active) {
-#pragma unroll
-                for (int j = 0; j < 8; ++j) *reinterpret_cast<uint4 *>(brow + ((j ^ (t & 7)) << 4)) = f[j];
+                tmem_st_32x32b_x32(tmem + lane_bits + TCOL_A + (uint32_t)st * 64u + (uint32_t)tile * 32u, v);
+                tc_wait_st();
             }
-            fence_proxy_async_smem();      // generic stores -> visible to the tensor core
+            cp_async_wait_all();          // this thread's part of the token tile has landed ...
+            fence_proxy_async_smem();     // ... and is visible to the tensor core
+            tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&fullB[grp]);
+            if (lane == 0) mbar_arrive(&fullT[st]);
             for (int j = 0; j < NGRP; ++j) pr.step(c);
         }
-    } else {
-        // ------------------------------------------------ epilogue: one token row per thread
+    } else if (warp < WARP_I8) {
+        // ------------------------------------------------ epilogue: one weight row per thread
         const int e = warp - WARP_EPI0;          // 0..7
         const int q = warp & 3;                  // TMEM lane quarter
-        const int half = e >> 2;                 // which half of the 256 columns
-        const int trow = q * 32 + lane;          // token row within the item = TMEM lane
+        const int half = e >> 2;                 // phase 1: token chunks of this parity; phase 2: tile
+        const int r = q * 32 + lane;             // weight row within the tile = TMEM lane
         const uint32_t lane_bits = (uint32_t)(q * 32) << 16;
+        uint8_t *stg = smem + OFF_STG;
         uint32_t ci = 0;
+        AccSlots acc;
+        int *tab_row = reinterpret_cast<int *>(smem + OFF_TAB + e * NMAX * 8);   // this warp's table
+        float *tab_w = reinterpret_cast<float *>(tab_row + NMAX);
         for (int idx = blockIdx.x; idx < nitems && !*abort_flag; idx += gridDim.x, ++ci) {
             const WorkItem it = c.item(idx);
             if (!c.ok(it)) break;
-            const int b = ci & 1;
-            if (!warp_wait(&accfull[b], (ci >> 1) & 1, a.err, OMC_SITE_GEMM_EPILOGUE, abort_flag)) break;
-            tc_fence_after();
-            const uint32_t acc = tmem + lane_bits + (uint32_t)b * 256;
+            acc.begin(it.n);
             const omc_expert_ptrs P = L.experts[it.g];
-            const bool live = trow < it.n;
-            const int row = it.n0 + trow;        // operand row of this token slot
-            // the item's 256 weight-row scales -> smem (one load round trip per item)
-            float *sc = reinterpret_cast<float *>(smem + OFF_SC) + b * 256;
-            {
-                const int j = e * 32 + lane;     // 0..255
-                float v = 0.f;
-                if (PHASE == 1) {
-                    const int Iw = it.g == L.E ? L.Is : L.I;
-                    const int f = it.mt * OMC_TM + (j & 127);
-                    if (f < Iw) v = j < 128 ? P.gs[f] : P.us[f];
-                } else {
-                    const int d = 2 * it.mt * OMC_TM + j;
-                    if (d < L.D) v = P.ds[d];
+            // fetch what the item needs before waiting for its accumulator
+            float sc0 = 0.f, sc1 = 0.f;
+            if (PHASE == 1) {
+                const int Iw = it.g == L.E ? L.Is : L.I;
+                const int f = it.mt * OMC_TM + r;
+                if (f < Iw) {
+                    sc0 = P.gs[f];
+                    sc1 = P.us[f];
                 }
-                sc[j] = v;
-                asm volatile("bar.sync 1, %0;" ::"n"(NEPI * 32) : "memory");
+            } else {
+                const int d = (2 * it.mt + half) * OMC_TM + r;
+                if (half < item_nmat<PHASE>(L, it) && d < L.D) sc0 = P.ds[d];
+                // per token row: its ypart row (token * (k+1) + choice; -1 padding) and weight
+                const int K = L.k;
+                for (int j = lane; j < it.n; j += 32) {
+                    const int slot = a.rowinfo[it.n0 + j];
+                    int dst = -1;
+                    if (slot >= 0 && slot < a.T * K) dst = slot / K * (K + 1) + slot % K;
+                    else if (slot >= a.T * K) dst = (slot - a.T * K) * (K + 1) + K;
+                    tab_row[j] = dst;
+                    tab_w[j] = a.roww[it.n0 + j];
+                }
+                __syncwarp();
             }
+            bool ok = true;
+            for (int j = 0; j < acc.nslots && ok; ++j)
+                ok = warp_wait(&accfull[acc.slot(j)], acc.parity(j), a.err, OMC_SITE_GEMM_EPILOGUE, abort_flag);
+            if (!ok) break;
+            tc_fence_after();
             if (PHASE == 1) {
                 const int Iw = it.g == L.E ? L.Is : L.I;
                 const int Iw_pad = it.g == L.E ? L.Is_pad : L.I_pad;
-                uint8_t *hrow = reinterpret_cast<uint8_t *>(a.hout) + (size_t)row * 128;
+                const int f = it.mt * OMC_TM + r;                  // feature of this thread
+                // staging of the previous item has been read by its bulk store
+                if (!warp_wait(stgfree, (ci & 1) ^ 1, a.err, OMC_SITE_GEMM_EPILOGUE, abort_flag)) break;
+                // staging: [64-feature half][token row][128 B, 16-byte chunks XOR-ed with row & 7]
+                uint8_t *sbase = stg + (r >> 6) * (NMAX * 128) + (r & 7) * 2;
+                const int chunk = (r & 63) >> 3;
+                const int nch = it.n >> 4;
 #pragma unroll 1
-                for (int j0 = half * 64; j0 < half * 64 + 64; j0 += 16) {
-                    const int f0 = it.mt * OMC_TM + j0;              // first feature of the chunk
+                for (int ch = half; ch < nch; ch += 2) {
                     uint32_t gv[16], uv[16];
-                    tmem_ld_32x32b_x16(acc + j0, gv);
-                    tmem_ld_32x32b_x16(acc + 128 + j0, uv);
+                    tmem_ld_32x32b_x16(tmem + lane_bits + acc.col(0) + ch * 16, gv);
+                    tmem_ld_32x32b_x16(tmem + lane_bits + acc.col(1) + ch * 16, uv);
                     tc_wait_ld();
-                    uint32_t hv[8];
 #pragma unroll
-                    for (int jj = 0; jj < 16; jj += 2) {
-                        const float h0 = f0 + jj < Iw ? swiglu_f(L.family, __uint_as_float(gv[jj]) * sc[j0 + jj],
-                                                                  __uint_as_float(uv[jj]) * sc[128 + j0 + jj])
-                                                       : 0.f;
-                        const float h1 = f0 + jj + 1 < Iw
-                                             ? swiglu_f(L.family, __uint_as_float(gv[jj + 1]) * sc[j0 + jj + 1],
-                                                        __uint_as_float(uv[jj + 1]) * sc[128 + j0 + jj + 1])
-                                             : 0.f;
-                        hv[jj >> 1] = f32x2_to_f16x2_sat(h0, h1);
+                    for (int jj = 0; jj < 16; ++jj) {
+                        const int j = ch * 16 + jj;                // token row within the item
+                        const float hv = f < Iw ? swiglu_f(L.family, __uint_as_float(gv[jj]) * sc0,
+                                                           __uint_as_float(uv[jj]) * sc1)
+                                                : 0.f;
+                        // operand row n0 + j; n0 % 16 == 0, so its swizzle phase is j & 7 = jj & 7
+                        *reinterpret_cast<__half *>(sbase + j * 128 + ((chunk ^ (jj & 7)) << 4)) =
+                            __float2half_rn(fminf(fmaxf(hv, -65504.f), 65504.f));
                     }
-                    if (live && f0 < Iw_pad) {
-                        uint8_t *kbase = hrow + (size_t)(f0 >> 6) * a.R * 128;
-                        const int cb = (f0 & 63) >> 3;
-                        *reinterpret_cast<uint4 *>(kbase + ((cb ^ (row & 7)) << 4)) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
-                        *reinterpret_cast<uint4 *>(kbase + (((cb + 1) ^ (row & 7)) << 4)) =
-                            make_uint4(hv[4], hv[5], hv[6], hv[7]);
+                }
+                tc_fence_before();
+                fence_proxy_async_smem();                          // staging -> visible to the bulk store
+                __syncwarp();
+                if (lane == 0) {
+                    for (int j = 0; j < acc.nslots; ++j) mbar_arrive(&accempty[acc.slot(j)]);
+                    mbar_arrive(stgfull);
+                }
+                if (e == 0) {
+                    // one thread writes the two 64-feature halves of the tile's h rows
+                    if (!warp_wait(stgfull, ci & 1, a.err, OMC_SITE_GEMM_EPILOGUE, abort_flag)) break;
+                    if (lane == 0) {
+                        for (int kh = 0; kh < 2; ++kh) {
+                            const int f0 = it.mt * OMC_TM + kh * 64;
+                            if (f0 >= Iw_pad) break;
+                            uint8_t *dst = reinterpret_cast<uint8_t *>(a.hout) +
+                                           ((size_t)(f0 >> 6) * a.R + (size_t)it.n0) * 128;
+                            bulk_s2g(dst, stg + kh * (NMAX * 128), (uint32_t)it.n * 128);
+                        }
+                        bulk_commit();
+                        bulk_wait_read0();
+                        mbar_arrive(stgfree);
                     }
+                    __syncwarp();
                 }
             } else {
-                const int K = L.k;
-                const int nmat = item_nmat<PHASE>(L, it);
-                int slot = -1;
-                float w = 1.f;
-                if (live) {
-                    slot = a.rowinfo[row];
-                    if (slot >= 0 && slot < a.T * K) w = a.topk_w[slot];
-                }
-                float *dst = nullptr;
-                if (slot >= 0) {
-                    const int tk = slot < a.T * K ? slot / K : slot - a.T * K;
-                    const int kk = slot < a.T * K ? slot - tk * K : K;
-                    dst = a.ypart + ((size_t)tk * (K + 1) + kk) * L.D;
-                }
-                const bool shared_row = slot >= a.T * K;
-                if (half < nmat) {
+                if (half < item_nmat<PHASE>(L, it)) {
+                    const int d = (2 * it.mt + half) * OMC_TM + r;  // output row of this thread
+                    const uint32_t col = acc.col(half);
 #pragma unroll 1
-                    for (int j0 = half * 128; j0 < half * 128 + 128; j0 += 16) {
-                        const int d0 = 2 * it.mt * OMC_TM + j0;      // first output row of the chunk
+                    for (int ch = 0; ch * 16 < it.n; ++ch) {
                         uint32_t yv[16];
-                        tmem_ld_32x32b_x16(acc + j0, yv);
+                        tmem_ld_32x32b_x16(tmem + lane_bits + col + ch * 16, yv);
                         tc_wait_ld();
-                        float o[16];
 #pragma unroll
                         for (int jj = 0; jj < 16; ++jj) {
-                            const float y = __fmul_rn(__uint_as_float(yv[jj]), sc[j0 + jj]);   // matmul_q: acc * scale
-                            o[jj] = shared_row ? y : __fmul_rn(w, y);                         // w * hh
-                        }
-                        if (dst && d0 < L.D) {
-#pragma unroll
-                            for (int jj = 0; jj < 16; jj += 4)
-                                if (d0 + jj < L.D)
-                                    *reinterpret_cast<float4 *>(dst + d0 + jj) =
-                                        make_float4(o[jj], o[jj + 1], o[jj + 2], o[jj + 3]);
+                            const int dst = tab_row[ch * 16 + jj];
+                            if (dst < 0 || d >= L.D) continue;
+                            // matmul_q: acc * scale; then w * hh (w = 1 for the shared expert)
+                            const float y = __fmul_rn(__uint_as_float(yv[jj]), sc0);
+                            a.ypart[(size_t)dst * L.D + d] = __fmul_rn(tab_w[ch * 16 + jj], y);
                         }
                     }
                 }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0)
+                    for (int j = 0; j < acc.nslots; ++j) mbar_arrive(&accempty[acc.slot(j)]);
             }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&accempty[b]);
+            acc.end();
         }
+        if (PHASE == 1 && e == 0 && lane == 0) bulk_wait0();      // h rows written before the CTA exits
     }
 
     tc_fence_before();
@@ -552,14 +649,17 @@ __global__ void __launch_bounds__(1024) plan_kernel(const int *__restrict__ coun
 // One warp per task: routed slot, shared row, or padding row.
 __global__ void __launch_bounds__(256) gather_kernel(const float *__restrict__ x, int T, int D, int D_pad, int K,
                                                      int E, int has_shared, const int32_t *__restrict__ topk_idx,
+                                                     const float *__restrict__ topk_w,
                                                      const int *__restrict__ counts, const int *__restrict__ offsets,
                                                      int *__restrict__ fill, int *__restrict__ rowinfo,
-                                                     uint16_t *__restrict__ xp, int R, int *err) {
+                                                     float *__restrict__ roww, uint16_t *__restrict__ xp, int R,
+                                                     int *err) {
     const int task = blockIdx.x * 8 + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
     const int nrouted = T * K, nshared = has_shared ? T : 0;
     const int G = E + (has_shared ? 1 : 0);
     int row = -1, t = -1, info = -1;
+    float wrow = 0.f;
     if (task < nrouted) {
         const int e = topk_idx[task];
         if (e < 0 || e >= E) {
@@ -572,10 +672,12 @@ __global__ void __launch_bounds__(256) gather_kernel(const float *__restrict__ x
         row = offsets[e] + pos;
         t = task / K;
         info = task;
+        wrow = topk_w[task];
     } else if (task < nrouted + nshared) {
         t = task - nrouted;
         row = offsets[E] + t;
         info = nrouted + t;
+        wrow = 1.f;
     } else {
         const int p = task - nrouted - nshared;
         const int g = p / (OMC_ROW_ALIGN - 1), j = p % (OMC_ROW_ALIGN - 1);
@@ -588,7 +690,10 @@ __global__ void __launch_bounds__(256) gather_kernel(const float *__restrict__ x
         if (lane == 0) omc_dev_error(err, OMC_DEVERR_BOUNDS, OMC_SITE_DISPATCH, row);
         return;
     }
-    if (lane == 0) rowinfo[row] = info;
+    if (lane == 0) {
+        rowinfo[row] = info;
+        roww[row] = wrow;
+    }
     uint8_t *base = reinterpret_cast<uint8_t *>(xp);
     const int nkb = D_pad / 64;
     for (int kb0 = 0; kb0 < nkb; kb0 += 4) {
@@ -670,8 +775,9 @@ extern "C" int omc_launch_mma_ffn(const omc_layer_dev *L, const float *x, int T,
     plan_kernel<<<1, 1024, 0, s>>>(ws->counts, E, L->has_shared, T, L->I_rows, L->Is_rows, L->D_rows, R, cap1, cap2,
                                    ws->offsets, ws->fill, work1, work2, ws->nwork, ws->err);
     const int ntasks = T * L->k + (L->has_shared ? T : 0) + G * (OMC_ROW_ALIGN - 1);
-    gather_kernel<<<(ntasks + 7) / 8, 256, 0, s>>>(x, T, L->D, L->D_pad, L->k, E, L->has_shared, topk_idx, ws->counts,
-                                                  ws->offsets, ws->fill, ws->rowinfo, ws->xp, R, ws->err);
+    gather_kernel<<<(ntasks + 7) / 8, 256, 0, s>>>(x, T, L->D, L->D_pad, L->k, E, L->has_shared, topk_idx, topk_w,
+                                                  ws->counts, ws->offsets, ws->fill, ws->rowinfo, ws->roww, ws->xp,
+                                                  R, ws->err);
     GemmArgs ga;
     ga.L = *L;
     ga.work = work1;
@@ -680,7 +786,7 @@ extern "C" int omc_launch_mma_ffn(const omc_layer_dev *L, const float *x, int T,
     ga.hout = ws->hp;
     ga.ypart = ws->ypart;
     ga.rowinfo = ws->rowinfo;
-    ga.topk_w = topk_w;
+    ga.roww = ws->roww;
     ga.T = T;
     ga.R = R;
     ga.err = ws->err;

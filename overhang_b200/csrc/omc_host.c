@@ -183,6 +183,8 @@ void omc_shutdown(void) {
     G.staging = NULL;
     G.staging_bytes = 0;
     for (int i = 0; i < OMC_NSTAGE_EV; ++i) cudaEventDestroy(G.ev[i]);
+    if (G.timer_created)
+        for (int i = 0; i < 2 * OMC_TIMER_RING; ++i) cudaEventDestroy(G.timer_ev[i]);
     cudaFree(G.d_err);
     cudaStreamDestroy(G.stream);
     memset(&G, 0, sizeof(G));
@@ -283,23 +285,23 @@ int omc_layer_init(int layer, const omc_moe_desc *d, const void *router_w, const
     return OMC_OK;
 }
 
-/* Upload one row-major int8 matrix [O][K] + scales [O] into slab tiles. */
-static int upload_matrix(const int8_t *q, const float *s, int O, int K, int O_pad, int K_pad, const int8_t **wq,
+/* Upload one row-major int8 matrix [O][K] + scales [O] into slab tiles at
+ * dq (paired layout, see omc_expert_ptrs; `member` as in
+ * omc_launch_relayout). */
+static int upload_matrix(const int8_t *q, const float *s, int O, int K, int O_pad, int K_pad, int8_t *dq, int member,
                          const float **ws) {
     int on_host;
-    int8_t *dq = omc_slab_alloc((size_t)O_pad * K_pad, &on_host);
     float *dsc = omc_slab_alloc((size_t)O_pad * sizeof(float), &on_host);
-    if (!dq || !dsc) return omc_fail(OMC_ENOMEM, "expert upload: slab and host overflow exhausted");
+    if (!dsc) return omc_fail(OMC_ENOMEM, "expert upload: slab and host overflow exhausted");
     int rc = staging_ensure((size_t)O * K);
     if (rc) return rc;
     CK(cudaMemcpyAsync(G.staging, q, (size_t)O * K, cudaMemcpyHostToDevice, G.stream));
-    rc = omc_launch_relayout((const int8_t *)G.staging, O, K, dq, O_pad, K_pad, G.stream);
+    rc = omc_launch_relayout((const int8_t *)G.staging, O, K, dq, O_pad, K_pad, member, G.stream);
     if (rc) return omc_fail(rc, "expert upload: relayout launch");
     CK(cudaMemsetAsync(dsc, 0, (size_t)O_pad * sizeof(float), G.stream));
     CK(cudaMemcpyAsync(dsc, s, (size_t)O * sizeof(float), cudaMemcpyHostToDevice, G.stream));
     /* the staging buffer is reused by the next matrix */
     CK(cudaStreamSynchronize(G.stream));
-    *wq = dq;
     *ws = dsc;
     return OMC_OK;
 }
@@ -308,10 +310,23 @@ static int set_expert_slot(omc_layer *L, int slot, int I_, int I_pad, int I_rows
                            const int8_t *u, const float *us, const int8_t *d, const float *ds) {
     const omc_layer_dev *P = &L->dev;
     omc_expert_ptrs ep;
-    int rc;
-    if ((rc = upload_matrix(g, gs, I_, P->D, I_rows, P->D_pad, &ep.g, &ep.gs))) return rc;
-    if ((rc = upload_matrix(u, us, I_, P->D, I_rows, P->D_pad, &ep.u, &ep.us))) return rc;
-    if ((rc = upload_matrix(d, ds, P->D, I_, P->D_rows, I_pad, &ep.d, &ep.ds))) return rc;
+    int rc, on_host, on_host2;
+    /* g and u interleave as the two members of each tile pair; d's row tiles
+     * pair up (an odd last tile leaves its partner's blocks zero) */
+    const size_t gu_bytes = (size_t)2 * I_rows * P->D_pad;
+    const size_t d_bytes = (size_t)omc_round_up(P->D_rows, 2 * OMC_TM) * I_pad;
+    int8_t *gu = omc_slab_alloc(gu_bytes, &on_host);
+    int8_t *dd = omc_slab_alloc(d_bytes, &on_host2);
+    if (!gu || !dd) return omc_fail(OMC_ENOMEM, "expert upload: slab and host overflow exhausted");
+    (void)on_host;
+    (void)on_host2;
+    CK(cudaMemsetAsync(dd, 0, d_bytes, G.stream));   /* gu is fully written by the two relayouts */
+    if ((rc = upload_matrix(g, gs, I_, P->D, I_rows, P->D_pad, gu, 0, &ep.gs))) return rc;
+    if ((rc = upload_matrix(u, us, I_, P->D, I_rows, P->D_pad, gu, 1, &ep.us))) return rc;
+    if ((rc = upload_matrix(d, ds, P->D, I_, P->D_rows, I_pad, dd, -1, &ep.ds))) return rc;
+    ep.g = gu;
+    ep.u = gu + OMC_BLK_BYTES;
+    ep.d = dd;
     L->h_experts[slot] = ep;
     L->have[slot] = 1;
     CK(cudaMemcpy(L->d_experts_tab + slot, &ep, sizeof(ep), cudaMemcpyHostToDevice));
@@ -403,7 +418,7 @@ int omc_ws_ensure(const omc_layer *L, int T, int host_io) {
     if ((rc = ws_buf(4, (void **)&W->topk_w, Tz * K * 4))) return rc;
     if ((rc = ws_buf(5, (void **)&W->sg, Tz * 4))) return rc;
     if ((rc = ws_buf(6, (void **)&W->counts, (E + 4) * 4 * 3 + 64))) return rc;
-    if ((rc = ws_buf(7, (void **)&W->rowinfo, R * 4))) return rc;
+    if ((rc = ws_buf(7, (void **)&W->rowinfo, R * 8))) return rc;   /* rowinfo, then roww */
     if ((rc = ws_buf(8, (void **)&W->work, (size_t)omc_mma_work_items(P, (int)R) * 16))) return rc;
     if ((rc = ws_buf(9, (void **)&W->xp, (size_t)P->D_pad * R * 2))) return rc;
     if ((rc = ws_buf(10, (void **)&W->hp, Imax_pad * R * 2))) return rc;
@@ -423,6 +438,7 @@ int omc_ws_ensure(const omc_layer *L, int T, int host_io) {
     ws->fill = W->counts + 2 * (E + 4);
     ws->nwork = W->counts + 3 * (E + 4);
     ws->rowinfo = W->rowinfo;
+    ws->roww = (float *)(W->rowinfo + R);
     ws->work = W->work;
     ws->xp = W->xp;
     ws->hp = W->hp;
@@ -476,21 +492,81 @@ const char *omc_stage_name(int i) {
     return G.prof_names[i];
 }
 
+/* Stage timer.  Every stage boundary of a forward re-records the tentative
+ * start event of the current ring slot; the end of the named stage records
+ * the slot's end event and moves to the next slot, so slot i keeps the
+ * boundary just before the named stage and the one just after it. */
+int omc_time_stage(const char *name) {
+    if (!G.init) return omc_fail(OMC_ENOINIT, "omc_time_stage: omc_init not called");
+    if (!name) {
+        G.timer_on = 0;
+        return OMC_OK;
+    }
+    if (strlen(name) >= sizeof(G.timer_name)) return omc_fail(OMC_EINVAL, "omc_time_stage: name too long");
+    if (!G.timer_created) {
+        for (int i = 0; i < 2 * OMC_TIMER_RING; ++i) CK(cudaEventCreate(&G.timer_ev[i]));
+        G.timer_created = 1;
+    }
+    CK(cudaDeviceSynchronize());   /* no pair of an earlier timing is still pending */
+    strcpy(G.timer_name, name);
+    G.timer_n = 0;
+    G.timer_on = 1;
+    return OMC_OK;
+}
+
+int omc_stage_timer(float *mean_ms, int *count) {
+    if (!G.init) return omc_fail(OMC_ENOINIT, "omc_stage_timer: omc_init not called");
+    if (!mean_ms || !count) return omc_fail(OMC_EINVAL, "omc_stage_timer: null output");
+    *mean_ms = 0.f;
+    *count = 0;
+    if (!G.timer_created || G.timer_n == 0) return OMC_OK;
+    const int n = G.timer_n;
+    const int last = (n - 1) % OMC_TIMER_RING;
+    CK(cudaEventSynchronize(G.timer_ev[2 * last + 1]));
+    /* once the ring has wrapped, the current slot holds a tentative start */
+    const int cur = n % OMC_TIMER_RING;
+    double sum = 0.0;
+    int k = 0;
+    for (int i = 0; i < OMC_TIMER_RING && i < n; ++i) {
+        if (n >= OMC_TIMER_RING && i == cur) continue;
+        float t = 0.f;
+        CK(cudaEventElapsedTime(&t, G.timer_ev[2 * i], G.timer_ev[2 * i + 1]));
+        sum += t;
+        ++k;
+    }
+    *mean_ms = k ? (float)(sum / k) : 0.f;
+    *count = k;
+    return OMC_OK;
+}
+
+static void timer_boundary(cudaStream_t s, const char *ended) {
+    const int slot = G.timer_n % OMC_TIMER_RING;
+    if (ended && !strcmp(ended, G.timer_name)) {
+        cudaEventRecord(G.timer_ev[2 * slot + 1], s);
+        G.timer_n++;
+        cudaEventRecord(G.timer_ev[2 * (G.timer_n % OMC_TIMER_RING)], s);
+    } else {
+        cudaEventRecord(G.timer_ev[2 * slot], s);
+    }
+}
+
 static void prof_begin(cudaStream_t s) {
     G.prof_nev = 0;
     if (G.profiling) {
         cudaEventRecord(G.ev[0], s);
         G.prof_nev = 1;
     }
+    if (G.timer_on) timer_boundary(s, NULL);
 }
 
-/* Ends the stage `name` on stream s (profiling mode only). */
+/* Ends the stage `name` on stream s (profiling or stage-timer mode only). */
 void omc_prof_mark(cudaStream_t s, const char *name) {
     if (G.profiling && G.prof_nev > 0 && G.prof_nev < OMC_NSTAGE_EV) {
         cudaEventRecord(G.ev[G.prof_nev], s);
         G.prof_names[G.prof_nev - 1] = name;
         G.prof_nev++;
     }
+    if (G.timer_on) timer_boundary(s, name);
 }
 
 /* ---------------------------------------------------------------- forward -- */
@@ -561,7 +637,7 @@ static size_t noalloc_layout(const omc_layer_dev *P, int T, char *base, omc_ws *
     TAKE(topk_w, float *, Tz * K * 4);
     TAKE(sg, float *, Tz * 4);
     TAKE(counts, int *, (E + 4) * 4 * 3 + 64);
-    TAKE(rowinfo, int *, R * 4);
+    TAKE(rowinfo, int *, R * 8);   /* rowinfo, then roww */
     TAKE(work, int *, (size_t)omc_mma_work_items(P, (int)R) * 16);
     TAKE(xp, uint16_t *, (size_t)P->D_pad * R * 2);
     TAKE(hp, uint16_t *, Imax_pad * R * 2);
@@ -572,6 +648,7 @@ static size_t noalloc_layout(const omc_layer_dev *P, int T, char *base, omc_ws *
         ws->offsets = ws->counts + (E + 4);
         ws->fill = ws->counts + 2 * (E + 4);
         ws->nwork = ws->counts + 3 * (E + 4);
+        ws->roww = (float *)(ws->rowinfo + R);
         ws->x = ws->out = NULL;
         ws->T_cap = T;
         ws->R_cap = (int)R;

@@ -13,6 +13,7 @@ extern "C" {
 #define OMC_MAX_CHUNKS 512
 #define OMC_MAX_HOST_BLOCKS 65536
 #define OMC_NSTAGE_EV 12
+#define OMC_TIMER_RING 1024          /* stage-timer event pairs kept */
 
 typedef struct {
     int used;
@@ -57,6 +58,10 @@ typedef struct {
     int profiling, prof_valid, prof_nev;
     cudaEvent_t ev[OMC_NSTAGE_EV];
     const char *prof_names[OMC_NSTAGE_EV];
+    /* stage timer: one event pair around a named stage of every forward */
+    int timer_on, timer_n, timer_created;
+    char timer_name[32];
+    cudaEvent_t timer_ev[2 * OMC_TIMER_RING];
     int path_override;              /* 0 auto, 1 gemv, 2 mma (OMC_FFN_PATH) */
     /* expert parallelism */
     int ep_rank, ep_world;

@@ -60,11 +60,28 @@ extern "C" {
 
 static inline int omc_round_up(int x, int m) { return (x + m - 1) / m * m; }
 
-/* One expert's three tiled matrices and padded scales. */
+/* One expert's three tiled matrices and padded scales.
+ *
+ * Weights are stored as 128-row x 64-column int8 blocks (8 KiB; inside a
+ * block, 16-byte chunk c of row r sits at (c*128 + r)*16) grouped in tile
+ * PAIRS whose K blocks interleave: block kb of member m of pair p is at
+ * ((p*nkb + kb)*2 + m) * 8 KiB, so one K block of a pair is 16 KiB of
+ * contiguous memory (one bulk copy).  g and u share one buffer as members
+ * 0 and 1 of pair mt (u = g + 8 KiB); the down matrix pairs its consecutive
+ * row tiles 2p and 2p+1.  OMC_PAIR_STRIDE is the distance between two K
+ * blocks of one tile. */
 typedef struct {
     const int8_t *g, *u, *d;
     const float *gs, *us, *ds;
 } omc_expert_ptrs;
+
+#define OMC_PAIR_STRIDE (2 * OMC_BLK_BYTES)
+
+/* Byte offset of block (row tile t, K block kb) of a matrix whose tiles pair
+ * up consecutively (the down matrix). */
+static inline __host__ __device__ size_t omc_dblk(int t, int kb, int nkb) {
+    return ((size_t)((t >> 1) * nkb + kb) * 2 + (t & 1)) * OMC_BLK_BYTES;
+}
 
 /* Layer parameters handed to kernels by value. */
 typedef struct {
@@ -90,6 +107,7 @@ typedef struct {
     int *offsets;                 /* [E + 3] padded row offsets           */
     int *fill;                    /* [E + 2]                              */
     int *rowinfo;                 /* [R]: routed slot t*k+kk, T*k+t shared, -1 pad */
+    float *roww;                  /* [R]: routing weight of the row (1 shared, 0 pad) */
     int *work;                    /* tile work list                       */
     int *nwork;                   /* [4] work counts                      */
     uint16_t *xp;                 /* AOL f16 [D_pad/64][R][64]            */
@@ -100,7 +118,10 @@ typedef struct {
 } omc_ws;
 
 /* ---- launchers (CUDA files), all enqueue on `s` ---------------------- */
-int omc_launch_relayout(const int8_t *src, int O, int K, int8_t *dst, int O_pad, int K_pad, cudaStream_t s);
+/* member >= 0: tile t of src becomes member `member` of pair t (g, u);
+ * member < 0: tiles pair up consecutively (d). */
+int omc_launch_relayout(const int8_t *src, int O, int K, int8_t *dst, int O_pad, int K_pad, int member,
+                        cudaStream_t s);
 int omc_launch_i8_to_f32(const int8_t *src, float *dst, long long n, cudaStream_t s);
 int omc_launch_router(const omc_layer_dev *L, const float *x, int T, const omc_ws *ws,
                       int32_t *topk_idx, float *topk_w, cudaStream_t s);

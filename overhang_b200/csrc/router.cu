@@ -18,15 +18,21 @@
 
 namespace {
 
-constexpr int RT_EXPERTS = 32;   // experts per block (one per lane)
-constexpr int RT_WARPS = 4;      // warps per block
-constexpr int RT_R = 2;          // tokens per thread: two independent chains fill the FADD latency
-constexpr int RT_TOKENS = RT_WARPS * RT_R;
-constexpr int RT_CHUNK = 128;    // K elements per pipeline stage
-constexpr int RT_STAGES = 4;     // cp.async stages in flight
-constexpr int RT_WROW = RT_CHUNK + 4;   // padded smem row (conflict-free float4 reads)
-constexpr int RT_STAGE_FLOATS = RT_EXPERTS * RT_WROW + RT_TOKENS * RT_CHUNK;
-constexpr size_t RT_SMEM = (size_t)RT_STAGES * RT_STAGE_FLOATS * sizeof(float);
+// ---- logits -----------------------------------------------------------------
+// Block = 8 tokens x 32 router rows, 4 warps.  Lane l of warp w owns token
+// (l & 7) and rows 8w + 2(l >> 3) + {0, 1}: two chains per thread.  Per four
+// K elements a warp reads one 16-byte x vector (8 distinct tokens, one
+// wavefront) and two 16-byte row vectors (4 distinct rows each, one wavefront
+// each), so shared-memory traffic is 3 wavefronts per 64 chains instead of 5
+// per 32 with one row per lane.  K streams through a 4-stage cp.async ring.
+constexpr int RL_TOK = 8;                   // tokens per block
+constexpr int RL_ROWS = 32;                 // router rows per block
+constexpr int RL_THREADS = 128;
+constexpr int RL_CH = 128;                  // K elements per stage
+constexpr int RL_ST = 4;                    // stages
+constexpr int RL_LD = RL_CH + 4;            // padded row: 8 consecutive rows hit 8 distinct bank quads
+constexpr int RL_STAGE = (RL_TOK + RL_ROWS) * RL_LD;            // floats per stage
+constexpr size_t RL_SMEM = (size_t)RL_ST * RL_STAGE * sizeof(float);   // 84,480 B
 
 __device__ __forceinline__ void cp_async16(void *smem_dst, const void *gsrc, bool valid) {
     const uint32_t d = smem_u32(smem_dst);
@@ -37,102 +43,109 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
+// (a0, a1) = (RN(a0 + b0), RN(a1 + b1)): two independent IEEE single adds in
+// one packed instruction; each lane of the pair rounds exactly as add.rn.f32.
+__device__ __forceinline__ void add2_rn(float &a0, float &a1, float b0, float b1) {
+    asm("{\n\t.reg .b64 ra, rb;\n\t"
+        "mov.b64 ra, {%0, %1};\n\t"
+        "mov.b64 rb, {%2, %3};\n\t"
+        "add.rn.f32x2 ra, ra, rb;\n\t"
+        "mov.b64 {%0, %1}, ra;\n\t}"
+        : "+f"(a0), "+f"(a1)
+        : "f"(b0), "f"(b1));
+}
+
 // logits[t][j], j < nrows: rows 0..E-1 are the router, row E (when
-// has_shared) the shared-expert gate vector.  Each thread runs two
-// (token, expert) chains side by side, so a warp issues every cycle while
-// each chain keeps its own sequential order; the K dimension streams through
-// a 4-stage cp.async ring so the chains never wait on memory.
-__global__ void __launch_bounds__(RT_WARPS * 32) router_logits_kernel(const float *__restrict__ x, int T, int D,
-                                                            const float *__restrict__ W,
-                                                            const float *__restrict__ Ws, int E,
-                                                            const float *__restrict__ sh_gate, int nrows,
-                                                            float *__restrict__ logits, int ldl) {
+// has_shared) the shared-expert gate vector.  Every (token, row) value is the
+// reference's chain acc = RN(acc + RN(x[i] * w[i])), i ascending.
+__global__ void __launch_bounds__(RL_THREADS) router_logits_kernel(const float *__restrict__ x, int T, int D,
+                                                                    const float *__restrict__ W,
+                                                                    const float *__restrict__ Ws, int E,
+                                                                    const float *__restrict__ sh_gate, int nrows,
+                                                                    float *__restrict__ logits, int ldl) {
     extern __shared__ __align__(16) float rsm[];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int row0 = blockIdx.y * RT_EXPERTS, t0 = blockIdx.x * RT_TOKENS;
-    const int row = row0 + lane, ta = t0 + warp * RT_R;
-    const int nchunk = (D + RT_CHUNK - 1) / RT_CHUNK;
-    auto load = [&](int chunk) {
-        float *st = rsm + (size_t)(chunk % RT_STAGES) * RT_STAGE_FLOATS;
-        float *ws = st, *xs = st + RT_EXPERTS * RT_WROW;
-        const int c0 = chunk * RT_CHUNK;
-        for (int i = threadIdx.x; i < (RT_EXPERTS + RT_TOKENS) * (RT_CHUNK / 4); i += blockDim.x) {
-            const int r = i / (RT_CHUNK / 4), c = (i % (RT_CHUNK / 4)) * 4;
-            if (r < RT_EXPERTS) {
-                const int gr = row0 + r;
-                const bool ok = gr < nrows && c0 + c < D;
-                const float *src = ok ? ((gr < E) ? W + (size_t)gr * D : sh_gate) + c0 + c : W;
-                cp_async16(ws + r * RT_WROW + c, src, ok);
+    const int t0 = blockIdx.x * RL_TOK, row0 = blockIdx.y * RL_ROWS;
+    const int tok = lane & 7, rl = warp * 8 + (lane >> 3) * 2;   // rows rl, rl+1 of the block
+    const int nch = (D + RL_CH - 1) / RL_CH;
+    auto load = [&](int ch) {
+        float *st = rsm + (size_t)(ch % RL_ST) * RL_STAGE;
+        const int c0 = ch * RL_CH;
+        // one warp copies one 512-byte row segment per pass (coalesced)
+        for (int i = threadIdx.x; i < (RL_TOK + RL_ROWS) * (RL_CH / 4); i += RL_THREADS) {
+            const int r = i / (RL_CH / 4), c = (i % (RL_CH / 4)) * 4;
+            const float *src;
+            bool ok;
+            if (r < RL_TOK) {
+                ok = t0 + r < T && c0 + c < D;
+                src = x + (size_t)(t0 + r) * D + c0 + c;
             } else {
-                const int tr = r - RT_EXPERTS;
-                const bool ok = t0 + tr < T && c0 + c < D;
-                cp_async16(xs + tr * RT_CHUNK + c, ok ? x + (size_t)(t0 + tr) * D + c0 + c : x, ok);
+                const int gr = row0 + r - RL_TOK;
+                ok = gr < nrows && c0 + c < D;
+                src = (gr < E ? W + (size_t)gr * D : sh_gate) + c0 + c;
             }
+            cp_async16(st + r * RL_LD + c, ok ? src : x, ok);
         }
     };
 #pragma unroll
-    for (int sidx = 0; sidx < RT_STAGES - 1; ++sidx) {
-        if (sidx < nchunk) load(sidx);
+    for (int s = 0; s < RL_ST - 1; ++s) {
+        if (s < nch) load(s);
         cp_async_commit();
     }
     float acc0 = 0.f, acc1 = 0.f;
-    for (int chunk = 0; chunk < nchunk; ++chunk) {
-        if (chunk + RT_STAGES - 1 < nchunk) load(chunk + RT_STAGES - 1);
+    for (int ch = 0; ch < nch; ++ch) {
+        cp_async_wait<RL_ST - 2>();   // chunk ch has landed (this thread's copies)
+        __syncthreads();              // ... everyone's; and chunk ch-1's stage is free
+        if (ch + RL_ST - 1 < nch) load(ch + RL_ST - 1);
         cp_async_commit();
-        cp_async_wait<RT_STAGES - 1>();
-        __syncthreads();
-        const float *st = rsm + (size_t)(chunk % RT_STAGES) * RT_STAGE_FLOATS;
-        const float *wrow = st + lane * RT_WROW;
-        const float *xrow0 = st + RT_EXPERTS * RT_WROW + (warp * RT_R) * RT_CHUNK;
-        const float *xrow1 = xrow0 + RT_CHUNK;
-        const int clen = min(RT_CHUNK, D - chunk * RT_CHUNK);   // multiple of 4
-        // per chain: acc = RN(acc + RN(x*w)) in index order (no contraction)
-#pragma unroll 4
+        const float *st = rsm + (size_t)(ch % RL_ST) * RL_STAGE;
+        const float *xr = st + tok * RL_LD;
+        const float *w0 = st + (RL_TOK + rl) * RL_LD, *w1 = w0 + RL_LD;
+        const int clen = min(RL_CH, D - ch * RL_CH);     // a multiple of 4
+#pragma unroll 8
         for (int c = 0; c < clen; c += 4) {
-            const float4 wv = *reinterpret_cast<const float4 *>(wrow + c);
-            const float4 x0 = *reinterpret_cast<const float4 *>(xrow0 + c);
-            const float4 x1 = *reinterpret_cast<const float4 *>(xrow1 + c);
-            acc0 = __fadd_rn(acc0, __fmul_rn(x0.x, wv.x));
-            acc1 = __fadd_rn(acc1, __fmul_rn(x1.x, wv.x));
-            acc0 = __fadd_rn(acc0, __fmul_rn(x0.y, wv.y));
-            acc1 = __fadd_rn(acc1, __fmul_rn(x1.y, wv.y));
-            acc0 = __fadd_rn(acc0, __fmul_rn(x0.z, wv.z));
-            acc1 = __fadd_rn(acc1, __fmul_rn(x1.z, wv.z));
-            acc0 = __fadd_rn(acc0, __fmul_rn(x0.w, wv.w));
-            acc1 = __fadd_rn(acc1, __fmul_rn(x1.w, wv.w));
+            const float4 xv = *reinterpret_cast<const float4 *>(xr + c);
+            const float4 a = *reinterpret_cast<const float4 *>(w0 + c);
+            const float4 b = *reinterpret_cast<const float4 *>(w1 + c);
+            add2_rn(acc0, acc1, __fmul_rn(xv.x, a.x), __fmul_rn(xv.x, b.x));
+            add2_rn(acc0, acc1, __fmul_rn(xv.y, a.y), __fmul_rn(xv.y, b.y));
+            add2_rn(acc0, acc1, __fmul_rn(xv.z, a.z), __fmul_rn(xv.z, b.z));
+            add2_rn(acc0, acc1, __fmul_rn(xv.w, a.w), __fmul_rn(xv.w, b.w));
         }
-        __syncthreads();
     }
-    if (row < nrows) {
-        if (Ws && row < E) {                                // matmul_q: y = acc * scale
-            acc0 = __fmul_rn(acc0, Ws[row]);
-            acc1 = __fmul_rn(acc1, Ws[row]);
-        }
-        if (ta < T) logits[(size_t)ta * ldl + row] = acc0;
-        if (ta + 1 < T) logits[(size_t)(ta + 1) * ldl + row] = acc1;
+    const int t = t0 + tok, r0 = row0 + rl;
+    if (t < T) {
+        if (r0 < nrows) logits[(size_t)t * ldl + r0] = (Ws && r0 < E) ? __fmul_rn(acc0, Ws[r0]) : acc0;
+        if (r0 + 1 < nrows) logits[(size_t)t * ldl + r0 + 1] = (Ws && r0 + 1 < E) ? __fmul_rn(acc1, Ws[r0 + 1]) : acc1;
     }
 }
 
-// One warp per token: softmax, top-k, renorm, shared-gate sigmoid, expert counts.
+// ---- select -----------------------------------------------------------------
+// One warp per token: softmax, top-k, renorm, shared-gate sigmoid, expert
+// counts.  Lane l holds logits l, l+32, ...; order-dependent sums run from a
+// shared-memory copy so that their dependent chain is the add latency alone.
+constexpr int SEL_WARPS = 4;
+
 template <int SEL_MAXV>   // ceil(E / 32) rounded up to a power of two
-__global__ void __launch_bounds__(128) router_select_kernel(const float *__restrict__ logits, int ldl, int T,
-                                                            int E, int K, int family, int renorm,
-                                                            int has_shared, int32_t *__restrict__ topk_idx,
-                                                            float *__restrict__ topk_w, float *__restrict__ sg,
-                                                            int *__restrict__ counts, int *err) {
+__global__ void __launch_bounds__(SEL_WARPS * 32) router_select_kernel(const float *__restrict__ logits, int ldl, int T,
+                                                                       int E, int K, int family, int renorm,
+                                                                       int has_shared, int32_t *__restrict__ topk_idx,
+                                                                       float *__restrict__ topk_w, float *__restrict__ sg,
+                                                                       int *__restrict__ counts, int *err) {
+    __shared__ __align__(16) float es_all[SEL_WARPS][SEL_MAXV * 32];
     const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
-    const int t = blockIdx.x * 4 + wib;
+    const int t = blockIdx.x * SEL_WARPS + wib;
     if (t >= T) return;
+    float *es = es_all[wib];
     const float *lg = logits + (size_t)t * ldl;
-    const int nv = (E + 31) / 32;
     float v[SEL_MAXV];
     // max, as `if (x[i] > m) m = x[i]` from m = -1e30f
     float m = -1e30f;
 #pragma unroll
     for (int j = 0; j < SEL_MAXV; ++j) {
         const int i = lane + 32 * j;
-        v[j] = (j < nv && i < E) ? lg[i] : -INFINITY;
-        if (j < nv && i < E && v[j] > m) m = v[j];
+        v[j] = i < E ? lg[i] : -INFINITY;
+        if (i < E && v[j] > m) m = v[j];
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
@@ -142,88 +155,103 @@ __global__ void __launch_bounds__(128) router_select_kernel(const float *__restr
 #pragma unroll
     for (int j = 0; j < SEL_MAXV; ++j) {
         const int i = lane + 32 * j;
-        if (j < nv && i < E) {
+        if (i < E) {
             v[j] = omc_expf_glibc(__fsub_rn(v[j], m));
             tiny |= v[j] < exact_floor;
+            es[i] = v[j];
         }
     }
     __syncwarp();
     float sf;   // the divisor as the reference uses it
-    if (family == OMC_FAMILY_QWEN) {
+    if (family == OMC_FAMILY_QWEN && !__any_sync(0xffffffffu, tiny)) {
         // double running sum.  When every term is >= 2^(ceil(log2 E) - 30) all
-        // partial sums are exact in double, so any order gives the reference's
-        // value; otherwise sum sequentially in index order like the CPU.
-        double s;
-        if (!__any_sync(0xffffffffu, tiny)) {
-            s = 0.0;
+        // partial sums are exact in double, so any order gives the
+        // reference's value: a butterfly.
+        double s = 0.0;
 #pragma unroll
-            for (int j = 0; j < SEL_MAXV; ++j) {
-                const int i = lane + 32 * j;
-                if (j < nv && i < E) s = __dadd_rn(s, (double)v[j]);
-            }
+        for (int j = 0; j < SEL_MAXV; ++j)
+            if (lane + 32 * j < E) s = __dadd_rn(s, (double)v[j]);
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) s = __dadd_rn(s, __shfl_xor_sync(0xffffffffu, s, o));
-        } else {
-            // every lane runs the same index-order sum; values arrive by shuffle
-            s = 0.0;
-#pragma unroll
-            for (int j = 0; j < SEL_MAXV; ++j) {
-                if (j >= nv) break;
-                for (int l = 0; l < 32 && 32 * j + l < E; ++l) s = __dadd_rn(s, (double)__shfl_sync(0xffffffffu, v[j], l));
-            }
+        for (int o = 16; o > 0; o >>= 1) s = __dadd_rn(s, __shfl_xor_sync(0xffffffffu, s, o));
+        sf = __double2float_rn(s);
+    } else if (family == OMC_FAMILY_QWEN) {
+        // otherwise the index-order double sum of engines/qwen.c:163, every lane
+        double s = 0.0;
+        int i = 0;
+        for (; i + 4 <= E; i += 4) {
+            const float4 q = *reinterpret_cast<const float4 *>(es + i);
+            s = __dadd_rn(s, (double)q.x);
+            s = __dadd_rn(s, (double)q.y);
+            s = __dadd_rn(s, (double)q.z);
+            s = __dadd_rn(s, (double)q.w);
         }
+        for (; i < E; ++i) s = __dadd_rn(s, (double)es[i]);
         sf = __double2float_rn(s);
     } else {
-        // float running sum in index order (engines/olmoe.c:172); every lane
-        // runs the same chain, values arrive by shuffle
+        // float running sum in index order (engines/olmoe.c:172), every lane
         float s = 0.f;
-#pragma unroll
-        for (int j = 0; j < SEL_MAXV; ++j) {
-            if (j >= nv) break;
-            for (int l = 0; l < 32 && 32 * j + l < E; ++l) s = __fadd_rn(s, __shfl_sync(0xffffffffu, v[j], l));
+        int i = 0;
+#pragma unroll 4
+        for (; i + 4 <= E; i += 4) {
+            const float4 q = *reinterpret_cast<const float4 *>(es + i);
+            s = __fadd_rn(s, q.x);
+            s = __fadd_rn(s, q.y);
+            s = __fadd_rn(s, q.z);
+            s = __fadd_rn(s, q.w);
         }
+        for (; i < E; ++i) s = __fadd_rn(s, es[i]);
         sf = s;
     }
+    // probabilities as order keys: p >= 0, so bits(p) + 1 orders like p and
+    // 0 marks "not available" (outside E, NaN, or already taken).
+    uint32_t key[SEL_MAXV];
+    float pv[SEL_MAXV];
 #pragma unroll
-    for (int j = 0; j < SEL_MAXV; ++j) v[j] = (j < nv && lane + 32 * j < E) ? __fdiv_rn(v[j], sf) : -INFINITY;
-    // top-k: largest probability, ties to the lowest id
-    uint32_t taken = 0;
-    float val[OMC_MAX_K];
-    int idx[OMC_MAX_K];
-    for (int kk = 0; kk < K; ++kk) {
-        float bv = -INFINITY;
-        int bi = 0x7fffffff;
-#pragma unroll
-        for (int j = 0; j < SEL_MAXV; ++j) {
-            const int i = lane + 32 * j;
-            if (j < nv && i < E && !((taken >> j) & 1u) && v[j] > bv) { bv = v[j]; bi = i; }
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-            if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
-        }
-        if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
-        val[kk] = bv;
-        idx[kk] = bi;
+    for (int j = 0; j < SEL_MAXV; ++j) {
+        const int i = lane + 32 * j;
+        pv[j] = i < E ? __fdiv_rn(v[j], sf) : 0.f;
+        key[j] = (i < E && pv[j] == pv[j]) ? __float_as_uint(pv[j]) + 1u : 0u;
     }
-    if (lane == 0) {
-        if (renorm || family == OMC_FAMILY_QWEN) {
-            float sm = 0.f;
-            for (int kk = 0; kk < K; ++kk) sm = __fadd_rn(sm, val[kk]);
-            for (int kk = 0; kk < K; ++kk) val[kk] = __fdiv_rn(val[kk], sm);
+    // top-k: engines/olmoe.c:355-362 -- largest p, ties to the lowest id
+    int my_idx = -1;
+    float my_val = 0.f;
+    for (int kk = 0; kk < K; ++kk) {
+        uint32_t bk = 0;
+        int bj = 0;
+#pragma unroll
+        for (int j = 0; j < SEL_MAXV; ++j)
+            if (key[j] > bk) { bk = key[j]; bj = j; }      // strict: lowest j (= lowest id) of this lane
+        const uint32_t kmax = __reduce_max_sync(0xffffffffu, bk);
+        const uint32_t cand = (bk == kmax && kmax != 0u) ? (uint32_t)(lane + 32 * bj) : 0xffffffffu;
+        const uint32_t best = __reduce_min_sync(0xffffffffu, cand);
+        if (kmax != 0u && (int)(best & 31) == lane) {
+#pragma unroll
+            for (int j = 0; j < SEL_MAXV; ++j)
+                if (j == (int)(best >> 5)) key[j] = 0u;
         }
-        for (int kk = 0; kk < K; ++kk) {
-            if (idx[kk] < 0 || idx[kk] >= E) { omc_dev_error(err, OMC_DEVERR_ROUTE, OMC_SITE_ROUTER, t); continue; }
-            topk_idx[(size_t)t * K + kk] = idx[kk];
-            topk_w[(size_t)t * K + kk] = val[kk];
-            atomicAdd(&counts[idx[kk]], 1);
+        if (lane == kk) {
+            my_idx = kmax != 0u ? (int)best : -1;
+            my_val = __uint_as_float(kmax - 1u);
         }
-        if (has_shared) {
-            const float z = lg[E];
-            sg[t] = __fdiv_rn(1.f, __fadd_rn(1.f, omc_expf_glibc(-z)));   // engines/qwen.c:158,461
+    }
+    // renorm: float sum in selection order, then divide (engines/olmoe.c:363)
+    if (renorm || family == OMC_FAMILY_QWEN) {
+        float sm = 0.f;
+        for (int kk = 0; kk < K; ++kk) sm = __fadd_rn(sm, __shfl_sync(0xffffffffu, my_val, kk));
+        my_val = __fdiv_rn(my_val, sm);
+    }
+    if (lane < K) {
+        if (my_idx < 0 || my_idx >= E) {
+            omc_dev_error(err, OMC_DEVERR_ROUTE, OMC_SITE_ROUTER, t);
+        } else {
+            topk_idx[(size_t)t * K + lane] = my_idx;
+            topk_w[(size_t)t * K + lane] = my_val;
+            atomicAdd(&counts[my_idx], 1);
         }
+    }
+    if (has_shared && lane == 0) {
+        const float z = lg[E];
+        sg[t] = __fdiv_rn(1.f, __fadd_rn(1.f, omc_expf_glibc(-z)));   // engines/qwen.c:158,461
     }
 }
 
@@ -235,21 +263,22 @@ extern "C" int omc_launch_router(const omc_layer_dev *L, const float *x, int T, 
     if (L->E > OMC_MAX_E || L->k > OMC_MAX_K || (L->D & 3)) return OMC_EINVAL;
     static int attr_done = 0;
     if (!attr_done) {
-        if (cudaFuncSetAttribute(router_logits_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)RT_SMEM) !=
+        if (cudaFuncSetAttribute(router_logits_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)RL_SMEM) !=
             cudaSuccess)
             return OMC_ECUDA;
         attr_done = 1;
     }
     const int nrows = L->E + (L->has_shared ? 1 : 0);
     const int ldl = L->E + 1;
-    dim3 g1((T + RT_TOKENS - 1) / RT_TOKENS, (nrows + RT_EXPERTS - 1) / RT_EXPERTS);
-    router_logits_kernel<<<g1, RT_WARPS * 32, RT_SMEM, s>>>(x, T, L->D, L->router, L->router_i8 ? L->router_s : nullptr, L->E,
-                                                  L->sh_gate, nrows, ws->logits, ldl);
+    const dim3 g1((T + RL_TOK - 1) / RL_TOK, (nrows + RL_ROWS - 1) / RL_ROWS);
+    router_logits_kernel<<<g1, RL_THREADS, RL_SMEM, s>>>(x, T, L->D, L->router, L->router_i8 ? L->router_s : nullptr,
+                                                         L->E, L->sh_gate, nrows, ws->logits, ldl);
     omc_prof_mark(s, "router_logits");
     const int nv = (L->E + 31) / 32;
-    const dim3 g2((T + 3) / 4);
-#define SEL(NV) router_select_kernel<NV><<<g2, 128, 0, s>>>(ws->logits, ldl, T, L->E, L->k, L->family, L->renorm, \
-                                                          L->has_shared, topk_idx, topk_w, ws->sg, ws->counts, ws->err)
+    const dim3 g2((T + SEL_WARPS - 1) / SEL_WARPS);
+#define SEL(NV)                                                                                                    \
+    router_select_kernel<NV><<<g2, SEL_WARPS * 32, 0, s>>>(ws->logits, ldl, T, L->E, L->k, L->family, L->renorm, \
+                                                         L->has_shared, topk_idx, topk_w, ws->sg, ws->counts, ws->err)
     if (nv <= 1) SEL(1);
     else if (nv <= 2) SEL(2);
     else if (nv <= 4) SEL(4);

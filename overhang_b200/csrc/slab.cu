@@ -9,7 +9,7 @@
 namespace {
 
 __global__ void relayout_kernel(const int8_t *__restrict__ src, int O, int K, int8_t *__restrict__ dst,
-                                int O_pad, int K_pad) {
+                                int O_pad, int K_pad, int member) {
     const int nkb = K_pad / OMC_KB;
     const long long nchunks = (long long)O_pad * K_pad / 16;
     for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < nchunks;
@@ -32,7 +32,10 @@ __global__ void relayout_kernel(const int8_t *__restrict__ src, int O, int K, in
                 }
             }
         }
-        *reinterpret_cast<int4 *>(dst + idx * 16) = make_int4(w[0], w[1], w[2], w[3]);
+        // paired tiles: member `member` of pair ot, or tiles 2p / 2p+1 of pair p
+        const size_t boff = member >= 0 ? ((size_t)ot * nkb + kb) * 2 * OMC_BLK_BYTES + (size_t)member * OMC_BLK_BYTES
+                                        : omc_dblk(ot, kb, nkb);
+        *reinterpret_cast<int4 *>(dst + boff + (size_t)within * 16) = make_int4(w[0], w[1], w[2], w[3]);
     }
 }
 
@@ -44,10 +47,10 @@ __global__ void i8_to_f32_kernel(const int8_t *__restrict__ src, float *__restri
 }  // namespace
 
 extern "C" int omc_launch_relayout(const int8_t *src, int O, int K, int8_t *dst, int O_pad, int K_pad,
-                                   cudaStream_t s) {
+                                   int member, cudaStream_t s) {
     const long long nchunks = (long long)O_pad * K_pad / 16;
     const int grid = (int)((nchunks + 255) / 256 < 65535 ? (nchunks + 255) / 256 : 65535);
-    relayout_kernel<<<grid, 256, 0, s>>>(src, O, K, dst, O_pad, K_pad);
+    relayout_kernel<<<grid, 256, 0, s>>>(src, O, K, dst, O_pad, K_pad, member);
     omc_g_launches += 1;
     return cudaGetLastError() == cudaSuccess ? 0 : OMC_ECUDA;
 }
