@@ -113,7 +113,9 @@ int omc_moe_forward(int layer, const float *x, int T, float *out,
                     int32_t *topk_idx, float *topk_w);
 
 /* The same with DEVICE pointers, enqueued on `stream` (a cudaStream_t; NULL
- * = the library's stream).  Returns once enqueued; the caller synchronises. */
+ * = the library's stream).  Returns once enqueued; the caller synchronises.
+ * x and out must be 16-byte aligned (OMC_EINVAL otherwise): rows are moved
+ * with 16-byte bulk copies and vector stores. */
 int omc_moe_forward_dev(int layer, const float *x, int T, float *out,
                         int32_t *topk_idx, float *topk_w, void *stream);
 

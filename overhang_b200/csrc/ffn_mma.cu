@@ -4,12 +4,11 @@
 // engines/qwen.c:480-493) and the Metal per-expert dq_gemm dispatches
 // (metal/om_metal.mm:186-229) with four kernels:
 //
-//   plan    one block: expert row counts -> 16-row padded offsets, and the
-//           tile work lists of the two GEMMs (the batch-union of
-//           engines/olmoe.c:366-378, on the device)
 //   gather  every routed (token, choice) slot -> one f16 row of the
-//           activation operand, grouped by expert (+ one row per token for
-//           the shared expert); padding rows zeroed
+//           activation operand at the row the dispatch plan gave it
+//           (omc_plan.cuh, built by the router's last select block),
+//           grouped by expert (+ one row per token for the shared expert);
+//           padding rows zeroed
 //   gemm<1> per (expert, 128 rows of I, <=128 tokens): gate and up
 //           H^T = silu(gs*Wg.X^T) * (us*Wu.X^T), written as the f16 operand of
 //   gemm<2> per (expert, 128 rows of D, <=128 tokens): Y^T = ds*Wd.H^T,
@@ -61,7 +60,7 @@
 
 namespace {
 
-constexpr int NMAX = 128;                 // tokens per work item (MMA N)
+constexpr int NMAX = OMC_NMAX;            // tokens per work item (MMA N)
 constexpr int NGRP = 2;                   // dequant groups (alternate K blocks)
 constexpr int NDQ = 8;                    // warps per dequant group: 2 tiles x 4 lane quarters
 constexpr int NEPI = 8;                   // epilogue warps: two per TMEM lane quarter
@@ -98,7 +97,8 @@ struct GemmArgs {
     omc_layer_dev L;
     const int4 *work;
     const int *nwork;
-    const uint16_t *act;       // A operand rows (AOL): x (gemm1) or h (gemm2)
+    const uint16_t *act;       // gemm2: h operand rows (AOL, swizzled)
+    const uint16_t *xh;        // gemm1: f16 tokens [T][D], gathered per operand row
     uint16_t *hout;            // gemm1: h operand out
     float *ypart;              // gemm2: per-slot partials [T][k+1][D]
     const int *rowinfo;        // gemm2: row -> slot
@@ -128,11 +128,6 @@ __device__ __forceinline__ bool warp_wait(uint64_t *bar, uint32_t parity, int *e
     return __all_sync(0xffffffffu, wait_or_abort(bar, parity, err, site, abort_flag));
 }
 
-__device__ __forceinline__ uint32_t f32x2_to_f16x2_sat(float lo, float hi) {
-    uint32_t r;
-    asm("cvt.rn.satfinite.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
-    return r;
-}
 
 __device__ __forceinline__ float swiglu_f(int family, float g, float u) {
     const float e = __expf(-g);
@@ -140,9 +135,6 @@ __device__ __forceinline__ float swiglu_f(int family, float g, float u) {
     return __fdividef(g, 1.f + e) * u;
 }
 
-__device__ __forceinline__ void fence_proxy_async_smem() {
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
 
 // The 128-row weight blocks an item multiplies: phase 1 = gate tile mt and up
 // tile mt; phase 2 = down tiles 2*mt and 2*mt+1 (the second absent past D_rows).
@@ -220,6 +212,12 @@ struct StageIter {
 __device__ __forceinline__ void cp_async16_hint(void *smem_dst, const void *gsrc, uint64_t policy) {
     asm volatile("cp.async.cg.shared.global.L2::cache_hint [%0], [%1], 16, %2;" ::"r"(smem_u32(smem_dst)), "l"(gsrc),
                  "l"(policy)
+                 : "memory");
+}
+// The same with src_size 0 when !valid: the 16 bytes are zero-filled.
+__device__ __forceinline__ void cp_async16_zfill_hint(void *smem_dst, const void *gsrc, bool valid, uint64_t policy) {
+    asm volatile("cp.async.cg.shared.global.L2::cache_hint [%0], [%1], 16, %2, %3;" ::"r"(smem_u32(smem_dst)),
+                 "l"(gsrc), "r"(valid ? 16 : 0), "l"(policy)
                  : "memory");
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
@@ -401,6 +399,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_gemm_kernel(const GemmArgs a)
         for (int j = 0; j < grp; ++j) pr.step(c);
         const int gt = (dq % NDQ) * 32 + lane;   // thread index within the group, 0..255
         const uint64_t keep = l2_policy_evict_last();
+        int xrow_item = -1, xrow[4] = {-1, -1, -1, -1};   // gemm1: token of each row this lane copies
         for (uint32_t i = grp; pr.valid && !*abort_flag; i += NGRP) {
             const int si = i % SI, st = i % ST, sa = i % SA;
             // token tile of this K block: per-lane cp.async (not a bulk copy, which would queue
@@ -408,10 +407,42 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_gemm_kernel(const GemmArgs a)
             // latency overlaps the int8 wait and the conversion
             if (!warp_wait(&emptyA[sa], ((i / SA) & 1) ^ 1, a.err, OMC_SITE_GEMM_DEQUANT, abort_flag)) break;
             {
-                const uint8_t *src = reinterpret_cast<const uint8_t *>(a.act) + (size_t)pr.kb * a.R * 128 +
-                                     (size_t)pr.n0 * 128;
                 uint8_t *dst = smem + OFF_A + sa * A_BYTES;
-                for (int ch = gt; ch < pr.n * 8; ch += NDQ * 32) cp_async16_hint(dst + ch * 16, src + ch * 16, keep);
+                if (PHASE == 1) {
+                    // gather: operand row j of the item is token xrow[j] of xh (its
+                    // routed slot's token, or every token for the shared expert);
+                    // padding rows are zero-filled.  Chunk ch = gt + 256u of the
+                    // tile is row (gt >> 3) + 32u, 16-byte column gt & 7.
+                    if (pr.idx != xrow_item) {
+                        xrow_item = pr.idx;
+#pragma unroll
+                        for (int u = 0; u < 4; ++u) {
+                            const int j = (gt >> 3) + 32 * u;
+                            int t = -1;
+                            if (j < pr.n) {
+                                const int slot = a.rowinfo[pr.n0 + j];
+                                const int nr = a.T * L.k;
+                                t = slot < 0 ? -1 : (slot < nr ? slot / L.k : slot - nr);
+                            }
+                            xrow[u] = t;
+                        }
+                    }
+                    const int c = gt & 7;
+                    const uint8_t *xcol = reinterpret_cast<const uint8_t *>(a.xh) + (size_t)pr.kb * 128 + c * 16;
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        const int j = (gt >> 3) + 32 * u;
+                        if (j >= pr.n) break;
+                        const bool live = xrow[u] >= 0;
+                        const uint8_t *src = live ? xcol + (size_t)xrow[u] * (size_t)L.D * 2 : xcol;
+                        cp_async16_zfill_hint(dst + j * 128 + ((c ^ (j & 7)) << 4), src, live, keep);
+                    }
+                } else {
+                    const uint8_t *src = reinterpret_cast<const uint8_t *>(a.act) + (size_t)pr.kb * a.R * 128 +
+                                         (size_t)pr.n0 * 128;
+                    for (int ch = gt; ch < pr.n * 8; ch += NDQ * 32)
+                        cp_async16_hint(dst + ch * 16, src + ch * 16, keep);
+                }
                 cp_async_commit();
             }
             if (!warp_wait(&fullI[si], (i / SI) & 1, a.err, OMC_SITE_GEMM_DEQUANT, abort_flag)) break;
@@ -581,138 +612,6 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_gemm_kernel(const GemmArgs a)
     }
 }
 
-// ---------------------------------------------------------------- plan ---
-// counts[g]: routed rows of expert g (the router's atomics); the shared
-// expert (g = E) gets T rows.  Writes offsets[0..G], the two work lists and
-// nwork[0..1]; zeroes fill[].
-__global__ void __launch_bounds__(1024) plan_kernel(const int *__restrict__ counts, int E, int has_shared, int T,
-                                                    int I_rows, int Is_rows, int D_rows, int R_cap, int cap1,
-                                                    int cap2, int *__restrict__ offsets, int *__restrict__ fill,
-                                                    int4 *__restrict__ work1, int4 *__restrict__ work2,
-                                                    int *__restrict__ nwork, int *err) {
-    __shared__ int s_pad[OMC_MAX_E + 1], s_off[OMC_MAX_E + 2], s_w1[OMC_MAX_E + 2], s_w2[OMC_MAX_E + 2];
-    const int G = E + (has_shared ? 1 : 0);
-    for (int g = threadIdx.x; g < G; g += blockDim.x) {
-        const int c = g < E ? counts[g] : T;
-        const int pad = (c + OMC_ROW_ALIGN - 1) / OMC_ROW_ALIGN * OMC_ROW_ALIGN;
-        s_pad[g] = pad;
-        const int nch = (pad + NMAX - 1) / NMAX;
-        const int mt1 = (g < E ? I_rows : Is_rows) / OMC_TM;
-        s_w1[g] = nch * mt1;
-        s_w2[g] = nch * ((D_rows / OMC_TM + 1) / 2);
-        fill[g] = 0;
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) {   // G <= 1025: a serial scan is a few microseconds
-        int o = 0, w1 = 0, w2 = 0;
-        for (int g = 0; g < G; ++g) {
-            s_off[g] = o;
-            o += s_pad[g];
-            const int a1 = s_w1[g], a2 = s_w2[g];
-            s_w1[g] = w1;
-            s_w2[g] = w2;
-            w1 += a1;
-            w2 += a2;
-        }
-        s_off[G] = o;
-        s_w1[G] = w1;
-        s_w2[G] = w2;
-        if (o > R_cap || w1 > cap1 || w2 > cap2) {
-            omc_dev_error(err, OMC_DEVERR_BOUNDS, OMC_SITE_DISPATCH, o);
-            nwork[0] = nwork[1] = 0;
-        } else {
-            nwork[0] = w1;
-            nwork[1] = w2;
-        }
-        nwork[2] = o;
-    }
-    __syncthreads();
-    const bool okcap = s_off[G] <= R_cap && s_w1[G] <= cap1 && s_w2[G] <= cap2;
-    for (int g = threadIdx.x; g <= G; g += blockDim.x) offsets[g] = s_off[g];
-    if (!okcap) return;
-    for (int g = threadIdx.x; g < G; g += blockDim.x) {
-        const int pad = s_pad[g];
-        if (!pad) continue;
-        const int nch = (pad + NMAX - 1) / NMAX;
-        const int mt1 = (g < E ? I_rows : Is_rows) / OMC_TM, mt2 = (D_rows / OMC_TM + 1) / 2;
-        int p1 = s_w1[g], p2 = s_w2[g];
-        for (int c = 0; c < nch; ++c) {
-            const int n0 = s_off[g] + c * NMAX;
-            const int n = min(NMAX, pad - c * NMAX);
-            for (int m = 0; m < mt1; ++m) work1[p1++] = make_int4(g, m, n0, n);
-            for (int m = 0; m < mt2; ++m) work2[p2++] = make_int4(g, m, n0, n);
-        }
-    }
-}
-
-// -------------------------------------------------------------- gather ---
-// One warp per task: routed slot, shared row, or padding row.
-__global__ void __launch_bounds__(256) gather_kernel(const float *__restrict__ x, int T, int D, int D_pad, int K,
-                                                     int E, int has_shared, const int32_t *__restrict__ topk_idx,
-                                                     const float *__restrict__ topk_w,
-                                                     const int *__restrict__ counts, const int *__restrict__ offsets,
-                                                     int *__restrict__ fill, int *__restrict__ rowinfo,
-                                                     float *__restrict__ roww, uint16_t *__restrict__ xp, int R,
-                                                     int *err) {
-    const int task = blockIdx.x * 8 + (threadIdx.x >> 5);
-    const int lane = threadIdx.x & 31;
-    const int nrouted = T * K, nshared = has_shared ? T : 0;
-    const int G = E + (has_shared ? 1 : 0);
-    int row = -1, t = -1, info = -1;
-    float wrow = 0.f;
-    if (task < nrouted) {
-        const int e = topk_idx[task];
-        if (e < 0 || e >= E) {
-            if (lane == 0) omc_dev_error(err, OMC_DEVERR_ROUTE, OMC_SITE_DISPATCH, task);
-            return;
-        }
-        int pos = 0;
-        if (lane == 0) pos = atomicAdd(&fill[e], 1);
-        pos = __shfl_sync(0xffffffffu, pos, 0);
-        row = offsets[e] + pos;
-        t = task / K;
-        info = task;
-        wrow = topk_w[task];
-    } else if (task < nrouted + nshared) {
-        t = task - nrouted;
-        row = offsets[E] + t;
-        info = nrouted + t;
-        wrow = 1.f;
-    } else {
-        const int p = task - nrouted - nshared;
-        const int g = p / (OMC_ROW_ALIGN - 1), j = p % (OMC_ROW_ALIGN - 1);
-        if (g >= G) return;
-        const int c = g < E ? counts[g] : T;
-        if (offsets[g] + c + j >= offsets[g + 1]) return;
-        row = offsets[g] + c + j;
-    }
-    if (row < 0 || row >= R) {
-        if (lane == 0) omc_dev_error(err, OMC_DEVERR_BOUNDS, OMC_SITE_DISPATCH, row);
-        return;
-    }
-    if (lane == 0) {
-        rowinfo[row] = info;
-        roww[row] = wrow;
-    }
-    uint8_t *base = reinterpret_cast<uint8_t *>(xp);
-    const int nkb = D_pad / 64;
-    for (int kb0 = 0; kb0 < nkb; kb0 += 4) {
-        const int kb = kb0 + (lane >> 3), c = lane & 7;
-        if (kb >= nkb) continue;
-        const int k = kb * 64 + c * 8;
-        uint4 o = make_uint4(0u, 0u, 0u, 0u);
-        if (t >= 0 && k < D) {
-            const float4 a = *reinterpret_cast<const float4 *>(x + (size_t)t * D + k);
-            const float4 b = *reinterpret_cast<const float4 *>(x + (size_t)t * D + k + 4);
-            o.x = f32x2_to_f16x2_sat(a.x, a.y);
-            o.y = f32x2_to_f16x2_sat(a.z, a.w);
-            o.z = f32x2_to_f16x2_sat(b.x, b.y);
-            o.w = f32x2_to_f16x2_sat(b.z, b.w);
-        }
-        *reinterpret_cast<uint4 *>(base + (size_t)kb * R * 128 + (size_t)row * 128 + ((c ^ (row & 7)) << 4)) = o;
-    }
-}
-
 // ------------------------------------------------------------- combine ---
 __global__ void __launch_bounds__(256) combine_kernel(const float *__restrict__ ypart, const float *__restrict__ sg,
                                                       int T, int D, int K, int has_shared, float *__restrict__ out) {
@@ -764,25 +663,17 @@ extern "C" int omc_launch_mma_ffn(const omc_layer_dev *L, const float *x, int T,
         cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
         attr_done = 1;
     }
-    const int E = L->E, G = E + (L->has_shared ? 1 : 0);
     const int R = ws->R_cap;
-    const int Imax_rows = L->has_shared && L->Is_rows > L->I_rows ? L->Is_rows : L->I_rows;
-    const int chunks_max = R / NMAX + G;
-    const int cap1 = chunks_max * (Imax_rows / OMC_TM);
-    const int cap2 = chunks_max * ((L->D_rows / OMC_TM + 1) / 2);
-    int4 *work1 = reinterpret_cast<int4 *>(ws->work);
-    int4 *work2 = work1 + cap1;
-    plan_kernel<<<1, 1024, 0, s>>>(ws->counts, E, L->has_shared, T, L->I_rows, L->Is_rows, L->D_rows, R, cap1, cap2,
-                                   ws->offsets, ws->fill, work1, work2, ws->nwork, ws->err);
-    const int ntasks = T * L->k + (L->has_shared ? T : 0) + G * (OMC_ROW_ALIGN - 1);
-    gather_kernel<<<(ntasks + 7) / 8, 256, 0, s>>>(x, T, L->D, L->D_pad, L->k, E, L->has_shared, topk_idx, topk_w,
-                                                  ws->counts, ws->offsets, ws->fill, ws->rowinfo, ws->roww, ws->xp,
-                                                  R, ws->err);
+    omc_plan_args pa;                      // built on the device by the router's last select block
+    omc_plan_setup(L, T, ws, &pa);
+    const int4 *work1 = reinterpret_cast<const int4 *>(pa.work1), *work2 = reinterpret_cast<const int4 *>(pa.work2);
+
     GemmArgs ga;
     ga.L = *L;
     ga.work = work1;
     ga.nwork = ws->nwork;
-    ga.act = ws->xp;
+    ga.act = ws->hp;
+    ga.xh = ws->xh;
     ga.hout = ws->hp;
     ga.ypart = ws->ypart;
     ga.rowinfo = ws->rowinfo;
@@ -801,6 +692,32 @@ extern "C" int omc_launch_mma_ffn(const omc_layer_dev *L, const float *x, int T,
     dim3 gc((L->D / 4 + 255) / 256, T);
     combine_kernel<<<gc, 256, 0, s>>>(ws->ypart, ws->sg, T, L->D, L->k, L->has_shared, out);
     omc_prof_mark(s, "combine");
-    omc_g_launches += 5;
+    omc_g_launches += 3;
     return cudaGetLastError() == cudaSuccess ? 0 : OMC_ECUDA;
+}
+
+extern "C" void omc_plan_setup(const omc_layer_dev *L, int T, const omc_ws *ws, omc_plan_args *pa) {
+    const int E = L->E, G = E + (L->has_shared ? 1 : 0);
+    const int R = ws->R_cap;
+    const int Imax_rows = L->has_shared && L->Is_rows > L->I_rows ? L->Is_rows : L->I_rows;
+    const int chunks_max = R / NMAX + G;
+    pa->E = E;
+    pa->K = L->k;
+    pa->T = T;
+    pa->has_shared = L->has_shared;
+    pa->I_rows = L->I_rows;
+    pa->Is_rows = L->Is_rows;
+    pa->D_rows = L->D_rows;
+    pa->R_cap = R;
+    pa->cap1 = chunks_max * (Imax_rows / OMC_TM);
+    pa->cap2 = chunks_max * ((L->D_rows / OMC_TM + 1) / 2);
+    pa->counts = ws->counts;
+    pa->offsets = ws->offsets;
+    pa->nwork = ws->nwork;
+    pa->slotrow = ws->slotrow;
+    pa->work1 = ws->work;
+    pa->work2 = ws->work + 4 * (size_t)pa->cap1;
+    pa->done = ws->done;
+    pa->rowinfo = ws->rowinfo;
+    pa->roww = ws->roww;
 }

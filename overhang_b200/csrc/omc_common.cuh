@@ -147,6 +147,19 @@ __device__ __forceinline__ void bulk_g2s(void *smem_dst, const void *gmem_src, u
         : "memory");
 }
 
+// (lo, hi) -> f16x2, round to nearest, saturated to +-65504.
+__device__ __forceinline__ uint32_t f32x2_to_f16x2_sat(float lo, float hi) {
+    uint32_t r;
+    asm("cvt.rn.satfinite.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+    return r;
+}
+
+// Orders this thread's generic-proxy accesses to shared memory with later
+// async-proxy ones (bulk copies, tcgen05.mma operand reads) and vice versa.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 // L2 eviction policies for the hinted copies: operands streamed once (the
 // expert weights) go first, operands re-read soon after they were written
 // (token tiles, h) stay.

@@ -420,10 +420,11 @@ int omc_ws_ensure(const omc_layer *L, int T, int host_io) {
     if ((rc = ws_buf(6, (void **)&W->counts, (E + 4) * 4 * 3 + 64))) return rc;
     if ((rc = ws_buf(7, (void **)&W->rowinfo, R * 8))) return rc;   /* rowinfo, then roww */
     if ((rc = ws_buf(8, (void **)&W->work, (size_t)omc_mma_work_items(P, (int)R) * 16))) return rc;
-    if ((rc = ws_buf(9, (void **)&W->xp, (size_t)P->D_pad * R * 2))) return rc;
+    if ((rc = ws_buf(9, (void **)&W->xh, Tz * D * 2))) return rc;
     if ((rc = ws_buf(10, (void **)&W->hp, Imax_pad * R * 2))) return rc;
     if ((rc = ws_buf(11, (void **)&W->ypart, Tz * (K + 1) * D * 4))) return rc;
     if ((rc = ws_buf(12, (void **)&W->hbuf, (Tz * K + Tz) * Imax_rows * 4))) return rc;
+    if ((rc = ws_buf(13, (void **)&W->slotrow, Tz * K * 4))) return rc;
     omc_ws *ws = &G.ws;
     ws->T_cap = T;
     ws->R_cap = (int)R;
@@ -435,12 +436,13 @@ int omc_ws_ensure(const omc_layer *L, int T, int host_io) {
     ws->sg = W->sg;
     ws->counts = W->counts;
     ws->offsets = W->counts + (E + 4);
-    ws->fill = W->counts + 2 * (E + 4);
+    ws->done = W->counts + 2 * (E + 4);
     ws->nwork = W->counts + 3 * (E + 4);
+    ws->slotrow = W->slotrow;
     ws->rowinfo = W->rowinfo;
     ws->roww = (float *)(W->rowinfo + R);
     ws->work = W->work;
-    ws->xp = W->xp;
+    ws->xh = W->xh;
     ws->hp = W->hp;
     ws->ypart = W->ypart;
     ws->hbuf = W->hbuf;
@@ -595,10 +597,16 @@ static int forward_on_ws(omc_layer *L, const omc_ws *ws, const float *x, int T, 
     float *w = topk_w ? topk_w : ws->topk_w;
     G.prof_valid = 0;
     prof_begin(s);
-    CK(cudaMemsetAsync(ws->counts, 0, sizeof(int) * (size_t)(L->desc.E + 4) * 3, s));
-    if ((rc = omc_launch_router(&L->dev, x, T, ws, idx, w, s))) return omc_fail(rc, "router launch failed");
+    const int mma = use_mma(L, T);
+    omc_plan_args plan;
+    if (mma) {
+        omc_plan_setup(&L->dev, T, ws, &plan);
+        CK(cudaMemsetAsync(ws->done, 0, sizeof(int), s));
+    }
+    if ((rc = omc_launch_router(&L->dev, x, T, ws, idx, w, mma ? &plan : NULL, s)))
+        return omc_fail(rc, "router launch failed");
     omc_prof_mark(s, "router_select");
-    if (use_mma(L, T)) {
+    if (mma) {
         rc = omc_launch_mma_ffn(&L->dev, x, T, ws, idx, w, out, s);
         if (rc == OMC_EUNSUPPORTED && G.path_override != 2) rc = omc_launch_gemv_ffn(&L->dev, x, T, ws, idx, w, out, s);
     } else {
@@ -639,14 +647,15 @@ static size_t noalloc_layout(const omc_layer_dev *P, int T, char *base, omc_ws *
     TAKE(counts, int *, (E + 4) * 4 * 3 + 64);
     TAKE(rowinfo, int *, R * 8);   /* rowinfo, then roww */
     TAKE(work, int *, (size_t)omc_mma_work_items(P, (int)R) * 16);
-    TAKE(xp, uint16_t *, (size_t)P->D_pad * R * 2);
+    TAKE(xh, uint16_t *, Tz * D * 2);
     TAKE(hp, uint16_t *, Imax_pad * R * 2);
     TAKE(ypart, float *, Tz * (K + 1) * D * 4);
     TAKE(hbuf, float *, (Tz * K + Tz) * Imax_rows * 4);
+    TAKE(slotrow, int *, Tz * K * 4);
 #undef TAKE
     if (base) {
         ws->offsets = ws->counts + (E + 4);
-        ws->fill = ws->counts + 2 * (E + 4);
+        ws->done = ws->counts + 2 * (E + 4);
         ws->nwork = ws->counts + 3 * (E + 4);
         ws->roww = (float *)(ws->rowinfo + R);
         ws->x = ws->out = NULL;
@@ -663,6 +672,8 @@ int omc_moe_forward_noalloc(int layer, const float *x, int T, float *out, int32_
     omc_layer *L = omc_get_layer(layer);
     if (!L) return omc_fail(OMC_ENOINIT, "omc_moe_forward_noalloc: layer %d not initialised", layer);
     if (T < 0 || (T > 0 && (!x || !out))) return omc_fail(OMC_EINVAL, "omc_moe_forward_noalloc: bad T or pointers");
+    if (((uintptr_t)x | (uintptr_t)out) & 15)
+        return omc_fail(OMC_EINVAL, "omc_moe_forward_noalloc: x and out must be 16-byte aligned");
     if (G.ep_world > 1)
         return omc_fail(OMC_EUNSUPPORTED, "omc_moe_forward_noalloc: not available with expert parallelism");
     if (T == 0) return OMC_OK;
@@ -696,6 +707,8 @@ int omc_moe_forward_dev(int layer, const float *x, int T, float *out, int32_t *t
     omc_layer *L = omc_get_layer(layer);
     if (!L) return omc_fail(OMC_ENOINIT, "omc_moe_forward_dev: layer %d not initialised", layer);
     if (T < 0 || (T > 0 && (!x || !out))) return omc_fail(OMC_EINVAL, "omc_moe_forward_dev: bad T or pointers");
+    if (((uintptr_t)x | (uintptr_t)out) & 15)
+        return omc_fail(OMC_EINVAL, "omc_moe_forward_dev: x and out must be 16-byte aligned");
     if (T == 0 && G.ep_world <= 1) return OMC_OK;
     cudaStream_t s = stream ? (cudaStream_t)stream : G.stream;
     return omc_forward_device(L, x, T, out, topk_idx, topk_w, s);
@@ -760,12 +773,12 @@ int omc_debug_expf(const float *x, float *y, long long n) {
 }
 
 /* Copies a workspace buffer of the last forward to host memory (debugging):
- * 0 xp, 1 hp, 2 ypart, 3 rowinfo, 4 counts/offsets/fill/nwork, 5 logits. */
+ * 0 xp, 1 hp, 2 ypart, 3 rowinfo, 4 counts/offsets/done/nwork, 5 logits. */
 int omc_debug_ws_copy(int which, void *dst, size_t bytes) {
     if (!G.init) return omc_fail(OMC_ENOINIT, "omc_debug_ws_copy: omc_init not called");
     const void *src = NULL;
     switch (which) {
-    case 0: src = G.ws.xp; break;
+    case 0: src = G.ws.xh; break;
     case 1: src = G.ws.hp; break;
     case 2: src = G.ws.ypart; break;
     case 3: src = G.ws.rowinfo; break;

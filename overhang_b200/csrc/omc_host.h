@@ -30,8 +30,9 @@ typedef struct {
     int32_t *topk_idx;
     float *topk_w, *sg;
     int *counts, *rowinfo, *work;
-    uint16_t *xp, *hp;
+    uint16_t *xh, *hp;
     float *ypart, *hbuf;
+    int *slotrow;
 } omc_ws_ptrs;
 
 typedef struct {

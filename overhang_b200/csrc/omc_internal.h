@@ -94,6 +94,25 @@ typedef struct {
     const omc_expert_ptrs *experts;  /* device table [E + 1]; entry E = shared expert */
 } omc_layer_dev;
 
+#define OMC_NMAX 128              /* token rows per grouped-GEMM work item (MMA N) */
+
+/* The dispatch plan of a tensor-core forward (the batch union of
+ * engines/olmoe.c:366-378, on the device): built by the last block of the
+ * router's select kernel once every token's routing is written. */
+typedef struct {
+    int E, K, T, has_shared;
+    int I_rows, Is_rows, D_rows;  /* row extents of gate/up (routed, shared) and down */
+    int R_cap, cap1, cap2;        /* operand rows and work-list capacities      */
+    int *counts;                  /* [E + 1] rows per group (shared group: T)   */
+    int *offsets;                 /* [E + 2] 16-row-padded row offsets          */
+    int *nwork;                   /* [0] gate/up items [1] down items [2] rows  */
+    int *slotrow;                 /* [T * K] rank of each routed slot in its expert */
+    int *work1, *work2;           /* work items (g, mt, n0, n) as 4 ints        */
+    int *rowinfo;                 /* [R] slot of each operand row (-1 padding)  */
+    float *roww;                  /* [R] routing weight of each operand row     */
+    int *done;                    /* select blocks finished; zero at start      */
+} omc_plan_args;
+
 /* Per-forward workspace (device pointers, grow-only). */
 typedef struct {
     int T_cap, R_cap;             /* capacity in tokens and activation rows */
@@ -105,12 +124,13 @@ typedef struct {
     float *sg;                    /* [T] shared-gate sigmoid              */
     int *counts;                  /* [E + 2] rows per expert (+ shared)   */
     int *offsets;                 /* [E + 3] padded row offsets           */
-    int *fill;                    /* [E + 2]                              */
+    int *done;                    /* [1] select blocks finished (plan trigger) */
+    int *slotrow;                 /* [T * k] rank of each routed slot in its expert */
     int *rowinfo;                 /* [R]: routed slot t*k+kk, T*k+t shared, -1 pad */
     float *roww;                  /* [R]: routing weight of the row (1 shared, 0 pad) */
     int *work;                    /* tile work list                       */
     int *nwork;                   /* [4] work counts                      */
-    uint16_t *xp;                 /* AOL f16 [D_pad/64][R][64]            */
+    uint16_t *xh;                 /* [T][D] f16 token operand (tensor-core path) */
     uint16_t *hp;                 /* AOL f16 [Imax_pad/64][R][64]         */
     float *ypart;                 /* [T][k + 1][D]                        */
     float *hbuf;                  /* [T*k + T][Imax_pad] (GEMV path)      */
@@ -123,8 +143,11 @@ typedef struct {
 int omc_launch_relayout(const int8_t *src, int O, int K, int8_t *dst, int O_pad, int K_pad, int member,
                         cudaStream_t s);
 int omc_launch_i8_to_f32(const int8_t *src, float *dst, long long n, cudaStream_t s);
+/* plan != NULL: the select kernel's last block also builds the dispatch plan */
 int omc_launch_router(const omc_layer_dev *L, const float *x, int T, const omc_ws *ws,
-                      int32_t *topk_idx, float *topk_w, cudaStream_t s);
+                      int32_t *topk_idx, float *topk_w, const omc_plan_args *plan, cudaStream_t s);
+/* fills the plan arguments of a tensor-core forward over workspace ws */
+void omc_plan_setup(const omc_layer_dev *L, int T, const omc_ws *ws, omc_plan_args *pa);
 int omc_launch_gemv_ffn(const omc_layer_dev *L, const float *x, int T, const omc_ws *ws,
                         const int32_t *topk_idx, const float *topk_w, float *out, cudaStream_t s);
 int omc_launch_mma_ffn(const omc_layer_dev *L, const float *x, int T, const omc_ws *ws,

@@ -14,7 +14,7 @@
 //   renorm : engines/olmoe.c:363, engines/qwen.c:476-477 (float sum in
 //            selection order, then divide).
 //   shared gate: engines/qwen.c:460-461, sigmoid(sum sh_gate[i]*x[i]).
-#include "omc_common.cuh"
+#include "omc_plan.cuh"
 
 namespace {
 
@@ -62,7 +62,9 @@ __global__ void __launch_bounds__(RL_THREADS) router_logits_kernel(const float *
                                                                     const float *__restrict__ W,
                                                                     const float *__restrict__ Ws, int E,
                                                                     const float *__restrict__ sh_gate, int nrows,
-                                                                    float *__restrict__ logits, int ldl) {
+                                                                    float *__restrict__ logits, int ldl,
+                                                                    uint16_t *__restrict__ xh, int *err) {
+    (void)err;
     extern __shared__ __align__(16) float rsm[];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int t0 = blockIdx.x * RL_TOK, row0 = blockIdx.y * RL_ROWS;
@@ -99,6 +101,21 @@ __global__ void __launch_bounds__(RL_THREADS) router_logits_kernel(const float *
         if (ch + RL_ST - 1 < nch) load(ch + RL_ST - 1);
         cp_async_commit();
         const float *st = rsm + (size_t)(ch % RL_ST) * RL_STAGE;
+        if (xh && blockIdx.y == 0) {
+            // the f16 token operand of the expert GEMMs (row t of xh = x[t] rounded
+            // to f16, saturated): written from the staged chunk by the first
+            // column of blocks, 8 values per thread
+            const int r = threadIdx.x >> 4, c = (threadIdx.x & 15) * 8, k = ch * RL_CH + c;
+            if (t0 + r < T && k < D) {
+                const float *v = st + r * RL_LD + c;
+                uint4 o;
+                o.x = f32x2_to_f16x2_sat(v[0], v[1]);
+                o.y = f32x2_to_f16x2_sat(v[2], v[3]);
+                o.z = f32x2_to_f16x2_sat(v[4], v[5]);
+                o.w = f32x2_to_f16x2_sat(v[6], v[7]);
+                *reinterpret_cast<uint4 *>(xh + (size_t)(t0 + r) * D + k) = o;
+            }
+        }
         const float *xr = st + tok * RL_LD;
         const float *w0 = st + (RL_TOK + rl) * RL_LD, *w1 = w0 + RL_LD;
         const int clen = min(RL_CH, D - ch * RL_CH);     // a multiple of 4
@@ -121,22 +138,19 @@ __global__ void __launch_bounds__(RL_THREADS) router_logits_kernel(const float *
 }
 
 // ---- select -----------------------------------------------------------------
-// One warp per token: softmax, top-k, renorm, shared-gate sigmoid, expert
-// counts.  Lane l holds logits l, l+32, ...; order-dependent sums run from a
-// shared-memory copy so that their dependent chain is the add latency alone.
-constexpr int SEL_WARPS = 4;
+// One warp per token: softmax, top-k, renorm, shared-gate sigmoid.  Lane l
+// holds logits l, l+32, ...; order-dependent sums run from a shared-memory
+// copy so that their dependent chain is the add latency alone.  With a plan
+// (tensor-core forwards) the block that finishes last builds the dispatch
+// plan from every token's routing: no per-expert atomics in global memory.
+constexpr int SEL_WARPS = 8;
 
 template <int SEL_MAXV>   // ceil(E / 32) rounded up to a power of two
-__global__ void __launch_bounds__(SEL_WARPS * 32) router_select_kernel(const float *__restrict__ logits, int ldl, int T,
-                                                                       int E, int K, int family, int renorm,
-                                                                       int has_shared, int32_t *__restrict__ topk_idx,
-                                                                       float *__restrict__ topk_w, float *__restrict__ sg,
-                                                                       int *__restrict__ counts, int *err) {
-    __shared__ __align__(16) float es_all[SEL_WARPS][SEL_MAXV * 32];
-    const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
-    const int t = blockIdx.x * SEL_WARPS + wib;
-    if (t >= T) return;
-    float *es = es_all[wib];
+__device__ __forceinline__ void select_token(const float *__restrict__ logits, int ldl, int t, int E, int K,
+                                             int family, int renorm, int has_shared,
+                                             int32_t *__restrict__ topk_idx, float *__restrict__ topk_w,
+                                             float *__restrict__ sg, int *err, float *es) {
+    const int lane = threadIdx.x & 31;
     const float *lg = logits + (size_t)t * ldl;
     float v[SEL_MAXV];
     // max, as `if (x[i] > m) m = x[i]` from m = -1e30f
@@ -241,13 +255,9 @@ __global__ void __launch_bounds__(SEL_WARPS * 32) router_select_kernel(const flo
         my_val = __fdiv_rn(my_val, sm);
     }
     if (lane < K) {
-        if (my_idx < 0 || my_idx >= E) {
-            omc_dev_error(err, OMC_DEVERR_ROUTE, OMC_SITE_ROUTER, t);
-        } else {
-            topk_idx[(size_t)t * K + lane] = my_idx;
-            topk_w[(size_t)t * K + lane] = my_val;
-            atomicAdd(&counts[my_idx], 1);
-        }
+        if (my_idx < 0 || my_idx >= E) omc_dev_error(err, OMC_DEVERR_ROUTE, OMC_SITE_ROUTER, t);
+        topk_idx[(size_t)t * K + lane] = my_idx;
+        topk_w[(size_t)t * K + lane] = my_val;
     }
     if (has_shared && lane == 0) {
         const float z = lg[E];
@@ -255,10 +265,37 @@ __global__ void __launch_bounds__(SEL_WARPS * 32) router_select_kernel(const flo
     }
 }
 
+__host__ __device__ constexpr int SEL_SMEM_FLOATS(int maxv) { return SEL_WARPS * maxv * 32 > OMC_PLAN_SMEM_INTS ? SEL_WARPS * maxv * 32 : OMC_PLAN_SMEM_INTS; }
+
+template <int SEL_MAXV>
+__global__ void __launch_bounds__(SEL_WARPS * 32) router_select_kernel(const float *__restrict__ logits, int ldl, int T,
+                                                                       int E, int K, int family, int renorm,
+                                                                       int has_shared, int32_t *__restrict__ topk_idx,
+                                                                       float *__restrict__ topk_w, float *__restrict__ sg,
+                                                                       omc_plan_args plan, int do_plan, int *err) {
+    // per-warp softmax rows, reused by the plan in the last block
+    __shared__ __align__(16) float sbuf[SEL_SMEM_FLOATS(SEL_MAXV)];
+    __shared__ int s_last;
+    const int wib = threadIdx.x >> 5;
+    const int t = blockIdx.x * SEL_WARPS + wib;
+    if (t < T)
+        select_token<SEL_MAXV>(logits, ldl, t, E, K, family, renorm, has_shared, topk_idx, topk_w, sg, err,
+                               sbuf + wib * SEL_MAXV * 32);
+    if (!do_plan) return;
+    // last-block handoff: every block's routing is visible to the block that counts last
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) s_last = atomicAdd(plan.done, 1) == (int)gridDim.x - 1;
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    omc_plan_block(plan, topk_idx, topk_w, err, reinterpret_cast<int *>(sbuf));
+}
+
 }  // namespace
 
 extern "C" int omc_launch_router(const omc_layer_dev *L, const float *x, int T, const omc_ws *ws,
-                                 int32_t *topk_idx, float *topk_w, cudaStream_t s) {
+                                 int32_t *topk_idx, float *topk_w, const omc_plan_args *plan, cudaStream_t s) {
     if (T <= 0) return 0;
     if (L->E > OMC_MAX_E || L->k > OMC_MAX_K || (L->D & 3)) return OMC_EINVAL;
     static int attr_done = 0;
@@ -272,13 +309,18 @@ extern "C" int omc_launch_router(const omc_layer_dev *L, const float *x, int T, 
     const int ldl = L->E + 1;
     const dim3 g1((T + RL_TOK - 1) / RL_TOK, (nrows + RL_ROWS - 1) / RL_ROWS);
     router_logits_kernel<<<g1, RL_THREADS, RL_SMEM, s>>>(x, T, L->D, L->router, L->router_i8 ? L->router_s : nullptr,
-                                                         L->E, L->sh_gate, nrows, ws->logits, ldl);
+                                                         L->E, L->sh_gate, nrows, ws->logits, ldl,
+                                                         plan ? ws->xh : nullptr, ws->err);
     omc_prof_mark(s, "router_logits");
     const int nv = (L->E + 31) / 32;
     const dim3 g2((T + SEL_WARPS - 1) / SEL_WARPS);
+    omc_plan_args pa;
+    if (plan) pa = *plan;
+    else memset(&pa, 0, sizeof(pa));
 #define SEL(NV)                                                                                                    \
     router_select_kernel<NV><<<g2, SEL_WARPS * 32, 0, s>>>(ws->logits, ldl, T, L->E, L->k, L->family, L->renorm, \
-                                                         L->has_shared, topk_idx, topk_w, ws->sg, ws->counts, ws->err)
+                                                         L->has_shared, topk_idx, topk_w, ws->sg, pa, plan != nullptr, \
+                                                         ws->err)
     if (nv <= 1) SEL(1);
     else if (nv <= 2) SEL(2);
     else if (nv <= 4) SEL(4);

@@ -51,3 +51,22 @@ def test_forward_before_experts_uploaded(gpu):
     rc = gpu.lib().omc_moe_forward(lid, x.ctypes.data_as(C.c_void_p), 2, out.ctypes.data_as(C.c_void_p),
                                    None, None)
     assert rc == gpu.ENOINIT
+
+
+def test_misaligned_device_pointers_are_rejected(gpu, oracle):
+    """The device entries move x and out rows with 16-byte bulk copies and
+    vector stores: a pointer off a 16-byte boundary is refused on the host
+    (OMC_EINVAL) before anything is launched."""
+    import torch
+    L = oracle.make_layer(oracle.FAMILY_OLMOE, 128, 64, 8, 2, seed=82)
+    m = gpu.MoELayer.from_oracle_layer(next_layer_id(), L)
+    buf = torch.zeros(4 * 128 + 4, dtype=torch.float32, device="cuda")
+    out = torch.zeros(4 * 128 + 4, dtype=torch.float32, device="cuda")
+    lib = gpu.lib()
+    for fn in (lib.omc_moe_forward_dev, lib.omc_moe_forward_noalloc):
+        rc = fn(m.layer, C.c_void_p(buf.data_ptr() + 4), 4, C.c_void_p(out.data_ptr()), None, None, None)
+        assert rc == gpu.EINVAL, gpu.last_error()
+        assert "16-byte aligned" in gpu.last_error()
+        rc = fn(m.layer, C.c_void_p(buf.data_ptr()), 4, C.c_void_p(out.data_ptr() + 8), None, None, None)
+        assert rc == gpu.EINVAL
+    gpu.sync()
