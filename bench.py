@@ -352,11 +352,11 @@ def run_ours(args):
 
     hbm, tf, src = peaks()
     # algorithmic bytes of one launch of the dominant kernel: every active
-    # expert's int8 gate+up rows and their scales, the f16 token operand it
-    # reads (one row per routed slot) and the f16 h it writes.
+    # expert's int8 gate+up rows and their scales, the f16 copy of the tokens
+    # it gathers rows from (T x D) and the f16 h it writes (one row per slot).
     n_active = int(len(np.unique(idx.cpu().numpy())))
     if dom == "gemm_gateup":
-        alg_bytes = n_active * (2 * I * D + 2 * I * 4) + T * K * D * 2 + T * K * I * 2
+        alg_bytes = n_active * (2 * I * D + 2 * I * 4) + T * D * 2 + T * K * I * 2
     else:
         alg_bytes = n_active * (2 * I * D + 2 * I * 4) + T * D * 4 + T * K * I * 4
     achieved = alg_bytes / (dom_ms / 1e3) / 1e9 if dom_ms > 0 else None
