@@ -143,19 +143,46 @@ int omc_moe_forward_dev(int layer, const float *x, int T, float *out,
 int omc_moe_forward_noalloc(int layer, const float *x, int T, float *out,
                             int32_t *topk_idx, float *topk_w, void *stream);
 
+/* ---- building blocks for expert parallelism ------------------------ */
+/* A caller that spreads the experts of a layer over GPUs (one process per
+ * GPU, its own exchange, e.g. torch.distributed) composes a forward from
+ * these two.  Both take device pointers and enqueue on `stream`.
+ *
+ * omc_moe_route_dev: the router alone (the first half of moe(),
+ * engines/olmoe.c:347-364 / moe_step(), engines/qwen.c:463-477): topk_idx,
+ * topk_w [T,k] in selection order, and for layers with a shared expert the
+ * sigmoid gate shared_gate [T] (nullable) of engines/qwen.c:460-461.
+ *
+ * omc_moe_experts_dev: y[r] = weight[r] * expert[r](x_rows[r]) for R rows of
+ * D floats, each with its own expert: a routed expert resident on this
+ * process (see omc_ep_init for the resident range; all of them when no
+ * group was joined) or E for the layer's shared expert (weight 1 then gives
+ * the unweighted shared output).  The product is rounded exactly as the
+ * forward rounds w * y (engines/olmoe.c:396), so summing a token's rows in
+ * selection order after sigmoid(gate) * shared reproduces omc_moe_forward
+ * bit for bit.  A row naming a non-resident expert is skipped and reported
+ * as OMC_EDEVICE by the next omc_sync.  x_rows and y are 16-byte aligned. */
+int omc_moe_route_dev(int layer, const float *x, int T, int32_t *topk_idx, float *topk_w, float *shared_gate,
+                      void *stream);
+int omc_moe_experts_dev(int layer, const float *x_rows, int R, const int32_t *expert, const float *weight,
+                        float *y, void *stream);
+
 /* Wait for all work of the library; reports a pending device error. */
 int omc_sync(void);
 
 /* ---- expert parallelism (1 process per GPU) ------------------------- */
 
-/* Join an expert-parallel group of `world` ranks.  unique_id is the 128-byte
- * ncclUniqueId made by rank 0 and shared by the caller.  Layers initialised
- * afterwards keep only experts [rank*E/world, (rank+1)*E/world) in the slab;
- * omc_moe_forward[_dev] then routes the caller's tokens, dispatches them to
- * their experts' ranks and combines the results (NCCL over NVLink). */
+/* Declare this process rank `rank` of `world` expert-parallel ranks (call
+ * after omc_init, before the first omc_layer_init).  Layers initialised
+ * afterwards hold only routed experts [rank*E/world, (rank+1)*E/world) in
+ * the slab (omc_expert_set ignores the others) plus the shared expert; the
+ * caller composes a forward from omc_moe_route_dev and omc_moe_experts_dev
+ * over its own transport, and omc_moe_forward[_dev] on such a layer returns
+ * OMC_EUNSUPPORTED.  unique_id must be NULL: the library owns no NCCL group
+ * (a non-NULL id returns OMC_EUNSUPPORTED). */
 int omc_ep_init(int rank, int world, const void *unique_id);
 
-/* Write a fresh 128-byte ncclUniqueId into buf (rank 0 only). */
+/* Not provided (the library owns no NCCL group): OMC_EUNSUPPORTED. */
 int omc_ep_unique_id(void *buf, size_t len);
 
 /* ---- introspection -------------------------------------------------- */

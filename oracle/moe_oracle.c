@@ -180,6 +180,57 @@ int orc_moe(const orc_desc *d, const orc_weights *w, const float *x, int T,
     return 0;
 }
 
+int orc_shared_gate(const orc_desc *d, const orc_weights *w, const float *x, int T, float *sg) {
+    if (!desc_ok(d) || T < 0 || !d->has_shared) return -1;
+    for (int t = 0; t < T; t++) {
+        const float *xs = x + (int64_t)t * d->D;
+        float s = 0;
+        for (int i = 0; i < d->D; i++) s += w->sh_gate[i] * xs[i];
+        sg[t] = ref_sigmoidf(s);
+    }
+    return 0;
+}
+
+int orc_expert_rows(const orc_desc *d, const orc_weights *w, const float *x, int R, const int32_t *ids,
+                    float *y) {
+    if (!desc_ok(d) || R < 0) return -1;
+    for (int r = 0; r < R; r++)
+        if (ids[r] < 0 || ids[r] > d->E || (ids[r] == d->E && !d->has_shared)) return -1;
+    const int D = d->D, I = d->I, E = d->E;
+    const int Wmax = (d->has_shared && d->Is > I) ? d->Is : I;
+    #pragma omp parallel
+    {
+        float *g = malloc(sizeof(float) * Wmax), *u = malloc(sizeof(float) * Wmax);
+        #pragma omp for schedule(dynamic, 1)
+        for (int r = 0; r < R; r++) {
+            const float *xs = x + (int64_t)r * D;
+            float *ys = y + (int64_t)r * D;
+            const int e = ids[r];
+            if (e == E) {
+                /* engines/qwen.c:455-459: shared expert, sigmoid gate applied by the caller */
+                const int SI = d->Is;
+                ref_matmul_q(g, xs, w->sh_g, w->sh_gs, D, SI);
+                ref_matmul_q(u, xs, w->sh_u, w->sh_us, D, SI);
+                for (int i = 0; i < SI; i++) g[i] = ref_siluf(g[i]) * u[i];
+                ref_matmul_q(ys, g, w->sh_d, w->sh_ds, SI, D);
+                continue;
+            }
+            const int8_t *qg = w->g + (int64_t)e * I * D, *qu = w->u + (int64_t)e * I * D;
+            const int8_t *qd = w->d + (int64_t)e * D * I;
+            ref_matmul_q(g, xs, qg, w->gs + (int64_t)e * I, D, I);
+            ref_matmul_q(u, xs, qu, w->us + (int64_t)e * I, D, I);
+            if (d->family == ORC_FAMILY_QWEN) {
+                for (int i = 0; i < I; i++) g[i] = ref_siluf(g[i]) * u[i];          /* qwen.c:485 */
+            } else {
+                for (int i = 0; i < I; i++) { float gv = g[i]; g[i] = (gv / (1.f + expf(-gv))) * u[i]; } /* olmoe.c:393 */
+            }
+            ref_matmul_q(ys, g, qd, w->ds + (int64_t)e * D, I, D);
+        }
+        free(g); free(u);
+    }
+    return 0;
+}
+
 /* ---- quantisers and inputs ----------------------------------------- */
 
 /* tools/convert_olmoe.py:32-38 (same rule in convert_qwen.py / convert_gemma.py) */

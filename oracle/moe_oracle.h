@@ -55,6 +55,17 @@ int orc_moe(const orc_desc *dsc, const orc_weights *w, const float *x, int T,
             float *out, int32_t *topk_idx, float *topk_w);
 
 /* Routing only (router GEMV + softmax + top-k + optional renorm), same rules. */
+/* One expert per row, unweighted: y[r] = expert ids[r] applied to x[r]
+ * ([D] -> [D]), with the reference's arithmetic for one expert of moe() /
+ * moe_step() (engines/olmoe.c:386-394, engines/qwen.c:480-491); id E is the
+ * shared expert (engines/qwen.c:455-459, before its sigmoid gate).  Returns
+ * -1 on a bad descriptor or id.  (Expert-parallel tests sum these rows.) */
+int orc_expert_rows(const orc_desc *dsc, const orc_weights *w, const float *x, int R, const int32_t *ids,
+                    float *y);
+
+/* sg[t] = sigmoid(sum_i sh_gate[i] * x[t][i]) (engines/qwen.c:460-461). */
+int orc_shared_gate(const orc_desc *dsc, const orc_weights *w, const float *x, int T, float *sg);
+
 int orc_route(const orc_desc *dsc, const orc_weights *w, const float *x, int T,
               int32_t *topk_idx, float *topk_w);
 

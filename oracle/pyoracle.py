@@ -60,6 +60,11 @@ def lib():
         L.orc_route.restype = C.c_int
         L.orc_route.argtypes = [C.POINTER(OrcDesc), C.POINTER(OrcWeights), _f32p, C.c_int,
                                 C.c_void_p, C.c_void_p]
+        L.orc_shared_gate.restype = C.c_int
+        L.orc_shared_gate.argtypes = [C.POINTER(OrcDesc), C.POINTER(OrcWeights), _f32p, C.c_int, _f32p]
+        L.orc_expert_rows.restype = C.c_int
+        L.orc_expert_rows.argtypes = [C.POINTER(OrcDesc), C.POINTER(OrcWeights), _f32p, C.c_int,
+                                      C.c_void_p, _f32p]
         L.orc_quantize_rows_py.argtypes = [_f32p, C.c_int, C.c_int, _i8p, _f32p]
         L.orc_quantize_rows_c.argtypes = [_f32p, C.c_int, C.c_int, _i8p, _f32p]
         L.orc_fill_normal.argtypes = [C.c_uint64, _f32p, C.c_int64, C.c_float]
@@ -198,6 +203,27 @@ def oracle_moe(L: Layer, x: np.ndarray):
     if rc:
         raise ValueError("orc_moe rejected the descriptor")
     return out, idx, w
+
+
+def oracle_expert_rows(L: Layer, x: np.ndarray, ids: np.ndarray) -> np.ndarray:
+    """y [R,D]: expert ids[r] (E = the shared expert) applied to x[r], unweighted."""
+    x = np.ascontiguousarray(x, np.float32)
+    ids = np.ascontiguousarray(ids, np.int32)
+    y = np.empty((x.shape[0], L.D), np.float32)
+    d, ww = L.desc(), L.weights()
+    if lib().orc_expert_rows(C.byref(d), C.byref(ww), x, x.shape[0], ids.ctypes.data, y):
+        raise ValueError("orc_expert_rows rejected the descriptor or an id")
+    return y
+
+
+def oracle_shared_gate(L: Layer, x: np.ndarray) -> np.ndarray:
+    """sg [T]: the shared expert's sigmoid gate."""
+    x = np.ascontiguousarray(x, np.float32)
+    sg = np.empty(x.shape[0], np.float32)
+    d, ww = L.desc(), L.weights()
+    if lib().orc_shared_gate(C.byref(d), C.byref(ww), x, x.shape[0], sg):
+        raise ValueError("orc_shared_gate rejected the descriptor")
+    return sg
 
 
 def oracle_route(L: Layer, x: np.ndarray):

@@ -54,6 +54,8 @@ SIGNATURES = {
     "omc_moe_forward": (_i, [_i, _vp, _i, _vp, _vp, _vp]),
     "omc_moe_forward_dev": (_i, [_i, _vp, _i, _vp, _vp, _vp, _vp]),
     "omc_moe_forward_noalloc": (_i, [_i, _vp, _i, _vp, _vp, _vp, _vp]),
+    "omc_moe_route_dev": (_i, [_i, _vp, _i, _vp, _vp, _vp, _vp]),
+    "omc_moe_experts_dev": (_i, [_i, _vp, _i, _vp, _vp, _vp, _vp]),
     "omc_sync": (_i, []),
     "omc_ep_init": (_i, [_i, _i, _vp]),
     "omc_ep_unique_id": (_i, [_vp, _sz]),
@@ -144,6 +146,12 @@ def set_profiling(on: bool) -> None:
     lib().omc_set_profiling(1 if on else 0)
 
 
+def ep_init(rank: int, world: int) -> None:
+    """Hold routed experts [rank*E/world, (rank+1)*E/world) of every layer
+    created afterwards (see overhang_b200.ep)."""
+    check(lib().omc_ep_init(rank, world, None), "omc_ep_init")
+
+
 def time_stage(name) -> None:
     """Time stage `name` ("gemm_gateup", ...) in every following forward with
     one CUDA-event pair on its stream; None stops."""
@@ -175,6 +183,11 @@ class MoELayer:
         rs = None if router_s is None else np.ascontiguousarray(router_s, np.float32)
         check(lib().omc_layer_init(layer, C.byref(self.desc), _p(self._keep[0]), _p(rs)),
               "omc_layer_init")
+
+    D = property(lambda self: self.desc.D)
+    E = property(lambda self: self.desc.E)
+    k = property(lambda self: self.desc.k)
+    has_shared = property(lambda self: self.desc.has_shared)
 
     @classmethod
     def from_oracle_layer(cls, layer: int, L) -> "MoELayer":

@@ -56,7 +56,7 @@
 //
 // Every mbarrier wait is bounded (~1 s); on expiry the CTA records
 // OMC_DEVERR_TIMEOUT, raises a shared abort flag, and all roles unwind.
-#include "omc_common.cuh"
+#include "omc_plan.cuh"
 
 namespace {
 
@@ -101,8 +101,12 @@ struct GemmArgs {
     const uint16_t *xh;        // gemm1: f16 tokens [T][D], gathered per operand row
     uint16_t *hout;            // gemm1: h operand out
     float *ypart;              // gemm2: per-slot partials [T][k+1][D]
-    const int *rowinfo;        // gemm2: row -> slot
+    const int *rowinfo;        // row -> slot (-1 padding)
     const float *roww;         // gemm2: row -> routing weight (1 for the shared expert)
+    int K, nrouted;            // slots per token and routed slots: a slot s < nrouted is
+                               // token s / K, choice s % K; s >= nrouted is token s - nrouted
+    int ydirect;               // gemm2: 1 = write row slot of ypart ([slots][D]) instead of
+                               // the [T][K+1][D] partials
     int T, R;                  // tokens, operand rows
     int *err;
 };
@@ -421,8 +425,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_gemm_kernel(const GemmArgs a)
                             int t = -1;
                             if (j < pr.n) {
                                 const int slot = a.rowinfo[pr.n0 + j];
-                                const int nr = a.T * L.k;
-                                t = slot < 0 ? -1 : (slot < nr ? slot / L.k : slot - nr);
+                                t = slot < 0 ? -1 : (slot < a.nrouted ? slot / a.K : slot - a.nrouted);
                             }
                             xrow[u] = t;
                         }
@@ -506,13 +509,15 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_gemm_kernel(const GemmArgs a)
             } else {
                 const int d = (2 * it.mt + half) * OMC_TM + r;
                 if (half < item_nmat<PHASE>(L, it) && d < L.D) sc0 = P.ds[d];
-                // per token row: its ypart row (token * (k+1) + choice; -1 padding) and weight
-                const int K = L.k;
+                // per token row: its ypart row (token * (k+1) + choice, or the slot
+                // itself when ydirect; -1 padding) and weight
+                const int K = a.K;
                 for (int j = lane; j < it.n; j += 32) {
                     const int slot = a.rowinfo[it.n0 + j];
                     int dst = -1;
-                    if (slot >= 0 && slot < a.T * K) dst = slot / K * (K + 1) + slot % K;
-                    else if (slot >= a.T * K) dst = (slot - a.T * K) * (K + 1) + K;
+                    if (slot >= 0 && a.ydirect) dst = slot;
+                    else if (slot >= 0 && slot < a.nrouted) dst = slot / K * (K + 1) + slot % K;
+                    else if (slot >= a.nrouted) dst = (slot - a.nrouted) * (K + 1) + K;
                     tab_row[j] = dst;
                     tab_w[j] = a.roww[it.n0 + j];
                 }
@@ -612,6 +617,28 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_gemm_kernel(const GemmArgs a)
     }
 }
 
+// -------------------------------------------------- explicit-rows pass ---
+// f16 operand rows from f32 rows (saturated), 8 values per thread.
+__global__ void __launch_bounds__(256) rows_to_f16_kernel(const float *__restrict__ x, long long n8,
+                                                          uint16_t *__restrict__ xh) {
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n8; i += (long long)gridDim.x * blockDim.x) {
+        const float4 a = reinterpret_cast<const float4 *>(x)[2 * i], b = reinterpret_cast<const float4 *>(x)[2 * i + 1];
+        uint4 o;
+        o.x = f32x2_to_f16x2_sat(a.x, a.y);
+        o.y = f32x2_to_f16x2_sat(a.z, a.w);
+        o.z = f32x2_to_f16x2_sat(b.x, b.y);
+        o.w = f32x2_to_f16x2_sat(b.z, b.w);
+        reinterpret_cast<uint4 *>(xh)[i] = o;
+    }
+}
+
+// The dispatch plan of an explicit-rows pass, as one block.
+__global__ void __launch_bounds__(1024) plan_rows_kernel(omc_plan_args p, const int32_t *__restrict__ ids,
+                                                         const float *__restrict__ w, int *err) {
+    __shared__ int smem[OMC_PLAN_SMEM_INTS];
+    omc_plan_block(p, ids, w, err, smem);
+}
+
 // ------------------------------------------------------------- combine ---
 __global__ void __launch_bounds__(256) combine_kernel(const float *__restrict__ ypart, const float *__restrict__ sg,
                                                       int T, int D, int K, int has_shared, float *__restrict__ out) {
@@ -647,10 +674,8 @@ extern "C" long long omc_mma_work_items(const omc_layer_dev *L, int R) {
     return chunks_max * (Imax_rows / OMC_TM) + chunks_max * ((L->D_rows / OMC_TM + 1) / 2);
 }
 
-extern "C" int omc_launch_mma_ffn(const omc_layer_dev *L, const float *x, int T, const omc_ws *ws,
-                                  const int32_t *topk_idx, const float *topk_w, float *out, cudaStream_t s) {
-    if (T <= 0) return 0;
-    if (L->D % 4) return OMC_EUNSUPPORTED;
+// Once per process: the GEMM's shared-memory attribute and the SM count.
+static int gemm_setup() {
     static int attr_done = 0;
     if (!attr_done) {
         if (cudaFuncSetAttribute(moe_gemm_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) !=
@@ -663,6 +688,14 @@ extern "C" int omc_launch_mma_ffn(const omc_layer_dev *L, const float *x, int T,
         cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
         attr_done = 1;
     }
+    return 0;
+}
+
+extern "C" int omc_launch_mma_ffn(const omc_layer_dev *L, const float *x, int T, const omc_ws *ws,
+                                  const int32_t *topk_idx, const float *topk_w, float *out, cudaStream_t s) {
+    if (T <= 0) return 0;
+    if (L->D % 4) return OMC_EUNSUPPORTED;
+    if (gemm_setup()) return OMC_ECUDA;
     const int R = ws->R_cap;
     omc_plan_args pa;                      // built on the device by the router's last select block
     omc_plan_setup(L, T, ws, &pa);
@@ -678,6 +711,9 @@ extern "C" int omc_launch_mma_ffn(const omc_layer_dev *L, const float *x, int T,
     ga.ypart = ws->ypart;
     ga.rowinfo = ws->rowinfo;
     ga.roww = ws->roww;
+    ga.K = L->k;
+    ga.nrouted = T * L->k;
+    ga.ydirect = 0;
     ga.T = T;
     ga.R = R;
     ga.err = ws->err;
@@ -705,6 +741,9 @@ extern "C" void omc_plan_setup(const omc_layer_dev *L, int T, const omc_ws *ws, 
     pa->K = L->k;
     pa->T = T;
     pa->has_shared = L->has_shared;
+    pa->rows_mode = 0;
+    pa->e_lo = 0;
+    pa->e_hi = E;
     pa->I_rows = L->I_rows;
     pa->Is_rows = L->Is_rows;
     pa->D_rows = L->D_rows;
@@ -720,4 +759,49 @@ extern "C" void omc_plan_setup(const omc_layer_dev *L, int T, const omc_ws *ws, 
     pa->done = ws->done;
     pa->rowinfo = ws->rowinfo;
     pa->roww = ws->roww;
+}
+
+// Explicit-rows pass (expert parallelism: rows received from other ranks):
+// y[r] = w[r] * expert ids[r] (x[r]) for R rows of D f32, through the same
+// plan and grouped GEMMs as a forward.  ids must be resident experts
+// [e_lo, e_hi), or E for the shared expert.
+extern "C" int omc_launch_mma_rows(const omc_layer_dev *L, const float *x, int R, const omc_ws *ws,
+                                   const int32_t *ids, const float *w, int e_lo, int e_hi, float *y,
+                                   cudaStream_t s) {
+    if (R <= 0) return 0;
+    if (gemm_setup()) return OMC_ECUDA;
+    const long long n8 = (long long)R * L->D / 8;
+    rows_to_f16_kernel<<<(int)((n8 + 255) / 256 < 4096 ? (n8 + 255) / 256 : 4096), 256, 0, s>>>(x, n8, ws->xh);
+    omc_plan_args pa;
+    omc_plan_setup(L, R, ws, &pa);
+    pa.K = 1;
+    pa.rows_mode = 1;
+    pa.e_lo = e_lo;
+    pa.e_hi = e_hi;
+    plan_rows_kernel<<<1, 1024, 0, s>>>(pa, ids, w, ws->err);
+    omc_prof_mark(s, "dispatch");
+    GemmArgs ga;
+    ga.L = *L;
+    ga.work = reinterpret_cast<const int4 *>(pa.work1);
+    ga.nwork = ws->nwork;
+    ga.act = ws->hp;
+    ga.xh = ws->xh;
+    ga.hout = ws->hp;
+    ga.ypart = y;
+    ga.rowinfo = ws->rowinfo;
+    ga.roww = ws->roww;
+    ga.K = 1;
+    ga.nrouted = R;
+    ga.ydirect = 1;
+    ga.T = R;
+    ga.R = ws->R_cap;
+    ga.err = ws->err;
+    const int grid = g_num_sms > 0 ? g_num_sms : 148;
+    moe_gemm_kernel<1><<<grid, NTHREADS, SMEM_BYTES, s>>>(ga);
+    omc_prof_mark(s, "gemm_gateup");
+    ga.work = reinterpret_cast<const int4 *>(pa.work2);
+    moe_gemm_kernel<2><<<grid, NTHREADS, SMEM_BYTES, s>>>(ga);
+    omc_prof_mark(s, "gemm_down");
+    omc_g_launches += 4;
+    return cudaGetLastError() == cudaSuccess ? 0 : OMC_ECUDA;
 }

@@ -400,13 +400,16 @@ static int ws_buf(int slot, void **ptr, size_t need) {
     return OMC_OK;
 }
 
-int omc_ws_ensure(const omc_layer *L, int T, int host_io) {
+/* Workspace for Tz tokens (or explicit rows) with nslots routed slots and
+ * nshared implicit shared-expert rows. */
+static int ws_ensure_core(const omc_layer *L, size_t Tz, size_t nslots, size_t nshared, int host_io) {
     const omc_layer_dev *P = &L->dev;
-    const size_t Tz = (size_t)T, D = (size_t)P->D, E = (size_t)P->E, K = (size_t)P->k;
+    const size_t D = (size_t)P->D, E = (size_t)P->E, K = (size_t)P->k;
     const size_t Imax_rows = (size_t)(P->Is_rows > P->I_rows ? P->Is_rows : P->I_rows);
     const size_t Imax_pad = (size_t)(P->Is_pad > P->I_pad ? P->Is_pad : P->I_pad);
+    const int T = (int)Tz;
     /* activation rows: every routed slot + shared rows + 16-row padding per expert */
-    const size_t R = omc_round_up((int)(Tz * K + (P->has_shared ? Tz : 0) + (E + 1) * OMC_ROW_ALIGN), 128);
+    const size_t R = omc_round_up((int)(nslots + nshared + (E + 1) * OMC_ROW_ALIGN), 128);
     int rc = 0;
     omc_ws_ptrs *W = &G.ws_ptrs;
     if (host_io) {
@@ -424,7 +427,7 @@ int omc_ws_ensure(const omc_layer *L, int T, int host_io) {
     if ((rc = ws_buf(10, (void **)&W->hp, Imax_pad * R * 2))) return rc;
     if ((rc = ws_buf(11, (void **)&W->ypart, Tz * (K + 1) * D * 4))) return rc;
     if ((rc = ws_buf(12, (void **)&W->hbuf, (Tz * K + Tz) * Imax_rows * 4))) return rc;
-    if ((rc = ws_buf(13, (void **)&W->slotrow, Tz * K * 4))) return rc;
+    if ((rc = ws_buf(13, (void **)&W->slotrow, (nslots > Tz * K ? nslots : Tz * K) * 4))) return rc;
     omc_ws *ws = &G.ws;
     ws->T_cap = T;
     ws->R_cap = (int)R;
@@ -448,6 +451,15 @@ int omc_ws_ensure(const omc_layer *L, int T, int host_io) {
     ws->hbuf = W->hbuf;
     ws->err = G.d_err;
     return OMC_OK;
+}
+
+int omc_ws_ensure(const omc_layer *L, int T, int host_io) {
+    const size_t Tz = (size_t)T;
+    return ws_ensure_core(L, Tz, Tz * (size_t)L->dev.k, L->dev.has_shared ? Tz : 0, host_io);
+}
+
+static int ws_ensure_rows(const omc_layer *L, int rows) {
+    return ws_ensure_core(L, (size_t)rows, (size_t)rows, 0, 0);
 }
 
 /* ---------------------------------------------------------------- errors -- */
@@ -712,6 +724,50 @@ int omc_moe_forward_dev(int layer, const float *x, int T, float *out, int32_t *t
     if (T == 0 && G.ep_world <= 1) return OMC_OK;
     cudaStream_t s = stream ? (cudaStream_t)stream : G.stream;
     return omc_forward_device(L, x, T, out, topk_idx, topk_w, s);
+}
+
+int omc_moe_route_dev(int layer, const float *x, int T, int32_t *topk_idx, float *topk_w, float *shared_gate,
+                      void *stream) {
+    if (!G.init) return omc_fail(OMC_ENOINIT, "omc_moe_route_dev: omc_init not called");
+    omc_layer *L = omc_get_layer(layer);
+    if (!L) return omc_fail(OMC_ENOINIT, "omc_moe_route_dev: layer %d not initialised", layer);
+    if (T < 0 || (T > 0 && (!x || !topk_idx || !topk_w))) return omc_fail(OMC_EINVAL, "omc_moe_route_dev: bad T or pointers");
+    if ((uintptr_t)x & 15) return omc_fail(OMC_EINVAL, "omc_moe_route_dev: x must be 16-byte aligned");
+    if (T == 0) return OMC_OK;
+    int rc;
+    if ((rc = omc_ws_ensure(L, T, 0))) return rc;
+    cudaStream_t s = stream ? (cudaStream_t)stream : G.stream;
+    G.prof_valid = 0;
+    if ((rc = omc_launch_router(&L->dev, x, T, &G.ws, topk_idx, topk_w, NULL, s)))
+        return omc_fail(rc, "omc_moe_route_dev: router launch failed");
+    if (shared_gate && L->desc.has_shared)
+        CK(cudaMemcpyAsync(shared_gate, G.ws.sg, (size_t)T * sizeof(float), cudaMemcpyDeviceToDevice, s));
+    return OMC_OK;
+}
+
+int omc_moe_experts_dev(int layer, const float *x_rows, int R, const int32_t *expert, const float *weight, float *y,
+                        void *stream) {
+    if (!G.init) return omc_fail(OMC_ENOINIT, "omc_moe_experts_dev: omc_init not called");
+    omc_layer *L = omc_get_layer(layer);
+    if (!L) return omc_fail(OMC_ENOINIT, "omc_moe_experts_dev: layer %d not initialised", layer);
+    if (R < 0 || (R > 0 && (!x_rows || !expert || !weight || !y)))
+        return omc_fail(OMC_EINVAL, "omc_moe_experts_dev: bad R or pointers");
+    if (((uintptr_t)x_rows | (uintptr_t)y) & 15)
+        return omc_fail(OMC_EINVAL, "omc_moe_experts_dev: x_rows and y must be 16-byte aligned");
+    if (R == 0) return OMC_OK;
+    int rc;
+    for (int e = L->e0; e < L->e0 + L->ne; ++e)
+        if (!L->have[e]) return omc_fail(OMC_ENOINIT, "omc_moe_experts_dev: expert %d not uploaded", e);
+    if (L->desc.has_shared && !L->have[L->desc.E])
+        return omc_fail(OMC_ENOINIT, "omc_moe_experts_dev: shared expert not uploaded");
+    if ((rc = ws_ensure_rows(L, R))) return rc;
+    cudaStream_t s = stream ? (cudaStream_t)stream : G.stream;
+    G.prof_valid = 0;
+    prof_begin(s);
+    if ((rc = omc_launch_mma_rows(&L->dev, x_rows, R, &G.ws, expert, weight, L->e0, L->e0 + L->ne, y, s)))
+        return omc_fail(rc, "omc_moe_experts_dev: launch failed");
+    G.prof_valid = G.profiling;
+    return OMC_OK;
 }
 
 int omc_moe_forward(int layer, const float *x, int T, float *out, int32_t *topk_idx, float *topk_w) {

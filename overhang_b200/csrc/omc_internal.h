@@ -101,6 +101,10 @@ typedef struct {
  * router's select kernel once every token's routing is written. */
 typedef struct {
     int E, K, T, has_shared;
+    int rows_mode;                /* 1: every slot is an explicit row (K = 1) whose
+                                     expert id may be E (the shared expert); no
+                                     implicit shared rows                          */
+    int e_lo, e_hi;               /* routed experts resident here: [e_lo, e_hi)  */
     int I_rows, Is_rows, D_rows;  /* row extents of gate/up (routed, shared) and down */
     int R_cap, cap1, cap2;        /* operand rows and work-list capacities      */
     int *counts;                  /* [E + 1] rows per group (shared group: T)   */
@@ -154,6 +158,9 @@ int omc_launch_mma_ffn(const omc_layer_dev *L, const float *x, int T, const omc_
                        const int32_t *topk_idx, const float *topk_w, float *out, cudaStream_t s);
 int omc_launch_test_wait(int *err, cudaStream_t s);
 long long omc_mma_work_items(const omc_layer_dev *L, int R);
+/* explicit-rows pass: y[r] = w[r] * expert ids[r] (x[r]), ids in [e_lo, e_hi) or E (shared) */
+int omc_launch_mma_rows(const omc_layer_dev *L, const float *x, int R, const omc_ws *ws, const int32_t *ids,
+                        const float *w, int e_lo, int e_hi, float *y, cudaStream_t s);
 int omc_noalloc_setup(int device);
 void *omc_noalloc_scratch_ptr(int device);
 int omc_launch_expf_probe(const float *x, float *y, long long n, cudaStream_t s);

@@ -21,7 +21,7 @@ __device__ inline void omc_plan_block(const omc_plan_args &p, const int32_t *__r
         *s_w2 = s_w1 + (OMC_MAX_E + 2);
     const int tid = threadIdx.x, nt = blockDim.x, lane = tid & 31;
     const int E = p.E, G = E + (p.has_shared ? 1 : 0), nslots = p.T * p.K;
-    for (int g = tid; g < G; g += nt) s_cnt[g] = g < E ? 0 : p.T;
+    for (int g = tid; g < G; g += nt) s_cnt[g] = (g < E || p.rows_mode) ? 0 : p.T;
     __syncthreads();
     // rank of each routed slot within its expert (arrival order; the rows of
     // an expert are independent, so their order does not change any value).
@@ -40,7 +40,8 @@ __device__ inline void omc_plan_block(const omc_plan_args &p, const int32_t *__r
             const int s = base + u * nt;
             if (s >= nslots) break;
             int pos = -1;
-            if (e[u] >= 0 && e[u] < E) pos = atomicAdd(&s_cnt[e[u]], 1);
+            const bool ok = (e[u] >= p.e_lo && e[u] < p.e_hi) || (p.rows_mode && p.has_shared && e[u] == E);
+            if (ok) pos = atomicAdd(&s_cnt[e[u]], 1);
             else omc_dev_error(err, OMC_DEVERR_ROUTE, OMC_SITE_DISPATCH, s);
             rank[s] = pos;
         }
@@ -133,7 +134,7 @@ __device__ inline void omc_plan_block(const omc_plan_args &p, const int32_t *__r
             p.roww[row] = w[u];
         }
     }
-    if (p.has_shared)       // the shared expert: token t at row offsets[E] + t, weight 1
+    if (p.has_shared && !p.rows_mode)       // the shared expert: token t at row offsets[E] + t, weight 1
         for (int t = tid; t < p.T; t += nt) {
             p.rowinfo[s_off[E] + t] = nslots + t;
             p.roww[s_off[E] + t] = 1.f;
