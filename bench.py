@@ -14,8 +14,11 @@ Arms
       (device entry omc_moe_forward_dev), timed with CUDA events on the
       launching stream, max over ranks; `e2e` = the same through the host
       entry omc_moe_forward (pinned host x in, host out/top-k back every
-      step).  N>1: each rank runs its own copy of the workload (weak
-      scaling, no data-path collective).
+      step).  N>1 (--mode replica, the default): N independent copies of
+      the workload (the OLMoE layer fits one GPU; weak scaling, no data-path
+      collective).  --mode ep: expert parallel -- each rank holds E/N of the
+      layer's experts and brings its own 512 tokens; routed rows go to their
+      experts' ranks and back with all_to_all over NCCL (overhang_b200.ep).
   reference: the reference's own CPU MoE (engines/olmoe.c moe(), compiled from
       its sources into oracle/_ref by oracle/Makefile) on all host cores, each
       step a bounded token sample; rank 0 only.
@@ -260,10 +263,18 @@ def run_ours(args):
     torch.cuda.set_device(dev)
     import overhang_b200 as ob
     ob.init(dev, 1 << 30)      # one layer: 403 MB of experts + router
+    ep_mode = world > 1 and args.mode == "ep"
+    if ep_mode:
+        ob.ep_init(rank, world)            # this rank holds experts [rank*E/world, (rank+1)*E/world)
     pyoracle, L = make_layer()
     layer = ob.MoELayer.from_oracle_layer(0, L)
+    ep = None
+    if ep_mode:
+        from overhang_b200.ep import ExpertParallel, LibCompute
+        ep = ExpertParallel(LibCompute(layer), E, K, D, False)
     nbuf = 8
-    xs = [torch.from_numpy(pyoracle.normal(SEED_X + i, (T, D))).to(f"cuda:{dev}") for i in range(nbuf)]
+    xs = [torch.from_numpy(pyoracle.normal(SEED_X + rank * nbuf + i, (T, D))).to(f"cuda:{dev}")
+          for i in range(nbuf)]
     out = torch.empty((T, D), dtype=torch.float32, device=f"cuda:{dev}")
     idx = torch.empty((T, K), dtype=torch.int32, device=f"cuda:{dev}")
     wts = torch.empty((T, K), dtype=torch.float32, device=f"cuda:{dev}")
@@ -273,6 +284,10 @@ def run_ours(args):
     sptr = stream.cuda_stream
 
     def step(i):
+        if ep_mode:
+            o, ii, _ = ep.forward(xs[i % nbuf])
+            idx.copy_(ii)
+            return
         layer.forward_dev(xs[i % nbuf].data_ptr(), T, out.data_ptr(), idx.data_ptr(), wts.data_ptr(),
                           sptr)
 
@@ -326,13 +341,23 @@ def run_ours(args):
     value = world * T * args.steps / (t_max / 1e3)
 
     # end to end through the host entry: pinned x in, out + routing back
-    hx = [torch.from_numpy(pyoracle.normal(SEED_X + i, (T, D))).pin_memory() for i in range(nbuf)]
+    hx = [torch.from_numpy(pyoracle.normal(SEED_X + rank * nbuf + i, (T, D))).pin_memory() for i in range(nbuf)]
     hout = torch.empty((T, D), dtype=torch.float32).pin_memory()
     hidx = torch.empty((T, K), dtype=torch.int32).pin_memory()
     hw = torch.empty((T, K), dtype=torch.float32).pin_memory()
     lib = ob.lib()
 
     def step_e2e(i):
+        if ep_mode:
+            # the expert-parallel forward of this rank's tokens: x from pinned host memory,
+            # out and the routing back to pinned host memory, every step
+            xd = hx[i % nbuf].to(f"cuda:{dev}", non_blocking=True)
+            o, ii, ww = ep.forward(xd)
+            hout.copy_(o, non_blocking=True)
+            hidx.copy_(ii, non_blocking=True)
+            hw.copy_(ww, non_blocking=True)
+            torch.cuda.current_stream().synchronize()
+            return
         rc = lib.omc_moe_forward(0, C.c_void_p(hx[i % nbuf].data_ptr()), T, C.c_void_p(hout.data_ptr()),
                                  C.c_void_p(hidx.data_ptr()), C.c_void_p(hw.data_ptr()))
         ob.check(rc, "omc_moe_forward")
@@ -354,9 +379,17 @@ def run_ours(args):
     # algorithmic bytes of one launch of the dominant kernel: every active
     # expert's int8 gate+up rows and their scales, the f16 copy of the tokens
     # it gathers rows from (T x D) and the f16 h it writes (one row per slot).
-    n_active = int(len(np.unique(idx.cpu().numpy())))
+    ids_seen = np.unique(idx.cpu().numpy())
+    if ep_mode:
+        # this rank's launch: its experts that received rows, and the rows it received
+        lo, hi = rank * E // world, (rank + 1) * E // world
+        n_active = int(((ids_seen >= lo) & (ids_seen < hi)).sum())
+        rows = ep.last_recv_rows
+    else:
+        n_active, rows = int(len(ids_seen)), T * K
     if dom == "gemm_gateup":
-        alg_bytes = n_active * (2 * I * D + 2 * I * 4) + T * D * 2 + T * K * I * 2
+        xh_rows = rows if ep_mode else T
+        alg_bytes = n_active * (2 * I * D + 2 * I * 4) + xh_rows * D * 2 + rows * I * 2
     else:
         alg_bytes = n_active * (2 * I * D + 2 * I * 4) + T * D * 4 + T * K * I * 4
     achieved = alg_bytes / (dom_ms / 1e3) / 1e9 if dom_ms > 0 else None
@@ -364,7 +397,9 @@ def run_ours(args):
     line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": t_max / args.steps, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f16xint8->f32",
-            "data": "synthetic", "config": dict(CONFIG, parallelism=f"replica{world}"),
+            "data": "synthetic",
+            "config": dict(CONFIG, parallelism=(f"ep{world}" if ep_mode else f"replica{world}"),
+                           tokens_per_rank=T),
             "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": T * D * 4,
                     "d2h_bytes_per_step": T * D * 4 + T * K * 8},
             "gpu_launches": launches,
@@ -394,6 +429,10 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--mode", default="replica", choices=["ep", "replica"],
+                    help="N>1: N independent replicas (the layer fits one GPU), or expert parallel "
+                         "(each rank holds E/N experts and its own 512 tokens; rows exchanged with "
+                         "all_to_all over NCCL)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

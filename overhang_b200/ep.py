@@ -92,6 +92,7 @@ class ExpertParallel:
         send_split = send_counts.tolist()
         recv_split = recv_counts.tolist()
         n_recv = int(sum(recv_split))
+        self.last_recv_rows = n_recv
         send_rows = x.index_select(0, order // k)
         meta = torch.stack([idx.reshape(-1)[order], w.reshape(-1)[order].view(torch.int32)], 1).contiguous()
         recv_rows = torch.empty((n_recv, D), dtype=x.dtype, device=dev)
