@@ -805,3 +805,56 @@ extern "C" int omc_launch_mma_rows(const omc_layer_dev *L, const float *x, int R
     omc_g_launches += 4;
     return cudaGetLastError() == cudaSuccess ? 0 : OMC_ECUDA;
 }
+
+// ------------------------------------------ job-driven pass (omm_moe) ---
+namespace {
+// rows[r] = x[pos[r]] (D floats, a multiple of 4).
+__global__ void __launch_bounds__(256) gather_rows_kernel(const float *__restrict__ x, const int *__restrict__ pos,
+                                                          int R, int S, int D, float *__restrict__ rows, int *err) {
+    const int r = blockIdx.y;
+    const int d = (blockIdx.x * blockDim.x + threadIdx.x) * 4;
+    if (r >= R || d >= D) return;
+    const int p = pos[r];
+    if (p < 0 || p >= S) {
+        if (d == 0) omc_dev_error(err, OMC_DEVERR_BOUNDS, OMC_SITE_DISPATCH, r);
+        return;
+    }
+    *reinterpret_cast<float4 *>(rows + (size_t)r * D + d) = *reinterpret_cast<const float4 *>(x + (size_t)p * D + d);
+}
+
+// out[s] += y[list[j]] for j in [off[s], off[s+1]), in that order (the jobs'
+// order): each element is one sequential fp32 chain, so the sums are
+// deterministic.
+__global__ void __launch_bounds__(256) ordered_add_kernel(float *__restrict__ out, const float *__restrict__ y,
+                                                          const int *__restrict__ off, const int *__restrict__ list,
+                                                          int S, int D) {
+    const int s = blockIdx.y;
+    const int d = (blockIdx.x * blockDim.x + threadIdx.x) * 4;
+    if (s >= S || d >= D) return;
+    float4 acc = *reinterpret_cast<const float4 *>(out + (size_t)s * D + d);
+    for (int j = off[s]; j < off[s + 1]; ++j) {
+        const float4 v = *reinterpret_cast<const float4 *>(y + (size_t)list[j] * D + d);
+        acc.x = __fadd_rn(acc.x, v.x);
+        acc.y = __fadd_rn(acc.y, v.y);
+        acc.z = __fadd_rn(acc.z, v.z);
+        acc.w = __fadd_rn(acc.w, v.w);
+    }
+    *reinterpret_cast<float4 *>(out + (size_t)s * D + d) = acc;
+}
+}  // namespace
+
+extern "C" int omc_launch_gather_rows(const float *x, const int *pos, int R, int S, int D, float *rows, int *err,
+                                      cudaStream_t s) {
+    if (R <= 0) return 0;
+    gather_rows_kernel<<<dim3((D / 4 + 255) / 256, R), 256, 0, s>>>(x, pos, R, S, D, rows, err);
+    omc_g_launches += 1;
+    return cudaGetLastError() == cudaSuccess ? 0 : OMC_ECUDA;
+}
+
+extern "C" int omc_launch_ordered_add(float *out, const float *y, const int *off, const int *list, int S, int D,
+                                      cudaStream_t s) {
+    if (S <= 0) return 0;
+    ordered_add_kernel<<<dim3((D / 4 + 255) / 256, S), 256, 0, s>>>(out, y, off, list, S, D);
+    omc_g_launches += 1;
+    return cudaGetLastError() == cudaSuccess ? 0 : OMC_ECUDA;
+}

@@ -289,9 +289,9 @@ int omc_layer_init(int layer, const omc_moe_desc *d, const void *router_w, const
  * dq (paired layout, see omc_expert_ptrs; `member` as in
  * omc_launch_relayout). */
 static int upload_matrix(const int8_t *q, const float *s, int O, int K, int O_pad, int K_pad, int8_t *dq, int member,
-                         const float **ws) {
+                         const float **ws, const float *scales_into) {
     int on_host;
-    float *dsc = omc_slab_alloc((size_t)O_pad * sizeof(float), &on_host);
+    float *dsc = scales_into ? (float *)scales_into : omc_slab_alloc((size_t)O_pad * sizeof(float), &on_host);
     if (!dsc) return omc_fail(OMC_ENOMEM, "expert upload: slab and host overflow exhausted");
     int rc = staging_ensure((size_t)O * K);
     if (rc) return rc;
@@ -302,7 +302,39 @@ static int upload_matrix(const int8_t *q, const float *s, int O, int K, int O_pa
     CK(cudaMemcpyAsync(dsc, s, (size_t)O * sizeof(float), cudaMemcpyHostToDevice, G.stream));
     /* the staging buffer is reused by the next matrix */
     CK(cudaStreamSynchronize(G.stream));
-    *ws = dsc;
+    if (ws) *ws = dsc;
+    return OMC_OK;
+}
+
+/* One expert (g, u [I][D], d [D][I] row-major int8, per-row scales) into the
+ * paired tile layout.  reuse != 0: overwrite the buffers ep already points to
+ * (same shape); otherwise allocate them from the slab. */
+int omc_expert_upload(int D, int D_pad, int D_rows, int I_, int I_pad, int I_rows, const int8_t *g, const float *gs,
+                      const int8_t *u, const float *us, const int8_t *d, const float *ds, omc_expert_ptrs *ep,
+                      int reuse) {
+    int rc, on_host = 0, on_host2 = 0;
+    /* g and u interleave as the two members of each tile pair; d's row tiles
+     * pair up (an odd last tile leaves its partner's blocks zero) */
+    const size_t gu_bytes = (size_t)2 * I_rows * D_pad;
+    const size_t d_bytes = (size_t)omc_round_up(D_rows, 2 * OMC_TM) * I_pad;
+    int8_t *gu = reuse ? (int8_t *)ep->g : omc_slab_alloc(gu_bytes, &on_host);
+    int8_t *dd = reuse ? (int8_t *)ep->d : omc_slab_alloc(d_bytes, &on_host2);
+    if (!gu || !dd) return omc_fail(OMC_ENOMEM, "expert upload: slab and host overflow exhausted");
+    (void)on_host;
+    (void)on_host2;
+    CK(cudaMemsetAsync(dd, 0, d_bytes, G.stream));   /* gu is fully written by the two relayouts */
+    const float *sg_ = NULL, *su_ = NULL, *sd_ = NULL;
+    if ((rc = upload_matrix(g, gs, I_, D, I_rows, D_pad, gu, 0, reuse ? NULL : &sg_, reuse ? ep->gs : NULL))) return rc;
+    if ((rc = upload_matrix(u, us, I_, D, I_rows, D_pad, gu, 1, reuse ? NULL : &su_, reuse ? ep->us : NULL))) return rc;
+    if ((rc = upload_matrix(d, ds, D, I_, D_rows, I_pad, dd, -1, reuse ? NULL : &sd_, reuse ? ep->ds : NULL))) return rc;
+    if (!reuse) {
+        ep->gs = sg_;
+        ep->us = su_;
+        ep->ds = sd_;
+    }
+    ep->g = gu;
+    ep->u = gu + OMC_BLK_BYTES;
+    ep->d = dd;
     return OMC_OK;
 }
 
@@ -310,23 +342,9 @@ static int set_expert_slot(omc_layer *L, int slot, int I_, int I_pad, int I_rows
                            const int8_t *u, const float *us, const int8_t *d, const float *ds) {
     const omc_layer_dev *P = &L->dev;
     omc_expert_ptrs ep;
-    int rc, on_host, on_host2;
-    /* g and u interleave as the two members of each tile pair; d's row tiles
-     * pair up (an odd last tile leaves its partner's blocks zero) */
-    const size_t gu_bytes = (size_t)2 * I_rows * P->D_pad;
-    const size_t d_bytes = (size_t)omc_round_up(P->D_rows, 2 * OMC_TM) * I_pad;
-    int8_t *gu = omc_slab_alloc(gu_bytes, &on_host);
-    int8_t *dd = omc_slab_alloc(d_bytes, &on_host2);
-    if (!gu || !dd) return omc_fail(OMC_ENOMEM, "expert upload: slab and host overflow exhausted");
-    (void)on_host;
-    (void)on_host2;
-    CK(cudaMemsetAsync(dd, 0, d_bytes, G.stream));   /* gu is fully written by the two relayouts */
-    if ((rc = upload_matrix(g, gs, I_, P->D, I_rows, P->D_pad, gu, 0, &ep.gs))) return rc;
-    if ((rc = upload_matrix(u, us, I_, P->D, I_rows, P->D_pad, gu, 1, &ep.us))) return rc;
-    if ((rc = upload_matrix(d, ds, P->D, I_, P->D_rows, I_pad, dd, -1, &ep.ds))) return rc;
-    ep.g = gu;
-    ep.u = gu + OMC_BLK_BYTES;
-    ep.d = dd;
+    int rc;
+    memset(&ep, 0, sizeof(ep));
+    if ((rc = omc_expert_upload(P->D, P->D_pad, P->D_rows, I_, I_pad, I_rows, g, gs, u, us, d, ds, &ep, 0))) return rc;
     L->h_experts[slot] = ep;
     L->have[slot] = 1;
     CK(cudaMemcpy(L->d_experts_tab + slot, &ep, sizeof(ep), cudaMemcpyHostToDevice));
@@ -458,7 +476,7 @@ int omc_ws_ensure(const omc_layer *L, int T, int host_io) {
     return ws_ensure_core(L, Tz, Tz * (size_t)L->dev.k, L->dev.has_shared ? Tz : 0, host_io);
 }
 
-static int ws_ensure_rows(const omc_layer *L, int rows) {
+int omc_ws_ensure_rows(const omc_layer *L, int rows) {
     return ws_ensure_core(L, (size_t)rows, (size_t)rows, 0, 0);
 }
 
@@ -760,7 +778,7 @@ int omc_moe_experts_dev(int layer, const float *x_rows, int R, const int32_t *ex
         if (!L->have[e]) return omc_fail(OMC_ENOINIT, "omc_moe_experts_dev: expert %d not uploaded", e);
     if (L->desc.has_shared && !L->have[L->desc.E])
         return omc_fail(OMC_ENOINIT, "omc_moe_experts_dev: shared expert not uploaded");
-    if ((rc = ws_ensure_rows(L, R))) return rc;
+    if ((rc = omc_ws_ensure_rows(L, R))) return rc;
     cudaStream_t s = stream ? (cudaStream_t)stream : G.stream;
     G.prof_valid = 0;
     prof_begin(s);

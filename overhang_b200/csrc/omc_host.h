@@ -75,6 +75,10 @@ int omc_fail(int code, const char *fmt, ...);
 void *omc_slab_alloc(size_t n, int *on_host);
 omc_layer *omc_get_layer(int layer);
 int omc_ws_ensure(const omc_layer *L, int T, int host_io);
+int omc_ws_ensure_rows(const omc_layer *L, int rows);
+int omc_expert_upload(int D, int D_pad, int D_rows, int I_, int I_pad, int I_rows, const int8_t *g, const float *gs,
+                      const int8_t *u, const float *us, const int8_t *d, const float *ds, omc_expert_ptrs *ep,
+                      int reuse);
 int omc_check_device_error(void);
 int omc_forward_device(omc_layer *L, const float *x, int T, float *out, int32_t *topk_idx, float *topk_w,
                        cudaStream_t s);

@@ -158,6 +158,9 @@ int omc_launch_mma_ffn(const omc_layer_dev *L, const float *x, int T, const omc_
                        const int32_t *topk_idx, const float *topk_w, float *out, cudaStream_t s);
 int omc_launch_test_wait(int *err, cudaStream_t s);
 long long omc_mma_work_items(const omc_layer_dev *L, int R);
+/* job-driven pass helpers: rows[r] = x[pos[r]]; out[s] += y[list[j]] over j in [off[s], off[s+1]) in order */
+int omc_launch_gather_rows(const float *x, const int *pos, int R, int S, int D, float *rows, int *err, cudaStream_t s);
+int omc_launch_ordered_add(float *out, const float *y, const int *off, const int *list, int S, int D, cudaStream_t s);
 /* explicit-rows pass: y[r] = w[r] * expert ids[r] (x[r]), ids in [e_lo, e_hi) or E (shared) */
 int omc_launch_mma_rows(const omc_layer_dev *L, const float *x, int R, const omc_ws *ws, const int32_t *ids,
                         const float *w, int e_lo, int e_hi, float *y, cudaStream_t s);

@@ -1,14 +1,39 @@
 /* omm_shim.c -- the engines' omm_* GPU seam (metal/om_metal.h:14-46) on CUDA.
- * Placeholder: device bring-up and pinned allocation work; the MoE entry
- * returns -3 (unsupported) so the engines keep their CPU path until the
- * job-driven expert pass lands. */
+ *
+ * The unmodified engines, built with -DOM_METAL against include/om_metal.h,
+ * hand their prefill MoE here (engines/olmoe.c:365-384): routing stays on the
+ * CPU, and omm_moe() receives one job per expert that received tokens (the
+ * batch union, experts ascending) with that expert's int8 weights, the
+ * positions routed to it and their router weights.  The reference backend
+ * computes out[pos[r]] += w[r] * SwiGLU_expert(x[pos[r]]) job by job
+ * (metal/om_metal.mm:208-296); so does this one, on the tensor-core grouped
+ * GEMM of the full forward:
+ *
+ *   - a job's weights (host memory of the engine's expert slots) are copied
+ *     once into HBM in the paired tile layout and looked up by the slot's g
+ *     pointer afterwards.  The engine's LRU may load another expert into the
+ *     same slot (engines/olmoe.c:263-270); a slot whose three scale vectors
+ *     changed is re-uploaded into the same device buffers;
+ *   - x is copied in, each job's rows gathered, the jobs run as one
+ *     explicit-rows pass (the jobs are the experts of a scratch layer), and
+ *     every position's weighted rows are added to out in job order, one
+ *     sequential fp32 chain per element, then out is copied back.
+ *
+ * Status codes are the reference's: 0 done, -1 allocation or device failure
+ * (the engine then falls back to its CPU path), -3 a shape this build does
+ * not serve (gelu_tanh, D or I not a multiple of 64, more than 1024 jobs).
+ * omm_dense*: -3, the engines keep their CPU dense path. */
+#include <stdint.h>
 #include <stdlib.h>
+#include <string.h>
 
 #include <cuda_runtime.h>
 
 #include "om_metal.h"
 #include "om_cuda.h"
 #include "omc_host.h"
+
+#define G omc_G
 
 int omm_init(void) {
     static int state = -1;
@@ -27,9 +52,186 @@ void *omm_alloc(size_t n) {
     return p;
 }
 
+/* ---- device copies of the engine's expert slots ------------------------ */
+typedef struct {
+    const int8_t *hg;            /* the slot's g pointer (its identity) */
+    int D, I;
+    float *sc;                   /* host copy of gs | us | ds the device copy was made from */
+    omc_expert_ptrs dev;
+} omm_slot;
+
+static omm_slot *g_slots;
+static int g_nslots, g_cap;
+
+static int resolve(const omm_job *j, int D, int I, omc_expert_ptrs *out) {
+    const size_t nsc = (size_t)2 * I + D;
+    omm_slot *sl = NULL;
+    for (int i = 0; i < g_nslots; ++i)
+        if (g_slots[i].hg == j->g && g_slots[i].D == D && g_slots[i].I == I) {
+            sl = &g_slots[i];
+            break;
+        }
+    if (sl && !memcmp(sl->sc, j->gs, (size_t)I * 4) && !memcmp(sl->sc + I, j->us, (size_t)I * 4) &&
+        !memcmp(sl->sc + 2 * I, j->ds, (size_t)D * 4)) {
+        *out = sl->dev;
+        return OMC_OK;
+    }
+    int reuse = sl != NULL;
+    if (!sl) {
+        if (g_nslots == g_cap) {
+            const int nc = g_cap ? 2 * g_cap : 64;
+            omm_slot *ns = realloc(g_slots, sizeof(omm_slot) * (size_t)nc);
+            if (!ns) return OMC_ENOMEM;
+            g_slots = ns;
+            g_cap = nc;
+        }
+        sl = &g_slots[g_nslots];
+        memset(sl, 0, sizeof(*sl));
+        sl->sc = malloc(sizeof(float) * nsc);
+        if (!sl->sc) return OMC_ENOMEM;
+        sl->hg = j->g;
+        sl->D = D;
+        sl->I = I;
+    }
+    const int Dr = omc_round_up(D, OMC_TM), Ir = omc_round_up(I, OMC_TM);
+    int rc = omc_expert_upload(D, D, Dr, I, I, Ir, j->g, j->gs, j->u, j->us, j->d, j->ds, &sl->dev, reuse);
+    if (rc) return rc;
+    if (!reuse) ++g_nslots;
+    memcpy(sl->sc, j->gs, (size_t)I * 4);
+    memcpy(sl->sc + I, j->us, (size_t)I * 4);
+    memcpy(sl->sc + 2 * I, j->ds, (size_t)D * 4);
+    *out = sl->dev;
+    return OMC_OK;
+}
+
+/* ---- grow-only device scratch of the job pass -------------------------- */
+enum { B_TAB, B_X, B_OUT, B_ROWS, B_Y, B_POS, B_W, B_IDS, B_OFF, B_LIST, NBUF };
+static void *g_buf[NBUF];
+static size_t g_bytes[NBUF];
+
+static void *scratch(int i, size_t n) {
+    if (g_bytes[i] >= n && g_buf[i]) return g_buf[i];
+    if (g_buf[i]) cudaFree(g_buf[i]);
+    g_buf[i] = NULL;
+    g_bytes[i] = 0;
+    if (cudaMalloc(&g_buf[i], n ? n : 16) != cudaSuccess) {
+        cudaGetLastError();
+        return NULL;
+    }
+    g_bytes[i] = n;
+    return g_buf[i];
+}
+
 int omm_moe_act(const omm_job *jobs, int nj, const float *x, int S, int D, int I, float *out, int gelu) {
-    (void)jobs; (void)nj; (void)x; (void)S; (void)D; (void)I; (void)out; (void)gelu;
-    return -3;
+    if (gelu) return -3;                       /* gelu_tanh (Gemma) is not served by this build */
+    if (!omm_init()) return -1;
+    if (nj <= 0 || S <= 0) return 0;
+    if (!jobs || !x || !out || D <= 0 || I <= 0 || D % 64 || I % 64 || nj > OMC_MAX_E) return -3;
+    long long Rl = 0;
+    for (int j = 0; j < nj; ++j) {
+        if (jobs[j].mpos < 0 || (jobs[j].mpos > 0 && (!jobs[j].pos || !jobs[j].w))) return -3;
+        for (int r = 0; r < jobs[j].mpos; ++r)
+            if (jobs[j].pos[r] < 0 || jobs[j].pos[r] >= S) return -3;
+        Rl += jobs[j].mpos;
+    }
+    if (Rl == 0) return 0;
+    if (Rl > (1 << 28)) return -3;
+    const int R = (int)Rl;
+    cudaSetDevice(G.device);
+    cudaStream_t s = G.stream;
+    int rc = 0;
+
+    /* the jobs as the experts of a scratch layer */
+    omc_expert_ptrs *tab = malloc(sizeof(omc_expert_ptrs) * (size_t)nj);
+    int *hpos = malloc(sizeof(int) * (size_t)R), *hids = malloc(sizeof(int) * (size_t)R);
+    int *hoff = calloc((size_t)S + 1, sizeof(int)), *hlist = malloc(sizeof(int) * (size_t)R);
+    float *hw = malloc(sizeof(float) * (size_t)R);
+    if (!tab || !hpos || !hids || !hoff || !hlist || !hw) {
+        rc = -1;
+        goto done;
+    }
+    for (int j = 0; j < nj; ++j)
+        if (resolve(&jobs[j], D, I, &tab[j])) {
+            rc = -1;
+            goto done;
+        }
+    /* rows in job order; per position, its rows in job order */
+    for (int j = 0, r = 0; j < nj; ++j)
+        for (int q = 0; q < jobs[j].mpos; ++q, ++r) {
+            hpos[r] = jobs[j].pos[q];
+            hw[r] = jobs[j].w[q];
+            hids[r] = j;
+            hoff[hpos[r] + 1]++;
+        }
+    for (int i = 0; i < S; ++i) hoff[i + 1] += hoff[i];
+    {
+        int *fill = calloc((size_t)S, sizeof(int));
+        if (!fill) {
+            rc = -1;
+            goto done;
+        }
+        for (int r = 0; r < R; ++r) hlist[hoff[hpos[r]] + fill[hpos[r]]++] = r;
+        free(fill);
+    }
+    omc_layer TL;
+    memset(&TL, 0, sizeof(TL));
+    TL.desc.family = OMC_FAMILY_OLMOE;         /* SwiGLU g/(1+exp(-g))*u, engines/olmoe.c:393 */
+    TL.desc.D = D;
+    TL.desc.I = I;
+    TL.desc.E = nj;
+    TL.desc.k = 1;
+    TL.dev.family = OMC_FAMILY_OLMOE;
+    TL.dev.D = D;
+    TL.dev.I = I;
+    TL.dev.E = nj;
+    TL.dev.k = 1;
+    TL.dev.D_pad = D;
+    TL.dev.I_pad = I;
+    TL.dev.D_rows = omc_round_up(D, OMC_TM);
+    TL.dev.I_rows = omc_round_up(I, OMC_TM);
+    TL.e0 = 0;
+    TL.ne = nj;
+    void *d_tab = scratch(B_TAB, sizeof(omc_expert_ptrs) * (size_t)(nj + 1));
+    float *d_x = scratch(B_X, (size_t)S * D * 4), *d_out = scratch(B_OUT, (size_t)S * D * 4);
+    float *d_rows = scratch(B_ROWS, (size_t)R * D * 4), *d_y = scratch(B_Y, (size_t)R * D * 4);
+    int *d_pos = scratch(B_POS, (size_t)R * 4), *d_ids = scratch(B_IDS, (size_t)R * 4);
+    float *d_w = scratch(B_W, (size_t)R * 4);
+    int *d_off = scratch(B_OFF, ((size_t)S + 1) * 4), *d_list = scratch(B_LIST, (size_t)R * 4);
+    if (!d_tab || !d_x || !d_out || !d_rows || !d_y || !d_pos || !d_ids || !d_w || !d_off || !d_list ||
+        omc_ws_ensure_rows(&TL, R)) {
+        rc = -1;
+        goto done;
+    }
+    TL.dev.experts = (const omc_expert_ptrs *)d_tab;
+    if (cudaMemcpyAsync(d_tab, tab, sizeof(omc_expert_ptrs) * (size_t)nj, cudaMemcpyHostToDevice, s) ||
+        cudaMemcpyAsync(d_x, x, (size_t)S * D * 4, cudaMemcpyHostToDevice, s) ||
+        cudaMemcpyAsync(d_out, out, (size_t)S * D * 4, cudaMemcpyHostToDevice, s) ||
+        cudaMemcpyAsync(d_pos, hpos, (size_t)R * 4, cudaMemcpyHostToDevice, s) ||
+        cudaMemcpyAsync(d_ids, hids, (size_t)R * 4, cudaMemcpyHostToDevice, s) ||
+        cudaMemcpyAsync(d_w, hw, (size_t)R * 4, cudaMemcpyHostToDevice, s) ||
+        cudaMemcpyAsync(d_off, hoff, ((size_t)S + 1) * 4, cudaMemcpyHostToDevice, s) ||
+        cudaMemcpyAsync(d_list, hlist, (size_t)R * 4, cudaMemcpyHostToDevice, s)) {
+        cudaGetLastError();
+        rc = -1;
+        goto done;
+    }
+    if (omc_launch_gather_rows(d_x, d_pos, R, S, D, d_rows, G.d_err, s) ||
+        omc_launch_mma_rows(&TL.dev, d_rows, R, &G.ws, d_ids, d_w, 0, nj, d_y, s) ||
+        omc_launch_ordered_add(d_out, d_y, d_off, d_list, S, D, s) ||
+        cudaMemcpyAsync(out, d_out, (size_t)S * D * 4, cudaMemcpyDeviceToHost, s) || cudaStreamSynchronize(s)) {
+        cudaGetLastError();
+        rc = -1;
+        goto done;
+    }
+    if (omc_check_device_error()) rc = -1;
+done:
+    free(tab);
+    free(hpos);
+    free(hids);
+    free(hoff);
+    free(hlist);
+    free(hw);
+    return rc;
 }
 
 int omm_moe(const omm_job *jobs, int nj, const float *x, int S, int D, int I, float *out) {
