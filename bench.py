@@ -41,6 +41,7 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 D, I, E, K, T = 2048, 1024, 64, 8, 512
+FAMILY, IS = "olmoe", 0                              # layer family, shared-expert width
 SEED_W, SEED_X = 1, 4242
 METRIC, UNIT = "MoE-block tokens/s", "tokens/s"
 WORKLOAD = "olmoe_layer_prefill_T512"
@@ -49,6 +50,33 @@ CONFIG = {"workload": WORKLOAD, "D": D, "I": I, "E": E, "k": K, "T": T,
           "weights": "int8 per-row + f32 scales, N(0,0.02) seed 1",
           "x": "f32 N(0,1) seed 4242, 8 rotating batches",
           "l2": "expert weights 403 MB > 126 MB L2 stream from HBM every step"}
+
+# The BASELINE configs measured by this script (the default line is configs[1]):
+#   olmoe_prefill  OLMoE-shaped layer, T=512 (C1)        olmoe_decode  the same, T=1
+#   qwen_prefill   Qwen-shaped layer with shared expert, int8 router, T=2048 (C2)
+#   qwen_decode    the same, T=1 (C2 decode)
+WORKLOADS = {
+    "olmoe_prefill": ("olmoe", 512), "olmoe_decode": ("olmoe", 1),
+    "qwen_prefill": ("qwen", 2048), "qwen_decode": ("qwen", 1),
+}
+
+
+def set_workload(name):
+    global D, I, E, K, T, FAMILY, IS, SEED_W, WORKLOAD, EXPERT_BYTES, CONFIG
+    FAMILY, T = WORKLOADS[name]
+    if FAMILY == "olmoe":
+        D, I, E, K, IS, SEED_W = 2048, 1024, 64, 8, 0, 1
+    else:
+        D, I, E, K, IS, SEED_W = 2048, 512, 256, 8, 512, 2
+    EXPERT_BYTES = 3 * D * I + 4 * (2 * I + D)
+    WORKLOAD = f"{FAMILY}_layer_{'prefill' if T > 1 else 'decode'}_T{T}"
+    total = E * EXPERT_BYTES + (3 * D * IS + 4 * (2 * IS + D) if IS else 0)
+    CONFIG = {"workload": WORKLOAD, "D": D, "I": I, "E": E, "k": K, "T": T,
+              "weights": f"int8 per-row + f32 scales, N(0,0.02) seed {SEED_W}",
+              "x": "f32 N(0,1) seed 4242, 8 rotating batches",
+              "l2": f"expert weights {total / 1e6:.0f} MB > 126 MB L2 stream from HBM every step"}
+    if IS:
+        CONFIG.update(shared_expert_I=IS, router="int8 + f32 scale", renorm=1)
 
 
 def env_rank():
@@ -164,11 +192,11 @@ class ClockSampler:
         return out
 
 
-def profiled_traffic(kernel):
+def profiled_traffic(kernel, workload):
     """DRAM bytes (read + write) per launch of `kernel`, from the committed
-    ncu summary profiles/<kernel>_olmoe_T512.md (its `traffic_bytes:` line),
+    ncu summary profiles/<kernel>_<workload>.md (its `traffic_bytes:` line),
     or None."""
-    p = os.path.join(ROOT, "profiles", f"{kernel}_olmoe_T512.md")
+    p = os.path.join(ROOT, "profiles", f"{kernel}_{workload}.md")
     if not os.path.exists(p):
         return None
     for ln in open(p):
@@ -183,6 +211,8 @@ def profiled_traffic(kernel):
 def make_layer():
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import pyoracle
+    if FAMILY == "qwen":
+        return pyoracle, pyoracle.qwen_layer(SEED_W, D=D, I=I, E=E, k=K, Is=IS)
     return pyoracle, pyoracle.olmoe_layer(SEED_W, D=D, I=I, E=E, k=K)
 
 
@@ -271,7 +301,7 @@ def run_ours(args):
     ep = None
     if ep_mode:
         from overhang_b200.ep import ExpertParallel, LibCompute
-        ep = ExpertParallel(LibCompute(layer), E, K, D, False)
+        ep = ExpertParallel(LibCompute(layer), E, K, D, bool(IS))
     nbuf = 8
     xs = [torch.from_numpy(pyoracle.normal(SEED_X + rank * nbuf + i, (T, D))).to(f"cuda:{dev}")
           for i in range(nbuf)]
@@ -387,13 +417,19 @@ def run_ours(args):
         rows = ep.last_recv_rows
     else:
         n_active, rows = int(len(ids_seen)), T * K
+    shared_w = (2 * IS * D + 2 * IS * 4) if IS else 0          # the shared expert's gate+up
+    srows = T if IS else 0
     if dom == "gemm_gateup":
         xh_rows = rows if ep_mode else T
-        alg_bytes = n_active * (2 * I * D + 2 * I * 4) + xh_rows * D * 2 + rows * I * 2
+        alg_bytes = (n_active * (2 * I * D + 2 * I * 4) + shared_w + xh_rows * D * 2
+                     + (rows + srows) * max(I, IS) * 2)
     else:
-        alg_bytes = n_active * (2 * I * D + 2 * I * 4) + T * D * 4 + T * K * I * 4
+        alg_bytes = n_active * (2 * I * D + 2 * I * 4) + shared_w + T * D * 4 + (T * K + srows) * max(I, IS) * 4
+    # the whole step's weight bytes (every active expert + shared + router) over the step time
+    router_bytes = E * D * (1 if IS else 4) + (4 * E if IS else 0) + (4 * D if IS else 0)
+    step_bytes = n_active * EXPERT_BYTES + (3 * D * IS + 4 * (2 * IS + D) if IS else 0) + router_bytes
     achieved = alg_bytes / (dom_ms / 1e3) / 1e9 if dom_ms > 0 else None
-    traffic = profiled_traffic(dom)
+    traffic = profiled_traffic(dom, args.workload)
     line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": t_max / args.steps, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f16xint8->f32",
@@ -407,7 +443,9 @@ def run_ours(args):
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
                          "frac": achieved / hbm if achieved else None, "traffic": traffic,
                          "kernel": dom, "peak_source": src, "alg_bytes_per_launch": alg_bytes,
-                         "launch_ms": dom_ms, "launches_timed": dom_n},
+                         "launch_ms": dom_ms, "launches_timed": dom_n,
+                         "step_weight_bytes": step_bytes,
+                         "step_hbm_frac": step_bytes / (t_max / args.steps / 1e3) / (hbm * 1e9)},
             "clocks": clocks}
     if rank == 0 and world == 1 and not args.no_cpu:
         tps, n, kind, cores, dt = cpu_reference_tokens_per_s(pyoracle, L, args.cpu_seconds)
@@ -429,6 +467,9 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--workload", default="olmoe_prefill", choices=sorted(WORKLOADS),
+                    help="olmoe_prefill (BASELINE configs[1], the default line), olmoe_decode, "
+                         "qwen_prefill, qwen_decode")
     ap.add_argument("--mode", default="replica", choices=["ep", "replica"],
                     help="N>1: N independent replicas (the layer fits one GPU), or expert parallel "
                          "(each rank holds E/N experts and its own 512 tokens; rows exchanged with "
@@ -436,6 +477,7 @@ def main():
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    set_workload(args.workload)
     if args.impl == "reference":
         run_reference(args)
     else:
