@@ -344,7 +344,10 @@ def run_ours(args):
     stage_ms = np.array([[v for _, v in row] for row in st]).mean(axis=0).tolist() if stage_names else []
     stages = dict(zip(stage_names, stage_ms))
     # the dominant kernel: the gate/up expert pass (2/3 of the weight bytes)
-    dom = "gemm_gateup" if "gemm_gateup" in stages else "gemv_gateup"
+    # the dominant kernel: the gate/up expert pass (2/3 of the weight bytes),
+    # or at decode sizes the fused kernel that is the whole block
+    dom = ("gemm_gateup" if "gemm_gateup" in stages else
+           "decode_moe" if "decode_moe" in stages else "gemv_gateup")
 
     barrier()
     clk = ClockSampler(dev)
@@ -419,15 +422,18 @@ def run_ours(args):
         n_active, rows = int(len(ids_seen)), T * K
     shared_w = (2 * IS * D + 2 * IS * 4) if IS else 0          # the shared expert's gate+up
     srows = T if IS else 0
+    # the whole step's weight bytes (every active expert + shared + router) over the step time
+    router_bytes = E * D * (1 if IS else 4) + (4 * E if IS else 0) + (4 * D if IS else 0)
+    step_bytes = n_active * EXPERT_BYTES + (3 * D * IS + 4 * (2 * IS + D) if IS else 0) + router_bytes
     if dom == "gemm_gateup":
         xh_rows = rows if ep_mode else T
         alg_bytes = (n_active * (2 * I * D + 2 * I * 4) + shared_w + xh_rows * D * 2
                      + (rows + srows) * max(I, IS) * 2)
+    elif dom == "decode_moe":
+        # one launch is the block: every weight byte of the step, x in, out back
+        alg_bytes = step_bytes + 2 * T * D * 4
     else:
         alg_bytes = n_active * (2 * I * D + 2 * I * 4) + shared_w + T * D * 4 + (T * K + srows) * max(I, IS) * 4
-    # the whole step's weight bytes (every active expert + shared + router) over the step time
-    router_bytes = E * D * (1 if IS else 4) + (4 * E if IS else 0) + (4 * D if IS else 0)
-    step_bytes = n_active * EXPERT_BYTES + (3 * D * IS + 4 * (2 * IS + D) if IS else 0) + router_bytes
     achieved = alg_bytes / (dom_ms / 1e3) / 1e9 if dom_ms > 0 else None
     traffic = profiled_traffic(dom, args.workload)
     line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,

@@ -81,11 +81,12 @@ SIGNATURES = {
     "omc_debug_ws_copy": (_i, [_i, _vp, _sz]),
 }
 
-PATH_AUTO, PATH_GEMV, PATH_MMA = 0, 1, 2
+PATH_AUTO, PATH_GEMV, PATH_MMA, PATH_DECODE = 0, 1, 2, 3
 
 
 def set_path(path: int) -> None:
-    """Force the expert path (tests): PATH_AUTO, PATH_GEMV or PATH_MMA."""
+    """Force the expert path (tests): PATH_AUTO, PATH_GEMV, PATH_MMA or PATH_DECODE
+    (the fused decode forward, T <= 8)."""
     check(lib().omc_debug_set_path(path), "omc_debug_set_path")
 
 _lib = None

@@ -48,7 +48,7 @@ __device__ __forceinline__ uint64_t omc_globaltimer() {
 // restatement does the same with explicit fma().  Checked equal to the host
 // glibc expf on all 2^32 float inputs (tests/test_oracle.py exercises the
 // host side; tests/test_router_gpu.py the device side).
-__constant__ uint64_t omc_exp2_tab[32] = {
+__device__ const uint64_t omc_exp2_tab[32] = {
     0x3ff0000000000000ULL, 0x3fefd9b0d3158574ULL, 0x3fefb5586cf9890fULL, 0x3fef9301d0125b51ULL,
     0x3fef72b83c7d517bULL, 0x3fef54873168b9aaULL, 0x3fef387a6e756238ULL, 0x3fef1e9df51fdee1ULL,
     0x3fef06fe0a31b715ULL, 0x3feef1a7373aa9cbULL, 0x3feedea64c123422ULL, 0x3feece086061892dULL,
@@ -57,7 +57,9 @@ __constant__ uint64_t omc_exp2_tab[32] = {
     0x3feeace5422aa0dbULL, 0x3feeb737b0cdc5e5ULL, 0x3feec49182a3f090ULL, 0x3feed503b23e255dULL,
     0x3feee89f995ad3adULL, 0x3feeff76f2fb5e47ULL, 0x3fef199bdd85529cULL, 0x3fef3720dcef9069ULL,
     0x3fef5818dcfba487ULL, 0x3fef7c97337b9b5fULL, 0x3fefa4afa2a490daULL, 0x3fefd0765b6e4540ULL};
-// table entry i = bits(2^(i/32)) - (i << 47), computed in 300-bit arithmetic
+// table entry i = bits(2^(i/32)) - (i << 47), computed in 300-bit arithmetic.
+// Global memory through the read-only path, not __constant__: lanes index
+// it with different i, which the constant cache would serialise.
 
 __device__ __forceinline__ float omc_expf_glibc(float x) {
     const uint32_t ix = __float_as_uint(x);
@@ -78,7 +80,7 @@ __device__ __forceinline__ float omc_expf_glibc(float x) {
     const uint64_t ki = (uint64_t)__double_as_longlong(kd);
     kd = __dsub_rn(kd, Shift);
     const double r = fma(InvLn2N, xd, -kd);
-    uint64_t t = omc_exp2_tab[ki & 31];
+    uint64_t t = __ldg(&omc_exp2_tab[ki & 31]);
     t += ki << 47;
     const double s = __longlong_as_double((long long)t);
     const double z = fma(C0, r, C1);

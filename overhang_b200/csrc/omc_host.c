@@ -159,11 +159,12 @@ int omc_init(int device, size_t slab_bytes) {
     G.device = device;
     G.init = 1;
     const char *p = getenv("OMC_FFN_PATH");
-    G.path_override = !p ? 0 : (!strcmp(p, "gemv") ? 1 : (!strcmp(p, "mma") ? 2 : 0));
+    G.path_override = !p ? 0 : (!strcmp(p, "gemv") ? 1 : (!strcmp(p, "mma") ? 2 : (!strcmp(p, "decode") ? 3 : 0)));
     return OMC_OK;
 }
 
 static void ws_free(void);
+static int dec_ensure(const omc_layer_dev *P);
 
 void omc_shutdown(void) {
     if (!G.init) return;
@@ -282,6 +283,10 @@ int omc_layer_init(int layer, const omc_moe_desc *d, const void *router_w, const
     P->experts = L->d_experts_tab;
     L->used = 1;
     CK(cudaStreamSynchronize(G.stream));
+    if (G.ep_world <= 1) {
+        int rc = dec_ensure(P);
+        if (rc) return rc;
+    }
     return OMC_OK;
 }
 
@@ -397,6 +402,36 @@ static void ws_free(void) {
     }
     memset(&G.ws, 0, sizeof(G.ws));
     memset(G.ws_bytes, 0, sizeof(G.ws_bytes));
+    cudaFree(G.dec_ctr);
+    cudaFree(G.dec_part);
+    G.dec_ctr = NULL;
+    G.dec_part = NULL;
+    G.dec_ctr_n = G.dec_part_n = 0;
+}
+
+/* Grows the fused-decode state to serve layer P (every T <= 8).  New
+ * counters start at zero; the kernel leaves them at zero after a forward. */
+static int dec_ensure(const omc_layer_dev *P) {
+    size_t ci = 0, pf = 0;
+    if (omc_decode_state_size(P, G.num_sms, &ci, &pf)) return OMC_OK;   /* layer not served by it */
+    if (ci <= G.dec_ctr_n && pf <= G.dec_part_n) return OMC_OK;
+    if (ci < G.dec_ctr_n) ci = G.dec_ctr_n;
+    if (pf < G.dec_part_n) pf = G.dec_part_n;
+    CK(cudaDeviceSynchronize());
+    cudaFree(G.dec_ctr);
+    cudaFree(G.dec_part);
+    G.dec_ctr = NULL;
+    G.dec_part = NULL;
+    G.dec_ctr_n = G.dec_part_n = 0;
+    if (cudaMalloc((void **)&G.dec_ctr, ci * sizeof(int)) != cudaSuccess ||
+        cudaMalloc((void **)&G.dec_part, pf * sizeof(float)) != cudaSuccess) {
+        cudaGetLastError();
+        return omc_fail(OMC_ENOMEM, "decode state: cudaMalloc(%zu ints, %zu floats) failed", ci, pf);
+    }
+    CK(cudaMemset(G.dec_ctr, 0, ci * sizeof(int)));
+    G.dec_ctr_n = ci;
+    G.dec_part_n = pf;
+    return OMC_OK;
 }
 
 /* grow-only buffer */
@@ -487,6 +522,8 @@ int omc_check_device_error(void) {
     if (e != cudaSuccess) return omc_fail(OMC_ECUDA, "reading device error word: %s", cudaGetErrorString(e));
     if (!h[0]) return OMC_OK;
     cudaMemset(G.d_err, 0, sizeof(h));
+    /* a forward that stopped at a lost wait may leave decode counters set */
+    if (G.dec_ctr) cudaMemset(G.dec_ctr, 0, G.dec_ctr_n * sizeof(int));
     const int st = h[0] == OMC_DEVERR_TIMEOUT ? OMC_ETIMEOUT : OMC_EDEVICE;
     return omc_fail(st, "device error code %d at site %d (detail %d)", h[0], h[1], h[2]);
 }
@@ -613,7 +650,7 @@ static int layer_ready(const omc_layer *L) {
 /* Choose the expert path: tensor-core grouped GEMM when experts see enough
  * tokens to fill an MMA N of 16, CUDA-core GEMV otherwise. */
 static int use_mma(const omc_layer *L, int T) {
-    if (G.path_override == 1) return 0;
+    if (G.path_override == 1 || G.path_override == 3) return 0;
     if (G.path_override == 2) return 1;
     const long long slots = (long long)T * L->desc.k;
     return slots >= 4LL * L->desc.E;   /* >= 4 tokens per expert on average */
@@ -633,6 +670,18 @@ static int forward_on_ws(omc_layer *L, const omc_ws *ws, const float *x, int T, 
         omc_plan_setup(&L->dev, T, ws, &plan);
         CK(cudaMemsetAsync(ws->done, 0, sizeof(int), s));
     }
+    /* decode: the whole block in one launch (decode.cu).  Chosen on its own
+     * at T = 1, where it beats the router + GEMV kernels; from T = 2 its
+     * CUDA-core dequant-and-dot is the bound and the separate kernels win
+     * (measured on B200), so larger T take it only when it is forced. */
+    if (!mma && G.ep_world <= 1 && (G.path_override == 3 || (G.path_override == 0 && T == 1)) &&
+        omc_decode_supported(&L->dev, T, G.num_sms, G.dec_ctr_n, G.dec_part_n)) {
+        if ((rc = omc_launch_decode(&L->dev, x, T, ws, G.num_sms, G.dec_ctr, G.dec_part, idx, w, out, s)))
+            return omc_fail(rc, "fused decode launch failed (%s)", omc_strerror(rc));
+        G.prof_valid = G.profiling;
+        return OMC_OK;
+    }
+    if (G.path_override == 3) return omc_fail(OMC_EUNSUPPORTED, "fused decode path forced but not available for T=%d", T);
     if ((rc = omc_launch_router(&L->dev, x, T, ws, idx, w, mma ? &plan : NULL, s)))
         return omc_fail(rc, "router launch failed");
     omc_prof_mark(s, "router_select");
@@ -825,9 +874,9 @@ int omc_debug_wait_timeout(void) {
 }
 
 /* Forces the expert path (0 auto, 1 CUDA-core GEMV, 2 tensor-core grouped
- * GEMM); tests use it to run both paths on the same inputs. */
+ * GEMM, 3 fused decode); tests use it to run every path on the same inputs. */
 int omc_debug_set_path(int path) {
-    if (path < 0 || path > 2) return omc_fail(OMC_EINVAL, "omc_debug_set_path: %d", path);
+    if (path < 0 || path > 3) return omc_fail(OMC_EINVAL, "omc_debug_set_path: %d", path);
     G.path_override = path;
     return OMC_OK;
 }

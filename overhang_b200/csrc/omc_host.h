@@ -63,7 +63,11 @@ typedef struct {
     int timer_on, timer_n, timer_created;
     char timer_name[32];
     cudaEvent_t timer_ev[2 * OMC_TIMER_RING];
-    int path_override;              /* 0 auto, 1 gemv, 2 mma (OMC_FFN_PATH) */
+    int path_override;              /* 0 auto, 1 gemv, 2 mma, 3 fused decode (OMC_FFN_PATH) */
+    /* fused decode state: counters (zero between forwards) and pieces */
+    int *dec_ctr;
+    float *dec_part;
+    size_t dec_ctr_n, dec_part_n;
     /* expert parallelism */
     int ep_rank, ep_world;
     void *ep;                       /* omc_ep_state (omc_ep.c)              */

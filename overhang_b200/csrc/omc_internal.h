@@ -56,6 +56,7 @@ extern "C" {
 #define OMC_SITE_DISPATCH      21
 #define OMC_SITE_GEMV          22
 #define OMC_SITE_COMBINE       23
+#define OMC_SITE_DECODE        24
 #define OMC_SITE_TEST_WAIT     90
 
 static inline int omc_round_up(int x, int m) { return (x + m - 1) / m * m; }
@@ -157,6 +158,12 @@ int omc_launch_gemv_ffn(const omc_layer_dev *L, const float *x, int T, const omc
 int omc_launch_mma_ffn(const omc_layer_dev *L, const float *x, int T, const omc_ws *ws,
                        const int32_t *topk_idx, const float *topk_w, float *out, cudaStream_t s);
 int omc_launch_test_wait(int *err, cudaStream_t s);
+/* fused decode forward (decode.cu): the state (counters, zeroed once, and
+ * pieces) serves every T <= 8 of a layer on a grid of G CTAs */
+int omc_decode_state_size(const omc_layer_dev *L, int G, size_t *ctr_ints, size_t *part_floats);
+int omc_decode_supported(const omc_layer_dev *L, int T, int G, size_t ctr_ints, size_t part_floats);
+int omc_launch_decode(const omc_layer_dev *L, const float *x, int T, const omc_ws *ws, int G, int *ctr, float *part,
+                      int32_t *topk_idx, float *topk_w, float *out, cudaStream_t s);
 long long omc_mma_work_items(const omc_layer_dev *L, int R);
 /* job-driven pass helpers: rows[r] = x[pos[r]]; out[s] += y[list[j]] over j in [off[s], off[s+1]) in order */
 int omc_launch_gather_rows(const float *x, const int *pos, int R, int S, int D, float *rows, int *err, cudaStream_t s);

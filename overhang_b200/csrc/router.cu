@@ -15,6 +15,7 @@
 //            selection order, then divide).
 //   shared gate: engines/qwen.c:460-461, sigmoid(sum sh_gate[i]*x[i]).
 #include "omc_plan.cuh"
+#include "omc_select.cuh"
 
 namespace {
 
@@ -137,134 +138,62 @@ __global__ void __launch_bounds__(RL_THREADS) router_logits_kernel(const float *
     }
 }
 
-// ---- select -----------------------------------------------------------------
-// One warp per token: softmax, top-k, renorm, shared-gate sigmoid.  Lane l
-// holds logits l, l+32, ...; order-dependent sums run from a shared-memory
-// copy so that their dependent chain is the add latency alone.  With a plan
-// (tensor-core forwards) the block that finishes last builds the dispatch
-// plan from every token's routing: no per-expert atomics in global memory.
-constexpr int SEL_WARPS = 8;
+// ---- logits, few tokens --------------------------------------------------------
+// Decode-sized batches (T <= 8): one block per 8 router rows stages all of D
+// for its rows and the T tokens at once (one memory latency instead of a
+// chunk pipeline), then one thread per (token, row) runs the exact chain.
+// The chain (D dependent adds) is the floor; the standard kernel would spread
+// 8 tokens x 32 rows over a single block and walk D in 16 staged chunks.
+constexpr int RS_ROWS = 8;
+constexpr int RS_TMAX = 8;
 
-template <int SEL_MAXV>   // ceil(E / 32) rounded up to a power of two
-__device__ __forceinline__ void select_token(const float *__restrict__ logits, int ldl, int t, int E, int K,
-                                             int family, int renorm, int has_shared,
-                                             int32_t *__restrict__ topk_idx, float *__restrict__ topk_w,
-                                             float *__restrict__ sg, int *err, float *es) {
-    const int lane = threadIdx.x & 31;
-    const float *lg = logits + (size_t)t * ldl;
-    float v[SEL_MAXV];
-    // max, as `if (x[i] > m) m = x[i]` from m = -1e30f
-    float m = -1e30f;
-#pragma unroll
-    for (int j = 0; j < SEL_MAXV; ++j) {
-        const int i = lane + 32 * j;
-        v[j] = i < E ? lg[i] : -INFINITY;
-        if (i < E && v[j] > m) m = v[j];
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    // e_i = expf(x_i - m)
-    bool tiny = false;
-    const float exact_floor = ldexpf(1.0f, (32 - __clz(max(E - 1, 1))) - 30);   // 2^(ceil(log2 E) - 30)
-#pragma unroll
-    for (int j = 0; j < SEL_MAXV; ++j) {
-        const int i = lane + 32 * j;
-        if (i < E) {
-            v[j] = omc_expf_glibc(__fsub_rn(v[j], m));
-            tiny |= v[j] < exact_floor;
-            es[i] = v[j];
+__global__ void __launch_bounds__(256) router_logits_small_kernel(const float *__restrict__ x, int T, int D,
+                                                                   const float *__restrict__ W,
+                                                                   const float *__restrict__ Ws, int E,
+                                                                   const float *__restrict__ sh_gate, int nrows,
+                                                                   float *__restrict__ logits, int ldl) {
+    extern __shared__ __align__(16) float sm[];     // [T][D+4] tokens, then [RS_ROWS][D+4] rows
+    const int LD = D + 4, tid = threadIdx.x;
+    const int r0 = blockIdx.x * RS_ROWS;
+    float *xs = sm, *wsm = sm + (size_t)T * LD;
+    const int q4 = D / 4;
+    for (int i = tid; i < (T + RS_ROWS) * q4; i += blockDim.x) {
+        const int row = i / q4, c = (i % q4) * 4;
+        const float *src;
+        float *dst;
+        bool ok;
+        if (row < T) {
+            ok = true;
+            src = x + (size_t)row * D + c;
+            dst = xs + (size_t)row * LD + c;
+        } else {
+            const int gr = r0 + row - T;
+            ok = gr < nrows;
+            src = (gr < E ? W + (size_t)gr * D : sh_gate) + c;
+            dst = wsm + (size_t)(row - T) * LD + c;
         }
+        cp_async16(dst, ok ? src : x, ok);
     }
-    __syncwarp();
-    float sf;   // the divisor as the reference uses it
-    if (family == OMC_FAMILY_QWEN && !__any_sync(0xffffffffu, tiny)) {
-        // double running sum.  When every term is >= 2^(ceil(log2 E) - 30) all
-        // partial sums are exact in double, so any order gives the
-        // reference's value: a butterfly.
-        double s = 0.0;
-#pragma unroll
-        for (int j = 0; j < SEL_MAXV; ++j)
-            if (lane + 32 * j < E) s = __dadd_rn(s, (double)v[j]);
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) s = __dadd_rn(s, __shfl_xor_sync(0xffffffffu, s, o));
-        sf = __double2float_rn(s);
-    } else if (family == OMC_FAMILY_QWEN) {
-        // otherwise the index-order double sum of engines/qwen.c:163, every lane
-        double s = 0.0;
-        int i = 0;
-        for (; i + 4 <= E; i += 4) {
-            const float4 q = *reinterpret_cast<const float4 *>(es + i);
-            s = __dadd_rn(s, (double)q.x);
-            s = __dadd_rn(s, (double)q.y);
-            s = __dadd_rn(s, (double)q.z);
-            s = __dadd_rn(s, (double)q.w);
-        }
-        for (; i < E; ++i) s = __dadd_rn(s, (double)es[i]);
-        sf = __double2float_rn(s);
-    } else {
-        // float running sum in index order (engines/olmoe.c:172), every lane
-        float s = 0.f;
-        int i = 0;
-#pragma unroll 4
-        for (; i + 4 <= E; i += 4) {
-            const float4 q = *reinterpret_cast<const float4 *>(es + i);
-            s = __fadd_rn(s, q.x);
-            s = __fadd_rn(s, q.y);
-            s = __fadd_rn(s, q.z);
-            s = __fadd_rn(s, q.w);
-        }
-        for (; i < E; ++i) s = __fadd_rn(s, es[i]);
-        sf = s;
+    cp_async_commit();
+    cp_async_wait<0>();
+    __syncthreads();
+    if (tid >= T * RS_ROWS) return;
+    const int t = tid / RS_ROWS, r = tid % RS_ROWS, gr = r0 + r;
+    const float *xr = xs + (size_t)t * LD, *wr = wsm + (size_t)r * LD;
+    float acc = 0.f;
+#pragma unroll 8
+    for (int c = 0; c < D; c += 4) {
+        const float4 xv = *reinterpret_cast<const float4 *>(xr + c);
+        const float4 wv = *reinterpret_cast<const float4 *>(wr + c);
+        acc = __fadd_rn(acc, __fmul_rn(xv.x, wv.x));
+        acc = __fadd_rn(acc, __fmul_rn(xv.y, wv.y));
+        acc = __fadd_rn(acc, __fmul_rn(xv.z, wv.z));
+        acc = __fadd_rn(acc, __fmul_rn(xv.w, wv.w));
     }
-    // probabilities as order keys: p >= 0, so bits(p) + 1 orders like p and
-    // 0 marks "not available" (outside E, NaN, or already taken).
-    uint32_t key[SEL_MAXV];
-    float pv[SEL_MAXV];
-#pragma unroll
-    for (int j = 0; j < SEL_MAXV; ++j) {
-        const int i = lane + 32 * j;
-        pv[j] = i < E ? __fdiv_rn(v[j], sf) : 0.f;
-        key[j] = (i < E && pv[j] == pv[j]) ? __float_as_uint(pv[j]) + 1u : 0u;
-    }
-    // top-k: engines/olmoe.c:355-362 -- largest p, ties to the lowest id
-    int my_idx = -1;
-    float my_val = 0.f;
-    for (int kk = 0; kk < K; ++kk) {
-        uint32_t bk = 0;
-        int bj = 0;
-#pragma unroll
-        for (int j = 0; j < SEL_MAXV; ++j)
-            if (key[j] > bk) { bk = key[j]; bj = j; }      // strict: lowest j (= lowest id) of this lane
-        const uint32_t kmax = __reduce_max_sync(0xffffffffu, bk);
-        const uint32_t cand = (bk == kmax && kmax != 0u) ? (uint32_t)(lane + 32 * bj) : 0xffffffffu;
-        const uint32_t best = __reduce_min_sync(0xffffffffu, cand);
-        if (kmax != 0u && (int)(best & 31) == lane) {
-#pragma unroll
-            for (int j = 0; j < SEL_MAXV; ++j)
-                if (j == (int)(best >> 5)) key[j] = 0u;
-        }
-        if (lane == kk) {
-            my_idx = kmax != 0u ? (int)best : -1;
-            my_val = __uint_as_float(kmax - 1u);
-        }
-    }
-    // renorm: float sum in selection order, then divide (engines/olmoe.c:363)
-    if (renorm || family == OMC_FAMILY_QWEN) {
-        float sm = 0.f;
-        for (int kk = 0; kk < K; ++kk) sm = __fadd_rn(sm, __shfl_sync(0xffffffffu, my_val, kk));
-        my_val = __fdiv_rn(my_val, sm);
-    }
-    if (lane < K) {
-        if (my_idx < 0 || my_idx >= E) omc_dev_error(err, OMC_DEVERR_ROUTE, OMC_SITE_ROUTER, t);
-        topk_idx[(size_t)t * K + lane] = my_idx;
-        topk_w[(size_t)t * K + lane] = my_val;
-    }
-    if (has_shared && lane == 0) {
-        const float z = lg[E];
-        sg[t] = __fdiv_rn(1.f, __fadd_rn(1.f, omc_expf_glibc(-z)));   // engines/qwen.c:158,461
-    }
+    if (gr < nrows) logits[(size_t)t * ldl + gr] = (Ws && gr < E) ? __fmul_rn(acc, Ws[gr]) : acc;
 }
 
+// ---- select: select_token (omc_select.cuh) -------------------------------
 __host__ __device__ constexpr int SEL_SMEM_FLOATS(int maxv) { return SEL_WARPS * maxv * 32 > OMC_PLAN_SMEM_INTS ? SEL_WARPS * maxv * 32 : OMC_PLAN_SMEM_INTS; }
 
 template <int SEL_MAXV>
@@ -298,7 +227,7 @@ extern "C" int omc_launch_router(const omc_layer_dev *L, const float *x, int T, 
                                  int32_t *topk_idx, float *topk_w, const omc_plan_args *plan, cudaStream_t s) {
     if (T <= 0) return 0;
     if (L->E > OMC_MAX_E || L->k > OMC_MAX_K || (L->D & 3)) return OMC_EINVAL;
-    static int attr_done = 0;
+    static int attr_done = 0, attr_small = 0;
     if (!attr_done) {
         if (cudaFuncSetAttribute(router_logits_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)RL_SMEM) !=
             cudaSuccess)
@@ -307,10 +236,22 @@ extern "C" int omc_launch_router(const omc_layer_dev *L, const float *x, int T, 
     }
     const int nrows = L->E + (L->has_shared ? 1 : 0);
     const int ldl = L->E + 1;
-    const dim3 g1((T + RL_TOK - 1) / RL_TOK, (nrows + RL_ROWS - 1) / RL_ROWS);
-    router_logits_kernel<<<g1, RL_THREADS, RL_SMEM, s>>>(x, T, L->D, L->router, L->router_i8 ? L->router_s : nullptr,
-                                                         L->E, L->sh_gate, nrows, ws->logits, ldl,
-                                                         plan ? ws->xh : nullptr, ws->err);
+    const size_t small_smem = (size_t)(T + RS_ROWS) * (L->D + 4) * sizeof(float);
+    if (!plan && T <= RS_TMAX && small_smem <= 200 * 1024) {
+        if (!attr_small) {
+            if (cudaFuncSetAttribute(router_logits_small_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     200 * 1024) != cudaSuccess)
+                return OMC_ECUDA;
+            attr_small = 1;
+        }
+        router_logits_small_kernel<<<(nrows + RS_ROWS - 1) / RS_ROWS, 256, small_smem, s>>>(
+            x, T, L->D, L->router, L->router_i8 ? L->router_s : nullptr, L->E, L->sh_gate, nrows, ws->logits, ldl);
+    } else {
+        const dim3 g1((T + RL_TOK - 1) / RL_TOK, (nrows + RL_ROWS - 1) / RL_ROWS);
+        router_logits_kernel<<<g1, RL_THREADS, RL_SMEM, s>>>(x, T, L->D, L->router, L->router_i8 ? L->router_s : nullptr,
+                                                             L->E, L->sh_gate, nrows, ws->logits, ldl,
+                                                             plan ? ws->xh : nullptr, ws->err);
+    }
     omc_prof_mark(s, "router_logits");
     const int nv = (L->E + 31) / 32;
     const dim3 g2((T + SEL_WARPS - 1) / SEL_WARPS);
