@@ -1,0 +1,34 @@
+"""GPU: greedy tokens of the OLMoE engine with its MoE layer on the GPU are
+identical to the reference engine's on the CPU (random-init model).
+
+A smaller model than the C0 configuration (2 layers, vocab 4096) keeps the
+suite short; every layer has the full OLMoE-shaped MoE (D 2048, 64 experts,
+top-8, I 1024).  The 32-token prompt runs the prefill through the library
+(routing, dispatch, experts, combine on the GPU) and every generated token
+the decode path.  Both expert paths for the prompt are checked: the default
+(tensor-core grouped GEMM with f16 operands) and the CUDA-core path with f32
+activations.  The full C0 run is `python tests/e2e_olmoe.py`.
+"""
+import os
+
+import pytest
+
+import e2e_olmoe as E2E
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def snapshot(tmp_path_factory):
+    if not (os.path.exists(E2E.REF_ENGINE) and os.path.exists(E2E.OMC_ENGINE)):
+        pytest.skip("engine builds missing (oracle/_ref/olmoe, olmoe_omc): run the build")
+    d = str(tmp_path_factory.mktemp("olmoe_e2e"))
+    E2E.make_snapshot(os.path.join(d, "snap"), layers=2, vocab=4096)
+    return d
+
+
+@pytest.mark.parametrize("path", [None, "gemv"])
+def test_greedy_tokens_identical(snapshot, path):
+    # the engine processes initialise the library themselves (their own slab)
+    r = E2E.compare(layers=2, vocab=4096, n_prompt=32, n_new=16, path=path, workdir=snapshot)
+    assert r["identical"], f"first difference at token {r['first_difference']}: {r['cpu_tokens']} vs {r['gpu_tokens']}"
