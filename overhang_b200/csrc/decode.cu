@@ -107,9 +107,9 @@ __device__ __forceinline__ void red_release_add(int *p, int v) {
     asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 // Release/acquire fence at GPU scope.  After a block (or named) barrier it
-// also releases what the other threads wrote before the barrier.  Not
-// __threadfence(): its sequentially consistent fence stalled a thread for
-// tens of microseconds here while the SM's bulk copies were in flight.
+// also releases what the other threads wrote before the barrier (the
+// pattern CUTLASS's inter-CTA barrier uses); it is weaker, and cheaper, than
+// the sequentially consistent fence of __threadfence().
 __device__ __forceinline__ void fence_acqrel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
 __device__ __forceinline__ void cons_bar() { asm volatile("bar.sync 1, %0;" ::"n"(DC_CT) : "memory"); }
 
@@ -138,7 +138,7 @@ __device__ bool wait_value(const int *p, int want, int *err, int detail) {
 __device__ __forceinline__ void mbar_wait_s(uint64_t *bar, uint32_t parity, int *err) {
     if (mbar_try_wait(bar, parity)) return;
     const uint64_t t0 = omc_globaltimer();
-    while (!mbar_try_wait_sleep(bar, parity, 256u)) {   // a longer hint oversleeps the phase flip
+    while (!mbar_try_wait_sleep(bar, parity, 256u)) {   // short hint: wake-up latency stays small
         if (omc_globaltimer() - t0 > OMC_WAIT_LIMIT_NS) {
             omc_dev_error(err, OMC_DEVERR_TIMEOUT, OMC_SITE_DECODE, (int)parity);
             return;
