@@ -61,9 +61,11 @@ WORKLOADS = {
 }
 
 
-def set_workload(name):
+def set_workload(name, tokens=None):
     global D, I, E, K, T, FAMILY, IS, SEED_W, WORKLOAD, EXPERT_BYTES, CONFIG
     FAMILY, T = WORKLOADS[name]
+    if tokens:
+        T = tokens
     if FAMILY == "olmoe":
         D, I, E, K, IS, SEED_W = 2048, 1024, 64, 8, 0, 1
     else:
@@ -425,6 +427,9 @@ def run_ours(args):
     # the whole step's weight bytes (every active expert + shared + router) over the step time
     router_bytes = E * D * (1 if IS else 4) + (4 * E if IS else 0) + (4 * D if IS else 0)
     step_bytes = n_active * EXPERT_BYTES + (3 * D * IS + 4 * (2 * IS + D) if IS else 0) + router_bytes
+    # one GPU's algorithmic FLOP per step (per token: k experts' three projections, the
+    # router, and the shared expert with its gate)
+    step_flop = T * (2 * K * 3 * D * I + 2 * D * E + ((2 * 3 * D * IS + 2 * D) if IS else 0))
     if dom == "gemm_gateup":
         xh_rows = rows if ep_mode else T
         alg_bytes = (n_active * (2 * I * D + 2 * I * 4) + shared_w + xh_rows * D * 2
@@ -451,7 +456,10 @@ def run_ours(args):
                          "kernel": dom, "peak_source": src, "alg_bytes_per_launch": alg_bytes,
                          "launch_ms": dom_ms, "launches_timed": dom_n,
                          "step_weight_bytes": step_bytes,
-                         "step_hbm_frac": step_bytes / (t_max / args.steps / 1e3) / (hbm * 1e9)},
+                         "step_hbm_frac": step_bytes / (t_max / args.steps / 1e3) / (hbm * 1e9),
+                         "step_flop": step_flop,
+                         "step_tensor_frac": (step_flop / (t_max / args.steps / 1e3) / (tf * 1e12)
+                                              if tf else None)},
             "clocks": clocks}
     if rank == 0 and world == 1 and not args.no_cpu:
         tps, n, kind, cores, dt = cpu_reference_tokens_per_s(pyoracle, L, args.cpu_seconds)
@@ -476,6 +484,8 @@ def main():
     ap.add_argument("--workload", default="olmoe_prefill", choices=sorted(WORKLOADS),
                     help="olmoe_prefill (BASELINE configs[1], the default line), olmoe_decode, "
                          "qwen_prefill, qwen_decode")
+    ap.add_argument("--tokens", type=int, default=None,
+                    help="tokens per rank instead of the workload's T (the T sweep of the prefill rows)")
     ap.add_argument("--mode", default="replica", choices=["ep", "replica"],
                     help="N>1: N independent replicas (the layer fits one GPU), or expert parallel "
                          "(each rank holds E/N experts and its own 512 tokens; rows exchanged with "
@@ -483,7 +493,7 @@ def main():
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    set_workload(args.workload)
+    set_workload(args.workload, args.tokens)
     if args.impl == "reference":
         run_reference(args)
     else:

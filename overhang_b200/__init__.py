@@ -78,6 +78,7 @@ SIGNATURES = {
     "omc_debug_wait_timeout": (_i, []),
     "omc_debug_expf": (_i, [_vp, _vp, C.c_longlong]),
     "omc_debug_set_path": (_i, [_i]),
+    "omc_debug_router_tile": (_i, [_i, _i, _i]),
     "omc_debug_ws_copy": (_i, [_i, _vp, _sz]),
 }
 
@@ -88,6 +89,14 @@ def set_path(path: int) -> None:
     """Force the expert path (tests): PATH_AUTO, PATH_GEMV, PATH_MMA or PATH_DECODE
     (the fused decode forward, T <= 8)."""
     check(lib().omc_debug_set_path(path), "omc_debug_set_path")
+
+
+ROUTER_TILES = [(16, 4, 4), (16, 2, 2), (16, 1, 1), (8, 1, 1)]
+
+
+def set_router_tile(g: int = 0, tt: int = 0, rr: int = 0) -> None:
+    """Force the router logits tile (tests): one of ROUTER_TILES, or 0,0,0 = automatic."""
+    check(lib().omc_debug_router_tile(g, tt, rr), "omc_debug_router_tile")
 
 _lib = None
 

@@ -20,20 +20,22 @@
 namespace {
 
 // ---- logits -----------------------------------------------------------------
-// Block = 8 tokens x 32 router rows, 4 warps.  Lane l of warp w owns token
-// (l & 7) and rows 8w + 2(l >> 3) + {0, 1}: two chains per thread.  Per four
-// K elements a warp reads one 16-byte x vector (8 distinct tokens, one
-// wavefront) and two 16-byte row vectors (4 distinct rows each, one wavefront
-// each), so shared-memory traffic is 3 wavefronts per 64 chains instead of 5
-// per 32 with one row per lane.  K streams through a 4-stage cp.async ring.
-constexpr int RL_TOK = 8;                   // tokens per block
-constexpr int RL_ROWS = 32;                 // router rows per block
-constexpr int RL_THREADS = 128;
-constexpr int RL_CH = 128;                  // K elements per stage
-constexpr int RL_ST = 4;                    // stages
-constexpr int RL_LD = RL_CH + 4;            // padded row: 8 consecutive rows hit 8 distinct bank quads
-constexpr int RL_STAGE = (RL_TOK + RL_ROWS) * RL_LD;            // floats per stage
-constexpr size_t RL_SMEM = (size_t)RL_ST * RL_STAGE * sizeof(float);   // 84,480 B
+// Block = G x G threads (G = 16 or 8); thread (tg, rg) runs the TT x RR
+// chains of tokens tg + Gi and router rows rg + Gj of the block's (G TT) x
+// (G RR) tile (strided, so a warp's token rows fall in distinct bank quads
+// and its row groups broadcast).  Per four K elements a thread loads TT + RR
+// 16-byte vectors and advances 4 TT RR chains: separately rounded products,
+// then two chains' adds at a time as one packed add.rn.f32x2.  K
+// streams through a 4-stage cp.async ring of KC-element chunks; a partial
+// last chunk is zero-filled (adding 0*0 leaves a chain's value unchanged: it
+// starts at +0, so it is never -0).  The tile is chosen per launch
+// (launch_logits): 2 x 2 chains per thread with 64-element chunks once the
+// grid fills the SMs, else one chain per thread with 128-element chunks, so
+// that three chunks of chain work cover a chunk's L2 latency.
+constexpr int RT_ST = 4;                    // stages
+
+template <int G, int TT, int RR, int KC>
+constexpr size_t rt_smem() { return (size_t)RT_ST * (G * TT + G * RR) * (KC + 4) * sizeof(float); }
 
 __device__ __forceinline__ void cp_async16(void *smem_dst, const void *gsrc, bool valid) {
     const uint32_t d = smem_u32(smem_dst);
@@ -44,97 +46,135 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
-// (a0, a1) = (RN(a0 + b0), RN(a1 + b1)): two independent IEEE single adds in
-// one packed instruction; each lane of the pair rounds exactly as add.rn.f32.
-__device__ __forceinline__ void add2_rn(float &a0, float &a1, float b0, float b1) {
-    asm("{\n\t.reg .b64 ra, rb;\n\t"
-        "mov.b64 ra, {%0, %1};\n\t"
-        "mov.b64 rb, {%2, %3};\n\t"
-        "add.rn.f32x2 ra, ra, rb;\n\t"
-        "mov.b64 {%0, %1}, ra;\n\t}"
-        : "+f"(a0), "+f"(a1)
-        : "f"(b0), "f"(b1));
+// Packed IEEE add, two lanes, each rounded to nearest as add.rn.f32.  The
+// products stay scalar __fmul_rn: with a packed multiply feeding it, the
+// chains came out a few ulps off the reference (as if the product were not
+// rounded on its own), so they are kept as two separately rounded multiplies.
+__device__ __forceinline__ float2 add2_rn(float2 a, float2 b) {
+    float2 r;
+    asm("{\n\t.reg .b64 ra, rb, rc;\n\t"
+        "mov.b64 ra, {%2, %3};\n\t"
+        "mov.b64 rb, {%4, %5};\n\t"
+        "add.rn.f32x2 rc, ra, rb;\n\t"
+        "mov.b64 {%0, %1}, rc;\n\t}"
+        : "=f"(r.x), "=f"(r.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+    return r;
 }
 
 // logits[t][j], j < nrows: rows 0..E-1 are the router, row E (when
 // has_shared) the shared-expert gate vector.  Every (token, row) value is the
 // reference's chain acc = RN(acc + RN(x[i] * w[i])), i ascending.
-__global__ void __launch_bounds__(RL_THREADS) router_logits_kernel(const float *__restrict__ x, int T, int D,
-                                                                    const float *__restrict__ W,
-                                                                    const float *__restrict__ Ws, int E,
-                                                                    const float *__restrict__ sh_gate, int nrows,
-                                                                    float *__restrict__ logits, int ldl,
-                                                                    uint16_t *__restrict__ xh, int *err) {
-    (void)err;
+template <int G, int TT, int RR, int KC>
+__global__ void __launch_bounds__(G * G, 2) router_tile_kernel(const float *__restrict__ x, int T, int D,
+                                                                  const float *__restrict__ W,
+                                                                  const float *__restrict__ Ws, int E,
+                                                                  const float *__restrict__ sh_gate, int nrows,
+                                                                  float *__restrict__ logits, int ldl,
+                                                                  uint16_t *__restrict__ xh) {
     extern __shared__ __align__(16) float rsm[];
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int t0 = blockIdx.x * RL_TOK, row0 = blockIdx.y * RL_ROWS;
-    const int tok = lane & 7, rl = warp * 8 + (lane >> 3) * 2;   // rows rl, rl+1 of the block
-    const int nch = (D + RL_CH - 1) / RL_CH;
+    constexpr int NT = G * G, BT = G * TT, BR = G * RR, LD = KC + 4, STAGE = (BT + BR) * LD;
+    const int tid = threadIdx.x, tg = tid % G, rg = tid / G;
+    const int t0 = blockIdx.x * BT, r0 = blockIdx.y * BR;
+    const int nch = (D + KC - 1) / KC;
     auto load = [&](int ch) {
-        float *st = rsm + (size_t)(ch % RL_ST) * RL_STAGE;
-        const int c0 = ch * RL_CH;
-        // one warp copies one 512-byte row segment per pass (coalesced)
-        for (int i = threadIdx.x; i < (RL_TOK + RL_ROWS) * (RL_CH / 4); i += RL_THREADS) {
-            const int r = i / (RL_CH / 4), c = (i % (RL_CH / 4)) * 4;
+        float *st = rsm + (size_t)(ch % RT_ST) * STAGE;
+        const int c0 = ch * KC;
+        for (int i = tid; i < (BT + BR) * (KC / 4); i += NT) {
+            const int r = i / (KC / 4), c = (i % (KC / 4)) * 4;
             const float *src;
             bool ok;
-            if (r < RL_TOK) {
-                ok = t0 + r < T && c0 + c < D;
+            if (r < BT) {
+                ok = t0 + r < T;
                 src = x + (size_t)(t0 + r) * D + c0 + c;
             } else {
-                const int gr = row0 + r - RL_TOK;
-                ok = gr < nrows && c0 + c < D;
+                const int gr = r0 + r - BT;
+                ok = gr < nrows;
                 src = (gr < E ? W + (size_t)gr * D : sh_gate) + c0 + c;
             }
-            cp_async16(st + r * RL_LD + c, ok ? src : x, ok);
+            ok = ok && c0 + c < D;
+            cp_async16(st + r * LD + c, ok ? src : x, ok);
         }
     };
 #pragma unroll
-    for (int s = 0; s < RL_ST - 1; ++s) {
+    for (int s = 0; s < RT_ST - 1; ++s) {
         if (s < nch) load(s);
         cp_async_commit();
     }
-    float acc0 = 0.f, acc1 = 0.f;
+    float acc[TT][RR];
+#pragma unroll
+    for (int i = 0; i < TT; ++i)
+#pragma unroll
+        for (int j = 0; j < RR; ++j) acc[i][j] = 0.f;
     for (int ch = 0; ch < nch; ++ch) {
-        cp_async_wait<RL_ST - 2>();   // chunk ch has landed (this thread's copies)
+        cp_async_wait<RT_ST - 2>();   // chunk ch has landed (this thread's copies)
         __syncthreads();              // ... everyone's; and chunk ch-1's stage is free
-        if (ch + RL_ST - 1 < nch) load(ch + RL_ST - 1);
+        if (ch + RT_ST - 1 < nch) load(ch + RT_ST - 1);
         cp_async_commit();
-        const float *st = rsm + (size_t)(ch % RL_ST) * RL_STAGE;
+        const float *st = rsm + (size_t)(ch % RT_ST) * STAGE;
         if (xh && blockIdx.y == 0) {
-            // the f16 token operand of the expert GEMMs (row t of xh = x[t] rounded
-            // to f16, saturated): written from the staged chunk by the first
-            // column of blocks, 8 values per thread
-            const int r = threadIdx.x >> 4, c = (threadIdx.x & 15) * 8, k = ch * RL_CH + c;
-            if (t0 + r < T && k < D) {
-                const float *v = st + r * RL_LD + c;
-                uint4 o;
-                o.x = f32x2_to_f16x2_sat(v[0], v[1]);
-                o.y = f32x2_to_f16x2_sat(v[2], v[3]);
-                o.z = f32x2_to_f16x2_sat(v[4], v[5]);
-                o.w = f32x2_to_f16x2_sat(v[6], v[7]);
-                *reinterpret_cast<uint4 *>(xh + (size_t)(t0 + r) * D + k) = o;
+            // the f16 token operand of the expert GEMMs (row t of xh = x[t]
+            // rounded to f16, saturated), written by the first row of blocks
+            for (int i = tid; i < BT * (KC / 8); i += NT) {
+                const int r = i / (KC / 8), c = (i % (KC / 8)) * 8;
+                if (t0 + r < T && ch * KC + c < D) {
+                    const float *v = st + r * LD + c;
+                    uint4 o;
+                    o.x = f32x2_to_f16x2_sat(v[0], v[1]);
+                    o.y = f32x2_to_f16x2_sat(v[2], v[3]);
+                    o.z = f32x2_to_f16x2_sat(v[4], v[5]);
+                    o.w = f32x2_to_f16x2_sat(v[6], v[7]);
+                    *reinterpret_cast<uint4 *>(xh + (size_t)(t0 + r) * D + ch * KC + c) = o;
+                }
             }
         }
-        const float *xr = st + tok * RL_LD;
-        const float *w0 = st + (RL_TOK + rl) * RL_LD, *w1 = w0 + RL_LD;
-        const int clen = min(RL_CH, D - ch * RL_CH);     // a multiple of 4
-#pragma unroll 8
-        for (int c = 0; c < clen; c += 4) {
-            const float4 xv = *reinterpret_cast<const float4 *>(xr + c);
-            const float4 a = *reinterpret_cast<const float4 *>(w0 + c);
-            const float4 b = *reinterpret_cast<const float4 *>(w1 + c);
-            add2_rn(acc0, acc1, __fmul_rn(xv.x, a.x), __fmul_rn(xv.x, b.x));
-            add2_rn(acc0, acc1, __fmul_rn(xv.y, a.y), __fmul_rn(xv.y, b.y));
-            add2_rn(acc0, acc1, __fmul_rn(xv.z, a.z), __fmul_rn(xv.z, b.z));
-            add2_rn(acc0, acc1, __fmul_rn(xv.w, a.w), __fmul_rn(xv.w, b.w));
+#pragma unroll 2
+        for (int kk = 0; kk < KC; kk += 4) {
+            float4 xv[TT], wv[RR];
+#pragma unroll
+            for (int i = 0; i < TT; ++i) xv[i] = *reinterpret_cast<const float4 *>(st + (tg + G * i) * LD + kk);
+#pragma unroll
+            for (int j = 0; j < RR; ++j)
+                wv[j] = *reinterpret_cast<const float4 *>(st + (BT + rg + G * j) * LD + kk);
+#pragma unroll
+            for (int sk = 0; sk < 4; ++sk) {
+                const float *xs = reinterpret_cast<const float *>(xv);   // xv[i] component sk: xs[4i + sk]
+                const float *ws = reinterpret_cast<const float *>(wv);
+                if constexpr (RR >= 2) {
+#pragma unroll
+                    for (int i = 0; i < TT; ++i)
+#pragma unroll
+                        for (int j = 0; j < RR; j += 2) {
+                            const float2 p = make_float2(__fmul_rn(xs[4 * i + sk], ws[4 * j + sk]),
+                                                         __fmul_rn(xs[4 * i + sk], ws[4 * (j + 1) + sk]));
+                            const float2 r = add2_rn(make_float2(acc[i][j], acc[i][j + 1]), p);
+                            acc[i][j] = r.x;
+                            acc[i][j + 1] = r.y;
+                        }
+                } else if constexpr (TT >= 2) {
+#pragma unroll
+                    for (int i = 0; i < TT; i += 2) {
+                        const float2 p = make_float2(__fmul_rn(xs[4 * i + sk], ws[sk]),
+                                                     __fmul_rn(xs[4 * (i + 1) + sk], ws[sk]));
+                        const float2 r = add2_rn(make_float2(acc[i][0], acc[i + 1][0]), p);
+                        acc[i][0] = r.x;
+                        acc[i + 1][0] = r.y;
+                    }
+                } else {
+                    acc[0][0] = __fadd_rn(acc[0][0], __fmul_rn(xs[sk], ws[sk]));
+                }
+            }
         }
     }
-    const int t = t0 + tok, r0 = row0 + rl;
-    if (t < T) {
-        if (r0 < nrows) logits[(size_t)t * ldl + r0] = (Ws && r0 < E) ? __fmul_rn(acc0, Ws[r0]) : acc0;
-        if (r0 + 1 < nrows) logits[(size_t)t * ldl + r0 + 1] = (Ws && r0 + 1 < E) ? __fmul_rn(acc1, Ws[r0 + 1]) : acc1;
+#pragma unroll
+    for (int i = 0; i < TT; ++i) {
+        const int t = t0 + tg + G * i;
+        if (t >= T) continue;
+#pragma unroll
+        for (int j = 0; j < RR; ++j) {
+            const int r = r0 + rg + G * j;
+            if (r < nrows) logits[(size_t)t * ldl + r] = (Ws && r < E) ? __fmul_rn(acc[i][j], Ws[r]) : acc[i][j];
+        }
     }
 }
 
@@ -221,19 +261,69 @@ __global__ void __launch_bounds__(SEL_WARPS * 32) router_select_kernel(const flo
     omc_plan_block(plan, topk_idx, topk_w, err, reinterpret_cast<int *>(sbuf));
 }
 
+template <int G, int TT, int RR, int KC>
+int launch_tile(const omc_layer_dev *L, const float *x, int T, int nrows, float *logits, int ldl, uint16_t *xh,
+                cudaStream_t s) {
+    static int attr_done = 0;
+    if (!attr_done) {
+        if (cudaFuncSetAttribute(router_tile_kernel<G, TT, RR, KC>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)rt_smem<G, TT, RR, KC>()) != cudaSuccess)
+            return OMC_ECUDA;
+        attr_done = 1;
+    }
+    const dim3 g((T + G * TT - 1) / (G * TT), (nrows + G * RR - 1) / (G * RR));
+    router_tile_kernel<G, TT, RR, KC><<<g, G * G, rt_smem<G, TT, RR, KC>(), s>>>(
+        x, T, L->D, L->router, L->router_i8 ? L->router_s : nullptr, L->E, L->sh_gate, nrows, logits, ldl, xh);
+    return 0;
+}
+
+// Test hook: a forced tile (G, TT, RR), 0 = automatic.
+int g_force_tile = 0;
+
+// The largest tile whose blocks still cover every SM (smaller T: smaller tiles).
+int launch_logits(const omc_layer_dev *L, const float *x, int T, int nrows, float *logits, int ldl, uint16_t *xh,
+                  cudaStream_t s) {
+    static int nsm = 0;
+    if (!nsm) {
+        int dev = 0;
+        if (cudaGetDevice(&dev) != cudaSuccess ||
+            cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+            return OMC_ECUDA;
+    }
+    auto blocks = [&](int g, int tt, int rr) {
+        return (long long)((T + g * tt - 1) / (g * tt)) * ((nrows + g * rr - 1) / (g * rr));
+    };
+    const long long want = nsm;
+    switch (g_force_tile) {
+    case 1644: return launch_tile<16, 4, 4, 32>(L, x, T, nrows, logits, ldl, xh, s);
+    case 1622: return launch_tile<16, 2, 2, 64>(L, x, T, nrows, logits, ldl, xh, s);
+    case 1611: return launch_tile<16, 1, 1, 128>(L, x, T, nrows, logits, ldl, xh, s);
+    case 811: return launch_tile<8, 1, 1, 128>(L, x, T, nrows, logits, ldl, xh, s);
+    default: break;
+    }
+    // Measured on B200 (logits stage, OLMoE T=512 and Qwen T=2048): 2 x 2 chains
+    // per thread beat 4 x 4 and 2 x 4 once the grid fills the SMs; below that,
+    // one chain per thread on 16 x 16 threads beat the 8 x 8-thread tiles.
+    if (blocks(16, 2, 2) >= want) return launch_tile<16, 2, 2, 64>(L, x, T, nrows, logits, ldl, xh, s);
+    return launch_tile<16, 1, 1, 128>(L, x, T, nrows, logits, ldl, xh, s);
+}
+
 }  // namespace
+
+// Forces the router's logits tile for tests (g, tt, rr as one of 16x4x4,
+// 16x2x2, 16x1x1, 8x1x1); 0,0,0 = automatic.
+extern "C" int omc_debug_router_tile(int g, int tt, int rr) {
+    const int code = g * 100 + tt * 10 + rr;
+    if (code != 0 && code != 1644 && code != 1622 && code != 1611 && code != 811) return OMC_EINVAL;
+    g_force_tile = code;
+    return 0;
+}
 
 extern "C" int omc_launch_router(const omc_layer_dev *L, const float *x, int T, const omc_ws *ws,
                                  int32_t *topk_idx, float *topk_w, const omc_plan_args *plan, cudaStream_t s) {
     if (T <= 0) return 0;
     if (L->E > OMC_MAX_E || L->k > OMC_MAX_K || (L->D & 3)) return OMC_EINVAL;
-    static int attr_done = 0, attr_small = 0;
-    if (!attr_done) {
-        if (cudaFuncSetAttribute(router_logits_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)RL_SMEM) !=
-            cudaSuccess)
-            return OMC_ECUDA;
-        attr_done = 1;
-    }
+    static int attr_small = 0;
     const int nrows = L->E + (L->has_shared ? 1 : 0);
     const int ldl = L->E + 1;
     const size_t small_smem = (size_t)(T + RS_ROWS) * (L->D + 4) * sizeof(float);
@@ -247,10 +337,8 @@ extern "C" int omc_launch_router(const omc_layer_dev *L, const float *x, int T, 
         router_logits_small_kernel<<<(nrows + RS_ROWS - 1) / RS_ROWS, 256, small_smem, s>>>(
             x, T, L->D, L->router, L->router_i8 ? L->router_s : nullptr, L->E, L->sh_gate, nrows, ws->logits, ldl);
     } else {
-        const dim3 g1((T + RL_TOK - 1) / RL_TOK, (nrows + RL_ROWS - 1) / RL_ROWS);
-        router_logits_kernel<<<g1, RL_THREADS, RL_SMEM, s>>>(x, T, L->D, L->router, L->router_i8 ? L->router_s : nullptr,
-                                                             L->E, L->sh_gate, nrows, ws->logits, ldl,
-                                                             plan ? ws->xh : nullptr, ws->err);
+        const int rc = launch_logits(L, x, T, nrows, ws->logits, ldl, plan ? ws->xh : nullptr, s);
+        if (rc) return rc;
     }
     omc_prof_mark(s, "router_logits");
     const int nv = (L->E + 31) / 32;

@@ -71,3 +71,23 @@ def test_routing_ties_many(gpu, oracle):
     ridx, rw = oracle.oracle_route(L, x)
     assert np.array_equal(idx, ridx)
     assert np.array_equal(w.view(np.uint32), rw.view(np.uint32))
+
+
+@pytest.mark.parametrize("tile", [(16, 4, 4), (16, 2, 2), (16, 1, 1), (8, 1, 1)])
+@pytest.mark.parametrize("kind,T", [("olmoe", 96), ("qwen", 70)])
+def test_every_logits_tile_bitexact(gpu, oracle, tile, kind, T):
+    """Each register tile of the logits kernel (the launch picks one by T x E)
+    keeps every chain's order: routing equal to the oracle's with `==`.  T is
+    a multiple of no tile, so the token tail is exercised too; Qwen adds the
+    int8 router and the shared-gate row."""
+    L = olmoe_full() if kind == "olmoe" else qwen_full()
+    m = gpu.MoELayer.from_oracle_layer(next_layer_id(), L)
+    x = oracle.normal(9500 + T, (T, L.D))
+    gpu.set_router_tile(*tile)
+    try:
+        _, idx, w = m.forward(x)
+    finally:
+        gpu.set_router_tile()
+    ridx, rw = oracle.oracle_route(L, x)
+    assert np.array_equal(idx, ridx)
+    assert np.array_equal(w.view(np.uint32), rw.view(np.uint32))
