@@ -55,9 +55,12 @@ CONFIG = {"workload": WORKLOAD, "D": D, "I": I, "E": E, "k": K, "T": T,
 #   olmoe_prefill  OLMoE-shaped layer, T=512 (C1)        olmoe_decode  the same, T=1
 #   qwen_prefill   Qwen-shaped layer with shared expert, int8 router, T=2048 (C2)
 #   qwen_decode    the same, T=1 (C2 decode)
+#   olmoe_decode64 / qwen_decode64   one decode step of 64 sequences (T=64), the batched
+#                  decode of the next-steps row; run it with --graph (CUDA graph replay)
 WORKLOADS = {
     "olmoe_prefill": ("olmoe", 512), "olmoe_decode": ("olmoe", 1),
     "qwen_prefill": ("qwen", 2048), "qwen_decode": ("qwen", 1),
+    "olmoe_decode64": ("olmoe", 64), "qwen_decode64": ("qwen", 64),
 }
 
 
@@ -71,7 +74,8 @@ def set_workload(name, tokens=None):
     else:
         D, I, E, K, IS, SEED_W = 2048, 512, 256, 8, 512, 2
     EXPERT_BYTES = 3 * D * I + 4 * (2 * I + D)
-    WORKLOAD = f"{FAMILY}_layer_{'prefill' if T > 1 else 'decode'}_T{T}"
+    kind = "decode" if (T == 1 or "decode" in name) else "prefill"
+    WORKLOAD = f"{FAMILY}_layer_{kind}_T{T}"
     total = E * EXPERT_BYTES + (3 * D * IS + 4 * (2 * IS + D) if IS else 0)
     CONFIG = {"workload": WORKLOAD, "D": D, "I": I, "E": E, "k": K, "T": T,
               "weights": f"int8 per-row + f32 scales, N(0,0.02) seed {SEED_W}",
@@ -351,19 +355,43 @@ def run_ours(args):
     dom = ("gemm_gateup" if "gemm_gateup" in stages else
            "decode_moe" if "decode_moe" in stages else "gemv_gateup")
 
+    graph = None
+    if args.graph:
+        # one captured forward per input buffer; the timed region replays the graph
+        ob.launch_count(reset=True)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            for i in range(nbuf):
+                step(i)
+        graph_launches = ob.launch_count()
+        graph.replay()
+        torch.cuda.synchronize()
+        args.steps = max(1, args.steps // nbuf) * nbuf
+
     barrier()
     clk = ClockSampler(dev)
     clk.start()
     ob.launch_count(reset=True)
-    ob.time_stage(dom)          # one event pair around `dom` per step, on the launching stream
+    if graph is None:
+        ob.time_stage(dom)      # one event pair around `dom` per step, on the launching stream
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
-    for i in range(args.steps):
-        step(i)
+    if graph is None:
+        for i in range(args.steps):
+            step(i)
+    else:
+        for _ in range(args.steps // nbuf):
+            graph.replay()
     e1.record(stream)
     barrier()
-    launches = ob.launch_count()
+    launches = ob.launch_count() if graph is None else graph_launches * (args.steps // nbuf)
     clocks = clk.stop()
+    if graph is not None:
+        # the dominant kernel's launch time, from a short pass outside the graph
+        ob.time_stage(dom)
+        for i in range(max(16, args.steps // 8)):
+            step(i)
+        torch.cuda.synchronize()
     dom_ms, dom_n = ob.stage_timer()
     ob.time_stage(None)
     ob.sync()
@@ -446,6 +474,7 @@ def run_ours(args):
             "scaling": "weak", "vs_baseline": None, "dtype": "f16xint8->f32",
             "data": "synthetic",
             "config": dict(CONFIG, parallelism=(f"ep{world}" if ep_mode else f"replica{world}"),
+                           launch=("cuda_graph" if graph is not None else "stream"),
                            tokens_per_rank=T),
             "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": T * D * 4,
                     "d2h_bytes_per_step": T * D * 4 + T * K * 8},
@@ -484,6 +513,8 @@ def main():
     ap.add_argument("--workload", default="olmoe_prefill", choices=sorted(WORKLOADS),
                     help="olmoe_prefill (BASELINE configs[1], the default line), olmoe_decode, "
                          "qwen_prefill, qwen_decode")
+    ap.add_argument("--graph", action="store_true",
+                    help="capture one forward per input buffer in a CUDA graph and time graph replays")
     ap.add_argument("--tokens", type=int, default=None,
                     help="tokens per rank instead of the workload's T (the T sweep of the prefill rows)")
     ap.add_argument("--mode", default="replica", choices=["ep", "replica"],
