@@ -8,6 +8,8 @@
  * Reference interfaces this header replaces:
  *   - moe()       engines/olmoe.c:344-402  (router + top-k + experts + combine)
  *   - moe_step()  engines/qwen.c:453-495   (shared expert + router + experts)
+ *   - route_token() + the expert union of step_batch()
+ *                 engines/gemma.c:455-478, :580-685 (GEMMA family)
  *   - the GPU seam metal/om_metal.h:14-46 (omm_*), whose prototypes are
  *     mirrored one-for-one by om_metal.h in this directory.
  *
@@ -48,9 +50,18 @@ extern "C" {
  *          g/(1+exp(-g)) (olmoe.c:393), out = sum_k w_k*y_k (olmoe.c:395-397)
  *   QWEN : softmax_ double sum (engines/qwen.c:161-165), silu as
  *          g*sigmoid(g) (qwen.c:158-159), renormalised top-k, out =
- *          sigmoid(sh_gate.x)*shared(x) + sum_k w_k*y_k (qwen.c:455-492) */
+ *          sigmoid(sh_gate.x)*shared(x) + sum_k w_k*y_k (qwen.c:455-492)
+ *   GEMMA: x is the RESIDUAL row (engines/gemma.c:582).  The router reads
+ *          rms(x)*router.scale*D^-0.5 and the experts rms(x)*
+ *          pre_feedforward_layernorm_2 (gemma.c:458-460, :608); top-k over
+ *          the softmax numerators, renormalised, times per_expert_scale
+ *          (gemma.c:461-477); experts gelu_tanh(g)*u (gemma.c:319-321,
+ *          :671); no shared expert.  Needs omc_layer_gemma_norms().
+ *          out = sum_k w_k*y_k, the MoE term before post_feedforward_
+ *          layernorm_2 (gemma.c:691). */
 #define OMC_FAMILY_OLMOE 0
 #define OMC_FAMILY_QWEN  1
+#define OMC_FAMILY_GEMMA 2
 
 #define OMC_ROUTER_F32 0    /* router weights f32 [E,D]                       */
 #define OMC_ROUTER_I8  1    /* int8 [E,D] + f32 scale [E] (qwen.c:284 stream)  */
@@ -58,10 +69,10 @@ extern "C" {
 typedef struct omc_moe_desc {
     int family;        /* OMC_FAMILY_*                                          */
     int D;             /* hidden size (multiple of 64)                          */
-    int I;             /* routed-expert FFN width (multiple of 64)              */
+    int I;             /* routed-expert FFN width (multiple of 16)              */
     int E;             /* routed experts (<= 1024)                              */
     int k;             /* experts per token (<= 32)                             */
-    int renorm;        /* 1: top-k weights divided by their sum (forced for QWEN) */
+    int renorm;        /* 1: top-k weights divided by their sum (forced for QWEN, GEMMA) */
     int router_dtype;  /* OMC_ROUTER_*                                          */
     int has_shared;    /* 1: always-on shared expert behind a sigmoid gate (QWEN) */
     int Is;            /* shared-expert FFN width (multiple of 64)               */
@@ -83,6 +94,17 @@ void omc_shutdown(void);
 int omc_layer_init(int layer, const omc_moe_desc *desc,
                    const void *router_w, const float *router_s);
 
+/* GEMMA layers: the router's norm parameters and the experts' input norm
+ * (engines/gemma.c:409, :423-424): router_scale [D] (router.scale),
+ * per_expert_scale [E] (router.per_expert_scale), expert_norm [D]
+ * (pre_feedforward_layernorm_2 weight; NULL = ones) and eps
+ * (rms_norm_eps).  Call after omc_layer_init, before the first forward.
+ * The router's rms factor (mean(x^2)+eps)^-0.5 is the correctly rounded
+ * value; the reference's libm powf is up to 1 ulp from it (0.06% of rows on
+ * glibc), which moves those rows' top-k weights by a few ulps. */
+int omc_layer_gemma_norms(int layer, float eps, const float *router_scale, const float *per_expert_scale,
+                          const float *expert_norm);
+
 /* Upload routed expert e of a layer into the HBM slab (re-tiled for the
  * kernels).  Row-major int8 container tensors as written by the converters
  * (tools/convert_olmoe.py:93-99): g,u [I,D], d [D,I], per-row f32 scales
@@ -97,6 +119,10 @@ int omc_expert_set(int layer, int e,
 int omc_experts_set_packed(int layer,
                            const int8_t *g, const float *gs, const int8_t *u, const float *us,
                            const int8_t *d, const float *ds);
+
+/* GEMMA's container keeps gate and up fused (gate_up_proj int8 [2I,D] with
+ * .qs [2I], engines/gemma.c:342-361): pass g = gate_up, u = gate_up + I*D,
+ * gs = qs, us = qs + I. */
 
 /* QWEN shared expert: g,u int8 [Is,D], d int8 [D,Is], their row scales, and
  * the f32 gate vector sh_gate [D] (engines/qwen.c:279-287). */

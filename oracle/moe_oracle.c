@@ -84,9 +84,81 @@ static float ref_siluf(float z) { return z * ref_sigmoidf(z); }
 
 static int desc_ok(const orc_desc *d) {
     if (!d || d->D <= 0 || d->I <= 0 || d->E <= 0 || d->k <= 0 || d->k > d->E || d->k > 64) return 0;
-    if (d->family != ORC_FAMILY_OLMOE && d->family != ORC_FAMILY_QWEN) return 0;
+    if (d->family != ORC_FAMILY_OLMOE && d->family != ORC_FAMILY_QWEN && d->family != ORC_FAMILY_GEMMA) return 0;
     if (d->has_shared && (d->family != ORC_FAMILY_QWEN || d->Is <= 0)) return 0;
     return 1;
+}
+
+static int gemma_ok(const orc_desc *d, const orc_weights *w) {
+    return d->family != ORC_FAMILY_GEMMA || (w->g_rscale && w->g_pes);
+}
+
+/* ---- gemma ---------------------------------------------------------- */
+
+/* engines/gemma.c:313-317 rmsnorm's factor: double running sum of x^2,
+ * (float)(ms/n) + eps, then powf(., -0.5f) (ORC_RSQRT_LIBM) or the double
+ * 1/sqrt rounded once to float (ORC_RSQRT_CR). */
+static float gemma_norm_factor(const orc_desc *d, const float *x) {
+    double ms = 0;
+    for (int i = 0; i < d->D; i++) ms += (double)x[i] * x[i];
+    const float y = (float)(ms / d->D) + d->eps;
+    if (d->rsqrt_mode == ORC_RSQRT_LIBM) return powf(y, -0.5f);
+    return (float)(1.0 / sqrt((double)y));
+}
+
+/* engines/gemma.c:458-460 (router input: rmsnorm without weight, then
+ * *= router.scale[i] * D^-0.5) and :608 (expert input: rmsnorm with
+ * pre_feedforward_layernorm_2).  rmsnorm writes x[i]*r*w[i] left to right,
+ * with w[i] = 1.f when there is no weight. */
+static void gemma_inputs(const orc_desc *d, const orc_weights *w, const float *x, float *xr, float *xe,
+                         float *rout) {
+    const float r = gemma_norm_factor(d, x);
+    const float rroot = 1.f / sqrtf((float)d->D);
+    for (int i = 0; i < d->D; i++) {
+        const float n = x[i] * r;
+        if (xr) xr[i] = (n * 1.f) * (w->g_rscale[i] * rroot);
+        if (xe) xe[i] = n * (w->g_enorm ? w->g_enorm[i] : 1.f);
+    }
+    if (rout) *rout = r;
+}
+
+/* engines/gemma.c:319-321 */
+static float ref_gelu_tanh(float x) {
+    return 0.5f * x * (1.f + tanhf(0.7978845608028654f * (x + 0.044715f * x * x * x)));
+}
+
+/* engines/gemma.c:461-477: router logits of the pre-scaled input, e_i =
+ * expf(l_i - max) with a float running sum, top-k over the e_i (strict '>'
+ * from -1, so ties keep the lower id), w_k = e_k/sum renormalised by the
+ * float sum of those quotients in selection order, times per_expert_scale. */
+static void gemma_route(const orc_desc *d, const orc_weights *w, const float *xr, float *pr, int *idx, float *val) {
+    const int E = d->E, K = d->k;
+    if (d->router_i8) ref_matmul_q(pr, xr, (const int8_t *)w->router, w->router_s, d->D, E);
+    else              ref_matvec_f32(pr, xr, (const float *)w->router, d->D, E);
+    float pmx = -1e30f;
+    for (int e = 0; e < E; e++) if (pr[e] > pmx) pmx = pr[e];
+    float psum = 0.f;
+    for (int e = 0; e < E; e++) { pr[e] = expf(pr[e] - pmx); psum += pr[e]; }
+    float wsum = 0.f;
+    for (int kk = 0; kk < K; kk++) {
+        int best = -1; float bv = -1.f;
+        for (int e = 0; e < E; e++) {
+            int taken = 0;
+            for (int j = 0; j < kk; j++) if (idx[j] == e) taken = 1;
+            if (!taken && pr[e] > bv) { bv = pr[e]; best = e; }
+        }
+        idx[kk] = best; val[kk] = bv / psum; wsum += bv / psum;
+    }
+    for (int kk = 0; kk < K; kk++) val[kk] = val[kk] / wsum * w->g_pes[idx[kk]];
+}
+
+int orc_gemma_prenorm(const orc_desc *d, const orc_weights *w, const float *x, int T, float *xr, float *xe,
+                      float *r) {
+    if (!desc_ok(d) || d->family != ORC_FAMILY_GEMMA || !gemma_ok(d, w) || T < 0) return -1;
+    for (int t = 0; t < T; t++)
+        gemma_inputs(d, w, x + (int64_t)t * d->D, xr ? xr + (int64_t)t * d->D : NULL,
+                     xe ? xe + (int64_t)t * d->D : NULL, r ? r + t : NULL);
+    return 0;
 }
 
 /* Routes one token: logits -> softmax -> top-k -> renorm.
@@ -94,6 +166,13 @@ static int desc_ok(const orc_desc *d) {
  * qwen : engines/qwen.c:465-477 (DM router, softmax_, top-k, renorm) */
 static void route_one(const orc_desc *d, const orc_weights *w, const float *xs, float *pr,
                       int *idx, float *val) {
+    if (d->family == ORC_FAMILY_GEMMA) {
+        float *xr = malloc(sizeof(float) * d->D);
+        gemma_inputs(d, w, xs, xr, NULL, NULL);
+        gemma_route(d, w, xr, pr, idx, val);
+        free(xr);
+        return;
+    }
     if (d->router_i8) ref_matmul_q(pr, xs, (const int8_t *)w->router, w->router_s, d->D, d->E);
     else              ref_matvec_f32(pr, xs, (const float *)w->router, d->D, d->E);
     if (d->family == ORC_FAMILY_QWEN) ref_softmax_f64sum(pr, d->E);
@@ -104,7 +183,7 @@ static void route_one(const orc_desc *d, const orc_weights *w, const float *xs, 
 
 int orc_route(const orc_desc *d, const orc_weights *w, const float *x, int T,
               int32_t *topk_idx, float *topk_w) {
-    if (!desc_ok(d) || T < 0) return -1;
+    if (!desc_ok(d) || !gemma_ok(d, w) || T < 0) return -1;
     #pragma omp parallel
     {
         float *pr = malloc(sizeof(float) * d->E);
@@ -127,16 +206,44 @@ int orc_route(const orc_desc *d, const orc_weights *w, const float *x, int T,
 /* Tokens are independent in the reference (every buffer below is per token),
  * so they are spread over OpenMP threads; each token's arithmetic is the
  * reference's, in the reference's order. */
+/* One routed expert e on one input row: g,u = int8 GEMVs, the family's
+ * activation, then the down GEMV into y.
+ * olmoe: engines/olmoe.c:386-394 (g/(1+exp(-g))*u)
+ * qwen : engines/qwen.c:480-491 (silu(g)*u)
+ * gemma: engines/gemma.c:667-672 (gelu_tanh(g)*u; gate_up rows [0,mi) and
+ *        [mi,2mi) are the g and u matrices here) */
+static int family_act(const orc_desc *d) { return d->family; }   /* ORC_ACT_* equals the family */
+
+static void expert_apply(const orc_desc *d, const orc_weights *w, int act, int e, const float *xs, float *g, float *u,
+                         float *y) {
+    const int D = d->D, I = d->I;
+    const int8_t *qg = w->g + (int64_t)e * I * D, *qu = w->u + (int64_t)e * I * D;
+    const int8_t *qd = w->d + (int64_t)e * D * I;
+    ref_matmul_q(g, xs, qg, w->gs + (int64_t)e * I, D, I);
+    ref_matmul_q(u, xs, qu, w->us + (int64_t)e * I, D, I);
+    if (act == ORC_ACT_SILU_SIG) {
+        for (int i = 0; i < I; i++) g[i] = ref_siluf(g[i]) * u[i];          /* qwen.c:485 */
+    } else if (act == ORC_ACT_GELU_TANH) {
+        for (int i = 0; i < I; i++) g[i] = ref_gelu_tanh(g[i]) * u[i];      /* gemma.c:671 */
+    } else {
+        for (int i = 0; i < I; i++) { float gv = g[i]; g[i] = (gv / (1.f + expf(-gv))) * u[i]; } /* olmoe.c:393 */
+    }
+    ref_matmul_q(y, g, qd, w->ds + (int64_t)e * D, I, D);
+}
+
+/* Tokens are independent in the reference (every buffer below is per token),
+ * so they are spread over OpenMP threads; each token's arithmetic is the
+ * reference's, in the reference's order. */
 int orc_moe(const orc_desc *d, const orc_weights *w, const float *x, int T,
             float *out, int32_t *topk_idx, float *topk_w) {
-    if (!desc_ok(d) || T < 0) return -1;
+    if (!desc_ok(d) || !gemma_ok(d, w) || T < 0) return -1;
     const int D = d->D, I = d->I, E = d->E, K = d->k;
     const int Wmax = (d->has_shared && d->Is > I) ? d->Is : I;
     #pragma omp parallel
     {
         float *pr = malloc(sizeof(float) * E);
         float *g = malloc(sizeof(float) * Wmax), *u = malloc(sizeof(float) * Wmax);
-        float *hh = malloc(sizeof(float) * D);
+        float *hh = malloc(sizeof(float) * D), *xe = malloc(sizeof(float) * D);
         int idx[64]; float val[64];
         #pragma omp for schedule(dynamic, 1)
         for (int s = 0; s < T; s++) {
@@ -154,28 +261,33 @@ int orc_moe(const orc_desc *d, const orc_weights *w, const float *x, int T,
                 sg = ref_sigmoidf(sg);
                 for (int i = 0; i < D; i++) os[i] *= sg;
             } else {
-                memset(os, 0, sizeof(float) * D);        /* engines/olmoe.c:348 */
+                memset(os, 0, sizeof(float) * D);        /* engines/olmoe.c:348, gemma.c:610 */
             }
             route_one(d, w, xs, pr, idx, val);
             for (int kk = 0; kk < K; kk++) {
-                const int e = idx[kk];
-                const int8_t *qg = w->g + (int64_t)e * I * D, *qu = w->u + (int64_t)e * I * D;
-                const int8_t *qd = w->d + (int64_t)e * D * I;
-                ref_matmul_q(g, xs, qg, w->gs + (int64_t)e * I, D, I);
-                ref_matmul_q(u, xs, qu, w->us + (int64_t)e * I, D, I);
-                if (d->family == ORC_FAMILY_QWEN) {
-                    for (int i = 0; i < I; i++) g[i] = ref_siluf(g[i]) * u[i];          /* qwen.c:485 */
-                } else {
-                    for (int i = 0; i < I; i++) { float gv = g[i]; g[i] = (gv / (1.f + expf(-gv))) * u[i]; } /* olmoe.c:393 */
-                }
-                ref_matmul_q(hh, g, qd, w->ds + (int64_t)e * D, I, D);
+                if (topk_idx) topk_idx[(int64_t)s * K + kk] = idx[kk];
+                if (topk_w)   topk_w[(int64_t)s * K + kk] = val[kk];
+            }
+            if (d->family == ORC_FAMILY_GEMMA) {
+                /* gemma.c:608 expert input; hits combined in ascending expert
+                 * id (the union loop over e, gemma.c:641-659, reduced in hit
+                 * order at :680-685) */
+                gemma_inputs(d, w, xs, NULL, xe, NULL);
+                for (int e = 0; e < E; e++)
+                    for (int kk = 0; kk < K; kk++) {
+                        if (idx[kk] != e) continue;
+                        expert_apply(d, w, family_act(d), e, xe, g, u, hh);
+                        for (int i = 0; i < D; i++) os[i] += val[kk] * hh[i];
+                    }
+                continue;
+            }
+            for (int kk = 0; kk < K; kk++) {
+                expert_apply(d, w, family_act(d), idx[kk], xs, g, u, hh);
                 const float wk = val[kk];
                 for (int i = 0; i < D; i++) os[i] += wk * hh[i];   /* olmoe.c:395-397, qwen.c:492 */
-                if (topk_idx) topk_idx[(int64_t)s * K + kk] = e;
-                if (topk_w)   topk_w[(int64_t)s * K + kk] = wk;
             }
         }
-        free(pr); free(g); free(u); free(hh);
+        free(pr); free(g); free(u); free(hh); free(xe);
     }
     return 0;
 }
@@ -193,7 +305,7 @@ int orc_shared_gate(const orc_desc *d, const orc_weights *w, const float *x, int
 
 int orc_expert_rows(const orc_desc *d, const orc_weights *w, const float *x, int R, const int32_t *ids,
                     float *y) {
-    if (!desc_ok(d) || R < 0) return -1;
+    if (!desc_ok(d) || !gemma_ok(d, w) || R < 0) return -1;
     for (int r = 0; r < R; r++)
         if (ids[r] < 0 || ids[r] > d->E || (ids[r] == d->E && !d->has_shared)) return -1;
     const int D = d->D, I = d->I, E = d->E;
@@ -201,6 +313,7 @@ int orc_expert_rows(const orc_desc *d, const orc_weights *w, const float *x, int
     #pragma omp parallel
     {
         float *g = malloc(sizeof(float) * Wmax), *u = malloc(sizeof(float) * Wmax);
+        float *xe = malloc(sizeof(float) * D);
         #pragma omp for schedule(dynamic, 1)
         for (int r = 0; r < R; r++) {
             const float *xs = x + (int64_t)r * D;
@@ -215,17 +328,28 @@ int orc_expert_rows(const orc_desc *d, const orc_weights *w, const float *x, int
                 ref_matmul_q(ys, g, w->sh_d, w->sh_ds, SI, D);
                 continue;
             }
-            const int8_t *qg = w->g + (int64_t)e * I * D, *qu = w->u + (int64_t)e * I * D;
-            const int8_t *qd = w->d + (int64_t)e * D * I;
-            ref_matmul_q(g, xs, qg, w->gs + (int64_t)e * I, D, I);
-            ref_matmul_q(u, xs, qu, w->us + (int64_t)e * I, D, I);
-            if (d->family == ORC_FAMILY_QWEN) {
-                for (int i = 0; i < I; i++) g[i] = ref_siluf(g[i]) * u[i];          /* qwen.c:485 */
-            } else {
-                for (int i = 0; i < I; i++) { float gv = g[i]; g[i] = (gv / (1.f + expf(-gv))) * u[i]; } /* olmoe.c:393 */
+            if (d->family == ORC_FAMILY_GEMMA) {     /* rows are residual rows: gemma.c:608 first */
+                gemma_inputs(d, w, xs, NULL, xe, NULL);
+                xs = xe;
             }
-            ref_matmul_q(ys, g, qd, w->ds + (int64_t)e * D, I, D);
+            expert_apply(d, w, family_act(d), e, xs, g, u, ys);
         }
+        free(g); free(u); free(xe);
+    }
+    return 0;
+}
+
+int orc_expert_rows_act(const orc_desc *d, const orc_weights *w, const float *x, int R, const int32_t *ids, int act,
+                        float *y) {
+    if (!desc_ok(d) || R < 0 || act < ORC_ACT_SILU_DIV || act > ORC_ACT_GELU_TANH) return -1;
+    for (int r = 0; r < R; r++)
+        if (ids[r] < 0 || ids[r] >= d->E) return -1;
+    #pragma omp parallel
+    {
+        float *g = malloc(sizeof(float) * d->I), *u = malloc(sizeof(float) * d->I);
+        #pragma omp for schedule(dynamic, 1)
+        for (int r = 0; r < R; r++)
+            expert_apply(d, w, act, ids[r], x + (int64_t)r * d->D, g, u, y + (int64_t)r * d->D);
         free(g); free(u);
     }
     return 0;

@@ -8,6 +8,9 @@
  *   - OLMoE  moe()       engines/olmoe.c:344-402
  *   - Qwen   moe_step()  engines/qwen.c:453-495   (stream mode: int8 router,
  *                                                  int8 shared expert)
+ *   - Gemma  route_token() engines/gemma.c:455-478 and the expert union of
+ *                         step_batch() engines/gemma.c:606-685 (CPU path,
+ *                         int8 stream-mode experts)
  * in the same floating-point order (sequential fp32 sums, no FMA
  * contraction, glibc expf), so that on identical inputs its outputs are
  * bit-identical to the reference built with gcc -O3 on x86-64.  That
@@ -24,7 +27,15 @@ extern "C" {
 
 /* Model family: fixes the reference's arithmetic for routing, the SwiGLU
  * form and the combine order.  Same values as OMC_FAMILY_* in om_cuda.h. */
-enum { ORC_FAMILY_OLMOE = 0, ORC_FAMILY_QWEN = 1 };
+enum { ORC_FAMILY_OLMOE = 0, ORC_FAMILY_QWEN = 1, ORC_FAMILY_GEMMA = 2 };
+
+/* Gemma's router norm takes (mean(x^2) + eps)^-0.5 with powf
+ * (engines/gemma.c:313-317).  libm's powf is not correctly rounded: glibc
+ * 2.39 on x86-64 is 1 ulp off the correctly rounded value for 207,500 of the
+ * 335,544,321 floats in [2^-20, 2^20].  ORC_RSQRT_LIBM calls powf (the
+ * reference on this host, bit for bit); ORC_RSQRT_CR rounds the double
+ * 1/sqrt once to float, the value the device computes. */
+enum { ORC_RSQRT_CR = 0, ORC_RSQRT_LIBM = 1 };
 
 typedef struct {
     int family;        /* ORC_FAMILY_* */
@@ -33,6 +44,8 @@ typedef struct {
     int router_i8;     /* 0: f32 router [E,D] (olmoe.c:74-85); 1: int8 [E,D] + f32 scale[E] (qwen.c:284,465) */
     int has_shared;    /* qwen shared expert (qwen.c:455-462) */
     int Is;            /* shared expert FFN width */
+    float eps;         /* gemma: rms_norm_eps (gemma.c:94) */
+    int rsqrt_mode;    /* gemma: ORC_RSQRT_* */
 } orc_desc;
 
 /* Expert weights, packed expert-major (the int8 container layout of
@@ -47,7 +60,17 @@ typedef struct {
     const float  *gs, *us, *ds;
     const int8_t *sh_g, *sh_u, *sh_d;
     const float  *sh_gs, *sh_us, *sh_ds, *sh_gate;
+    /* gemma (gemma.c:422-424, :608): router.scale [D], router.per_expert_scale
+     * [E], pre_feedforward_layernorm_2 [D] (nullable: ones) */
+    const float  *g_rscale, *g_pes, *g_enorm;
 } orc_weights;
+
+/* For the GEMMA family, x is the layer's residual stream (the row
+ * route_token reads, gemma.c:582): the router input is
+ * rms(x) * router.scale * D^-0.5 and the experts' input rms(x) *
+ * pre_feedforward_layernorm_2, both computed here (and on the device).  The
+ * experts are gelu_tanh(g) * u (gemma.c:319-321, :671), and a token's hits are
+ * combined in ascending expert id (the union order of gemma.c:641-685). */
 
 /* out[T,D] = MoE(x[T,D]).  topk_idx/topk_w [T,k] (nullable) receive the
  * routing in selection order.  Returns 0, or -1 on a bad descriptor. */
@@ -62,6 +85,21 @@ int orc_moe(const orc_desc *dsc, const orc_weights *w, const float *x, int T,
  * -1 on a bad descriptor or id.  (Expert-parallel tests sum these rows.) */
 int orc_expert_rows(const orc_desc *dsc, const orc_weights *w, const float *x, int R, const int32_t *ids,
                     float *y);
+
+/* GEMMA: the router input xr and the expert input xe [T,D] of residual rows x,
+ * and the norm factor r [T] (engines/gemma.c:313-317, :458-460, :608). */
+int orc_gemma_prenorm(const orc_desc *dsc, const orc_weights *w, const float *x, int T,
+                      float *xr, float *xe, float *r);
+
+/* Expert activations (h = act(g) * u); ORC_ACT_x equals the family whose
+ * form it is: olmoe.c:393, qwen.c:158,485, gemma.c:319-321,671. */
+enum { ORC_ACT_SILU_DIV = 0, ORC_ACT_SILU_SIG = 1, ORC_ACT_GELU_TANH = 2 };
+
+/* Like orc_expert_rows for routed experts, with the activation given and the
+ * rows taken as the experts' input as they are (no GEMMA norm): the
+ * omm_moe_act job pass (metal/om_metal.h:49-51, `gelu` selects gelu_tanh). */
+int orc_expert_rows_act(const orc_desc *dsc, const orc_weights *w, const float *x, int R, const int32_t *ids,
+                        int act, float *y);
 
 /* sg[t] = sigmoid(sum_i sh_gate[i] * x[t][i]) (engines/qwen.c:460-461). */
 int orc_shared_gate(const orc_desc *dsc, const orc_weights *w, const float *x, int T, float *sg);

@@ -7,10 +7,12 @@ baseline.  The product library (``overhang_b200/libomc.so``) never loads it.
 Two checkers live here:
 
 * ``liboracle.so``: the C restatement in ``moe_oracle.c`` (always built);
-* ``_ref/libref_olmoe.so`` / ``_ref/libref_qwen.so``: the reference engines'
-  own ``moe()`` (engines/olmoe.c:344-402) and ``moe_step()``
-  (engines/qwen.c:453-495), compiled from the reference sources by
-  ``oracle/Makefile`` (present wherever they were built and shipped).
+* ``_ref/libref_olmoe.so`` / ``_ref/libref_qwen.so`` / ``_ref/libref_gemma.so``:
+  the reference engines' own ``moe()`` (engines/olmoe.c:344-402),
+  ``moe_step()`` (engines/qwen.c:453-495) and ``route_token()`` with the
+  expert union (engines/gemma.c:455-478, :580-685), compiled from the
+  reference sources by ``oracle/Makefile`` (present wherever they were built
+  and shipped).
 
 It also generates the seeded synthetic layers used by tests and bench: weights
 N(0, 0.02) through the converters' per-row int8 rule
@@ -25,7 +27,8 @@ from dataclasses import dataclass, field
 import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-FAMILY_OLMOE, FAMILY_QWEN = 0, 1
+FAMILY_OLMOE, FAMILY_QWEN, FAMILY_GEMMA = 0, 1, 2
+RSQRT_CR, RSQRT_LIBM = 0, 1
 
 _f32p = np.ctypeslib.ndpointer(np.float32, flags="C_CONTIGUOUS")
 _i8p = np.ctypeslib.ndpointer(np.int8, flags="C_CONTIGUOUS")
@@ -34,13 +37,15 @@ _i32p = np.ctypeslib.ndpointer(np.int32, flags="C_CONTIGUOUS")
 
 class OrcDesc(C.Structure):
     _fields_ = [(n, C.c_int) for n in
-                ("family", "D", "I", "E", "k", "renorm", "router_i8", "has_shared", "Is")]
+                ("family", "D", "I", "E", "k", "renorm", "router_i8", "has_shared", "Is")] + \
+               [("eps", C.c_float), ("rsqrt_mode", C.c_int)]
 
 
 class OrcWeights(C.Structure):
     _fields_ = [(n, C.c_void_p) for n in
                 ("router", "router_s", "g", "u", "d", "gs", "us", "ds",
-                 "sh_g", "sh_u", "sh_d", "sh_gs", "sh_us", "sh_ds", "sh_gate")]
+                 "sh_g", "sh_u", "sh_d", "sh_gs", "sh_us", "sh_ds", "sh_gate",
+                 "g_rscale", "g_pes", "g_enorm")]
 
 
 _lib = None
@@ -65,6 +70,12 @@ def lib():
         L.orc_expert_rows.restype = C.c_int
         L.orc_expert_rows.argtypes = [C.POINTER(OrcDesc), C.POINTER(OrcWeights), _f32p, C.c_int,
                                       C.c_void_p, _f32p]
+        L.orc_expert_rows_act.restype = C.c_int
+        L.orc_expert_rows_act.argtypes = [C.POINTER(OrcDesc), C.POINTER(OrcWeights), _f32p, C.c_int,
+                                          C.c_void_p, C.c_int, _f32p]
+        L.orc_gemma_prenorm.restype = C.c_int
+        L.orc_gemma_prenorm.argtypes = [C.POINTER(OrcDesc), C.POINTER(OrcWeights), _f32p, C.c_int,
+                                        _f32p, _f32p, _f32p]
         L.orc_quantize_rows_py.argtypes = [_f32p, C.c_int, C.c_int, _i8p, _f32p]
         L.orc_quantize_rows_c.argtypes = [_f32p, C.c_int, C.c_int, _i8p, _f32p]
         L.orc_fill_normal.argtypes = [C.c_uint64, _f32p, C.c_int64, C.c_float]
@@ -76,7 +87,7 @@ def lib():
 
 
 def ref_lib(name: str):
-    """The compiled reference (``olmoe`` or ``qwen``), or None if not built."""
+    """The compiled reference (``olmoe``, ``qwen`` or ``gemma``), or None if not built."""
     if name not in _ref:
         path = os.path.join(HERE, "_ref", f"libref_{name}.so")
         _ref[name] = C.CDLL(path) if os.path.exists(path) else None
@@ -84,7 +95,7 @@ def ref_lib(name: str):
 
 
 def ref_available() -> bool:
-    return ref_lib("olmoe") is not None and ref_lib("qwen") is not None
+    return ref_lib("olmoe") is not None and ref_lib("qwen") is not None and ref_lib("gemma") is not None
 
 
 def normal(seed: int, shape, sigma: float = 1.0) -> np.ndarray:
@@ -132,10 +143,12 @@ class Layer:
     has_shared: int = 0
     Is: int = 0
     arrays: dict = field(default_factory=dict)
+    eps: float = 1e-6          # gemma: rms_norm_eps
+    rsqrt_mode: int = RSQRT_CR  # gemma: RSQRT_CR (the device's value) or RSQRT_LIBM (powf)
 
     def desc(self) -> OrcDesc:
         return OrcDesc(self.family, self.D, self.I, self.E, self.k, self.renorm,
-                       self.router_i8, self.has_shared, self.Is)
+                       self.router_i8, self.has_shared, self.Is, self.eps, self.rsqrt_mode)
 
     def weights(self) -> OrcWeights:
         a = self.arrays
@@ -146,18 +159,24 @@ class Layer:
 
         return OrcWeights(p("router"), p("router_s"), p("g"), p("u"), p("d"), p("gs"),
                           p("us"), p("ds"), p("sh_g"), p("sh_u"), p("sh_d"), p("sh_gs"),
-                          p("sh_us"), p("sh_ds"), p("sh_gate"))
+                          p("sh_us"), p("sh_ds"), p("sh_gate"), p("g_rscale"), p("g_pes"),
+                          p("g_enorm"))
 
 
 def make_layer(family: int, D: int, I: int, E: int, k: int, seed: int, *, renorm: int = 0,
                router_i8: int = 0, has_shared: int = 0, Is: int = 0,
-               sigma: float = 0.02, router_bias=None) -> Layer:
+               sigma: float = 0.02, router_bias=None, eps: float = 1e-6) -> Layer:
     """Seeded random layer.  Experts: N(0, sigma) quantised per row with the
     converter rule.  Router: f32 N(0, sigma), or (router_i8) quantised with the
     engine's load-time rule as qwen.c does in stream mode (qwen.c:283-288).
     The shared expert is quantised the same way (qwen.c:285-287); sh_gate
-    stays f32 (qwen.c:282)."""
-    L = Layer(family, D, I, E, k, renorm, router_i8, has_shared, Is)
+    stays f32 (qwen.c:282).
+
+    GEMMA: the router is N(0, 1) (its input is unit-RMS scaled by D^-0.5, so
+    logits have unit spread), int8 with the converter rule when router_i8
+    (tools/convert_gemma.py:31-40 quantises router.proj); router.scale,
+    per_expert_scale and pre_feedforward_layernorm_2 are 1 + N(0, 0.1)."""
+    L = Layer(family, D, I, E, k, renorm, router_i8, has_shared, Is, eps=eps)
     a = L.arrays
     g = np.empty((E, I, D), np.int8); u = np.empty((E, I, D), np.int8)
     d = np.empty((E, D, I), np.int8)
@@ -169,6 +188,16 @@ def make_layer(family: int, D: int, I: int, E: int, k: int, seed: int, *, renorm
         u[e], us[e] = quantize_py(normal(base + 3 * e + 2, (I, D), sigma))
         d[e], ds[e] = quantize_py(normal(base + 3 * e + 3, (D, I), sigma))
     a.update(g=g, u=u, d=d, gs=gs, us=us, ds=ds)
+    if family == FAMILY_GEMMA:
+        rw = normal(base + 7, (E, D), 1.0)
+        if router_i8:
+            a["router"], a["router_s"] = quantize_py(rw)
+        else:
+            a["router"] = rw
+        a["g_rscale"] = 1.0 + normal(base + 15, (D,), 0.1)
+        a["g_pes"] = 1.0 + normal(base + 16, (E,), 0.1)
+        a["g_enorm"] = 1.0 + normal(base + 17, (D,), 0.1)
+        return L
     rw = normal(base + 7, (E, D), sigma)
     if router_i8:
         a["router"], a["router_s"] = quantize_c(rw)
@@ -189,6 +218,25 @@ def olmoe_layer(seed: int = 1, D=2048, I=1024, E=64, k=8, renorm=0) -> Layer:
 def qwen_layer(seed: int = 2, D=2048, I=512, E=256, k=8, Is=512, router_i8=1) -> Layer:
     return make_layer(FAMILY_QWEN, D, I, E, k, seed, renorm=1, router_i8=router_i8,
                       has_shared=1, Is=Is)
+
+
+def gemma_layer(seed: int = 3, D=2816, I=704, E=128, k=8, router_i8=1) -> Layer:
+    """Gemma-4-26B-A4B-shaped MoE layer (hidden 2816, 128 experts, top-8,
+    moe_intermediate 704), int8 router as the converter writes it."""
+    return make_layer(FAMILY_GEMMA, D, I, E, k, seed, router_i8=router_i8)
+
+
+def oracle_prenorm(L: Layer, x: np.ndarray):
+    """GEMMA: (router input xr [T,D], expert input xe [T,D], norm factor r [T])."""
+    x = np.ascontiguousarray(x, np.float32)
+    T = x.shape[0]
+    xr = np.empty((T, L.D), np.float32)
+    xe = np.empty((T, L.D), np.float32)
+    r = np.empty(T, np.float32)
+    d, ww = L.desc(), L.weights()
+    if lib().orc_gemma_prenorm(C.byref(d), C.byref(ww), x, T, xr, xe, r):
+        raise ValueError("orc_gemma_prenorm rejected the descriptor")
+    return xr, xe, r
 
 
 def oracle_moe(L: Layer, x: np.ndarray):
@@ -213,6 +261,20 @@ def oracle_expert_rows(L: Layer, x: np.ndarray, ids: np.ndarray) -> np.ndarray:
     d, ww = L.desc(), L.weights()
     if lib().orc_expert_rows(C.byref(d), C.byref(ww), x, x.shape[0], ids.ctypes.data, y):
         raise ValueError("orc_expert_rows rejected the descriptor or an id")
+    return y
+
+
+ACT_SILU_DIV, ACT_SILU_SIG, ACT_GELU_TANH = 0, 1, 2
+
+
+def oracle_expert_rows_act(L: Layer, x: np.ndarray, ids: np.ndarray, act: int) -> np.ndarray:
+    """y [R,D]: routed expert ids[r] on row x[r] as given, activation `act`."""
+    x = np.ascontiguousarray(x, np.float32)
+    ids = np.ascontiguousarray(ids, np.int32)
+    y = np.empty((x.shape[0], L.D), np.float32)
+    d, ww = L.desc(), L.weights()
+    if lib().orc_expert_rows_act(C.byref(d), C.byref(ww), x, x.shape[0], ids.ctypes.data, act, y):
+        raise ValueError("orc_expert_rows_act rejected the descriptor, an id or act")
     return y
 
 
@@ -244,7 +306,21 @@ def reference_moe(L: Layer, x: np.ndarray) -> np.ndarray:
     out = np.zeros((T, L.D), np.float32)
     a = L.arrays
     vp = lambda n: a[n].ctypes.data_as(C.c_void_p)  # noqa: E731
-    if L.family == FAMILY_OLMOE:
+    if L.family == FAMILY_GEMMA:
+        R = ref_lib("gemma")
+        if R is None:
+            raise RuntimeError("oracle/_ref not built")
+        gq = np.ascontiguousarray(np.concatenate([a["g"], a["u"]], axis=1))     # [E, 2I, D]
+        gsc = np.ascontiguousarray(np.concatenate([a["gs"], a["us"]], axis=1))  # [E, 2I]
+        rs = a.get("router_s")
+        rc = R.ref_gemma_moe(C.c_int(L.D), C.c_int(L.E), C.c_int(L.k), C.c_int(L.I), C.c_float(L.eps),
+                             C.c_int(L.router_i8), vp("router"),
+                             None if rs is None else rs.ctypes.data_as(C.c_void_p),
+                             vp("g_rscale"), vp("g_pes"), vp("g_enorm"),
+                             gq.ctypes.data_as(C.c_void_p), gsc.ctypes.data_as(C.c_void_p),
+                             vp("d"), vp("ds"), x.ctypes.data_as(C.c_void_p), C.c_int(T),
+                             out.ctypes.data_as(C.c_void_p))
+    elif L.family == FAMILY_OLMOE:
         R = ref_lib("olmoe")
         if R is None:
             raise RuntimeError("oracle/_ref not built")
@@ -267,3 +343,26 @@ def reference_moe(L: Layer, x: np.ndarray) -> np.ndarray:
     if rc:
         raise RuntimeError("reference harness failed")
     return out
+
+
+def reference_route(L: Layer, x: np.ndarray):
+    """GEMMA: (topk_idx [T,k], topk_w [T,k]) from the reference's own compiled
+    route_token (engines/gemma.c:455-478)."""
+    assert L.family == FAMILY_GEMMA
+    R = ref_lib("gemma")
+    if R is None:
+        raise RuntimeError("oracle/_ref not built")
+    x = np.ascontiguousarray(x, np.float32)
+    T = x.shape[0]
+    idx = np.empty((T, L.k), np.int32)
+    w = np.empty((T, L.k), np.float32)
+    a = L.arrays
+    rs = a.get("router_s")
+    vp = lambda n: a[n].ctypes.data_as(C.c_void_p)  # noqa: E731
+    rc = R.ref_gemma_route(C.c_int(L.D), C.c_int(L.E), C.c_int(L.k), C.c_float(L.eps), C.c_int(L.router_i8),
+                           vp("router"), None if rs is None else rs.ctypes.data_as(C.c_void_p),
+                           vp("g_rscale"), vp("g_pes"), x.ctypes.data_as(C.c_void_p), C.c_int(T),
+                           idx.ctypes.data_as(C.c_void_p), w.ctypes.data_as(C.c_void_p))
+    if rc:
+        raise RuntimeError("reference harness failed")
+    return idx, w

@@ -17,7 +17,7 @@ import numpy as np
 PKG = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(PKG, "libomc.so")
 
-FAMILY_OLMOE, FAMILY_QWEN = 0, 1
+FAMILY_OLMOE, FAMILY_QWEN, FAMILY_GEMMA = 0, 1, 2
 ROUTER_F32, ROUTER_I8 = 0, 1
 
 OK, EINVAL, ENOMEM, ENOINIT, ECUDA, EDEVICE, ETIMEOUT, ENCCL, EUNSUPPORTED = 0, -1, -2, -3, -4, -5, -6, -7, -8
@@ -48,6 +48,7 @@ SIGNATURES = {
     "omc_init": (_i, [_i, _sz]),
     "omc_shutdown": (None, []),
     "omc_layer_init": (_i, [_i, C.POINTER(MoEDesc), _vp, _vp]),
+    "omc_layer_gemma_norms": (_i, [_i, C.c_float, _vp, _vp, _vp]),
     "omc_expert_set": (_i, [_i, _i, _vp, _vp, _vp, _vp, _vp, _vp]),
     "omc_experts_set_packed": (_i, [_i, _vp, _vp, _vp, _vp, _vp, _vp]),
     "omc_shared_set": (_i, [_i, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
@@ -80,6 +81,7 @@ SIGNATURES = {
     "omc_debug_set_path": (_i, [_i]),
     "omc_debug_router_tile": (_i, [_i, _i, _i]),
     "omc_debug_ws_copy": (_i, [_i, _vp, _sz]),
+    "omc_debug_gemma_prenorm": (_i, [_i, _vp, _i, _vp, _vp, _vp]),
 }
 
 PATH_AUTO, PATH_GEMV, PATH_MMA, PATH_DECODE = 0, 1, 2, 3
@@ -205,11 +207,32 @@ class MoELayer:
         a = L.arrays
         m = cls(layer, L.family, L.D, L.I, L.E, L.k, a["router"], a.get("router_s"),
                 L.renorm, L.has_shared, L.Is)
+        if L.family == FAMILY_GEMMA:
+            m.set_gemma_norms(L.eps, a["g_rscale"], a["g_pes"], a.get("g_enorm"))
         m.set_experts_packed(a["g"], a["gs"], a["u"], a["us"], a["d"], a["ds"])
         if L.has_shared:
             m.set_shared(a["sh_g"], a["sh_gs"], a["sh_u"], a["sh_us"], a["sh_d"], a["sh_ds"],
                          a["sh_gate"])
         return m
+
+    def set_gemma_norms(self, eps: float, router_scale, per_expert_scale, expert_norm=None) -> None:
+        """GEMMA: router.scale [D], per_expert_scale [E], pre_feedforward_layernorm_2 [D]."""
+        arrs = [None if v is None else np.ascontiguousarray(v, np.float32)
+                for v in (router_scale, per_expert_scale, expert_norm)]
+        self._keep += [v for v in arrs if v is not None]
+        check(lib().omc_layer_gemma_norms(self.layer, float(eps), *[_p(v) for v in arrs]),
+              "omc_layer_gemma_norms")
+
+    def debug_prenorm(self, x: np.ndarray):
+        """GEMMA: (router input, expert input, norm factor) from the device kernel."""
+        x = np.ascontiguousarray(x, np.float32)
+        T = x.shape[0]
+        xr = np.empty((T, self.desc.D), np.float32)
+        xe = np.empty((T, self.desc.D), np.float32)
+        r = np.empty(T, np.float32)
+        check(lib().omc_debug_gemma_prenorm(self.layer, _p(x), T, _p(xr), _p(xe), _p(r)),
+              "omc_debug_gemma_prenorm")
+        return xr, xe, r
 
     def set_experts_packed(self, g, gs, u, us, d, ds) -> None:
         arrs = [np.ascontiguousarray(v) for v in (g, gs, u, us, d, ds)]

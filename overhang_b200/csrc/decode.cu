@@ -77,7 +77,8 @@ constexpr int CTR_FIXED = CTR_HFLAG + DC_GMAX * DC_TILES_MAX;
 
 struct DecArgs {
     omc_layer_dev L;
-    const float *x;
+    const float *x;       // the experts' input rows
+    const float *xr;      // the router's input rows (x except for GEMMA)
     int T;
     int32_t *topk_idx;
     float *topk_w, *logits;
@@ -172,9 +173,10 @@ __device__ __forceinline__ void u8x4_f2(uint32_t u, float2 &lo, float2 &hi) {
                     bias);
 }
 
-__device__ __forceinline__ float swiglu(int family, float g, float u) {
+__device__ __forceinline__ float swiglu(int act, float g, float u) {
+    if (act == OMC_ACT_GELU_TANH) return __fmul_rn(omc_gelu_tanh(g), u);   // engines/gemma.c:671
     const float e = omc_expf_glibc(-g);
-    if (family == OMC_FAMILY_QWEN) return __fmul_rn(__fmul_rn(g, __fdiv_rn(1.f, __fadd_rn(1.f, e))), u);
+    if (act == OMC_ACT_SILU_SIG) return __fmul_rn(__fmul_rn(g, __fdiv_rn(1.f, __fadd_rn(1.f, e))), u);
     return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.f, e)), u);
 }
 
@@ -291,7 +293,7 @@ __global__ void __launch_bounds__(DC_THREADS, 1) decode_moe_kernel(const DecArgs
             for (int ch = 0; ch < DC_RCH; ++ch) {
                 mbar_arrive_expect_tx(&rbar[ch], (uint32_t)((T + nr) * cw * 4));
                 for (int t = 0; t < T; ++t)
-                    bulk_g2s(xs + (size_t)t * a.ldx + ch * cw, a.x + (size_t)t * D + ch * cw, cw * 4, &rbar[ch]);
+                    bulk_g2s(xs + (size_t)t * a.ldx + ch * cw, a.xr + (size_t)t * D + ch * cw, cw * 4, &rbar[ch]);
                 for (int r = 0; r < nr; ++r) {
                     const int gr = r0 + r;
                     const float *src = gr < E ? L.router + (size_t)gr * D : L.sh_gate;
@@ -344,10 +346,20 @@ __global__ void __launch_bounds__(DC_THREADS, 1) decode_moe_kernel(const DecArgs
                 a.logits[(size_t)t * a.ldl + gr] = (L.router_i8 && gr < E) ? __fmul_rn(acc, L.router_s[gr]) : acc;
         }
         __syncthreads();   // this CTA's logits are written; x chunks have landed
+        if (a.xr != a.x) {
+            // GEMMA: the experts read another input; it replaces the router's
+            // rows (columns D.. stay zero) while the other router CTAs finish
+            for (int i = tid; i < T * (D / 4); i += DC_THREADS) {
+                const int t = i / (D / 4), col = (i - t * (D / 4)) * 4;
+                cp_async16(xs + (size_t)t * a.ldx + col, a.x + (size_t)t * D + col);
+            }
+            asm volatile("cp.async.commit_group;" ::: "memory");
+        }
         if (tid == 0) {
             fence_acqrel_gpu();
             red_release_add(ctr + CTR_ROUTER, 1);
         }
+        if (a.xr != a.x) asm volatile("cp.async.wait_group 0;" ::: "memory");
     } else {
         asm volatile("cp.async.wait_group 0;" ::: "memory");
     }
@@ -356,7 +368,7 @@ __global__ void __launch_bounds__(DC_THREADS, 1) decode_moe_kernel(const DecArgs
     if (tid == 0 && !wait_value(ctr + CTR_ROUTER, a.nrc, a.err, -1)) s_abort = 1;
     __syncthreads();
     if (!s_abort && warp < T)
-        select_token<NV>(a.logits, a.ldl, warp, E, K, L.family, L.renorm, L.has_shared, s_tidx, s_tw, s_sg, a.err,
+        select_token<NV>(a.logits, a.ldl, warp, E, K, L.family, L.renorm, L.has_shared, L.g_pes, s_tidx, s_tw, s_sg, a.err,
                          reinterpret_cast<float *>(ring) + warp * NV * 32);
     __syncthreads();
 
@@ -635,7 +647,7 @@ __global__ void __launch_bounds__(DC_THREADS, 1) decode_moe_kernel(const DecArgs
                     const int j = q >> 7, rt = q & (OMC_TM - 1), hrow = mt * OMC_TM + rt;
                     const float gsum = gather(a.partA, j, rt), usum = gather(a.partA, j, OMC_TM + rt);
                     a.hbuf[(size_t)s_gslot[g * DC_TMAX + j] * ldh + hrow] =
-                        hrow < Iw ? swiglu(L.family, __fmul_rn(gsum, gs[hrow]), __fmul_rn(usum, us[hrow])) : 0.f;
+                        hrow < Iw ? swiglu(L.act, __fmul_rn(gsum, gs[hrow]), __fmul_rn(usum, us[hrow])) : 0.f;
                 }
                 cons_bar();
                 if (ci == 0) {
@@ -819,8 +831,9 @@ extern "C" int omc_decode_supported(const omc_layer_dev *L, int T, int G, size_t
     return (size_t)g.nctr <= ctr_ints && g.partA_floats + g.partB_floats <= part_floats;
 }
 
-extern "C" int omc_launch_decode(const omc_layer_dev *L, const float *x, int T, const omc_ws *ws, int G, int *ctr,
-                                 float *part, int32_t *topk_idx, float *topk_w, float *out, cudaStream_t s) {
+extern "C" int omc_launch_decode(const omc_layer_dev *L, const float *x, const float *xr, int T, const omc_ws *ws,
+                                 int G, int *ctr, float *part, int32_t *topk_idx, float *topk_w, float *out,
+                                 cudaStream_t s) {
     if (T <= 0) return 0;
     DecGeom g;
     int rc;
@@ -828,6 +841,7 @@ extern "C" int omc_launch_decode(const omc_layer_dev *L, const float *x, int T, 
     DecArgs a;
     a.L = *L;
     a.x = x;
+    a.xr = xr ? xr : x;
     a.T = T;
     a.topk_idx = topk_idx;
     a.topk_w = topk_w;

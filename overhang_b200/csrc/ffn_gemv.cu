@@ -48,10 +48,11 @@ __device__ __forceinline__ float dot16(float acc, int4 w, const float *x) {
     return acc;
 }
 
-// SwiGLU in the family's arithmetic form.
-__device__ __forceinline__ float swiglu(int family, float g, float u) {
+// SwiGLU in the family's arithmetic form (GEMMA: the GELU-tanh gate).
+__device__ __forceinline__ float swiglu(int act, float g, float u) {
+    if (act == OMC_ACT_GELU_TANH) return __fmul_rn(omc_gelu_tanh(g), u);   // engines/gemma.c:671
     const float e = omc_expf_glibc(-g);
-    if (family == OMC_FAMILY_QWEN) return __fmul_rn(__fmul_rn(g, __fdiv_rn(1.f, __fadd_rn(1.f, e))), u);
+    if (act == OMC_ACT_SILU_SIG) return __fmul_rn(__fmul_rn(g, __fdiv_rn(1.f, __fadd_rn(1.f, e))), u);
     return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.f, e)), u);
 }
 
@@ -82,7 +83,13 @@ __global__ void __launch_bounds__(GV_WARPS * 32) gemv_gateup_kernel(omc_layer_de
         e = L.E;
         Iw = L.Is;
     }
-    if (rg * 32 >= Iw) return;
+    if (rg * 32 >= Iw) {
+        // rows past the expert's width still feed the down projection (its
+        // K runs to I_pad against zero weights): they must hold zeros, not
+        // whatever an earlier forward left there
+        if (w == 0) hbuf[(size_t)s * ldh + rg * 32 + lane] = 0.f;
+        return;
+    }
     for (int i = threadIdx.x * 4; i < L.D_pad; i += blockDim.x * 4) {
         float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
         if (i < L.D) v = *reinterpret_cast<const float4 *>(x + (size_t)t * L.D + i);
@@ -124,7 +131,7 @@ __global__ void __launch_bounds__(GV_WARPS * 32) gemv_gateup_kernel(omc_layer_de
     if (row < Iw) {
         const float g = __fmul_rn(ag, P.gs[row]);
         const float u = __fmul_rn(au, P.us[row]);
-        h = swiglu(L.family, g, u);
+        h = swiglu(L.act, g, u);
     }
     hbuf[(size_t)s * ldh + row] = h;
 }

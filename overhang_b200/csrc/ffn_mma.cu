@@ -133,9 +133,10 @@ __device__ __forceinline__ bool warp_wait(uint64_t *bar, uint32_t parity, int *e
 }
 
 
-__device__ __forceinline__ float swiglu_f(int family, float g, float u) {
+__device__ __forceinline__ float swiglu_f(int act, float g, float u) {
+    if (act == OMC_ACT_GELU_TANH) return omc_gelu_tanh(g) * u;   // engines/gemma.c:671
     const float e = __expf(-g);
-    if (family == OMC_FAMILY_QWEN) return g * __frcp_rn(1.f + e) * u;
+    if (act == OMC_ACT_SILU_SIG) return g * __frcp_rn(1.f + e) * u;
     return __fdividef(g, 1.f + e) * u;
 }
 
@@ -547,7 +548,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_gemm_kernel(const GemmArgs a)
 #pragma unroll
                     for (int jj = 0; jj < 16; ++jj) {
                         const int j = ch * 16 + jj;                // token row within the item
-                        const float hv = f < Iw ? swiglu_f(L.family, __uint_as_float(gv[jj]) * sc0,
+                        const float hv = f < Iw ? swiglu_f(L.act, __uint_as_float(gv[jj]) * sc0,
                                                            __uint_as_float(uv[jj]) * sc1)
                                                 : 0.f;
                         // operand row n0 + j; n0 % 16 == 0, so its swizzle phase is j & 7 = jj & 7
@@ -771,7 +772,12 @@ extern "C" int omc_launch_mma_rows(const omc_layer_dev *L, const float *x, int R
     if (R <= 0) return 0;
     if (gemm_setup()) return OMC_ECUDA;
     const long long n8 = (long long)R * L->D / 8;
-    rows_to_f16_kernel<<<(int)((n8 + 255) / 256 < 4096 ? (n8 + 255) / 256 : 4096), 256, 0, s>>>(x, n8, ws->xh);
+    if (L->family == OMC_FAMILY_GEMMA) {   // residual rows: the experts' input norm first
+        const int rc = omc_launch_gemma_prenorm(L, x, R, nullptr, nullptr, ws->xh, nullptr, s);
+        if (rc) return rc;
+    } else {
+        rows_to_f16_kernel<<<(int)((n8 + 255) / 256 < 4096 ? (n8 + 255) / 256 : 4096), 256, 0, s>>>(x, n8, ws->xh);
+    }
     omc_plan_args pa;
     omc_plan_setup(L, R, ws, &pa);
     pa.K = 1;
@@ -802,7 +808,7 @@ extern "C" int omc_launch_mma_rows(const omc_layer_dev *L, const float *x, int R
     ga.work = reinterpret_cast<const int4 *>(pa.work2);
     moe_gemm_kernel<2><<<grid, NTHREADS, SMEM_BYTES, s>>>(ga);
     omc_prof_mark(s, "gemm_down");
-    omc_g_launches += 4;
+    omc_g_launches += L->family == OMC_FAMILY_GEMMA ? 3 : 4;   // prenorm counts itself
     return cudaGetLastError() == cudaSuccess ? 0 : OMC_ECUDA;
 }
 

@@ -38,6 +38,17 @@ __device__ __forceinline__ uint64_t omc_globaltimer() {
     return t;
 }
 
+// ------------------------------------------------------------- gelu_tanh --
+// engines/gemma.c:319-321, operation for operation: 0.5f*x*(1 + tanhf(c*(x +
+// 0.044715f*x*x*x))).  tanhf is CUDA's (within 2 ulp of the exact value); the
+// reference's is libm's, so expert outputs agree within the output tolerance,
+// not bit for bit.
+__device__ __forceinline__ float omc_gelu_tanh(float x) {
+    const float c3 = __fmul_rn(__fmul_rn(__fmul_rn(0.044715f, x), x), x);
+    const float th = tanhf(__fmul_rn(0.7978845608028654f, __fadd_rn(x, c3)));
+    return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.f, th));
+}
+
 // ------------------------------------------------------------------ expf --
 // Device restatement of glibc's expf (glibc >= 2.28, x86-64 FMA build), the
 // function the reference's softmax calls (engines/olmoe.c:172,

@@ -14,6 +14,7 @@
  * the Metal backend's arena (metal/om_metal.mm:14-48) with cudaHostAlloc'd
  * memory for the omm_* seam (omm_shim.c).
  */
+#include <math.h>
 #include <stdarg.h>
 #include <stdio.h>
 #include <stdlib.h>
@@ -211,11 +212,11 @@ static int staging_ensure(size_t n) {
 int omc_layer_init(int layer, const omc_moe_desc *d, const void *router_w, const float *router_s) {
     if (!G.init) return omc_fail(OMC_ENOINIT, "omc_layer_init: omc_init not called");
     if (layer < 0 || layer > 4096 || !d || !router_w) return omc_fail(OMC_EINVAL, "omc_layer_init: bad arguments");
-    if (d->family != OMC_FAMILY_OLMOE && d->family != OMC_FAMILY_QWEN)
+    if (d->family != OMC_FAMILY_OLMOE && d->family != OMC_FAMILY_QWEN && d->family != OMC_FAMILY_GEMMA)
         return omc_fail(OMC_EINVAL, "omc_layer_init: unknown family %d", d->family);
     if (d->D <= 0 || d->I <= 0 || d->E <= 0 || d->k <= 0 || d->k > d->E || d->k > OMC_MAX_K || d->E > OMC_MAX_E ||
-        (d->D % 64) || (d->I % 32))
-        return omc_fail(OMC_EINVAL, "omc_layer_init: shape D=%d I=%d E=%d k=%d (D%%64, I%%32, k<=%d, E<=%d)", d->D,
+        (d->D % 64) || (d->I % 16))
+        return omc_fail(OMC_EINVAL, "omc_layer_init: shape D=%d I=%d E=%d k=%d (D%%64, I%%16, k<=%d, E<=%d)", d->D,
                         d->I, d->E, d->k, OMC_MAX_K, OMC_MAX_E);
     if (d->has_shared && (d->family != OMC_FAMILY_QWEN || d->Is <= 0 || (d->Is % 32)))
         return omc_fail(OMC_EINVAL, "omc_layer_init: shared expert needs QWEN family and Is%%32==0");
@@ -237,9 +238,12 @@ int omc_layer_init(int layer, const omc_moe_desc *d, const void *router_w, const
     }
     memset(L, 0, sizeof(*L));
     L->desc = *d;
-    if (d->family == OMC_FAMILY_QWEN) L->desc.renorm = 1;
+    if (d->family == OMC_FAMILY_QWEN || d->family == OMC_FAMILY_GEMMA) L->desc.renorm = 1;
     omc_layer_dev *P = &L->dev;
-    P->family = d->family; P->D = d->D; P->I = d->I; P->E = d->E; P->k = d->k;
+    P->family = d->family;
+    P->act = d->family == OMC_FAMILY_QWEN ? OMC_ACT_SILU_SIG
+           : d->family == OMC_FAMILY_GEMMA ? OMC_ACT_GELU_TANH : OMC_ACT_SILU_DIV;
+    P->D = d->D; P->I = d->I; P->E = d->E; P->k = d->k;
     P->renorm = L->desc.renorm; P->router_i8 = d->router_dtype == OMC_ROUTER_I8;
     P->has_shared = d->has_shared; P->Is = d->has_shared ? d->Is : 0;
     P->D_pad = omc_round_up(d->D, OMC_KB);
@@ -287,6 +291,43 @@ int omc_layer_init(int layer, const omc_moe_desc *d, const void *router_w, const
         int rc = dec_ensure(P);
         if (rc) return rc;
     }
+    return OMC_OK;
+}
+
+int omc_layer_gemma_norms(int layer, float eps, const float *router_scale, const float *per_expert_scale,
+                          const float *expert_norm) {
+    if (!G.init) return omc_fail(OMC_ENOINIT, "omc_layer_gemma_norms: omc_init not called");
+    omc_layer *L = omc_get_layer(layer);
+    if (!L) return omc_fail(OMC_ENOINIT, "omc_layer_gemma_norms: layer %d not initialised", layer);
+    if (L->desc.family != OMC_FAMILY_GEMMA)
+        return omc_fail(OMC_EINVAL, "omc_layer_gemma_norms: layer %d is not a GEMMA layer", layer);
+    if (!router_scale || !per_expert_scale || !(eps >= 0.f))
+        return omc_fail(OMC_EINVAL, "omc_layer_gemma_norms: router_scale and per_expert_scale are required, eps >= 0");
+    const int D = L->desc.D, E = L->desc.E;
+    float *h = malloc(sizeof(float) * (size_t)D);
+    if (!h) return omc_fail(OMC_ENOMEM, "omc_layer_gemma_norms: host alloc");
+    /* engines/gemma.c:459-460: the float product router.scale[i] * rroot,
+     * rroot = 1.f/sqrtf((float)D), which the reference forms per element */
+    const float rroot = 1.f / sqrtf((float)D);
+    for (int i = 0; i < D; i++) h[i] = router_scale[i] * rroot;
+    int on_host;
+    float *s2 = omc_slab_alloc((size_t)D * sizeof(float), &on_host);
+    float *pes = omc_slab_alloc((size_t)E * sizeof(float), &on_host);
+    float *en = expert_norm ? omc_slab_alloc((size_t)D * sizeof(float), &on_host) : NULL;
+    if (!s2 || !pes || (expert_norm && !en)) {
+        free(h);
+        return omc_fail(OMC_ENOMEM, "omc_layer_gemma_norms: slab");
+    }
+    cudaError_t e1 = cudaMemcpy(s2, h, (size_t)D * sizeof(float), cudaMemcpyHostToDevice);
+    free(h);
+    CK(e1);
+    CK(cudaMemcpy(pes, per_expert_scale, (size_t)E * sizeof(float), cudaMemcpyHostToDevice));
+    if (en) CK(cudaMemcpy(en, expert_norm, (size_t)D * sizeof(float), cudaMemcpyHostToDevice));
+    L->dev.eps = eps;
+    L->dev.g_s2 = s2;
+    L->dev.g_pes = pes;
+    L->dev.g_en = en;
+    L->gemma_ready = 1;
     return OMC_OK;
 }
 
@@ -481,6 +522,10 @@ static int ws_ensure_core(const omc_layer *L, size_t Tz, size_t nslots, size_t n
     if ((rc = ws_buf(11, (void **)&W->ypart, Tz * (K + 1) * D * 4))) return rc;
     if ((rc = ws_buf(12, (void **)&W->hbuf, (Tz * K + Tz) * Imax_rows * 4))) return rc;
     if ((rc = ws_buf(13, (void **)&W->slotrow, (nslots > Tz * K ? nslots : Tz * K) * 4))) return rc;
+    if (P->family == OMC_FAMILY_GEMMA) {
+        if ((rc = ws_buf(14, (void **)&W->xg_r, Tz * D * 4))) return rc;
+        if ((rc = ws_buf(15, (void **)&W->xg_e, Tz * D * 4))) return rc;
+    }
     omc_ws *ws = &G.ws;
     ws->T_cap = T;
     ws->R_cap = (int)R;
@@ -502,6 +547,8 @@ static int ws_ensure_core(const omc_layer *L, size_t Tz, size_t nslots, size_t n
     ws->hp = W->hp;
     ws->ypart = W->ypart;
     ws->hbuf = W->hbuf;
+    ws->xg_r = P->family == OMC_FAMILY_GEMMA ? W->xg_r : NULL;
+    ws->xg_e = P->family == OMC_FAMILY_GEMMA ? W->xg_e : NULL;
     ws->err = G.d_err;
     return OMC_OK;
 }
@@ -644,6 +691,8 @@ static int layer_ready(const omc_layer *L) {
         if (!L->have[e]) return omc_fail(OMC_ENOINIT, "forward: expert %d of layer not uploaded", e);
     if (L->desc.has_shared && !L->have[L->desc.E])
         return omc_fail(OMC_ENOINIT, "forward: shared expert not uploaded");
+    if (L->desc.family == OMC_FAMILY_GEMMA && !L->gemma_ready)
+        return omc_fail(OMC_ENOINIT, "forward: GEMMA layer without omc_layer_gemma_norms");
     return OMC_OK;
 }
 
@@ -675,26 +724,42 @@ static int forward_on_ws(omc_layer *L, const omc_ws *ws, const float *x, int T, 
         omc_plan_setup(&L->dev, T, ws, &plan);
         CK(cudaMemsetAsync(ws->done, 0, sizeof(int), s));
     }
+    /* GEMMA: x is the residual; the router and the experts each read their
+     * own norm of it (prenorm.cu).  The tensor-core path takes the experts'
+     * input as its f16 operand, the CUDA-core paths as f32. */
+    const int gemma = L->dev.family == OMC_FAMILY_GEMMA;
+    const float *xr = x, *xe = x;
+    if (gemma) {
+        if ((rc = omc_launch_gemma_prenorm(&L->dev, x, T, ws->xg_r, mma ? NULL : ws->xg_e, mma ? ws->xh : NULL, NULL,
+                                           s)))
+            return omc_fail(rc, "prenorm launch failed");
+        xr = ws->xg_r;
+        xe = ws->xg_e;
+    }
     /* decode: the whole block in one launch (decode.cu).  Chosen on its own
      * at T = 1, where it beats the router + GEMV kernels; from T = 2 its
      * CUDA-core dequant-and-dot is the bound and the separate kernels win
      * (measured on B200), so larger T take it only when it is forced. */
     if (!mma && G.ep_world <= 1 && (G.path_override == 3 || (G.path_override == 0 && T == 1)) &&
         omc_decode_supported(&L->dev, T, G.num_sms, G.dec_ctr_n, G.dec_part_n)) {
-        if ((rc = omc_launch_decode(&L->dev, x, T, ws, G.num_sms, G.dec_ctr, G.dec_part, idx, w, out, s)))
+        if ((rc = omc_launch_decode(&L->dev, xe, xr, T, ws, G.num_sms, G.dec_ctr, G.dec_part, idx, w, out, s)))
             return omc_fail(rc, "fused decode launch failed (%s)", omc_strerror(rc));
         G.prof_valid = G.profiling;
         return OMC_OK;
     }
     if (G.path_override == 3) return omc_fail(OMC_EUNSUPPORTED, "fused decode path forced but not available for T=%d", T);
-    if ((rc = omc_launch_router(&L->dev, x, T, ws, idx, w, mma ? &plan : NULL, s)))
+    if ((rc = omc_launch_router(&L->dev, xr, T, ws, idx, w, mma ? &plan : NULL, s)))
         return omc_fail(rc, "router launch failed");
     omc_prof_mark(s, "router_select");
     if (mma) {
-        rc = omc_launch_mma_ffn(&L->dev, x, T, ws, idx, w, out, s);
-        if (rc == OMC_EUNSUPPORTED && G.path_override != 2) rc = omc_launch_gemv_ffn(&L->dev, x, T, ws, idx, w, out, s);
+        rc = omc_launch_mma_ffn(&L->dev, xe, T, ws, idx, w, out, s);
+        if (rc == OMC_EUNSUPPORTED && G.path_override != 2) {
+            if (gemma && (rc = omc_launch_gemma_prenorm(&L->dev, x, T, NULL, ws->xg_e, NULL, NULL, s)))
+                return omc_fail(rc, "prenorm launch failed");
+            rc = omc_launch_gemv_ffn(&L->dev, xe, T, ws, idx, w, out, s);
+        }
     } else {
-        rc = omc_launch_gemv_ffn(&L->dev, x, T, ws, idx, w, out, s);
+        rc = omc_launch_gemv_ffn(&L->dev, xe, T, ws, idx, w, out, s);
     }
     if (rc) return omc_fail(rc, "expert FFN launch failed (%s)", omc_strerror(rc));
     G.prof_valid = G.profiling;
@@ -736,6 +801,10 @@ static size_t noalloc_layout(const omc_layer_dev *P, int T, char *base, omc_ws *
     TAKE(ypart, float *, Tz * (K + 1) * D * 4);
     TAKE(hbuf, float *, (Tz * K + Tz) * Imax_rows * 4);
     TAKE(slotrow, int *, Tz * K * 4);
+    if (P->family == OMC_FAMILY_GEMMA) {
+        TAKE(xg_r, float *, Tz * D * 4);
+        TAKE(xg_e, float *, Tz * D * 4);
+    }
 #undef TAKE
     if (base) {
         ws->offsets = ws->counts + (E + 4);
@@ -808,8 +877,15 @@ int omc_moe_route_dev(int layer, const float *x, int T, int32_t *topk_idx, float
     if (T == 0) return OMC_OK;
     int rc;
     if ((rc = omc_ws_ensure(L, T, 0))) return rc;
+    if (L->desc.family == OMC_FAMILY_GEMMA && !L->gemma_ready)
+        return omc_fail(OMC_ENOINIT, "omc_moe_route_dev: GEMMA layer without omc_layer_gemma_norms");
     cudaStream_t s = stream ? (cudaStream_t)stream : G.stream;
     G.prof_valid = 0;
+    if (L->desc.family == OMC_FAMILY_GEMMA) {
+        if ((rc = omc_launch_gemma_prenorm(&L->dev, x, T, G.ws.xg_r, NULL, NULL, NULL, s)))
+            return omc_fail(rc, "omc_moe_route_dev: prenorm launch failed");
+        x = G.ws.xg_r;
+    }
     if ((rc = omc_launch_router(&L->dev, x, T, &G.ws, topk_idx, topk_w, NULL, s)))
         return omc_fail(rc, "omc_moe_route_dev: router launch failed");
     if (shared_gate && L->desc.has_shared)
@@ -832,6 +908,8 @@ int omc_moe_experts_dev(int layer, const float *x_rows, int R, const int32_t *ex
         if (!L->have[e]) return omc_fail(OMC_ENOINIT, "omc_moe_experts_dev: expert %d not uploaded", e);
     if (L->desc.has_shared && !L->have[L->desc.E])
         return omc_fail(OMC_ENOINIT, "omc_moe_experts_dev: shared expert not uploaded");
+    if (L->desc.family == OMC_FAMILY_GEMMA && !L->gemma_ready)
+        return omc_fail(OMC_ENOINIT, "omc_moe_experts_dev: GEMMA layer without omc_layer_gemma_norms");
     if ((rc = omc_ws_ensure_rows(L, R))) return rc;
     cudaStream_t s = stream ? (cudaStream_t)stream : G.stream;
     G.prof_valid = 0;
@@ -919,4 +997,26 @@ int omc_debug_ws_copy(int which, void *dst, size_t bytes) {
     CK(cudaDeviceSynchronize());
     CK(cudaMemcpy(dst, src, bytes, cudaMemcpyDeviceToHost));
     return OMC_OK;
+}
+
+/* GEMMA test hook: the prenorm kernel's outputs for host rows x [T][D]:
+ * router input xr, expert input xe [T][D] and the norm factor r [T]. */
+int omc_debug_gemma_prenorm(int layer, const float *x, int T, float *xr, float *xe, float *r) {
+    if (!G.init) return omc_fail(OMC_ENOINIT, "omc_debug_gemma_prenorm: omc_init not called");
+    omc_layer *L = omc_get_layer(layer);
+    if (!L || L->desc.family != OMC_FAMILY_GEMMA || !L->gemma_ready)
+        return omc_fail(OMC_EINVAL, "omc_debug_gemma_prenorm: layer %d is not a ready GEMMA layer", layer);
+    if (T <= 0 || !x || !xr || !xe || !r) return omc_fail(OMC_EINVAL, "omc_debug_gemma_prenorm: bad arguments");
+    int rc;
+    if ((rc = omc_ws_ensure(L, T, 1))) return rc;
+    const size_t n = (size_t)T * L->desc.D * sizeof(float);
+    cudaStream_t s = G.stream;
+    CK(cudaMemcpyAsync(G.ws.x, x, n, cudaMemcpyHostToDevice, s));
+    if ((rc = omc_launch_gemma_prenorm(&L->dev, G.ws.x, T, G.ws.xg_r, G.ws.xg_e, NULL, G.ws.sg, s)))
+        return omc_fail(rc, "omc_debug_gemma_prenorm: launch failed");
+    CK(cudaMemcpyAsync(xr, G.ws.xg_r, n, cudaMemcpyDeviceToHost, s));
+    CK(cudaMemcpyAsync(xe, G.ws.xg_e, n, cudaMemcpyDeviceToHost, s));
+    CK(cudaMemcpyAsync(r, G.ws.sg, (size_t)T * sizeof(float), cudaMemcpyDeviceToHost, s));
+    CK(cudaStreamSynchronize(s));
+    return omc_check_device_error();
 }

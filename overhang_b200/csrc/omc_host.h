@@ -23,6 +23,7 @@ typedef struct {
     omc_expert_ptrs *d_experts_tab; /* device pointer table [E+1]           */
     unsigned char *have;            /* uploaded flags [E+1]                 */
     int e0, ne;                     /* experts owned by this rank (EP)      */
+    int gemma_ready;                /* GEMMA: omc_layer_gemma_norms called  */
 } omc_layer;
 
 typedef struct {
@@ -33,6 +34,7 @@ typedef struct {
     uint16_t *xh, *hp;
     float *ypart, *hbuf;
     int *slotrow;
+    float *xg_r, *xg_e;
 } omc_ws_ptrs;
 
 typedef struct {
@@ -97,6 +99,7 @@ int omc_debug_expf(const float *x, float *y, long long n);
 int omc_debug_set_path(int path);
 int omc_debug_router_tile(int g, int tt, int rr);
 int omc_debug_ws_copy(int which, void *dst, size_t bytes);
+int omc_debug_gemma_prenorm(int layer, const float *x, int T, float *xr, float *xe, float *r);
 
 #ifdef __cplusplus
 }

@@ -85,14 +85,25 @@ static inline __host__ __device__ size_t omc_dblk(int t, int kb, int nkb) {
 }
 
 /* Layer parameters handed to kernels by value. */
+/* expert activation, h = act(g) * u */
+#define OMC_ACT_SILU_DIV  0   /* g/(1+exp(-g))      engines/olmoe.c:393   */
+#define OMC_ACT_SILU_SIG  1   /* g*(1/(1+exp(-g)))  engines/qwen.c:158,485 */
+#define OMC_ACT_GELU_TANH 2   /* gelu_tanh(g)       engines/gemma.c:319,671 */
+
 typedef struct {
     int family, D, I, E, k, renorm, router_i8, has_shared, Is;
+    int act;                      /* OMC_ACT_* (the family's, or the caller's for job passes) */
     int D_pad, I_pad, Is_pad;     /* roundup(.., 64): K extent of a tiled matrix   */
     int D_rows, I_rows, Is_rows;  /* roundup(.., 128): row extent of a tiled matrix */
     const float *router;          /* f32 [E][D] (int8 routers stored as their exact f32 values) */
     const float *router_s;        /* [E] for int8 routers, else NULL */
     const float *sh_gate;         /* [D] or NULL */
     const omc_expert_ptrs *experts;  /* device table [E + 1]; entry E = shared expert */
+    /* GEMMA only (NULL / 0 otherwise) */
+    float eps;                    /* rms_norm_eps                                   */
+    const float *g_s2;            /* [D] router.scale[i] * D^-0.5 (float product)   */
+    const float *g_en;            /* [D] expert-input norm weight, NULL = ones      */
+    const float *g_pes;           /* [E] per_expert_scale                           */
 } omc_layer_dev;
 
 #define OMC_NMAX 128              /* token rows per grouped-GEMM work item (MMA N) */
@@ -139,6 +150,7 @@ typedef struct {
     uint16_t *hp;                 /* AOL f16 [Imax_pad/64][R][64]         */
     float *ypart;                 /* [T][k + 1][D]                        */
     float *hbuf;                  /* [T*k + T][Imax_pad] (GEMV path)      */
+    float *xg_r, *xg_e;           /* GEMMA: [T][D] router and expert inputs */
     int *err;                     /* [4] device error word                */
 } omc_ws;
 
@@ -148,7 +160,9 @@ typedef struct {
 int omc_launch_relayout(const int8_t *src, int O, int K, int8_t *dst, int O_pad, int K_pad, int member,
                         cudaStream_t s);
 int omc_launch_i8_to_f32(const int8_t *src, float *dst, long long n, cudaStream_t s);
-/* plan != NULL: the select kernel's last block also builds the dispatch plan */
+/* plan != NULL: the select kernel's last block also builds the dispatch plan
+ * (and, except for GEMMA, the logits kernel writes the f16 token operand
+ * ws->xh from x) */
 int omc_launch_router(const omc_layer_dev *L, const float *x, int T, const omc_ws *ws,
                       int32_t *topk_idx, float *topk_w, const omc_plan_args *plan, cudaStream_t s);
 /* fills the plan arguments of a tensor-core forward over workspace ws */
@@ -162,8 +176,14 @@ int omc_launch_test_wait(int *err, cudaStream_t s);
  * pieces) serves every T <= 8 of a layer on a grid of G CTAs */
 int omc_decode_state_size(const omc_layer_dev *L, int G, size_t *ctr_ints, size_t *part_floats);
 int omc_decode_supported(const omc_layer_dev *L, int T, int G, size_t ctr_ints, size_t part_floats);
-int omc_launch_decode(const omc_layer_dev *L, const float *x, int T, const omc_ws *ws, int G, int *ctr, float *part,
-                      int32_t *topk_idx, float *topk_w, float *out, cudaStream_t s);
+/* x = the experts' input rows, xr = the router's (the same pointer except
+ * for GEMMA) */
+int omc_launch_decode(const omc_layer_dev *L, const float *x, const float *xr, int T, const omc_ws *ws, int G, int *ctr,
+                      float *part, int32_t *topk_idx, float *topk_w, float *out, cudaStream_t s);
+/* GEMMA: router input xr, expert input xe (f32) and xh (f16 token operand)
+ * of residual rows x, each nullable; r [T] the norm factor (nullable) */
+int omc_launch_gemma_prenorm(const omc_layer_dev *L, const float *x, int T, float *xr, float *xe, uint16_t *xh,
+                             float *r, cudaStream_t s);
 long long omc_mma_work_items(const omc_layer_dev *L, int R);
 /* job-driven pass helpers: rows[r] = x[pos[r]]; out[s] += y[list[j]] over j in [off[s], off[s+1]) in order */
 int omc_launch_gather_rows(const float *x, const int *pos, int R, int S, int D, float *rows, int *err, cudaStream_t s);

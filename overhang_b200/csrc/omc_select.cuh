@@ -10,6 +10,10 @@
 //   renorm : engines/olmoe.c:363, engines/qwen.c:476-477 (float sum in
 //            selection order, then divide).
 //   shared gate: engines/qwen.c:460-461, sigmoid(logit row E).
+//   gemma  : engines/gemma.c:463-477 -- the float-sum softmax numerators e_i
+//            are ranked themselves (strict '>' from -1: ties to the lowest
+//            id), w_k = e_k/sum, renormalised by the float sum of the w_k in
+//            selection order, then times per_expert_scale[id].
 // Logits are read through L2 (ld.global.cg): they may have been written by
 // other blocks of the same kernel.
 #pragma once
@@ -25,6 +29,7 @@ constexpr int SEL_WARPS = 8;
 template <int SEL_MAXV>   // ceil(E / 32) rounded up to a power of two
 __device__ __forceinline__ void select_token(const float *__restrict__ logits, int ldl, int t, int E, int K,
                                              int family, int renorm, int has_shared,
+                                             const float *__restrict__ pes,
                                              int32_t *__restrict__ topk_idx, float *__restrict__ topk_w,
                                              float *__restrict__ sg, int *err, float *es) {
     const int lane = threadIdx.x & 31;
@@ -93,14 +98,16 @@ __device__ __forceinline__ void select_token(const float *__restrict__ logits, i
         for (; i < E; ++i) s = __fadd_rn(s, es[i]);
         sf = s;
     }
-    // probabilities as order keys: p >= 0, so bits(p) + 1 orders like p and
-    // 0 marks "not available" (outside E, NaN, or already taken).
+    // probabilities (gemma: the numerators) as order keys: p >= 0, so
+    // bits(p) + 1 orders like p and 0 marks "not available" (outside E, NaN,
+    // or already taken).
+    const bool gemma = family == OMC_FAMILY_GEMMA;
     uint32_t key[SEL_MAXV];
     float pv[SEL_MAXV];
 #pragma unroll
     for (int j = 0; j < SEL_MAXV; ++j) {
         const int i = lane + 32 * j;
-        pv[j] = i < E ? __fdiv_rn(v[j], sf) : 0.f;
+        pv[j] = i < E ? (gemma ? v[j] : __fdiv_rn(v[j], sf)) : 0.f;
         key[j] = (i < E && pv[j] == pv[j]) ? __float_as_uint(pv[j]) + 1u : 0u;
     }
     // top-k: engines/olmoe.c:355-362 -- largest p, ties to the lowest id
@@ -125,12 +132,15 @@ __device__ __forceinline__ void select_token(const float *__restrict__ logits, i
             my_val = __uint_as_float(kmax - 1u);
         }
     }
-    // renorm: float sum in selection order, then divide (engines/olmoe.c:363)
-    if (renorm || family == OMC_FAMILY_QWEN) {
+    if (gemma) my_val = __fdiv_rn(my_val, sf);   // tw[k] = bv/psum (engines/gemma.c:474)
+    // renorm: float sum in selection order, then divide (engines/olmoe.c:363,
+    // engines/gemma.c:474,477)
+    if (renorm || family == OMC_FAMILY_QWEN || gemma) {
         float sm = 0.f;
         for (int kk = 0; kk < K; ++kk) sm = __fadd_rn(sm, __shfl_sync(0xffffffffu, my_val, kk));
         my_val = __fdiv_rn(my_val, sm);
     }
+    if (gemma && lane < K && my_idx >= 0 && my_idx < E) my_val = __fmul_rn(my_val, __ldg(pes + my_idx));
     if (lane < K) {
         if (my_idx < 0 || my_idx >= E) omc_dev_error(err, OMC_DEVERR_ROUTE, OMC_SITE_ROUTER, t);
         topk_idx[(size_t)t * K + lane] = my_idx;

@@ -21,7 +21,8 @@
  *
  * Status codes are the reference's: 0 done, -1 allocation or device failure
  * (the engine then falls back to its CPU path), -3 a shape this build does
- * not serve (gelu_tanh, D or I not a multiple of 64, more than 1024 jobs).
+ * not serve (D or I not a multiple of 64, more than 1024 jobs).  gelu = 1 runs
+ * the experts with gelu_tanh (engines/gemma.c:319-321), as Gemma's call does.
  * omm_dense*: -3, the engines keep their CPU dense path. */
 #include <stdint.h>
 #include <stdlib.h>
@@ -123,7 +124,6 @@ static void *scratch(int i, size_t n) {
 }
 
 int omm_moe_act(const omm_job *jobs, int nj, const float *x, int S, int D, int I, float *out, int gelu) {
-    if (gelu) return -3;                       /* gelu_tanh (Gemma) is not served by this build */
     if (!omm_init()) return -1;
     if (nj <= 0 || S <= 0) return 0;
     if (!jobs || !x || !out || D <= 0 || I <= 0 || D % 64 || I % 64 || nj > OMC_MAX_E) return -3;
@@ -181,6 +181,10 @@ int omm_moe_act(const omm_job *jobs, int nj, const float *x, int S, int D, int I
     TL.desc.E = nj;
     TL.desc.k = 1;
     TL.dev.family = OMC_FAMILY_OLMOE;
+    /* rows are already the experts' input (the caller normed them);
+     * gelu != 0: gelu_tanh(g)*u (engines/gemma.c:319-321 via omm_moe_act,
+     * :628), else the SwiGLU of engines/olmoe.c:393 */
+    TL.dev.act = gelu ? OMC_ACT_GELU_TANH : OMC_ACT_SILU_DIV;
     TL.dev.D = D;
     TL.dev.I = I;
     TL.dev.E = nj;

@@ -239,7 +239,8 @@ __host__ __device__ constexpr int SEL_SMEM_FLOATS(int maxv) { return SEL_WARPS *
 template <int SEL_MAXV>
 __global__ void __launch_bounds__(SEL_WARPS * 32) router_select_kernel(const float *__restrict__ logits, int ldl, int T,
                                                                        int E, int K, int family, int renorm,
-                                                                       int has_shared, int32_t *__restrict__ topk_idx,
+                                                                       int has_shared, const float *__restrict__ pes,
+                                                                       int32_t *__restrict__ topk_idx,
                                                                        float *__restrict__ topk_w, float *__restrict__ sg,
                                                                        omc_plan_args plan, int do_plan, int *err) {
     // per-warp softmax rows, reused by the plan in the last block
@@ -248,7 +249,7 @@ __global__ void __launch_bounds__(SEL_WARPS * 32) router_select_kernel(const flo
     const int wib = threadIdx.x >> 5;
     const int t = blockIdx.x * SEL_WARPS + wib;
     if (t < T)
-        select_token<SEL_MAXV>(logits, ldl, t, E, K, family, renorm, has_shared, topk_idx, topk_w, sg, err,
+        select_token<SEL_MAXV>(logits, ldl, t, E, K, family, renorm, has_shared, pes, topk_idx, topk_w, sg, err,
                                sbuf + wib * SEL_MAXV * 32);
     if (!do_plan) return;
     // last-block handoff: every block's routing is visible to the block that counts last
@@ -337,7 +338,9 @@ extern "C" int omc_launch_router(const omc_layer_dev *L, const float *x, int T, 
         router_logits_small_kernel<<<(nrows + RS_ROWS - 1) / RS_ROWS, 256, small_smem, s>>>(
             x, T, L->D, L->router, L->router_i8 ? L->router_s : nullptr, L->E, L->sh_gate, nrows, ws->logits, ldl);
     } else {
-        const int rc = launch_logits(L, x, T, nrows, ws->logits, ldl, plan ? ws->xh : nullptr, s);
+        // GEMMA's expert operand is not the router's input: prenorm writes it
+        const int rc = launch_logits(L, x, T, nrows, ws->logits, ldl,
+                                     (plan && L->family != OMC_FAMILY_GEMMA) ? ws->xh : nullptr, s);
         if (rc) return rc;
     }
     omc_prof_mark(s, "router_logits");
@@ -348,7 +351,8 @@ extern "C" int omc_launch_router(const omc_layer_dev *L, const float *x, int T, 
     else memset(&pa, 0, sizeof(pa));
 #define SEL(NV)                                                                                                    \
     router_select_kernel<NV><<<g2, SEL_WARPS * 32, 0, s>>>(ws->logits, ldl, T, L->E, L->k, L->family, L->renorm, \
-                                                         L->has_shared, topk_idx, topk_w, ws->sg, pa, plan != nullptr, \
+                                                         L->has_shared, L->g_pes, topk_idx, topk_w, ws->sg, pa,   \
+                                                         plan != nullptr,                                         \
                                                          ws->err)
     if (nv <= 1) SEL(1);
     else if (nv <= 2) SEL(2);

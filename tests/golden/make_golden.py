@@ -25,6 +25,18 @@ Cases:
                 stream mode runs it: experts with the converter rule
                 (tools/convert_qwen.py:23-27), router and shared expert with
                 the engine's load-time rule (engines/qwen.c:124-138,283-288)
+  gemma_small   D=128 I=64 E=16 k=4, f32 router; x is the residual row
+  gemma_i8      D=128 I=32 E=24 k=8, int8 router (tools/convert_gemma.py:31-40)
+  gemma_ties    D=128 I=64 E=8 k=3, router rows duplicated -> tied softmax
+                numerators, broken by lower expert id (engines/gemma.c:468-475)
+  gemma_tiny_l0 / gemma_tiny_l5
+                the reference's own Gemma fixture (oracle/gemma_tiny,
+                tools/make_gemma_oracle.py) layers 0 and 5: its f32 router,
+                router.scale, per_expert_scale and pre_feedforward_layernorm_2;
+                its fused gate_up / down experts quantised with the converter
+                rule (tools/convert_gemma.py:35-40)
+For Gemma the oracle runs with the reference's powf (RSQRT_LIBM) so that it
+is bit-identical to the reference; ``eps`` holds rms_norm_eps.
 """
 import ctypes as C
 import os
@@ -51,6 +63,10 @@ def save(name, L, x, out_ref, extra=None):
                     np.int32)
     arrays = {k: v for k, v in L.arrays.items()}
     arrays.update(meta=meta, x=x, out_ref=out_ref, idx_ref=idx, w_ref=w)
+    if L.family == P.FAMILY_GEMMA:
+        ridx, rw = P.reference_route(L, x)
+        assert np.array_equal(ridx, idx) and bits_equal(rw, w), f"{name}: routing differs"
+        arrays.update(eps=np.array([L.eps], np.float32))
     if extra:
         arrays.update(extra)
     np.savez_compressed(os.path.join(HERE, f"golden_{name}.npz"), **arrays)
@@ -88,6 +104,70 @@ def tiny_layer(li):
     return L, R
 
 
+def gemma_tiny_layer(li):
+    R = P.ref_lib("gemma")
+    snap = os.path.join(REF_ROOT, "oracle", "gemma_tiny").encode()
+    R.ref_gemma_tiny_load(C.c_char_p(snap))
+    dims = (C.c_int * 6)()
+    eps = C.c_float()
+    R.ref_gemma_tiny_dims(dims, C.byref(eps))
+    D, E, K, MI = dims[0], dims[1], dims[2], dims[3]
+    assert dims[5] == 0, "gemma_tiny is expected f32-resident"
+    f = lambda *s: np.zeros(s, np.float32)  # noqa: E731
+    router, rscale, pes, enorm = f(E, D), f(D), f(E), f(D)
+    eg, ed = f(E, 2 * MI, D), f(E, D, MI)
+    vp = lambda a: a.ctypes.data_as(C.c_void_p)  # noqa: E731
+    rc = R.ref_gemma_tiny_weights(C.c_int(li), vp(router), vp(rscale), vp(pes), vp(enorm), vp(eg), vp(ed))
+    assert rc == 0, rc
+    L = P.Layer(P.FAMILY_GEMMA, D, MI, E, K, 1, 0, 0, 0, eps=eps.value, rsqrt_mode=P.RSQRT_LIBM)
+    a = L.arrays
+    a["router"], a["g_rscale"], a["g_pes"], a["g_enorm"] = router, rscale, pes, enorm
+    # the converter quantises the fused gate_up rows [2MI, D] as one matrix
+    q = [P.quantize_py(m) for m in eg]
+    gq, gsc = np.stack([t[0] for t in q]), np.stack([t[1] for t in q])
+    a["g"], a["u"] = np.ascontiguousarray(gq[:, :MI]), np.ascontiguousarray(gq[:, MI:])
+    a["gs"], a["us"] = np.ascontiguousarray(gsc[:, :MI]), np.ascontiguousarray(gsc[:, MI:])
+    q = [P.quantize_py(m) for m in ed]
+    a["d"], a["ds"] = np.stack([t[0] for t in q]), np.stack([t[1] for t in q])
+    return L, R
+
+
+def gemma_cases():
+    L = P.make_layer(P.FAMILY_GEMMA, 128, 64, 16, 4, seed=201)
+    L.rsqrt_mode = P.RSQRT_LIBM
+    x = P.normal(2001, (12, 128), 3.0)
+    save("gemma_small", L, x, P.reference_moe(L, x))
+
+    L = P.make_layer(P.FAMILY_GEMMA, 128, 32, 24, 8, seed=202, router_i8=1)
+    L.rsqrt_mode = P.RSQRT_LIBM
+    x = P.normal(2002, (10, 128), 0.5)
+    save("gemma_i8", L, x, P.reference_moe(L, x))
+
+    L = P.make_layer(P.FAMILY_GEMMA, 128, 64, 8, 3, seed=203)
+    L.rsqrt_mode = P.RSQRT_LIBM
+    r = L.arrays["router"]
+    r[5] = r[2]
+    r[6] = r[1]
+    x = P.normal(2003, (16, 128))
+    out = P.reference_moe(L, x)
+    _, idx, w = P.oracle_moe(L, x)
+    ties = sum(int(idx[t, j] in (1, 2) and idx[t, j + 1] in (5, 6)) for t in range(16) for j in range(2))
+    assert ties > 0, "tie case produced no tied selections"
+    save("gemma_ties", L, x, out)
+
+    for li in (0, 5):
+        L, R = gemma_tiny_layer(li)
+        x = P.normal(2100 + li, (8, L.D), 2.0)
+        out = P.reference_moe(L, x)
+        ti = np.zeros((8, L.k), np.int32)
+        tw = np.zeros((8, L.k), np.float32)
+        R.ref_gemma_tiny_route(C.c_int(li), x.ctypes.data_as(C.c_void_p), C.c_int(8),
+                               ti.ctypes.data_as(C.c_void_p), tw.ctypes.data_as(C.c_void_p))
+        ridx, rw = P.reference_route(L, x)
+        assert np.array_equal(ti, ridx) and bits_equal(tw, rw), "fixture routing differs from its arrays"
+        save(f"gemma_tiny_l{li}", L, x, out)
+
+
 def main():
     assert P.ref_available(), "build oracle/_ref first (make -C oracle)"
     L = P.make_layer(P.FAMILY_OLMOE, 128, 64, 8, 2, seed=101)
@@ -122,6 +202,8 @@ def main():
         R.ref_qwen_tiny_moe(C.c_int(li), x.ctypes.data_as(C.c_void_p), C.c_int(x.shape[0]),
                             f32.ctypes.data_as(C.c_void_p))
         save(f"qwen_tiny_l{li}", L, x, out, {"out_ref_f32_resident": f32})
+
+    gemma_cases()
 
 
 if __name__ == "__main__":
