@@ -19,9 +19,11 @@ Arms
       collective).  --mode ep: expert parallel -- each rank holds E/N of the
       layer's experts and brings its own 512 tokens; routed rows go to their
       experts' ranks and back with all_to_all over NCCL (overhang_b200.ep).
-  reference: the reference's own CPU MoE (engines/olmoe.c moe(), compiled from
-      its sources into oracle/_ref by oracle/Makefile) on all host cores, each
-      step a bounded token sample; rank 0 only.
+  reference: the reference's own CPU MoE (engines/olmoe.c moe(), or the
+      workload family's: engines/qwen.c moe_step(), engines/gemma.c route_token
+      + expert union; compiled from its sources into oracle/_ref by
+      oracle/Makefile) on all host cores, each step a bounded token sample;
+      rank 0 only.
 """
 from __future__ import annotations
 
@@ -41,7 +43,7 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 D, I, E, K, T = 2048, 1024, 64, 8, 512
-FAMILY, IS = "olmoe", 0                              # layer family, shared-expert width
+FAMILY, IS, RI8 = "olmoe", 0, 0                      # layer family, shared-expert width, int8 router
 SEED_W, SEED_X = 1, 4242
 METRIC, UNIT = "MoE-block tokens/s", "tokens/s"
 WORKLOAD = "olmoe_layer_prefill_T512"
@@ -57,22 +59,30 @@ CONFIG = {"workload": WORKLOAD, "D": D, "I": I, "E": E, "k": K, "T": T,
 #   qwen_decode    the same, T=1 (C2 decode)
 #   olmoe_decode64 / qwen_decode64   one decode step of 64 sequences (T=64), the batched
 #                  decode of the next-steps row; run it with --graph (CUDA graph replay)
+#   gemma_prefill / gemma_decode / gemma_decode64   a Gemma-4-26B-A4B-shaped layer
+#                  (D=2816, 128 experts, top-8, moe_intermediate 704, int8 router;
+#                  x is the residual row), T=2048 / 1 / 64
 WORKLOADS = {
     "olmoe_prefill": ("olmoe", 512), "olmoe_decode": ("olmoe", 1),
     "qwen_prefill": ("qwen", 2048), "qwen_decode": ("qwen", 1),
     "olmoe_decode64": ("olmoe", 64), "qwen_decode64": ("qwen", 64),
+    "gemma_prefill": ("gemma", 2048), "gemma_decode": ("gemma", 1), "gemma_decode64": ("gemma", 64),
 }
+REF_FN = {"olmoe": "engines/olmoe.c moe()", "qwen": "engines/qwen.c moe_step()",
+          "gemma": "engines/gemma.c route_token() + expert union"}
 
 
 def set_workload(name, tokens=None):
-    global D, I, E, K, T, FAMILY, IS, SEED_W, WORKLOAD, EXPERT_BYTES, CONFIG
+    global D, I, E, K, T, FAMILY, IS, RI8, SEED_W, WORKLOAD, EXPERT_BYTES, CONFIG
     FAMILY, T = WORKLOADS[name]
     if tokens:
         T = tokens
     if FAMILY == "olmoe":
-        D, I, E, K, IS, SEED_W = 2048, 1024, 64, 8, 0, 1
+        D, I, E, K, IS, RI8, SEED_W = 2048, 1024, 64, 8, 0, 0, 1
+    elif FAMILY == "gemma":
+        D, I, E, K, IS, RI8, SEED_W = 2816, 704, 128, 8, 0, 1, 3
     else:
-        D, I, E, K, IS, SEED_W = 2048, 512, 256, 8, 512, 2
+        D, I, E, K, IS, RI8, SEED_W = 2048, 512, 256, 8, 512, 1, 2
     EXPERT_BYTES = 3 * D * I + 4 * (2 * I + D)
     kind = "decode" if (T == 1 or "decode" in name) else "prefill"
     WORKLOAD = f"{FAMILY}_layer_{kind}_T{T}"
@@ -83,6 +93,9 @@ def set_workload(name, tokens=None):
               "l2": f"expert weights {total / 1e6:.0f} MB > 126 MB L2 stream from HBM every step"}
     if IS:
         CONFIG.update(shared_expert_I=IS, router="int8 + f32 scale", renorm=1)
+    if FAMILY == "gemma":
+        CONFIG.update(router="int8 + f32 scale (N(0,1) before quantisation)", renorm=1,
+                      activation="gelu_tanh", x="f32 N(0,1) residual rows seed 4242, 8 rotating batches")
 
 
 def env_rank():
@@ -219,6 +232,8 @@ def make_layer():
     import pyoracle
     if FAMILY == "qwen":
         return pyoracle, pyoracle.qwen_layer(SEED_W, D=D, I=I, E=E, k=K, Is=IS)
+    if FAMILY == "gemma":
+        return pyoracle, pyoracle.gemma_layer(SEED_W, D=D, I=I, E=E, k=K)
     return pyoracle, pyoracle.olmoe_layer(SEED_W, D=D, I=I, E=E, k=K)
 
 
@@ -228,7 +243,7 @@ def cpu_reference_tokens_per_s(pyoracle, L, budget_s, kind_pref="reference"):
     cores = os.cpu_count() or 1
     os.environ.setdefault("OMP_NUM_THREADS", str(cores))
     fn, kind = None, "port"
-    if kind_pref == "reference" and pyoracle.ref_lib("olmoe") is not None:
+    if kind_pref == "reference" and pyoracle.ref_lib(FAMILY) is not None:
         fn, kind = (lambda xx: pyoracle.reference_moe(L, xx)), "reference"
     else:
         fn = lambda xx: pyoracle.oracle_moe(L, xx)[0]  # noqa: E731
@@ -255,7 +270,7 @@ def run_reference(args):
     pyoracle, L = make_layer()
     cores = os.cpu_count() or 1
     os.environ.setdefault("OMP_NUM_THREADS", str(cores))
-    if pyoracle.ref_lib("olmoe") is not None:
+    if pyoracle.ref_lib(FAMILY) is not None:
         kind, fn = "reference", (lambda xx: pyoracle.reference_moe(L, xx))
     else:
         kind, fn = "port", (lambda xx: pyoracle.oracle_moe(L, xx)[0])
@@ -280,7 +295,7 @@ def run_reference(args):
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic", "config": dict(CONFIG, sample_tokens_per_step=n),
             "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": kind,
-                             "sample": f"{n} of {T} tokens per step, engines/olmoe.c moe() "
+                             "sample": f"{n} of {T} tokens per step, {REF_FN[FAMILY]} "
                                        f"OpenMP on {cores} threads"},
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -453,7 +468,8 @@ def run_ours(args):
     shared_w = (2 * IS * D + 2 * IS * 4) if IS else 0          # the shared expert's gate+up
     srows = T if IS else 0
     # the whole step's weight bytes (every active expert + shared + router) over the step time
-    router_bytes = E * D * (1 if IS else 4) + (4 * E if IS else 0) + (4 * D if IS else 0)
+    router_bytes = (E * D * (1 if RI8 else 4) + (4 * E if RI8 else 0) + (4 * D if IS else 0)
+                    + (2 * 4 * D + 4 * E if FAMILY == "gemma" else 0))
     step_bytes = n_active * EXPERT_BYTES + (3 * D * IS + 4 * (2 * IS + D) if IS else 0) + router_bytes
     # one GPU's algorithmic FLOP per step (per token: k experts' three projections, the
     # router, and the shared expert with its gate)
@@ -494,7 +510,7 @@ def run_ours(args):
         tps, n, kind, cores, dt = cpu_reference_tokens_per_s(pyoracle, L, args.cpu_seconds)
         line["cpu_baseline"] = {"value": tps, "unit": UNIT, "cores": cores, "kind": kind,
                                 "sample": f"{n} of {T} tokens per call for {dt:.1f} s, "
-                                          f"engines/olmoe.c moe() OpenMP"}
+                                          f"{REF_FN[FAMILY]} OpenMP"}
     if rank == 0:
         print(json.dumps(line), flush=True)
     ob.shutdown()

@@ -310,8 +310,10 @@ def reference_moe(L: Layer, x: np.ndarray) -> np.ndarray:
         R = ref_lib("gemma")
         if R is None:
             raise RuntimeError("oracle/_ref not built")
-        gq = np.ascontiguousarray(np.concatenate([a["g"], a["u"]], axis=1))     # [E, 2I, D]
-        gsc = np.ascontiguousarray(np.concatenate([a["gs"], a["us"]], axis=1))  # [E, 2I]
+        if "_gate_up" not in a:      # the container's fused gate_up layout, built once
+            a["_gate_up"] = np.ascontiguousarray(np.concatenate([a["g"], a["u"]], axis=1))     # [E, 2I, D]
+            a["_gate_up_s"] = np.ascontiguousarray(np.concatenate([a["gs"], a["us"]], axis=1))  # [E, 2I]
+        gq, gsc = a["_gate_up"], a["_gate_up_s"]
         rs = a.get("router_s")
         rc = R.ref_gemma_moe(C.c_int(L.D), C.c_int(L.E), C.c_int(L.k), C.c_int(L.I), C.c_float(L.eps),
                              C.c_int(L.router_i8), vp("router"),

@@ -61,7 +61,7 @@ def save(name, L, x, out_ref, extra=None):
     assert bits_equal(o, out_ref), f"{name}: oracle differs from the reference"
     meta = np.array([L.family, L.D, L.I, L.E, L.k, L.renorm, L.router_i8, L.has_shared, L.Is],
                     np.int32)
-    arrays = {k: v for k, v in L.arrays.items()}
+    arrays = {k: v for k, v in L.arrays.items() if not k.startswith("_")}
     arrays.update(meta=meta, x=x, out_ref=out_ref, idx_ref=idx, w_ref=w)
     if L.family == P.FAMILY_GEMMA:
         ridx, rw = P.reference_route(L, x)
