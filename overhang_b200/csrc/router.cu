@@ -32,10 +32,13 @@ namespace {
 // (launch_logits): 2 x 2 chains per thread with 64-element chunks once the
 // grid fills the SMs, else one chain per thread with 128-element chunks, so
 // that three chunks of chain work cover a chunk's L2 latency.
-constexpr int RT_ST = 4;                    // stages
+constexpr int RT_ST = 4;                    // stages (8 measured no faster, and halves occupancy)
 
 template <int G, int TT, int RR, int KC>
 constexpr size_t rt_smem() { return (size_t)RT_ST * (G * TT + G * RR) * (KC + 4) * sizeof(float); }
+static_assert(rt_smem<16, 4, 4, 32>() <= 200 * 1024 && rt_smem<16, 2, 2, 64>() <= 200 * 1024 &&
+                  rt_smem<16, 1, 1, 128>() <= 200 * 1024,
+              "router staging");
 
 __device__ __forceinline__ void cp_async16(void *smem_dst, const void *gsrc, bool valid) {
     const uint32_t d = smem_u32(smem_dst);
@@ -302,10 +305,28 @@ int launch_logits(const omc_layer_dev *L, const float *x, int T, int nrows, floa
     case 811: return launch_tile<8, 1, 1, 128>(L, x, T, nrows, logits, ldl, xh, s);
     default: break;
     }
-    // Measured on B200 (logits stage, OLMoE T=512 and Qwen T=2048): 2 x 2 chains
-    // per thread beat 4 x 4 and 2 x 4 once the grid fills the SMs; below that,
-    // one chain per thread on 16 x 16 threads beat the 8 x 8-thread tiles.
-    if (blocks(16, 2, 2) >= want) return launch_tile<16, 2, 2, 64>(L, x, T, nrows, logits, ldl, xh, s);
+    // Measured on B200 (logits stage in us, every tile forced; OLMoE D=2048
+    // E=64, Gemma D=2816 E=128, Qwen D=2048 E=256+1):
+    //                 16x4x4  16x2x2  16x1x1  8x1x1  8x2x2  16x2x1
+    //   OLMoE  T=512    137      55      31     35     51      45
+    //   OLMoE  T=2048   137      56      84     88     60      63
+    //   OLMoE  T=8192   145     158     227    301    172     192
+    //   Gemma  T=512    176      72      53     74     58      53
+    //   Gemma  T=2048   176     104     156    198    135     144
+    //   Gemma  T=8192   292     326     592    768    411     484
+    //   Qwen   T=2048   219     148     230    287    174     202
+    // (8x2x2 and 16x2x1 are not built: never the fastest.  Neither were a
+    // lane-per-router-row kernel with broadcast token reads, nor 8-stage
+    // staging; ncu on 16x1x1 at T=512: 2 warps per scheduler, ~6 issued
+    // instructions per chain step, each waiting ~4.6 cycles on the add chain
+    // and shared-memory loads.)
+    // A 64 x 64 tile wins once its blocks make one nearly full wave (or
+    // enough waves that the last one's tail is small); else 32 x 32 once
+    // those fill the SMs; else one chain per thread.
+    const long long b44 = blocks(16, 4, 4);
+    if (10 * b44 >= 8 * want && (b44 <= want || 10 * b44 >= 16 * want))
+        return launch_tile<16, 4, 4, 32>(L, x, T, nrows, logits, ldl, xh, s);
+    if (10 * blocks(16, 2, 2) >= 8 * want) return launch_tile<16, 2, 2, 64>(L, x, T, nrows, logits, ldl, xh, s);
     return launch_tile<16, 1, 1, 128>(L, x, T, nrows, logits, ldl, xh, s);
 }
 
