@@ -341,10 +341,13 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_gemm_kernel(const GemmArgs a)
         }
     } else if (warp == 1) {
         // ------------------------------------------------ MMA issuer
-        // The whole warp runs the loop (operands warp-uniform) and one elected
-        // lane issues each instruction: issued from a lane-0-only branch,
-        // every tcgen05.mma cost the issuing thread ~110 cycles, against the
-        // 40 cycles an M=128 N=80 MMA takes on the tensor core.
+        // The whole warp runs the loop (operands warp-uniform); one elected
+        // lane issues a K block's eight MMAs back to back.  Measured with
+        // clock64 stamps (OLMoE T=512): an elect + __syncwarp around every MMA
+        // cost ~73 cycles an MMA and made this warp the pipeline's bottleneck
+        // (one K block per ~1,020 cycles); one elect per block issues the
+        // eight in ~330 cycles, and the block period falls to ~960 cycles,
+        // now set by the dequant group.
         uint32_t i = 0;
         AccSlots acc;
         for (int idx = blockIdx.x; idx < nitems && !*abort_flag; idx += gridDim.x) {
@@ -369,16 +372,17 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_gemm_kernel(const GemmArgs a)
                 tc_fence_after();
                 const uint64_t bd = tc_sdesc_k_sw128(smem_u32(smem + OFF_A + sa * A_BYTES));
                 const uint32_t acol = tmem + TCOL_A + (uint32_t)st * 64u;
+                // the block's MMAs (K = 16 each: +32 B along K is +2 in the smem
+                // descriptor, +8 TMEM columns) from one elected lane, back to back
+                if (elect_one()) {
 #pragma unroll
-                for (int k16 = 0; k16 < 4; ++k16) {   // +32 B along K: +2 in the smem descriptor, +8 TMEM columns
-                    const uint32_t accum = (kb > 0 || k16 > 0) ? 1u : 0u;
-                    if (elect_one()) tc_mma_ts(d0, acol + 8u * k16, bd + 2 * k16, idesc, accum);
-                    __syncwarp();
-                    if (nmat > 1) {
-                        if (elect_one()) tc_mma_ts(d1, acol + 32u + 8u * k16, bd + 2 * k16, idesc, accum);
-                        __syncwarp();
+                    for (int k16 = 0; k16 < 4; ++k16) {
+                        const uint32_t accum = (kb > 0 || k16 > 0) ? 1u : 0u;
+                        tc_mma_ts(d0, acol + 8u * k16, bd + 2 * k16, idesc, accum);
+                        if (nmat > 1) tc_mma_ts(d1, acol + 32u + 8u * k16, bd + 2 * k16, idesc, accum);
                     }
                 }
+                __syncwarp();
                 if (elect_one()) {
                     tc_commit(&emptyA[sa]);
                     tc_commit(&emptyT[st]);
