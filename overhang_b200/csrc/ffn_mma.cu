@@ -64,7 +64,7 @@ constexpr int NMAX = OMC_NMAX;            // tokens per work item (MMA N)
 constexpr int NGRP = 2;                   // dequant groups (alternate K blocks)
 constexpr int NDQ = 8;                    // warps per dequant group: 2 tiles x 4 lane quarters
 constexpr int NEPI = 8;                   // epilogue warps: two per TMEM lane quarter
-constexpr int SA = 4;                     // token-tile ring (smem)
+constexpr int SA = 5;                     // token-tile ring (smem)
 constexpr int ST = 3;                     // weight A stages (TMEM)
 constexpr int SI = 6;                     // int8 ring (smem)
 constexpr int WARP_DQ0 = 2;
