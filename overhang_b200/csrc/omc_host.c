@@ -721,8 +721,11 @@ static int forward_on_ws(omc_layer *L, const omc_ws *ws, const float *x, int T, 
     const int mma = use_mma(L, T);
     omc_plan_args plan;
     if (mma) {
+        /* the per-expert counts (counted by the select blocks) and the
+         * select-done counter start at zero: counts, offsets, done are one
+         * run of ints in the workspace */
         omc_plan_setup(&L->dev, T, ws, &plan);
-        CK(cudaMemsetAsync(ws->done, 0, sizeof(int), s));
+        CK(cudaMemsetAsync(ws->counts, 0, (size_t)(ws->done - ws->counts + 1) * sizeof(int), s));
     }
     /* GEMMA: x is the residual; the router and the experts each read their
      * own norm of it (prenorm.cu).  The tensor-core path takes the experts'

@@ -15,20 +15,28 @@ constexpr int OMC_PLAN_SMEM_INTS = 4 * (OMC_MAX_E + 2);
 
 // Run by every thread of one block (any size that is a multiple of 32).
 // topk_idx [T][K] must be visible to the block.  smem: OMC_PLAN_SMEM_INTS.
+//
+// counted = false: the block also counts the routed slots per expert (their
+// ranks into p.slotrow) and writes every operand row's slot and weight; one
+// block does all of it (the explicit-rows pass).  counted = true: the router's
+// select blocks have counted already (p.counts[e] = routed rows of e, every
+// slot's rank in p.slotrow, one global atomic per slot), and the rows are
+// written afterwards by omc_plan_fill_rows over all slots; the block does the
+// scans, the offsets, the work lists and the padding rows.
 __device__ inline void omc_plan_block(const omc_plan_args &p, const int32_t *__restrict__ topk_idx,
-                                      const float *__restrict__ topk_w, int *err, int *smem) {
+                                      const float *__restrict__ topk_w, int *err, int *smem, bool counted = false) {
     int *s_cnt = smem, *s_off = s_cnt + (OMC_MAX_E + 2), *s_w1 = s_off + (OMC_MAX_E + 2),
         *s_w2 = s_w1 + (OMC_MAX_E + 2);
     const int tid = threadIdx.x, nt = blockDim.x, lane = tid & 31;
     const int E = p.E, G = E + (p.has_shared ? 1 : 0), nslots = p.T * p.K;
-    for (int g = tid; g < G; g += nt) s_cnt[g] = (g < E || p.rows_mode) ? 0 : p.T;
+    for (int g = tid; g < G; g += nt) s_cnt[g] = (g < E || p.rows_mode) ? (counted ? __ldcg(p.counts + g) : 0) : p.T;
     __syncthreads();
     // rank of each routed slot within its expert (arrival order; the rows of
     // an expert are independent, so their order does not change any value).
     // Loads go out 8 at a time: one L2 round trip per 8 slots, not per slot.
     // The gather adds the expert's row offset.
     int *__restrict__ rank = p.slotrow;
-    for (int base = tid; base < nslots; base += 8 * nt) {
+    for (int base = tid; !counted && base < nslots; base += 8 * nt) {
         int e[8];
 #pragma unroll
         for (int u = 0; u < 8; ++u) {
@@ -115,7 +123,7 @@ __device__ inline void omc_plan_block(const omc_plan_args &p, const int32_t *__r
     }
     // operand rows: routed slot s -> row offsets[e] + rank, with its slot and
     // routing weight (the same thread wrote rank[s] above)
-    for (int base = tid; base < nslots; base += 8 * nt) {
+    for (int base = tid; !counted && base < nslots; base += 8 * nt) {
         int e[8], rk[8];
         float w[8];
 #pragma unroll
@@ -134,7 +142,7 @@ __device__ inline void omc_plan_block(const omc_plan_args &p, const int32_t *__r
             p.roww[row] = w[u];
         }
     }
-    if (p.has_shared && !p.rows_mode)       // the shared expert: token t at row offsets[E] + t, weight 1
+    if (p.has_shared && !p.rows_mode && !counted)   // the shared expert: token t at row offsets[E] + t, weight 1
         for (int t = tid; t < p.T; t += nt) {
             p.rowinfo[s_off[E] + t] = nslots + t;
             p.roww[s_off[E] + t] = 1.f;
@@ -144,4 +152,26 @@ __device__ inline void omc_plan_block(const omc_plan_args &p, const int32_t *__r
             p.rowinfo[r] = -1;
             p.roww[r] = 0.f;
         }
+}
+
+// The row pass of a counted plan, one thread per routed slot (then one per
+// token for the shared expert): row offsets[e] + rank gets the slot and its
+// routing weight.  Rows past the capacity are skipped (the plan reported the
+// overflow and queued no work).
+static __global__ void __launch_bounds__(256) omc_plan_fill_rows(omc_plan_args p, const int32_t *__restrict__ topk_idx,
+                                                          const float *__restrict__ topk_w) {
+    const int nslots = p.T * p.K, i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < nslots) {
+        const int e = topk_idx[i], rk = p.slotrow[i];
+        if (rk < 0 || e < 0 || e >= p.E) return;
+        const int row = p.offsets[e] + rk;
+        if (row >= p.R_cap) return;
+        p.rowinfo[row] = i;
+        p.roww[row] = topk_w[i];
+    } else if (p.has_shared && i < nslots + p.T) {
+        const int t = i - nslots, row = p.offsets[p.E] + t;
+        if (row >= p.R_cap) return;
+        p.rowinfo[row] = nslots + t;
+        p.roww[row] = 1.f;
+    }
 }

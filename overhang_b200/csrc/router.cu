@@ -255,6 +255,14 @@ __global__ void __launch_bounds__(SEL_WARPS * 32) router_select_kernel(const flo
         select_token<SEL_MAXV>(logits, ldl, t, E, K, family, renorm, has_shared, pes, topk_idx, topk_w, sg, err,
                                sbuf + wib * SEL_MAXV * 32);
     if (!do_plan) return;
+    // count the routed slots per expert here, one global atomic per slot:
+    // its rank is its row within the expert's group (arrival order; an
+    // expert's rows are independent, so the order changes no value)
+    if (t < T && (threadIdx.x & 31) < K) {
+        const int s = t * K + (threadIdx.x & 31);
+        const int e = topk_idx[s];   // this thread's own write in select_token
+        plan.slotrow[s] = (e >= plan.e_lo && e < plan.e_hi) ? atomicAdd(plan.counts + e, 1) : -1;
+    }
     // last-block handoff: every block's routing is visible to the block that counts last
     __threadfence();
     __syncthreads();
@@ -262,7 +270,7 @@ __global__ void __launch_bounds__(SEL_WARPS * 32) router_select_kernel(const flo
     __syncthreads();
     if (!s_last) return;
     __threadfence();
-    omc_plan_block(plan, topk_idx, topk_w, err, reinterpret_cast<int *>(sbuf));
+    omc_plan_block(plan, topk_idx, topk_w, err, reinterpret_cast<int *>(sbuf), true);
 }
 
 template <int G, int TT, int RR, int KC>
@@ -383,6 +391,11 @@ extern "C" int omc_launch_router(const omc_layer_dev *L, const float *x, int T, 
     else SEL(32);
 #undef SEL
     omc_g_launches += 2;
+    if (plan) {
+        const int nfill = T * L->k + (L->has_shared ? T : 0);
+        omc_plan_fill_rows<<<(nfill + 255) / 256, 256, 0, s>>>(pa, topk_idx, topk_w);
+        omc_g_launches += 1;
+    }
     return cudaGetLastError() == cudaSuccess ? 0 : OMC_ECUDA;
 }
 
