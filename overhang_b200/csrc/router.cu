@@ -131,14 +131,27 @@ __global__ void __launch_bounds__(G * G, 2) router_tile_kernel(const float *__re
                 }
             }
         }
-#pragma unroll 2
+        // operands of the next four K elements are loaded before this
+        // four's chain steps, so a shared-memory load's latency is not on
+        // the add chain
+        float4 xv[TT], wv[RR], xn[TT], wn[RR];
+#pragma unroll
+        for (int i = 0; i < TT; ++i) xn[i] = *reinterpret_cast<const float4 *>(st + (tg + G * i) * LD);
+#pragma unroll
+        for (int j = 0; j < RR; ++j) wn[j] = *reinterpret_cast<const float4 *>(st + (BT + rg + G * j) * LD);
+#pragma unroll 4
         for (int kk = 0; kk < KC; kk += 4) {
-            float4 xv[TT], wv[RR];
 #pragma unroll
-            for (int i = 0; i < TT; ++i) xv[i] = *reinterpret_cast<const float4 *>(st + (tg + G * i) * LD + kk);
+            for (int i = 0; i < TT; ++i) xv[i] = xn[i];
 #pragma unroll
-            for (int j = 0; j < RR; ++j)
-                wv[j] = *reinterpret_cast<const float4 *>(st + (BT + rg + G * j) * LD + kk);
+            for (int j = 0; j < RR; ++j) wv[j] = wn[j];
+            if (kk + 4 < KC) {
+#pragma unroll
+                for (int i = 0; i < TT; ++i) xn[i] = *reinterpret_cast<const float4 *>(st + (tg + G * i) * LD + kk + 4);
+#pragma unroll
+                for (int j = 0; j < RR; ++j)
+                    wn[j] = *reinterpret_cast<const float4 *>(st + (BT + rg + G * j) * LD + kk + 4);
+            }
 #pragma unroll
             for (int sk = 0; sk < 4; ++sk) {
                 const float *xs = reinterpret_cast<const float *>(xv);   // xv[i] component sk: xs[4i + sk]
