@@ -18,8 +18,15 @@
  *                                         are matched to their HBM copy by slot
  *                                         pointer; a slot whose scale rows
  *                                         changed (LRU refill) is re-uploaded.
- *   omm_dense_q / omm_dense               not served here: return -3, and the
- *                metal/om_metal.h:38-46   engines keep their CPU path.
+ *   omm_dense_q  metal/om_metal.h:38-41   out[S,N] = x[S,K] . dequant(Wq)^T on
+ *                                         the tensor-core GEMM; the int8 matrix
+ *                                         is copied to HBM once and found by
+ *                                         pointer (again if its scales change);
+ *                                         K % 64 or N % 32: -3, as the reference.
+ *   omm_dense    metal/om_metal.h:43-46   out[S,N] = x[S,K] . W^T: a half copy
+ *                                         of the f32 W made on first use (as the
+ *                                         reference does), f32 accumulation
+ *                                         (cuBLAS); K % 8: -3.
  *
  * Return codes follow metal/om_metal.mm: 0 ok, -1 allocation failure,
  * -2 pointer not from omm_alloc, -3 unsupported shape.

@@ -679,6 +679,49 @@ extern "C" long long omc_mma_work_items(const omc_layer_dev *L, int R) {
     return chunks_max * (Imax_rows / OMC_TM) + chunks_max * ((L->D_rows / OMC_TM + 1) / 2);
 }
 
+// Dense pass (omm_dense_q): the operand rows are the S input rows in order.
+// Writes rowinfo/roww (row r < S is slot r with weight 1, padding rows -1),
+// the f16 operand of the down GEMM in the AOL layout (element (r, k) at
+// (k/64)*R*128 + r*128 + ((k%64)/8 ^ (r&7))*16 + (k%8)*2; columns >= K and
+// rows >= S zero) and the work items (matrix 0, row-tile pair p, 128-row
+// chunks of the Sp padded rows).
+__global__ void __launch_bounds__(256) dense_prep_kernel(const float *__restrict__ x, int S, int K, int K_pad, int Sp,
+                                                         int R, uint16_t *__restrict__ act, int *__restrict__ rowinfo,
+                                                         float *__restrict__ roww, int4 *__restrict__ work,
+                                                         int *__restrict__ nwork, int npairs) {
+    const int stride = gridDim.x * blockDim.x, tid0 = blockIdx.x * blockDim.x + threadIdx.x;
+    for (int r = tid0; r < Sp; r += stride) {
+        rowinfo[r] = r < S ? r : -1;
+        roww[r] = r < S ? 1.f : 0.f;
+    }
+    const long long nck = (long long)Sp * (K_pad / 8);
+    for (long long i = tid0; i < nck; i += stride) {
+        const int r = (int)(i % Sp), kc = (int)(i / Sp), k0 = kc * 8, kb = k0 >> 6, c = (k0 & 63) >> 3;
+        uint4 o = make_uint4(0u, 0u, 0u, 0u);
+        if (r < S && k0 < K) {
+            const float4 a = *reinterpret_cast<const float4 *>(x + (size_t)r * K + k0);
+            const float4 b = *reinterpret_cast<const float4 *>(x + (size_t)r * K + k0 + 4);
+            o.x = f32x2_to_f16x2_sat(a.x, a.y);
+            o.y = f32x2_to_f16x2_sat(a.z, a.w);
+            o.z = f32x2_to_f16x2_sat(b.x, b.y);
+            o.w = f32x2_to_f16x2_sat(b.z, b.w);
+        }
+        *reinterpret_cast<uint4 *>(reinterpret_cast<uint8_t *>(act) + (size_t)kb * R * 128 + (size_t)r * 128 +
+                                   ((c ^ (r & 7)) << 4)) = o;
+    }
+    if (blockIdx.x == 0) {
+        const int nch = (Sp + NMAX - 1) / NMAX;
+        for (int j = threadIdx.x; j < nch * npairs; j += blockDim.x) {
+            const int ch = j / npairs, p = j - ch * npairs, n0 = ch * NMAX;
+            work[j] = make_int4(0, p, n0, min(NMAX, Sp - n0));
+        }
+        if (threadIdx.x == 0) {
+            nwork[0] = 0;
+            nwork[1] = nch * npairs;
+        }
+    }
+}
+
 // Once per process: the GEMM's shared-memory attribute and the SM count.
 static int gemm_setup() {
     static int attr_done = 0;
@@ -865,6 +908,54 @@ extern "C" int omc_launch_ordered_add(float *out, const float *y, const int *off
                                       cudaStream_t s) {
     if (S <= 0) return 0;
     ordered_add_kernel<<<dim3((D / 4 + 255) / 256, S), 256, 0, s>>>(out, y, off, list, S, D);
+    omc_g_launches += 1;
+    return cudaGetLastError() == cudaSuccess ? 0 : OMC_ECUDA;
+}
+
+// y[S][N] = x[S][K] . (ds * Wd)^T for the one-matrix layer L (its expert 0's
+// down matrix, D = N output rows, I = K): the down GEMM with every row its own
+// slot (ydirect) and weight 1.  x is f32 [S][K] on the device (K % 64 == 0),
+// y f32 [S][N]; the workspace was sized for S rows.
+extern "C" int omc_launch_dense_i8(const omc_layer_dev *L, const float *x, int S, const omc_ws *ws, float *y,
+                                   cudaStream_t s) {
+    if (S <= 0) return 0;
+    if (gemm_setup()) return OMC_ECUDA;
+    const int Sp = (S + OMC_ROW_ALIGN - 1) / OMC_ROW_ALIGN * OMC_ROW_ALIGN;
+    if (Sp > ws->R_cap || (L->I % 64) || L->E != 1) return OMC_EINVAL;
+    const int npairs = (L->D_rows / OMC_TM + 1) / 2;
+    const long long nck = (long long)Sp * (L->I_pad / 8);
+    const int blocks = (int)((nck + 255) / 256 < 2048 ? (nck + 255) / 256 : 2048);
+    dense_prep_kernel<<<blocks, 256, 0, s>>>(x, S, L->I, L->I_pad, Sp, ws->R_cap, ws->hp, ws->rowinfo, ws->roww,
+                                             reinterpret_cast<int4 *>(ws->work), ws->nwork, npairs);
+    GemmArgs ga;
+    ga.L = *L;
+    ga.work = reinterpret_cast<const int4 *>(ws->work);
+    ga.nwork = ws->nwork;
+    ga.act = ws->hp;
+    ga.xh = nullptr;
+    ga.hout = ws->hp;
+    ga.ypart = y;
+    ga.rowinfo = ws->rowinfo;
+    ga.roww = ws->roww;
+    ga.K = 1;
+    ga.nrouted = S;
+    ga.ydirect = 1;
+    ga.T = S;
+    ga.R = ws->R_cap;
+    ga.err = ws->err;
+    const int grid = g_num_sms > 0 ? g_num_sms : 148;
+    moe_gemm_kernel<2><<<grid, NTHREADS, SMEM_BYTES, s>>>(ga);
+    omc_g_launches += 2;
+    return cudaGetLastError() == cudaSuccess ? 0 : OMC_ECUDA;
+}
+
+// dst[i] = f16(src[i]) (round to nearest, saturated) for n a multiple of 8,
+// both 16-byte aligned.
+extern "C" int omc_launch_f32_to_f16(const float *src, long long n, uint16_t *dst, cudaStream_t s) {
+    if (n <= 0) return 0;
+    if (n % 8) return OMC_EINVAL;
+    const long long n8 = n / 8;
+    rows_to_f16_kernel<<<(int)((n8 + 255) / 256 < 4096 ? (n8 + 255) / 256 : 4096), 256, 0, s>>>(src, n8, dst);
     omc_g_launches += 1;
     return cudaGetLastError() == cudaSuccess ? 0 : OMC_ECUDA;
 }

@@ -384,6 +384,24 @@ int omc_expert_upload(int D, int D_pad, int D_rows, int I_, int I_pad, int I_row
     return OMC_OK;
 }
 
+/* One row-major int8 matrix [O][K] + row scales as the down matrix of a
+ * one-expert layer (row tiles paired consecutively).  reuse != 0: write into
+ * the buffers *dq and *ds already hold (same shape). */
+int omc_matrix_upload(const int8_t *q, const float *s, int O, int K, int8_t **dq, const float **ds, int reuse) {
+    const int O_rows = omc_round_up(O, OMC_TM), K_pad = omc_round_up(K, OMC_KB);
+    const size_t bytes = (size_t)omc_round_up(O_rows, 2 * OMC_TM) * K_pad;
+    int on_host = 0, rc;
+    int8_t *d = reuse ? *dq : omc_slab_alloc(bytes, &on_host);
+    if (!d) return omc_fail(OMC_ENOMEM, "matrix upload: slab and host overflow exhausted");
+    (void)on_host;
+    CK(cudaMemsetAsync(d, 0, bytes, G.stream));
+    const float *sd = NULL;
+    if ((rc = upload_matrix(q, s, O, K, O_rows, K_pad, d, -1, reuse ? NULL : &sd, reuse ? *ds : NULL))) return rc;
+    if (!reuse) *ds = sd;
+    *dq = d;
+    return OMC_OK;
+}
+
 static int set_expert_slot(omc_layer *L, int slot, int I_, int I_pad, int I_rows, const int8_t *g, const float *gs,
                            const int8_t *u, const float *us, const int8_t *d, const float *ds) {
     const omc_layer_dev *P = &L->dev;

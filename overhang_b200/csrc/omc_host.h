@@ -85,6 +85,7 @@ int omc_ws_ensure_rows(const omc_layer *L, int rows);
 int omc_expert_upload(int D, int D_pad, int D_rows, int I_, int I_pad, int I_rows, const int8_t *g, const float *gs,
                       const int8_t *u, const float *us, const int8_t *d, const float *ds, omc_expert_ptrs *ep,
                       int reuse);
+int omc_matrix_upload(const int8_t *q, const float *s, int O, int K, int8_t **dq, const float **ds, int reuse);
 int omc_check_device_error(void);
 int omc_forward_device(omc_layer *L, const float *x, int T, float *out, int32_t *topk_idx, float *topk_w,
                        cudaStream_t s);

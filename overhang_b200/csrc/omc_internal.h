@@ -191,6 +191,11 @@ int omc_launch_ordered_add(float *out, const float *y, const int *off, const int
 /* explicit-rows pass: y[r] = w[r] * expert ids[r] (x[r]), ids in [e_lo, e_hi) or E (shared) */
 int omc_launch_mma_rows(const omc_layer_dev *L, const float *x, int R, const omc_ws *ws, const int32_t *ids,
                         const float *w, int e_lo, int e_hi, float *y, cudaStream_t s);
+/* dense pass: y[S][N] = x[S][K] . (ds * Wd)^T, Wd the down matrix of L's
+ * expert 0 (L: E = 1, D = N, I = K with K % 64 == 0) */
+int omc_launch_dense_i8(const omc_layer_dev *L, const float *x, int S, const omc_ws *ws, float *y, cudaStream_t s);
+/* dst = f16(src), n % 8 == 0 */
+int omc_launch_f32_to_f16(const float *src, long long n, uint16_t *dst, cudaStream_t s);
 int omc_noalloc_setup(int device);
 void *omc_noalloc_scratch_ptr(int device);
 int omc_launch_expf_probe(const float *x, float *y, long long n, cudaStream_t s);

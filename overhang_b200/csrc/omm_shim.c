@@ -23,11 +23,13 @@
  * (the engine then falls back to its CPU path), -3 a shape this build does
  * not serve (D or I not a multiple of 64, more than 1024 jobs).  gelu = 1 runs
  * the experts with gelu_tanh (engines/gemma.c:319-321), as Gemma's call does.
- * omm_dense*: -3, the engines keep their CPU dense path. */
+ * omm_dense_q runs the engine's int8 projections on the tensor-core GEMM,
+ * omm_dense its f32 ones through a cached half copy and cuBLAS (below). */
 #include <stdint.h>
 #include <stdlib.h>
 #include <string.h>
 
+#include <cublas_v2.h>
 #include <cuda_runtime.h>
 
 #include "om_metal.h"
@@ -242,12 +244,177 @@ int omm_moe(const omm_job *jobs, int nj, const float *x, int S, int D, int I, fl
     return omm_moe_act(jobs, nj, x, S, D, I, out, 0);
 }
 
-int omm_dense_q(const int8_t *Wq, const float *scales, int N, int K, const float *x, int S, float *out) {
-    (void)Wq; (void)scales; (void)N; (void)K; (void)x; (void)S; (void)out;
-    return -3;
+/* ---- dense projections ------------------------------------------------- */
+/* omm_dense_q (metal/om_metal.h:38-41): out[S,N] = x[S,K] . dequant(Wq)^T.
+ * The engine's int8 matrix (engines/gemma.c:158-175 mat_load, called from
+ * mat_apply_b :287-293) is copied once into HBM in the tile layout of the
+ * grouped GEMM and found again by its pointer; a matrix whose row scales
+ * changed is copied again.  The product runs on the tensor-core down GEMM as
+ * a one-matrix layer (tokens in f16, accumulation in f32, the row scale
+ * applied to the f32 sum as matmul_q does).  Like the reference backend it
+ * takes K % 64 == 0 and N % 32 == 0 and returns -3 otherwise. */
+typedef struct {
+    const int8_t *hq;            /* the engine's matrix pointer (its identity) */
+    int N, K;
+    float *sc;                   /* host copy of the scales the device copy was made from */
+    int8_t *dq;
+    const float *ds;
+} omm_dmat;
+
+static omm_dmat *g_dm;
+static int g_ndm, g_dmcap;
+
+static int dense_resolve(const int8_t *Wq, const float *scales, int N, int K, omc_expert_ptrs *ep) {
+    omm_dmat *m = NULL;
+    for (int i = 0; i < g_ndm; ++i)
+        if (g_dm[i].hq == Wq && g_dm[i].N == N && g_dm[i].K == K) {
+            m = &g_dm[i];
+            break;
+        }
+    const int reuse = m != NULL;
+    if (!m || memcmp(m->sc, scales, (size_t)N * 4)) {
+        if (!m) {
+            if (g_ndm == g_dmcap) {
+                const int nc = g_dmcap ? 2 * g_dmcap : 64;
+                omm_dmat *nm = realloc(g_dm, sizeof(omm_dmat) * (size_t)nc);
+                if (!nm) return OMC_ENOMEM;
+                g_dm = nm;
+                g_dmcap = nc;
+            }
+            m = &g_dm[g_ndm];
+            memset(m, 0, sizeof(*m));
+            m->sc = malloc((size_t)N * 4);
+            if (!m->sc) return OMC_ENOMEM;
+            m->hq = Wq;
+            m->N = N;
+            m->K = K;
+        }
+        const int rc = omc_matrix_upload(Wq, scales, N, K, &m->dq, &m->ds, reuse);
+        if (rc) return rc;
+        memcpy(m->sc, scales, (size_t)N * 4);
+        if (!reuse) ++g_ndm;
+    }
+    memset(ep, 0, sizeof(*ep));
+    ep->d = m->dq;
+    ep->ds = m->ds;
+    return OMC_OK;
 }
 
+int omm_dense_q(const int8_t *Wq, const float *scales, int N, int K, const float *x, int S, float *out) {
+    if (!omm_init()) return -1;
+    if (S <= 0) return 0;
+    if (!Wq || !scales || !x || !out || N <= 0 || K <= 0 || K % 64 || N % 32) return -3;
+    cudaSetDevice(G.device);
+    cudaStream_t s = G.stream;
+    omc_expert_ptrs tab[2];
+    if (dense_resolve(Wq, scales, N, K, &tab[0])) return -1;
+    memset(&tab[1], 0, sizeof(tab[1]));
+    omc_layer TL;
+    memset(&TL, 0, sizeof(TL));
+    TL.desc.family = OMC_FAMILY_OLMOE;
+    TL.desc.D = N;
+    TL.desc.I = K;
+    TL.desc.E = 1;
+    TL.desc.k = 1;
+    TL.dev.family = OMC_FAMILY_OLMOE;
+    TL.dev.D = N;
+    TL.dev.I = K;
+    TL.dev.E = 1;
+    TL.dev.k = 1;
+    TL.dev.D_pad = omc_round_up(N, OMC_KB);
+    TL.dev.I_pad = K;
+    TL.dev.D_rows = omc_round_up(N, OMC_TM);
+    TL.dev.I_rows = omc_round_up(K, OMC_TM);
+    TL.e0 = 0;
+    TL.ne = 1;
+    void *d_tab = scratch(B_TAB, sizeof(tab));
+    float *d_x = scratch(B_X, (size_t)S * K * 4), *d_y = scratch(B_OUT, (size_t)S * N * 4);
+    if (!d_tab || !d_x || !d_y || omc_ws_ensure_rows(&TL, S)) return -1;
+    TL.dev.experts = (const omc_expert_ptrs *)d_tab;
+    if (cudaMemcpyAsync(d_tab, tab, sizeof(tab), cudaMemcpyHostToDevice, s) ||
+        cudaMemcpyAsync(d_x, x, (size_t)S * K * 4, cudaMemcpyHostToDevice, s) ||
+        omc_launch_dense_i8(&TL.dev, d_x, S, &G.ws, d_y, s) ||
+        cudaMemcpyAsync(out, d_y, (size_t)S * N * 4, cudaMemcpyDeviceToHost, s) || cudaStreamSynchronize(s)) {
+        cudaGetLastError();
+        return -1;
+    }
+    return omc_check_device_error() ? -1 : 0;
+}
+
+/* omm_dense (metal/om_metal.h:43-46): out[S,N] = x[S,K] . W^T with the
+ * engine's resident f32 W (engines/olmoe.c:286-292 dense_mm).  As in the
+ * reference backend, a half copy of W is made on first use and kept by
+ * pointer; x is rounded to half too, the products are summed in f32
+ * (cuBLAS GemmEx: a plain library GEMM, f16 inputs, f32 compute and output).
+ * K % 8 == 0, else -3. */
+typedef struct {
+    const float *hw;
+    int N, K;
+    uint16_t *dw;
+} omm_fmat;
+
+static omm_fmat *g_fm;
+static int g_nfm, g_fmcap;
+static cublasHandle_t g_cublas;
+
 int omm_dense(const float *W, int N, int K, const float *x, int S, float *out) {
-    (void)W; (void)N; (void)K; (void)x; (void)S; (void)out;
-    return -3;
+    if (!omm_init()) return -1;
+    if (S <= 0) return 0;
+    if (!W || !x || !out || N <= 0 || K <= 0 || K % 8) return -3;
+    cudaSetDevice(G.device);
+    cudaStream_t s = G.stream;
+    if (!g_cublas && cublasCreate(&g_cublas) != CUBLAS_STATUS_SUCCESS) return -1;
+    if (cublasSetStream(g_cublas, s) != CUBLAS_STATUS_SUCCESS) return -1;
+    omm_fmat *m = NULL;
+    for (int i = 0; i < g_nfm; ++i)
+        if (g_fm[i].hw == W && g_fm[i].N == N && g_fm[i].K == K) {
+            m = &g_fm[i];
+            break;
+        }
+    if (!m) {
+        if (g_nfm == g_fmcap) {
+            const int nc = g_fmcap ? 2 * g_fmcap : 64;
+            omm_fmat *nm = realloc(g_fm, sizeof(omm_fmat) * (size_t)nc);
+            if (!nm) return -1;
+            g_fm = nm;
+            g_fmcap = nc;
+        }
+        m = &g_fm[g_nfm];
+        memset(m, 0, sizeof(*m));
+        const size_t n = (size_t)N * K;
+        float *stage = scratch(B_ROWS, n * 4);
+        if (!stage || cudaMalloc((void **)&m->dw, n * 2) != cudaSuccess) {
+            cudaGetLastError();
+            return -1;
+        }
+        if (cudaMemcpyAsync(stage, W, n * 4, cudaMemcpyHostToDevice, s) ||
+            omc_launch_f32_to_f16(stage, (long long)n, m->dw, s) || cudaStreamSynchronize(s)) {
+            cudaGetLastError();
+            cudaFree(m->dw);
+            return -1;
+        }
+        m->hw = W;
+        m->N = N;
+        m->K = K;
+        ++g_nfm;
+    }
+    float *d_x = scratch(B_X, (size_t)S * K * 4), *d_y = scratch(B_OUT, (size_t)S * N * 4);
+    uint16_t *d_xh = scratch(B_Y, (size_t)S * K * 2);
+    if (!d_x || !d_y || !d_xh) return -1;
+    const float alpha = 1.f, beta = 0.f;
+    if (cudaMemcpyAsync(d_x, x, (size_t)S * K * 4, cudaMemcpyHostToDevice, s) ||
+        omc_launch_f32_to_f16(d_x, (long long)S * K, d_xh, s)) {
+        cudaGetLastError();
+        return -1;
+    }
+    /* column-major view: C (N x S, ldc N) = W^T-view (W row-major [N][K] is
+     * K x N, lda K; op T) times x (row-major [S][K] is K x S, ldb K) */
+    if (cublasGemmEx(g_cublas, CUBLAS_OP_T, CUBLAS_OP_N, N, S, K, &alpha, m->dw, CUDA_R_16F, K, d_xh, CUDA_R_16F, K,
+                     &beta, d_y, CUDA_R_32F, N, CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT) != CUBLAS_STATUS_SUCCESS)
+        return -1;
+    if (cudaMemcpyAsync(out, d_y, (size_t)S * N * 4, cudaMemcpyDeviceToHost, s) || cudaStreamSynchronize(s)) {
+        cudaGetLastError();
+        return -1;
+    }
+    return omc_check_device_error() ? -1 : 0;
 }

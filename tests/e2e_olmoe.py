@@ -12,7 +12,12 @@ Then two builds of the unmodified engines/olmoe.c generate greedily from the
 same prompt (engines/olmoe.c:429-451, main :548-586):
   oracle/_ref/olmoe       the reference, all host cores (OpenMP)
   oracle/_ref/olmoe_omc   the same engine with moe() hooked to libomc
-                          (include/omc_engine_hook.h)
+                          (include/omc_engine_hook.h): level 2, the whole
+                          MoE block on the GPU at every step
+  oracle/_ref/olmoe_metal the unmodified engine built for its own GPU seam
+                          (-DOM_METAL, include/om_metal.h): level 1, the
+                          prefill's attention projections (omm_dense) and
+                          MoE union (omm_moe) on the GPU, decode on the CPU
 and their tokens are compared.  The engine's expert cache is given every
 expert of a layer (no LRU eviction).
 
@@ -39,6 +44,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
 REF_ENGINE = os.path.join(ROOT, "oracle", "_ref", "olmoe")
 OMC_ENGINE = os.path.join(ROOT, "oracle", "_ref", "olmoe_omc")
+METAL_ENGINE = os.path.join(ROOT, "oracle", "_ref", "olmoe_metal")
 
 # OLMoE-1B-7B shape (the C0 configuration)
 D, NH, E, K, I = 2048, 16, 64, 8, 1024
@@ -172,8 +178,10 @@ def run_engine(binary: str, snap: str, prompt: list, n_new: int, env_extra=None,
     return [int(t) for t in m.group(1).split()], dt, log
 
 
-def compare(layers: int, vocab: int, n_prompt: int, n_new: int, path: str | None, workdir: str | None = None):
-    """Builds the snapshot, runs both engines, returns the result dict."""
+def compare(layers: int, vocab: int, n_prompt: int, n_new: int, path: str | None, workdir: str | None = None,
+            level: int = 2):
+    """Builds the snapshot, runs the CPU engine and the GPU one (level 2: the
+    moe() hook; level 1: the engine's own omm_* seam), returns the result dict."""
     own = workdir is None
     workdir = workdir or tempfile.mkdtemp(prefix="olmoe_e2e_")
     snap = os.path.join(workdir, "snap")
@@ -185,10 +193,10 @@ def compare(layers: int, vocab: int, n_prompt: int, n_new: int, path: str | None
         prompt = prompt_ids(vocab, n_prompt)
         cpu, t_cpu, _ = run_engine(REF_ENGINE, snap, prompt, n_new)
         env = {"OMC_FFN_PATH": path} if path else {}
-        gpu, t_gpu, log = run_engine(OMC_ENGINE, snap, prompt, n_new, env)
+        gpu, t_gpu, log = run_engine(OMC_ENGINE if level == 2 else METAL_ENGINE, snap, prompt, n_new, env)
         first_diff = next((i for i, (a, b) in enumerate(zip(cpu, gpu)) if a != b), None)
         return {"layers": layers, "vocab": vocab, "prompt_tokens": n_prompt, "new_tokens": n_new,
-                "expert_path": path or "auto", "prompt": prompt, "cpu_tokens": cpu, "gpu_tokens": gpu,
+                "level": level, "expert_path": path or "auto", "prompt": prompt, "cpu_tokens": cpu, "gpu_tokens": gpu,
                 "matching": sum(a == b for a, b in zip(cpu, gpu)), "identical": cpu == gpu,
                 "first_difference": first_diff, "seconds": {"snapshot": round(t_gen, 1),
                                                             "cpu_engine": round(t_cpu, 1),
@@ -207,8 +215,10 @@ def main():
     ap.add_argument("--new", type=int, default=64)
     ap.add_argument("--path", default=None, choices=[None, "gemv", "mma"])
     ap.add_argument("--workdir", default=None, help="reuse a snapshot directory (kept)")
+    ap.add_argument("--level", type=int, default=2, choices=[1, 2],
+                    help="2: the moe() hook (olmoe_omc); 1: the engine's omm_* seam (olmoe_metal)")
     a = ap.parse_args()
-    print(json.dumps(compare(a.layers, a.vocab, a.prompt, a.new, a.path, a.workdir)), flush=True)
+    print(json.dumps(compare(a.layers, a.vocab, a.prompt, a.new, a.path, a.workdir, a.level)), flush=True)
 
 
 if __name__ == "__main__":

@@ -32,3 +32,14 @@ def test_greedy_tokens_identical(snapshot, path):
     # the engine processes initialise the library themselves (their own slab)
     r = E2E.compare(layers=2, vocab=4096, n_prompt=32, n_new=16, path=path, workdir=snapshot)
     assert r["identical"], f"first difference at token {r['first_difference']}: {r['cpu_tokens']} vs {r['gpu_tokens']}"
+
+
+def test_greedy_tokens_level1_seam(snapshot):
+    """The unmodified engine built with -DOM_METAL against include/om_metal.h:
+    its prefill attention projections (omm_dense, half copies of the f32
+    weights, as the reference backend makes them) and MoE union (omm_moe) run
+    on the GPU."""
+    if not os.path.exists(E2E.METAL_ENGINE):
+        pytest.skip("oracle/_ref/olmoe_metal not built")
+    r = E2E.compare(layers=2, vocab=4096, n_prompt=32, n_new=16, path=None, workdir=snapshot, level=1)
+    assert r["identical"], f"first difference at token {r['first_difference']}: {r['cpu_tokens']} vs {r['gpu_tokens']}"

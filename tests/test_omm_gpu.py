@@ -102,3 +102,70 @@ def test_omm_unsupported_shapes_fall_back(gpu):
     # tests/test_gemma_gpu.py::test_omm_moe_act_gelu)
     assert lib.omm_moe_act(job, 1, x.ctypes.data_as(C.c_void_p), 8, 96, 64, out.ctypes.data_as(C.c_void_p), 1) == -3
     assert lib.omm_dense(None, 64, 64, None, 8, None) == -3
+
+
+# ---- dense projections (metal/om_metal.h:38-46) ------------------------------
+
+def _dense_ref(x, W):
+    return (x.astype(np.float64) @ W.astype(np.float64).T).astype(np.float32)
+
+
+@pytest.mark.parametrize("S,N,K", [(8, 2048, 2048), (40, 1536, 2816), (200, 352, 704)])
+def test_omm_dense_q(gpu, oracle, S, N, K):
+    """omm_dense_q: out = x . dequant(Wq)^T on the tensor-core GEMM (the int8
+    projections of engines/gemma.c:287-293)."""
+    q, sc = oracle.quantize_py(oracle.normal(9000 + N, (N, K), 0.02))
+    x = oracle.normal(9100 + S, (S, K))
+    out = np.full((S, N), np.nan, np.float32)
+    lib = gpu.lib()
+    rc = lib.omm_dense_q(q.ctypes.data_as(C.c_void_p), sc.ctypes.data_as(C.c_void_p), N, K,
+                         x.ctypes.data_as(C.c_void_p), S, out.ctypes.data_as(C.c_void_p))
+    assert rc == 0, gpu.last_error()
+    assert_close(out, _dense_ref(x, q.astype(np.float32) * sc[:, None]), what=f"omm_dense_q S={S} N={N} K={K}")
+
+
+def test_omm_dense_q_cache_follows_scales(gpu, oracle):
+    """The device copy is found again by pointer; a matrix whose scales changed
+    in place is copied again (an engine reusing the buffer)."""
+    N, K, S = 256, 512, 16
+    q, sc = oracle.quantize_py(oracle.normal(9200, (N, K), 0.02))
+    x = oracle.normal(9201, (S, K))
+    lib = gpu.lib()
+    out = np.zeros((S, N), np.float32)
+    call = lambda: lib.omm_dense_q(q.ctypes.data_as(C.c_void_p), sc.ctypes.data_as(C.c_void_p), N, K,  # noqa: E731
+                                   x.ctypes.data_as(C.c_void_p), S, out.ctypes.data_as(C.c_void_p))
+    assert call() == 0
+    first = out.copy()
+    assert call() == 0 and np.array_equal(out, first)
+    q2, sc2 = oracle.quantize_py(oracle.normal(9202, (N, K), 0.02))
+    q[...] = q2
+    sc[...] = sc2
+    assert call() == 0
+    assert_close(out, _dense_ref(x, q.astype(np.float32) * sc[:, None]), what="omm_dense_q after refill")
+
+
+def test_omm_dense_q_unsupported(gpu):
+    lib = gpu.lib()
+    q = np.zeros((64, 96), np.int8)
+    sc = np.ones(64, np.float32)
+    x = np.zeros((8, 96), np.float32)
+    out = np.zeros((8, 64), np.float32)
+    args = lambda N, K: (q.ctypes.data_as(C.c_void_p), sc.ctypes.data_as(C.c_void_p), N, K,  # noqa: E731
+                         x.ctypes.data_as(C.c_void_p), 8, out.ctypes.data_as(C.c_void_p))
+    assert lib.omm_dense_q(*args(64, 96)) == -3      # K % 64
+    assert lib.omm_dense_q(*args(48, 64)) == -3      # N % 32
+
+
+@pytest.mark.parametrize("S,N,K", [(8, 2048, 2048), (64, 512, 1024)])
+def test_omm_dense_f32(gpu, oracle, S, N, K):
+    """omm_dense: the engine's f32 weights through a cached half copy (the
+    attention projections of engines/olmoe.c:286-292)."""
+    W = oracle.normal(9300 + N, (N, K), 0.02)
+    x = oracle.normal(9301 + S, (S, K))
+    out = np.zeros((S, N), np.float32)
+    lib = gpu.lib()
+    for _ in range(2):        # the second call uses the cached copy
+        rc = lib.omm_dense(W.ctypes.data_as(C.c_void_p), N, K, x.ctypes.data_as(C.c_void_p), S,
+                           out.ctypes.data_as(C.c_void_p))
+        assert rc == 0, gpu.last_error()
+        assert_close(out, _dense_ref(x, W), what=f"omm_dense S={S} N={N} K={K}")
