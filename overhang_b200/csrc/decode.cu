@@ -50,6 +50,7 @@
 // can be replayed from a CUDA graph.  All CTAs are co-resident (cooperative
 // launch).
 #include "omc_select.cuh"
+#include "omc_rms.cuh"
 
 namespace {
 
@@ -77,8 +78,8 @@ constexpr int CTR_FIXED = CTR_HFLAG + DC_GMAX * DC_TILES_MAX;
 
 struct DecArgs {
     omc_layer_dev L;
-    const float *x;       // the experts' input rows
-    const float *xr;      // the router's input rows (x except for GEMMA)
+    const float *x;       // the input rows (GEMMA: the residual rows, normed here)
+    const float *xr;      // the rows the router CTAs stage (x)
     int T;
     int32_t *topk_idx;
     float *topk_w, *logits;
@@ -266,6 +267,7 @@ __global__ void __launch_bounds__(DC_THREADS, 1) decode_moe_kernel(const DecArgs
     __shared__ const int8_t *s_gp[DC_GMAX], *s_dp[DC_GMAX];   // group's gate/up and down matrices
     __shared__ int s_pcta[DC_NPMAX];                            // other CTAs holding pieces of a segment
     __shared__ int s_epoch, s_abort, s_ngr, s_np;
+    __shared__ float s_r[DC_TMAX];                              // GEMMA: each token's rms factor
     __shared__ int s_comb[DC_TMAX];
     int *ctr = a.ctr;
     const bool router = c < a.nrc;
@@ -322,7 +324,33 @@ __global__ void __launch_bounds__(DC_THREADS, 1) decode_moe_kernel(const DecArgs
         const int t = i / (D_pad - D), col = D + (i - t * (D_pad - D));
         xs[(size_t)t * a.ldx + col] = 0.f;
     }
+    const bool gemma = L.family == OMC_FAMILY_GEMMA;
+    // GEMMA: x is the residual row.  Each CTA takes every token's rms factor
+    // from its own copy (warp t, token t; omc_rms.cuh) and scales the copy
+    // into the router's input (router CTAs) or the experts' input.
+    auto gemma_factors = [&]() {
+        if (warp < T) {
+            const float r = omc_gemma_rms_factor(xs + (size_t)warp * a.ldx, D, L.eps);
+            if (lane == 0) s_r[warp] = r;
+        }
+    };
+    auto gemma_scale = [&](const float *__restrict__ w) {   // xs = (x*r)*w, x the staged rows
+        for (int i = tid; i < T * D; i += DC_THREADS) {
+            const int t = i / D, col = i - t * D;
+            float *v = xs + (size_t)t * a.ldx + col;
+            *v = __fmul_rn(__fmul_rn(*v, s_r[t]), w ? w[col] : 1.f);
+        }
+    };
     if (router) {
+        if (gemma) {
+            // the chains need the scaled row: every chunk first
+            if (warp < T)
+                for (int ch = 0; ch < DC_RCH; ++ch) mbar_wait(&rbar[ch], 0, a.err, OMC_SITE_DECODE);
+            gemma_factors();
+            __syncthreads();
+            gemma_scale(L.g_s2);
+            __syncthreads();
+        }
         if (tid < T * rr) {
             // the chain (about 5.5 cycles an element: the add latency plus
             // the loads and products it cannot hide)
@@ -346,22 +374,27 @@ __global__ void __launch_bounds__(DC_THREADS, 1) decode_moe_kernel(const DecArgs
                 a.logits[(size_t)t * a.ldl + gr] = (L.router_i8 && gr < E) ? __fmul_rn(acc, L.router_s[gr]) : acc;
         }
         __syncthreads();   // this CTA's logits are written; x chunks have landed
-        if (a.xr != a.x) {
-            // GEMMA: the experts read another input; it replaces the router's
-            // rows (columns D.. stay zero) while the other router CTAs finish
-            for (int i = tid; i < T * (D / 4); i += DC_THREADS) {
-                const int t = i / (D / 4), col = (i - t * (D / 4)) * 4;
-                cp_async16(xs + (size_t)t * a.ldx + col, a.x + (size_t)t * D + col);
-            }
-            asm volatile("cp.async.commit_group;" ::: "memory");
-        }
         if (tid == 0) {
             fence_acqrel_gpu();
             red_release_add(ctr + CTR_ROUTER, 1);
         }
-        if (a.xr != a.x) asm volatile("cp.async.wait_group 0;" ::: "memory");
+        if (gemma) {
+            // the experts' input replaces the router's (columns D.. stay zero):
+            // (x*r)*pre_feedforward_layernorm_2 from the residual rows in HBM
+            for (int i = tid; i < T * D; i += DC_THREADS) {
+                const int t = i / D, col = i - t * D;
+                xs[(size_t)t * a.ldx + col] =
+                    __fmul_rn(__fmul_rn(__ldg(a.x + (size_t)t * D + col), s_r[t]), L.g_en ? L.g_en[col] : 1.f);
+            }
+        }
     } else {
         asm volatile("cp.async.wait_group 0;" ::: "memory");
+        if (gemma) {
+            __syncthreads();   // every thread's copies of the rows have landed
+            gemma_factors();
+            __syncthreads();
+            gemma_scale(L.g_en);
+        }
     }
 
     // ---- 2. every router CTA done -> select, in every CTA ---------------------

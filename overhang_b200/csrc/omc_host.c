@@ -749,6 +749,18 @@ static int forward_on_ws(omc_layer *L, const omc_ws *ws, const float *x, int T, 
      * own norm of it (prenorm.cu).  The tensor-core path takes the experts'
      * input as its f16 operand, the CUDA-core paths as f32. */
     const int gemma = L->dev.family == OMC_FAMILY_GEMMA;
+    /* decode: the whole block in one launch (decode.cu).  Chosen on its own
+     * at T = 1, where it beats the router + GEMV kernels; from T = 2 its
+     * CUDA-core dequant-and-dot is the bound and the separate kernels win
+     * (measured on B200), so larger T take it only when it is forced.  It
+     * takes GEMMA's residual rows as they are and norms them itself. */
+    if (!mma && G.ep_world <= 1 && (G.path_override == 3 || (G.path_override == 0 && T == 1)) &&
+        omc_decode_supported(&L->dev, T, G.num_sms, G.dec_ctr_n, G.dec_part_n)) {
+        if ((rc = omc_launch_decode(&L->dev, x, x, T, ws, G.num_sms, G.dec_ctr, G.dec_part, idx, w, out, s)))
+            return omc_fail(rc, "fused decode launch failed (%s)", omc_strerror(rc));
+        G.prof_valid = G.profiling;
+        return OMC_OK;
+    }
     const float *xr = x, *xe = x;
     if (gemma) {
         if ((rc = omc_launch_gemma_prenorm(&L->dev, x, T, ws->xg_r, mma ? NULL : ws->xg_e, mma ? ws->xh : NULL, NULL,
@@ -756,17 +768,6 @@ static int forward_on_ws(omc_layer *L, const omc_ws *ws, const float *x, int T, 
             return omc_fail(rc, "prenorm launch failed");
         xr = ws->xg_r;
         xe = ws->xg_e;
-    }
-    /* decode: the whole block in one launch (decode.cu).  Chosen on its own
-     * at T = 1, where it beats the router + GEMV kernels; from T = 2 its
-     * CUDA-core dequant-and-dot is the bound and the separate kernels win
-     * (measured on B200), so larger T take it only when it is forced. */
-    if (!mma && G.ep_world <= 1 && (G.path_override == 3 || (G.path_override == 0 && T == 1)) &&
-        omc_decode_supported(&L->dev, T, G.num_sms, G.dec_ctr_n, G.dec_part_n)) {
-        if ((rc = omc_launch_decode(&L->dev, xe, xr, T, ws, G.num_sms, G.dec_ctr, G.dec_part, idx, w, out, s)))
-            return omc_fail(rc, "fused decode launch failed (%s)", omc_strerror(rc));
-        G.prof_valid = G.profiling;
-        return OMC_OK;
     }
     if (G.path_override == 3) return omc_fail(OMC_EUNSUPPORTED, "fused decode path forced but not available for T=%d", T);
     if ((rc = omc_launch_router(&L->dev, xr, T, ws, idx, w, mma ? &plan : NULL, s)))

@@ -176,8 +176,8 @@ int omc_launch_test_wait(int *err, cudaStream_t s);
  * pieces) serves every T <= 8 of a layer on a grid of G CTAs */
 int omc_decode_state_size(const omc_layer_dev *L, int G, size_t *ctr_ints, size_t *part_floats);
 int omc_decode_supported(const omc_layer_dev *L, int T, int G, size_t ctr_ints, size_t part_floats);
-/* x = the experts' input rows, xr = the router's (the same pointer except
- * for GEMMA) */
+/* x = the input rows (GEMMA: the residual rows, normed in the kernel); xr =
+ * the rows the router CTAs stage (x) */
 int omc_launch_decode(const omc_layer_dev *L, const float *x, const float *xr, int T, const omc_ws *ws, int G, int *ctr,
                       float *part, int32_t *topk_idx, float *topk_w, float *out, cudaStream_t s);
 /* GEMMA: router input xr, expert input xe (f32) and xh (f16 token operand)

@@ -22,23 +22,11 @@
 // (it equals the 64-bit long double result rounded to float on every
 // positive float).  Routing indices are unaffected in practice; top-k weights
 // move by a few ulps on the rows where the two differ.
-#include "omc_common.cuh"
+#include "omc_rms.cuh"
 
 namespace {
 
 constexpr int PN_WARPS = 8;
-
-// x[i]^2 summed in index order in double (engines/gemma.c:314): one lane.
-__device__ double seq_sumsq(const float *__restrict__ xt, int D) {
-    double s = 0.0;
-    for (int i = 0; i < D; ++i) {
-        const double v = (double)xt[i];
-        s = __dadd_rn(s, __dmul_rn(v, v));
-    }
-    return s;
-}
-
-__device__ __forceinline__ double sq(float v) { return __dmul_rn((double)v, (double)v); }
 
 __global__ void __launch_bounds__(PN_WARPS * 32)
     gemma_prenorm_kernel(const float *__restrict__ x, int T, int D, float eps, const float *__restrict__ s2,
@@ -50,36 +38,7 @@ __global__ void __launch_bounds__(PN_WARPS * 32)
     const float *xt = x + (size_t)t * D;
     const float4 *x4 = reinterpret_cast<const float4 *>(xt);
     const int n4 = D >> 2;
-    double s = 0.0;
-    for (int i = lane; i < n4; i += 32) {
-        const float4 v = __ldg(x4 + i);
-        s = __dadd_rn(s, sq(v.x));
-        s = __dadd_rn(s, sq(v.y));
-        s = __dadd_rn(s, sq(v.z));
-        s = __dadd_rn(s, sq(v.w));
-    }
-    // xor butterfly: every lane ends with the same bits (a + b == b + a)
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) s = __dadd_rn(s, __shfl_xor_sync(0xffffffffu, s, o));
-    double q = __ddiv_rn(s, (double)D);
-    float f = __double2float_rn(q);
-    const uint32_t fb = __float_as_uint(f);
-    bool sure = q >= 0.0 && fb < 0x7f7fffffu;   // finite, below FLT_MAX
-    if (sure) {
-        const double tol = (double)(D + 2) * 0x1p-51 * q;
-        const double lo = fb == 0u ? -1.0 : 0.5 * ((double)__uint_as_float(fb - 1u) + (double)f);
-        const double hi = 0.5 * ((double)f + (double)__uint_as_float(fb + 1u));
-        sure = (q - lo > tol) && (hi - q > tol);
-    }
-    if (!sure) {   // warp-uniform: every lane holds the same q
-        double sq_seq = 0.0;
-        if (lane == 0) sq_seq = seq_sumsq(xt, D);
-        s = __shfl_sync(0xffffffffu, sq_seq, 0);
-        q = __ddiv_rn(s, (double)D);
-        f = __double2float_rn(q);
-    }
-    const float y = __fadd_rn(f, eps);
-    const float r = __double2float_rn(__ddiv_rn(1.0, __dsqrt_rn((double)y)));
+    const float r = omc_gemma_rms_factor(xt, D, eps);
     if (rout && lane == 0) rout[t] = r;
     const float4 *s24 = reinterpret_cast<const float4 *>(s2);
     const float4 *en4 = reinterpret_cast<const float4 *>(en);
@@ -98,10 +57,9 @@ __global__ void __launch_bounds__(PN_WARPS * 32)
         }
         if (xe) reinterpret_cast<float4 *>(xe + (size_t)t * D)[i] = e;
         if (xh) {
-            const __half2 a = __floats2half2_rn(e.x, e.y), b = __floats2half2_rn(e.z, e.w);
-            uint2 o;
-            o.x = *reinterpret_cast<const uint32_t *>(&a);
-            o.y = *reinterpret_cast<const uint32_t *>(&b);
+            uint2 o;   // saturated, as every f16 token operand
+            o.x = f32x2_to_f16x2_sat(e.x, e.y);
+            o.y = f32x2_to_f16x2_sat(e.z, e.w);
             reinterpret_cast<uint2 *>(xh + (size_t)t * D)[i] = o;
         }
     }
