@@ -43,3 +43,14 @@ def test_greedy_tokens_level1_seam(snapshot):
         pytest.skip("oracle/_ref/olmoe_metal not built")
     r = E2E.compare(layers=2, vocab=4096, n_prompt=32, n_new=16, path=None, workdir=snapshot, level=1)
     assert r["identical"], f"first difference at token {r['first_difference']}: {r['cpu_tokens']} vs {r['gpu_tokens']}"
+
+
+def test_gemma_greedy_tokens_identical(tmp_path):
+    """The Gemma engine (int8 container, stream mode) with its routing and
+    expert union on the GPU (include/omc_gemma_hook.h) gives the CPU engine's
+    greedy tokens (prefill batched, then token-by-token decode)."""
+    import e2e_gemma as G
+    if not (os.path.exists(G.REF_ENGINE) and os.path.exists(G.OMC_ENGINE)):
+        pytest.skip("engine builds missing (oracle/_ref/gemma, gemma_omc): run the build")
+    r = G.compare(layers=4, vocab=4096, n_prompt=24, n_new=16, workdir=str(tmp_path))
+    assert r["identical"], f"first difference at token {r['first_difference']}: {r['cpu_tokens']} vs {r['gpu_tokens']}"
