@@ -124,6 +124,24 @@ int omc_experts_set_packed(int layer,
  * .qs [2I], engines/gemma.c:342-361): pass g = gate_up, u = gate_up + I*D,
  * gs = qs, us = qs + I. */
 
+/* Upload the routed experts of `layer` that this process holds straight from
+ * the engines' int8 container: every *.safetensors file of directory
+ * `snapshot` (one shard each).  name_g, name_u, name_d are printf patterns
+ * taking the container's layer index `src_layer` (the engine's layer, which
+ * the engines' hooks also use as the library's layer id) then the expert id,
+ * e.g.
+ *   "model.layers.%d.mlp.experts.%d.gate_proj.weight"   (OLMoE, Qwen)
+ * each tensor int8 [rows][cols] with its f32 row scales at name + ".qs"
+ * (tools/convert_olmoe.py:93-99).  name_u = NULL: name_g is the fused
+ * gate_up [2I,D] (Gemma, "model.layers.%d.experts.%d.gate_up_proj",
+ * tools/convert_gemma.py:386-394).  nthreads reader threads (0 = 8) read
+ * the tensors into pinned staging while the caller's thread uploads the
+ * finished experts in order.  Replaces the engines' per-expert disk fill
+ * (expert_get, engines/olmoe.c:250-272) at load time.  A missing tensor or
+ * a dtype/shape that differs from the layer: OMC_EINVAL, naming it. */
+int omc_experts_load(int layer, const char *snapshot, int src_layer, const char *name_g, const char *name_u,
+                     const char *name_d, int nthreads);
+
 /* QWEN shared expert: g,u int8 [Is,D], d int8 [D,Is], their row scales, and
  * the f32 gate vector sh_gate [D] (engines/qwen.c:279-287). */
 int omc_shared_set(int layer,

@@ -51,6 +51,7 @@ SIGNATURES = {
     "omc_layer_gemma_norms": (_i, [_i, C.c_float, _vp, _vp, _vp]),
     "omc_expert_set": (_i, [_i, _i, _vp, _vp, _vp, _vp, _vp, _vp]),
     "omc_experts_set_packed": (_i, [_i, _vp, _vp, _vp, _vp, _vp, _vp]),
+    "omc_experts_load": (_i, [_i, C.c_char_p, _i, C.c_char_p, C.c_char_p, C.c_char_p, _i]),
     "omc_shared_set": (_i, [_i, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "omc_moe_forward": (_i, [_i, _vp, _i, _vp, _vp, _vp]),
     "omc_moe_forward_dev": (_i, [_i, _vp, _i, _vp, _vp, _vp, _vp]),
@@ -82,6 +83,7 @@ SIGNATURES = {
     "omc_debug_router_tile": (_i, [_i, _i, _i]),
     "omc_debug_ws_copy": (_i, [_i, _vp, _sz]),
     "omc_debug_gemma_prenorm": (_i, [_i, _vp, _i, _vp, _vp, _vp]),
+    "omc_debug_container_read": (C.c_longlong, [C.c_char_p, C.c_char_p, _vp, C.c_longlong]),
 }
 
 PATH_AUTO, PATH_GEMV, PATH_MMA, PATH_DECODE = 0, 1, 2, 3
@@ -233,6 +235,15 @@ class MoELayer:
         check(lib().omc_debug_gemma_prenorm(self.layer, _p(x), T, _p(xr), _p(xe), _p(r)),
               "omc_debug_gemma_prenorm")
         return xr, xe, r
+
+    def load_experts(self, snapshot: str, src_layer: int, name_g: str, name_u, name_d: str,
+                     nthreads: int = 0) -> None:
+        """Upload this layer's experts from an int8 container directory
+        (omc_experts_load): printf name patterns taking (src_layer, expert);
+        name_u None = name_g is the fused gate_up."""
+        check(lib().omc_experts_load(self.layer, snapshot.encode(), src_layer, name_g.encode(),
+                                     None if name_u is None else name_u.encode(), name_d.encode(), nthreads),
+              "omc_experts_load")
 
     def set_experts_packed(self, g, gs, u, us, d, ds) -> None:
         arrs = [np.ascontiguousarray(v) for v in (g, gs, u, us, d, ds)]

@@ -101,6 +101,7 @@ int omc_debug_set_path(int path);
 int omc_debug_router_tile(int g, int tt, int rr);
 int omc_debug_ws_copy(int which, void *dst, size_t bytes);
 int omc_debug_gemma_prenorm(int layer, const float *x, int T, float *xr, float *xe, float *r);
+long long omc_debug_container_read(const char *snapshot, const char *name, void *dst, long long cap);
 
 #ifdef __cplusplus
 }
