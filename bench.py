@@ -11,7 +11,9 @@ MoE block over the 512 tokens.
 
 Arms
   ours (default): libomc.so.  `value` = tokens/s with inputs resident in HBM
-      (device entry omc_moe_forward_dev), timed with CUDA events on the
+      (device entry omc_moe_forward_dev: one forward per input buffer is
+      captured in a CUDA graph, and the timed region replays it; --stream
+      times stream launches instead), timed with CUDA events on the
       launching stream, max over ranks; `e2e` = the same through the host
       entry omc_moe_forward (pinned host x in, host out/top-k back every
       step).  N>1 (--mode replica, the default): N independent copies of
@@ -371,7 +373,7 @@ def run_ours(args):
            "decode_moe" if "decode_moe" in stages else "gemv_gateup")
 
     graph = None
-    if args.graph:
+    if args.graph and not ep_mode:
         # one captured forward per input buffer; the timed region replays the graph
         ob.launch_count(reset=True)
         graph = torch.cuda.CUDAGraph()
@@ -529,8 +531,11 @@ def main():
     ap.add_argument("--workload", default="olmoe_prefill", choices=sorted(WORKLOADS),
                     help="olmoe_prefill (BASELINE configs[1], the default line), olmoe_decode, "
                          "qwen_prefill, qwen_decode")
-    ap.add_argument("--graph", action="store_true",
-                    help="capture one forward per input buffer in a CUDA graph and time graph replays")
+    ap.add_argument("--graph", action="store_true", default=True,
+                    help="capture one forward per input buffer in a CUDA graph and time graph replays "
+                         "(the default; --mode ep always times stream launches)")
+    ap.add_argument("--stream", dest="graph", action="store_false",
+                    help="time stream launches of the forward instead of graph replays")
     ap.add_argument("--tokens", type=int, default=None,
                     help="tokens per rank instead of the workload's T (the T sweep of the prefill rows)")
     ap.add_argument("--mode", default="replica", choices=["ep", "replica"],
