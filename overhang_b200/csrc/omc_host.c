@@ -33,6 +33,13 @@ omc_state omc_G;
 
 static char g_errbuf[512];
 
+/* Generation of everything a forward enqueues (layers, workspace, forced
+ * paths): the host entry's replayed forwards are valid for one generation. */
+static int g_graph_gen;
+void omc_graphs_invalidate(void) { ++g_graph_gen; }
+#define graphs_invalidate omc_graphs_invalidate
+static void graphs_release(void);
+
 int omc_fail(int code, const char *fmt, ...) {
     va_list ap;
     va_start(ap, fmt);
@@ -171,6 +178,7 @@ void omc_shutdown(void) {
     if (!G.init) return;
     cudaSetDevice(G.device);
     cudaDeviceSynchronize();
+    graphs_release();
     omc_ep_release();
     for (int i = 0; i < G.nlayers; ++i) {
         free(G.layers[i].h_experts);
@@ -231,6 +239,7 @@ int omc_layer_init(int layer, const omc_moe_desc *d, const void *router_w, const
         G.nlayers = nn;
     }
     omc_layer *L = &G.layers[layer];
+    graphs_invalidate();
     if (L->used) {
         free(L->h_experts);
         cudaFree(L->d_experts_tab);
@@ -323,6 +332,7 @@ int omc_layer_gemma_norms(int layer, float eps, const float *router_scale, const
     CK(e1);
     CK(cudaMemcpy(pes, per_expert_scale, (size_t)E * sizeof(float), cudaMemcpyHostToDevice));
     if (en) CK(cudaMemcpy(en, expert_norm, (size_t)D * sizeof(float), cudaMemcpyHostToDevice));
+    graphs_invalidate();
     L->dev.eps = eps;
     L->dev.g_s2 = s2;
     L->dev.g_pes = pes;
@@ -417,6 +427,7 @@ static int set_expert_slot(omc_layer *L, int slot, int I_, int I_pad, int I_rows
 
 int omc_expert_set(int layer, int e, const int8_t *g, const float *gs, const int8_t *u, const float *us,
                    const int8_t *d, const float *ds) {
+    graphs_invalidate();
     omc_layer *L = omc_get_layer(layer);
     if (!L) return omc_fail(OMC_ENOINIT, "omc_expert_set: layer %d not initialised", layer);
     if (e < 0 || e >= L->desc.E || !g || !gs || !u || !us || !d || !ds)
@@ -427,6 +438,7 @@ int omc_expert_set(int layer, int e, const int8_t *g, const float *gs, const int
 
 int omc_experts_set_packed(int layer, const int8_t *g, const float *gs, const int8_t *u, const float *us,
                            const int8_t *d, const float *ds) {
+    graphs_invalidate();
     omc_layer *L = omc_get_layer(layer);
     if (!L) return omc_fail(OMC_ENOINIT, "omc_experts_set_packed: layer %d not initialised", layer);
     const size_t D = L->desc.D, I = L->desc.I;
@@ -440,6 +452,7 @@ int omc_experts_set_packed(int layer, const int8_t *g, const float *gs, const in
 
 int omc_shared_set(int layer, const int8_t *g, const float *gs, const int8_t *u, const float *us, const int8_t *d,
                    const float *ds, const float *sh_gate) {
+    graphs_invalidate();
     omc_layer *L = omc_get_layer(layer);
     if (!L) return omc_fail(OMC_ENOINIT, "omc_shared_set: layer %d not initialised", layer);
     if (!L->desc.has_shared) return omc_fail(OMC_EINVAL, "omc_shared_set: layer %d has no shared expert", layer);
@@ -477,6 +490,7 @@ static int dec_ensure(const omc_layer_dev *P) {
     if (ci < G.dec_ctr_n) ci = G.dec_ctr_n;
     if (pf < G.dec_part_n) pf = G.dec_part_n;
     CK(cudaDeviceSynchronize());
+    graphs_invalidate();
     cudaFree(G.dec_ctr);
     cudaFree(G.dec_part);
     G.dec_ctr = NULL;
@@ -499,6 +513,7 @@ static int ws_buf(int slot, void **ptr, size_t need) {
     if (G.ws_bytes[slot] >= need && *ptr) return OMC_OK;
     cudaStreamSynchronize(G.stream);
     cudaDeviceSynchronize();
+    graphs_invalidate();
     cudaFree(*ptr);
     *ptr = NULL;
     size_t n = need + need / 4;
@@ -942,6 +957,104 @@ int omc_moe_experts_dev(int layer, const float *x_rows, int R, const int32_t *ex
     return OMC_OK;
 }
 
+/* ---------------------------------------------------- replayed forwards -- */
+/* The device part of omc_moe_forward for one (layer, T) enqueues the same
+ * launches on the same workspace every call.  The first call runs it as is
+ * (allocations and one-time kernel attributes happen there); the second
+ * captures it in a CUDA graph; from then on the graph is replayed, so a
+ * tensor-core forward's six launches and memset cost one graph launch.  A
+ * graph is valid for one generation (graphs_invalidate: layer and expert
+ * set-up, workspace or decode-state growth, forced paths); profiling, the
+ * stage timer and expert parallelism bypass it, and OMC_GRAPHS=0 turns it
+ * off. */
+#define OMC_NGRAPH 64
+typedef struct {
+    int layer, T, gen, warm, failed;
+    cudaGraphExec_t exec;
+    long long launches;     /* kernels in one replay */
+} omc_fgraph;
+static omc_fgraph g_fg[OMC_NGRAPH];
+static int g_nfg, g_fg_next;
+
+static void graphs_release(void) {
+    for (int i = 0; i < g_nfg; ++i)
+        if (g_fg[i].exec) cudaGraphExecDestroy(g_fg[i].exec);
+    memset(g_fg, 0, sizeof(g_fg));
+    g_nfg = g_fg_next = 0;
+}
+
+static int graphs_enabled(void) {
+    static int on = -1;
+    if (on < 0) {
+        const char *e = getenv("OMC_GRAPHS");
+        on = !(e && *e == '0');
+    }
+    return on && !G.profiling && !G.timer_on && G.ep_world <= 1;
+}
+
+static int forward_replayed(omc_layer *L, int layer, int T, cudaStream_t s) {
+    omc_fgraph *g = NULL;
+    for (int i = 0; i < g_nfg; ++i)
+        if (g_fg[i].layer == layer && g_fg[i].T == T) g = &g_fg[i];
+    if (!g) {
+        if (g_nfg < OMC_NGRAPH) g = &g_fg[g_nfg++];
+        else {
+            g = &g_fg[g_fg_next];
+            g_fg_next = (g_fg_next + 1) % OMC_NGRAPH;
+            if (g->exec) cudaGraphExecDestroy(g->exec);
+        }
+        memset(g, 0, sizeof(*g));
+        g->layer = layer;
+        g->T = T;
+        g->gen = g_graph_gen;
+    }
+    if (g->gen != g_graph_gen) {
+        if (g->exec) cudaGraphExecDestroy(g->exec);
+        g->exec = NULL;
+        g->warm = g->failed = 0;
+        g->gen = g_graph_gen;
+    }
+    if (g->exec) {
+        if (cudaGraphLaunch(g->exec, s) != cudaSuccess) {
+            cudaGetLastError();
+            return omc_fail(OMC_ECUDA, "forward replay failed");
+        }
+        omc_g_launches += g->launches;
+        return OMC_OK;
+    }
+    if (!g->warm || g->failed) {
+        g->warm = 1;
+        return omc_forward_device(L, G.ws.x, T, G.ws.out, G.ws.topk_idx, G.ws.topk_w, s);
+    }
+    const long long l0 = omc_g_launches;
+    if (cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
+        cudaGetLastError();
+        g->failed = 1;
+        return omc_forward_device(L, G.ws.x, T, G.ws.out, G.ws.topk_idx, G.ws.topk_w, s);
+    }
+    int rc = omc_forward_device(L, G.ws.x, T, G.ws.out, G.ws.topk_idx, G.ws.topk_w, s);
+    cudaGraph_t graph = NULL;
+    const cudaError_t ce = cudaStreamEndCapture(s, &graph);
+    cudaError_t ie = cudaErrorUnknown;
+    if (!rc && ce == cudaSuccess && graph) ie = cudaGraphInstantiate(&g->exec, graph, 0);
+    if (graph) cudaGraphDestroy(graph);
+    g->launches = omc_g_launches - l0;   /* the kernels one replay launches */
+    omc_g_launches = l0;                 /* the capture itself launched nothing */
+    if (rc || ce != cudaSuccess || ie != cudaSuccess) {
+        cudaGetLastError();
+        g->exec = NULL;
+        g->failed = 1;
+        if (rc) return rc;
+        return omc_forward_device(L, G.ws.x, T, G.ws.out, G.ws.topk_idx, G.ws.topk_w, s);
+    }
+    if (cudaGraphLaunch(g->exec, s) != cudaSuccess) {
+        cudaGetLastError();
+        return omc_fail(OMC_ECUDA, "forward replay failed");
+    }
+    omc_g_launches += g->launches;
+    return OMC_OK;
+}
+
 int omc_moe_forward(int layer, const float *x, int T, float *out, int32_t *topk_idx, float *topk_w) {
     if (!G.init) return omc_fail(OMC_ENOINIT, "omc_moe_forward: omc_init not called");
     omc_layer *L = omc_get_layer(layer);
@@ -953,7 +1066,8 @@ int omc_moe_forward(int layer, const float *x, int T, float *out, int32_t *topk_
     const size_t D = (size_t)L->desc.D, K = (size_t)L->desc.k;
     cudaStream_t s = G.stream;
     if (T > 0) CK(cudaMemcpyAsync(G.ws.x, x, (size_t)T * D * 4, cudaMemcpyHostToDevice, s));
-    if ((rc = omc_forward_device(L, G.ws.x, T, G.ws.out, G.ws.topk_idx, G.ws.topk_w, s))) {
+    if ((rc = (T > 0 && graphs_enabled()) ? forward_replayed(L, layer, T, s)
+                                          : omc_forward_device(L, G.ws.x, T, G.ws.out, G.ws.topk_idx, G.ws.topk_w, s))) {
         cudaStreamSynchronize(s);
         return rc;
     }
@@ -983,6 +1097,7 @@ int omc_debug_wait_timeout(void) {
 int omc_debug_set_path(int path) {
     if (path < 0 || path > 3) return omc_fail(OMC_EINVAL, "omc_debug_set_path: %d", path);
     G.path_override = path;
+    graphs_invalidate();
     return OMC_OK;
 }
 

@@ -200,6 +200,10 @@ int omc_noalloc_setup(int device);
 void *omc_noalloc_scratch_ptr(int device);
 int omc_launch_expf_probe(const float *x, float *y, long long n, cudaStream_t s);
 
+/* anything that changes what a forward enqueues calls this: the host entry's
+ * replayed forwards are rebuilt */
+void omc_graphs_invalidate(void);
+
 /* profiling: ends the named stage on stream s (no-op unless profiling) */
 void omc_prof_mark(cudaStream_t s, const char *name);
 

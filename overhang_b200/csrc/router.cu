@@ -359,6 +359,7 @@ extern "C" int omc_debug_router_tile(int g, int tt, int rr) {
     const int code = g * 100 + tt * 10 + rr;
     if (code != 0 && code != 1644 && code != 1622 && code != 1611 && code != 811) return OMC_EINVAL;
     g_force_tile = code;
+    omc_graphs_invalidate();
     return 0;
 }
 
