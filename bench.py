@@ -320,7 +320,8 @@ def run_ours(args):
     if ep_mode:
         ob.ep_init(rank, world)            # this rank holds experts [rank*E/world, (rank+1)*E/world)
     pyoracle, L = make_layer()
-    layer = ob.MoELayer.from_oracle_layer(0, L)
+    tier = args.tier if args.tier and not ep_mode else 0
+    layer = ob.MoELayer.from_oracle_layer(0, L, tier=(tier, 1, 0) if tier else None)
     ep = None
     if ep_mode:
         from overhang_b200.ep import ExpertParallel, LibCompute
@@ -373,7 +374,7 @@ def run_ours(args):
            "decode_moe" if "decode_moe" in stages else "gemv_gateup")
 
     graph = None
-    if args.graph and not ep_mode:
+    if args.graph and not ep_mode and not tier:
         # one captured forward per input buffer; the timed region replays the graph
         ob.launch_count(reset=True)
         graph = torch.cuda.CUDAGraph()
@@ -508,6 +509,16 @@ def run_ours(args):
                          "step_tensor_frac": (step_flop / (t_max / args.steps / 1e3) / (tf * 1e12)
                                               if tf else None)},
             "clocks": clocks}
+    if tier:
+        # the tiered store: experts outside the HBM slots cross the host link
+        # once per step that routes to them (the tier_fetch stage)
+        _, _, _, slots_now, swaps = layer.tier_stats(tier)
+        misses = int(len(set(ids_seen.tolist()) - set(slots_now.tolist())))
+        f_ms = stages.get("tier_fetch", 0.0)
+        line["config"]["tier_hbm_slots"] = tier
+        line["tier"] = {"hbm_slots": tier, "experts": E, "swaps": swaps, "misses_per_step_est": misses,
+                        "miss_bytes_per_step_est": misses * EXPERT_BYTES, "fetch_stage_ms": f_ms,
+                        "fetch_gbs": misses * EXPERT_BYTES / (f_ms / 1e3) / 1e9 if f_ms > 0 and misses else None}
     if rank == 0 and world == 1 and not args.no_cpu:
         tps, n, kind, cores, dt = cpu_reference_tokens_per_s(pyoracle, L, args.cpu_seconds)
         line["cpu_baseline"] = {"value": tps, "unit": UNIT, "cores": cores, "kind": kind,
@@ -538,6 +549,9 @@ def main():
                     help="time stream launches of the forward instead of graph replays")
     ap.add_argument("--tokens", type=int, default=None,
                     help="tokens per rank instead of the workload's T (the T sweep of the prefill rows)")
+    ap.add_argument("--tier", type=int, default=0,
+                    help="tiered expert store: keep this many experts in HBM, the rest in pinned host memory "
+                         "(LFRU swaps every step; stream launches)")
     ap.add_argument("--mode", default="replica", choices=["ep", "replica"],
                     help="N>1: N independent replicas (the layer fits one GPU), or expert parallel "
                          "(each rank holds E/N experts and its own 512 tokens; rows exchanged with "

@@ -142,6 +142,39 @@ int omc_experts_set_packed(int layer,
 int omc_experts_load(int layer, const char *snapshot, int src_layer, const char *name_g, const char *name_u,
                      const char *name_d, int nthreads);
 
+/* ---- tiered expert store (layers larger than their HBM share) -------- */
+
+/* Keep only `hbm_slots` of the layer's routed experts in HBM; every expert
+ * gets a home copy in mapped pinned host memory, which the kernels read in
+ * place while the expert is not resident.  Replaces the engines' RAM expert
+ * cache (expert_get, engines/olmoe.c:250-272) one level up, with the
+ * reference's hot-store policy (include/tier.h:30-58): the device counts
+ * each forward's routings per expert (heat += slots, last = clock, clock
+ * += 1 per forward; heat halved every `decay_every` forwards, 0 = never);
+ * every `interval` forwards (0 = only omc_tier_step) the counters are read
+ * asynchronously and at most one swap is made -- the coldest slot by LFRU
+ * score (heat << 8 | recency) for the hottest non-resident expert, only past
+ * a 25% + 4-routing margin.  A swap is stream-ordered ahead of the next
+ * forward and changes no result.  Call after omc_layer_init and before the
+ * experts are uploaded (the first hbm_slots uploaded start resident).  Not
+ * with expert parallelism.  Forwards of a tiered layer must be ordered
+ * (one stream, or synchronised by the caller). */
+int omc_tier_enable(int layer, int hbm_slots, int interval, int decay_every);
+
+/* Synchronously read the counters and apply at most one swap now; *eid
+ * (nullable) = the expert moved into HBM, or -1. */
+int omc_tier_step(int layer, int *eid);
+
+/* The counters (heat, last [E], clock; each nullable), the expert in each
+ * HBM slot ([hbm_slots], -1 = not filled yet) and the swaps made so far. */
+int omc_tier_stats(int layer, uint32_t *heat, uint32_t *last, uint32_t *clock, int32_t *slot_expert,
+                   long long *swaps);
+
+/* The replacement rule alone (no device needed): include/tier.h:35-54's
+ * tier_pick_lfru with the same arguments and result. */
+int omc_tier_pick(const uint32_t *heat, const uint32_t *last, uint32_t clock, int nexpert, const int *pinned,
+                  int npin, int *slot, int *eid, long *gain);
+
 /* QWEN shared expert: g,u int8 [Is,D], d int8 [D,Is], their row scales, and
  * the f32 gate vector sh_gate [D] (engines/qwen.c:279-287). */
 int omc_shared_set(int layer,

@@ -426,3 +426,105 @@ void orc_expf_array(const float *x, float *y, int64_t n) {
     #pragma omp parallel for schedule(static)
     for (int64_t i = 0; i < n; i++) y[i] = expf(x[i]);
 }
+
+/* ------------------------------------------------------------ hot store -- */
+/* include/tier.h:30-33 */
+uint64_t orc_tier_score(uint32_t heat, uint32_t last, uint32_t clock) {
+    const uint32_t age = clock - last;
+    const uint64_t recency = age < 255u ? (uint64_t)(255u - age) : 0u;
+    return ((uint64_t)heat << 8) | recency;
+}
+
+/* Residency of expert e: is it named by any of the npin slots
+ * (tier.h:17,45 scan the slots per expert; a flag array is the same set). */
+static unsigned char *tier_resident(int nexpert, const int *pinned, int npin) {
+    unsigned char *r = calloc((size_t)nexpert, 1);
+    if (!r) return NULL;
+    for (int z = 0; z < npin; z++)
+        if (pinned[z] >= 0 && pinned[z] < nexpert) r[pinned[z]] = 1;
+    return r;
+}
+
+/* include/tier.h:35-54 */
+int orc_tier_pick_lfru(const uint32_t *heat, const uint32_t *last, uint32_t clock, int nexpert, const int *pinned,
+                       int npin, int *slot, int *eid, long *gain) {
+    if (!heat || !last || !pinned || npin < 1 || nexpert < 1) return 0;
+    int cold = 0;
+    uint64_t cs = orc_tier_score(heat[pinned[0]], last[pinned[0]], clock);
+    for (int z = 1; z < npin; z++) {
+        const uint64_t v = orc_tier_score(heat[pinned[z]], last[pinned[z]], clock);
+        if (v < cs) {
+            cs = v;
+            cold = z;
+        }
+    }
+    unsigned char *res = tier_resident(nexpert, pinned, npin);
+    if (!res) return 0;
+    int hot = -1;
+    uint64_t hs = 0;
+    for (int e = 0; e < nexpert; e++) {
+        if (res[e]) continue;
+        const uint64_t v = orc_tier_score(heat[e], last[e], clock);
+        if (hot < 0 || v > hs) {
+            hot = e;
+            hs = v;
+        }
+    }
+    free(res);
+    if (hot < 0 || hs <= cs + (cs >> 2) + (4u << 8)) return 0;
+    *slot = cold;
+    *eid = hot;
+    *gain = (long)((hs - cs) >> 8);
+    return 1;
+}
+
+/* include/tier.h:9-24 */
+int orc_tier_pick_heat(const uint32_t *heat, int nexpert, const int *pinned, int npin, int *slot, int *eid,
+                       long *gain) {
+    if (!heat || !pinned || npin < 1 || nexpert < 1) return 0;
+    int cold = 0;
+    for (int z = 1; z < npin; z++)
+        if (heat[pinned[z]] < heat[pinned[cold]]) cold = z;
+    unsigned char *res = tier_resident(nexpert, pinned, npin);
+    if (!res) return 0;
+    int hot = -1;
+    uint32_t hh = 0;
+    for (int e = 0; e < nexpert; e++)
+        if (!res[e] && heat[e] > hh) {
+            hh = heat[e];
+            hot = e;
+        }
+    free(res);
+    if (hot < 0) return 0;
+    const uint32_t hc = heat[pinned[cold]];
+    /* the margin is computed in 32-bit unsigned arithmetic, as tier.h:20 */
+    if (hh <= (uint32_t)(hc + (hc >> 2) + 4u)) return 0;
+    *slot = cold;
+    *eid = hot;
+    *gain = (long)hh - (long)hc;
+    return 1;
+}
+
+/* include/tier.h:56-58 */
+void orc_tier_decay(uint32_t *heat, int nexpert) {
+    for (int e = 0; e < nexpert; e++) heat[e] >>= 1;
+}
+
+void orc_tier_account(const int32_t *topk_idx, int nslots, int nexpert, uint32_t *heat, uint32_t *last,
+                      uint32_t *clock, int decay_every) {
+    const uint32_t clk = *clock + 1u;
+    uint32_t *n = calloc((size_t)(nexpert > 0 ? nexpert : 1), sizeof(uint32_t));
+    if (!n) return;
+    for (int s = 0; s < nslots; s++)
+        if (topk_idx[s] >= 0 && topk_idx[s] < nexpert) n[topk_idx[s]]++;
+    for (int e = 0; e < nexpert; e++) {
+        if (n[e]) {
+            const uint64_t h = (uint64_t)heat[e] + n[e];
+            heat[e] = h > 0xFFFFFFFFull ? 0xFFFFFFFFu : (uint32_t)h;
+            last[e] = clk;
+        }
+        if (decay_every > 0 && clk % (uint32_t)decay_every == 0) heat[e] >>= 1;
+    }
+    *clock = clk;
+    free(n);
+}

@@ -126,6 +126,38 @@ void orc_fill_normal(uint64_t seed, float *dst, int64_t n, float sigma);
 float orc_expf(float x);
 void orc_expf_array(const float *x, float *y, int64_t n);
 
+/* The hot-store replacement policy of include/tier.h (the reference header
+ * has no caller in its engines; these restate its three functions).
+ *
+ * orc_tier_score (tier.h:30-33): (heat << 8) | recency, recency = 255 - age
+ * for age = clock - last (unsigned, wraps) below 255, else 0.
+ *
+ * orc_tier_pick_lfru (tier.h:35-54): the coldest resident slot (lowest score,
+ * first slot on ties) and the hottest non-resident expert (highest score,
+ * lowest id on ties, the first one taken even at score 0); a swap only when
+ * hot > cold + cold/4 + 4*256.  Returns 1 and fills slot/eid/gain
+ * ((hot-cold) >> 8) on a swap, else 0; 0 on a null array, npin < 1 or
+ * nexpert < 1.
+ *
+ * orc_tier_pick_heat (tier.h:9-24): the same on heat alone (margin
+ * cold/4 + 4, a zero-heat expert is never picked).
+ *
+ * orc_tier_decay (tier.h:56-58): heat >>= 1 for every expert. */
+uint64_t orc_tier_score(uint32_t heat, uint32_t last, uint32_t clock);
+int orc_tier_pick_lfru(const uint32_t *heat, const uint32_t *last, uint32_t clock, int nexpert, const int *pinned,
+                       int npin, int *slot, int *eid, long *gain);
+int orc_tier_pick_heat(const uint32_t *heat, int nexpert, const int *pinned, int npin, int *slot, int *eid,
+                       long *gain);
+void orc_tier_decay(uint32_t *heat, int nexpert);
+
+/* The heat a tiered layer gathers from one forward's routing (the library's
+ * own accounting, which the reference leaves to its caller): clock += 1;
+ * for every expert e routed n > 0 times among the T*k slots, heat[e] += n
+ * (saturating at 2^32-1) and last[e] = clock; then, when decay_every > 0 and
+ * clock % decay_every == 0, heat >>= 1 for every expert. */
+void orc_tier_account(const int32_t *topk_idx, int nslots, int nexpert, uint32_t *heat, uint32_t *last,
+                      uint32_t *clock, int decay_every);
+
 #ifdef __cplusplus
 }
 #endif

@@ -368,3 +368,79 @@ def reference_route(L: Layer, x: np.ndarray):
     if rc:
         raise RuntimeError("reference harness failed")
     return idx, w
+
+
+# ------------------------------------------------------------- hot store --
+# include/tier.h restated (moe_oracle.c) and, when built, the reference's own
+# functions (_ref/libref_tier.so).  `pinned` names the expert in each HBM
+# slot; a pick returns (slot, eid, gain) or None.
+
+_u32p = np.ctypeslib.ndpointer(np.uint32, flags="C_CONTIGUOUS")
+_i32p = np.ctypeslib.ndpointer(np.int32, flags="C_CONTIGUOUS")
+
+
+def _tier_bind(L, prefix):
+    lfru = getattr(L, prefix + "pick_lfru")
+    lfru.restype = C.c_int
+    lfru.argtypes = [_u32p, _u32p, C.c_uint32, C.c_int, _i32p, C.c_int, C.POINTER(C.c_int), C.POINTER(C.c_int),
+                     C.POINTER(C.c_long)]
+    heat = getattr(L, prefix + ("pick_heat" if prefix == "orc_tier_" else "pick_swap"))
+    heat.restype = C.c_int
+    heat.argtypes = [_u32p, C.c_int, _i32p, C.c_int, C.POINTER(C.c_int), C.POINTER(C.c_int), C.POINTER(C.c_long)]
+    score = getattr(L, prefix + ("score" if prefix == "orc_tier_" else "lfru_score"))
+    score.restype = C.c_uint64
+    score.argtypes = [C.c_uint32, C.c_uint32, C.c_uint32]
+    getattr(L, prefix + "decay").argtypes = [_u32p, C.c_int]
+    return lfru, heat, score, getattr(L, prefix + "decay")
+
+
+class Tier:
+    """The four tier.h functions from one library (the restatement or the
+    reference build)."""
+
+    def __init__(self, which: str = "oracle"):
+        if which == "oracle":
+            L = lib()
+            self.lfru, self.heat, self.score_fn, self.decay_fn = _tier_bind(L, "orc_tier_")
+            L.orc_tier_account.argtypes = [_i32p, C.c_int, C.c_int, _u32p, _u32p, C.POINTER(C.c_uint32), C.c_int]
+            self._account = L.orc_tier_account
+        else:
+            R = ref_lib("tier")
+            if R is None:
+                raise RuntimeError("reference tier.h harness not built (oracle/_ref/libref_tier.so)")
+            self.lfru, self.heat, self.score_fn, self.decay_fn = _tier_bind(R, "ref_tier_")
+            self._account = None
+
+    @staticmethod
+    def _out(rc, slot, eid, gain):
+        return (slot.value, eid.value, gain.value) if rc else None
+
+    def pick_lfru(self, heat, last, clock, pinned):
+        heat, last = np.ascontiguousarray(heat, np.uint32), np.ascontiguousarray(last, np.uint32)
+        pinned = np.ascontiguousarray(pinned, np.int32)
+        s, e, g = C.c_int(-1), C.c_int(-1), C.c_long(0)
+        rc = self.lfru(heat, last, clock & 0xFFFFFFFF, heat.size, pinned, pinned.size, C.byref(s), C.byref(e),
+                       C.byref(g))
+        return self._out(rc, s, e, g)
+
+    def pick_heat(self, heat, pinned):
+        heat, pinned = np.ascontiguousarray(heat, np.uint32), np.ascontiguousarray(pinned, np.int32)
+        s, e, g = C.c_int(-1), C.c_int(-1), C.c_long(0)
+        rc = self.heat(heat, heat.size, pinned, pinned.size, C.byref(s), C.byref(e), C.byref(g))
+        return self._out(rc, s, e, g)
+
+    def score(self, heat, last, clock):
+        return int(self.score_fn(heat & 0xFFFFFFFF, last & 0xFFFFFFFF, clock & 0xFFFFFFFF))
+
+    def decay(self, heat):
+        h = np.array(heat, np.uint32)
+        self.decay_fn(h, h.size)
+        return h
+
+    def account(self, topk_idx, nexpert, heat, last, clock, decay_every=0):
+        """One forward's routing into (heat, last, clock); returns the new triple."""
+        idx = np.ascontiguousarray(topk_idx, np.int32).ravel()
+        h, l = np.array(heat, np.uint32), np.array(last, np.uint32)
+        c = C.c_uint32(clock)
+        self._account(idx, idx.size, nexpert, h, l, C.byref(c), decay_every)
+        return h, l, c.value

@@ -53,6 +53,10 @@ SIGNATURES = {
     "omc_experts_set_packed": (_i, [_i, _vp, _vp, _vp, _vp, _vp, _vp]),
     "omc_experts_load": (_i, [_i, C.c_char_p, _i, C.c_char_p, C.c_char_p, C.c_char_p, _i]),
     "omc_shared_set": (_i, [_i, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
+    "omc_tier_enable": (_i, [_i, _i, _i, _i]),
+    "omc_tier_step": (_i, [_i, _vp]),
+    "omc_tier_stats": (_i, [_i, _vp, _vp, _vp, _vp, _vp]),
+    "omc_tier_pick": (_i, [_vp, _vp, C.c_uint32, _i, _vp, _i, _vp, _vp, _vp]),
     "omc_moe_forward": (_i, [_i, _vp, _i, _vp, _vp, _vp]),
     "omc_moe_forward_dev": (_i, [_i, _vp, _i, _vp, _vp, _vp, _vp]),
     "omc_moe_forward_noalloc": (_i, [_i, _vp, _i, _vp, _vp, _vp, _vp]),
@@ -133,6 +137,17 @@ def _p(a):
     return None if a is None else a.ctypes.data_as(C.c_void_p)
 
 
+def tier_pick(heat, last, clock: int, pinned):
+    """The library's hot-store replacement rule (omc_tier_pick, no device
+    needed): (slot, expert, gain) of the swap it would make, or None."""
+    heat, last = np.ascontiguousarray(heat, np.uint32), np.ascontiguousarray(last, np.uint32)
+    pinned = np.ascontiguousarray(pinned, np.int32)
+    s, e, g = C.c_int(-1), C.c_int(-1), C.c_long(0)
+    rc = lib().omc_tier_pick(_p(heat), _p(last), clock & 0xFFFFFFFF, heat.size, _p(pinned), pinned.size,
+                             C.byref(s), C.byref(e), C.byref(g))
+    return (s.value, e.value, g.value) if rc else None
+
+
 def init(device: int = 0, slab_bytes: int = 0) -> None:
     check(lib().omc_init(device, slab_bytes), "omc_init")
 
@@ -204,11 +219,14 @@ class MoELayer:
     has_shared = property(lambda self: self.desc.has_shared)
 
     @classmethod
-    def from_oracle_layer(cls, layer: int, L) -> "MoELayer":
-        """Upload a seeded layer built by oracle.pyoracle.make_layer (tests/bench)."""
+    def from_oracle_layer(cls, layer: int, L, tier=None) -> "MoELayer":
+        """Upload a seeded layer built by oracle.pyoracle.make_layer (tests/bench).
+        tier = (hbm_slots, interval, decay_every): a tiered layer (omc_tier_enable)."""
         a = L.arrays
         m = cls(layer, L.family, L.D, L.I, L.E, L.k, a["router"], a.get("router_s"),
                 L.renorm, L.has_shared, L.Is)
+        if tier is not None:
+            m.tier_enable(*tier)
         if L.family == FAMILY_GEMMA:
             m.set_gemma_norms(L.eps, a["g_rscale"], a["g_pes"], a.get("g_enorm"))
         m.set_experts_packed(a["g"], a["gs"], a["u"], a["us"], a["d"], a["ds"])
@@ -235,6 +253,27 @@ class MoELayer:
         check(lib().omc_debug_gemma_prenorm(self.layer, _p(x), T, _p(xr), _p(xe), _p(r)),
               "omc_debug_gemma_prenorm")
         return xr, xe, r
+
+    def tier_enable(self, hbm_slots: int, interval: int = 1, decay_every: int = 0) -> None:
+        """Tiered expert store: hbm_slots experts in HBM, the rest read from
+        pinned host memory; LFRU swaps every `interval` forwards."""
+        check(lib().omc_tier_enable(self.layer, hbm_slots, interval, decay_every), "omc_tier_enable")
+
+    def tier_step(self) -> int:
+        """Apply at most one swap now; the expert moved into HBM, or -1."""
+        e = C.c_int(-1)
+        check(lib().omc_tier_step(self.layer, C.byref(e)), "omc_tier_step")
+        return e.value
+
+    def tier_stats(self, hbm_slots: int):
+        """(heat [E], last [E], clock, expert per HBM slot, swaps)."""
+        E = self.desc.E
+        heat, last = np.empty(E, np.uint32), np.empty(E, np.uint32)
+        clock, swaps = C.c_uint32(0), C.c_longlong(0)
+        slots = np.empty(hbm_slots, np.int32)
+        check(lib().omc_tier_stats(self.layer, _p(heat), _p(last), C.byref(clock), _p(slots), C.byref(swaps)),
+              "omc_tier_stats")
+        return heat, last, clock.value, slots, swaps.value
 
     def load_experts(self, snapshot: str, src_layer: int, name_g: str, name_u, name_d: str,
                      nthreads: int = 0) -> None:

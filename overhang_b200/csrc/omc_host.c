@@ -180,7 +180,9 @@ void omc_shutdown(void) {
     cudaDeviceSynchronize();
     graphs_release();
     omc_ep_release();
+    omc_tier_release();
     for (int i = 0; i < G.nlayers; ++i) {
+        omc_tier_free(&G.layers[i]);
         free(G.layers[i].h_experts);
         cudaFree(G.layers[i].d_experts_tab);
     }
@@ -241,6 +243,8 @@ int omc_layer_init(int layer, const omc_moe_desc *d, const void *router_w, const
     omc_layer *L = &G.layers[layer];
     graphs_invalidate();
     if (L->used) {
+        cudaDeviceSynchronize();
+        omc_tier_free(L);
         free(L->h_experts);
         cudaFree(L->d_experts_tab);
         /* slab space of a re-initialised layer is not reclaimed (bump allocator) */
@@ -433,6 +437,7 @@ int omc_expert_set(int layer, int e, const int8_t *g, const float *gs, const int
     if (e < 0 || e >= L->desc.E || !g || !gs || !u || !us || !d || !ds)
         return omc_fail(OMC_EINVAL, "omc_expert_set: bad expert %d or null pointer", e);
     if (e < L->e0 || e >= L->e0 + L->ne) return OMC_OK;   /* owned by another EP rank */
+    if (L->tier) return omc_tier_upload(L, e, g, gs, u, us, d, ds);
     return set_expert_slot(L, e, L->desc.I, L->dev.I_pad, L->dev.I_rows, g, gs, u, us, d, ds);
 }
 
@@ -769,7 +774,7 @@ static int forward_on_ws(omc_layer *L, const omc_ws *ws, const float *x, int T, 
      * CUDA-core dequant-and-dot is the bound and the separate kernels win
      * (measured on B200), so larger T take it only when it is forced.  It
      * takes GEMMA's residual rows as they are and norms them itself. */
-    if (!mma && G.ep_world <= 1 && (G.path_override == 3 || (G.path_override == 0 && T == 1)) &&
+    if (!mma && G.ep_world <= 1 && !L->tier && (G.path_override == 3 || (G.path_override == 0 && T == 1)) &&
         omc_decode_supported(&L->dev, T, G.num_sms, G.dec_ctr_n, G.dec_part_n)) {
         if ((rc = omc_launch_decode(&L->dev, x, x, T, ws, G.num_sms, G.dec_ctr, G.dec_part, idx, w, out, s)))
             return omc_fail(rc, "fused decode launch failed (%s)", omc_strerror(rc));
@@ -788,6 +793,8 @@ static int forward_on_ws(omc_layer *L, const omc_ws *ws, const float *x, int T, 
     if ((rc = omc_launch_router(&L->dev, xr, T, ws, idx, w, mma ? &plan : NULL, s)))
         return omc_fail(rc, "router launch failed");
     omc_prof_mark(s, "router_select");
+    /* a tiered layer: the routed experts outside HBM are copied in first */
+    if ((rc = omc_tier_route(L, idx, T, s))) return omc_fail(rc, "tier fetch launch failed");
     if (mma) {
         rc = omc_launch_mma_ffn(&L->dev, xe, T, ws, idx, w, out, s);
         if (rc == OMC_EUNSUPPORTED && G.path_override != 2) {
@@ -888,7 +895,9 @@ int omc_moe_forward_noalloc(int layer, const float *x, int T, float *out, int32_
     memset(&ws, 0, sizeof(ws));
     noalloc_layout(&L->dev, T, base, &ws);
     cudaStream_t s = stream ? (cudaStream_t)stream : G.stream;
-    return forward_on_ws(L, &ws, x, T, out, topk_idx, topk_w, s);
+    if ((rc = omc_tier_before(L, s))) return rc;
+    if ((rc = forward_on_ws(L, &ws, x, T, out, topk_idx, topk_w, s))) return rc;
+    return omc_tier_after(L, s);
 }
 
 int omc_moe_forward_dev(int layer, const float *x, int T, float *out, int32_t *topk_idx, float *topk_w,
@@ -901,7 +910,10 @@ int omc_moe_forward_dev(int layer, const float *x, int T, float *out, int32_t *t
         return omc_fail(OMC_EINVAL, "omc_moe_forward_dev: x and out must be 16-byte aligned");
     if (T == 0 && G.ep_world <= 1) return OMC_OK;
     cudaStream_t s = stream ? (cudaStream_t)stream : G.stream;
-    return omc_forward_device(L, x, T, out, topk_idx, topk_w, s);
+    int rc;
+    if ((rc = omc_tier_before(L, s))) return rc;
+    if ((rc = omc_forward_device(L, x, T, out, topk_idx, topk_w, s))) return rc;
+    return omc_tier_after(L, s);
 }
 
 int omc_moe_route_dev(int layer, const float *x, int T, int32_t *topk_idx, float *topk_w, float *shared_gate,
@@ -941,6 +953,7 @@ int omc_moe_experts_dev(int layer, const float *x_rows, int R, const int32_t *ex
         return omc_fail(OMC_EINVAL, "omc_moe_experts_dev: x_rows and y must be 16-byte aligned");
     if (R == 0) return OMC_OK;
     int rc;
+    if (L->tier) return omc_fail(OMC_EUNSUPPORTED, "omc_moe_experts_dev: not on a tiered layer");
     for (int e = L->e0; e < L->e0 + L->ne; ++e)
         if (!L->have[e]) return omc_fail(OMC_ENOINIT, "omc_moe_experts_dev: expert %d not uploaded", e);
     if (L->desc.has_shared && !L->have[L->desc.E])
@@ -1066,8 +1079,10 @@ int omc_moe_forward(int layer, const float *x, int T, float *out, int32_t *topk_
     const size_t D = (size_t)L->desc.D, K = (size_t)L->desc.k;
     cudaStream_t s = G.stream;
     if (T > 0) CK(cudaMemcpyAsync(G.ws.x, x, (size_t)T * D * 4, cudaMemcpyHostToDevice, s));
-    if ((rc = (T > 0 && graphs_enabled()) ? forward_replayed(L, layer, T, s)
-                                          : omc_forward_device(L, G.ws.x, T, G.ws.out, G.ws.topk_idx, G.ws.topk_w, s))) {
+    if ((rc = omc_tier_before(L, s)) ||
+        (rc = (T > 0 && graphs_enabled()) ? forward_replayed(L, layer, T, s)
+                                          : omc_forward_device(L, G.ws.x, T, G.ws.out, G.ws.topk_idx, G.ws.topk_w, s)) ||
+        (rc = omc_tier_after(L, s))) {
         cudaStreamSynchronize(s);
         return rc;
     }

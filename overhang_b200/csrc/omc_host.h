@@ -24,6 +24,7 @@ typedef struct {
     unsigned char *have;            /* uploaded flags [E+1]                 */
     int e0, ne;                     /* experts owned by this rank (EP)      */
     int gemma_ready;                /* GEMMA: omc_layer_gemma_norms called  */
+    void *tier;                     /* tiered expert store (omc_tier.c)     */
 } omc_layer;
 
 typedef struct {
@@ -89,6 +90,15 @@ int omc_matrix_upload(const int8_t *q, const float *s, int O, int K, int8_t **dq
 int omc_check_device_error(void);
 int omc_forward_device(omc_layer *L, const float *x, int T, float *out, int32_t *topk_idx, float *topk_w,
                        cudaStream_t s);
+
+/* tiered expert store (omc_tier.c) */
+int omc_tier_upload(omc_layer *L, int e, const int8_t *g, const float *gs, const int8_t *u, const float *us,
+                    const int8_t *d, const float *ds);
+void omc_tier_free(omc_layer *L);
+int omc_tier_before(omc_layer *L, cudaStream_t s);
+int omc_tier_route(omc_layer *L, const int32_t *idx, int T, cudaStream_t s);
+void omc_tier_release(void);
+int omc_tier_after(omc_layer *L, cudaStream_t s);
 
 /* expert parallelism (omc_ep.c) */
 int omc_ep_forward(omc_layer *L, const float *x, int T, float *out, int32_t *topk_idx, float *topk_w,

@@ -37,6 +37,12 @@ Cases:
                 rule (tools/convert_gemma.py:35-40)
 For Gemma the oracle runs with the reference's powf (RSQRT_LIBM) so that it
 is bit-identical to the reference; ``eps`` holds rms_norm_eps.
+
+``tier_cases.npz`` holds hot-store policy cases (include/tier.h, compiled
+from the reference as oracle/_ref/libref_tier.so): heat/last/clock/pinned
+inputs, including exact ties, margins on and one past the hysteresis bound,
+clock wrap-around and 32-bit heat overflow, with the results of the
+reference's tier_pick_lfru, tier_pick_swap, tier_lfru_score and tier_decay.
 """
 import ctypes as C
 import os
@@ -204,6 +210,57 @@ def main():
         save(f"qwen_tiny_l{li}", L, x, out, {"out_ref_f32_resident": f32})
 
     gemma_cases()
+    tier_cases()
+
+
+def tier_cases(n=480, emax=64):
+    """Policy cases through the reference's own tier.h functions."""
+    R = P.Tier("ref")
+    rng = np.random.default_rng(2024)
+    H = np.zeros((n, emax), np.uint32)
+    La = np.zeros((n, emax), np.uint32)
+    PIN = np.full((n, emax), -1, np.int32)
+    E_, NP, CLK = np.zeros(n, np.int32), np.zeros(n, np.int32), np.zeros(n, np.uint32)
+    for c in range(n):
+        E = int(rng.integers(1, emax + 1))
+        npin = int(rng.integers(1, E + 1))
+        kind = c % 8
+        hi = [4, 64, 1 << 12, 1 << 24, 2**32 - 1, 16, 1 << 10, 3][kind]
+        heat = rng.integers(0, hi, E, dtype=np.uint64).astype(np.uint32)
+        clock = int(rng.integers(0, 2**32)) if kind != 5 else int(rng.integers(0, 300))
+        last = ((clock - rng.integers(0, 600, E)) & 0xFFFFFFFF).astype(np.uint32)
+        if kind == 5:                       # last recorded before a clock wrap-around
+            last[: E // 2] = (2**32 - rng.integers(1, 50, E // 2)).astype(np.uint32)
+        pinned = rng.choice(E, npin, replace=False).astype(np.int32)
+        if kind == 2:                       # exact ties
+            heat[:] = heat[0]
+            last[:] = last[0]
+        if kind == 3 and npin < E:          # hottest outsider on, or one past, the margin
+            cold = int(pinned[0])
+            heat[pinned] = np.maximum(heat[pinned], heat[cold])
+            last[pinned] = clock
+            out = [e for e in range(E) if e not in set(pinned.tolist())]
+            cs = R.score(int(heat[cold]), int(last[cold]), clock)
+            bound = cs + (cs >> 2) + (4 << 8) + (c // 8) % 2
+            heat[out] = 0
+            heat[out[0]] = bound >> 8
+            last[out[0]] = (clock - (255 - (bound & 255))) & 0xFFFFFFFF
+        H[c, :E], La[c, :E], PIN[c, :npin] = heat, last, pinned
+        E_[c], NP[c], CLK[c] = E, npin, clock
+    res_l = np.full((n, 4), -1, np.int64)
+    res_h = np.full((n, 4), -1, np.int64)
+    scores = np.zeros((n, emax), np.uint64)
+    decayed = np.zeros((n, emax), np.uint32)
+    for c in range(n):
+        E, npin = int(E_[c]), int(NP[c])
+        a = R.pick_lfru(H[c, :E], La[c, :E], int(CLK[c]), PIN[c, :npin])
+        b = R.pick_heat(H[c, :E], PIN[c, :npin])
+        res_l[c] = (1, *a) if a else (0, -1, -1, 0)
+        res_h[c] = (1, *b) if b else (0, -1, -1, 0)
+        scores[c, :E] = [R.score(int(H[c, e]), int(La[c, e]), int(CLK[c])) for e in range(E)]
+        decayed[c, :E] = R.decay(H[c, :E])
+    np.savez_compressed(os.path.join(HERE, "tier_cases.npz"), heat=H, last=La, pinned=PIN, E=E_, npin=NP,
+                        clock=CLK, lfru=res_l, swap=res_h, score=scores, decay=decayed)
 
 
 if __name__ == "__main__":
