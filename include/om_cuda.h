@@ -81,8 +81,9 @@ typedef struct omc_moe_desc {
 /* ---- lifetime ------------------------------------------------------- */
 
 /* Bind this process to CUDA `device` and reserve the HBM expert slab.
- * slab_bytes = 0: use free HBM minus a 4 GiB reserve.  Replaces omm_init
- * (metal/om_metal.h:13-14). */
+ * slab_bytes = 0: use free HBM minus a 4 GiB reserve.  An upload past the
+ * budget fails with OMC_ENOMEM (a layer larger than its share of HBM uses
+ * omc_tier_enable).  Replaces omm_init (metal/om_metal.h:13-14). */
 int omc_init(int device, size_t slab_bytes);
 
 /* Free every device and pinned resource (and the NCCL communicator). */
@@ -145,8 +146,11 @@ int omc_experts_load(int layer, const char *snapshot, int src_layer, const char 
 /* ---- tiered expert store (layers larger than their HBM share) -------- */
 
 /* Keep only `hbm_slots` of the layer's routed experts in HBM; every expert
- * gets a home copy in mapped pinned host memory, which the kernels read in
- * place while the expert is not resident.  Replaces the engines' RAM expert
+ * gets a home copy in mapped pinned host memory.  A forward that routes to
+ * a non-resident expert copies it from its home into an HBM miss area right
+ * after routing (one crossing of the host link); kernels read HBM only.  The
+ * T = 1 forward of a tiered layer takes the router + CUDA-core path, not the
+ * fused decode kernel.  Replaces the engines' RAM expert
  * cache (expert_get, engines/olmoe.c:250-272) one level up, with the
  * reference's hot-store policy (include/tier.h:30-58): the device counts
  * each forward's routings per expert (heat += slots, last = clock, clock

@@ -83,55 +83,42 @@ long long omc_launch_count(int reset) {
 
 /* ---------------------------------------------------------------- slab -- */
 /* One budget of HBM for expert weights, handed out in 256-byte aligned
- * pieces from 1 GiB chunks cudaMalloc'd on demand.  Past the budget,
- * weights go to mapped pinned host memory, which the kernels read over the
- * host link (slower, but the layer still runs). */
+ * pieces from 1 GiB chunks cudaMalloc'd on demand.  Past the budget an
+ * upload fails with OMC_ENOMEM: the kernels copy weights with bulk
+ * asynchronous copies and are only ever given HBM.  A layer larger than its
+ * share of HBM uses the tiered store instead (omc_tier.c), whose host copies
+ * reach HBM before any kernel reads them.  *on_host is always 0. */
 #define SLAB_CHUNK ((size_t)1 << 30)
 
 void *omc_slab_alloc(size_t n, int *on_host) {
     n = (n + 255) & ~(size_t)255;
     *on_host = 0;
-    if (G.slab_used + n <= G.slab_budget) {
-        if (!G.nchunk || G.chunk_used + n > G.chunk_size[G.nchunk - 1]) {
-            if (G.nchunk == OMC_MAX_CHUNKS) goto host;
-            size_t sz = n > SLAB_CHUNK ? n : SLAB_CHUNK;
-            if (sz > G.slab_budget - G.slab_used) sz = G.slab_budget - G.slab_used;
-            if (sz < n) goto host;
-            void *p = NULL;
-            if (cudaMalloc(&p, sz) != cudaSuccess) {
-                cudaGetLastError();
-                goto host;
-            }
-            G.chunk[G.nchunk] = p;
-            G.chunk_size[G.nchunk] = sz;
-            G.nchunk++;
-            G.chunk_used = 0;
-        }
-        void *p = (char *)G.chunk[G.nchunk - 1] + G.chunk_used;
-        G.chunk_used += n;
-        G.slab_used += n;
-        return p;
-    }
-host:
-    if (G.nhost == OMC_MAX_HOST_BLOCKS) return NULL;
-    {
-        void *h = NULL;
-        if (cudaHostAlloc(&h, n, cudaHostAllocMapped | cudaHostAllocPortable) != cudaSuccess) {
+    if (G.slab_used + n > G.slab_budget) return NULL;
+    if (!G.nchunk || G.chunk_used + n > G.chunk_size[G.nchunk - 1]) {
+        if (G.nchunk == OMC_MAX_CHUNKS) return NULL;
+        size_t sz = n > SLAB_CHUNK ? n : SLAB_CHUNK;
+        if (sz > G.slab_budget - G.slab_used) sz = G.slab_budget - G.slab_used;
+        if (sz < n) return NULL;
+        void *p = NULL;
+        if (cudaMalloc(&p, sz) != cudaSuccess) {
             cudaGetLastError();
             return NULL;
         }
-        G.host_blocks[G.nhost++] = h;
-        G.host_bytes += n;
-        *on_host = 1;
-        return h;   /* UVA: the host pointer is valid in kernels */
+        G.chunk[G.nchunk] = p;
+        G.chunk_size[G.nchunk] = sz;
+        G.nchunk++;
+        G.chunk_used = 0;
     }
+    void *p = (char *)G.chunk[G.nchunk - 1] + G.chunk_used;
+    G.chunk_used += n;
+    G.slab_used += n;
+    return p;
 }
 
 static void slab_release(void) {
     for (int i = 0; i < G.nchunk; ++i) cudaFree(G.chunk[i]);
-    for (int i = 0; i < G.nhost; ++i) cudaFreeHost(G.host_blocks[i]);
-    G.nchunk = G.nhost = 0;
-    G.slab_used = G.chunk_used = G.host_bytes = 0;
+    G.nchunk = 0;
+    G.slab_used = G.chunk_used = 0;
 }
 
 /* ---------------------------------------------------------------- init -- */
@@ -352,7 +339,7 @@ static int upload_matrix(const int8_t *q, const float *s, int O, int K, int O_pa
                          const float **ws, const float *scales_into) {
     int on_host;
     float *dsc = scales_into ? (float *)scales_into : omc_slab_alloc((size_t)O_pad * sizeof(float), &on_host);
-    if (!dsc) return omc_fail(OMC_ENOMEM, "expert upload: slab and host overflow exhausted");
+    if (!dsc) return omc_fail(OMC_ENOMEM, "expert upload: slab budget exhausted (omc_init slab_bytes; omc_tier_enable for a layer larger than its HBM share)");
     int rc = staging_ensure((size_t)O * K);
     if (rc) return rc;
     CK(cudaMemcpyAsync(G.staging, q, (size_t)O * K, cudaMemcpyHostToDevice, G.stream));
@@ -379,7 +366,7 @@ int omc_expert_upload(int D, int D_pad, int D_rows, int I_, int I_pad, int I_row
     const size_t d_bytes = (size_t)omc_round_up(D_rows, 2 * OMC_TM) * I_pad;
     int8_t *gu = reuse ? (int8_t *)ep->g : omc_slab_alloc(gu_bytes, &on_host);
     int8_t *dd = reuse ? (int8_t *)ep->d : omc_slab_alloc(d_bytes, &on_host2);
-    if (!gu || !dd) return omc_fail(OMC_ENOMEM, "expert upload: slab and host overflow exhausted");
+    if (!gu || !dd) return omc_fail(OMC_ENOMEM, "expert upload: slab budget exhausted (omc_init slab_bytes; omc_tier_enable for a layer larger than its HBM share)");
     (void)on_host;
     (void)on_host2;
     CK(cudaMemsetAsync(dd, 0, d_bytes, G.stream));   /* gu is fully written by the two relayouts */
@@ -406,7 +393,7 @@ int omc_matrix_upload(const int8_t *q, const float *s, int O, int K, int8_t **dq
     const size_t bytes = (size_t)omc_round_up(O_rows, 2 * OMC_TM) * K_pad;
     int on_host = 0, rc;
     int8_t *d = reuse ? *dq : omc_slab_alloc(bytes, &on_host);
-    if (!d) return omc_fail(OMC_ENOMEM, "matrix upload: slab and host overflow exhausted");
+    if (!d) return omc_fail(OMC_ENOMEM, "matrix upload: slab budget exhausted (omc_init slab_bytes; omc_tier_enable for a layer larger than its HBM share)");
     (void)on_host;
     CK(cudaMemsetAsync(d, 0, bytes, G.stream));
     const float *sd = NULL;

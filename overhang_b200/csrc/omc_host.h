@@ -11,7 +11,6 @@ extern "C" {
 #endif
 
 #define OMC_MAX_CHUNKS 512
-#define OMC_MAX_HOST_BLOCKS 65536
 #define OMC_NSTAGE_EV 12
 #define OMC_TIMER_RING 1024          /* stage-timer event pairs kept */
 
@@ -43,12 +42,10 @@ typedef struct {
     cudaStream_t stream;
     int *d_err;
     /* slab */
-    size_t slab_budget, slab_used, chunk_used, host_bytes;
+    size_t slab_budget, slab_used, chunk_used;
     void *chunk[OMC_MAX_CHUNKS];
     size_t chunk_size[OMC_MAX_CHUNKS];
     int nchunk;
-    void *host_blocks[OMC_MAX_HOST_BLOCKS];
-    int nhost;
     void *staging;
     size_t staging_bytes;
     /* layers */
