@@ -359,11 +359,13 @@ def run_ours(args):
     # (profiling events between kernels, one synchronised forward at a time)
     ob.set_profiling(True)
     st = []
+    pmiss0 = layer.tier_stats(tier)[5] if tier else 0
     for i in range(5):
         step(i)
         torch.cuda.synchronize()
         st.append(ob.stage_times())
     ob.set_profiling(False)
+    prof_misses = ((layer.tier_stats(tier)[5] - pmiss0) / 5) if tier else 0
     stage_names = [n for n, _ in st[-1]] if st and st[-1] else []
     stage_ms = np.array([[v for _, v in row] for row in st]).mean(axis=0).tolist() if stage_names else []
     stages = dict(zip(stage_names, stage_ms))
@@ -387,6 +389,7 @@ def run_ours(args):
         args.steps = max(1, args.steps // nbuf) * nbuf
 
     barrier()
+    miss0 = layer.tier_stats(tier)[5] if tier else 0
     clk = ClockSampler(dev)
     clk.start()
     ob.launch_count(reset=True)
@@ -404,6 +407,7 @@ def run_ours(args):
     barrier()
     launches = ob.launch_count() if graph is None else graph_launches * (args.steps // nbuf)
     clocks = clk.stop()
+    miss1 = layer.tier_stats(tier)[5] if tier else 0
     if graph is not None:
         # the dominant kernel's launch time, from a short pass outside the graph
         ob.time_stage(dom)
@@ -512,13 +516,17 @@ def run_ours(args):
     if tier:
         # the tiered store: experts outside the HBM slots cross the host link
         # once per step that routes to them (the tier_fetch stage)
-        _, _, _, slots_now, swaps = layer.tier_stats(tier)
-        misses = int(len(set(ids_seen.tolist()) - set(slots_now.tolist())))
+        swaps = layer.tier_stats(tier)[4]
+        misses = (miss1 - miss0) / args.steps        # counted on the device over the timed steps
         f_ms = stages.get("tier_fetch", 0.0)
         line["config"]["tier_hbm_slots"] = tier
-        line["tier"] = {"hbm_slots": tier, "experts": E, "swaps": swaps, "misses_per_step_est": misses,
-                        "miss_bytes_per_step_est": misses * EXPERT_BYTES, "fetch_stage_ms": f_ms,
-                        "fetch_gbs": misses * EXPERT_BYTES / (f_ms / 1e3) / 1e9 if f_ms > 0 and misses else None}
+        line["tier"] = {"hbm_slots": tier, "experts": E, "swaps": swaps, "misses_per_step": misses,
+                        "miss_bytes_per_step": misses * EXPERT_BYTES,
+                        # the fetch stage (routing step + copies) timed over the five profiled steps,
+                        # against the misses of those same steps
+                        "fetch_stage_ms": f_ms, "fetch_misses_per_step": prof_misses,
+                        "fetch_gbs": (prof_misses * EXPERT_BYTES / (f_ms / 1e3) / 1e9
+                                      if f_ms > 0 and prof_misses else None)}
     if rank == 0 and world == 1 and not args.no_cpu:
         tps, n, kind, cores, dt = cpu_reference_tokens_per_s(pyoracle, L, args.cpu_seconds)
         line["cpu_baseline"] = {"value": tps, "unit": UNIT, "cores": cores, "kind": kind,

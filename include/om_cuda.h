@@ -170,9 +170,11 @@ int omc_tier_enable(int layer, int hbm_slots, int interval, int decay_every);
 int omc_tier_step(int layer, int *eid);
 
 /* The counters (heat, last [E], clock; each nullable), the expert in each
- * HBM slot ([hbm_slots], -1 = not filled yet) and the swaps made so far. */
+ * HBM slot ([hbm_slots], -1 = not filled yet), the swaps made so far and
+ * the misses so far (routed non-resident experts copied in, summed over
+ * forwards). */
 int omc_tier_stats(int layer, uint32_t *heat, uint32_t *last, uint32_t *clock, int32_t *slot_expert,
-                   long long *swaps);
+                   long long *swaps, long long *misses);
 
 /* The replacement rule alone (no device needed): include/tier.h:35-54's
  * tier_pick_lfru with the same arguments and result. */

@@ -55,7 +55,7 @@ SIGNATURES = {
     "omc_shared_set": (_i, [_i, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "omc_tier_enable": (_i, [_i, _i, _i, _i]),
     "omc_tier_step": (_i, [_i, _vp]),
-    "omc_tier_stats": (_i, [_i, _vp, _vp, _vp, _vp, _vp]),
+    "omc_tier_stats": (_i, [_i, _vp, _vp, _vp, _vp, _vp, _vp]),
     "omc_tier_pick": (_i, [_vp, _vp, C.c_uint32, _i, _vp, _i, _vp, _vp, _vp]),
     "omc_moe_forward": (_i, [_i, _vp, _i, _vp, _vp, _vp]),
     "omc_moe_forward_dev": (_i, [_i, _vp, _i, _vp, _vp, _vp, _vp]),
@@ -266,14 +266,14 @@ class MoELayer:
         return e.value
 
     def tier_stats(self, hbm_slots: int):
-        """(heat [E], last [E], clock, expert per HBM slot, swaps)."""
+        """(heat [E], last [E], clock, expert per HBM slot, swaps, misses)."""
         E = self.desc.E
         heat, last = np.empty(E, np.uint32), np.empty(E, np.uint32)
-        clock, swaps = C.c_uint32(0), C.c_longlong(0)
+        clock, swaps, misses = C.c_uint32(0), C.c_longlong(0), C.c_longlong(0)
         slots = np.empty(hbm_slots, np.int32)
-        check(lib().omc_tier_stats(self.layer, _p(heat), _p(last), C.byref(clock), _p(slots), C.byref(swaps)),
-              "omc_tier_stats")
-        return heat, last, clock.value, slots, swaps.value
+        check(lib().omc_tier_stats(self.layer, _p(heat), _p(last), C.byref(clock), _p(slots), C.byref(swaps),
+                                   C.byref(misses)), "omc_tier_stats")
+        return heat, last, clock.value, slots, swaps.value, misses.value
 
     def load_experts(self, snapshot: str, src_layer: int, name_g: str, name_u, name_d: str,
                      nthreads: int = 0) -> None:

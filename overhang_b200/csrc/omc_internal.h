@@ -207,11 +207,12 @@ void omc_graphs_invalidate(void);
 /* a tiered layer after routing (tier.cu): hot-store counters (stats =
  * [heat E][last E][clock]), routed non-resident experts listed and pointed
  * at miss-area images, which are then filled from their home images.
- * layout = {image bytes, off_d, off_gs, off_us, off_ds}; list [1 + E]. */
+ * layout = {image bytes, off_d, off_gs, off_us, off_ds}; list [1 + E];
+ * total accumulates the misses. */
 int omc_launch_tier_route(const int32_t *idx, int nslots, int E, uint32_t *stats, int decay_every,
                           omc_expert_ptrs *tab, const void *slots_lo, const void *slots_hi, const void *home,
-                          void *miss, int miss_cap, const size_t *layout, int *list, int *err, int grid,
-                          cudaStream_t s);
+                          void *miss, int miss_cap, const size_t *layout, int *list,
+                          unsigned long long *total, int *err, int grid, cudaStream_t s);
 
 /* profiling: ends the named stage on stream s (no-op unless profiling) */
 void omc_prof_mark(cudaStream_t s, const char *name);

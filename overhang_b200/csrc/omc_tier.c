@@ -55,6 +55,7 @@ typedef struct omc_tier {
     char *spare;                 /* one HBM image: upload scratch and the
                                     placeholder of unrouted entries      */
     int *d_list;                 /* [1 + E] miss list (device)            */
+    unsigned long long *d_total; /* misses over all forwards (device)     */
     int *pinned;                 /* [nslots] expert in each slot, -1 free */
     int *slot_of;                /* [E] slot of each expert, -1 = home    */
     uint32_t *d_stats;           /* [2E+1] heat, last, clock (device)     */
@@ -151,6 +152,7 @@ void omc_tier_free(omc_layer *L) {
     cudaFree(t->spare);
     cudaFree(t->d_stats);
     cudaFree(t->d_list);
+    cudaFree(t->d_total);
     free(t->pinned);
     free(t->slot_of);
     free(t);
@@ -199,6 +201,8 @@ int omc_tier_enable(int layer, int hbm_slots, int interval, int decay_every) {
     if (ce == cudaSuccess) ce = cudaMalloc((void **)&t->d_stats, sizeof(uint32_t) * (2 * (size_t)E + 1));
     if (ce == cudaSuccess) ce = cudaMalloc((void **)&t->d_list, sizeof(int) * ((size_t)E + 1));
     if (ce == cudaSuccess) ce = cudaMemset(t->d_list, 0, sizeof(int) * ((size_t)E + 1));
+    if (ce == cudaSuccess) ce = cudaMalloc((void **)&t->d_total, sizeof(unsigned long long));
+    if (ce == cudaSuccess) ce = cudaMemset(t->d_total, 0, sizeof(unsigned long long));
     if (ce == cudaSuccess) ce = cudaEventCreateWithFlags(&t->ev, cudaEventDisableTiming);
     if (ce == cudaSuccess) ce = cudaMemset(t->d_stats, 0, sizeof(uint32_t) * (2 * (size_t)E + 1));
     if (ce != cudaSuccess) {
@@ -305,7 +309,7 @@ int omc_tier_route(omc_layer *L, const int32_t *idx, int T, cudaStream_t s) {
     const size_t layout[5] = {t->bytes, t->off_d, t->off_gs, t->off_us, t->off_ds};
     return omc_launch_tier_route(idx, T * L->dev.k, E, t->d_stats, t->decay_every, L->d_experts_tab, t->slots,
                                  t->slots + (size_t)t->nslots * t->bytes, t->home, g_miss, E - t->nslots, layout,
-                                 t->d_list, omc_G.d_err, 4 * omc_G.num_sms, s);
+                                 t->d_list, t->d_total, omc_G.d_err, 4 * omc_G.num_sms, s);
 }
 
 /* Forward exit: every interval-th forward, snapshot the counters. */
@@ -336,7 +340,7 @@ int omc_tier_step(int layer, int *eid) {
 }
 
 int omc_tier_stats(int layer, uint32_t *heat, uint32_t *last, uint32_t *clock, int32_t *slot_expert,
-                   long long *swaps) {
+                   long long *swaps, long long *misses) {
     omc_layer *L = omc_get_layer(layer);
     if (!L || !tier_of(L)) return omc_fail(OMC_ENOINIT, "omc_tier_stats: layer %d is not tiered", layer);
     omc_tier *t = tier_of(L);
@@ -348,5 +352,10 @@ int omc_tier_stats(int layer, uint32_t *heat, uint32_t *last, uint32_t *clock, i
     if (slot_expert)
         for (int z = 0; z < t->nslots; ++z) slot_expert[z] = t->pinned[z];
     if (swaps) *swaps = t->swaps;
+    if (misses) {
+        unsigned long long m = 0;
+        CK(cudaMemcpy(&m, t->d_total, sizeof(m), cudaMemcpyDeviceToHost));
+        *misses = (long long)m;
+    }
     return OMC_OK;
 }

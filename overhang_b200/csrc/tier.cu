@@ -29,6 +29,7 @@ struct TierArgs {
     char *miss;                        // [miss_cap] HBM images
     size_t bytes, off_d, off_gs, off_us, off_ds;
     int *list;
+    unsigned long long *total;         // misses over all forwards
     int *err;
 };
 
@@ -86,7 +87,10 @@ __global__ void __launch_bounds__(1024) tier_route_kernel(TierArgs a) {
             }
             n += __popc(m);
         }
-        if (lane == 0) a.list[0] = min(n, a.miss_cap);
+        if (lane == 0) {
+            a.list[0] = min(n, a.miss_cap);
+            *a.total += (unsigned long long)min(n, a.miss_cap);
+        }
     }
 }
 
@@ -123,7 +127,7 @@ __global__ void __launch_bounds__(256) tier_fetch_kernel(TierArgs a) {
 extern "C" int omc_launch_tier_route(const int32_t *idx, int nslots, int E, uint32_t *stats, int decay_every,
                                      omc_expert_ptrs *tab, const void *slots_lo, const void *slots_hi,
                                      const void *home, void *miss, int miss_cap, const size_t *layout, int *list,
-                                     int *err, int grid, cudaStream_t s) {
+                                     unsigned long long *total, int *err, int grid, cudaStream_t s) {
     if (E <= 0 || E > OMC_MAX_E || nslots < 0 || (layout[0] & 255)) return OMC_EINVAL;
     TierArgs a;
     a.idx = idx;
@@ -143,6 +147,7 @@ extern "C" int omc_launch_tier_route(const int32_t *idx, int nslots, int E, uint
     a.off_us = layout[3];
     a.off_ds = layout[4];
     a.list = list;
+    a.total = total;
     a.err = err;
     tier_route_kernel<<<1, nslots >= 4096 ? 1024 : 256, 0, s>>>(a);
     omc_g_launches += 1;

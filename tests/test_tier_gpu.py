@@ -15,7 +15,8 @@ Bar:
     tensor-core grouped GEMM), through swaps, misses, graph replay, the
     device-pointer entry and the no-alloc entry;
   * the device heat counters equal the oracle's accounting of the routing
-    the forwards returned;
+    the forwards returned, and the device's miss count equals the routed
+    experts that were outside the slots;
   * every swap is the one the oracle's tier.h restatement picks from those
     counters, and the hot experts end up resident.
 """
@@ -61,8 +62,9 @@ def test_tier_bit_identical_and_policy(gpu, oracle, layer):
     orc = oracle.Tier("oracle")
     heat, last, clock = np.zeros(E, np.uint32), np.zeros(E, np.uint32), 0
     pinned = np.arange(SLOTS, dtype=np.int32)
-    _, _, _, slots, swaps = B.tier_stats(SLOTS)
-    assert np.array_equal(slots, pinned) and swaps == 0
+    _, _, _, slots, swaps, misses = B.tier_stats(SLOTS)
+    assert np.array_equal(slots, pinned) and swaps == 0 and misses == 0
+    want_misses = 0
     for i, T in enumerate(SEQ * 2):
         x = _inputs(oracle, layer, 9000 + i, T)
         # the decision made at this forward's entry: from the counters so far
@@ -79,10 +81,13 @@ def test_tier_bit_identical_and_policy(gpu, oracle, layer):
         if pick is not None:
             pinned = pinned.copy()
             pinned[pick[0]] = pick[1]
+        # this forward copied in every routed expert outside the slots it found
+        want_misses += len(set(np.unique(ib).tolist()) - set(pinned.tolist()))
         heat, last, clock = orc.account(ib, E, heat, last, clock)
-        h, l, c, slots, swaps = B.tier_stats(SLOTS)
+        h, l, c, slots, swaps, misses = B.tier_stats(SLOTS)
         assert c == clock and np.array_equal(h, heat) and np.array_equal(l, last), f"counters after forward {i}"
         assert np.array_equal(slots, pinned), f"slots after forward {i}: {slots} vs {pinned}"
+        assert misses == want_misses, f"misses after forward {i}"
     assert swaps >= SLOTS // 2
     assert len(set(slots.tolist()) & set(HOT.tolist())) >= SLOTS - 2
 
@@ -101,7 +106,7 @@ def test_tier_step_and_decay(gpu, oracle, layer):
         ro, ridx, _ = ref(layer, x)
         assert np.array_equal(idx, ridx)
         heat, last, clock = orc.account(idx, E, heat, last, clock, decay_every=3)
-        h, l, c, slots, swaps = B.tier_stats(SLOTS)
+        h, l, c, slots, swaps, _ = B.tier_stats(SLOTS)
         assert c == clock and np.array_equal(h, heat) and np.array_equal(l, last)
         assert np.array_equal(slots, pinned)          # no automatic decisions
         if i % 2 == 1:
