@@ -32,14 +32,18 @@
 //                byte is read once per forward).  One thread issuing 8 KiB
 //                copies tops out near 5.3 TB/s on B200; 16 KiB ones reach
 //                ~6.9 TB/s;
-//   warps 2..17  dequant, two groups of 8 warps taking alternate K blocks.
-//                A group first starts its K block's f16 token tile (n rows
-//                x 128 B, contiguous in the AOL operand) into a 4-deep smem
-//                ring with per-lane cp.async, L2 evict-last (bulk copies of
-//                one SM share a queue: one issued behind the int8 stream
-//                waits ~4k cycles even on an L2 hit); then,
-//                within a group warp w writes weight rows 32*(w%4)..+31 (its
-//                TMEM lane quarter) of tile (gate/up or down 2mt / 2mt+1):
+//   warps 2..17  dequant, four groups of 4 warps, group g taking the K
+//                blocks i with i % 4 == g, so four blocks' latency chains
+//                overlap (with two groups of 8 the block period was ~960
+//                cycles, set by that chain: token-tile landing, int8 wait,
+//                conversion, TMEM stage wait, store).  A group first starts
+//                its K block's f16 token tile (n rows x 128 B, contiguous in
+//                the AOL operand) into a 5-deep smem ring with per-lane
+//                cp.async, L2 evict-last (bulk copies of one SM share a
+//                queue: one issued behind the int8 stream waits ~4k cycles
+//                even on an L2 hit); then warp w of the group writes weight
+//                rows 32*(w%4)..+31 (its TMEM lane quarter) of both tiles
+//                (gate/up or down 2mt / 2mt+1), one after the other:
 //                64 int8 -> exact f16 -> tcgen05.st into a 3-deep ring of
 //                TMEM A stages (64 columns each: 2 tiles x 32);
 //   warp 1       TMEM allocator + tcgen05.mma issuer: the warp runs the
@@ -61,8 +65,9 @@
 namespace {
 
 constexpr int NMAX = OMC_NMAX;            // tokens per work item (MMA N)
-constexpr int NGRP = 2;                   // dequant groups (alternate K blocks)
-constexpr int NDQ = 8;                    // warps per dequant group: 2 tiles x 4 lane quarters
+constexpr int NGRP = 4;                   // dequant groups (K blocks i with i % NGRP == group)
+constexpr int NDQ = 4;                    // warps per dequant group: one per TMEM lane quarter, both tiles
+constexpr int GTHREADS = NDQ * 32;        // threads of a group (its token-tile copies)
 constexpr int NEPI = 8;                   // epilogue warps: two per TMEM lane quarter
 constexpr int SA = 5;                     // token-tile ring (smem)
 constexpr int ST = 3;                     // weight A stages (TMEM)
@@ -399,16 +404,18 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_gemm_kernel(const GemmArgs a)
         // ------------------------------------------------ dequant: int8 ring -> TMEM A stage
         const int dq = warp - WARP_DQ0;
         const int grp = dq / NDQ;                // K blocks i with i % NGRP == grp
-        const int tile = (dq % NDQ) / 4;         // 0: gate / down 2mt, 1: up / down 2mt+1
-        const int q = warp & 3;                  // this warp's TMEM lane quarter
-        const int r = q * 32 + lane;             // weight row within the 128-row tile
+        const int q = warp & 3;                  // this warp's TMEM lane quarter (the group's 4 warps cover all 4)
+        const int r = q * 32 + lane;             // weight row within each 128-row tile
         const uint32_t lane_bits = (uint32_t)(q * 32) << 16;
         StageIter<PHASE> pr;
         pr.init(c, blockIdx.x, nitems, gridDim.x);
         for (int j = 0; j < grp; ++j) pr.step(c);
-        const int gt = (dq % NDQ) * 32 + lane;   // thread index within the group, 0..255
+        const int gt = (dq % NDQ) * 32 + lane;   // thread index within the group
+        constexpr int XR = NMAX * 8 / GTHREADS;  // token rows this thread copies per tile
         const uint64_t keep = l2_policy_evict_last();
-        int xrow_item = -1, xrow[4] = {-1, -1, -1, -1};   // gemm1: token of each row this lane copies
+        int xrow_item = -1, xrow[XR];            // gemm1: token of each row this lane copies
+#pragma unroll
+        for (int u = 0; u < XR; ++u) xrow[u] = -1;
         for (uint32_t i = grp; pr.valid && !*abort_flag; i += NGRP) {
             const int si = i % SI, st = i % ST, sa = i % SA;
             // token tile of this K block: per-lane cp.async (not a bulk copy, which would queue
@@ -420,13 +427,13 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_gemm_kernel(const GemmArgs a)
                 if (PHASE == 1) {
                     // gather: operand row j of the item is token xrow[j] of xh (its
                     // routed slot's token, or every token for the shared expert);
-                    // padding rows are zero-filled.  Chunk ch = gt + 256u of the
-                    // tile is row (gt >> 3) + 32u, 16-byte column gt & 7.
+                    // padding rows are zero-filled.  Chunk ch = gt + GTHREADS*u of the
+                    // tile is row (gt >> 3) + (GTHREADS/8)*u, 16-byte column gt & 7.
                     if (pr.idx != xrow_item) {
                         xrow_item = pr.idx;
 #pragma unroll
-                        for (int u = 0; u < 4; ++u) {
-                            const int j = (gt >> 3) + 32 * u;
+                        for (int u = 0; u < XR; ++u) {
+                            const int j = (gt >> 3) + (GTHREADS / 8) * u;
                             int t = -1;
                             if (j < pr.n) {
                                 const int slot = a.rowinfo[pr.n0 + j];
@@ -438,8 +445,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_gemm_kernel(const GemmArgs a)
                     const int c = gt & 7;
                     const uint8_t *xcol = reinterpret_cast<const uint8_t *>(a.xh) + (size_t)pr.kb * 128 + c * 16;
 #pragma unroll
-                    for (int u = 0; u < 4; ++u) {
-                        const int j = (gt >> 3) + 32 * u;
+                    for (int u = 0; u < XR; ++u) {
+                        const int j = (gt >> 3) + (GTHREADS / 8) * u;
                         if (j >= pr.n) break;
                         const bool live = xrow[u] >= 0;
                         const uint8_t *src = live ? xcol + (size_t)xrow[u] * (size_t)L.D * 2 : xcol;
@@ -448,16 +455,20 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_gemm_kernel(const GemmArgs a)
                 } else {
                     const uint8_t *src = reinterpret_cast<const uint8_t *>(a.act) + (size_t)pr.kb * a.R * 128 +
                                          (size_t)pr.n0 * 128;
-                    for (int ch = gt; ch < pr.n * 8; ch += NDQ * 32)
+                    for (int ch = gt; ch < pr.n * 8; ch += GTHREADS)
                         cp_async16_hint(dst + ch * 16, src + ch * 16, keep);
                 }
                 cp_async_commit();
             }
             if (!warp_wait(&fullI[si], (i / SI) & 1, a.err, OMC_SITE_GEMM_DEQUANT, abort_flag)) break;
-            const bool active = tile < pr.nmat;  // warp-uniform
-            uint32_t v[32];
-            if (active) {
-                const uint8_t *m = smem + OFF_I8 + si * 2 * W_BYTES + tile * W_BYTES;
+            if (!warp_wait(&emptyT[st], ((i / ST) & 1) ^ 1, a.err, OMC_SITE_GEMM_DEQUANT, abort_flag)) break;
+            tc_fence_after();
+            // both tiles of the pair, one after the other through the same registers:
+            // 64 int8 of row r -> exact f16 -> TMEM columns 32*tile.. of stage st
+            const uint8_t *m0 = smem + OFF_I8 + si * 2 * W_BYTES;
+            for (int tile = 0; tile < pr.nmat; ++tile) {   // warp-uniform
+                uint32_t v[32];
+                const uint8_t *m = m0 + tile * W_BYTES;
 #pragma unroll
                 for (int cc = 0; cc < 4; ++cc) {   // 16 int8 of K per chunk -> TMEM columns 8cc..8cc+7
                     const uint4 qv = *reinterpret_cast<const uint4 *>(m + (cc * 128 + r) * 16);
@@ -466,18 +477,12 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_gemm_kernel(const GemmArgs a)
                     i8x4_to_f16x4(qv.z, v[8 * cc + 4], v[8 * cc + 5]);
                     i8x4_to_f16x4(qv.w, v[8 * cc + 6], v[8 * cc + 7]);
                 }
-            }
-            // release the int8 slot only once its bytes are in registers as
-            // f16 (an arrive with the ld.shared still in flight would let the
-            // next bulk copy overwrite them)
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&emptyI[si]);
-            if (!warp_wait(&emptyT[st], ((i / ST) & 1) ^ 1, a.err, OMC_SITE_GEMM_DEQUANT, abort_flag)) break;
-            tc_fence_after();
-            if (active) {
                 tmem_st_32x32b_x32(tmem + lane_bits + TCOL_A + (uint32_t)st * 64u + (uint32_t)tile * 32u, v);
                 tc_wait_st();
             }
+            // every int8 byte of the slot this warp reads is in TMEM now: release it
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&emptyI[si]);
             cp_async_wait_all();          // this thread's part of the token tile has landed ...
             fence_proxy_async_smem();     // ... and is visible to the tensor core
             tc_fence_before();
