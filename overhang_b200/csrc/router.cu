@@ -336,7 +336,15 @@ int launch_logits(const omc_layer_dev *L, const float *x, int T, int nrows, floa
     //   Gemma  T=2048   176     104     156    198    135     144
     //   Gemma  T=8192   292     326     592    768    411     484
     //   Qwen   T=2048   219     148     230    287    174     202
-    // (8x2x2 and 16x2x1 are not built: never the fastest.  Neither were a
+    // Later, with 64-thread blocks of two chains a thread (256 blocks at OLMoE T=512):
+    //                 8x2x1   8x1x2  (16x1x1 in the same run)
+    //   OLMoE  T=512   39.3    36.3    31.6
+    //   OLMoE  T=2048  75.9    72.4    86.8   (16x2x2: 56.9)
+    //   Gemma  T=512   51.8    49.8    49.9
+    //   Qwen   T=2048 250.4   248.1   233.9   (16x2x2: 148.4)
+    // so the bound is each warp's instruction chain (~4.3 cycles an instruction
+    // at 2 warps a scheduler), not the SMs a grid covers.
+    // (8x2x2, 16x2x1, 8x2x1 and 8x1x2 are not built: never the fastest.  Neither were a
     // lane-per-router-row kernel with broadcast token reads, nor 8-stage
     // staging; ncu on 16x1x1 at T=512: 2 warps per scheduler, ~6 issued
     // instructions per chain step, each waiting ~4.6 cycles on the add chain
