@@ -378,15 +378,28 @@ def run_ours(args):
     graph = None
     if args.graph and not ep_mode and not tier:
         # one captured forward per input buffer; the timed region replays the graph
-        ob.launch_count(reset=True)
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph, stream=stream):
-            for i in range(nbuf):
-                step(i)
-        graph_launches = ob.launch_count()
-        graph.replay()
-        torch.cuda.synchronize()
-        args.steps = max(1, args.steps // nbuf) * nbuf
+        ok = 1
+        try:
+            ob.launch_count(reset=True)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=stream):
+                for i in range(nbuf):
+                    step(i)
+            graph_launches = ob.launch_count()
+            graph.replay()
+            torch.cuda.synchronize()
+        except Exception as exc:   # time stream launches instead, on every rank alike
+            print(f"[bench] CUDA graph capture failed ({exc}); timing stream launches", file=sys.stderr)
+            ok = 0
+            torch.cuda.synchronize()
+        if dist:
+            f = torch.tensor([ok], device=f"cuda:{dev}")
+            dist.all_reduce(f, op=dist.ReduceOp.MIN)
+            ok = int(f.item())
+        if ok:
+            args.steps = max(1, args.steps // nbuf) * nbuf
+        else:
+            graph = None
 
     barrier()
     miss0 = layer.tier_stats(tier)[5] if tier else 0
