@@ -22,6 +22,11 @@
  * and the process exits with status 2.
  *
  * Environment: OMC_DEVICE selects the CUDA device (default 0).
+ * OMC_TIER_SLOTS=n (0 < n < experts) keeps only n experts of each layer in
+ * HBM and the rest in pinned host memory, moved in by the library's hot-store
+ * policy (omc_tier_enable: a model larger than its HBM share); the heat is
+ * halved every OMC_TIER_DECAY forwards (default 0: never).  Unset: every
+ * expert in HBM.
  */
 #ifndef OMC_ENGINE_HOOK_H
 #define OMC_ENGINE_HOOK_H
@@ -47,6 +52,12 @@ static void omc_hook_upload(Model *m, Layer *l, int layer) {
     d.renorm = c->norm_topk;
     d.router_dtype = OMC_ROUTER_F32;
     if ((rc = omc_layer_init(layer, &d, l->gate, NULL))) omc_hook_fail("omc_layer_init", rc);
+    {
+        const char *ts = getenv("OMC_TIER_SLOTS"), *td = getenv("OMC_TIER_DECAY");
+        const int slots = ts ? atoi(ts) : 0;
+        if (slots > 0 && slots < d.E && (rc = omc_tier_enable(layer, slots, 1, td ? atoi(td) : 0)))
+            omc_hook_fail("omc_tier_enable", rc);
+    }
     const int64_t n = (int64_t)c->inter * c->hidden;
     int8_t *g = malloc(n), *u = malloc(n), *dn = malloc(n);
     float *gs = falloc(c->inter), *us = falloc(c->inter), *ds = falloc(c->hidden), *tmp = falloc(n);

@@ -28,6 +28,11 @@
  * is no CPU fallback.
  *
  * Environment: OMC_DEVICE selects the CUDA device (default 0).
+ * OMC_TIER_SLOTS=n (0 < n < experts) keeps only n experts of each layer in
+ * HBM and the rest in pinned host memory, moved in by the library's hot-store
+ * policy (omc_tier_enable: a model larger than its HBM share); the heat is
+ * halved every OMC_TIER_DECAY forwards (default 0: never).  Unset: every
+ * expert in HBM.
  */
 #ifndef OMC_GEMMA_HOOK_H
 #define OMC_GEMMA_HOOK_H
@@ -58,6 +63,12 @@ static void omc_gh_upload(Model *m, Layer *l, int li) {
     d.router_dtype = l->rproj.q ? OMC_ROUTER_I8 : OMC_ROUTER_F32;
     const void *rw = l->rproj.q ? (const void *)l->rproj.q : (const void *)l->rproj.f;
     if ((rc = omc_layer_init(li, &d, rw, l->rproj.s))) omc_gh_fail("omc_layer_init", rc);
+    {
+        const char *ts = getenv("OMC_TIER_SLOTS"), *td = getenv("OMC_TIER_DECAY");
+        const int slots = ts ? atoi(ts) : 0;
+        if (slots > 0 && slots < d.E && (rc = omc_tier_enable(li, slots, 1, td ? atoi(td) : 0)))
+            omc_gh_fail("omc_tier_enable", rc);
+    }
     if ((rc = omc_layer_gemma_norms(li, c->eps, l->rscale, l->pes, l->pre_ffw2)))
         omc_gh_fail("omc_layer_gemma_norms", rc);
     const int D = c->hidden, mi = c->moe_inter;

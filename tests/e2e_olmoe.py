@@ -179,7 +179,7 @@ def run_engine(binary: str, snap: str, prompt: list, n_new: int, env_extra=None,
 
 
 def compare(layers: int, vocab: int, n_prompt: int, n_new: int, path: str | None, workdir: str | None = None,
-            level: int = 2):
+            level: int = 2, env_extra: dict | None = None):
     """Builds the snapshot, runs the CPU engine and the GPU one (level 2: the
     moe() hook; level 1: the engine's own omm_* seam), returns the result dict."""
     own = workdir is None
@@ -193,6 +193,7 @@ def compare(layers: int, vocab: int, n_prompt: int, n_new: int, path: str | None
         prompt = prompt_ids(vocab, n_prompt)
         cpu, t_cpu, _ = run_engine(REF_ENGINE, snap, prompt, n_new)
         env = {"OMC_FFN_PATH": path} if path else {}
+        env.update(env_extra or {})
         gpu, t_gpu, log = run_engine(OMC_ENGINE if level == 2 else METAL_ENGINE, snap, prompt, n_new, env)
         first_diff = next((i for i, (a, b) in enumerate(zip(cpu, gpu)) if a != b), None)
         return {"layers": layers, "vocab": vocab, "prompt_tokens": n_prompt, "new_tokens": n_new,

@@ -34,6 +34,15 @@ def test_greedy_tokens_identical(snapshot, path):
     assert r["identical"], f"first difference at token {r['first_difference']}: {r['cpu_tokens']} vs {r['gpu_tokens']}"
 
 
+def test_greedy_tokens_tiered(snapshot):
+    """The hooked engine with OMC_TIER_SLOTS=16: each layer keeps 16 of its 64
+    experts in HBM and copies the others in when routed (omc_tier_enable);
+    the greedy tokens still equal the CPU engine's."""
+    r = E2E.compare(layers=2, vocab=4096, n_prompt=32, n_new=16, path=None, workdir=snapshot,
+                    env_extra={"OMC_TIER_SLOTS": "16", "OMC_TIER_DECAY": "64"})
+    assert r["identical"], f"first difference at token {r['first_difference']}: {r['cpu_tokens']} vs {r['gpu_tokens']}"
+
+
 def test_greedy_tokens_level1_seam(snapshot):
     """The unmodified engine built with -DOM_METAL against include/om_metal.h:
     its prefill attention projections (omm_dense, half copies of the f32
