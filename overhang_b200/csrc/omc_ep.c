@@ -2,7 +2,7 @@
  *
  * A layer's routed experts are split into `world` contiguous ranges
  * (E/world each); the process of rank r holds range r in its slab
- * (SURVEY-style sharding, engines' experts are independent).  The exchange
+ * (the experts of a layer are independent of one another).  The exchange
  * itself -- routed rows to the ranks that hold their experts, weighted rows
  * back, the k-order sum at the token's home rank -- is composed by the
  * caller from omc_moe_route_dev and omc_moe_experts_dev over its own
