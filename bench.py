@@ -214,19 +214,13 @@ class ClockSampler:
 
 
 def profiled_traffic(kernel, workload):
-    """DRAM bytes (read + write) per launch of `kernel`, from the committed
-    ncu summary profiles/<kernel>_<workload>.md (its `traffic_bytes:` line),
-    or None."""
-    p = os.path.join(ROOT, "profiles", f"{kernel}_{workload}.md")
+    """DRAM bytes (read + write) per launch of `kernel` on `workload` from one
+    ncu capture, kept in the data file profiles/traffic.json, or None."""
+    p = os.path.join(ROOT, "profiles", "traffic.json")
     if not os.path.exists(p):
         return None
-    for ln in open(p):
-        if ln.strip().startswith("traffic_bytes:"):
-            try:
-                return float(ln.split(":", 1)[1].strip().split()[0])
-            except (ValueError, IndexError):
-                return None
-    return None
+    v = json.load(open(p)).get(f"{kernel}/{workload}")
+    return float(v) if isinstance(v, (int, float)) else None
 
 
 def make_layer():
@@ -375,18 +369,23 @@ def run_ours(args):
     dom = ("gemm_gateup" if "gemm_gateup" in stages else
            "decode_moe" if "decode_moe" in stages else "gemv_gateup")
 
-    graph = None
+    graphs = None
     if args.graph and not ep_mode and not tier:
-        # one captured forward per input buffer; the timed region replays the graph
+        # one captured forward per input buffer (graph i replays the forward of
+        # buffer i); the timed region replays graph i % nbuf at step i, so it
+        # runs exactly the requested steps
         ok = 1
         try:
             ob.launch_count(reset=True)
-            graph = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(graph, stream=stream):
-                for i in range(nbuf):
+            graphs = []
+            for i in range(nbuf):
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=stream):
                     step(i)
-            graph_launches = ob.launch_count()
-            graph.replay()
+                graphs.append(g)
+            graph_launches = ob.launch_count() / nbuf
+            for g in graphs:
+                g.replay()
             torch.cuda.synchronize()
         except Exception as exc:   # time stream launches instead, on every rank alike
             print(f"[bench] CUDA graph capture failed ({exc}); timing stream launches", file=sys.stderr)
@@ -396,33 +395,51 @@ def run_ours(args):
             f = torch.tensor([ok], device=f"cuda:{dev}")
             dist.all_reduce(f, op=dist.ReduceOp.MIN)
             ok = int(f.item())
-        if ok:
-            args.steps = max(1, args.steps // nbuf) * nbuf
-        else:
-            graph = None
+        if not ok:
+            graphs = None
 
-    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+    def timed_pass():
+        """Exactly args.steps steps between CUDA events on the launching
+        stream, bracketed by a barrier and a synchronize; max over ranks."""
+        barrier()
+        e0.record(stream)
+        for i in range(args.steps):
+            if graphs is None:
+                step(i)
+            else:
+                graphs[i % nbuf].replay()
+        e1.record(stream)
+        barrier()
+        ms = e0.elapsed_time(e1)
+        if dist:
+            tt = torch.tensor([ms], device=f"cuda:{dev}")
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            ms = float(tt.item())
+        return ms
+
     miss0 = layer.tier_stats(tier)[5] if tier else 0
     clk = ClockSampler(dev)
     clk.start()
     ob.launch_count(reset=True)
-    if graph is None:
+    if graphs is None:
         ob.time_stage(dom)      # one event pair around `dom` per step, on the launching stream
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    if graph is None:
-        for i in range(args.steps):
-            step(i)
-    else:
-        for _ in range(args.steps // nbuf):
-            graph.replay()
-    e1.record(stream)
-    barrier()
-    launches = ob.launch_count() if graph is None else graph_launches * (args.steps // nbuf)
+    # the timed pass is repeated until the passes add up to >= --min-seconds
+    # (every rank runs the same count); the line reports the median pass
+    passes = [timed_pass()]
+    repeats = max(1, int(np.ceil(args.min_seconds * 1e3 / max(passes[0], 1e-3))))
+    if dist:
+        rr = torch.tensor([repeats], device=f"cuda:{dev}")
+        dist.all_reduce(rr, op=dist.ReduceOp.MAX)
+        repeats = int(rr.item())
+    while len(passes) < repeats:
+        passes.append(timed_pass())
+    launches = (ob.launch_count() if graphs is None else graph_launches * args.steps * len(passes)) / len(passes)
     clocks = clk.stop()
     miss1 = layer.tier_stats(tier)[5] if tier else 0
-    if graph is not None:
-        # the dominant kernel's launch time, from a short pass outside the graph
+    if graphs is not None:
+        # the dominant kernel's launch time, from a short pass outside the graphs
         ob.time_stage(dom)
         for i in range(max(16, args.steps // 8)):
             step(i)
@@ -430,12 +447,7 @@ def run_ours(args):
     dom_ms, dom_n = ob.stage_timer()
     ob.time_stage(None)
     ob.sync()
-    ms = e0.elapsed_time(e1)
-    t_max = ms
-    if dist:
-        tt = torch.tensor([ms], device=f"cuda:{dev}")
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        t_max = float(tt.item())
+    t_max = float(statistics.median(passes))
     value = world * T * args.steps / (t_max / 1e3)
 
     # end to end through the host entry: pinned x in, out + routing back
@@ -510,11 +522,12 @@ def run_ours(args):
             "scaling": "weak", "vs_baseline": None, "dtype": "f16xint8->f32",
             "data": "synthetic",
             "config": dict(CONFIG, parallelism=(f"ep{world}" if ep_mode else f"replica{world}"),
-                           launch=("cuda_graph" if graph is not None else "stream"),
+                           launch=("cuda_graph" if graphs is not None else "stream"),
                            tokens_per_rank=T),
             "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": T * D * 4,
                     "d2h_bytes_per_step": T * D * 4 + T * K * 8},
             "gpu_launches": launches,
+            "repeats": len(passes), "pass_ms": [round(p, 4) for p in passes],
             "stage_ms": stages,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
                          "frac": achieved / hbm if achieved else None, "traffic": traffic,
@@ -530,7 +543,7 @@ def run_ours(args):
         # the tiered store: experts outside the HBM slots cross the host link
         # once per step that routes to them (the tier_fetch stage)
         swaps = layer.tier_stats(tier)[4]
-        misses = (miss1 - miss0) / args.steps        # counted on the device over the timed steps
+        misses = (miss1 - miss0) / (args.steps * len(passes))   # counted on the device over the timed steps
         f_ms = stages.get("tier_fetch", 0.0)
         line["config"]["tier_hbm_slots"] = tier
         line["tier"] = {"hbm_slots": tier, "experts": E, "swaps": swaps, "misses_per_step": misses,
@@ -560,6 +573,9 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--min-seconds", type=float, default=0.5,
+                    help="repeat the timed pass of --steps steps until the passes add up to this many seconds; "
+                         "the line reports the median pass")
     ap.add_argument("--workload", default="olmoe_prefill", choices=sorted(WORKLOADS),
                     help="olmoe_prefill (BASELINE configs[1], the default line), olmoe_decode, "
                          "qwen_prefill, qwen_decode")

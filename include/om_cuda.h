@@ -42,6 +42,11 @@ extern "C" {
 #define OMC_ETIMEOUT   -6   /* a bounded wait expired (device or NCCL)     */
 #define OMC_ENCCL      -7   /* NCCL error or NCCL unavailable              */
 #define OMC_EUNSUPPORTED -8 /* valid request this build does not handle    */
+#define OMC_ERANGE     -9   /* an activation outside the tensor-core path's
+                               f16 operand range (|v| >= 65520 or NaN): the
+                               forward's results are not valid.  The blocking
+                               entry omc_moe_forward recomputes such a forward
+                               on the f32 CUDA-core path and never returns it */
 
 /* ---- layer descriptor ------------------------------------------------ */
 /* Model family fixes the reference's arithmetic: the router's softmax sum
@@ -105,6 +110,15 @@ int omc_layer_init(int layer, const omc_moe_desc *desc,
  * glibc), which moves those rows' top-k weights by a few ulps. */
 int omc_layer_gemma_norms(int layer, float eps, const float *router_scale, const float *per_expert_scale,
                           const float *expert_norm);
+
+/* Router bias: bias [E] is added to expert e's router logit before the
+ * softmax (one f32 add: p = softmax(logit + bias)); NULL removes it.  This
+ * input has no counterpart in the reference: it lets a benchmark skew the
+ * expert load (e.g. bias_e = -1.1*ln(rank_e), a Zipf(1.1) preference over a
+ * permutation of the experts) on random-init weights.  The oracle adds it at
+ * the same point, so routing stays bit-exact with it.  Every value must be
+ * finite (OMC_EINVAL otherwise). */
+int omc_layer_router_bias(int layer, const float *bias);
 
 /* Upload routed expert e of a layer into the HBM slab (re-tiled for the
  * kernels).  Row-major int8 container tensors as written by the converters
@@ -216,13 +230,17 @@ int omc_moe_forward_dev(int layer, const float *x, int T, float *out,
  *
  * Limit: a forward whose workspace does not fit those 32 MiB is rejected with
  * OMC_EINVAL and a message giving the largest T for the layer (for the
- * OLMoE-shaped layer, D=2048 E=64 k=8 I=1024, T=167; for the Qwen-shaped
- * one, E=256 I=512 with its shared expert, T=84).  The caller still
+ * OLMoE-shaped layer, D=2048 E=64 k=8 I=1024, T=238; for the Qwen-shaped
+ * one, E=256 I=512 with its shared expert, T=273).  The caller still
  * passes x, out and the optional top-k buffers as device pointers.  Every call
  * uses the same array, which keeps the previous call's contents; the counters
  * that must start at zero are cleared on `stream` by each call.  Two calls
  * that can run at the same time on the GPU (different streams with no
- * ordering between them) race on the array: order them on one stream. */
+ * ordering between them) race on the array: order them on one stream.  The
+ * T = 1 fused decode kernel's counters (set up by omc_layer_init) and a
+ * tiered layer's miss area are shared with the other forward entries as
+ * well, so a no-alloc forward must also be ordered with every other forward
+ * of the library (one stream, or events). */
 int omc_moe_forward_noalloc(int layer, const float *x, int T, float *out,
                             int32_t *topk_idx, float *topk_w, void *stream);
 

@@ -135,6 +135,7 @@ static void gemma_route(const orc_desc *d, const orc_weights *w, const float *xr
     const int E = d->E, K = d->k;
     if (d->router_i8) ref_matmul_q(pr, xr, (const int8_t *)w->router, w->router_s, d->D, E);
     else              ref_matvec_f32(pr, xr, (const float *)w->router, d->D, E);
+    if (w->router_bias) for (int e = 0; e < E; e++) pr[e] += w->router_bias[e];
     float pmx = -1e30f;
     for (int e = 0; e < E; e++) if (pr[e] > pmx) pmx = pr[e];
     float psum = 0.f;
@@ -175,6 +176,8 @@ static void route_one(const orc_desc *d, const orc_weights *w, const float *xs, 
     }
     if (d->router_i8) ref_matmul_q(pr, xs, (const int8_t *)w->router, w->router_s, d->D, d->E);
     else              ref_matvec_f32(pr, xs, (const float *)w->router, d->D, d->E);
+    /* the harness's optional router bias, one float add per logit */
+    if (w->router_bias) for (int e = 0; e < d->E; e++) pr[e] += w->router_bias[e];
     if (d->family == ORC_FAMILY_QWEN) ref_softmax_f64sum(pr, d->E);
     else                              ref_softmax_f32sum(pr, d->E);
     ref_topk(pr, d->E, d->k, idx, val);

@@ -63,6 +63,10 @@ typedef struct {
     /* gemma (gemma.c:422-424, :608): router.scale [D], router.per_expert_scale
      * [E], pre_feedforward_layernorm_2 [D] (nullable: ones) */
     const float  *g_rscale, *g_pes, *g_enorm;
+    /* router bias [E] (nullable): added to each routed logit before the
+     * softmax.  A harness input with no counterpart in the reference (the
+     * engines have no bias term); benchmarks use it to skew expert load. */
+    const float  *router_bias;
 } orc_weights;
 
 /* For the GEMMA family, x is the layer's residual stream (the row

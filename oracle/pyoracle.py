@@ -45,7 +45,7 @@ class OrcWeights(C.Structure):
     _fields_ = [(n, C.c_void_p) for n in
                 ("router", "router_s", "g", "u", "d", "gs", "us", "ds",
                  "sh_g", "sh_u", "sh_d", "sh_gs", "sh_us", "sh_ds", "sh_gate",
-                 "g_rscale", "g_pes", "g_enorm")]
+                 "g_rscale", "g_pes", "g_enorm", "router_bias")]
 
 
 _lib = None
@@ -84,6 +84,17 @@ def lib():
         L.orc_expf_array.argtypes = [_f32p, _f32p, C.c_int64]
         _lib = L
     return _lib
+
+
+def ref_root():
+    """The reference sources (for fixture generation and harness builds):
+    $REF_ROOT, or a directory named `reference` beside this repository; None
+    when neither holds engines/olmoe.c."""
+    cands = [os.environ.get("REF_ROOT"), os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference")]
+    for c in cands:
+        if c and os.path.exists(os.path.join(c, "engines", "olmoe.c")):
+            return os.path.abspath(c)
+    return None
 
 
 def ref_lib(name: str):
@@ -160,7 +171,7 @@ class Layer:
         return OrcWeights(p("router"), p("router_s"), p("g"), p("u"), p("d"), p("gs"),
                           p("us"), p("ds"), p("sh_g"), p("sh_u"), p("sh_d"), p("sh_gs"),
                           p("sh_us"), p("sh_ds"), p("sh_gate"), p("g_rscale"), p("g_pes"),
-                          p("g_enorm"))
+                          p("g_enorm"), p("router_bias"))
 
 
 def make_layer(family: int, D: int, I: int, E: int, k: int, seed: int, *, renorm: int = 0,
@@ -178,6 +189,8 @@ def make_layer(family: int, D: int, I: int, E: int, k: int, seed: int, *, renorm
     per_expert_scale and pre_feedforward_layernorm_2 are 1 + N(0, 0.1)."""
     L = Layer(family, D, I, E, k, renorm, router_i8, has_shared, Is, eps=eps)
     a = L.arrays
+    if router_bias is not None:
+        a["router_bias"] = np.ascontiguousarray(router_bias, np.float32).reshape(E)
     g = np.empty((E, I, D), np.int8); u = np.empty((E, I, D), np.int8)
     d = np.empty((E, D, I), np.int8)
     gs = np.empty((E, I), np.float32); us = np.empty((E, I), np.float32)
@@ -209,6 +222,15 @@ def make_layer(family: int, D: int, I: int, E: int, k: int, seed: int, *, renorm
         a["sh_d"], a["sh_ds"] = quantize_c(normal(base + 13, (D, Is), sigma))
         a["sh_gate"] = normal(base + 14, (D,), sigma)
     return L
+
+
+def zipf_bias(E: int, s: float = 1.1, seed: int = 11) -> np.ndarray:
+    """Router bias for a Zipf(s) skew over the experts: bias_e = -s*ln(rank_e),
+    rank a seeded permutation of 1..E (a harness input; the reference has no
+    bias term).  Added to the logits, it multiplies expert e's softmax weight
+    by rank_e^-s."""
+    rank = np.random.default_rng(seed).permutation(E) + 1
+    return (-s * np.log(rank.astype(np.float64))).astype(np.float32)
 
 
 def olmoe_layer(seed: int = 1, D=2048, I=1024, E=64, k=8, renorm=0) -> Layer:

@@ -20,7 +20,7 @@ LIB_PATH = os.path.join(PKG, "libomc.so")
 FAMILY_OLMOE, FAMILY_QWEN, FAMILY_GEMMA = 0, 1, 2
 ROUTER_F32, ROUTER_I8 = 0, 1
 
-OK, EINVAL, ENOMEM, ENOINIT, ECUDA, EDEVICE, ETIMEOUT, ENCCL, EUNSUPPORTED = 0, -1, -2, -3, -4, -5, -6, -7, -8
+OK, EINVAL, ENOMEM, ENOINIT, ECUDA, EDEVICE, ETIMEOUT, ENCCL, EUNSUPPORTED, ERANGE = 0, -1, -2, -3, -4, -5, -6, -7, -8, -9
 
 
 class OmcError(RuntimeError):
@@ -49,6 +49,7 @@ SIGNATURES = {
     "omc_shutdown": (None, []),
     "omc_layer_init": (_i, [_i, C.POINTER(MoEDesc), _vp, _vp]),
     "omc_layer_gemma_norms": (_i, [_i, C.c_float, _vp, _vp, _vp]),
+    "omc_layer_router_bias": (_i, [_i, _vp]),
     "omc_expert_set": (_i, [_i, _i, _vp, _vp, _vp, _vp, _vp, _vp]),
     "omc_experts_set_packed": (_i, [_i, _vp, _vp, _vp, _vp, _vp, _vp]),
     "omc_experts_load": (_i, [_i, C.c_char_p, _i, C.c_char_p, C.c_char_p, C.c_char_p, _i]),
@@ -84,6 +85,7 @@ SIGNATURES = {
     "omc_debug_wait_timeout": (_i, []),
     "omc_debug_expf": (_i, [_vp, _vp, C.c_longlong]),
     "omc_debug_set_path": (_i, [_i]),
+    "omc_debug_plan_rows": (_i, [_i]),
     "omc_debug_router_tile": (_i, [_i, _i, _i]),
     "omc_debug_ws_copy": (_i, [_i, _vp, _sz]),
     "omc_debug_gemma_prenorm": (_i, [_i, _vp, _i, _vp, _vp, _vp]),
@@ -229,6 +231,8 @@ class MoELayer:
             m.tier_enable(*tier)
         if L.family == FAMILY_GEMMA:
             m.set_gemma_norms(L.eps, a["g_rscale"], a["g_pes"], a.get("g_enorm"))
+        if a.get("router_bias") is not None:
+            m.set_router_bias(a["router_bias"])
         m.set_experts_packed(a["g"], a["gs"], a["u"], a["us"], a["d"], a["ds"])
         if L.has_shared:
             m.set_shared(a["sh_g"], a["sh_gs"], a["sh_u"], a["sh_us"], a["sh_d"], a["sh_ds"],
@@ -242,6 +246,13 @@ class MoELayer:
         self._keep += [v for v in arrs if v is not None]
         check(lib().omc_layer_gemma_norms(self.layer, float(eps), *[_p(v) for v in arrs]),
               "omc_layer_gemma_norms")
+
+    def set_router_bias(self, bias) -> None:
+        """bias [E] added to every router logit before the softmax (None removes it)."""
+        b = None if bias is None else np.ascontiguousarray(bias, np.float32).reshape(self.desc.E)
+        if b is not None:
+            self._keep.append(b)
+        check(lib().omc_layer_router_bias(self.layer, _p(b)), "omc_layer_router_bias")
 
     def debug_prenorm(self, x: np.ndarray):
         """GEMMA: (router input, expert input, norm factor) from the device kernel."""

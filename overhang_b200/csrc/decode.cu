@@ -401,7 +401,8 @@ __global__ void __launch_bounds__(DC_THREADS, 1) decode_moe_kernel(const DecArgs
     if (tid == 0 && !wait_value(ctr + CTR_ROUTER, a.nrc, a.err, -1)) s_abort = 1;
     __syncthreads();
     if (!s_abort && warp < T)
-        select_token<NV>(a.logits, a.ldl, warp, E, K, L.family, L.renorm, L.has_shared, L.g_pes, s_tidx, s_tw, s_sg, a.err,
+        select_token<NV>(a.logits, a.ldl, warp, E, K, L.family, L.renorm, L.has_shared, L.g_pes, L.rbias, s_tidx, s_tw,
+                         s_sg, a.err,
                          reinterpret_cast<float *>(ring) + warp * NV * 32);
     __syncthreads();
 

@@ -549,6 +549,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_gemm_kernel(const GemmArgs a)
                 const int chunk = (r & 63) >> 3;
                 const int nch = it.n >> 4;
 #pragma unroll 1
+                bool outside = false;                              // an h value past the f16 range
                 for (int ch = half; ch < nch; ch += 2) {
                     uint32_t gv[16], uv[16];
                     tmem_ld_32x32b_x16(tmem + lane_bits + acc.col(0) + ch * 16, gv);
@@ -560,11 +561,13 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_gemm_kernel(const GemmArgs a)
                         const float hv = f < Iw ? swiglu_f(L.act, __uint_as_float(gv[jj]) * sc0,
                                                            __uint_as_float(uv[jj]) * sc1)
                                                 : 0.f;
+                        outside |= omc_f16_outside(hv);
                         // operand row n0 + j; n0 % 16 == 0, so its swizzle phase is j & 7 = jj & 7
                         *reinterpret_cast<__half *>(sbase + j * 128 + ((chunk ^ (jj & 7)) << 4)) =
                             __float2half_rn(fminf(fmaxf(hv, -65504.f), 65504.f));
                     }
                 }
+                if (outside) omc_dev_error(a.err, OMC_DEVERR_RANGE, OMC_SITE_GEMM_EPILOGUE, it.g);
                 tc_fence_before();
                 fence_proxy_async_smem();                          // staging -> visible to the bulk store
                 __syncwarp();
@@ -630,9 +633,12 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_gemm_kernel(const GemmArgs a)
 // -------------------------------------------------- explicit-rows pass ---
 // f16 operand rows from f32 rows (saturated), 8 values per thread.
 __global__ void __launch_bounds__(256) rows_to_f16_kernel(const float *__restrict__ x, long long n8,
-                                                          uint16_t *__restrict__ xh) {
+                                                          uint16_t *__restrict__ xh, int *err) {
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n8; i += (long long)gridDim.x * blockDim.x) {
         const float4 a = reinterpret_cast<const float4 *>(x)[2 * i], b = reinterpret_cast<const float4 *>(x)[2 * i + 1];
+        if (err && (omc_f16_outside(a.x) || omc_f16_outside(a.y) || omc_f16_outside(a.z) || omc_f16_outside(a.w) ||
+                    omc_f16_outside(b.x) || omc_f16_outside(b.y) || omc_f16_outside(b.z) || omc_f16_outside(b.w)))
+            omc_dev_error(err, OMC_DEVERR_RANGE, OMC_SITE_DISPATCH, (int)(i >> 20));
         uint4 o;
         o.x = f32x2_to_f16x2_sat(a.x, a.y);
         o.y = f32x2_to_f16x2_sat(a.z, a.w);
@@ -693,7 +699,7 @@ extern "C" long long omc_mma_work_items(const omc_layer_dev *L, int R) {
 __global__ void __launch_bounds__(256) dense_prep_kernel(const float *__restrict__ x, int S, int K, int K_pad, int Sp,
                                                          int R, uint16_t *__restrict__ act, int *__restrict__ rowinfo,
                                                          float *__restrict__ roww, int4 *__restrict__ work,
-                                                         int *__restrict__ nwork, int npairs) {
+                                                         int *__restrict__ nwork, int npairs, int *err) {
     const int stride = gridDim.x * blockDim.x, tid0 = blockIdx.x * blockDim.x + threadIdx.x;
     for (int r = tid0; r < Sp; r += stride) {
         rowinfo[r] = r < S ? r : -1;
@@ -706,6 +712,9 @@ __global__ void __launch_bounds__(256) dense_prep_kernel(const float *__restrict
         if (r < S && k0 < K) {
             const float4 a = *reinterpret_cast<const float4 *>(x + (size_t)r * K + k0);
             const float4 b = *reinterpret_cast<const float4 *>(x + (size_t)r * K + k0 + 4);
+            if (omc_f16_outside(a.x) || omc_f16_outside(a.y) || omc_f16_outside(a.z) || omc_f16_outside(a.w) ||
+                omc_f16_outside(b.x) || omc_f16_outside(b.y) || omc_f16_outside(b.z) || omc_f16_outside(b.w))
+                omc_dev_error(err, OMC_DEVERR_RANGE, OMC_SITE_DISPATCH, r);
             o.x = f32x2_to_f16x2_sat(a.x, a.y);
             o.y = f32x2_to_f16x2_sat(a.z, a.w);
             o.z = f32x2_to_f16x2_sat(b.x, b.y);
@@ -785,9 +794,22 @@ extern "C" int omc_launch_mma_ffn(const omc_layer_dev *L, const float *x, int T,
     return cudaGetLastError() == cudaSuccess ? 0 : OMC_ECUDA;
 }
 
+// Test hook: a smaller operand-row capacity for the dispatch plans that follow
+// (0 = the workspace's).  The workspace always has room for every routed row,
+// so only this reaches the plan's capacity check, which must end the forward
+// with an error status and no out-of-range access.
+static int g_plan_rows_limit = 0;
+
+extern "C" int omc_debug_plan_rows(int rows) {
+    if (rows < 0) return OMC_EINVAL;
+    g_plan_rows_limit = rows;
+    omc_graphs_invalidate();
+    return 0;
+}
+
 extern "C" void omc_plan_setup(const omc_layer_dev *L, int T, const omc_ws *ws, omc_plan_args *pa) {
     const int E = L->E, G = E + (L->has_shared ? 1 : 0);
-    const int R = ws->R_cap;
+    const int R = g_plan_rows_limit > 0 && g_plan_rows_limit < ws->R_cap ? g_plan_rows_limit : ws->R_cap;
     const int Imax_rows = L->has_shared && L->Is_rows > L->I_rows ? L->Is_rows : L->I_rows;
     const int chunks_max = R / NMAX + G;
     pa->E = E;
@@ -825,10 +847,11 @@ extern "C" int omc_launch_mma_rows(const omc_layer_dev *L, const float *x, int R
     if (gemm_setup()) return OMC_ECUDA;
     const long long n8 = (long long)R * L->D / 8;
     if (L->family == OMC_FAMILY_GEMMA) {   // residual rows: the experts' input norm first
-        const int rc = omc_launch_gemma_prenorm(L, x, R, nullptr, nullptr, ws->xh, nullptr, s);
+        const int rc = omc_launch_gemma_prenorm(L, x, R, nullptr, nullptr, ws->xh, nullptr, ws->err, s);
         if (rc) return rc;
     } else {
-        rows_to_f16_kernel<<<(int)((n8 + 255) / 256 < 4096 ? (n8 + 255) / 256 : 4096), 256, 0, s>>>(x, n8, ws->xh);
+        rows_to_f16_kernel<<<(int)((n8 + 255) / 256 < 4096 ? (n8 + 255) / 256 : 4096), 256, 0, s>>>(x, n8, ws->xh,
+                                                                                                   ws->err);
     }
     omc_plan_args pa;
     omc_plan_setup(L, R, ws, &pa);
@@ -931,7 +954,7 @@ extern "C" int omc_launch_dense_i8(const omc_layer_dev *L, const float *x, int S
     const long long nck = (long long)Sp * (L->I_pad / 8);
     const int blocks = (int)((nck + 255) / 256 < 2048 ? (nck + 255) / 256 : 2048);
     dense_prep_kernel<<<blocks, 256, 0, s>>>(x, S, L->I, L->I_pad, Sp, ws->R_cap, ws->hp, ws->rowinfo, ws->roww,
-                                             reinterpret_cast<int4 *>(ws->work), ws->nwork, npairs);
+                                             reinterpret_cast<int4 *>(ws->work), ws->nwork, npairs, ws->err);
     GemmArgs ga;
     ga.L = *L;
     ga.work = reinterpret_cast<const int4 *>(ws->work);
@@ -960,7 +983,8 @@ extern "C" int omc_launch_f32_to_f16(const float *src, long long n, uint16_t *ds
     if (n <= 0) return 0;
     if (n % 8) return OMC_EINVAL;
     const long long n8 = n / 8;
-    rows_to_f16_kernel<<<(int)((n8 + 255) / 256 < 4096 ? (n8 + 255) / 256 : 4096), 256, 0, s>>>(src, n8, dst);
+    rows_to_f16_kernel<<<(int)((n8 + 255) / 256 < 4096 ? (n8 + 255) / 256 : 4096), 256, 0, s>>>(src, n8, dst,
+                                                                                                 nullptr);
     omc_g_launches += 1;
     return cudaGetLastError() == cudaSuccess ? 0 : OMC_ECUDA;
 }

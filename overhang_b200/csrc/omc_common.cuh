@@ -175,6 +175,11 @@ __device__ __forceinline__ void bulk_g2s(void *smem_dst, const void *gmem_src, u
         : "memory");
 }
 
+// The tensor-core path's f16 operands: |v| >= 65520 rounds past the largest
+// f16 (65504) and would be saturated (NaN is outside too).  Writers check each
+// value and report OMC_DEVERR_RANGE instead of clipping silently.
+__device__ __forceinline__ bool omc_f16_outside(float v) { return !(fabsf(v) < 65520.f); }
+
 // (lo, hi) -> f16x2, round to nearest, saturated to +-65504.
 __device__ __forceinline__ uint32_t f32x2_to_f16x2_sat(float lo, float hi) {
     uint32_t r;

@@ -69,6 +69,7 @@ const char *omc_strerror(int st) {
     case OMC_ETIMEOUT: return "timeout";
     case OMC_ENCCL: return "NCCL error";
     case OMC_EUNSUPPORTED: return "unsupported";
+    case OMC_ERANGE: return "activation outside the f16 operand range";
     default: return "unknown status";
     }
 }
@@ -329,6 +330,28 @@ int omc_layer_gemma_norms(int layer, float eps, const float *router_scale, const
     L->dev.g_pes = pes;
     L->dev.g_en = en;
     L->gemma_ready = 1;
+    return OMC_OK;
+}
+
+/* A per-expert term added to every routed logit before the softmax (bias
+ * NULL: none).  Slab space of a replaced bias is not reclaimed. */
+int omc_layer_router_bias(int layer, const float *bias) {
+    if (!G.init) return omc_fail(OMC_ENOINIT, "omc_layer_router_bias: omc_init not called");
+    omc_layer *L = omc_get_layer(layer);
+    if (!L) return omc_fail(OMC_ENOINIT, "omc_layer_router_bias: layer %d not initialised", layer);
+    graphs_invalidate();
+    if (!bias) {
+        L->dev.rbias = NULL;
+        return OMC_OK;
+    }
+    const int E = L->desc.E;
+    for (int e = 0; e < E; ++e)
+        if (!isfinite(bias[e])) return omc_fail(OMC_EINVAL, "omc_layer_router_bias: bias[%d] is not finite", e);
+    int on_host;
+    float *b = omc_slab_alloc((size_t)E * sizeof(float), &on_host);
+    if (!b) return omc_fail(OMC_ENOMEM, "omc_layer_router_bias: slab");
+    CK(cudaMemcpy(b, bias, (size_t)E * sizeof(float), cudaMemcpyHostToDevice));
+    L->dev.rbias = b;
     return OMC_OK;
 }
 
@@ -596,7 +619,7 @@ int omc_check_device_error(void) {
     cudaMemset(G.d_err, 0, sizeof(h));
     /* a forward that stopped at a lost wait may leave decode counters set */
     if (G.dec_ctr) cudaMemset(G.dec_ctr, 0, G.dec_ctr_n * sizeof(int));
-    const int st = h[0] == OMC_DEVERR_TIMEOUT ? OMC_ETIMEOUT : OMC_EDEVICE;
+    const int st = h[0] == OMC_DEVERR_TIMEOUT ? OMC_ETIMEOUT : h[0] == OMC_DEVERR_RANGE ? OMC_ERANGE : OMC_EDEVICE;
     return omc_fail(st, "device error code %d at site %d (detail %d)", h[0], h[1], h[2]);
 }
 
@@ -727,8 +750,10 @@ static int layer_ready(const omc_layer *L) {
  * T=16 194 vs 135 us; Qwen T=16 174 vs 138 us, T=64 552 vs 234 us: the
  * GEMV path reads an expert's weights once per slot, the grouped GEMM once
  * per expert. */
+static int g_force_f32;   /* set by omc_moe_forward while it redoes a forward on the f32 path */
+
 static int use_mma(const omc_layer *L, int T) {
-    if (G.path_override == 1 || G.path_override == 3) return 0;
+    if (g_force_f32 || G.path_override == 1 || G.path_override == 3) return 0;
     if (G.path_override == 2) return 1;
     const long long slots = (long long)T * L->desc.k;
     const long long need = 4LL * L->desc.E < 128 ? 4LL * L->desc.E : 128;
@@ -771,7 +796,7 @@ static int forward_on_ws(omc_layer *L, const omc_ws *ws, const float *x, int T, 
     const float *xr = x, *xe = x;
     if (gemma) {
         if ((rc = omc_launch_gemma_prenorm(&L->dev, x, T, ws->xg_r, mma ? NULL : ws->xg_e, mma ? ws->xh : NULL, NULL,
-                                           s)))
+                                           ws->err, s)))
             return omc_fail(rc, "prenorm launch failed");
         xr = ws->xg_r;
         xe = ws->xg_e;
@@ -785,7 +810,7 @@ static int forward_on_ws(omc_layer *L, const omc_ws *ws, const float *x, int T, 
     if (mma) {
         rc = omc_launch_mma_ffn(&L->dev, xe, T, ws, idx, w, out, s);
         if (rc == OMC_EUNSUPPORTED && G.path_override != 2) {
-            if (gemma && (rc = omc_launch_gemma_prenorm(&L->dev, x, T, NULL, ws->xg_e, NULL, NULL, s)))
+            if (gemma && (rc = omc_launch_gemma_prenorm(&L->dev, x, T, NULL, ws->xg_e, NULL, NULL, ws->err, s)))
                 return omc_fail(rc, "prenorm launch failed");
             rc = omc_launch_gemv_ffn(&L->dev, xe, T, ws, idx, w, out, s);
         }
@@ -918,7 +943,7 @@ int omc_moe_route_dev(int layer, const float *x, int T, int32_t *topk_idx, float
     cudaStream_t s = stream ? (cudaStream_t)stream : G.stream;
     G.prof_valid = 0;
     if (L->desc.family == OMC_FAMILY_GEMMA) {
-        if ((rc = omc_launch_gemma_prenorm(&L->dev, x, T, G.ws.xg_r, NULL, NULL, NULL, s)))
+        if ((rc = omc_launch_gemma_prenorm(&L->dev, x, T, G.ws.xg_r, NULL, NULL, NULL, G.d_err, s)))
             return omc_fail(rc, "omc_moe_route_dev: prenorm launch failed");
         x = G.ws.xg_r;
     }
@@ -1073,13 +1098,26 @@ int omc_moe_forward(int layer, const float *x, int T, float *out, int32_t *topk_
         cudaStreamSynchronize(s);
         return rc;
     }
-    if (T > 0) {
-        CK(cudaMemcpyAsync(out, G.ws.out, (size_t)T * D * 4, cudaMemcpyDeviceToHost, s));
-        if (topk_idx) CK(cudaMemcpyAsync(topk_idx, G.ws.topk_idx, (size_t)T * K * 4, cudaMemcpyDeviceToHost, s));
-        if (topk_w) CK(cudaMemcpyAsync(topk_w, G.ws.topk_w, (size_t)T * K * 4, cudaMemcpyDeviceToHost, s));
+    for (int pass = 0;; ++pass) {
+        if (T > 0) {
+            CK(cudaMemcpyAsync(out, G.ws.out, (size_t)T * D * 4, cudaMemcpyDeviceToHost, s));
+            if (topk_idx) CK(cudaMemcpyAsync(topk_idx, G.ws.topk_idx, (size_t)T * K * 4, cudaMemcpyDeviceToHost, s));
+            if (topk_w) CK(cudaMemcpyAsync(topk_w, G.ws.topk_w, (size_t)T * K * 4, cudaMemcpyDeviceToHost, s));
+        }
+        CK(cudaStreamSynchronize(s));
+        rc = omc_check_device_error();
+        if (rc != OMC_ERANGE || pass > 0 || T == 0) return rc;
+        /* an activation outside the tensor-core path's f16 operand range:
+         * the same forward again on the CUDA-core path, f32 throughout (the
+         * routing is recomputed bit for bit, so only the expert path changes) */
+        g_force_f32 = 1;
+        rc = omc_forward_device(L, G.ws.x, T, G.ws.out, G.ws.topk_idx, G.ws.topk_w, s);
+        g_force_f32 = 0;
+        if (rc) {
+            cudaStreamSynchronize(s);
+            return rc;
+        }
     }
-    CK(cudaStreamSynchronize(s));
-    return omc_check_device_error();
 }
 
 /* ---------------------------------------------------------------- debug -- */
@@ -1151,7 +1189,7 @@ int omc_debug_gemma_prenorm(int layer, const float *x, int T, float *xr, float *
     const size_t n = (size_t)T * L->desc.D * sizeof(float);
     cudaStream_t s = G.stream;
     CK(cudaMemcpyAsync(G.ws.x, x, n, cudaMemcpyHostToDevice, s));
-    if ((rc = omc_launch_gemma_prenorm(&L->dev, G.ws.x, T, G.ws.xg_r, G.ws.xg_e, NULL, G.ws.sg, s)))
+    if ((rc = omc_launch_gemma_prenorm(&L->dev, G.ws.x, T, G.ws.xg_r, G.ws.xg_e, NULL, G.ws.sg, G.d_err, s)))
         return omc_fail(rc, "omc_debug_gemma_prenorm: launch failed");
     CK(cudaMemcpyAsync(xr, G.ws.xg_r, n, cudaMemcpyDeviceToHost, s));
     CK(cudaMemcpyAsync(xe, G.ws.xg_e, n, cudaMemcpyDeviceToHost, s));

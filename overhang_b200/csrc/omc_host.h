@@ -105,6 +105,7 @@ void omc_ep_release(void);
 int omc_debug_wait_timeout(void);
 int omc_debug_expf(const float *x, float *y, long long n);
 int omc_debug_set_path(int path);
+int omc_debug_plan_rows(int rows);
 int omc_debug_router_tile(int g, int tt, int rr);
 int omc_debug_ws_copy(int which, void *dst, size_t bytes);
 int omc_debug_gemma_prenorm(int layer, const float *x, int T, float *xr, float *xe, float *r);

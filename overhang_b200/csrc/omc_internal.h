@@ -46,6 +46,7 @@ extern "C" {
 #define OMC_DEVERR_BOUNDS  2
 #define OMC_DEVERR_ROUTE   3
 #define OMC_DEVERR_CONFIG  4
+#define OMC_DEVERR_RANGE   5   /* an activation outside the f16 operand range */
 
 /* error sites (err[1]) */
 #define OMC_SITE_GEMM_PRODUCER 10
@@ -104,6 +105,7 @@ typedef struct {
     const float *g_s2;            /* [D] router.scale[i] * D^-0.5 (float product)   */
     const float *g_en;            /* [D] expert-input norm weight, NULL = ones      */
     const float *g_pes;           /* [E] per_expert_scale                           */
+    const float *rbias;           /* [E] added to every router logit, or NULL       */
 } omc_layer_dev;
 
 #define OMC_NMAX 128              /* token rows per grouped-GEMM work item (MMA N) */
@@ -183,7 +185,7 @@ int omc_launch_decode(const omc_layer_dev *L, const float *x, const float *xr, i
 /* GEMMA: router input xr, expert input xe (f32) and xh (f16 token operand)
  * of residual rows x, each nullable; r [T] the norm factor (nullable) */
 int omc_launch_gemma_prenorm(const omc_layer_dev *L, const float *x, int T, float *xr, float *xe, uint16_t *xh,
-                             float *r, cudaStream_t s);
+                             float *r, int *err, cudaStream_t s);
 long long omc_mma_work_items(const omc_layer_dev *L, int R);
 /* job-driven pass helpers: rows[r] = x[pos[r]]; out[s] += y[list[j]] over j in [off[s], off[s+1]) in order */
 int omc_launch_gather_rows(const float *x, const int *pos, int R, int S, int D, float *rows, int *err, cudaStream_t s);

@@ -10,6 +10,9 @@
 //   renorm : engines/olmoe.c:363, engines/qwen.c:476-477 (float sum in
 //            selection order, then divide).
 //   shared gate: engines/qwen.c:460-461, sigmoid(logit row E).
+//   bias   : an optional per-expert term added to each routed logit before the
+//            softmax (a caller input with no counterpart in the reference: it
+//            skews expert load for benchmarks; the oracle adds it the same way).
 //   gemma  : engines/gemma.c:463-477 -- the float-sum softmax numerators e_i
 //            are ranked themselves (strict '>' from -1: ties to the lowest
 //            id), w_k = e_k/sum, renormalised by the float sum of the w_k in
@@ -29,7 +32,7 @@ constexpr int SEL_WARPS = 8;
 template <int SEL_MAXV>   // ceil(E / 32) rounded up to a power of two
 __device__ __forceinline__ void select_token(const float *__restrict__ logits, int ldl, int t, int E, int K,
                                              int family, int renorm, int has_shared,
-                                             const float *__restrict__ pes,
+                                             const float *__restrict__ pes, const float *__restrict__ bias,
                                              int32_t *__restrict__ topk_idx, float *__restrict__ topk_w,
                                              float *__restrict__ sg, int *err, float *es) {
     const int lane = threadIdx.x & 31;
@@ -41,6 +44,7 @@ __device__ __forceinline__ void select_token(const float *__restrict__ logits, i
     for (int j = 0; j < SEL_MAXV; ++j) {
         const int i = lane + 32 * j;
         v[j] = i < E ? __ldcg(lg + i) : -INFINITY;
+        if (bias && i < E) v[j] = __fadd_rn(v[j], __ldg(bias + i));   // logit + bias, one f32 add
         if (i < E && v[j] > m) m = v[j];
     }
 #pragma unroll

@@ -31,7 +31,7 @@ constexpr int PN_WARPS = 8;
 __global__ void __launch_bounds__(PN_WARPS * 32)
     gemma_prenorm_kernel(const float *__restrict__ x, int T, int D, float eps, const float *__restrict__ s2,
                          const float *__restrict__ en, float *__restrict__ xr, float *__restrict__ xe,
-                         __half *__restrict__ xh, float *__restrict__ rout) {
+                         __half *__restrict__ xh, float *__restrict__ rout, int *err) {
     const int lane = threadIdx.x & 31;
     const int t = blockIdx.x * PN_WARPS + (threadIdx.x >> 5);
     if (t >= T) return;
@@ -57,7 +57,9 @@ __global__ void __launch_bounds__(PN_WARPS * 32)
         }
         if (xe) reinterpret_cast<float4 *>(xe + (size_t)t * D)[i] = e;
         if (xh) {
-            uint2 o;   // saturated, as every f16 token operand
+            if (omc_f16_outside(e.x) || omc_f16_outside(e.y) || omc_f16_outside(e.z) || omc_f16_outside(e.w))
+                omc_dev_error(err, OMC_DEVERR_RANGE, OMC_SITE_ROUTER, t);
+            uint2 o;
             o.x = f32x2_to_f16x2_sat(e.x, e.y);
             o.y = f32x2_to_f16x2_sat(e.z, e.w);
             reinterpret_cast<uint2 *>(xh + (size_t)t * D)[i] = o;
@@ -70,11 +72,11 @@ __global__ void __launch_bounds__(PN_WARPS * 32)
 // xr (router input, f32), xe (expert input, f32) and xh (expert input, f16)
 // are each nullable; r receives the norm factor per row (nullable).
 extern "C" int omc_launch_gemma_prenorm(const omc_layer_dev *L, const float *x, int T, float *xr, float *xe,
-                                        uint16_t *xh, float *r, cudaStream_t s) {
+                                        uint16_t *xh, float *r, int *err, cudaStream_t s) {
     if (T <= 0) return 0;
     if (L->family != OMC_FAMILY_GEMMA || (L->D & 3) || !L->g_s2) return OMC_EINVAL;
     gemma_prenorm_kernel<<<(T + PN_WARPS - 1) / PN_WARPS, PN_WARPS * 32, 0, s>>>(
-        x, T, L->D, L->eps, L->g_s2, L->g_en, xr, xe, reinterpret_cast<__half *>(xh), r);
+        x, T, L->D, L->eps, L->g_s2, L->g_en, xr, xe, reinterpret_cast<__half *>(xh), r, err);
     omc_g_launches += 1;
     omc_prof_mark(s, "prenorm");
     return cudaGetLastError() == cudaSuccess ? 0 : OMC_ECUDA;

@@ -74,7 +74,7 @@ __global__ void __launch_bounds__(G * G, 2) router_tile_kernel(const float *__re
                                                                   const float *__restrict__ Ws, int E,
                                                                   const float *__restrict__ sh_gate, int nrows,
                                                                   float *__restrict__ logits, int ldl,
-                                                                  uint16_t *__restrict__ xh) {
+                                                                  uint16_t *__restrict__ xh, int *err) {
     extern __shared__ __align__(16) float rsm[];
     constexpr int NT = G * G, BT = G * TT, BR = G * RR, LD = KC + 4, STAGE = (BT + BR) * LD;
     const int tid = threadIdx.x, tg = tid % G, rg = tid / G;
@@ -117,11 +117,16 @@ __global__ void __launch_bounds__(G * G, 2) router_tile_kernel(const float *__re
         const float *st = rsm + (size_t)(ch % RT_ST) * STAGE;
         if (xh && blockIdx.y == 0) {
             // the f16 token operand of the expert GEMMs (row t of xh = x[t]
-            // rounded to f16, saturated), written by the first row of blocks
+            // rounded to f16), written by the first row of blocks; a value
+            // outside the f16 range is reported, not clipped silently
             for (int i = tid; i < BT * (KC / 8); i += NT) {
                 const int r = i / (KC / 8), c = (i % (KC / 8)) * 8;
                 if (t0 + r < T && ch * KC + c < D) {
                     const float *v = st + r * LD + c;
+                    bool out = false;
+#pragma unroll
+                    for (int q = 0; q < 8; ++q) out |= omc_f16_outside(v[q]);
+                    if (out) omc_dev_error(err, OMC_DEVERR_RANGE, OMC_SITE_ROUTER, t0 + r);
                     uint4 o;
                     o.x = f32x2_to_f16x2_sat(v[0], v[1]);
                     o.y = f32x2_to_f16x2_sat(v[2], v[3]);
@@ -256,6 +261,7 @@ template <int SEL_MAXV>
 __global__ void __launch_bounds__(SEL_WARPS * 32) router_select_kernel(const float *__restrict__ logits, int ldl, int T,
                                                                        int E, int K, int family, int renorm,
                                                                        int has_shared, const float *__restrict__ pes,
+                                                                       const float *__restrict__ bias,
                                                                        int32_t *__restrict__ topk_idx,
                                                                        float *__restrict__ topk_w, float *__restrict__ sg,
                                                                        omc_plan_args plan, int do_plan, int *err) {
@@ -265,7 +271,7 @@ __global__ void __launch_bounds__(SEL_WARPS * 32) router_select_kernel(const flo
     const int wib = threadIdx.x >> 5;
     const int t = blockIdx.x * SEL_WARPS + wib;
     if (t < T)
-        select_token<SEL_MAXV>(logits, ldl, t, E, K, family, renorm, has_shared, pes, topk_idx, topk_w, sg, err,
+        select_token<SEL_MAXV>(logits, ldl, t, E, K, family, renorm, has_shared, pes, bias, topk_idx, topk_w, sg, err,
                                sbuf + wib * SEL_MAXV * 32);
     if (!do_plan) return;
     // count the routed slots per expert here, one global atomic per slot:
@@ -288,7 +294,7 @@ __global__ void __launch_bounds__(SEL_WARPS * 32) router_select_kernel(const flo
 
 template <int G, int TT, int RR, int KC>
 int launch_tile(const omc_layer_dev *L, const float *x, int T, int nrows, float *logits, int ldl, uint16_t *xh,
-                cudaStream_t s) {
+                int *err, cudaStream_t s) {
     static int attr_done = 0;
     if (!attr_done) {
         if (cudaFuncSetAttribute(router_tile_kernel<G, TT, RR, KC>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -298,7 +304,7 @@ int launch_tile(const omc_layer_dev *L, const float *x, int T, int nrows, float 
     }
     const dim3 g((T + G * TT - 1) / (G * TT), (nrows + G * RR - 1) / (G * RR));
     router_tile_kernel<G, TT, RR, KC><<<g, G * G, rt_smem<G, TT, RR, KC>(), s>>>(
-        x, T, L->D, L->router, L->router_i8 ? L->router_s : nullptr, L->E, L->sh_gate, nrows, logits, ldl, xh);
+        x, T, L->D, L->router, L->router_i8 ? L->router_s : nullptr, L->E, L->sh_gate, nrows, logits, ldl, xh, err);
     return 0;
 }
 
@@ -307,7 +313,7 @@ int g_force_tile = 0;
 
 // The largest tile whose blocks still cover every SM (smaller T: smaller tiles).
 int launch_logits(const omc_layer_dev *L, const float *x, int T, int nrows, float *logits, int ldl, uint16_t *xh,
-                  cudaStream_t s) {
+                  int *err, cudaStream_t s) {
     static int nsm = 0;
     if (!nsm) {
         int dev = 0;
@@ -320,10 +326,10 @@ int launch_logits(const omc_layer_dev *L, const float *x, int T, int nrows, floa
     };
     const long long want = nsm;
     switch (g_force_tile) {
-    case 1644: return launch_tile<16, 4, 4, 32>(L, x, T, nrows, logits, ldl, xh, s);
-    case 1622: return launch_tile<16, 2, 2, 64>(L, x, T, nrows, logits, ldl, xh, s);
-    case 1611: return launch_tile<16, 1, 1, 128>(L, x, T, nrows, logits, ldl, xh, s);
-    case 811: return launch_tile<8, 1, 1, 128>(L, x, T, nrows, logits, ldl, xh, s);
+    case 1644: return launch_tile<16, 4, 4, 32>(L, x, T, nrows, logits, ldl, xh, err, s);
+    case 1622: return launch_tile<16, 2, 2, 64>(L, x, T, nrows, logits, ldl, xh, err, s);
+    case 1611: return launch_tile<16, 1, 1, 128>(L, x, T, nrows, logits, ldl, xh, err, s);
+    case 811: return launch_tile<8, 1, 1, 128>(L, x, T, nrows, logits, ldl, xh, err, s);
     default: break;
     }
     // Measured on B200 (logits stage in us, every tile forced; OLMoE D=2048
@@ -354,9 +360,9 @@ int launch_logits(const omc_layer_dev *L, const float *x, int T, int nrows, floa
     // those fill the SMs; else one chain per thread.
     const long long b44 = blocks(16, 4, 4);
     if (10 * b44 >= 8 * want && (b44 <= want || 10 * b44 >= 16 * want))
-        return launch_tile<16, 4, 4, 32>(L, x, T, nrows, logits, ldl, xh, s);
-    if (10 * blocks(16, 2, 2) >= 8 * want) return launch_tile<16, 2, 2, 64>(L, x, T, nrows, logits, ldl, xh, s);
-    return launch_tile<16, 1, 1, 128>(L, x, T, nrows, logits, ldl, xh, s);
+        return launch_tile<16, 4, 4, 32>(L, x, T, nrows, logits, ldl, xh, err, s);
+    if (10 * blocks(16, 2, 2) >= 8 * want) return launch_tile<16, 2, 2, 64>(L, x, T, nrows, logits, ldl, xh, err, s);
+    return launch_tile<16, 1, 1, 128>(L, x, T, nrows, logits, ldl, xh, err, s);
 }
 
 }  // namespace
@@ -391,7 +397,7 @@ extern "C" int omc_launch_router(const omc_layer_dev *L, const float *x, int T, 
     } else {
         // GEMMA's expert operand is not the router's input: prenorm writes it
         const int rc = launch_logits(L, x, T, nrows, ws->logits, ldl,
-                                     (plan && L->family != OMC_FAMILY_GEMMA) ? ws->xh : nullptr, s);
+                                     (plan && L->family != OMC_FAMILY_GEMMA) ? ws->xh : nullptr, ws->err, s);
         if (rc) return rc;
     }
     omc_prof_mark(s, "router_logits");
@@ -402,7 +408,8 @@ extern "C" int omc_launch_router(const omc_layer_dev *L, const float *x, int T, 
     else memset(&pa, 0, sizeof(pa));
 #define SEL(NV)                                                                                                    \
     router_select_kernel<NV><<<g2, SEL_WARPS * 32, 0, s>>>(ws->logits, ldl, T, L->E, L->k, L->family, L->renorm, \
-                                                         L->has_shared, L->g_pes, topk_idx, topk_w, ws->sg, pa,   \
+                                                         L->has_shared, L->g_pes, L->rbias, topk_idx, topk_w, ws->sg, \
+                                                         pa,                                                      \
                                                          plan != nullptr,                                         \
                                                          ws->err)
     if (nv <= 1) SEL(1);

@@ -55,7 +55,9 @@ ROOT = os.path.dirname(os.path.dirname(HERE))
 sys.path.insert(0, os.path.join(ROOT, "oracle"))
 import pyoracle as P  # noqa: E402
 
-REF_ROOT = os.environ.get("REF_ROOT", "/root/reference")
+REF_ROOT = P.ref_root()
+if REF_ROOT is None:
+    sys.exit("the reference sources are needed: set REF_ROOT")
 
 
 def bits_equal(a, b):

@@ -149,12 +149,12 @@ def test_oracle_bitexact_vs_reference_build(oracle, case):
 
 @needs_ref
 @pytest.mark.parametrize("model", ["qwen", "gemma"])
-def test_reference_token_oracle_through_harness_build(model):
+def test_reference_token_oracle_through_harness_build(oracle, model):
     """The reference's own known-answer tests (Makefile:37-41) still pass with
     the reference compiled by oracle/Makefile: the build is faithful."""
-    ref_root = os.environ.get("REF_ROOT", "/root/reference")
-    snap = os.path.join(ref_root, "oracle", f"{model}_tiny")
-    if not os.path.isdir(snap):
+    ref_root = oracle.ref_root()
+    snap = os.path.join(ref_root or "", "oracle", f"{model}_tiny")
+    if ref_root is None or not os.path.isdir(snap):
         pytest.skip("reference sources not present")
     exe = os.path.join(ROOT, "oracle", "_ref", model)
     p = subprocess.run([exe, os.path.join(ref_root, "oracle", f"ref_{model}.json")],

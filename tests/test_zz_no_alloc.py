@@ -25,16 +25,17 @@ def _run(gpu, lib_fn, layer, x_dev, out_dev, idx_dev, w_dev, stream):
     assert rc == 0, gpu.last_error()
 
 
-@pytest.mark.parametrize("case", ["olmoe_T160", "qwen_T48", "olmoe_T3"])
+@pytest.mark.parametrize("case", ["olmoe_T160", "qwen_T48", "olmoe_T3", "olmoe_T1", "qwen_T1"])
 def test_noalloc_matches_device_entry_twice(gpu, oracle, case):
+    """T=1 takes the fused decode kernel, whose routing and pieces then live in
+    the static array too; it is also checked against the oracle."""
     import torch
+    T = int(case.split("T")[1])
     if case.startswith("olmoe"):
         L = oracle.make_layer(oracle.FAMILY_OLMOE, 2048, 1024, 64, 8, seed=61)
-        T = int(case.split("T")[1])
     else:
         L = oracle.make_layer(oracle.FAMILY_QWEN, 2048, 512, 256, 8, seed=62, renorm=1, router_i8=1,
                               has_shared=1, Is=512)
-        T = 48
     lid = next_layer_id()
     gpu.MoELayer.from_oracle_layer(lid, L)
     lib = gpu.lib()
@@ -56,6 +57,35 @@ def test_noalloc_matches_device_entry_twice(gpu, oracle, case):
         assert np.array_equal(i, ref_idx), name
         assert np.array_equal(w, ref_w), name
         assert_close(o, ref_out, what=name)
+    if T == 1:
+        ro, ridx, rw = oracle.oracle_moe(L, x.cpu().numpy())
+        o, i, w = outs["noalloc2"]
+        assert np.array_equal(i, ridx)
+        assert np.array_equal(w.view(np.uint32), rw.view(np.uint32))
+        assert_close(o, ro, what=f"{case} vs oracle")
+
+
+@pytest.mark.parametrize("family,limit", [("olmoe", 238), ("qwen", 273)])
+def test_noalloc_limit_is_exact(gpu, oracle, family, limit):
+    """The largest T the static array holds is the one the header and the docs
+    quote: T=limit runs, T=limit+1 is rejected with that bound."""
+    import torch
+    if family == "olmoe":
+        L = oracle.make_layer(oracle.FAMILY_OLMOE, 2048, 1024, 64, 8, seed=64)
+    else:
+        L = oracle.make_layer(oracle.FAMILY_QWEN, 2048, 512, 256, 8, seed=65, renorm=1, router_i8=1,
+                              has_shared=1, Is=512)
+    lid = next_layer_id()
+    gpu.MoELayer.from_oracle_layer(lid, L)
+    x = torch.from_numpy(oracle.normal(6300, (limit + 1, L.D))).cuda()
+    out = torch.zeros((limit + 1, L.D), device="cuda")
+    fn = gpu.lib().omc_moe_forward_noalloc
+    rc = fn(lid, C.c_void_p(x.data_ptr()), limit, C.c_void_p(out.data_ptr()), None, None, None)
+    assert rc == 0, gpu.last_error()
+    gpu.sync()
+    rc = fn(lid, C.c_void_p(x.data_ptr()), limit + 1, C.c_void_p(out.data_ptr()), None, None, None)
+    assert rc == gpu.EINVAL
+    assert f"at most T={limit} " in gpu.last_error()
 
 
 def test_noalloc_rejects_T_beyond_scratch(gpu, oracle):
