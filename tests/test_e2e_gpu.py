@@ -63,3 +63,27 @@ def test_gemma_greedy_tokens_identical(tmp_path):
         pytest.skip("engine builds missing (oracle/_ref/gemma, gemma_omc): run the build")
     r = G.compare(layers=4, vocab=4096, n_prompt=24, n_new=16, workdir=str(tmp_path))
     assert r["identical"], f"first difference at token {r['first_difference']}: {r['cpu_tokens']} vs {r['gpu_tokens']}"
+
+
+def test_qwen_tiny_int8_greedy_tokens(tmp_path):
+    """The reference's tiny Qwen fixture converted by its own converter (int8
+    stream mode, tests/golden/qwen_tiny_i8): the engine with moe_step on the
+    GPU (include/omc_qwen_hook.h) gives the CPU engine's greedy tokens, which
+    are the reference's recorded ones (oracle/ref_qwen.json)."""
+    import e2e_qwen as Q
+    if not (os.path.exists(Q.REF_ENGINE) and os.path.exists(Q.OMC_ENGINE)):
+        pytest.skip("engine builds missing (oracle/_ref/qwen, qwen_omc): run the build")
+    r = Q.compare(model="tiny", workdir=str(tmp_path))
+    assert r["identical"], f"first difference at token {r['first_difference']}: {r['cpu_tokens']} vs {r['gpu_tokens']}"
+    assert r["gpu_equals_reference_fixture"], (r["gpu_tokens"], r["reference_tokens"])
+
+
+def test_qwen_shaped_greedy_tokens(tmp_path):
+    """A random-init Qwen3.6-35B-A3B-shaped model (4 layers: three gated
+    DeltaNet, one full attention; 256 experts top-8 + shared expert, int8
+    container): the hooked engine's greedy tokens equal the CPU engine's."""
+    import e2e_qwen as Q
+    if not (os.path.exists(Q.REF_ENGINE) and os.path.exists(Q.OMC_ENGINE)):
+        pytest.skip("engine builds missing (oracle/_ref/qwen, qwen_omc): run the build")
+    r = Q.compare(model="shaped", layers=4, vocab=4096, n_prompt=16, n_new=16, workdir=str(tmp_path))
+    assert r["identical"], f"first difference at token {r['first_difference']}: {r['cpu_tokens']} vs {r['gpu_tokens']}"
