@@ -16,11 +16,13 @@ Arms
       times stream launches instead), timed with CUDA events on the
       launching stream, max over ranks; `e2e` = the same through the host
       entry omc_moe_forward (pinned host x in, host out/top-k back every
-      step).  N>1 (--mode replica, the default): N independent copies of
-      the workload (the OLMoE layer fits one GPU; weak scaling, no data-path
-      collective).  --mode ep: expert parallel -- each rank holds E/N of the
-      layer's experts and brings its own 512 tokens; routed rows go to their
-      experts' ranks and back with all_to_all over NCCL (overhang_b200.ep).
+      step).  N>1 (--mode ep, the default): expert parallel through the
+      library's own NCCL data plane (omc_ep_init with a unique id; each rank
+      holds E/N of the layer's experts and routes its own tokens, rows go to
+      their experts' ranks and back inside omc_moe_forward[_dev]).  The N>1
+      default workload is qwen_ep (the 256-expert
+      Qwen-shaped layer, T=8192 tokens in total split over the ranks, router
+      bias uniform or --bias zipf); --mode replica runs N independent copies.
   reference: the reference's own CPU MoE (engines/olmoe.c moe(), or the
       workload family's: engines/qwen.c moe_step(), engines/gemma.c route_token
       + expert union; compiled from its sources into oracle/_ref by
@@ -69,16 +71,25 @@ WORKLOADS = {
     "qwen_prefill": ("qwen", 2048), "qwen_decode": ("qwen", 1),
     "olmoe_decode64": ("olmoe", 64), "qwen_decode64": ("qwen", 64),
     "gemma_prefill": ("gemma", 2048), "gemma_decode": ("gemma", 1), "gemma_decode64": ("gemma", 64),
+    "qwen_ep": ("qwen", 8192),
 }
+BIAS = "uniform"                 # qwen_ep: router bias, uniform (none) or zipf
+T_TOTAL = None                   # qwen_ep: tokens over all ranks
 REF_FN = {"olmoe": "engines/olmoe.c moe()", "qwen": "engines/qwen.c moe_step()",
           "gemma": "engines/gemma.c route_token() + expert union"}
 
 
-def set_workload(name, tokens=None):
-    global D, I, E, K, T, FAMILY, IS, RI8, SEED_W, WORKLOAD, EXPERT_BYTES, CONFIG
+def set_workload(name, tokens=None, world=1, bias="uniform"):
+    global D, I, E, K, T, FAMILY, IS, RI8, SEED_W, WORKLOAD, EXPERT_BYTES, CONFIG, BIAS, T_TOTAL
     FAMILY, T = WORKLOADS[name]
     if tokens:
         T = tokens
+    if name == "qwen_ep":
+        # T tokens in total, T / world per home rank
+        T_TOTAL, BIAS = T, bias
+        if T % world:
+            raise SystemExit(f"qwen_ep: T={T} is not divisible by {world} ranks")
+        T = T // world
     if FAMILY == "olmoe":
         D, I, E, K, IS, RI8, SEED_W = 2048, 1024, 64, 8, 0, 0, 1
     elif FAMILY == "gemma":
@@ -88,6 +99,8 @@ def set_workload(name, tokens=None):
     EXPERT_BYTES = 3 * D * I + 4 * (2 * I + D)
     kind = "decode" if (T == 1 or "decode" in name) else "prefill"
     WORKLOAD = f"{FAMILY}_layer_{kind}_T{T}"
+    if name == "qwen_ep":
+        WORKLOAD = f"qwen_layer_ep_T{T_TOTAL}_{BIAS}"
     total = E * EXPERT_BYTES + (3 * D * IS + 4 * (2 * IS + D) if IS else 0)
     CONFIG = {"workload": WORKLOAD, "D": D, "I": I, "E": E, "k": K, "T": T,
               "weights": f"int8 per-row + f32 scales, N(0,0.02) seed {SEED_W}",
@@ -95,6 +108,12 @@ def set_workload(name, tokens=None):
               "l2": f"expert weights {total / 1e6:.0f} MB > 126 MB L2 stream from HBM every step"}
     if IS:
         CONFIG.update(shared_expert_I=IS, router="int8 + f32 scale", renorm=1)
+    if name == "qwen_ep":
+        CONFIG.update(T=T_TOTAL, tokens_total=T_TOTAL, router_bias=BIAS,
+                      experts_per_rank=E // world,
+                      x="f32 N(0,1), each rank's own seeded tokens, 8 rotating batches")
+        if BIAS == "zipf":
+            CONFIG["router_bias_rule"] = "bias_e = -1.1 ln(rank_e), rank a seeded permutation of 1..256 (seed 22)"
     if FAMILY == "gemma":
         CONFIG.update(router="int8 + f32 scale (N(0,1) before quantisation)", renorm=1,
                       activation="gelu_tanh", x="f32 N(0,1) residual rows seed 4242, 8 rotating batches")
@@ -227,7 +246,9 @@ def make_layer():
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import pyoracle
     if FAMILY == "qwen":
-        return pyoracle, pyoracle.qwen_layer(SEED_W, D=D, I=I, E=E, k=K, Is=IS)
+        bias = pyoracle.zipf_bias(E, 1.1, seed=22) if BIAS == "zipf" else None
+        return pyoracle, pyoracle.make_layer(pyoracle.FAMILY_QWEN, D, I, E, K, SEED_W, renorm=1, router_i8=1,
+                                             has_shared=1, Is=IS, router_bias=bias)
     if FAMILY == "gemma":
         return pyoracle, pyoracle.gemma_layer(SEED_W, D=D, I=I, E=E, k=K)
     return pyoracle, pyoracle.olmoe_layer(SEED_W, D=D, I=I, E=E, k=K)
@@ -312,14 +333,13 @@ def run_ours(args):
     ob.init(dev, 1 << 30)      # one layer: 403 MB of experts + router
     ep_mode = world > 1 and args.mode == "ep"
     if ep_mode:
-        ob.ep_init(rank, world)            # this rank holds experts [rank*E/world, (rank+1)*E/world)
+        # the library's own NCCL group: rank 0's unique id, passed over torch.distributed
+        uid = [ob.ep_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        ob.ep_init(rank, world, uid[0])    # this rank holds experts [rank*E/world, (rank+1)*E/world)
     pyoracle, L = make_layer()
     tier = args.tier if args.tier and not ep_mode else 0
     layer = ob.MoELayer.from_oracle_layer(0, L, tier=(tier, 1, 0) if tier else None)
-    ep = None
-    if ep_mode:
-        from overhang_b200.ep import ExpertParallel, LibCompute
-        ep = ExpertParallel(LibCompute(layer), E, K, D, bool(IS))
     nbuf = 8
     xs = [torch.from_numpy(pyoracle.normal(SEED_X + rank * nbuf + i, (T, D))).to(f"cuda:{dev}")
           for i in range(nbuf)]
@@ -332,10 +352,6 @@ def run_ours(args):
     sptr = stream.cuda_stream
 
     def step(i):
-        if ep_mode:
-            o, ii, _ = ep.forward(xs[i % nbuf])
-            idx.copy_(ii)
-            return
         layer.forward_dev(xs[i % nbuf].data_ptr(), T, out.data_ptr(), idx.data_ptr(), wts.data_ptr(),
                           sptr)
 
@@ -458,16 +474,6 @@ def run_ours(args):
     lib = ob.lib()
 
     def step_e2e(i):
-        if ep_mode:
-            # the expert-parallel forward of this rank's tokens: x from pinned host memory,
-            # out and the routing back to pinned host memory, every step
-            xd = hx[i % nbuf].to(f"cuda:{dev}", non_blocking=True)
-            o, ii, ww = ep.forward(xd)
-            hout.copy_(o, non_blocking=True)
-            hidx.copy_(ii, non_blocking=True)
-            hw.copy_(ww, non_blocking=True)
-            torch.cuda.current_stream().synchronize()
-            return
         rc = lib.omc_moe_forward(0, C.c_void_p(hx[i % nbuf].data_ptr()), T, C.c_void_p(hout.data_ptr()),
                                  C.c_void_p(hidx.data_ptr()), C.c_void_p(hw.data_ptr()))
         ob.check(rc, "omc_moe_forward")
@@ -489,14 +495,24 @@ def run_ours(args):
     # algorithmic bytes of one launch of the dominant kernel: every active
     # expert's int8 gate+up rows and their scales, the f16 copy of the tokens
     # it gathers rows from (T x D) and the f16 h it writes (one row per slot).
-    ids_seen = np.unique(idx.cpu().numpy())
+    idx_np = idx.cpu().numpy()
+    balance = None
     if ep_mode:
-        # this rank's launch: its experts that received rows, and the rows it received
+        # this rank's gate/up launch: its experts that received slots, those slots,
+        # and the token rows it received (one per token with any expert here)
+        allidx = [torch.empty_like(idx) for _ in range(world)]
+        dist.all_gather(allidx, idx)
+        full = np.concatenate([a.cpu().numpy() for a in allidx])
         lo, hi = rank * E // world, (rank + 1) * E // world
-        n_active = int(((ids_seen >= lo) & (ids_seen < hi)).sum())
-        rows = ep.last_recv_rows
+        here = (full >= lo) & (full < hi)
+        n_active = int(len(np.unique(full[here])))
+        rows = int(here.sum())
+        recv_rows = int(here.any(axis=1).sum())
+        per_rank = [int(((full >= r * E // world) & (full < (r + 1) * E // world)).sum()) for r in range(world)]
+        balance = {"slots_per_rank": per_rank, "max_over_mean": max(per_rank) / (sum(per_rank) / world)}
     else:
-        n_active, rows = int(len(ids_seen)), T * K
+        n_active, rows = int(len(np.unique(idx_np))), T * K
+        recv_rows = T
     shared_w = (2 * IS * D + 2 * IS * 4) if IS else 0          # the shared expert's gate+up
     srows = T if IS else 0
     # the whole step's weight bytes (every active expert + shared + router) over the step time
@@ -507,7 +523,7 @@ def run_ours(args):
     # router, and the shared expert with its gate)
     step_flop = T * (2 * K * 3 * D * I + 2 * D * E + ((2 * 3 * D * IS + 2 * D) if IS else 0))
     if dom == "gemm_gateup":
-        xh_rows = rows if ep_mode else T
+        xh_rows = recv_rows + (T if IS and ep_mode else 0)
         alg_bytes = (n_active * (2 * I * D + 2 * I * 4) + shared_w + xh_rows * D * 2
                      + (rows + srows) * max(I, IS) * 2)
     elif dom == "decode_moe":
@@ -517,9 +533,20 @@ def run_ours(args):
         alg_bytes = n_active * (2 * I * D + 2 * I * 4) + shared_w + T * D * 4 + (T * K + srows) * max(I, IS) * 4
     achieved = alg_bytes / (dom_ms / 1e3) / 1e9 if dom_ms > 0 else None
     traffic = profiled_traffic(dom, args.workload)
+    # the gate/up GEMM's FLOP per launch (every slot's two I x D products, and the
+    # shared expert's for the home tokens): the tensor roofline of the large-T rows
+    dom_flop = 2 * 2 * I * D * rows + (2 * 2 * IS * D * T if IS else 0)
+    roof = {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
+            "frac": achieved / hbm if achieved else None, "traffic": traffic}
+    if args.workload == "qwen_ep" and dom == "gemm_gateup" and dom_ms > 0 and tf:
+        # M_avg = 256 rows per expert: compute-bound, judged against the bf16 peak
+        ach_t = dom_flop / (dom_ms / 1e3) / 1e12
+        roof = {"bound": "tensor", "achieved": ach_t, "peak": tf, "unit": "TFLOP/s", "frac": ach_t / tf,
+                "traffic": traffic, "hbm_achieved_gbs": achieved}
     line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": t_max / args.steps, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f16xint8->f32",
+            "scaling": "strong" if args.workload == "qwen_ep" else "weak", "vs_baseline": None,
+            "dtype": "f16xint8->f32",
             "data": "synthetic",
             "config": dict(CONFIG, parallelism=(f"ep{world}" if ep_mode else f"replica{world}"),
                            launch=("cuda_graph" if graphs is not None else "stream"),
@@ -529,16 +556,17 @@ def run_ours(args):
             "gpu_launches": launches,
             "repeats": len(passes), "pass_ms": [round(p, 4) for p in passes],
             "stage_ms": stages,
-            "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
-                         "frac": achieved / hbm if achieved else None, "traffic": traffic,
+            "roofline": dict(roof, **{
                          "kernel": dom, "peak_source": src, "alg_bytes_per_launch": alg_bytes,
                          "launch_ms": dom_ms, "launches_timed": dom_n,
                          "step_weight_bytes": step_bytes,
                          "step_hbm_frac": step_bytes / (t_max / args.steps / 1e3) / (hbm * 1e9),
                          "step_flop": step_flop,
                          "step_tensor_frac": (step_flop / (t_max / args.steps / 1e3) / (tf * 1e12)
-                                              if tf else None)},
+                                              if tf else None), "flop_per_launch": dom_flop}),
             "clocks": clocks}
+    if balance:
+        line["ep_balance"] = balance
     if tier:
         # the tiered store: experts outside the HBM slots cross the host link
         # once per step that routes to them (the tier_fetch stage)
@@ -576,9 +604,11 @@ def main():
     ap.add_argument("--min-seconds", type=float, default=0.5,
                     help="repeat the timed pass of --steps steps until the passes add up to this many seconds; "
                          "the line reports the median pass")
-    ap.add_argument("--workload", default="olmoe_prefill", choices=sorted(WORKLOADS),
-                    help="olmoe_prefill (BASELINE configs[1], the default line), olmoe_decode, "
-                         "qwen_prefill, qwen_decode")
+    ap.add_argument("--workload", default=None, choices=sorted(WORKLOADS),
+                    help="olmoe_prefill (BASELINE configs[1], the default line on one GPU), olmoe_decode, "
+                         "qwen_prefill, qwen_decode, ...; qwen_ep (configs[3], the default on N>1 GPUs)")
+    ap.add_argument("--bias", default="uniform", choices=["uniform", "zipf"],
+                    help="qwen_ep: router bias (zipf: bias_e = -1.1 ln(rank_e), skewed expert load)")
     ap.add_argument("--graph", action="store_true", default=True,
                     help="capture one forward per input buffer in a CUDA graph and time graph replays "
                          "(the default; --mode ep always times stream launches)")
@@ -589,14 +619,16 @@ def main():
     ap.add_argument("--tier", type=int, default=0,
                     help="tiered expert store: keep this many experts in HBM, the rest in pinned host memory "
                          "(LFRU swaps every step; stream launches)")
-    ap.add_argument("--mode", default="replica", choices=["ep", "replica"],
-                    help="N>1: N independent replicas (the layer fits one GPU), or expert parallel "
-                         "(each rank holds E/N experts and its own 512 tokens; rows exchanged with "
-                         "all_to_all over NCCL)")
+    ap.add_argument("--mode", default="ep", choices=["ep", "replica"],
+                    help="N>1: expert parallel through the library's NCCL data plane (each rank holds E/N "
+                         "experts and routes its own tokens), or N independent replicas")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    set_workload(args.workload, args.tokens)
+    world = env_rank()[1]
+    if args.workload is None:
+        args.workload = "olmoe_prefill" if world == 1 or args.mode == "replica" else "qwen_ep"
+    set_workload(args.workload, args.tokens, world, args.bias)
     if args.impl == "reference":
         run_reference(args)
     else:

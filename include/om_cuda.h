@@ -273,18 +273,43 @@ int omc_sync(void);
 
 /* ---- expert parallelism (1 process per GPU) ------------------------- */
 
-/* Declare this process rank `rank` of `world` expert-parallel ranks (call
- * after omc_init, before the first omc_layer_init).  Layers initialised
- * afterwards hold only routed experts [rank*E/world, (rank+1)*E/world) in
- * the slab (omc_expert_set ignores the others) plus the shared expert; the
- * caller composes a forward from omc_moe_route_dev and omc_moe_experts_dev
- * over its own transport, and omc_moe_forward[_dev] on such a layer returns
- * OMC_EUNSUPPORTED.  unique_id must be NULL: the library owns no NCCL group
- * (a non-NULL id returns OMC_EUNSUPPORTED). */
+/* Declare this process rank `rank` of `world` expert-parallel ranks, one
+ * process per GPU (call after omc_init, before the first omc_layer_init;
+ * world <= 16).  Layers initialised afterwards hold only routed experts
+ * [rank*E/world, (rank+1)*E/world) in the slab (omc_expert_set ignores the
+ * others) plus the shared expert; E must be divisible by world.
+ *
+ * unique_id = the 128 bytes rank 0 got from omc_ep_unique_id, passed to
+ * every rank by the caller (any channel): the ranks join one NCCL group
+ * (NCCL is loaded at run time; OMC_ENCCL if absent), and omc_moe_forward /
+ * omc_moe_forward_dev on a layer run the whole expert-parallel forward of
+ * this rank's own T tokens (any T >= 0, every rank calling for the same
+ * layer in the same order): route, each token sent once to every rank
+ * holding one of its experts (f16 rows), the experts there, the weighted f32
+ * partials back, and the combine at home in the reference's order; the
+ * result equals one GPU's tensor-core forward bit for bit.  One host wait per
+ * forward (the per-peer row counts) is bounded, see omc_ep_set_timeout.
+ *
+ * unique_id = NULL: no group; the caller composes a forward from
+ * omc_moe_route_dev and omc_moe_experts_dev over its own transport, and
+ * omc_moe_forward[_dev] on such a layer returns OMC_EUNSUPPORTED. */
 int omc_ep_init(int rank, int world, const void *unique_id);
 
-/* Not provided (the library owns no NCCL group): OMC_EUNSUPPORTED. */
+/* A new NCCL unique id (rank 0; len >= 128 bytes) for omc_ep_init. */
 int omc_ep_unique_id(void *buf, size_t len);
+
+/* The deadline of every host wait of an expert-parallel forward (default
+ * 30000 ms): the wait polls the work's completion and the NCCL
+ * communicator's asynchronous error; past the deadline (a peer rank that
+ * left or stopped calling) or on an NCCL error the communicator is aborted
+ * and the call returns OMC_ETIMEOUT or OMC_ENCCL.  Later expert-parallel
+ * forwards return OMC_ENCCL until omc_ep_init joins a new group. */
+int omc_ep_set_timeout(int timeout_ms);
+
+/* Waits, with that deadline, for the last expert-parallel forward enqueued by
+ * omc_moe_forward_dev (its stream), then reports a pending device error.
+ * omc_sync does the same first when a group was joined. */
+int omc_ep_wait(void);
 
 /* ---- introspection -------------------------------------------------- */
 

@@ -66,6 +66,10 @@ SIGNATURES = {
     "omc_sync": (_i, []),
     "omc_ep_init": (_i, [_i, _i, _vp]),
     "omc_ep_unique_id": (_i, [_vp, _sz]),
+    "omc_ep_set_timeout": (_i, [_i]),
+    "omc_ep_wait": (_i, []),
+    "omc_ep_layout_host": (_i, [_vp, _vp, _i, _i, _i, _i, _vp, _vp, _vp, _vp]),
+    "omc_ep_unpack_host": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _vp, _vp, _vp]),
     "omc_strerror": (C.c_char_p, [_i]),
     "omc_last_error": (C.c_char_p, []),
     "omc_set_profiling": (_i, [_i]),
@@ -177,10 +181,23 @@ def set_profiling(on: bool) -> None:
     lib().omc_set_profiling(1 if on else 0)
 
 
-def ep_init(rank: int, world: int) -> None:
+def ep_unique_id() -> bytes:
+    """A new NCCL unique id (128 bytes) for ep_init, made on rank 0."""
+    buf = C.create_string_buffer(128)
+    check(lib().omc_ep_unique_id(buf, 128), "omc_ep_unique_id")
+    return buf.raw
+
+
+def ep_init(rank: int, world: int, unique_id: bytes = None) -> None:
     """Hold routed experts [rank*E/world, (rank+1)*E/world) of every layer
-    created afterwards (see overhang_b200.ep)."""
-    check(lib().omc_ep_init(rank, world, None), "omc_ep_init")
+    created afterwards; with unique_id (ep_unique_id() of rank 0) the ranks
+    join one NCCL group and every forward runs expert-parallel."""
+    uid = None if unique_id is None else C.create_string_buffer(bytes(unique_id), 128)
+    check(lib().omc_ep_init(rank, world, uid), "omc_ep_init")
+
+
+def ep_set_timeout(ms: int) -> None:
+    check(lib().omc_ep_set_timeout(ms), "omc_ep_set_timeout")
 
 
 def time_stage(name) -> None:

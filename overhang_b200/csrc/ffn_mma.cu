@@ -112,6 +112,8 @@ struct GemmArgs {
                                // token s / K, choice s % K; s >= nrouted is token s - nrouted
     int ydirect;               // gemm2: 1 = write row slot of ypart ([slots][D]) instead of
                                // the [T][K+1][D] partials
+    const int *slot_tok;       // gemm1: token row of each slot (xh row), or NULL: derived
+                               // from the slot as above
     int T, R;                  // tokens, operand rows
     int *err;
 };
@@ -437,7 +439,9 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_gemm_kernel(const GemmArgs a)
                             int t = -1;
                             if (j < pr.n) {
                                 const int slot = a.rowinfo[pr.n0 + j];
-                                t = slot < 0 ? -1 : (slot < a.nrouted ? slot / a.K : slot - a.nrouted);
+                                t = slot < 0 ? -1
+                                             : (a.slot_tok ? a.slot_tok[slot]
+                                                           : (slot < a.nrouted ? slot / a.K : slot - a.nrouted));
                             }
                             xrow[u] = t;
                         }
@@ -776,6 +780,7 @@ extern "C" int omc_launch_mma_ffn(const omc_layer_dev *L, const float *x, int T,
     ga.K = L->k;
     ga.nrouted = T * L->k;
     ga.ydirect = 0;
+    ga.slot_tok = nullptr;
     ga.T = T;
     ga.R = R;
     ga.err = ws->err;
@@ -874,6 +879,7 @@ extern "C" int omc_launch_mma_rows(const omc_layer_dev *L, const float *x, int R
     ga.K = 1;
     ga.nrouted = R;
     ga.ydirect = 1;
+    ga.slot_tok = nullptr;
     ga.T = R;
     ga.R = ws->R_cap;
     ga.err = ws->err;
@@ -884,6 +890,60 @@ extern "C" int omc_launch_mma_rows(const omc_layer_dev *L, const float *x, int R
     moe_gemm_kernel<2><<<grid, NTHREADS, SMEM_BYTES, s>>>(ga);
     omc_prof_mark(s, "gemm_down");
     omc_g_launches += L->family == OMC_FAMILY_GEMMA ? 3 : 4;   // prenorm counts itself
+    return cudaGetLastError() == cudaSuccess ? 0 : OMC_ECUDA;
+}
+
+// Expert-parallel pass over explicit slots: slot s multiplies operand row
+// slot_tok[s] of xh (f16 [rows][D], already converted) by expert slot_e[s]
+// (a resident routed expert, or E for the shared expert) and writes
+// y[s] = slot_w[s] * expert(x) (rounded as the forward rounds w * y).  The
+// slots were counted into their groups already (ws->counts, ws->slotrow,
+// one atomic each, by ep_unpack_kernel); this builds the rest of the plan
+// (one block), the operand rows, and runs the two grouped GEMMs.
+__global__ void __launch_bounds__(1024) plan_counted_kernel(omc_plan_args p, const int32_t *__restrict__ ids,
+                                                            const float *__restrict__ w, int *err) {
+    __shared__ int smem[OMC_PLAN_SMEM_INTS];
+    omc_plan_block(p, ids, w, err, smem, true);
+}
+
+extern "C" int omc_launch_mma_slots(const omc_layer_dev *L, const uint16_t *xh, int nslots, const int32_t *slot_tok,
+                                    const int32_t *slot_e, const float *slot_w, const omc_ws *ws, int e_lo, int e_hi,
+                                    float *y, cudaStream_t s) {
+    if (nslots <= 0) return 0;
+    if (gemm_setup()) return OMC_ECUDA;
+    omc_plan_args pa;
+    omc_plan_setup(L, nslots, ws, &pa);
+    pa.K = 1;
+    pa.rows_mode = 1;
+    pa.e_lo = e_lo;
+    pa.e_hi = e_hi;
+    plan_counted_kernel<<<1, 1024, 0, s>>>(pa, slot_e, slot_w, ws->err);
+    omc_plan_fill_rows<<<(nslots + 255) / 256, 256, 0, s>>>(pa, slot_e, slot_w);
+    omc_prof_mark(s, "dispatch");
+    GemmArgs ga;
+    ga.L = *L;
+    ga.work = reinterpret_cast<const int4 *>(pa.work1);
+    ga.nwork = ws->nwork;
+    ga.act = ws->hp;
+    ga.xh = xh;
+    ga.hout = ws->hp;
+    ga.ypart = y;
+    ga.rowinfo = ws->rowinfo;
+    ga.roww = ws->roww;
+    ga.K = 1;
+    ga.nrouted = nslots;
+    ga.ydirect = 1;
+    ga.slot_tok = slot_tok;
+    ga.T = nslots;
+    ga.R = ws->R_cap;
+    ga.err = ws->err;
+    const int grid = g_num_sms > 0 ? g_num_sms : 148;
+    moe_gemm_kernel<1><<<grid, NTHREADS, SMEM_BYTES, s>>>(ga);
+    omc_prof_mark(s, "gemm_gateup");
+    ga.work = reinterpret_cast<const int4 *>(pa.work2);
+    moe_gemm_kernel<2><<<grid, NTHREADS, SMEM_BYTES, s>>>(ga);
+    omc_prof_mark(s, "gemm_down");
+    omc_g_launches += 4;
     return cudaGetLastError() == cudaSuccess ? 0 : OMC_ECUDA;
 }
 
@@ -968,6 +1028,7 @@ extern "C" int omc_launch_dense_i8(const omc_layer_dev *L, const float *x, int S
     ga.K = 1;
     ga.nrouted = S;
     ga.ydirect = 1;
+    ga.slot_tok = nullptr;
     ga.T = S;
     ga.R = ws->R_cap;
     ga.err = ws->err;

@@ -625,6 +625,10 @@ int omc_check_device_error(void) {
 
 int omc_sync(void) {
     if (!G.init) return omc_fail(OMC_ENOINIT, "omc_sync: omc_init not called");
+    if (G.ep_world > 1) {   /* a peer that left must not hang this wait */
+        const int rc = omc_ep_wait();
+        if (rc) return rc;
+    }
     cudaError_t e = cudaDeviceSynchronize();
     if (e != cudaSuccess) return omc_fail(OMC_ECUDA, "omc_sync: %s", cudaGetErrorString(e));
     return omc_check_device_error();
@@ -827,7 +831,10 @@ int omc_forward_device(omc_layer *L, const float *x, int T, float *out, int32_t 
     int rc;
     if ((rc = layer_ready(L))) return rc;
     if ((rc = omc_ws_ensure(L, T, 0))) return rc;
-    if (G.ep_world > 1) return omc_ep_forward(L, x, T, out, topk_idx, topk_w, s);
+    if (G.ep_world > 1) {
+        prof_begin(s);
+        return omc_ep_forward(L, x, T, out, topk_idx, topk_w, s);
+    }
     return forward_on_ws(L, &G.ws, x, T, out, topk_idx, topk_w, s);
 }
 
@@ -1098,6 +1105,7 @@ int omc_moe_forward(int layer, const float *x, int T, float *out, int32_t *topk_
         cudaStreamSynchronize(s);
         return rc;
     }
+    if (G.ep_world > 1 && (rc = omc_ep_wait())) return rc;   /* bounded: a peer may have left */
     for (int pass = 0;; ++pass) {
         if (T > 0) {
             CK(cudaMemcpyAsync(out, G.ws.out, (size_t)T * D * 4, cudaMemcpyDeviceToHost, s));
@@ -1106,7 +1114,9 @@ int omc_moe_forward(int layer, const float *x, int T, float *out, int32_t *topk_
         }
         CK(cudaStreamSynchronize(s));
         rc = omc_check_device_error();
-        if (rc != OMC_ERANGE || pass > 0 || T == 0) return rc;
+        /* (an expert-parallel forward is not redone: the other ranks would not
+         * take part in the repeated exchange) */
+        if (rc != OMC_ERANGE || pass > 0 || T == 0 || G.ep_world > 1) return rc;
         /* an activation outside the tensor-core path's f16 operand range:
          * the same forward again on the CUDA-core path, f32 throughout (the
          * routing is recomputed bit for bit, so only the expert path changes) */

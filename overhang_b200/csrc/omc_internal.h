@@ -196,6 +196,23 @@ int omc_launch_mma_rows(const omc_layer_dev *L, const float *x, int R, const omc
 /* dense pass: y[S][N] = x[S][K] . (ds * Wd)^T, Wd the down matrix of L's
  * expert 0 (L: E = 1, D = N, I = K with K % 64 == 0) */
 int omc_launch_dense_i8(const omc_layer_dev *L, const float *x, int S, const omc_ws *ws, float *y, cudaStream_t s);
+/* expert-parallel pass over explicit slots (ffn_mma.cu): y[s] = slot_w[s] *
+ * expert slot_e[s] (operand row slot_tok[s] of xh); the slots were counted
+ * into ws->counts / ws->slotrow already */
+int omc_launch_mma_slots(const omc_layer_dev *L, const uint16_t *xh, int nslots, const int32_t *slot_tok,
+                         const int32_t *slot_e, const float *slot_w, const omc_ws *ws, int e_lo, int e_hi, float *y,
+                         cudaStream_t s);
+/* expert-parallel exchange kernels (ep.cu; index arithmetic in omc_ep_plan.h) */
+int omc_launch_ep_layout(const int32_t *idx, int T, int k, int ne, int P, int32_t *tok_pos, int32_t *slot_pos,
+                         int32_t *counts, int32_t *pairs, cudaStream_t s);
+int omc_launch_ep_pack(const float *x, const int32_t *idx, const float *w, int T, int D, int k, int ne, int P,
+                       const int32_t *tok_pos, const int32_t *slot_pos, const int32_t *counts, uint16_t *send_x,
+                       int32_t *send_meta, uint16_t *home_xh, int *err, cudaStream_t s);
+int omc_launch_ep_unpack(const int32_t *meta, int Rr, int k, int P, const int *recv_base, const int *slot_base,
+                         int Thome, int E, int e_lo, int e_hi, int has_shared, int Sr, int32_t *slot_tok,
+                         int32_t *slot_e, float *slot_w, int *counts_e, int *slotrow, int *err, cudaStream_t s);
+int omc_launch_ep_combine(const float *ret, const int32_t *slot_pos, const float *y_shared, const float *sg, int T,
+                          int D, int k, int has_shared, float *out, cudaStream_t s);
 /* dst = f16(src), n % 8 == 0 */
 int omc_launch_f32_to_f16(const float *src, long long n, uint16_t *dst, cudaStream_t s);
 int omc_noalloc_setup(int device);

@@ -163,12 +163,13 @@ static __global__ void __launch_bounds__(256) omc_plan_fill_rows(omc_plan_args p
     const int nslots = p.T * p.K, i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i < nslots) {
         const int e = topk_idx[i], rk = p.slotrow[i];
-        if (rk < 0 || e < 0 || e >= p.E) return;
+        // explicit rows may name the shared expert (group E) themselves
+        if (rk < 0 || e < 0 || e > p.E || (e == p.E && !(p.rows_mode && p.has_shared))) return;
         const int row = p.offsets[e] + rk;
         if (row >= p.R_cap) return;
         p.rowinfo[row] = i;
         p.roww[row] = topk_w[i];
-    } else if (p.has_shared && i < nslots + p.T) {
+    } else if (p.has_shared && !p.rows_mode && i < nslots + p.T) {
         const int t = i - nslots, row = p.offsets[p.E] + t;
         if (row >= p.R_cap) return;
         p.rowinfo[row] = nslots + t;

@@ -48,3 +48,34 @@ def golden(name):
 GOLDEN_NAMES = ["olmoe_small", "olmoe_renorm", "olmoe_ties", "qwen_small", "qwen_tiny_l0",
                 "qwen_tiny_l3"]
 GEMMA_GOLDEN = ["gemma_small", "gemma_i8", "gemma_ties", "gemma_tiny_l0", "gemma_tiny_l5"]
+
+
+def route_dev(m, xd):
+    """omc_moe_route_dev on device tensor xd [T, D]: (idx, w, shared gate or None)."""
+    import ctypes as C
+    import torch
+    import overhang_b200 as ob
+    T = xd.shape[0]
+    idx = torch.empty((T, m.k), dtype=torch.int32, device=xd.device)
+    w = torch.empty((T, m.k), dtype=torch.float32, device=xd.device)
+    sg = torch.empty(T, dtype=torch.float32, device=xd.device) if m.has_shared else None
+    s = torch.cuda.current_stream(xd.device).cuda_stream
+    ob.check(ob.lib().omc_moe_route_dev(m.layer, C.c_void_p(xd.data_ptr()), T, C.c_void_p(idx.data_ptr()),
+                                        C.c_void_p(w.data_ptr()), C.c_void_p(sg.data_ptr() if sg is not None else None),
+                                        C.c_void_p(s)), "omc_moe_route_dev")
+    return idx, w, sg
+
+
+def experts_dev(m, rows, ids, w):
+    """omc_moe_experts_dev: y [R, D] = w[r] * expert ids[r] (rows[r]) on device tensors."""
+    import ctypes as C
+    import torch
+    import overhang_b200 as ob
+    R = rows.shape[0]
+    y = torch.empty((R, m.D), dtype=torch.float32, device=rows.device)
+    rows, ids, w = rows.contiguous(), ids.to(torch.int32).contiguous(), w.to(torch.float32).contiguous()
+    s = torch.cuda.current_stream(rows.device).cuda_stream
+    ob.check(ob.lib().omc_moe_experts_dev(m.layer, C.c_void_p(rows.data_ptr()), R, C.c_void_p(ids.data_ptr()),
+                                          C.c_void_p(w.data_ptr()), C.c_void_p(y.data_ptr()), C.c_void_p(s)),
+             "omc_moe_experts_dev")
+    return y

@@ -111,13 +111,12 @@ def test_gemma_route_and_expert_rows(gpu, oracle):
     takes residual rows, omc_moe_experts_dev residual rows too (it applies the
     experts' input norm), y = w * expert(rows)."""
     import torch
-    from overhang_b200.ep import LibCompute
+    from gpu_common import route_dev, experts_dev
     L = gemma_full()
     m = gpu.MoELayer.from_oracle_layer(next_layer_id(), L)
     x = oracle.normal(7300, (48, L.D), 1.5)
-    lc = LibCompute(m)
     xd = torch.from_numpy(x).cuda()
-    idx, w, _ = lc.route(xd)
+    idx, w, _ = route_dev(m, xd)
     torch.cuda.synchronize()
     ridx, rw = oracle.oracle_route(L, x)
     assert np.array_equal(idx.cpu().numpy(), ridx)
@@ -125,7 +124,7 @@ def test_gemma_route_and_expert_rows(gpu, oracle):
     rows = x[np.arange(48).repeat(2)]
     ids = np.array([e for t in range(48) for e in ridx[t, :2]], np.int32)
     wt = np.array([v for t in range(48) for v in rw[t, :2]], np.float32)
-    y = lc.experts(torch.from_numpy(rows).cuda(), torch.from_numpy(ids).cuda(), torch.from_numpy(wt).cuda())
+    y = experts_dev(m, torch.from_numpy(rows).cuda(), torch.from_numpy(ids).cuda(), torch.from_numpy(wt).cuda())
     torch.cuda.synchronize()
     want = oracle.oracle_expert_rows(L, rows, ids) * wt[:, None]
     assert_close(y.cpu().numpy(), want, what="gemma expert rows")

@@ -155,12 +155,12 @@ def test_tier_dev_noalloc_and_gemma(gpu, oracle, layer):
 
 def test_tier_rejects_rows_entry_and_forced_decode(gpu, oracle, layer):
     import torch
-    from overhang_b200.ep import LibCompute
+    from gpu_common import experts_dev
     B = gpu.MoELayer.from_oracle_layer(next_layer_id(), layer, tier=(SLOTS, 1, 0))
     rows = torch.from_numpy(oracle.normal(8830, (4, D))).cuda()
     ids = torch.zeros(4, dtype=torch.int32, device="cuda")
     with pytest.raises(gpu.OmcError):
-        LibCompute(B).experts(rows, ids, torch.ones(4, device="cuda"))
+        experts_dev(B, rows, ids, torch.ones(4, device="cuda"))
     gpu.set_path(gpu.PATH_DECODE)
     try:
         with pytest.raises(gpu.OmcError):
