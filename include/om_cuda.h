@@ -209,6 +209,24 @@ int omc_shared_set(int layer,
 int omc_moe_forward(int layer, const float *x, int T, float *out,
                     int32_t *topk_idx, float *topk_w);
 
+/* omc_moe_forward as a pipeline: enqueues the upload of x, the forward and
+ * the download of out / topk_idx / topk_w (nullable) and returns at once
+ * with *ticket; omc_moe_wait(ticket) returns when that call's results are in
+ * the host buffers.  Consecutive calls overlap: the upload of the next call's
+ * x and the download of the previous call's out run on their own copy
+ * streams while a forward runs, so a serving loop that keeps two or three
+ * calls in flight pays for the host<->device copies only where they exceed
+ * the forward.  x must stay unchanged until the call's ticket is waited for
+ * (or the next three calls were submitted), and out/topk until its wait;
+ * pinned host memory (cudaHostAlloc / cudaHostRegister) makes the copies
+ * asynchronous.  At most three calls are in flight: a fourth first waits for
+ * the oldest.  A device-side error is reported by the next omc_moe_wait; an
+ * OMC_ERANGE forward is not recomputed here (omc_moe_forward does that).  Not
+ * for expert-parallel layers (OMC_EUNSUPPORTED). */
+int omc_moe_forward_async(int layer, const float *x, int T, float *out,
+                          int32_t *topk_idx, float *topk_w, long long *ticket);
+int omc_moe_wait(long long ticket);
+
 /* The same with DEVICE pointers, enqueued on `stream` (a cudaStream_t; NULL
  * = the library's stream).  Returns once enqueued; the caller synchronises.
  * x and out must be 16-byte aligned (OMC_EINVAL otherwise): rows are moved

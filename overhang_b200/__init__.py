@@ -60,6 +60,8 @@ SIGNATURES = {
     "omc_tier_pick": (_i, [_vp, _vp, C.c_uint32, _i, _vp, _i, _vp, _vp, _vp]),
     "omc_moe_forward": (_i, [_i, _vp, _i, _vp, _vp, _vp]),
     "omc_moe_forward_dev": (_i, [_i, _vp, _i, _vp, _vp, _vp, _vp]),
+    "omc_moe_forward_async": (_i, [_i, _vp, _i, _vp, _vp, _vp, C.POINTER(C.c_longlong)]),
+    "omc_moe_wait": (_i, [C.c_longlong]),
     "omc_moe_forward_noalloc": (_i, [_i, _vp, _i, _vp, _vp, _vp, _vp]),
     "omc_moe_route_dev": (_i, [_i, _vp, _i, _vp, _vp, _vp, _vp]),
     "omc_moe_experts_dev": (_i, [_i, _vp, _i, _vp, _vp, _vp, _vp]),

@@ -39,6 +39,7 @@ static int g_graph_gen;
 void omc_graphs_invalidate(void) { ++g_graph_gen; }
 #define graphs_invalidate omc_graphs_invalidate
 static void graphs_release(void);
+static void async_release(void);
 
 int omc_fail(int code, const char *fmt, ...) {
     va_list ap;
@@ -167,6 +168,7 @@ void omc_shutdown(void) {
     cudaSetDevice(G.device);
     cudaDeviceSynchronize();
     graphs_release();
+    async_release();
     omc_ep_release();
     omc_tier_release();
     for (int i = 0; i < G.nlayers; ++i) {
@@ -1002,6 +1004,7 @@ int omc_moe_experts_dev(int layer, const float *x_rows, int R, const int32_t *ex
 #define OMC_NGRAPH 64
 typedef struct {
     int layer, T, gen, warm, failed;
+    const float *x;         /* the input buffer the graph reads (one graph per staging buffer) */
     cudaGraphExec_t exec;
     long long launches;     /* kernels in one replay */
 } omc_fgraph;
@@ -1024,10 +1027,11 @@ static int graphs_enabled(void) {
     return on && !G.profiling && !G.timer_on && G.ep_world <= 1;
 }
 
-static int forward_replayed(omc_layer *L, int layer, int T, cudaStream_t s) {
+static int forward_replayed(omc_layer *L, int layer, int T, const float *x, float *out, int32_t *idx, float *w,
+                            cudaStream_t s) {
     omc_fgraph *g = NULL;
     for (int i = 0; i < g_nfg; ++i)
-        if (g_fg[i].layer == layer && g_fg[i].T == T) g = &g_fg[i];
+        if (g_fg[i].layer == layer && g_fg[i].T == T && g_fg[i].x == x) g = &g_fg[i];
     if (!g) {
         if (g_nfg < OMC_NGRAPH) g = &g_fg[g_nfg++];
         else {
@@ -1038,6 +1042,7 @@ static int forward_replayed(omc_layer *L, int layer, int T, cudaStream_t s) {
         memset(g, 0, sizeof(*g));
         g->layer = layer;
         g->T = T;
+        g->x = x;
         g->gen = g_graph_gen;
     }
     if (g->gen != g_graph_gen) {
@@ -1056,15 +1061,15 @@ static int forward_replayed(omc_layer *L, int layer, int T, cudaStream_t s) {
     }
     if (!g->warm || g->failed) {
         g->warm = 1;
-        return omc_forward_device(L, G.ws.x, T, G.ws.out, G.ws.topk_idx, G.ws.topk_w, s);
+        return omc_forward_device(L, x, T, out, idx, w, s);
     }
     const long long l0 = omc_g_launches;
     if (cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
         cudaGetLastError();
         g->failed = 1;
-        return omc_forward_device(L, G.ws.x, T, G.ws.out, G.ws.topk_idx, G.ws.topk_w, s);
+        return omc_forward_device(L, x, T, out, idx, w, s);
     }
-    int rc = omc_forward_device(L, G.ws.x, T, G.ws.out, G.ws.topk_idx, G.ws.topk_w, s);
+    int rc = omc_forward_device(L, x, T, out, idx, w, s);
     cudaGraph_t graph = NULL;
     const cudaError_t ce = cudaStreamEndCapture(s, &graph);
     cudaError_t ie = cudaErrorUnknown;
@@ -1077,7 +1082,7 @@ static int forward_replayed(omc_layer *L, int layer, int T, cudaStream_t s) {
         g->exec = NULL;
         g->failed = 1;
         if (rc) return rc;
-        return omc_forward_device(L, G.ws.x, T, G.ws.out, G.ws.topk_idx, G.ws.topk_w, s);
+        return omc_forward_device(L, x, T, out, idx, w, s);
     }
     if (cudaGraphLaunch(g->exec, s) != cudaSuccess) {
         cudaGetLastError();
@@ -1099,7 +1104,7 @@ int omc_moe_forward(int layer, const float *x, int T, float *out, int32_t *topk_
     cudaStream_t s = G.stream;
     if (T > 0) CK(cudaMemcpyAsync(G.ws.x, x, (size_t)T * D * 4, cudaMemcpyHostToDevice, s));
     if ((rc = omc_tier_before(L, s)) ||
-        (rc = (T > 0 && graphs_enabled()) ? forward_replayed(L, layer, T, s)
+        (rc = (T > 0 && graphs_enabled()) ? forward_replayed(L, layer, T, G.ws.x, G.ws.out, G.ws.topk_idx, G.ws.topk_w, s)
                                           : omc_forward_device(L, G.ws.x, T, G.ws.out, G.ws.topk_idx, G.ws.topk_w, s)) ||
         (rc = omc_tier_after(L, s))) {
         cudaStreamSynchronize(s);
@@ -1128,6 +1133,119 @@ int omc_moe_forward(int layer, const float *x, int T, float *out, int32_t *topk_
             return rc;
         }
     }
+}
+
+/* ------------------------------------------------------ pipelined forward -- */
+/* omc_moe_forward split into three stream stages so that consecutive calls
+ * overlap: the upload of call i+1's x (copy stream), the forward of call i
+ * (the library stream, replayed from a CUDA graph per staging slot) and the
+ * download of call i-1's results (a second copy stream).  OMC_NASYNC staging
+ * slots of device x/out/top-k rotate; events order each slot's reuse. */
+#define OMC_NASYNC 3
+typedef struct {
+    int ready;
+    cudaStream_t up, down;
+    cudaEvent_t ev_up[OMC_NASYNC], ev_fwd[OMC_NASYNC], ev_down[OMC_NASYNC];
+    float *x[OMC_NASYNC], *out[OMC_NASYNC], *w[OMC_NASYNC];
+    int32_t *idx[OMC_NASYNC];
+    size_t cap_rows[OMC_NASYNC], cap_k[OMC_NASYNC];   /* bytes of x/out, of idx/w */
+    long long submitted, waited;                      /* tickets [waited, submitted) are in flight */
+} omc_async_state;
+static omc_async_state g_as;
+
+static void async_release(void) {
+    if (!g_as.ready) return;
+    for (int i = 0; i < OMC_NASYNC; ++i) {
+        cudaFree(g_as.x[i]);
+        cudaFree(g_as.out[i]);
+        cudaFree(g_as.idx[i]);
+        cudaFree(g_as.w[i]);
+        cudaEventDestroy(g_as.ev_up[i]);
+        cudaEventDestroy(g_as.ev_fwd[i]);
+        cudaEventDestroy(g_as.ev_down[i]);
+    }
+    cudaStreamDestroy(g_as.up);
+    cudaStreamDestroy(g_as.down);
+    memset(&g_as, 0, sizeof(g_as));
+}
+
+int omc_moe_wait(long long ticket) {
+    if (!G.init) return omc_fail(OMC_ENOINIT, "omc_moe_wait: omc_init not called");
+    if (!g_as.ready || ticket < g_as.waited) return OMC_OK;
+    if (ticket >= g_as.submitted) return omc_fail(OMC_EINVAL, "omc_moe_wait: ticket %lld was not submitted", ticket);
+    int rc = OMC_OK;
+    for (; g_as.waited <= ticket; ++g_as.waited) {
+        const cudaError_t e = cudaEventSynchronize(g_as.ev_down[g_as.waited % OMC_NASYNC]);
+        if (e != cudaSuccess && !rc) rc = omc_fail(OMC_ECUDA, "omc_moe_wait: %s", cudaGetErrorString(e));
+    }
+    if (rc) return rc;
+    return omc_check_device_error();
+}
+
+int omc_moe_forward_async(int layer, const float *x, int T, float *out, int32_t *topk_idx, float *topk_w,
+                          long long *ticket) {
+    if (!G.init) return omc_fail(OMC_ENOINIT, "omc_moe_forward_async: omc_init not called");
+    omc_layer *L = omc_get_layer(layer);
+    if (!L) return omc_fail(OMC_ENOINIT, "omc_moe_forward_async: layer %d not initialised", layer);
+    if (T < 1 || !x || !out || !ticket) return omc_fail(OMC_EINVAL, "omc_moe_forward_async: bad T or pointers");
+    if (G.ep_world > 1)
+        return omc_fail(OMC_EUNSUPPORTED, "omc_moe_forward_async: expert-parallel layers use omc_moe_forward");
+    int rc;
+    if (!g_as.ready) {
+        CK(cudaStreamCreateWithFlags(&g_as.up, cudaStreamNonBlocking));
+        CK(cudaStreamCreateWithFlags(&g_as.down, cudaStreamNonBlocking));
+        for (int i = 0; i < OMC_NASYNC; ++i) {
+            CK(cudaEventCreateWithFlags(&g_as.ev_up[i], cudaEventDisableTiming));
+            CK(cudaEventCreateWithFlags(&g_as.ev_fwd[i], cudaEventDisableTiming));
+            CK(cudaEventCreateWithFlags(&g_as.ev_down[i], cudaEventDisableTiming));
+        }
+        g_as.ready = 1;
+    }
+    /* a slot is reused after its previous call was waited for */
+    if (g_as.submitted - g_as.waited >= OMC_NASYNC && (rc = omc_moe_wait(g_as.submitted - OMC_NASYNC))) return rc;
+    const int slot = (int)(g_as.submitted % OMC_NASYNC);
+    const size_t D = (size_t)L->desc.D, K = (size_t)L->desc.k;
+    const size_t nrow = (size_t)T * D * 4, nk = (size_t)T * K * 4;
+    if (g_as.cap_rows[slot] < nrow || g_as.cap_k[slot] < nk) {
+        CK(cudaDeviceSynchronize());
+        graphs_invalidate();
+        cudaFree(g_as.x[slot]);
+        cudaFree(g_as.out[slot]);
+        cudaFree(g_as.idx[slot]);
+        cudaFree(g_as.w[slot]);
+        g_as.x[slot] = g_as.out[slot] = g_as.w[slot] = NULL;
+        g_as.idx[slot] = NULL;
+        g_as.cap_rows[slot] = g_as.cap_k[slot] = 0;
+        CK(cudaMalloc((void **)&g_as.x[slot], nrow));
+        CK(cudaMalloc((void **)&g_as.out[slot], nrow));
+        CK(cudaMalloc((void **)&g_as.idx[slot], nk));
+        CK(cudaMalloc((void **)&g_as.w[slot], nk));
+        g_as.cap_rows[slot] = nrow;
+        g_as.cap_k[slot] = nk;
+    }
+    if ((rc = omc_ws_ensure(L, T, 0))) return rc;
+    cudaStream_t s = G.stream;
+    /* upload: after the slot's previous forward has read its x */
+    CK(cudaStreamWaitEvent(g_as.up, g_as.ev_fwd[slot], 0));
+    CK(cudaMemcpyAsync(g_as.x[slot], x, nrow, cudaMemcpyHostToDevice, g_as.up));
+    CK(cudaEventRecord(g_as.ev_up[slot], g_as.up));
+    /* forward: after the upload, and after the slot's previous download has read out */
+    CK(cudaStreamWaitEvent(s, g_as.ev_up[slot], 0));
+    CK(cudaStreamWaitEvent(s, g_as.ev_down[slot], 0));
+    if ((rc = omc_tier_before(L, s)) ||
+        (rc = graphs_enabled() ? forward_replayed(L, layer, T, g_as.x[slot], g_as.out[slot], g_as.idx[slot], g_as.w[slot], s)
+                               : omc_forward_device(L, g_as.x[slot], T, g_as.out[slot], g_as.idx[slot], g_as.w[slot], s)) ||
+        (rc = omc_tier_after(L, s)))
+        return rc;
+    CK(cudaEventRecord(g_as.ev_fwd[slot], s));
+    /* download */
+    CK(cudaStreamWaitEvent(g_as.down, g_as.ev_fwd[slot], 0));
+    CK(cudaMemcpyAsync(out, g_as.out[slot], nrow, cudaMemcpyDeviceToHost, g_as.down));
+    if (topk_idx) CK(cudaMemcpyAsync(topk_idx, g_as.idx[slot], nk, cudaMemcpyDeviceToHost, g_as.down));
+    if (topk_w) CK(cudaMemcpyAsync(topk_w, g_as.w[slot], nk, cudaMemcpyDeviceToHost, g_as.down));
+    CK(cudaEventRecord(g_as.ev_down[slot], g_as.down));
+    *ticket = g_as.submitted++;
+    return OMC_OK;
 }
 
 /* ---------------------------------------------------------------- debug -- */
