@@ -207,7 +207,8 @@ __global__ void __launch_bounds__(256) ep_unpack_kernel(const int32_t *__restric
 }
 
 // out[t] = [sg[t] * y_shared[t]] + sum_kk ret[slot_pos[t][kk]], kk ascending:
-// the single-GPU combine (combine_kernel in ffn_mma.cu) on the returned rows.
+// the single-GPU combine (fused into the down GEMM's epilogue, ffn_mma.cu) on
+// the returned rows, in the same order.
 __global__ void __launch_bounds__(256) ep_combine_kernel(const float *__restrict__ ret,
                                                           const int32_t *__restrict__ slot_pos,
                                                           const float *__restrict__ y_shared,

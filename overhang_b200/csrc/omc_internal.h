@@ -148,6 +148,8 @@ typedef struct {
     float *roww;                  /* [R]: routing weight of the row (1 shared, 0 pad) */
     int *work;                    /* tile work list                       */
     int *nwork;                   /* [4] work counts                      */
+    int *fin;                     /* [T][row-tile pairs] partials written, the down GEMM's fused
+                                     combine (after nwork; zeroed with counts per forward) */
     uint16_t *xh;                 /* [T][D] f16 token operand (tensor-core path) */
     uint16_t *hp;                 /* AOL f16 [Imax_pad/64][R][64]         */
     float *ypart;                 /* [T][k + 1][D]                        */
