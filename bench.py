@@ -72,6 +72,7 @@ WORKLOADS = {
     "olmoe_decode64": ("olmoe", 64), "qwen_decode64": ("qwen", 64),
     "gemma_prefill": ("gemma", 2048), "gemma_decode": ("gemma", 1), "gemma_decode64": ("gemma", 64),
     "qwen_ep": ("qwen", 8192),
+    "qwen_decode40": ("qwen", 1),
 }
 BIAS = "uniform"                 # qwen_ep: router bias, uniform (none) or zipf
 T_TOTAL = None                   # qwen_ep: tokens over all ranks
@@ -101,6 +102,8 @@ def set_workload(name, tokens=None, world=1, bias="uniform"):
     WORKLOAD = f"{FAMILY}_layer_{kind}_T{T}"
     if name == "qwen_ep":
         WORKLOAD = f"qwen_layer_ep_T{T_TOTAL}_{BIAS}"
+    if name == "qwen_decode40":
+        WORKLOAD = "qwen_40layers_decode_T1"
     total = E * EXPERT_BYTES + (3 * D * IS + 4 * (2 * IS + D) if IS else 0)
     CONFIG = {"workload": WORKLOAD, "D": D, "I": I, "E": E, "k": K, "T": T,
               "weights": f"int8 per-row + f32 scales, N(0,0.02) seed {SEED_W}",
@@ -292,6 +295,11 @@ def run_reference(args):
     else:
         kind, fn = "port", (lambda xx: pyoracle.oracle_moe(L, xx)[0])
     x = pyoracle.normal(SEED_X, (T, D))
+    if args.workload == "qwen_decode40":
+        # one decode step is one token through every layer: the reference's
+        # moe_step once per layer (each layer's weights are the same size)
+        one = fn
+        fn = lambda xx: [one(xx) for _ in range(args.layers)]  # noqa: E731
     # size each step so the whole run stays within ~150 s of CPU time
     per_step = max(0.25, min(10.0, 150.0 / max(args.steps + args.warmup, 1)))
     t0 = time.perf_counter()
@@ -624,6 +632,144 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+def run_layers(args):
+    """configs[2] decode: the Qwen-shaped layer's int8 weights for every one of
+    args.layers layers resident in HBM at once (40 layers: ~32 GB of experts),
+    one decode step = one token through every layer in turn (each layer's
+    forward_dev on its own input row, all captured in one CUDA graph).  The
+    layers share one seeded expert set, stored once per layer in its own HBM
+    (layer l's expert e is seeded expert (e + 37 l) mod E, and layer l's router
+    its own seed), so every step streams every layer's routed experts from
+    HBM: no layer reads another's weights from L2."""
+    import torch
+    rank, world, local = env_rank()
+    if world > 1:
+        raise SystemExit("--workload qwen_decode40 runs on one GPU")
+    dev = local
+    torch.cuda.set_device(dev)
+    import overhang_b200 as ob
+    NL = args.layers
+    ob.init(dev, 0)
+    pyoracle, L = make_layer()
+    a = L.arrays
+    t0 = time.perf_counter()
+    layers = []
+    for l in range(NL):
+        perm = (np.arange(E) + 37 * l) % E
+        rq, rs = pyoracle.quantize_c(pyoracle.normal(SEED_W * 1000003 + 7 + 101 * l, (E, D), 0.02))
+        m = ob.MoELayer(l, FAMILY, D, I, E, K, rq, rs, 1, 1, IS)
+        m.set_experts_packed(a["g"][perm], a["gs"][perm], a["u"][perm], a["us"][perm], a["d"][perm],
+                             a["ds"][perm])
+        m.set_shared(a["sh_g"], a["sh_gs"], a["sh_u"], a["sh_us"], a["sh_d"], a["sh_ds"], a["sh_gate"])
+        layers.append(m)
+    t_up = time.perf_counter() - t0
+    nbuf = 4
+    xs = [[torch.from_numpy(pyoracle.normal(SEED_X + 97 * l + i, (T, D))).cuda() for l in range(NL)]
+          for i in range(nbuf)]
+    outs = [torch.empty((T, D), dtype=torch.float32, device="cuda") for _ in range(NL)]
+    idx = torch.empty((T, K), dtype=torch.int32, device="cuda")
+    wts = torch.empty((T, K), dtype=torch.float32, device="cuda")
+    stream = torch.cuda.Stream(device=dev)
+    torch.cuda.set_stream(stream)
+    sptr = stream.cuda_stream
+
+    def step(i):
+        for l, m in enumerate(layers):
+            m.forward_dev(xs[i % nbuf][l].data_ptr(), T, outs[l].data_ptr(), idx.data_ptr(), wts.data_ptr(), sptr)
+
+    for i in range(args.warmup):
+        step(i)
+    ob.sync()
+    ob.set_profiling(True)
+    stage = []
+    for i in range(3):
+        step(i)
+        torch.cuda.synchronize()
+        stage.append(ob.stage_times())
+    ob.set_profiling(False)
+    ob.launch_count(reset=True)
+    graphs = []
+    for i in range(nbuf):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            step(i)
+        graphs.append(g)
+    per_step_launches = ob.launch_count() / nbuf
+    for g in graphs:
+        g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+    def timed_pass():
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for i in range(args.steps):
+            graphs[i % nbuf].replay()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1)
+
+    clk = ClockSampler(dev)
+    clk.start()
+    passes = [timed_pass()]
+    repeats = max(1, int(np.ceil(args.min_seconds * 1e3 / max(passes[0], 1e-3))))
+    while len(passes) < repeats:
+        passes.append(timed_pass())
+    clocks = clk.stop()
+    t_ms = float(statistics.median(passes))
+    step_s = t_ms / args.steps / 1e3
+    value = T * args.steps / (t_ms / 1e3)
+    hbm, tf, src = peaks()
+    # one step's algorithmic bytes: in every layer, each routed expert a token
+    # chose (distinct per layer), the shared expert, the int8 router and its
+    # scales, the shared gate vector, and x in / out back
+    idx_all = []
+    for l, m in enumerate(layers):
+        _, li, _ = m.forward(xs[0][l].cpu().numpy())
+        idx_all.append(len(np.unique(li)))
+    shared_bytes = 3 * D * IS + 4 * (2 * IS + D)
+    router_bytes = E * D + 4 * E + 4 * D
+    step_bytes = sum(n * EXPERT_BYTES + shared_bytes + router_bytes + 2 * T * D * 4 for n in idx_all)
+    ach = step_bytes / step_s / 1e9
+    # the host entry, one call per layer (x in, out + routing back), every step
+    hx = [torch.from_numpy(xs[0][l].cpu().numpy()).pin_memory() for l in range(NL)]
+    hout = torch.empty((T, D), dtype=torch.float32).pin_memory()
+    lib = ob.lib()
+
+    def host_step():
+        for l in range(NL):
+            ob.check(lib.omc_moe_forward(l, C.c_void_p(hx[l].data_ptr()), T, C.c_void_p(hout.data_ptr()), None,
+                                         None), "omc_moe_forward")
+
+    for _ in range(args.warmup):
+        host_step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        host_step()
+    e2e = T * args.steps / (time.perf_counter() - t0)
+    names = [n for n, _ in stage[-1]]
+    st = dict(zip(names, np.array([[v for _, v in row] for row in stage]).mean(axis=0).tolist()))
+    line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": 1, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": t_ms / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32xint8->f32", "data": "synthetic",
+            "config": dict(CONFIG, workload=WORKLOAD, layers=NL, parallelism="single",
+                           launch="cuda_graph (one step = every layer)",
+                           resident_expert_bytes=NL * (E * EXPERT_BYTES + shared_bytes),
+                           upload_s=round(t_up, 1),
+                           l2="every step streams each layer's own routed experts: distinct HBM per layer"),
+            "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": NL * T * D * 4,
+                    "d2h_bytes_per_step": NL * T * D * 4, "entry": "omc_moe_forward per layer (blocking)"},
+            "gpu_launches": per_step_launches * args.steps, "repeats": len(passes),
+            "pass_ms": [round(v, 4) for v in passes],
+            "stage_ms_last_layer": st,
+            "roofline": {"bound": "hbm", "achieved": ach, "peak": hbm, "unit": "GB/s", "frac": ach / hbm,
+                         "traffic": None, "kernel": "decode_moe (every layer of a step)", "peak_source": src,
+                         "alg_bytes_per_step": step_bytes, "layer_us": t_ms / args.steps / NL * 1e3},
+            "clocks": clocks}
+    print(json.dumps(line), flush=True)
+    ob.shutdown()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -638,6 +784,8 @@ def main():
     ap.add_argument("--workload", default=None, choices=sorted(WORKLOADS),
                     help="olmoe_prefill (BASELINE configs[1], the default line on one GPU), olmoe_decode, "
                          "qwen_prefill, qwen_decode, ...; qwen_ep (configs[3], the default on N>1 GPUs)")
+    ap.add_argument("--layers", type=int, default=40,
+                    help="qwen_decode40: layers resident at once (each with its own copy of the expert set)")
     ap.add_argument("--bias", default="uniform", choices=["uniform", "zipf"],
                     help="qwen_ep: router bias (zipf: bias_e = -1.1 ln(rank_e), skewed expert load)")
     ap.add_argument("--graph", action="store_true", default=True,
@@ -662,6 +810,8 @@ def main():
     set_workload(args.workload, args.tokens, world, args.bias)
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload == "qwen_decode40":
+        run_layers(args)
     else:
         run_ours(args)
 

@@ -84,6 +84,7 @@ constexpr uint32_t TMEM_COLS = 512;
 constexpr uint32_t ACC_SLOT_COLS = 160;   // accumulator slots at columns 0 and 160
 constexpr uint32_t TCOL_A = 320;          // A stages: 320 + 64*stage + 32*tile
 constexpr int SMALL_N = 80;               // items up to this many tokens take one slot
+constexpr int FIN_K = 8;                  // fused combine: partial loads unrolled up to this k
 static_assert(TCOL_A + ST * 64 <= TMEM_COLS && 2 * ACC_SLOT_COLS <= TCOL_A, "TMEM columns");
 
 // smem layout (bytes, from a 1024-aligned base)
@@ -661,14 +662,47 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_gemm_kernel(const GemmArgs a)
                     const int d = (2 * it.mt + half) * OMC_TM + r;     // output row of this thread
                     if (half < item_nmat<PHASE>(L, it) && d < L.D) {
                         const int K = a.K;
-                        for (int j = 0; j < it.n; ++j) {
-                            const int t = s_fin[j];
-                            if (t < 0) continue;
-                            const float *yp = a.ypart + (size_t)t * (K + 1) * L.D + d;
-                            float v = 0.f;
-                            if (L.has_shared) v = __fmul_rn(__ldcg(yp + (size_t)K * L.D), __ldg(a.sg + t));
-                            for (int kk = 0; kk < K; ++kk) v = __fadd_rn(v, __ldcg(yp + (size_t)kk * L.D));
-                            a.out[(size_t)t * L.D + d] = v;
+                        const size_t DD = (size_t)L.D;
+                        int j = 0;
+                        for (;;) {
+                            // the next two tokens this item finalises: every partial of both
+                            // is loaded before the sums, so the L2 round trips overlap
+                            int t0 = -1, t1 = -1;
+                            for (; j < it.n && t0 < 0; ++j) t0 = s_fin[j];
+                            for (; j < it.n && t1 < 0; ++j) t1 = s_fin[j];
+                            if (t0 < 0) break;
+                            const float *y0 = a.ypart + (size_t)t0 * (K + 1) * DD + d;
+                            const float *y1 = a.ypart + (size_t)(t1 < 0 ? t0 : t1) * (K + 1) * DD + d;
+                            if (K <= FIN_K) {
+                                float p0[FIN_K], p1[FIN_K];
+#pragma unroll
+                                for (int kk = 0; kk < FIN_K; ++kk) {
+                                    p0[kk] = kk < K ? __ldcg(y0 + kk * DD) : 0.f;
+                                    p1[kk] = kk < K && t1 >= 0 ? __ldcg(y1 + kk * DD) : 0.f;
+                                }
+                                float v0 = 0.f, v1 = 0.f;
+                                if (L.has_shared) {
+                                    v0 = __fmul_rn(__ldcg(y0 + K * DD), __ldg(a.sg + t0));
+                                    if (t1 >= 0) v1 = __fmul_rn(__ldcg(y1 + K * DD), __ldg(a.sg + t1));
+                                }
+#pragma unroll
+                                for (int kk = 0; kk < FIN_K; ++kk)
+                                    if (kk < K) {
+                                        v0 = __fadd_rn(v0, p0[kk]);
+                                        v1 = __fadd_rn(v1, p1[kk]);
+                                    }
+                                a.out[(size_t)t0 * DD + d] = v0;
+                                if (t1 >= 0) a.out[(size_t)t1 * DD + d] = v1;
+                            } else {
+                                for (int q = 0; q < 2; ++q) {
+                                    const int t = q ? t1 : t0;
+                                    if (t < 0) continue;
+                                    const float *yp = q ? y1 : y0;
+                                    float v = L.has_shared ? __fmul_rn(__ldcg(yp + K * DD), __ldg(a.sg + t)) : 0.f;
+                                    for (int kk = 0; kk < K; ++kk) v = __fadd_rn(v, __ldcg(yp + kk * DD));
+                                    a.out[(size_t)t * DD + d] = v;
+                                }
+                            }
                         }
                     }
                 }

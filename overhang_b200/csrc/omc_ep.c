@@ -101,6 +101,11 @@ typedef struct {
     void *buf[16];
     size_t cap[16];
     int *h_cnt;                 /* pinned: own counts [4P], received pairs [2P] */
+    /* the expert pass's own workspace: growing it never touches the library's
+     * (whose top-k buffers the blocking entry hands to this forward) */
+    omc_ws xws;
+    omc_ws_ptrs xW;
+    size_t xbytes[16];
     cudaEvent_t ev;
     cudaStream_t last_stream;
 } omc_ep_state;
@@ -351,8 +356,8 @@ int omc_ep_forward(omc_layer *L, const float *x, int T, float *out, int32_t *top
     omc_prof_mark(s, "ep_dispatch");
     /* 5. the slots through the local experts (and the home tokens' shared expert) */
     if (Ntot > 0) {
-        if ((rc = omc_ws_ensure_rows(L, Ntot))) return rc;
-        omc_ws *ws = &G.ws;
+        if ((rc = omc_ws_ensure_rows_in(L, Ntot, &st->xws, &st->xW, st->xbytes))) return rc;
+        omc_ws *ws = &st->xws;
         CK(cudaMemsetAsync(ws->counts, 0, (size_t)(ws->done - ws->counts + 1) * sizeof(int), s));
         if ((rc = omc_launch_ep_unpack(recv_m, Rr, k, P, recv_base, slot_base, Tz, E, L->e0, L->e0 + L->ne, sh, Sr,
                                        slot_tok, slot_e, slot_w, ws->counts, ws->slotrow, G.d_err, s)))
@@ -388,6 +393,7 @@ void omc_ep_release(void) {
     if (!st) return;
     if (st->have_comm) N.CommDestroy(st->comm);
     for (int i = 0; i < 16; ++i) cudaFree(st->buf[i]);
+    omc_ws_free_in(&st->xW, st->xbytes, 16);
     if (st->h_cnt) cudaFreeHost(st->h_cnt);
     if (st->ev) cudaEventDestroy(st->ev);
     free(st);

@@ -524,10 +524,10 @@ static int dec_ensure(const omc_layer_dev *P) {
     return OMC_OK;
 }
 
-/* grow-only buffer */
-static int ws_buf(int slot, void **ptr, size_t need) {
+/* grow-only buffer of a workspace whose sizes are bytes[] */
+static int ws_buf_in(size_t *bytes, int slot, void **ptr, size_t need) {
     if (need == 0) need = 256;
-    if (G.ws_bytes[slot] >= need && *ptr) return OMC_OK;
+    if (bytes[slot] >= need && *ptr) return OMC_OK;
     cudaStreamSynchronize(G.stream);
     cudaDeviceSynchronize();
     graphs_invalidate();
@@ -537,16 +537,18 @@ static int ws_buf(int slot, void **ptr, size_t need) {
     cudaError_t e = cudaMalloc(ptr, n);
     if (e != cudaSuccess) {
         cudaGetLastError();
-        G.ws_bytes[slot] = 0;
+        bytes[slot] = 0;
         return omc_fail(OMC_ENOMEM, "workspace: cudaMalloc(%zu) failed", n);
     }
-    G.ws_bytes[slot] = n;
+    bytes[slot] = n;
     return OMC_OK;
 }
 
 /* Workspace for Tz tokens (or explicit rows) with nslots routed slots and
- * nshared implicit shared-expert rows. */
-static int ws_ensure_core(const omc_layer *L, size_t Tz, size_t nslots, size_t nshared, int host_io) {
+ * nshared implicit shared-expert rows, in (ws, W, bytes): the library's own
+ * (G.ws) or another caller's (the expert-parallel pass). */
+static int ws_ensure_in(const omc_layer *L, size_t Tz, size_t nslots, size_t nshared, int host_io, omc_ws *ws,
+                        omc_ws_ptrs *W, size_t *bytes) {
     const omc_layer_dev *P = &L->dev;
     const size_t D = (size_t)P->D, E = (size_t)P->E, K = (size_t)P->k;
     const size_t Imax_rows = (size_t)(P->Is_rows > P->I_rows ? P->Is_rows : P->I_rows);
@@ -555,7 +557,7 @@ static int ws_ensure_core(const omc_layer *L, size_t Tz, size_t nslots, size_t n
     /* activation rows: every routed slot + shared rows + 16-row padding per expert */
     const size_t R = omc_round_up((int)(nslots + nshared + (E + 1) * OMC_ROW_ALIGN), 128);
     int rc = 0;
-    omc_ws_ptrs *W = &G.ws_ptrs;
+#define ws_buf(slot, ptr, need) ws_buf_in(bytes, slot, ptr, need)
     if (host_io) {
         if ((rc = ws_buf(0, (void **)&W->x, Tz * D * 4))) return rc;
         if ((rc = ws_buf(1, (void **)&W->out, Tz * D * 4))) return rc;
@@ -577,7 +579,7 @@ static int ws_ensure_core(const omc_layer *L, size_t Tz, size_t nslots, size_t n
         if ((rc = ws_buf(14, (void **)&W->xg_r, Tz * D * 4))) return rc;
         if ((rc = ws_buf(15, (void **)&W->xg_e, Tz * D * 4))) return rc;
     }
-    omc_ws *ws = &G.ws;
+#undef ws_buf
     ws->T_cap = T;
     ws->R_cap = (int)R;
     ws->x = W->x;
@@ -607,11 +609,25 @@ static int ws_ensure_core(const omc_layer *L, size_t Tz, size_t nslots, size_t n
 
 int omc_ws_ensure(const omc_layer *L, int T, int host_io) {
     const size_t Tz = (size_t)T;
-    return ws_ensure_core(L, Tz, Tz * (size_t)L->dev.k, L->dev.has_shared ? Tz : 0, host_io);
+    return ws_ensure_in(L, Tz, Tz * (size_t)L->dev.k, L->dev.has_shared ? Tz : 0, host_io, &G.ws, &G.ws_ptrs,
+                        G.ws_bytes);
 }
 
 int omc_ws_ensure_rows(const omc_layer *L, int rows) {
-    return ws_ensure_core(L, (size_t)rows, (size_t)rows, 0, 0);
+    return ws_ensure_in(L, (size_t)rows, (size_t)rows, 0, 0, &G.ws, &G.ws_ptrs, G.ws_bytes);
+}
+
+int omc_ws_ensure_rows_in(const omc_layer *L, int rows, omc_ws *ws, omc_ws_ptrs *W, size_t *bytes) {
+    return ws_ensure_in(L, (size_t)rows, (size_t)rows, 0, 0, ws, W, bytes);
+}
+
+void omc_ws_free_in(omc_ws_ptrs *W, size_t *bytes, int nbytes) {
+    void **p = (void **)W;
+    for (size_t i = 0; i < sizeof(*W) / sizeof(void *); ++i) {
+        cudaFree(p[i]);
+        p[i] = NULL;
+    }
+    memset(bytes, 0, sizeof(size_t) * (size_t)nbytes);
 }
 
 /* ---------------------------------------------------------------- errors -- */

@@ -80,6 +80,9 @@ void *omc_slab_alloc(size_t n, int *on_host);
 omc_layer *omc_get_layer(int layer);
 int omc_ws_ensure(const omc_layer *L, int T, int host_io);
 int omc_ws_ensure_rows(const omc_layer *L, int rows);
+/* the same for a workspace other than the library's own (the expert-parallel pass) */
+int omc_ws_ensure_rows_in(const omc_layer *L, int rows, omc_ws *ws, omc_ws_ptrs *W, size_t *bytes);
+void omc_ws_free_in(omc_ws_ptrs *W, size_t *bytes, int nbytes);
 int omc_expert_upload(int D, int D_pad, int D_rows, int I_, int I_pad, int I_rows, const int8_t *g, const float *gs,
                       const int8_t *u, const float *us, const int8_t *d, const float *ds, omc_expert_ptrs *ep,
                       int reuse);
