@@ -345,6 +345,7 @@ def run_ours(args):
         uid = [ob.ep_unique_id() if rank == 0 else None]
         dist.broadcast_object_list(uid, src=0)
         ob.ep_init(rank, world, uid[0])    # this rank holds experts [rank*E/world, (rank+1)*E/world)
+        ob.ep_set_combine(ob.EP_RANKSUM if args.ep_combine == "ranksum" else ob.EP_EXACT)
     pyoracle, L = make_layer()
     tier = args.tier if args.tier and not ep_mode else 0
     layer = ob.MoELayer.from_oracle_layer(0, L, tier=(tier, 1, 0) if tier else None)
@@ -472,6 +473,17 @@ def run_ours(args):
     ob.time_stage(None)
     ob.sync()
     t_max = float(statistics.median(passes))
+    other_combine = None
+    if ep_mode:
+        # the other return mode, timed the same way (three passes), for comparison
+        other = "exact" if args.ep_combine == "ranksum" else "ranksum"
+        ob.ep_set_combine(ob.EP_EXACT if other == "exact" else ob.EP_RANKSUM)
+        for i in range(args.warmup):
+            step(i)
+        op = float(statistics.median([timed_pass() for _ in range(3)]))
+        ob.ep_set_combine(ob.EP_RANKSUM if args.ep_combine == "ranksum" else ob.EP_EXACT)
+        other_combine = {"ep_combine": other, "value": world * T * args.steps / (op / 1e3),
+                         "ms_per_step": op / args.steps}
     value = world * T * args.steps / (t_max / 1e3)
 
     # end to end through the host entry: pinned x in, out + routing back
@@ -606,6 +618,9 @@ def run_ours(args):
             "clocks": clocks}
     if balance:
         line["ep_balance"] = balance
+    if other_combine:
+        line["config"]["ep_combine"] = args.ep_combine
+        line["ep_other_combine"] = other_combine
     if tier:
         # the tiered store: experts outside the HBM slots cross the host link
         # once per step that routes to them (the tier_fetch stage)
@@ -784,6 +799,9 @@ def main():
     ap.add_argument("--workload", default=None, choices=sorted(WORKLOADS),
                     help="olmoe_prefill (BASELINE configs[1], the default line on one GPU), olmoe_decode, "
                          "qwen_prefill, qwen_decode, ...; qwen_ep (configs[3], the default on N>1 GPUs)")
+    ap.add_argument("--ep-combine", default="ranksum", choices=["ranksum", "exact"],
+                    help="N>1 expert parallel: results back as one row per (token, rank) summed there "
+                         "(ranksum) or one row per slot summed at home (exact: bit-equal to one GPU)")
     ap.add_argument("--layers", type=int, default=40,
                     help="qwen_decode40: layers resident at once (each with its own copy of the expert set)")
     ap.add_argument("--bias", default="uniform", choices=["uniform", "zipf"],

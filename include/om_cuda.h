@@ -324,6 +324,21 @@ int omc_ep_unique_id(void *buf, size_t len);
  * forwards return OMC_ENCCL until omc_ep_init joins a new group. */
 int omc_ep_set_timeout(int timeout_ms);
 
+/* How the expert ranks return their results (every rank of a group must use
+ * the same mode):
+ *   OMC_EP_EXACT   one f32 row per routed slot, summed at home in selection
+ *                  order: the result equals one GPU's forward bit for bit
+ *                  (the default);
+ *   OMC_EP_RANKSUM one f32 row per (token, expert rank), the sum of the
+ *                  token's slots on that rank in selection order, added at
+ *                  home rank by rank: fewer bytes back (one row per token and
+ *                  rank instead of one per slot: 4x fewer at 2 ranks of top-8),
+ *                  the same terms in another order (within the parity
+ *                  tolerance of the reference, not bit-equal to one GPU). */
+#define OMC_EP_EXACT   0
+#define OMC_EP_RANKSUM 1
+int omc_ep_set_combine(int mode);
+
 /* Waits, with that deadline, for the last expert-parallel forward enqueued by
  * omc_moe_forward_dev (its stream), then reports a pending device error.
  * omc_sync does the same first when a group was joined. */

@@ -69,6 +69,7 @@ SIGNATURES = {
     "omc_ep_init": (_i, [_i, _i, _vp]),
     "omc_ep_unique_id": (_i, [_vp, _sz]),
     "omc_ep_set_timeout": (_i, [_i]),
+    "omc_ep_set_combine": (_i, [_i]),
     "omc_ep_wait": (_i, []),
     "omc_ep_layout_host": (_i, [_vp, _vp, _i, _i, _i, _i, _vp, _vp, _vp, _vp]),
     "omc_ep_unpack_host": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _vp, _vp, _vp]),
@@ -196,6 +197,14 @@ def ep_init(rank: int, world: int, unique_id: bytes = None) -> None:
     join one NCCL group and every forward runs expert-parallel."""
     uid = None if unique_id is None else C.create_string_buffer(bytes(unique_id), 128)
     check(lib().omc_ep_init(rank, world, uid), "omc_ep_init")
+
+
+EP_EXACT, EP_RANKSUM = 0, 1
+
+
+def ep_set_combine(mode: int) -> None:
+    """EP_EXACT (bit-equal to one GPU) or EP_RANKSUM (one row per token and rank back)."""
+    check(lib().omc_ep_set_combine(mode), "omc_ep_set_combine")
 
 
 def ep_set_timeout(ms: int) -> None:

@@ -207,8 +207,7 @@ __global__ void __launch_bounds__(256) ep_unpack_kernel(const int32_t *__restric
 }
 
 // out[t] = [sg[t] * y_shared[t]] + sum_kk ret[slot_pos[t][kk]], kk ascending:
-// the single-GPU combine (fused into the down GEMM's epilogue, ffn_mma.cu) on
-// the returned rows, in the same order.
+// the single-GPU combine (combine_kernel in ffn_mma.cu) on the returned rows.
 __global__ void __launch_bounds__(256) ep_combine_kernel(const float *__restrict__ ret,
                                                           const int32_t *__restrict__ slot_pos,
                                                           const float *__restrict__ y_shared,
@@ -231,6 +230,65 @@ __global__ void __launch_bounds__(256) ep_combine_kernel(const float *__restrict
         acc.y = __fadd_rn(acc.y, p.y);
         acc.z = __fadd_rn(acc.z, p.z);
         acc.w = __fadd_rn(acc.w, p.w);
+    }
+    *reinterpret_cast<float4 *>(out + (size_t)t * D + d) = acc;
+}
+
+// Per-rank-sum return (OMC_EP_RANKSUM): one f32 row per received token row,
+// the sum of its slots' weighted partials on this rank in selection order.
+// A thread per (row, 4 columns).
+__global__ void __launch_bounds__(256) ep_ranksum_kernel(const int32_t *__restrict__ meta, int Rr, int k, EpBases b,
+                                                          const float *__restrict__ y, int D, float *__restrict__ rows) {
+    const int j = blockIdx.y;
+    const int d = (blockIdx.x * blockDim.x + threadIdx.x) * 4;
+    if (j >= Rr || d >= D) return;
+    const int M = omc_ep_meta_ints(k);
+    const int p = omc_ep_row_peer(b.recv_base, b.P, j);
+    const int32_t *m = meta + (size_t)j * M;
+    const int base = b.slot_base[p] + m[0], n = m[1];
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int q = 0; q < n; ++q) {
+        const float4 v = *reinterpret_cast<const float4 *>(y + (size_t)(base + q) * D + d);
+        acc.x = __fadd_rn(acc.x, v.x);
+        acc.y = __fadd_rn(acc.y, v.y);
+        acc.z = __fadd_rn(acc.z, v.z);
+        acc.w = __fadd_rn(acc.w, v.w);
+    }
+    *reinterpret_cast<float4 *>(rows + (size_t)j * D + d) = acc;
+}
+
+// Home combine of per-rank sums: out = [sg * shared] + the row each rank
+// returned, ranks taken in the order their first expert appears in the
+// token's selection.
+__global__ void __launch_bounds__(256) ep_combine_ranksum_kernel(const float *__restrict__ ret,
+                                                                  const int32_t *__restrict__ tok_pos,
+                                                                  const int32_t *__restrict__ idx,
+                                                                  const float *__restrict__ y_shared,
+                                                                  const float *__restrict__ sg, int T, int D, int k,
+                                                                  int ne, int P, int has_shared,
+                                                                  float *__restrict__ out) {
+    const int t = blockIdx.y;
+    const int d = (blockIdx.x * blockDim.x + threadIdx.x) * 4;
+    if (t >= T || d >= D) return;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (has_shared) {
+        const float4 s = *reinterpret_cast<const float4 *>(y_shared + (size_t)t * D + d);
+        const float g = sg[t];
+        acc = make_float4(__fmul_rn(s.x, g), __fmul_rn(s.y, g), __fmul_rn(s.z, g), __fmul_rn(s.w, g));
+    }
+    unsigned seen = 0u;
+    for (int kk = 0; kk < k; ++kk) {
+        const int e = idx[(size_t)t * k + kk];
+        const int r = e >= 0 ? e / ne : -1;
+        if (r < 0 || r >= P || (seen >> r & 1u)) continue;
+        seen |= 1u << r;
+        const int pos = tok_pos[(size_t)t * P + r];
+        if (pos < 0) continue;
+        const float4 v = *reinterpret_cast<const float4 *>(ret + (size_t)pos * D + d);
+        acc.x = __fadd_rn(acc.x, v.x);
+        acc.y = __fadd_rn(acc.y, v.y);
+        acc.z = __fadd_rn(acc.z, v.z);
+        acc.w = __fadd_rn(acc.w, v.w);
     }
     *reinterpret_cast<float4 *>(out + (size_t)t * D + d) = acc;
 }
@@ -282,6 +340,32 @@ extern "C" int omc_launch_ep_combine(const float *ret, const int32_t *slot_pos, 
     if (D % 4) return OMC_EINVAL;
     ep_combine_kernel<<<dim3((D / 4 + 255) / 256, T), 256, 0, s>>>(ret, slot_pos, y_shared, sg, T, D, k, has_shared,
                                                                   out);
+    omc_g_launches += 1;
+    return cudaGetLastError() == cudaSuccess ? 0 : OMC_ECUDA;
+}
+
+extern "C" int omc_launch_ep_ranksum(const int32_t *meta, int Rr, int k, int P, const int *recv_base,
+                                     const int *slot_base, const float *y, int D, float *rows, cudaStream_t s) {
+    if (Rr <= 0) return 0;
+    if (P > EP_MAXR || D % 4) return OMC_EINVAL;
+    EpBases b;
+    b.P = P;
+    for (int p = 0; p <= P; ++p) {
+        b.recv_base[p] = recv_base[p];
+        b.slot_base[p] = slot_base[p];
+    }
+    ep_ranksum_kernel<<<dim3((D / 4 + 255) / 256, Rr), 256, 0, s>>>(meta, Rr, k, b, y, D, rows);
+    omc_g_launches += 1;
+    return cudaGetLastError() == cudaSuccess ? 0 : OMC_ECUDA;
+}
+
+extern "C" int omc_launch_ep_combine_ranksum(const float *ret, const int32_t *tok_pos, const int32_t *idx,
+                                             const float *y_shared, const float *sg, int T, int D, int k, int ne,
+                                             int P, int has_shared, float *out, cudaStream_t s) {
+    if (T <= 0) return 0;
+    if (D % 4 || P > 32) return OMC_EINVAL;
+    ep_combine_ranksum_kernel<<<dim3((D / 4 + 255) / 256, T), 256, 0, s>>>(ret, tok_pos, idx, y_shared, sg, T, D, k,
+                                                                          ne, P, has_shared, out);
     omc_g_launches += 1;
     return cudaGetLastError() == cudaSuccess ? 0 : OMC_ECUDA;
 }

@@ -12,11 +12,9 @@
 //   gemm<1> per (expert, 128 rows of I, <=128 tokens): gate and up
 //           H^T = silu(gs*Wg.X^T) * (us*Wu.X^T), written as the f16 operand of
 //   gemm<2> per (expert, 128 rows of D, <=128 tokens): Y^T = ds*Wd.H^T,
-//           times the routing weight, into a per-(token, choice) partial;
-//           the combine is fused into its epilogue: the item whose partials
-//           complete a token's row-tile pair sums out = [sigmoid gate *
-//           shared] + sum_k partial_k in the reference's order
-//           (engines/olmoe.c:395-397, engines/qwen.c:459-462,492)
+//           times the routing weight, into a per-(token, choice) partial
+//   combine out = [sigmoid gate * shared] + sum_k partial_k, in the reference's
+//           order (engines/olmoe.c:395-397, engines/qwen.c:459-462,492)
 //
 // GEMM design (one persistent CTA per SM, warp-specialised, 864 threads).
 // The dequantised expert weights are the MMA's A operand, held in tensor
@@ -84,7 +82,6 @@ constexpr uint32_t TMEM_COLS = 512;
 constexpr uint32_t ACC_SLOT_COLS = 160;   // accumulator slots at columns 0 and 160
 constexpr uint32_t TCOL_A = 320;          // A stages: 320 + 64*stage + 32*tile
 constexpr int SMALL_N = 80;               // items up to this many tokens take one slot
-constexpr int FIN_K = 8;                  // fused combine: partial loads unrolled up to this k
 static_assert(TCOL_A + ST * 64 <= TMEM_COLS && 2 * ACC_SLOT_COLS <= TCOL_A, "TMEM columns");
 
 // smem layout (bytes, from a 1024-aligned base)
@@ -93,8 +90,7 @@ constexpr int OFF_I8 = OFF_A + SA * A_BYTES;
 constexpr int OFF_STG = OFF_I8 + SI * 2 * W_BYTES;         // [2 K halves][NMAX rows][128 B] h staging
 constexpr int OFF_TAB = OFF_STG + 2 * NMAX * 128;        // [NEPI][NMAX] (ypart row, weight) per epilogue warp
 constexpr int OFF_BAR = OFF_TAB + NEPI * NMAX * 8;
-constexpr int OFF_FIN = OFF_BAR + 512;                     // [NMAX] token each row finalises (-1 none)
-constexpr int SMEM_BYTES = OFF_FIN + NMAX * 4 + 1024;
+constexpr int SMEM_BYTES = OFF_BAR + 512 + 1024;
 static_assert(SMEM_BYTES <= 227 * 1024, "smem budget");
 static_assert(OFF_I8 % 1024 == 0 && OFF_STG % 1024 == 0, "alignment");
 
@@ -118,13 +114,6 @@ struct GemmArgs {
                                // the [T][K+1][D] partials
     const int *slot_tok;       // gemm1: token row of each slot (xh row), or NULL: derived
                                // from the slot as above
-    // gemm2, combine fused into the epilogue (fin != NULL): per (token, row-tile
-    // pair) a count of written partials [T][npairs]; the item whose partials
-    // complete a count (need = k + shared) sums that token's partials into out
-    int *fin;
-    float *out;
-    const float *sg;           // shared-expert gate per token (has_shared)
-    int npairs, need;
     int T, R;                  // tokens, operand rows
     int *err;
 };
@@ -304,10 +293,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_gemm_kernel(const GemmArgs a)
     uint64_t *accempty = accfull + 2;                                 // [2] accumulator slot drained
     uint64_t *stgfull = accempty + 2;                                 // h staging written (phase 1)
     uint64_t *stgfree = stgfull + 1;                                  // h staging read by its bulk store
-    uint64_t *finA = stgfree + 1;                                     // phase 2: the item's partials written
-    uint64_t *finB = finA + 1;                                        // phase 2: the rows to finalise known
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(finB + 1);
-    int *s_fin = reinterpret_cast<int *>(smem + OFF_FIN);
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(stgfree + 1);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -331,8 +317,6 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_gemm_kernel(const GemmArgs a)
         }
         mbar_init(stgfull, NEPI);
         mbar_init(stgfree, 1);
-        mbar_init(finA, NEPI);
-        mbar_init(finB, NEPI);
         *abort_flag = 0;
         fence_barrier_init();
     }
@@ -635,77 +619,6 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_gemm_kernel(const GemmArgs a)
                 __syncwarp();
                 if (lane == 0)
                     for (int j = 0; j < acc.nslots; ++j) mbar_arrive(&accempty[acc.slot(j)]);
-                if (a.fin) {
-                    // The combine, fused: each token of the item counts this item's
-                    // partial of its row-tile pair (one atomic, after every epilogue
-                    // warp's stores are fenced); the item that completes a count sums
-                    // the token's k (+ shared) partials in the reference's order
-                    // (engines/olmoe.c:395-397, engines/qwen.c:459-492) into out.
-                    // The waits are bounded mbarriers, as everywhere in this kernel.
-                    __threadfence();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(finA);
-                    if (!warp_wait(finA, ci & 1, a.err, OMC_SITE_GEMM_EPILOGUE, abort_flag)) break;
-                    const int et = e * 32 + lane;                     // 0 .. NEPI*32-1 >= NMAX
-                    if (et < it.n) {
-                        const int slot = a.rowinfo[it.n0 + et];
-                        int t = -1, fin = -1;
-                        if (slot >= 0) t = slot < a.nrouted ? slot / a.K : slot - a.nrouted;
-                        if (t >= 0 && t < a.T && atomicAdd(a.fin + (size_t)t * a.npairs + it.mt, 1) == a.need - 1)
-                            fin = t;
-                        s_fin[et] = fin;
-                    }
-                    __threadfence();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(finB);
-                    if (!warp_wait(finB, ci & 1, a.err, OMC_SITE_GEMM_EPILOGUE, abort_flag)) break;
-                    const int d = (2 * it.mt + half) * OMC_TM + r;     // output row of this thread
-                    if (half < item_nmat<PHASE>(L, it) && d < L.D) {
-                        const int K = a.K;
-                        const size_t DD = (size_t)L.D;
-                        int j = 0;
-                        for (;;) {
-                            // the next two tokens this item finalises: every partial of both
-                            // is loaded before the sums, so the L2 round trips overlap
-                            int t0 = -1, t1 = -1;
-                            for (; j < it.n && t0 < 0; ++j) t0 = s_fin[j];
-                            for (; j < it.n && t1 < 0; ++j) t1 = s_fin[j];
-                            if (t0 < 0) break;
-                            const float *y0 = a.ypart + (size_t)t0 * (K + 1) * DD + d;
-                            const float *y1 = a.ypart + (size_t)(t1 < 0 ? t0 : t1) * (K + 1) * DD + d;
-                            if (K <= FIN_K) {
-                                float p0[FIN_K], p1[FIN_K];
-#pragma unroll
-                                for (int kk = 0; kk < FIN_K; ++kk) {
-                                    p0[kk] = kk < K ? __ldcg(y0 + kk * DD) : 0.f;
-                                    p1[kk] = kk < K && t1 >= 0 ? __ldcg(y1 + kk * DD) : 0.f;
-                                }
-                                float v0 = 0.f, v1 = 0.f;
-                                if (L.has_shared) {
-                                    v0 = __fmul_rn(__ldcg(y0 + K * DD), __ldg(a.sg + t0));
-                                    if (t1 >= 0) v1 = __fmul_rn(__ldcg(y1 + K * DD), __ldg(a.sg + t1));
-                                }
-#pragma unroll
-                                for (int kk = 0; kk < FIN_K; ++kk)
-                                    if (kk < K) {
-                                        v0 = __fadd_rn(v0, p0[kk]);
-                                        v1 = __fadd_rn(v1, p1[kk]);
-                                    }
-                                a.out[(size_t)t0 * DD + d] = v0;
-                                if (t1 >= 0) a.out[(size_t)t1 * DD + d] = v1;
-                            } else {
-                                for (int q = 0; q < 2; ++q) {
-                                    const int t = q ? t1 : t0;
-                                    if (t < 0) continue;
-                                    const float *yp = q ? y1 : y0;
-                                    float v = L.has_shared ? __fmul_rn(__ldcg(yp + K * DD), __ldg(a.sg + t)) : 0.f;
-                                    for (int kk = 0; kk < K; ++kk) v = __fadd_rn(v, __ldcg(yp + kk * DD));
-                                    a.out[(size_t)t * DD + d] = v;
-                                }
-                            }
-                        }
-                    }
-                }
             }
             acc.end();
         }
@@ -744,6 +657,29 @@ __global__ void __launch_bounds__(1024) plan_rows_kernel(omc_plan_args p, const 
                                                          const float *__restrict__ w, int *err) {
     __shared__ int smem[OMC_PLAN_SMEM_INTS];
     omc_plan_block(p, ids, w, err, smem);
+}
+
+// ------------------------------------------------------------- combine ---
+__global__ void __launch_bounds__(256) combine_kernel(const float *__restrict__ ypart, const float *__restrict__ sg,
+                                                      int T, int D, int K, int has_shared, float *__restrict__ out) {
+    const int t = blockIdx.y;
+    const int d = (blockIdx.x * blockDim.x + threadIdx.x) * 4;
+    if (t >= T || d >= D) return;
+    const float *yp = ypart + (size_t)t * (K + 1) * D + d;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (has_shared) {
+        const float4 s = *reinterpret_cast<const float4 *>(yp + (size_t)K * D);
+        const float gsg = sg[t];
+        acc = make_float4(__fmul_rn(s.x, gsg), __fmul_rn(s.y, gsg), __fmul_rn(s.z, gsg), __fmul_rn(s.w, gsg));
+    }
+    for (int kk = 0; kk < K; ++kk) {
+        const float4 p = *reinterpret_cast<const float4 *>(yp + (size_t)kk * D);
+        acc.x = __fadd_rn(acc.x, p.x);
+        acc.y = __fadd_rn(acc.y, p.y);
+        acc.z = __fadd_rn(acc.z, p.z);
+        acc.w = __fadd_rn(acc.w, p.w);
+    }
+    *reinterpret_cast<float4 *>(out + (size_t)t * D + d) = acc;
 }
 
 int g_num_sms = 0;
@@ -845,10 +781,6 @@ extern "C" int omc_launch_mma_ffn(const omc_layer_dev *L, const float *x, int T,
     ga.nrouted = T * L->k;
     ga.ydirect = 0;
     ga.slot_tok = nullptr;
-    ga.fin = nullptr;
-    ga.out = nullptr;
-    ga.sg = nullptr;
-    ga.npairs = ga.need = 0;
     ga.T = T;
     ga.R = R;
     ga.err = ws->err;
@@ -858,14 +790,12 @@ extern "C" int omc_launch_mma_ffn(const omc_layer_dev *L, const float *x, int T,
     omc_prof_mark(s, "gemm_gateup");
     ga.work = work2;
     ga.act = ws->hp;
-    ga.fin = ws->fin;                      // counts zeroed with the plan's (forward_on_ws)
-    ga.out = out;
-    ga.sg = ws->sg;
-    ga.npairs = (L->D_rows / OMC_TM + 1) / 2;
-    ga.need = L->k + (L->has_shared ? 1 : 0);
     moe_gemm_kernel<2><<<grid, NTHREADS, SMEM_BYTES, s>>>(ga);
     omc_prof_mark(s, "gemm_down");
-    omc_g_launches += 2;
+    dim3 gc((L->D / 4 + 255) / 256, T);
+    combine_kernel<<<gc, 256, 0, s>>>(ws->ypart, ws->sg, T, L->D, L->k, L->has_shared, out);
+    omc_prof_mark(s, "combine");
+    omc_g_launches += 3;
     return cudaGetLastError() == cudaSuccess ? 0 : OMC_ECUDA;
 }
 
@@ -950,10 +880,6 @@ extern "C" int omc_launch_mma_rows(const omc_layer_dev *L, const float *x, int R
     ga.nrouted = R;
     ga.ydirect = 1;
     ga.slot_tok = nullptr;
-    ga.fin = nullptr;
-    ga.out = nullptr;
-    ga.sg = nullptr;
-    ga.npairs = ga.need = 0;
     ga.T = R;
     ga.R = ws->R_cap;
     ga.err = ws->err;
@@ -1008,10 +934,6 @@ extern "C" int omc_launch_mma_slots(const omc_layer_dev *L, const uint16_t *xh, 
     ga.nrouted = nslots;
     ga.ydirect = 1;
     ga.slot_tok = slot_tok;
-    ga.fin = nullptr;
-    ga.out = nullptr;
-    ga.sg = nullptr;
-    ga.npairs = ga.need = 0;
     ga.T = nslots;
     ga.R = ws->R_cap;
     ga.err = ws->err;
@@ -1107,10 +1029,6 @@ extern "C" int omc_launch_dense_i8(const omc_layer_dev *L, const float *x, int S
     ga.nrouted = S;
     ga.ydirect = 1;
     ga.slot_tok = nullptr;
-    ga.fin = nullptr;
-    ga.out = nullptr;
-    ga.sg = nullptr;
-    ga.npairs = ga.need = 0;
     ga.T = S;
     ga.R = ws->R_cap;
     ga.err = ws->err;

@@ -97,6 +97,7 @@ typedef struct {
     ncclComm_t comm;
     int have_comm, broken;
     int timeout_ms;
+    int combine;                /* OMC_EP_EXACT or OMC_EP_RANKSUM */
     /* grow-only device buffers; sizes in bytes */
     void *buf[16];
     size_t cap[16];
@@ -110,7 +111,8 @@ typedef struct {
     cudaStream_t last_stream;
 } omc_ep_state;
 
-enum { B_IDX, B_W, B_SG, B_XE, B_POS, B_SENDX, B_SENDM, B_OPND, B_RECVM, B_STOK, B_SE, B_SW, B_Y, B_RET, B_SMALL };
+enum { B_IDX, B_W, B_SG, B_XE, B_POS, B_SENDX, B_SENDM, B_OPND, B_RECVM, B_STOK, B_SE, B_SW, B_Y, B_RET, B_SMALL,
+       B_RSUM };
 
 static omc_ep_state *S(void) {
     if (!G.ep) {
@@ -233,6 +235,14 @@ int omc_ep_set_timeout(int timeout_ms) {
     return OMC_OK;
 }
 
+int omc_ep_set_combine(int mode) {
+    if (mode != OMC_EP_EXACT && mode != OMC_EP_RANKSUM) return omc_fail(OMC_EINVAL, "omc_ep_set_combine: mode %d", mode);
+    omc_ep_state *st = S();
+    if (!st) return omc_fail(OMC_ENOMEM, "omc_ep_set_combine: host alloc");
+    st->combine = mode;
+    return OMC_OK;
+}
+
 int omc_ep_wait(void) {
     if (!G.init) return omc_fail(OMC_ENOINIT, "omc_ep_wait: omc_init not called");
     omc_ep_state *st = S();
@@ -320,8 +330,12 @@ int omc_ep_forward(omc_layer *L, const float *x, int T, float *out, int32_t *top
     }
     const int Rr = recv_base[P], Sr = slot_base[P];
     const int Ntot = Sr + (sh ? Tz : 0);
-    size_t sent_slots = 0;
-    for (int p = 0; p < P; ++p) sent_slots += (size_t)send_slots[p];
+    size_t sent_slots = 0, sent_rows = 0;
+    for (int p = 0; p < P; ++p) {
+        sent_slots += (size_t)send_slots[p];
+        sent_rows += (size_t)send_rows[p];
+    }
+    const int ranksum = st->combine == OMC_EP_RANKSUM;
     /* 4. pack and send the rows */
     uint16_t *send_x = NULL, *opnd = NULL;
     int32_t *send_m = NULL, *recv_m = NULL, *slot_tok = NULL, *slot_e = NULL;
@@ -334,8 +348,10 @@ int omc_ep_forward(omc_layer *L, const float *x, int T, float *out, int32_t *top
         (rc = ep_buf(st, B_SE, (size_t)Ntot * 4, (void **)&slot_e)) ||
         (rc = ep_buf(st, B_SW, (size_t)Ntot * 4, (void **)&slot_w)) ||
         (rc = ep_buf(st, B_Y, (size_t)Ntot * D * 4, (void **)&y)) ||
-        (rc = ep_buf(st, B_RET, sent_slots * D * 4, (void **)&ret)))
+        (rc = ep_buf(st, B_RET, (ranksum ? sent_rows : sent_slots) * D * 4, (void **)&ret)))
         return rc;
+    float *rsum = NULL;
+    if (ranksum && (rc = ep_buf(st, B_RSUM, (size_t)Rr * D * 4, (void **)&rsum))) return rc;
     if (T > 0 && (rc = omc_launch_ep_pack(gemma ? xe : x, idx, w, T, D, k, ne, P, tok_pos, slot_pos, counts, send_x,
                                           send_m, sh ? opnd : NULL, G.d_err, s)))
         return omc_fail(rc, "ep pack launch failed");
@@ -365,20 +381,33 @@ int omc_ep_forward(omc_layer *L, const float *x, int T, float *out, int32_t *top
         if ((rc = omc_launch_mma_slots(P_, opnd, Ntot, slot_tok, slot_e, slot_w, ws, L->e0, L->e0 + L->ne, y, s)))
             return omc_fail(rc, "ep expert pass launch failed (%s)", omc_strerror(rc));
     }
-    /* 6. the partials back home */
+    /* 6. the partials back home: one f32 row per routed slot (exact), or per
+     * received token row the sum of its slots here, in selection order */
+    if (ranksum && Rr > 0 &&
+        (rc = omc_launch_ep_ranksum(recv_m, Rr, k, P, recv_base, slot_base, y, D, rsum, s)))
+        return omc_fail(rc, "ep rank-sum launch failed");
     NCK(N.GroupStart());
     for (int p = 0; p < P; ++p) {
-        const int ns = slot_base[p + 1] - slot_base[p];
-        if (ns) NCK(N.Send(y + (size_t)slot_base[p] * D, (size_t)ns * D, ncclFloat32, p, st->comm, s));
-        if (send_slots[p])
-            NCK(N.Recv(ret + (size_t)ret_base[p] * D, (size_t)send_slots[p] * D, ncclFloat32, p, st->comm, s));
+        if (ranksum) {
+            const int nr = recv_base[p + 1] - recv_base[p];
+            if (nr) NCK(N.Send(rsum + (size_t)recv_base[p] * D, (size_t)nr * D, ncclFloat32, p, st->comm, s));
+            if (send_rows[p])
+                NCK(N.Recv(ret + (size_t)send_base[p] * D, (size_t)send_rows[p] * D, ncclFloat32, p, st->comm, s));
+        } else {
+            const int ns = slot_base[p + 1] - slot_base[p];
+            if (ns) NCK(N.Send(y + (size_t)slot_base[p] * D, (size_t)ns * D, ncclFloat32, p, st->comm, s));
+            if (send_slots[p])
+                NCK(N.Recv(ret + (size_t)ret_base[p] * D, (size_t)send_slots[p] * D, ncclFloat32, p, st->comm, s));
+        }
     }
     NCK(N.GroupEnd());
     omc_prof_mark(s, "ep_return");
     /* 7. combine at home */
     if (T > 0) {
-        if ((rc = omc_launch_ep_combine(ret, slot_pos, sh ? y + (size_t)Sr * D : NULL, sg, T, D, k, sh, out, s)))
-            return omc_fail(rc, "ep combine launch failed");
+        rc = ranksum ? omc_launch_ep_combine_ranksum(ret, tok_pos, idx, sh ? y + (size_t)Sr * D : NULL, sg, T, D, k,
+                                                     ne, P, sh, out, s)
+                     : omc_launch_ep_combine(ret, slot_pos, sh ? y + (size_t)Sr * D : NULL, sg, T, D, k, sh, out, s);
+        if (rc) return omc_fail(rc, "ep combine launch failed");
         if (topk_idx) CK(cudaMemcpyAsync(topk_idx, idx, (size_t)T * k * 4, cudaMemcpyDeviceToDevice, s));
         if (topk_w) CK(cudaMemcpyAsync(topk_w, w, (size_t)T * k * 4, cudaMemcpyDeviceToDevice, s));
     }

@@ -566,8 +566,7 @@ static int ws_ensure_in(const omc_layer *L, size_t Tz, size_t nslots, size_t nsh
     if ((rc = ws_buf(3, (void **)&W->topk_idx, Tz * K * 4))) return rc;
     if ((rc = ws_buf(4, (void **)&W->topk_w, Tz * K * 4))) return rc;
     if ((rc = ws_buf(5, (void **)&W->sg, Tz * 4))) return rc;
-    const size_t npairs = (size_t)(P->D_rows / OMC_TM + 1) / 2;
-    if ((rc = ws_buf(6, (void **)&W->counts, (E + 4) * 4 * 4 + Tz * npairs * 4))) return rc;
+    if ((rc = ws_buf(6, (void **)&W->counts, (E + 4) * 4 * 3 + 64))) return rc;
     if ((rc = ws_buf(7, (void **)&W->rowinfo, R * 8))) return rc;   /* rowinfo, then roww */
     if ((rc = ws_buf(8, (void **)&W->work, (size_t)omc_mma_work_items(P, (int)R) * 16))) return rc;
     if ((rc = ws_buf(9, (void **)&W->xh, Tz * D * 2))) return rc;
@@ -592,7 +591,6 @@ static int ws_ensure_in(const omc_layer *L, size_t Tz, size_t nslots, size_t nsh
     ws->offsets = W->counts + (E + 4);
     ws->done = W->counts + 2 * (E + 4);
     ws->nwork = W->counts + 3 * (E + 4);
-    ws->fin = W->counts + 4 * (E + 4);
     ws->slotrow = W->slotrow;
     ws->rowinfo = W->rowinfo;
     ws->roww = (float *)(W->rowinfo + R);
@@ -795,12 +793,11 @@ static int forward_on_ws(omc_layer *L, const omc_ws *ws, const float *x, int T, 
     const int mma = use_mma(L, T);
     omc_plan_args plan;
     if (mma) {
-        /* the per-expert counts (counted by the select blocks), the
-         * select-done counter and the fused combine's partial counts start at
-         * zero: counts, offsets, done, nwork, fin are one run of ints */
+        /* the per-expert counts (counted by the select blocks) and the
+         * select-done counter start at zero: counts, offsets, done are one
+         * run of ints in the workspace */
         omc_plan_setup(&L->dev, T, ws, &plan);
-        const size_t nfin = (size_t)T * ((L->dev.D_rows / OMC_TM + 1) / 2);
-        CK(cudaMemsetAsync(ws->counts, 0, ((size_t)(ws->fin - ws->counts) + nfin) * sizeof(int), s));
+        CK(cudaMemsetAsync(ws->counts, 0, (size_t)(ws->done - ws->counts + 1) * sizeof(int), s));
     }
     /* GEMMA: x is the residual; the router and the experts each read their
      * own norm of it (prenorm.cu).  The tensor-core path takes the experts'
@@ -877,7 +874,7 @@ static size_t noalloc_layout(const omc_layer_dev *P, int T, char *base, omc_ws *
     TAKE(topk_idx, int32_t *, Tz * K * 4);
     TAKE(topk_w, float *, Tz * K * 4);
     TAKE(sg, float *, Tz * 4);
-    TAKE(counts, int *, (E + 4) * 4 * 4 + Tz * (size_t)((P->D_rows / OMC_TM + 1) / 2) * 4);
+    TAKE(counts, int *, (E + 4) * 4 * 3 + 64);
     TAKE(rowinfo, int *, R * 8);   /* rowinfo, then roww */
     TAKE(work, int *, (size_t)omc_mma_work_items(P, (int)R) * 16);
     TAKE(xh, uint16_t *, Tz * D * 2);
@@ -894,7 +891,6 @@ static size_t noalloc_layout(const omc_layer_dev *P, int T, char *base, omc_ws *
         ws->offsets = ws->counts + (E + 4);
         ws->done = ws->counts + 2 * (E + 4);
         ws->nwork = ws->counts + 3 * (E + 4);
-        ws->fin = ws->counts + 4 * (E + 4);
         ws->roww = (float *)(ws->rowinfo + R);
         ws->x = ws->out = NULL;
         ws->T_cap = T;

@@ -148,8 +148,6 @@ typedef struct {
     float *roww;                  /* [R]: routing weight of the row (1 shared, 0 pad) */
     int *work;                    /* tile work list                       */
     int *nwork;                   /* [4] work counts                      */
-    int *fin;                     /* [T][row-tile pairs] partials written, the down GEMM's fused
-                                     combine (after nwork; zeroed with counts per forward) */
     uint16_t *xh;                 /* [T][D] f16 token operand (tensor-core path) */
     uint16_t *hp;                 /* AOL f16 [Imax_pad/64][R][64]         */
     float *ypart;                 /* [T][k + 1][D]                        */
@@ -215,6 +213,11 @@ int omc_launch_ep_unpack(const int32_t *meta, int Rr, int k, int P, const int *r
                          int32_t *slot_e, float *slot_w, int *counts_e, int *slotrow, int *err, cudaStream_t s);
 int omc_launch_ep_combine(const float *ret, const int32_t *slot_pos, const float *y_shared, const float *sg, int T,
                           int D, int k, int has_shared, float *out, cudaStream_t s);
+int omc_launch_ep_ranksum(const int32_t *meta, int Rr, int k, int P, const int *recv_base, const int *slot_base,
+                          const float *y, int D, float *rows, cudaStream_t s);
+int omc_launch_ep_combine_ranksum(const float *ret, const int32_t *tok_pos, const int32_t *idx, const float *y_shared,
+                                  const float *sg, int T, int D, int k, int ne, int P, int has_shared, float *out,
+                                  cudaStream_t s);
 /* dst = f16(src), n % 8 == 0 */
 int omc_launch_f32_to_f16(const float *src, long long n, uint16_t *dst, cudaStream_t s);
 int omc_noalloc_setup(int device);
