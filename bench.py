@@ -672,7 +672,7 @@ def run_layers(args):
     for l in range(NL):
         perm = (np.arange(E) + 37 * l) % E
         rq, rs = pyoracle.quantize_c(pyoracle.normal(SEED_W * 1000003 + 7 + 101 * l, (E, D), 0.02))
-        m = ob.MoELayer(l, FAMILY, D, I, E, K, rq, rs, 1, 1, IS)
+        m = ob.MoELayer(l, ob.FAMILY_QWEN, D, I, E, K, rq, rs, 1, 1, IS)
         m.set_experts_packed(a["g"][perm], a["gs"][perm], a["u"][perm], a["us"][perm], a["d"][perm],
                              a["ds"][perm])
         m.set_shared(a["sh_g"], a["sh_gs"], a["sh_u"], a["sh_us"], a["sh_d"], a["sh_ds"], a["sh_gate"])

@@ -144,7 +144,9 @@ __global__ void __launch_bounds__(G * G, 2) router_tile_kernel(const float *__re
         for (int i = 0; i < TT; ++i) xn[i] = *reinterpret_cast<const float4 *>(st + (tg + G * i) * LD);
 #pragma unroll
         for (int j = 0; j < RR; ++j) wn[j] = *reinterpret_cast<const float4 *>(st + (BT + rg + G * j) * LD);
-#pragma unroll 4
+        // fully unrolled over the chunk: the next four columns' operands (xn,
+        // wn) become renamed registers, not copies
+#pragma unroll
         for (int kk = 0; kk < KC; kk += 4) {
 #pragma unroll
             for (int i = 0; i < TT; ++i) xv[i] = xn[i];
@@ -282,13 +284,19 @@ __global__ void __launch_bounds__(SEL_WARPS * 32) router_select_kernel(const flo
         const int e = topk_idx[s];   // this thread's own write in select_token
         plan.slotrow[s] = (e >= plan.e_lo && e < plan.e_hi) ? atomicAdd(plan.counts + e, 1) : -1;
     }
-    // last-block handoff: every block's routing is visible to the block that counts last
-    __threadfence();
+    // last-block handoff.  The block barrier orders every thread's routing
+    // writes before thread 0's gpu-scope fence, which (fences are cumulative)
+    // orders them before its count; the block that counts last fences again
+    // before its threads read every block's writes.  One fence per block, not
+    // one per thread.
     __syncthreads();
-    if (threadIdx.x == 0) s_last = atomicAdd(plan.done, 1) == (int)gridDim.x - 1;
+    if (threadIdx.x == 0) {
+        __threadfence();
+        s_last = atomicAdd(plan.done, 1) == (int)gridDim.x - 1;
+        if (s_last) __threadfence();
+    }
     __syncthreads();
     if (!s_last) return;
-    __threadfence();
     omc_plan_block(plan, topk_idx, topk_w, err, reinterpret_cast<int *>(sbuf), true);
 }
 
