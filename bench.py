@@ -73,6 +73,7 @@ WORKLOADS = {
     "gemma_prefill": ("gemma", 2048), "gemma_decode": ("gemma", 1), "gemma_decode64": ("gemma", 64),
     "qwen_ep": ("qwen", 8192),
     "qwen_decode40": ("qwen", 1),
+    "qwen_decode64_tier": ("qwen", 64),
 }
 BIAS = "uniform"                 # qwen_ep: router bias, uniform (none) or zipf
 T_TOTAL = None                   # qwen_ep: tokens over all ranks
@@ -104,6 +105,8 @@ def set_workload(name, tokens=None, world=1, bias="uniform"):
         WORKLOAD = f"qwen_layer_ep_T{T_TOTAL}_{BIAS}"
     if name == "qwen_decode40":
         WORKLOAD = "qwen_40layers_decode_T1"
+    if name == "qwen_decode64_tier":
+        WORKLOAD = "qwen_layers_decode64_tiered"
     total = E * EXPERT_BYTES + (3 * D * IS + 4 * (2 * IS + D) if IS else 0)
     CONFIG = {"workload": WORKLOAD, "D": D, "I": I, "E": E, "k": K, "T": T,
               "weights": f"int8 per-row + f32 scales, N(0,0.02) seed {SEED_W}",
@@ -785,6 +788,115 @@ def run_layers(args):
     ob.shutdown()
 
 
+def run_tier_sweep(args):
+    """C4 on the configs[2] set: args.layers Qwen-shaped layers, each a tiered
+    store (omc_tier_enable) holding round(args.tier_frac * E) of its routed
+    experts in HBM and every expert's home in pinned host memory; one step =
+    one decode step of 64 sequences (T = 64) through every layer.  Routed
+    experts outside HBM cross the host link once per forward that routes them;
+    the hot-store policy (LFRU, include/tier.h) swaps one expert per forward
+    at most.  Layer l's expert e is seeded expert (e + 37 l) mod E, as in
+    qwen_decode40.  Two extra fully resident copies of layers 0 and 1 check
+    that the tiered forwards are bit-identical."""
+    import torch
+    rank, world, local = env_rank()
+    if world > 1:
+        raise SystemExit("--workload qwen_decode64_tier runs on one GPU")
+    dev = local
+    torch.cuda.set_device(dev)
+    import overhang_b200 as ob
+    NL = args.layers
+    ob.init(dev, 0)
+    pyoracle, L = make_layer()
+    a = L.arrays
+    slots = max(1, min(E, int(round(args.tier_frac * E))))
+    tiered = slots < E
+    t0 = time.perf_counter()
+    layers = []
+    routers = []
+
+    def build(lid, l, tier_slots):
+        perm = (np.arange(E) + 37 * l) % E
+        if len(routers) <= l:
+            routers.append(pyoracle.quantize_c(pyoracle.normal(SEED_W * 1000003 + 7 + 101 * l, (E, D), 0.02)))
+        rq, rs = routers[l]
+        m = ob.MoELayer(lid, ob.FAMILY_QWEN, D, I, E, K, rq, rs, 1, 1, IS)
+        if tier_slots:
+            m.tier_enable(tier_slots, 1, 0)
+        m.set_experts_packed(a["g"][perm], a["gs"][perm], a["u"][perm], a["us"][perm], a["d"][perm], a["ds"][perm])
+        m.set_shared(a["sh_g"], a["sh_gs"], a["sh_u"], a["sh_us"], a["sh_d"], a["sh_ds"], a["sh_gate"])
+        return m
+
+    for l in range(NL):
+        layers.append(build(l, l, slots if tiered else 0))
+    refs = [build(NL + l, l, 0) for l in range(min(2, NL))] if tiered else []
+    t_up = time.perf_counter() - t0
+    nbuf = 2
+    xs = [[torch.from_numpy(pyoracle.normal(SEED_X + 97 * l + i, (T, D))).cuda() for l in range(NL)]
+          for i in range(nbuf)]
+    out = torch.empty((T, D), dtype=torch.float32, device="cuda")
+    idx = torch.empty((T, K), dtype=torch.int32, device="cuda")
+    wts = torch.empty((T, K), dtype=torch.float32, device="cuda")
+    stream = torch.cuda.Stream(device=dev)
+    torch.cuda.set_stream(stream)
+    sptr = stream.cuda_stream
+
+    def step(i):
+        for l, m in enumerate(layers):
+            m.forward_dev(xs[i % nbuf][l].data_ptr(), T, out.data_ptr(), idx.data_ptr(), wts.data_ptr(), sptr)
+
+    # bit-identity of tiered forwards (layers 0 and 1) against their resident copies
+    identical = None
+    if refs:
+        identical = True
+        for l, r in enumerate(refs):
+            xh = xs[0][l].cpu().numpy()
+            o1, i1, _ = layers[l].forward(xh)
+            o2, i2, _ = r.forward(xh)
+            identical &= bool(np.array_equal(i1, i2) and np.array_equal(o1.view(np.uint32), o2.view(np.uint32)))
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    ob.set_profiling(True)
+    step(0)
+    torch.cuda.synchronize()
+    ob.set_profiling(False)
+    last_stages = dict(ob.stage_times())
+    miss0 = sum(m.tier_stats(slots)[5] for m in layers) if tiered else 0
+    swaps0 = sum(m.tier_stats(slots)[4] for m in layers) if tiered else 0
+    clk = ClockSampler(dev)
+    clk.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for i in range(args.steps):
+        step(i)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    clocks = clk.stop()
+    t_ms = e0.elapsed_time(e1)
+    misses = ((sum(m.tier_stats(slots)[5] for m in layers) - miss0) / args.steps) if tiered else 0.0
+    swaps = ((sum(m.tier_stats(slots)[4] for m in layers) - swaps0) / args.steps) if tiered else 0.0
+    step_s = t_ms / args.steps / 1e3
+    miss_bytes = misses * EXPERT_BYTES
+    line = {"metric": METRIC, "value": T * args.steps / (t_ms / 1e3), "unit": UNIT, "n_gpus": 1,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": t_ms / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16xint8->f32",
+            "data": "synthetic",
+            "config": dict(CONFIG, workload=WORKLOAD, layers=NL, sequences=T, hbm_expert_fraction=slots / E,
+                           hbm_slots_per_layer=slots, launch="stream", upload_s=round(t_up, 1),
+                           host_expert_bytes=(NL * E * EXPERT_BYTES if tiered else 0)),
+            "tier": {"misses_per_step": misses, "miss_bytes_per_step": miss_bytes, "swaps_per_step": swaps,
+                     "link_gbs_over_step": miss_bytes / step_s / 1e9,
+                     "link_roofline_gbs": 51.0,
+                     "step_ms_if_link_bound": miss_bytes / 51e9 * 1e3,
+                     "last_layer_stage_ms": last_stages,
+                     "bit_identical_to_resident_layers_0_1": identical},
+            "clocks": clocks}
+    print(json.dumps(line), flush=True)
+    ob.shutdown()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -799,6 +911,9 @@ def main():
     ap.add_argument("--workload", default=None, choices=sorted(WORKLOADS),
                     help="olmoe_prefill (BASELINE configs[1], the default line on one GPU), olmoe_decode, "
                          "qwen_prefill, qwen_decode, ...; qwen_ep (configs[3], the default on N>1 GPUs)")
+    ap.add_argument("--tier-frac", type=float, default=0.5,
+                    help="qwen_decode64_tier: fraction of each layer's experts kept in HBM (the rest in pinned "
+                         "host memory)")
     ap.add_argument("--ep-combine", default="ranksum", choices=["ranksum", "exact"],
                     help="N>1 expert parallel: results back as one row per (token, rank) summed there "
                          "(ranksum) or one row per slot summed at home (exact: bit-equal to one GPU)")
@@ -830,6 +945,8 @@ def main():
         run_reference(args)
     elif args.workload == "qwen_decode40":
         run_layers(args)
+    elif args.workload == "qwen_decode64_tier":
+        run_tier_sweep(args)
     else:
         run_ours(args)
 

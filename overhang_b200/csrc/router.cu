@@ -276,14 +276,26 @@ __global__ void __launch_bounds__(SEL_WARPS * 32) router_select_kernel(const flo
         select_token<SEL_MAXV>(logits, ldl, t, E, K, family, renorm, has_shared, pes, bias, topk_idx, topk_w, sg, err,
                                sbuf + wib * SEL_MAXV * 32);
     if (!do_plan) return;
-    // count the routed slots per expert here, one global atomic per slot:
-    // its rank is its row within the expert's group (arrival order; an
-    // expert's rows are independent, so the order changes no value)
-    if (t < T && (threadIdx.x & 31) < K) {
-        const int s = t * K + (threadIdx.x & 31);
-        const int e = topk_idx[s];   // this thread's own write in select_token
-        plan.slotrow[s] = (e >= plan.e_lo && e < plan.e_hi) ? atomicAdd(plan.counts + e, 1) : -1;
+    // count the routed slots per expert here: a slot's rank is its row within
+    // the expert's group (arrival order; an expert's rows are independent, so
+    // the order changes no value).  Ranks within the block come from
+    // shared-memory atomics, then one global atomic per (block, expert) adds
+    // the block's count: under skewed routing a hot expert's counter takes one
+    // atomic per block instead of one per token.
+    __shared__ int s_cnt[OMC_MAX_E], s_gbase[OMC_MAX_E];
+    for (int e = threadIdx.x; e < E; e += blockDim.x) s_cnt[e] = 0;
+    __syncthreads();
+    int my_e = -1, my_local = -1;
+    const bool has_slot = t < T && (threadIdx.x & 31) < K;
+    if (has_slot) {
+        my_e = topk_idx[t * K + (threadIdx.x & 31)];   // this thread's own write in select_token
+        if (my_e >= plan.e_lo && my_e < plan.e_hi) my_local = atomicAdd(&s_cnt[my_e], 1);
     }
+    __syncthreads();
+    for (int e = threadIdx.x; e < E; e += blockDim.x)
+        if (s_cnt[e]) s_gbase[e] = atomicAdd(plan.counts + e, s_cnt[e]);
+    __syncthreads();
+    if (has_slot) plan.slotrow[t * K + (threadIdx.x & 31)] = my_local >= 0 ? s_gbase[my_e] + my_local : -1;
     // last-block handoff.  The block barrier orders every thread's routing
     // writes before thread 0's gpu-scope fence, which (fences are cumulative)
     // orders them before its count; the block that counts last fences again
