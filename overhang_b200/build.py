@@ -84,7 +84,7 @@ def build(verbose: bool = False, force: bool = False) -> str:
             sys.stdout.write(o)
     if force or jobs or _newer(objs, LIB):
         tmp = LIB + ".tmp"
-        _run([NVCC] + GENCODE + ["-shared", "-o", tmp] + objs + ["-ldl", "-lpthread", "-lm", "-lcublas"],
+        _run([NVCC] + GENCODE + ["-shared", "-o", tmp] + objs + ["-ldl", "-lpthread", "-lm"],
              os.path.join(BUILD, "link.log"))
         os.replace(tmp, LIB)
     return LIB

@@ -112,6 +112,8 @@ struct GemmArgs {
                                // token s / K, choice s % K; s >= nrouted is token s - nrouted
     int ydirect;               // gemm2: 1 = write row slot of ypart ([slots][D]) instead of
                                // the [T][K+1][D] partials
+    int wf16;                  // gemm2: the weights are f16 tiles (omm_dense): one 128-row tile
+                               // of 64 f16 columns per 16 KB K block, copied to TMEM as they are
     const int *slot_tok;       // gemm1: token row of each slot (xh row), or NULL: derived
                                // from the slot as above
     int T, R;                  // tokens, operand rows
@@ -149,11 +151,17 @@ __device__ __forceinline__ float swiglu_f(int act, float g, float u) {
 
 
 // The 128-row weight blocks an item multiplies: phase 1 = gate tile mt and up
-// tile mt; phase 2 = down tiles 2*mt and 2*mt+1 (the second absent past D_rows).
+// tile mt; phase 2 = down tiles 2*mt and 2*mt+1 (the second absent past D_rows),
+// or with f16 weights the one tile mt.
 template <int PHASE>
-__device__ __forceinline__ int item_nmat(const omc_layer_dev &L, const WorkItem &it) {
+__device__ __forceinline__ int item_nmat(const GemmArgs &a, const WorkItem &it) {
     if (PHASE == 1) return 2;
-    return (2 * it.mt + 1) * OMC_TM < L.D_rows ? 2 : 1;
+    if (a.wf16) return 1;
+    return (2 * it.mt + 1) * OMC_TM < a.L.D_rows ? 2 : 1;
+}
+// first output row of tile `half` of a phase-2 item
+__device__ __forceinline__ int item_row0(const GemmArgs &a, const WorkItem &it, int half) {
+    return (a.wf16 ? it.mt : 2 * it.mt + half) * OMC_TM;
 }
 
 template <int PHASE>
@@ -168,7 +176,7 @@ struct Ctx {
         if (it.g < 0 || it.g > L.E || (it.g == L.E && !L.has_shared)) return false;
         if (it.n <= 0 || it.n > NMAX || (it.n & 15) || it.n0 < 0 || it.n0 + it.n > a.R || (it.n0 & 15)) return false;
         if (PHASE == 1) return it.mt >= 0 && it.mt * OMC_TM < (it.g == L.E ? L.Is_rows : L.I_rows);
-        return it.mt >= 0 && 2 * it.mt * OMC_TM < L.D_rows;
+        return it.mt >= 0 && (a.wf16 ? it.mt : 2 * it.mt) * OMC_TM < L.D_rows;
     }
     __device__ int nkb(const WorkItem &it) const {
         if (PHASE == 1) return a.L.D_pad / OMC_KB;
@@ -198,7 +206,7 @@ struct StageIter {
             return;
         }
         nkb = c.nkb(it);
-        nmat = item_nmat<PHASE>(c.a.L, it);
+        nmat = item_nmat<PHASE>(c.a, it);
         w = c.pair_base(it);
         n0 = it.n0;
         n = it.n;
@@ -339,7 +347,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_gemm_kernel(const GemmArgs a)
                 if (!wait_or_abort(&emptyI[si], ((i / SI) & 1) ^ 1, a.err, OMC_SITE_GEMM_PRODUCER, abort_flag))
                     break;
                 // the pair's K block is one contiguous 16 KiB (8 KiB when the pair has one tile)
-                const uint32_t bytes = (uint32_t)it.nmat * W_BYTES;
+                const uint32_t bytes = (PHASE == 2 && a.wf16 ? 2u : (uint32_t)it.nmat) * W_BYTES;
                 mbar_arrive_expect_tx(&fullI[si], bytes);
                 bulk_g2s_hint(smem + OFF_I8 + si * 2 * W_BYTES, it.w + (size_t)it.kb * OMC_PAIR_STRIDE, bytes,
                               &fullI[si], stream);
@@ -361,7 +369,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_gemm_kernel(const GemmArgs a)
             const WorkItem it = c.item(idx);
             if (!c.ok(it)) break;
             const int nkb = c.nkb(it);
-            const int nmat = item_nmat<PHASE>(L, it);
+            const int nmat = item_nmat<PHASE>(a, it);
             acc.begin(it.n);
             bool ok = true;
             for (int j = 0; j < acc.nslots && ok; ++j)
@@ -470,7 +478,21 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_gemm_kernel(const GemmArgs a)
             // both tiles of the pair, one after the other through the same registers:
             // 64 int8 of row r -> exact f16 -> TMEM columns 32*tile.. of stage st
             const uint8_t *m0 = smem + OFF_I8 + si * 2 * W_BYTES;
-            for (int tile = 0; tile < pr.nmat; ++tile) {   // warp-uniform
+            if (PHASE == 2 && a.wf16) {
+                // f16 weights: 8 chunks of 8 columns of row r, as they are
+                uint32_t v[32];
+#pragma unroll
+                for (int c8 = 0; c8 < 8; ++c8) {
+                    const uint4 hv = *reinterpret_cast<const uint4 *>(m0 + (c8 * 128 + r) * 16);
+                    v[4 * c8 + 0] = hv.x;
+                    v[4 * c8 + 1] = hv.y;
+                    v[4 * c8 + 2] = hv.z;
+                    v[4 * c8 + 3] = hv.w;
+                }
+                tmem_st_32x32b_x32(tmem + lane_bits + TCOL_A + (uint32_t)st * 64u, v);
+                tc_wait_st();
+            }
+            for (int tile = 0; tile < (PHASE == 2 && a.wf16 ? 0 : pr.nmat); ++tile) {   // warp-uniform
                 uint32_t v[32];
                 const uint8_t *m = m0 + tile * W_BYTES;
 #pragma unroll
@@ -521,8 +543,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_gemm_kernel(const GemmArgs a)
                     sc1 = P.us[f];
                 }
             } else {
-                const int d = (2 * it.mt + half) * OMC_TM + r;
-                if (half < item_nmat<PHASE>(L, it) && d < L.D) sc0 = P.ds[d];
+                const int d = item_row0(a, it, half) + r;
+                if (half < item_nmat<PHASE>(a, it) && d < L.D) sc0 = P.ds[d];
                 // per token row: its ypart row (token * (k+1) + choice, or the slot
                 // itself when ydirect; -1 padding) and weight
                 const int K = a.K;
@@ -597,8 +619,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_gemm_kernel(const GemmArgs a)
                     __syncwarp();
                 }
             } else {
-                if (half < item_nmat<PHASE>(L, it)) {
-                    const int d = (2 * it.mt + half) * OMC_TM + r;  // output row of this thread
+                if (half < item_nmat<PHASE>(a, it)) {
+                    const int d = item_row0(a, it, half) + r;       // output row of this thread
                     const uint32_t col = acc.col(half);
 #pragma unroll 1
                     for (int ch = 0; ch * 16 < it.n; ++ch) {
@@ -781,6 +803,7 @@ extern "C" int omc_launch_mma_ffn(const omc_layer_dev *L, const float *x, int T,
     ga.nrouted = T * L->k;
     ga.ydirect = 0;
     ga.slot_tok = nullptr;
+    ga.wf16 = 0;
     ga.T = T;
     ga.R = R;
     ga.err = ws->err;
@@ -880,6 +903,7 @@ extern "C" int omc_launch_mma_rows(const omc_layer_dev *L, const float *x, int R
     ga.nrouted = R;
     ga.ydirect = 1;
     ga.slot_tok = nullptr;
+    ga.wf16 = 0;
     ga.T = R;
     ga.R = ws->R_cap;
     ga.err = ws->err;
@@ -934,6 +958,7 @@ extern "C" int omc_launch_mma_slots(const omc_layer_dev *L, const uint16_t *xh, 
     ga.nrouted = nslots;
     ga.ydirect = 1;
     ga.slot_tok = slot_tok;
+    ga.wf16 = 0;
     ga.T = nslots;
     ga.R = ws->R_cap;
     ga.err = ws->err;
@@ -1029,6 +1054,92 @@ extern "C" int omc_launch_dense_i8(const omc_layer_dev *L, const float *x, int S
     ga.nrouted = S;
     ga.ydirect = 1;
     ga.slot_tok = nullptr;
+    ga.wf16 = 0;
+    ga.T = S;
+    ga.R = ws->R_cap;
+    ga.err = ws->err;
+    const int grid = g_num_sms > 0 ? g_num_sms : 148;
+    moe_gemm_kernel<2><<<grid, NTHREADS, SMEM_BYTES, s>>>(ga);
+    omc_g_launches += 2;
+    return cudaGetLastError() == cudaSuccess ? 0 : OMC_ECUDA;
+}
+
+// f16 weight tiles of a row-major f32 matrix W [N][K] (omm_dense): tile t
+// (rows 128t..128t+127), K block kb (64 columns) is 16 KB at
+// ((t * nkb + kb) * 16384); inside it, 8-column chunk c of row r sits at
+// (c * 128 + r) * 16, so a warp reading 32 consecutive rows' chunk reads 512
+// contiguous bytes.  Rounded to nearest; rows >= N and columns >= K are zero;
+// a value outside the f16 range is reported (OMC_DEVERR_RANGE).
+__global__ void __launch_bounds__(256) f16_tiles_kernel(const float *__restrict__ W, int N, int K, int nkb,
+                                                        long long nchunks, uint16_t *__restrict__ dst, int *err) {
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < nchunks;
+         i += (long long)gridDim.x * blockDim.x) {
+        // i = ((t * nkb + kb) * 8 + c) * 128 + r: consecutive threads write consecutive 16 B
+        const int r = (int)(i & 127), c = (int)((i >> 7) & 7);
+        const long long tk = i >> 10;
+        const int kb = (int)(tk % nkb), t = (int)(tk / nkb);
+        const int row = t * OMC_TM + r, k0 = kb * OMC_KB + c * 8;
+        uint4 o = make_uint4(0u, 0u, 0u, 0u);
+        if (row < N && k0 < K) {
+            const float4 a = *reinterpret_cast<const float4 *>(W + (size_t)row * K + k0);
+            const float4 b = *reinterpret_cast<const float4 *>(W + (size_t)row * K + k0 + 4);
+            if (omc_f16_outside(a.x) || omc_f16_outside(a.y) || omc_f16_outside(a.z) || omc_f16_outside(a.w) ||
+                omc_f16_outside(b.x) || omc_f16_outside(b.y) || omc_f16_outside(b.z) || omc_f16_outside(b.w))
+                omc_dev_error(err, OMC_DEVERR_RANGE, OMC_SITE_DISPATCH, row);
+            o.x = f32x2_to_f16x2_sat(a.x, a.y);
+            o.y = f32x2_to_f16x2_sat(a.z, a.w);
+            o.z = f32x2_to_f16x2_sat(b.x, b.y);
+            o.w = f32x2_to_f16x2_sat(b.z, b.w);
+        }
+        reinterpret_cast<uint4 *>(dst)[i] = o;
+    }
+}
+
+extern "C" size_t omc_f16_tiles_bytes(int N, int K) {
+    return (size_t)((N + OMC_TM - 1) / OMC_TM) * ((K + OMC_KB - 1) / OMC_KB) * 16384;
+}
+
+extern "C" int omc_launch_f16_tiles(const float *W, int N, int K, uint16_t *dst, int *err, cudaStream_t s) {
+    if (N <= 0 || K <= 0 || K % 8) return OMC_EINVAL;
+    const int nkb = (K + OMC_KB - 1) / OMC_KB;
+    const long long nchunks = (long long)omc_f16_tiles_bytes(N, K) / 16;
+    const int blocks = (int)((nchunks + 255) / 256 < 8192 ? (nchunks + 255) / 256 : 8192);
+    f16_tiles_kernel<<<blocks, 256, 0, s>>>(W, N, K, nkb, nchunks, dst, err);
+    omc_g_launches += 1;
+    return cudaGetLastError() == cudaSuccess ? 0 : OMC_ECUDA;
+}
+
+// y[S][N] = x[S][K] . W^T on the tensor cores with f16 weights (omm_dense):
+// L is a one-matrix layer (E = 1, D = N output rows, I = K) whose expert 0
+// has d = the f16 tiles (omc_launch_f16_tiles) and ds = N_pad ones; x is f32
+// [S][K] on the device (K % 8 == 0), rounded to f16 as the operand; the
+// products are summed in f32 (TMEM).  The workspace was sized for S rows.
+extern "C" int omc_launch_dense_f16(const omc_layer_dev *L, const float *x, int S, const omc_ws *ws, float *y,
+                                    cudaStream_t s) {
+    if (S <= 0) return 0;
+    if (gemm_setup()) return OMC_ECUDA;
+    const int Sp = (S + OMC_ROW_ALIGN - 1) / OMC_ROW_ALIGN * OMC_ROW_ALIGN;
+    if (Sp > ws->R_cap || (L->I % 8) || L->E != 1) return OMC_EINVAL;
+    const int ntiles = L->D_rows / OMC_TM;
+    const long long nck = (long long)Sp * (L->I_pad / 8);
+    const int blocks = (int)((nck + 255) / 256 < 2048 ? (nck + 255) / 256 : 2048);
+    dense_prep_kernel<<<blocks, 256, 0, s>>>(x, S, L->I, L->I_pad, Sp, ws->R_cap, ws->hp, ws->rowinfo, ws->roww,
+                                             reinterpret_cast<int4 *>(ws->work), ws->nwork, ntiles, ws->err);
+    GemmArgs ga;
+    ga.L = *L;
+    ga.work = reinterpret_cast<const int4 *>(ws->work);
+    ga.nwork = ws->nwork;
+    ga.act = ws->hp;
+    ga.xh = nullptr;
+    ga.hout = ws->hp;
+    ga.ypart = y;
+    ga.rowinfo = ws->rowinfo;
+    ga.roww = ws->roww;
+    ga.K = 1;
+    ga.nrouted = S;
+    ga.ydirect = 1;
+    ga.slot_tok = nullptr;
+    ga.wf16 = 1;
     ga.T = S;
     ga.R = ws->R_cap;
     ga.err = ws->err;

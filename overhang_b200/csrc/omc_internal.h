@@ -218,6 +218,12 @@ int omc_launch_ep_ranksum(const int32_t *meta, int Rr, int k, int P, const int *
 int omc_launch_ep_combine_ranksum(const float *ret, const int32_t *tok_pos, const int32_t *idx, const float *y_shared,
                                   const float *sg, int T, int D, int k, int ne, int P, int has_shared, float *out,
                                   cudaStream_t s);
+/* omm_dense on the tensor cores: f16 weight tiles of a row-major f32 [N][K]
+ * (K % 8 == 0; omc_f16_tiles_bytes bytes), and y[S][N] = x[S][K] . W^T with
+ * L a one-matrix layer whose expert 0 has d = those tiles, ds = ones */
+size_t omc_f16_tiles_bytes(int N, int K);
+int omc_launch_f16_tiles(const float *W, int N, int K, uint16_t *dst, int *err, cudaStream_t s);
+int omc_launch_dense_f16(const omc_layer_dev *L, const float *x, int S, const omc_ws *ws, float *y, cudaStream_t s);
 /* dst = f16(src), n % 8 == 0 */
 int omc_launch_f32_to_f16(const float *src, long long n, uint16_t *dst, cudaStream_t s);
 int omc_noalloc_setup(int device);

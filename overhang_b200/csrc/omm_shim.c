@@ -24,12 +24,11 @@
  * not serve (D or I not a multiple of 64, more than 1024 jobs).  gelu = 1 runs
  * the experts with gelu_tanh (engines/gemma.c:319-321), as Gemma's call does.
  * omm_dense_q runs the engine's int8 projections on the tensor-core GEMM,
- * omm_dense its f32 ones through a cached half copy and cuBLAS (below). */
+ * omm_dense its f32 ones through a cached half copy on the same GEMM (below). */
 #include <stdint.h>
 #include <stdlib.h>
 #include <string.h>
 
-#include <cublas_v2.h>
 #include <cuda_runtime.h>
 
 #include "om_metal.h"
@@ -344,18 +343,19 @@ int omm_dense_q(const int8_t *Wq, const float *scales, int N, int K, const float
 /* omm_dense (metal/om_metal.h:43-46): out[S,N] = x[S,K] . W^T with the
  * engine's resident f32 W (engines/olmoe.c:286-292 dense_mm).  As in the
  * reference backend, a half copy of W is made on first use and kept by
- * pointer; x is rounded to half too, the products are summed in f32
- * (cuBLAS GemmEx: a plain library GEMM, f16 inputs, f32 compute and output).
- * K % 8 == 0, else -3. */
+ * pointer (here as the tensor-core GEMM's 128-row f16 tiles); x is rounded to
+ * half too, and the products are summed in f32 by the library's own
+ * tcgen05 GEMM (omc_launch_dense_f16: the down GEMM reading f16 weights into
+ * tensor memory as they are).  K % 8 == 0, else -3. */
 typedef struct {
     const float *hw;
     int N, K;
-    uint16_t *dw;
+    uint16_t *dw;               /* f16 tiles */
+    float *ones;                /* [N_pad] row scales of 1 */
 } omm_fmat;
 
 static omm_fmat *g_fm;
 static int g_nfm, g_fmcap;
-static cublasHandle_t g_cublas;
 
 int omm_dense(const float *W, int N, int K, const float *x, int S, float *out) {
     if (!omm_init()) return -1;
@@ -363,14 +363,13 @@ int omm_dense(const float *W, int N, int K, const float *x, int S, float *out) {
     if (!W || !x || !out || N <= 0 || K <= 0 || K % 8) return -3;
     cudaSetDevice(G.device);
     cudaStream_t s = G.stream;
-    if (!g_cublas && cublasCreate(&g_cublas) != CUBLAS_STATUS_SUCCESS) return -1;
-    if (cublasSetStream(g_cublas, s) != CUBLAS_STATUS_SUCCESS) return -1;
     omm_fmat *m = NULL;
     for (int i = 0; i < g_nfm; ++i)
         if (g_fm[i].hw == W && g_fm[i].N == N && g_fm[i].K == K) {
             m = &g_fm[i];
             break;
         }
+    const int N_rows = omc_round_up(N, OMC_TM);
     if (!m) {
         if (g_nfm == g_fmcap) {
             const int nc = g_fmcap ? 2 * g_fmcap : 64;
@@ -383,14 +382,24 @@ int omm_dense(const float *W, int N, int K, const float *x, int S, float *out) {
         memset(m, 0, sizeof(*m));
         const size_t n = (size_t)N * K;
         float *stage = scratch(B_ROWS, n * 4);
-        if (!stage || cudaMalloc((void **)&m->dw, n * 2) != cudaSuccess) {
+        float *h1 = malloc(sizeof(float) * (size_t)N_rows);
+        if (!stage || !h1 || cudaMalloc((void **)&m->dw, omc_f16_tiles_bytes(N, K)) != cudaSuccess ||
+            cudaMalloc((void **)&m->ones, sizeof(float) * (size_t)N_rows) != cudaSuccess) {
             cudaGetLastError();
+            free(h1);
+            cudaFree(m->dw);
             return -1;
         }
-        if (cudaMemcpyAsync(stage, W, n * 4, cudaMemcpyHostToDevice, s) ||
-            omc_launch_f32_to_f16(stage, (long long)n, m->dw, s) || cudaStreamSynchronize(s)) {
+        for (int i = 0; i < N_rows; ++i) h1[i] = 1.f;
+        const int bad = cudaMemcpyAsync(stage, W, n * 4, cudaMemcpyHostToDevice, s) ||
+                        cudaMemcpyAsync(m->ones, h1, sizeof(float) * (size_t)N_rows, cudaMemcpyHostToDevice, s) ||
+                        omc_launch_f16_tiles(stage, N, K, m->dw, G.d_err, s) || cudaStreamSynchronize(s) ||
+                        omc_check_device_error();
+        free(h1);
+        if (bad) {
             cudaGetLastError();
             cudaFree(m->dw);
+            cudaFree(m->ones);
             return -1;
         }
         m->hw = W;
@@ -398,21 +407,36 @@ int omm_dense(const float *W, int N, int K, const float *x, int S, float *out) {
         m->K = K;
         ++g_nfm;
     }
+    omc_expert_ptrs tab[2];
+    memset(tab, 0, sizeof(tab));
+    tab[0].d = (const int8_t *)m->dw;
+    tab[0].ds = m->ones;
+    omc_layer TL;
+    memset(&TL, 0, sizeof(TL));
+    TL.desc.family = OMC_FAMILY_OLMOE;
+    TL.desc.D = N;
+    TL.desc.I = K;
+    TL.desc.E = 1;
+    TL.desc.k = 1;
+    TL.dev.family = OMC_FAMILY_OLMOE;
+    TL.dev.D = N;
+    TL.dev.I = K;
+    TL.dev.E = 1;
+    TL.dev.k = 1;
+    TL.dev.D_pad = omc_round_up(N, OMC_KB);
+    TL.dev.I_pad = omc_round_up(K, OMC_KB);
+    TL.dev.D_rows = N_rows;
+    TL.dev.I_rows = omc_round_up(K, OMC_TM);
+    TL.e0 = 0;
+    TL.ne = 1;
+    void *d_tab = scratch(B_TAB, sizeof(tab));
     float *d_x = scratch(B_X, (size_t)S * K * 4), *d_y = scratch(B_OUT, (size_t)S * N * 4);
-    uint16_t *d_xh = scratch(B_Y, (size_t)S * K * 2);
-    if (!d_x || !d_y || !d_xh) return -1;
-    const float alpha = 1.f, beta = 0.f;
-    if (cudaMemcpyAsync(d_x, x, (size_t)S * K * 4, cudaMemcpyHostToDevice, s) ||
-        omc_launch_f32_to_f16(d_x, (long long)S * K, d_xh, s)) {
-        cudaGetLastError();
-        return -1;
-    }
-    /* column-major view: C (N x S, ldc N) = W^T-view (W row-major [N][K] is
-     * K x N, lda K; op T) times x (row-major [S][K] is K x S, ldb K) */
-    if (cublasGemmEx(g_cublas, CUBLAS_OP_T, CUBLAS_OP_N, N, S, K, &alpha, m->dw, CUDA_R_16F, K, d_xh, CUDA_R_16F, K,
-                     &beta, d_y, CUDA_R_32F, N, CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT) != CUBLAS_STATUS_SUCCESS)
-        return -1;
-    if (cudaMemcpyAsync(out, d_y, (size_t)S * N * 4, cudaMemcpyDeviceToHost, s) || cudaStreamSynchronize(s)) {
+    if (!d_tab || !d_x || !d_y || omc_ws_ensure_rows(&TL, S)) return -1;
+    TL.dev.experts = (const omc_expert_ptrs *)d_tab;
+    if (cudaMemcpyAsync(d_tab, tab, sizeof(tab), cudaMemcpyHostToDevice, s) ||
+        cudaMemcpyAsync(d_x, x, (size_t)S * K * 4, cudaMemcpyHostToDevice, s) ||
+        omc_launch_dense_f16(&TL.dev, d_x, S, &G.ws, d_y, s) ||
+        cudaMemcpyAsync(out, d_y, (size_t)S * N * 4, cudaMemcpyDeviceToHost, s) || cudaStreamSynchronize(s)) {
         cudaGetLastError();
         return -1;
     }

@@ -53,8 +53,10 @@ def omc_lib():
 
 @pytest.fixture(scope="session")
 def gpu(omc_lib):
-    """Initialised library on cuda:0 (GPU tests only)."""
-    omc_lib.init(0, 48 << 30)
+    """Initialised library on cuda:0 (GPU tests only).  Every test uploads its
+    own layers and the slab only grows (it is a bump allocator), so the
+    session's budget covers the whole suite: 120 GiB of the B200's 180."""
+    omc_lib.init(0, 120 << 30)
     yield omc_lib
 
 
