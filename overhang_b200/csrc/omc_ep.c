@@ -171,7 +171,10 @@ static int wait_bounded(omc_ep_state *st, cudaEvent_t ev, const char *what) {
             return omc_fail(OMC_ETIMEOUT, "expert parallelism (%s): no progress within %d ms (a peer rank left?); "
                                           "communicator aborted", what, st->timeout_ms);
         }
-        if (it > 64) usleep(20);
+        /* the counts arrive within microseconds when every peer is there:
+         * spin for the first 2 ms (a sleep of any length costs tens of us on
+         * the forward's critical path), then poll every 50 us */
+        if (it > 64 && (now_s() - t0) > 2e-3) usleep(50);
     }
 }
 
