@@ -120,6 +120,28 @@ int omc_layer_gemma_norms(int layer, float eps, const float *router_scale, const
  * finite (OMC_EINVAL otherwise). */
 int omc_layer_router_bias(int layer, const float *bias);
 
+/* Router of the forwards with T >= 16 (OLMoE- and Qwen-family layers with
+ * D % 8 == 0; T < 16 and GEMMA layers always take the exact router).
+ *   mode 1, exact:   the reference's sequential fp32 chain (engines/olmoe.c:
+ *                    74-85, engines/qwen.c:116-121) for every (token, expert);
+ *                    topk_idx and topk_w bit-exact.
+ *   mode 2, bounded: approximate logits on the tensor cores with a proven
+ *                    error interval, the exact chain only for the experts
+ *                    whose interval can reach the top k and for the shared
+ *                    gate, and every row exact for the rare token whose
+ *                    selection order could depend on the rest.  topk_idx is
+ *                    bit-exact; topk_w is within a few ulps of the reference's
+ *                    (its softmax sum includes the approximated logits of
+ *                    experts that cannot be selected).
+ *   mode 0 (the default): bounded for layers of 128 experts or more, exact
+ *                    below (where the dense exact kernel moves less data). */
+int omc_set_router_exact(int mode);
+/* Counters of the library's last bounded-router pass: out[0] exact chains
+ * run, out[1] chains of retried tokens, out[2] tokens taken whole from the
+ * start (non-finite or out-of-range values, too many candidates), out[3]
+ * tokens retried.  Synchronises the library's stream. */
+int omc_router_stats(int *out);
+
 /* Upload routed expert e of a layer into the HBM slab (re-tiled for the
  * kernels).  Row-major int8 container tensors as written by the converters
  * (tools/convert_olmoe.py:93-99): g,u [I,D], d [D,I], per-row f32 scales

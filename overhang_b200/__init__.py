@@ -82,6 +82,8 @@ SIGNATURES = {
     "omc_stage_timer": (_i, [C.POINTER(C.c_float), C.POINTER(_i)]),
     "omc_launch_count": (C.c_longlong, [_i]),
     "omc_version": (C.c_char_p, []),
+    "omc_set_router_exact": (_i, [_i]),
+    "omc_router_stats": (_i, [C.POINTER(_i)]),
     "omm_init": (_i, []),
     "omm_alloc": (_vp, [_sz]),
     "omm_moe": (_i, [C.POINTER(OmmJob), _i, _vp, _i, _i, _i, _vp]),
@@ -94,6 +96,7 @@ SIGNATURES = {
     "omc_debug_set_path": (_i, [_i]),
     "omc_debug_plan_rows": (_i, [_i]),
     "omc_debug_router_tile": (_i, [_i, _i, _i]),
+    "omc_debug_rf_force_retry": (_i, [_i]),
     "omc_debug_ws_copy": (_i, [_i, _vp, _sz]),
     "omc_debug_gemma_prenorm": (_i, [_i, _vp, _i, _vp, _vp, _vp]),
     "omc_debug_container_read": (C.c_longlong, [C.c_char_p, C.c_char_p, _vp, C.c_longlong]),
@@ -114,6 +117,45 @@ ROUTER_TILES = [(16, 4, 4), (16, 2, 2), (16, 1, 1), (8, 1, 1)]
 def set_router_tile(g: int = 0, tt: int = 0, rr: int = 0) -> None:
     """Force the router logits tile (tests): one of ROUTER_TILES, or 0,0,0 = automatic."""
     check(lib().omc_debug_router_tile(g, tt, rr), "omc_debug_router_tile")
+
+ROUTER_AUTO, ROUTER_EXACT, ROUTER_BOUNDED = 0, 1, 2
+_router_mode = ROUTER_AUTO
+
+
+def set_router_mode(mode: int) -> None:
+    """Router of the forwards with T >= 16: ROUTER_AUTO (the default: the
+    bounded router -- indices bit-exact, weights within a few ulps of the
+    reference's -- for layers of >= 128 experts, the exact one below),
+    ROUTER_EXACT (the exact chain for every (token, expert): weights bit-exact
+    too) or ROUTER_BOUNDED (the bounded router whatever E)."""
+    global _router_mode
+    check(lib().omc_set_router_exact(mode), "omc_set_router_exact")
+    _router_mode = mode
+
+
+def set_router_exact(on: bool) -> None:
+    set_router_mode(ROUTER_EXACT if on else ROUTER_AUTO)
+
+
+def router_mode() -> int:
+    return _router_mode
+
+
+def router_exact() -> bool:
+    return _router_mode == ROUTER_EXACT
+
+
+def router_stats() -> dict:
+    """Counters of the last bounded-router pass (synchronises the library's stream)."""
+    out = (C.c_int * 4)()
+    check(lib().omc_router_stats(out), "omc_router_stats")
+    return {"jobs": out[0], "retry_jobs": out[1], "whole_tokens": out[2], "retried_tokens": out[3]}
+
+
+def debug_rf_force_retry(on: bool) -> None:
+    """Test hook: every token of a bounded pass is retried with every row exact."""
+    check(lib().omc_debug_rf_force_retry(1 if on else 0), "omc_debug_rf_force_retry")
+
 
 _lib = None
 

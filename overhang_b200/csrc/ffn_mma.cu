@@ -1149,6 +1149,40 @@ extern "C" int omc_launch_dense_f16(const omc_layer_dev *L, const float *x, int 
     return cudaGetLastError() == cudaSuccess ? 0 : OMC_ECUDA;
 }
 
+// y[r][n] = act row r . W row n (f16 products summed in f32 in tensor memory)
+// over an operand that a caller already laid out: act in the AOL layout with
+// R rows, rowinfo / roww / the work items / nwork written by that caller (the
+// bounded router's prep kernel).  Ld is a one-matrix layer (E = 1, D = the
+// output rows, I = K) whose expert 0 has d = f16 tiles and ds = ones.
+extern "C" int omc_launch_gemm_dense_op(const omc_layer_dev *Ld, const uint16_t *act, int R, const int *rowinfo,
+                                        const float *roww, const int *work, const int *nwork, float *y, int *err,
+                                        cudaStream_t s) {
+    if (gemm_setup()) return OMC_ECUDA;
+    if (Ld->E != 1 || (Ld->I % 8) || (R % OMC_ROW_ALIGN)) return OMC_EINVAL;
+    GemmArgs ga;
+    ga.L = *Ld;
+    ga.work = reinterpret_cast<const int4 *>(work);
+    ga.nwork = nwork;
+    ga.act = act;
+    ga.xh = nullptr;
+    ga.hout = nullptr;
+    ga.ypart = y;
+    ga.rowinfo = rowinfo;
+    ga.roww = roww;
+    ga.K = 1;
+    ga.nrouted = R;
+    ga.ydirect = 1;
+    ga.slot_tok = nullptr;
+    ga.wf16 = 1;
+    ga.T = R;
+    ga.R = R;
+    ga.err = err;
+    const int grid = g_num_sms > 0 ? g_num_sms : 148;
+    moe_gemm_kernel<2><<<grid, NTHREADS, SMEM_BYTES, s>>>(ga);
+    omc_g_launches += 1;
+    return cudaGetLastError() == cudaSuccess ? 0 : OMC_ECUDA;
+}
+
 // dst[i] = f16(src[i]) (round to nearest, saturated) for n a multiple of 8,
 // both 16-byte aligned.
 extern "C" int omc_launch_f32_to_f16(const float *src, long long n, uint16_t *dst, cudaStream_t s) {

@@ -175,6 +175,7 @@ void omc_shutdown(void) {
         omc_tier_free(&G.layers[i]);
         free(G.layers[i].h_experts);
         cudaFree(G.layers[i].d_experts_tab);
+        cudaFree(G.layers[i].rf_mem);
     }
     free(G.layers);
     G.layers = NULL;
@@ -209,6 +210,91 @@ static int staging_ensure(size_t n) {
     return OMC_OK;
 }
 
+/* The bounded router's per-layer data (router_fast.cu), one allocation: the
+ * f16 tiles of the router rows (int8 routers: their values, exact in f16;
+ * f32 routers: the f16 rounding of each row, then the f16 rounding of the
+ * remainder, as rows E..2E-1), row scales of 1, the one-matrix pointer table,
+ * and each row's ||w||_2 and ||w||_1 from the host rows in double, rounded
+ * up.  GEMMA layers (the router reads a normed input), D % 8 != 0, and f32
+ * routers with a value outside the f16 range keep the exact router only. */
+static int rf_setup(omc_layer *L, const void *router_w) {
+    omc_layer_dev *P = &L->dev;
+    const int E = P->E, D = P->D;
+    P->rf_tab = NULL;
+    P->rf_wn = NULL;
+    P->rf_q = NULL;
+    P->rf_rows = 0;
+    P->rf_split = 0;
+    if (P->family == OMC_FAMILY_GEMMA || D % 8 || E <= 0) return OMC_OK;
+    float *hn = malloc(sizeof(float) * 2 * (size_t)E);
+    if (!hn) return omc_fail(OMC_ENOMEM, "omc_layer_init: host alloc");
+    double amax = 0.0;
+    for (int e = 0; e < E; ++e) {
+        double s2 = 0.0, s1 = 0.0;
+        for (int i = 0; i < D; ++i) {
+            const double w = P->router_i8 ? (double)((const int8_t *)router_w)[(size_t)e * D + i]
+                                          : (double)((const float *)router_w)[(size_t)e * D + i];
+            s2 += w * w;
+            s1 += fabs(w);
+            if (!(fabs(w) <= amax)) amax = fabs(w);   /* NaN sticks */
+        }
+        hn[e] = nextafterf((float)(sqrt(s2) * (1.0 + 1e-9)), INFINITY);
+        hn[E + e] = nextafterf((float)(s1 * (1.0 + 1e-9)), INFINITY);
+    }
+    if (!P->router_i8 && !(amax < 65000.0)) {
+        free(hn);
+        return OMC_OK;
+    }
+    const int M = P->router_i8 ? E : 2 * E;
+    const int Mrows = omc_round_up(M, OMC_TM);
+    const size_t tb = (omc_f16_tiles_bytes(M, D) + 255) & ~(size_t)255;
+    const size_t ob = ((size_t)Mrows * 4 + 255) & ~(size_t)255;
+    const size_t nb = ((size_t)E * 2 * 4 + 255) & ~(size_t)255;
+    const size_t qb = P->router_i8 ? (((size_t)E * D + 255) & ~(size_t)255) : 0;
+    char *mem = NULL;
+    float *tmp = NULL, *ones = malloc(sizeof(float) * (size_t)Mrows);
+    int rc = OMC_OK;
+    if (!ones || cudaMalloc((void **)&mem, tb + ob + nb + 256 + qb) != cudaSuccess ||
+        (!P->router_i8 && cudaMalloc((void **)&tmp, (size_t)2 * E * D * 4) != cudaSuccess)) {
+        cudaGetLastError();
+        rc = omc_fail(OMC_ENOMEM, "omc_layer_init: bounded router tiles");
+        goto out;
+    }
+    for (int i = 0; i < Mrows; ++i) ones[i] = 1.f;
+    uint16_t *tiles = (uint16_t *)mem;
+    float *d_ones = (float *)(mem + tb), *d_wn = (float *)(mem + tb + ob);
+    omc_expert_ptrs tab;
+    memset(&tab, 0, sizeof(tab));
+    tab.d = (const int8_t *)tiles;
+    tab.ds = d_ones;
+    omc_expert_ptrs *d_tab = (omc_expert_ptrs *)(mem + tb + ob + nb);
+    if (!P->router_i8 && (rc = omc_launch_rf_split_rows(P->router, E, D, tmp, G.stream))) goto out;
+    if ((rc = omc_launch_f16_tiles(P->router_i8 ? P->router : tmp, M, D, tiles, G.d_err, G.stream))) goto out;
+    if (cudaMemcpyAsync(d_ones, ones, sizeof(float) * (size_t)Mrows, cudaMemcpyHostToDevice, G.stream) ||
+        cudaMemcpyAsync(d_wn, hn, sizeof(float) * 2 * (size_t)E, cudaMemcpyHostToDevice, G.stream) ||
+        cudaMemcpyAsync(d_tab, &tab, sizeof(tab), cudaMemcpyHostToDevice, G.stream) ||
+        (qb && cudaMemcpyAsync(mem + tb + ob + nb + 256, router_w, (size_t)E * D, cudaMemcpyHostToDevice, G.stream)) ||
+        cudaStreamSynchronize(G.stream)) {
+        cudaGetLastError();
+        rc = omc_fail(OMC_ECUDA, "omc_layer_init: bounded router upload");
+        goto out;
+    }
+    if ((rc = omc_check_device_error())) goto out;
+    L->rf_mem = mem;
+    mem = NULL;
+    P->rf_tab = d_tab;
+    P->rf_wn = d_wn;
+    P->rf_rows = M;
+    P->rf_split = P->router_i8 ? 0 : 1;
+    P->rf_q = qb ? (const int8_t *)((char *)L->rf_mem + tb + ob + nb + 256) : NULL;
+out:
+    cudaFree(mem);
+    cudaFree(tmp);
+    free(ones);
+    free(hn);
+    return rc;
+}
+
 int omc_layer_init(int layer, const omc_moe_desc *d, const void *router_w, const float *router_s) {
     if (!G.init) return omc_fail(OMC_ENOINIT, "omc_layer_init: omc_init not called");
     if (layer < 0 || layer > 4096 || !d || !router_w) return omc_fail(OMC_EINVAL, "omc_layer_init: bad arguments");
@@ -237,6 +323,7 @@ int omc_layer_init(int layer, const omc_moe_desc *d, const void *router_w, const
         omc_tier_free(L);
         free(L->h_experts);
         cudaFree(L->d_experts_tab);
+        cudaFree(L->rf_mem);
         /* slab space of a re-initialised layer is not reclaimed (bump allocator) */
     }
     memset(L, 0, sizeof(*L));
@@ -282,6 +369,10 @@ int omc_layer_init(int layer, const omc_moe_desc *d, const void *router_w, const
         CK(cudaMemcpyAsync(router, router_w, rbytes, cudaMemcpyHostToDevice, G.stream));
     }
     P->router = router;
+    {
+        int rc = rf_setup(L, router_w);
+        if (rc) return rc;
+    }
     L->h_experts = calloc((size_t)d->E + 1, sizeof(omc_expert_ptrs));
     L->have = calloc((size_t)d->E + 1, 1);
     if (!L->h_experts || !L->have) return omc_fail(OMC_ENOMEM, "omc_layer_init: host alloc");
@@ -605,10 +696,65 @@ static int ws_ensure_in(const omc_layer *L, size_t Tz, size_t nslots, size_t nsh
     return OMC_OK;
 }
 
+/* The bounded router's buffers in the library's own workspace (the forward
+ * entries' prefill calls): the split operand (2T rows), the products, the row
+ * map and work items, the per-token state and two job lists of
+ * T * roundup(E + 1, 4) chains each (every token taken whole, the bound). */
+static int ws_ensure_rf(const omc_layer *L, int T) {
+    const omc_layer_dev *P = &L->dev;
+    if (!P->rf_tab || T < OMC_RF_TMIN || omc_router_exact == 1 || (omc_router_exact == 0 && P->E < OMC_RF_EMIN))
+        return OMC_OK;
+    const size_t R = (size_t)omc_round_up(2 * T, 128);
+    const size_t nitems = R / 128 * (size_t)((P->rf_rows + OMC_TM - 1) / OMC_TM);
+    const size_t jcap = (size_t)T * (size_t)((P->E + 4) & ~3);
+    const size_t nseg = (size_t)(P->D_pad + 255) / 256;
+    const size_t misc = R * 2 + nitems * 4 + 16 + (size_t)T * 4 + (size_t)T * nseg * 2;   /* ints */
+    int rc;
+    omc_ws_ptrs *W = &G.ws_ptrs;
+    size_t *bytes = G.ws_bytes;
+    if ((rc = ws_buf_in(bytes, 16, (void **)&W->rf_act, (size_t)P->D_pad * R * 2))) return rc;
+    if ((rc = ws_buf_in(bytes, 17, (void **)&W->rf_y, R * (size_t)P->rf_rows * 4))) return rc;
+    if ((rc = ws_buf_in(bytes, 18, (void **)&W->rf_misc, misc * 4))) return rc;
+    if ((rc = ws_buf_in(bytes, 19, (void **)&W->rf_jobs, jcap * 2 * 8))) return rc;
+    omc_ws *ws = &G.ws;
+    ws->rf_R = (int)R;
+    ws->rf_act = W->rf_act;
+    ws->rf_y = W->rf_y;
+    ws->rf_rowinfo = W->rf_misc;
+    ws->rf_roww = (float *)(W->rf_misc + R);
+    ws->rf_work = W->rf_misc + 2 * R;
+    /* every region starts on a multiple of 4 ints: rf_work and rf_tok are
+     * read and written as int4 */
+    ws->rf_ctl = W->rf_misc + 2 * R + nitems * 4;
+    ws->rf_tok = ws->rf_ctl + 16;
+    ws->rf_xn = (float *)(ws->rf_tok + (size_t)T * 4);
+    ws->rf_jobs = W->rf_jobs;
+    ws->rf_jobs2 = W->rf_jobs + jcap * 2;
+    ws->rf_jcap = (int)jcap;
+    return OMC_OK;
+}
+
+/* Counters of the last bounded-router pass on the library's workspace:
+ * out[0] chain jobs, out[1] retry jobs, out[2] tokens taken whole from the
+ * start, out[3] tokens retried (synchronises the library's stream). */
+int omc_router_stats(int *out) {
+    if (!G.init) return omc_fail(OMC_ENOINIT, "omc_router_stats: omc_init not called");
+    if (!out) return omc_fail(OMC_EINVAL, "omc_router_stats: null pointer");
+    memset(out, 0, sizeof(int) * 4);
+    if (!G.ws.rf_ctl) return OMC_OK;
+    CK(cudaStreamSynchronize(G.stream));
+    CK(cudaMemcpy(out, G.ws.rf_ctl + 4, sizeof(int) * 4, cudaMemcpyDeviceToHost));
+    return OMC_OK;
+}
+
 int omc_ws_ensure(const omc_layer *L, int T, int host_io) {
     const size_t Tz = (size_t)T;
-    return ws_ensure_in(L, Tz, Tz * (size_t)L->dev.k, L->dev.has_shared ? Tz : 0, host_io, &G.ws, &G.ws_ptrs,
-                        G.ws_bytes);
+    int rc = ws_ensure_in(L, Tz, Tz * (size_t)L->dev.k, L->dev.has_shared ? Tz : 0, host_io, &G.ws, &G.ws_ptrs,
+                          G.ws_bytes);
+    if (rc) return rc;
+    /* buffers grow only: the pointers set for a larger T serve this one, but
+     * rf_R and the job capacity are per call */
+    return ws_ensure_rf(L, T);
 }
 
 int omc_ws_ensure_rows(const omc_layer *L, int rows) {

@@ -24,6 +24,7 @@ typedef struct {
     int e0, ne;                     /* experts owned by this rank (EP)      */
     int gemma_ready;                /* GEMMA: omc_layer_gemma_norms called  */
     void *tier;                     /* tiered expert store (omc_tier.c)     */
+    void *rf_mem;                   /* bounded router's tiles, table, norms */
 } omc_layer;
 
 typedef struct {
@@ -35,6 +36,9 @@ typedef struct {
     float *ypart, *hbuf;
     int *slotrow;
     float *xg_r, *xg_e;
+    uint16_t *rf_act;               /* bounded router (allocated by omc_ws_ensure) */
+    float *rf_y;
+    int *rf_misc, *rf_jobs;
 } omc_ws_ptrs;
 
 typedef struct {
@@ -54,7 +58,7 @@ typedef struct {
     /* workspace */
     omc_ws ws;
     omc_ws_ptrs ws_ptrs;
-    size_t ws_bytes[16];
+    size_t ws_bytes[24];
     /* profiling */
     int profiling, prof_valid, prof_nev;
     cudaEvent_t ev[OMC_NSTAGE_EV];
@@ -110,6 +114,7 @@ int omc_debug_expf(const float *x, float *y, long long n);
 int omc_debug_set_path(int path);
 int omc_debug_plan_rows(int rows);
 int omc_debug_router_tile(int g, int tt, int rr);
+int omc_debug_rf_force_retry(int on);
 int omc_debug_ws_copy(int which, void *dst, size_t bytes);
 int omc_debug_gemma_prenorm(int layer, const float *x, int T, float *xr, float *xe, float *r);
 long long omc_debug_container_read(const char *snapshot, const char *name, void *dst, long long cap);

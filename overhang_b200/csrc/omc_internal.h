@@ -106,6 +106,15 @@ typedef struct {
     const float *g_en;            /* [D] expert-input norm weight, NULL = ones      */
     const float *g_pes;           /* [E] per_expert_scale                           */
     const float *rbias;           /* [E] added to every router logit, or NULL       */
+    /* bounded router (router_fast.cu; rf_tab NULL = exact router only): f16
+     * tiles of the router rows as a one-matrix layer (rf_tab[0].d, .ds = ones),
+     * rf_rows = E (int8 router: its values are exact in f16) or 2E (f32
+     * router: the f16 rounding of each row, then the f16 rounding of the
+     * remainder); rf_wn = [E] ||w_e||_2 then [E] ||w_e||_1, rounded up */
+    const omc_expert_ptrs *rf_tab;
+    int rf_rows, rf_split;
+    const float *rf_wn;
+    const int8_t *rf_q;           /* int8 routers: the router's int8 values [E][D] (chain staging) */
 } omc_layer_dev;
 
 #define OMC_NMAX 128              /* token rows per grouped-GEMM work item (MMA N) */
@@ -154,6 +163,20 @@ typedef struct {
     float *hbuf;                  /* [T*k + T][Imax_pad] (GEMV path)      */
     float *xg_r, *xg_e;           /* GEMMA: [T][D] router and expert inputs */
     int *err;                     /* [4] device error word                */
+    /* bounded router (router_fast.cu), NULL until a forward takes it */
+    int rf_R;                     /* operand rows (>= 2T, a multiple of 128) */
+    uint16_t *rf_act;             /* AOL f16 [D_pad/64][rf_R][64]: x_hi rows, then x_lo rows */
+    float *rf_y;                  /* [2T][rf_rows] products of the row parts */
+    int *rf_rowinfo;              /* [rf_R] identity rows (-1 padding) */
+    float *rf_roww;               /* [rf_R] ones */
+    int *rf_work;                 /* GEMM work items (int4) */
+    int *rf_ctl;                  /* [16]: [0..3] GEMM nwork, [4] jobs, [5] retry jobs,
+                                     [6] tokens taken whole from the start, [7] retried tokens */
+    float *rf_xn;                 /* [T][D_pad/256][2] per 256-column segment: sum x^2, sum |x| (rounded up) */
+    int *rf_tok;                  /* [T][4] first job, groups of 4, groups done, whole */
+    int *rf_jobs;                 /* [cap][2] (token, row) chains; row -1 = padding */
+    int *rf_jobs2;                /* [cap][2] retry chains */
+    int rf_jcap;                  /* capacity of each job list */
 } omc_ws;
 
 /* ---- launchers (CUDA files), all enqueue on `s` ---------------------- */
@@ -224,6 +247,25 @@ int omc_launch_ep_combine_ranksum(const float *ret, const int32_t *tok_pos, cons
 size_t omc_f16_tiles_bytes(int N, int K);
 int omc_launch_f16_tiles(const float *W, int N, int K, uint16_t *dst, int *err, cudaStream_t s);
 int omc_launch_dense_f16(const omc_layer_dev *L, const float *x, int S, const omc_ws *ws, float *y, cudaStream_t s);
+/* bounded router: per-layer tiles and norms (host side, at omc_layer_init),
+ * the GEMM over a prepared operand (ffn_mma.cu), and the forward's launches */
+int omc_launch_rf_split_rows(const float *W, int E, int D, float *dst, cudaStream_t s);
+int omc_launch_gemm_dense_op(const omc_layer_dev *Ld, const uint16_t *act, int R, const int *rowinfo,
+                             const float *roww, const int *work, const int *nwork, float *y, int *err,
+                             cudaStream_t s);
+int omc_rf_eligible(const omc_layer_dev *L, int T, const omc_ws *ws);
+int omc_launch_router_fast(const omc_layer_dev *L, const float *x, int T, const omc_ws *ws, uint16_t *xh,
+                           cudaStream_t s);
+/* smallest T, and by default the smallest E, that take the bounded router
+ * (below: the exact router).  Under 128 experts the dense exact kernel, whose
+ * register tiles share every staged operand, moves less data per routed
+ * token than the candidates' chains, each with its own router row. */
+#define OMC_RF_TMIN 16
+#define OMC_RF_EMIN 128
+/* router mode (omc_set_router_exact): 0 auto, 1 exact, 2 bounded */
+extern int omc_router_exact;
+/* test hook: 1 = every token of a bounded pass is retried whole */
+extern int omc_rf_force_retry;
 /* dst = f16(src), n % 8 == 0 */
 int omc_launch_f32_to_f16(const float *src, long long n, uint16_t *dst, cudaStream_t s);
 int omc_noalloc_setup(int device);

@@ -414,6 +414,10 @@ extern "C" int omc_launch_router(const omc_layer_dev *L, const float *x, int T, 
         }
         router_logits_small_kernel<<<(nrows + RS_ROWS - 1) / RS_ROWS, 256, small_smem, s>>>(
             x, T, L->D, L->router, L->router_i8 ? L->router_s : nullptr, L->E, L->sh_gate, nrows, ws->logits, ldl);
+    } else if (omc_rf_eligible(L, T, ws)) {
+        // the bounded router: exact chains only where the routing needs them
+        const int rc = omc_launch_router_fast(L, x, T, ws, plan ? ws->xh : nullptr, s);
+        if (rc) return rc;
     } else {
         // GEMMA's expert operand is not the router's input: prenorm writes it
         const int rc = launch_logits(L, x, T, nrows, ws->logits, ldl,

@@ -1,0 +1,736 @@
+// router_fast.cu -- the bounded router: the reference's routing (indices bit for
+// bit) without running the exact fp32 chain for every (token, expert).
+//
+// The exact router (router.cu) runs one sequential fp32 chain of D separately
+// rounded products and sums per (token, expert) -- the reference's matmul /
+// matmul_q order (engines/olmoe.c:74-85, engines/qwen.c:116-121).  That is
+// T*E*D dependent CUDA-core steps: at T = 8192 on a 256-expert router it
+// costs as much as the expert GEMMs.  Routing only needs the exact value of
+// the experts that can be selected, so the bounded router
+//
+//   1. prep   splits each token row into f16 parts, x = x_hi + x_lo + r with
+//             |r| <= 2^-22|x| + 2^-24, writes them as the rows of a GEMM
+//             operand (x_hi rows, then x_lo rows), writes x_hi as the expert
+//             GEMMs' f16 token operand, and ||x||_2, ||x||_1 rounded up;
+//   2. GEMM   on the tensor cores (the library's grouped GEMM, f16 weight
+//             tiles in tensor memory): the router rows as f16 (int8 routers
+//             are exact in f16; an f32 router contributes its f16 rounding and
+//             the f16 rounding of the remainder as two row sets), every
+//             product part of every (token, row) summed in f32;
+//   3. cand   per token: a_e = the sum of the parts, an interval that provably
+//             holds the exact chain's logit, and the candidates -- every
+//             expert whose interval reaches the k-th largest lower end (less
+//             a margin that keeps the non-candidates' probabilities strictly
+//             below the k-th).  Approximate logits go to the logits rows; the
+//             candidates (and the shared-gate row) become chain jobs;
+//   4. chain  the exact chain of every job, written over the approximation,
+//             then a check per token: candidates whose exp values (computed as
+//             the select kernel computes them) lie within 2^-21 of each other
+//             but differ, or a k-th value below 2^-100, could order
+//             differently under the approximate softmax sum, and the token is
+//             retried with every row exact (5.);
+//   5. chain  the retried tokens' remaining rows.
+// The select kernel (router.cu) then routes from the logits rows as before.
+// Non-candidates only enter through the softmax sum, so the routing weights
+// agree with the reference's within a few ulps, and the indices exactly.
+//
+// The interval (per token t, expert e, in the chain's units before the row
+// scale):  |a_e - c_e| <= coef * ||x_t||_2 ||w_e||_2 + 2^-23 (||w_e||_1 +
+// split * ||x_t||_1),  c_e the exact chain, where coef (host, rf_coef) adds
+//   gamma_D = D u/(1 - D u), u = 2^-24: sequential dot product of D separately
+//             rounded products vs the real value (Higham, Accuracy and
+//             Stability of Numerical Algorithms, 2nd ed., eq. 3.5);
+//   2^-21:    the f16 split of x (and w) against the real products;
+//   17 * 2^-23 * (D_pad/16 + 1) * 1.003: the tensor-core f32 accumulation.
+//             Products of f16 operands are exact in f32; each K=16 MMA step
+//             is taken to add its 16 products and the accumulator with an
+//             error below 17 units of 2^-23 of (|acc| + sum|p|): a truncating
+//             aligned adder loses less than one unit in the last place of the
+//             largest term per addend, a serial one rounds 16 times.  This is
+//             a model of the hardware, generous against the published
+//             measurements of NVIDIA tensor-core accumulation (Fasi, Higham,
+//             Mikaitis, Pranesh, PeerJ CS 7:e330, 2021);
+//   4u:       the three f32 adds of the parts.
+// Sum |x_d||w_d| <= ||x||_2 ||w||_2 (Cauchy-Schwarz).  The row scale and the
+// router bias are applied to the interval ends with directed rounding.
+#include <math.h>
+#include <string.h>
+
+#include "omc_common.cuh"
+
+namespace {
+
+constexpr int RF_CAPC = 28;          // candidates beyond this: the token is taken whole from the start
+
+__device__ __forceinline__ void rf_cp16(void *smem_dst, const void *gsrc, bool valid) {
+    const uint32_t d = smem_u32(smem_dst);
+    const int n = valid ? 16 : 0;   // 0 source bytes: zero fill
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(d), "l"(gsrc), "r"(n) : "memory");
+}
+__device__ __forceinline__ void rf_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void rf_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+// f16 split of two values: hi = RN_f16(v) (saturated), lo = RN_f16(v - hi).
+// v - f32(hi) is exact in f32 (hi is within half an f16 unit of v).
+__device__ __forceinline__ void rf_split2(float a, float b, uint32_t &hi, uint32_t &lo) {
+    hi = f32x2_to_f16x2_sat(a, b);
+    const __half2 h = *reinterpret_cast<const __half2 *>(&hi);
+    const float2 hf = __half22float2(h);
+    lo = f32x2_to_f16x2_sat(a - hf.x, b - hf.y);
+}
+
+// rows 0..T-1 of the operand: x_hi; rows T..2T-1: x_lo (AOL layout: element
+// (r, k) at (k/64)*R*128 + r*128 + ((k%64)/8 ^ (r&7))*16 + (k%8)*2); xh row t
+// = x_hi (when xh); xn[t][seg] = (sum x^2, sum |x|) of each 256-column
+// segment, rounded up.  Block 0 also
+// writes the identity row map, the GEMM's work items over the Sp operand
+// rows, and zeroes the job counters.
+__global__ void __launch_bounds__(256) rf_prep_kernel(const float *__restrict__ x, int T, int D, int D_pad, int R,
+                                                      uint16_t *__restrict__ act, uint16_t *__restrict__ xh,
+                                                      float *__restrict__ xn, int *__restrict__ rowinfo,
+                                                      float *__restrict__ roww, int4 *__restrict__ work,
+                                                      int *__restrict__ ctl, int ntiles, int *err) {
+    const int tid = blockIdx.x * blockDim.x + threadIdx.x, nthr = gridDim.x * blockDim.x;
+    const int Sp = (2 * T + OMC_ROW_ALIGN - 1) / OMC_ROW_ALIGN * OMC_ROW_ALIGN;
+    for (int r = tid; r < R; r += nthr) {
+        rowinfo[r] = r < 2 * T ? r : -1;
+        roww[r] = 1.f;
+    }
+    if (blockIdx.x == 0) {
+        const int nch = (Sp + OMC_NMAX - 1) / OMC_NMAX;
+        for (int j = threadIdx.x; j < nch * ntiles; j += blockDim.x) {
+            const int ch = j / ntiles, p = j - ch * ntiles, n0 = ch * OMC_NMAX;
+            work[j] = make_int4(0, p, n0, min(OMC_NMAX, Sp - n0));
+        }
+        if (threadIdx.x == 0) {
+            ctl[0] = 0;
+            ctl[1] = nch * ntiles;
+            ctl[4] = ctl[5] = ctl[6] = ctl[7] = 0;
+        }
+    }
+    // one warp per (token, 256-column segment); xn holds each segment's sums
+    const int lane = threadIdx.x & 31;
+    const int nseg = (D_pad + 255) / 256;
+    for (int w = tid >> 5; w < T * nseg; w += nthr >> 5) {
+        const int t = w / nseg, seg = w - t * nseg;
+        const int k0 = seg * 256 + lane * 8;
+        const float *xr = x + (size_t)t * D;
+        float s2 = 0.f, s1 = 0.f;
+        bool outside = false;
+        if (k0 < D_pad) {
+            float v[8];
+            if (k0 < D) {
+                const float4 a = *reinterpret_cast<const float4 *>(xr + k0);
+                const float4 b = *reinterpret_cast<const float4 *>(xr + k0 + 4);
+                v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+                v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+            } else {
+#pragma unroll
+                for (int q = 0; q < 8; ++q) v[q] = 0.f;
+            }
+            uint4 hi, lo;
+            rf_split2(v[0], v[1], hi.x, lo.x);
+            rf_split2(v[2], v[3], hi.y, lo.y);
+            rf_split2(v[4], v[5], hi.z, lo.z);
+            rf_split2(v[6], v[7], hi.w, lo.w);
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+                outside |= omc_f16_outside(v[q]);
+                s2 = __fmaf_ru(v[q], v[q], s2);
+                s1 = __fadd_ru(s1, fabsf(v[q]));
+            }
+            const int kb = k0 >> 6, c = (k0 & 63) >> 3;
+            uint8_t *base = reinterpret_cast<uint8_t *>(act) + (size_t)kb * R * 128;
+            *reinterpret_cast<uint4 *>(base + (size_t)t * 128 + ((c ^ (t & 7)) << 4)) = hi;
+            *reinterpret_cast<uint4 *>(base + (size_t)(T + t) * 128 + ((c ^ ((T + t) & 7)) << 4)) = lo;
+            if (xh && k0 < D) *reinterpret_cast<uint4 *>(xh + (size_t)t * D + k0) = hi;
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            s2 = __fadd_ru(s2, __shfl_xor_sync(0xffffffffu, s2, o));
+            s1 = __fadd_ru(s1, __shfl_xor_sync(0xffffffffu, s1, o));
+        }
+        // a value outside the f16 range (NaN too) saturates x_hi: the
+        // segment's sums are made infinite, so the candidate pass takes the
+        // token whole (every row exact).  It is an error only where x_hi is
+        // the expert GEMMs' operand (xh): the host then redoes the forward on
+        // the f32 path.
+        const bool out_any = __any_sync(0xffffffffu, outside);
+        if (lane == 0) {
+            xn[2 * w] = out_any ? INFINITY : s2;
+            xn[2 * w + 1] = out_any ? INFINITY : s1;
+            if (out_any && xh) omc_dev_error(err, OMC_DEVERR_RANGE, OMC_SITE_ROUTER, t);
+        }
+    }
+}
+
+// float -> unsigned key in the float order (NaN excluded by the caller)
+__device__ __forceinline__ uint32_t rf_ord(float f) {
+    const uint32_t b = __float_as_uint(f);
+    return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+__device__ __forceinline__ float rf_unord(uint32_t k) {
+    return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
+}
+
+// ---- candidates of one token (one warp) -------------------------------------
+// a_e = the sum of the GEMM's product parts; the interval [lo_e, hi_e] holds
+// the exact chain's logit (row scale and bias applied with directed rounding);
+// the candidates are the experts with hi_e >= (k-th largest lo) - mu.  Writes
+// every approximate logit (RN(a_e * s_e)) to the token's logits row and the
+// candidates, ascending, to cand[0..nc).  Returns nc, or -1 when the token is
+// taken whole (a non-finite or huge value, more than RF_CAPC candidates, or a
+// k-th value that may underflow the softmax).
+template <int MAXV>
+__device__ __forceinline__ int rf_token_candidates(const float *__restrict__ y, int M, int T, int t, int E, int K,
+                                                   int split, const float *__restrict__ Ws,
+                                                   const float *__restrict__ bias, const float *__restrict__ wn,
+                                                   const float *__restrict__ xn, int nseg, float coef,
+                                                   float *__restrict__ lrow, int16_t *cand) {
+    const int lane = threadIdx.x & 31;
+    // ||x||_2 and ||x||_1 from the segments' sums, rounded up
+    float s2 = lane < nseg ? xn[2 * (t * nseg + lane)] : 0.f, s1 = lane < nseg ? xn[2 * (t * nseg + lane) + 1] : 0.f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        s2 = __fadd_ru(s2, __shfl_xor_sync(0xffffffffu, s2, o));
+        s1 = __fadd_ru(s1, __shfl_xor_sync(0xffffffffu, s1, o));
+    }
+    const float x2 = __fsqrt_ru(s2), x1 = split ? s1 : 0.f;
+    const float *y0 = y + (size_t)t * M, *y1 = y + (size_t)(T + t) * M;
+    float hi[MAXV], lo[MAXV];
+    bool bad = false;
+#pragma unroll
+    for (int j = 0; j < MAXV; ++j) {
+        const int e = lane + 32 * j;
+        hi[j] = -INFINITY;
+        lo[j] = -INFINITY;
+        if (e >= E) continue;
+        float a = __fadd_rn(y0[e], y1[e]);
+        if (split) a = __fadd_rn(__fadd_rn(a, y0[E + e]), y1[E + e]);
+        const float B = __fadd_ru(__fmul_ru(coef, __fmul_ru(x2, wn[e])),
+                                  __fmul_ru(1.1920928955078125e-7f, __fadd_ru(wn[E + e], x1)));
+        const float cl = __fsub_rd(a, B), ch = __fadd_ru(a, B);
+        float l1 = cl, h1 = ch, ap = a;
+        if (Ws) {
+            const float s = Ws[e];
+            l1 = s >= 0.f ? __fmul_rd(cl, s) : __fmul_rd(ch, s);
+            h1 = s >= 0.f ? __fmul_ru(ch, s) : __fmul_ru(cl, s);
+            ap = __fmul_rn(a, s);
+        }
+        if (bias) {
+            const float b = bias[e];
+            l1 = __fadd_rd(l1, b);
+            h1 = __fadd_ru(h1, b);
+        }
+        lo[j] = l1;
+        hi[j] = h1;
+        bad |= !(fabsf(h1) < 1e30f) || !(fabsf(l1) < 1e30f) || !isfinite(ap);
+        lrow[e] = ap;
+    }
+    if (__any_sync(0xffffffffu, bad)) return -1;
+    // the k-th largest lower end: k passes of warp argmax with removal
+    uint32_t key[MAXV];
+#pragma unroll
+    for (int j = 0; j < MAXV; ++j) key[j] = lane + 32 * j < E ? rf_ord(lo[j]) : 0u;
+    uint32_t kmax = 0;
+    for (int kk = 0; kk < K; ++kk) {
+        uint32_t bk = 0;
+        int bj = 0;
+#pragma unroll
+        for (int j = 0; j < MAXV; ++j)
+            if (key[j] > bk) { bk = key[j]; bj = j; }
+        kmax = __reduce_max_sync(0xffffffffu, bk);
+        const uint32_t who = __reduce_min_sync(0xffffffffu, bk == kmax ? (uint32_t)lane : 32u);
+        if ((uint32_t)lane == who) {
+#pragma unroll
+            for (int j = 0; j < MAXV; ++j)
+                if (j == bj) key[j] = 0u;
+        }
+    }
+    float mh = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < MAXV; ++j) mh = fmaxf(mh, hi[j]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mh = fmaxf(mh, __shfl_xor_sync(0xffffffffu, mh, o));
+    const float kth = rf_unord(kmax);
+    // margin: a non-candidate's logit is below the k-th by more than two
+    // units in the last place of the softmax's differences plus 2^-20, so its
+    // exp value, and its probability, are strictly below the k-th
+    const float mu = __fadd_ru(1.9073486328125e-6f, __fmul_ru(4.76837158203125e-7f, __fadd_ru(fabsf(kth), fabsf(mh))));
+    const float thr = __fsub_rd(kth, mu);
+    if (kmax == 0u || __fsub_rd(kth, mh) < -60.f) return -1;
+    int nc = 0;
+#pragma unroll
+    for (int j = 0; j < MAXV; ++j) {
+        const bool c = lane + 32 * j < E && hi[j] >= thr;
+        const uint32_t m = __ballot_sync(0xffffffffu, c);
+        if (c && nc + __popc(m & ((1u << lane) - 1u)) < RF_CAPC)
+            cand[nc + __popc(m & ((1u << lane) - 1u))] = (int16_t)(lane + 32 * j);
+        nc += __popc(m);
+    }
+    return nc > RF_CAPC ? -1 : nc;
+}
+
+// int8 -> f32, exact: the byte (biased to unsigned) is placed in the low
+// mantissa bits of 2^23 and the bias subtracted.
+__device__ __forceinline__ float rf_i8f(uint32_t u4, uint32_t sel) {
+    return __fsub_rn(__uint_as_float(__byte_perm(u4, 0x4B000000u, sel)), 8388736.f);   // 2^23 + 128
+}
+
+// ---- bounded pass: candidates and their exact chains, a block of RX_TB tokens
+// Every block stages, per RX_KC-column chunk, all E router rows (int8 routers
+// as int8, f32 routers as f32), the shared-gate row and its tokens' rows: the
+// router is streamed once per RX_TB tokens and shared by all their chains.
+// While the first chunks land, each warp finds the candidates of four tokens
+// (rf_token_candidates).  The chains (the reference's sequential fp32 order)
+// are dealt round-robin, up to RX_MAXJ a thread; the shared-gate chains are
+// the last 32 jobs, one warp's (f32 rows, no divergence from the int8 rows).
+// Then one warp per token checks the order-sensitive near-ties and appends the
+// token's retry chains.  Tokens taken whole go to the retry list at once.
+constexpr int RX_TB = 32;
+constexpr int RX_NT = 256;
+constexpr int RX_MAXJ = 4;
+constexpr int RX_KC = 64;
+constexpr int RX_ST = 3;
+constexpr int RX_FROW = 4 * RX_KC + 16;          // bytes of a staged f32 row (x, shared gate, f32 router)
+constexpr int RX_QROW = RX_KC + 16;              // bytes of a staged int8 router row
+
+__host__ __device__ constexpr int rx_stage_bytes(int E, int w8, int has_shared) {
+    return E * (w8 ? RX_QROW : RX_FROW) + (has_shared ? RX_FROW : 0) + RX_TB * RX_FROW;
+}
+__host__ __device__ constexpr int rx_smem_bytes(int E, int w8, int has_shared) {
+    return RX_ST * rx_stage_bytes(E, w8, has_shared) + RX_TB * RF_CAPC * 2 + RX_TB * 8 + RX_NT * RX_MAXJ * 8 + 16;
+}
+
+template <int MAXV, bool W8>
+__global__ void __launch_bounds__(RX_NT) rf_exact_kernel(const float *__restrict__ x, int T, int D,
+                                                         const float *__restrict__ y, int M, int split, float coef,
+                                                         const float *__restrict__ Wf, const int8_t *__restrict__ Wq,
+                                                         const float *__restrict__ Ws,
+                                                         const float *__restrict__ sh_gate, int E, int K, int has_shared,
+                                                         const float *__restrict__ bias, const float *__restrict__ wn,
+                                                         const float *__restrict__ xn, int nseg,
+                                                         float *__restrict__ logits, int ldl,
+                                                         int2 *__restrict__ jobs2, int jcap,
+                                                         int *__restrict__ ctl, int force_retry, int *err) {
+    extern __shared__ __align__(16) unsigned char xsm[];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int wrow = W8 ? RX_QROW : RX_FROW;
+    const int sb = rx_stage_bytes(E, W8 ? 1 : 0, has_shared);
+    int16_t *s_cand = reinterpret_cast<int16_t *>(xsm + RX_ST * sb);          // [TB][CAPC]
+    int *s_nc = reinterpret_cast<int *>(s_cand + RX_TB * RF_CAPC);            // [TB] (-1: whole)
+    int *s_off = s_nc + RX_TB;                                                // [TB] first job
+    int *s_job = s_off + RX_TB;                                               // [NT*MAXJ] tok << 16 | row, -1
+    float *s_val = reinterpret_cast<float *>(s_job + RX_NT * RX_MAXJ);       // [NT*MAXJ]
+    int *s_njob = reinterpret_cast<int *>(s_val + RX_NT * RX_MAXJ);
+    const int t0 = blockIdx.x * RX_TB;
+    const int ntok = min(RX_TB, T - t0);
+    const int nch = (D + RX_KC - 1) / RX_KC;
+    auto stage = [&](int ch) {
+        unsigned char *st = xsm + (ch % RX_ST) * sb;
+        const int c0 = ch * RX_KC;
+        constexpr int PW = W8 ? RX_KC / 16 : RX_KC / 4;      // 16-byte pieces of a router row
+        for (int i = tid; i < E * PW; i += RX_NT) {
+            const int r = i / PW, p = i - r * PW, col = c0 + p * (W8 ? 16 : 4);
+            const bool ok = col < D;
+            const void *src = W8 ? static_cast<const void *>(Wq + (size_t)r * D + col)
+                                 : static_cast<const void *>(Wf + (size_t)r * D + col);
+            rf_cp16(st + r * wrow + p * 16, ok ? src : x, ok);
+        }
+        unsigned char *sg = st + E * wrow;
+        if (has_shared)
+            for (int i = tid; i < RX_KC / 4; i += RX_NT) {
+                const int col = c0 + i * 4;
+                const bool ok = col < D;
+                rf_cp16(sg + i * 16, ok ? sh_gate + col : x, ok);
+            }
+        unsigned char *xs = sg + (has_shared ? RX_FROW : 0);
+        for (int i = tid; i < RX_TB * (RX_KC / 4); i += RX_NT) {
+            const int r = i / (RX_KC / 4), p = i - r * (RX_KC / 4), col = c0 + p * 4;
+            const bool ok = r < ntok && col < D;
+            rf_cp16(xs + r * RX_FROW + p * 16, ok ? x + (size_t)(t0 + r) * D + col : x, ok);
+        }
+    };
+#pragma unroll
+    for (int s = 0; s < RX_ST - 1; ++s) {
+        if (s < nch) stage(s);
+        rf_commit();
+    }
+    // candidates, four tokens a warp, while the first chunks land
+    for (int tl = warp; tl < RX_TB; tl += RX_NT / 32) {
+        int nc = 0;
+        if (tl < ntok) {
+            const int t = t0 + tl;
+            nc = rf_token_candidates<MAXV>(y, M, T, t, E, K, split, Ws, bias, wn, xn, nseg, coef,
+                                           logits + (size_t)t * ldl, s_cand + tl * RF_CAPC);
+            if (nc < 0 && lane == 0) {
+                // taken whole: every row (and the shared gate) in the retry pass
+                const int n2 = (E + has_shared + 3) & ~3;
+                const int b = atomicAdd(ctl + 5, n2);
+                if (b + n2 > jcap) {
+                    omc_dev_error(err, OMC_DEVERR_BOUNDS, OMC_SITE_ROUTER, b + n2);
+                } else {
+                    for (int i = 0; i < n2; ++i) jobs2[b + i] = make_int2(t, i < E + has_shared ? i : -1);
+                }
+                atomicAdd(ctl + 6, 1);
+            }
+        }
+        if (lane == 0) s_nc[tl] = nc;
+    }
+    __syncthreads();
+    // the block's chains: routed candidates token by token, padding to a
+    // multiple of 32, then the shared-gate chains (one warp)
+    if (warp == 0) {
+        const int nc = s_nc[lane] > 0 ? s_nc[lane] : 0;
+        int inc = nc;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int v = __shfl_up_sync(0xffffffffu, inc, o);
+            if (lane >= o) inc += v;
+        }
+        const int off = inc - nc, total = __shfl_sync(0xffffffffu, inc, 31);
+        s_off[lane] = off;
+        for (int j = 0; j < nc; ++j) s_job[off + j] = (lane << 16) | s_cand[lane * RF_CAPC + j];
+        const int p32 = (total + 31) & ~31;
+        if (total + lane < p32) s_job[total + lane] = -1;
+        int nj = p32;
+        if (has_shared) {
+            s_job[p32 + lane] = (lane < ntok && s_nc[lane] >= 0) ? ((lane << 16) | E) : -1;
+            nj += 32;
+        }
+        if (lane == 0) s_njob[0] = nj;
+    }
+    __syncthreads();
+    const int njob = s_njob[0];
+    int jt[RX_MAXJ], je[RX_MAXJ];
+    float acc[RX_MAXJ];
+#pragma unroll
+    for (int q = 0; q < RX_MAXJ; ++q) {
+        const int j = tid + q * RX_NT;
+        const int code = j < njob ? s_job[j] : -1;
+        jt[q] = code >= 0 ? code >> 16 : 0;
+        je[q] = code >= 0 ? code & 0xffff : -1;
+        acc[q] = 0.f;
+    }
+    for (int ch = 0; ch < nch; ++ch) {
+        rf_wait<RX_ST - 2>();
+        __syncthreads();      // chunk ch landed for every thread; chunk ch-1's stage is free
+        if (ch + RX_ST - 1 < nch) stage(ch + RX_ST - 1);
+        rf_commit();
+        const unsigned char *st = xsm + (ch % RX_ST) * sb;
+        const unsigned char *xs = st + E * wrow + (has_shared ? RX_FROW : 0);
+#pragma unroll
+        for (int q = 0; q < RX_MAXJ; ++q) {
+            if (je[q] < 0) continue;
+            const float *xr = reinterpret_cast<const float *>(xs + jt[q] * RX_FROW);
+            float a = acc[q];
+            if (W8 && je[q] < E) {
+                const unsigned char *wr = st + je[q] * wrow;
+#pragma unroll
+                for (int c = 0; c < RX_KC; c += 16) {
+                    const uint4 qv = *reinterpret_cast<const uint4 *>(wr + c);
+                    const uint32_t u[4] = {qv.x ^ 0x80808080u, qv.y ^ 0x80808080u, qv.z ^ 0x80808080u,
+                                           qv.w ^ 0x80808080u};
+#pragma unroll
+                    for (int g = 0; g < 4; ++g) {
+                        const float4 xv = *reinterpret_cast<const float4 *>(xr + c + 4 * g);
+                        a = __fadd_rn(a, __fmul_rn(xv.x, rf_i8f(u[g], 0x7540u)));
+                        a = __fadd_rn(a, __fmul_rn(xv.y, rf_i8f(u[g], 0x7541u)));
+                        a = __fadd_rn(a, __fmul_rn(xv.z, rf_i8f(u[g], 0x7542u)));
+                        a = __fadd_rn(a, __fmul_rn(xv.w, rf_i8f(u[g], 0x7543u)));
+                    }
+                }
+            } else {
+                const float *wr = reinterpret_cast<const float *>(je[q] < E ? st + je[q] * wrow : st + E * wrow);
+#pragma unroll
+                for (int c = 0; c < RX_KC; c += 4) {
+                    const float4 xv = *reinterpret_cast<const float4 *>(xr + c);
+                    const float4 wv = *reinterpret_cast<const float4 *>(wr + c);
+                    a = __fadd_rn(a, __fmul_rn(xv.x, wv.x));
+                    a = __fadd_rn(a, __fmul_rn(xv.y, wv.y));
+                    a = __fadd_rn(a, __fmul_rn(xv.z, wv.z));
+                    a = __fadd_rn(a, __fmul_rn(xv.w, wv.w));
+                }
+            }
+            acc[q] = a;
+        }
+    }
+    rf_wait<0>();
+#pragma unroll
+    for (int q = 0; q < RX_MAXJ; ++q) {
+        if (je[q] < 0) continue;
+        const int t = t0 + jt[q];
+        const float v = (Ws && je[q] < E) ? __fmul_rn(acc[q], Ws[je[q]]) : acc[q];
+        logits[(size_t)t * ldl + je[q]] = v;
+        s_val[tid + q * RX_NT] = v;
+    }
+    __syncthreads();
+    // the order check, one warp per token: softmax numerators of the
+    // candidates as the select kernel computes them; two of the k + 1 largest
+    // that differ but lie within 2^-21 of each other, or a k-th below 2^-100,
+    // send the token to the retry pass with every row exact
+    for (int tl = warp; tl < ntok; tl += RX_NT / 32) {
+        const int nc = s_nc[tl];
+        if (nc < 0) continue;
+        const bool have = lane < nc;
+        float v = have ? s_val[s_off[tl] + lane] : -INFINITY;
+        if (have && bias) v = __fadd_rn(v, bias[s_cand[tl * RF_CAPC + lane]]);
+        float m = have && v > -1e30f ? v : -1e30f;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        const float ev = have ? omc_expf_glibc(__fsub_rn(v, m)) : -1.f;
+        // rank = how many candidates are strictly larger (every lane runs
+        // every shuffle: nc is warp-uniform)
+        int rank = 0;
+        for (int j = 0; j < nc; ++j) rank += __shfl_sync(0xffffffffu, ev, j) > ev ? 1 : 0;
+        bool near = false;
+        for (int j = 0; j < nc; ++j) {
+            const float o = __shfl_sync(0xffffffffu, ev, j);
+            const int rj = __shfl_sync(0xffffffffu, rank, j);
+            if (have && rank <= K && rj <= K && o != ev) {
+                const float big = fmaxf(o, ev), small = fminf(o, ev);
+                near |= big <= __fmul_ru(small, 1.000000476837158203125f);   // 1 + 2^-21
+            }
+        }
+        // the k-th numerator: the value of rank k-1
+        const bool kth_small = have && rank <= K - 1 && !(ev >= 7.888609052210118e-31f);   // 2^-100
+        const bool retry = force_retry > 0 || nc < K || __any_sync(0xffffffffu, near || kth_small);
+        if (retry && lane == 0) {
+            const int t = t0 + tl, n2 = (E + 3) & ~3;
+            const int b = atomicAdd(ctl + 5, n2);
+            if (b + n2 > jcap) {
+                omc_dev_error(err, OMC_DEVERR_BOUNDS, OMC_SITE_ROUTER, b + n2);
+            } else {
+                for (int i = 0; i < n2; ++i) jobs2[b + i] = make_int2(t, i < E ? i : -1);
+            }
+            atomicAdd(ctl + 7, 1);
+        }
+        if (lane == 0) atomicAdd(ctl + 4, nc + (has_shared ? 1 : 0));
+    }
+}
+
+// ---- retry chains: one warp per block, 32 jobs (groups of 4 per token) ------
+// The tokens retried or taken whole: their rows' exact chains, one per lane,
+// each group of four lanes sharing its token's staged row.  Stage: 8 token
+// slots and 32 router rows of RF_KC f32 columns, rows padded by 4 floats.
+constexpr int RF_KC = 32;
+constexpr int RF_ST = 6;
+constexpr int RF_LD = RF_KC + 4;
+constexpr int RF_STAGE = (8 + 32) * RF_LD;        // floats
+constexpr size_t RF_CHAIN_SMEM = (size_t)RF_ST * RF_STAGE * sizeof(float);
+
+__global__ void __launch_bounds__(32) rf_chain_kernel(const float *__restrict__ x, int D, const float *__restrict__ W,
+                                                      const float *__restrict__ Ws, const float *__restrict__ sh_gate,
+                                                      int E, const int2 *__restrict__ jobs,
+                                                      const int *__restrict__ njobs_p, float *__restrict__ logits,
+                                                      int ldl, int jcap) {
+    extern __shared__ __align__(16) float rsm[];
+    const int lane = threadIdx.x, g = lane >> 2;
+    // the counter may have passed the capacity (the writers then reported
+    // OMC_DEVERR_BOUNDS and wrote nothing past it)
+    const int njobs = min(*reinterpret_cast<volatile const int *>(njobs_p), jcap);
+    const int nwin = (njobs + 31) >> 5;
+    const int nch = (D + RF_KC - 1) / RF_KC;
+    for (int win = blockIdx.x; win < nwin; win += gridDim.x) {
+        const int j = win * 32 + lane;
+        int t = -1, e = -1;
+        if (j < njobs) {
+            const int2 jb = jobs[j];
+            t = jb.x;
+            e = jb.y;
+        }
+        const int tg = __shfl_sync(0xffffffffu, t, g * 4);
+        const float *wrow = e >= 0 ? (e < E ? W + (size_t)e * D : sh_gate) : nullptr;
+        const float *xrow = tg >= 0 ? x + (size_t)tg * D : nullptr;
+        auto stage = [&](int ch) {
+            float *st = rsm + (ch % RF_ST) * RF_STAGE;
+            const int c0 = ch * RF_KC;
+#pragma unroll
+            for (int q = 0; q < 2; ++q) {
+                const int piece = (lane & 3) * 2 + q, c = c0 + piece * 4;
+                const bool ok = xrow && c < D;
+                rf_cp16(st + g * RF_LD + piece * 4, ok ? xrow + c : x, ok);
+            }
+#pragma unroll
+            for (int q = 0; q < RF_KC / 4; ++q) {
+                const int c = c0 + q * 4;
+                const bool ok = wrow && c < D;
+                rf_cp16(st + (8 + lane) * RF_LD + q * 4, ok ? wrow + c : x, ok);
+            }
+        };
+#pragma unroll
+        for (int s = 0; s < RF_ST - 1; ++s) {
+            if (s < nch) stage(s);
+            rf_commit();
+        }
+        float acc = 0.f;
+        for (int ch = 0; ch < nch; ++ch) {
+            rf_wait<RF_ST - 2>();
+            __syncwarp();      // every lane's copies of chunk ch landed; chunk ch-1's stage is free
+            if (ch + RF_ST - 1 < nch) stage(ch + RF_ST - 1);
+            rf_commit();
+            const float *st = rsm + (ch % RF_ST) * RF_STAGE;
+            const float *xs = st + g * RF_LD, *wsr = st + (8 + lane) * RF_LD;
+#pragma unroll
+            for (int c = 0; c < RF_KC; c += 4) {
+                const float4 xv = *reinterpret_cast<const float4 *>(xs + c);
+                const float4 wv = *reinterpret_cast<const float4 *>(wsr + c);
+                acc = __fadd_rn(acc, __fmul_rn(xv.x, wv.x));
+                acc = __fadd_rn(acc, __fmul_rn(xv.y, wv.y));
+                acc = __fadd_rn(acc, __fmul_rn(xv.z, wv.z));
+                acc = __fadd_rn(acc, __fmul_rn(xv.w, wv.w));
+            }
+        }
+        rf_wait<0>();
+        __syncwarp();          // the ring is free for the next window
+        if (e >= 0) logits[(size_t)t * ldl + e] = (Ws && e < E) ? __fmul_rn(acc, Ws[e]) : acc;
+    }
+}
+
+__global__ void __launch_bounds__(256) rf_split_rows_kernel(const float *__restrict__ W, long long n, float *__restrict__ dst) {
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+        const float w = W[i];
+        const float h = __half2float(__float2half_rn(w));
+        dst[i] = h;
+        dst[n + i] = w - h;
+    }
+}
+
+}  // namespace
+
+int omc_router_exact = 0;
+int omc_rf_force_retry = 0;
+
+// 0 (the default): the bounded router for layers with E >= OMC_RF_EMIN from
+// T = OMC_RF_TMIN, the exact router otherwise; 1: the exact router for every
+// forward (bit-exact routing weights too); 2: the bounded router for every
+// eligible layer whatever E (tests of the small-E shapes).
+extern "C" int omc_set_router_exact(int mode) {
+    if (mode < 0 || mode > 2) return OMC_EINVAL;
+    omc_router_exact = mode;
+    omc_graphs_invalidate();
+    return 0;
+}
+
+// Test hook: 1 = every token of a bounded pass is retried with every row exact.
+extern "C" int omc_debug_rf_force_retry(int on) {
+    if (on != 0 && on != 1) return OMC_EINVAL;
+    omc_rf_force_retry = on;
+    omc_graphs_invalidate();
+    return 0;
+}
+
+// dst [2E][D]: the f16 rounding of W's rows (as f32), then the remainders.
+extern "C" int omc_launch_rf_split_rows(const float *W, int E, int D, float *dst, cudaStream_t s) {
+    const long long n = (long long)E * D;
+    if (n <= 0) return OMC_EINVAL;
+    rf_split_rows_kernel<<<(int)((n + 255) / 256 < 4096 ? (n + 255) / 256 : 4096), 256, 0, s>>>(W, n, dst);
+    omc_g_launches += 1;
+    return cudaGetLastError() == cudaSuccess ? 0 : OMC_ECUDA;
+}
+
+// Whether a forward of T tokens on L takes the bounded router: the mode (and,
+// by default, E >= OMC_RF_EMIN), the layer has its tiles (not GEMMA, D % 8 ==
+// 0), T >= OMC_RF_TMIN,
+// the workspace holds 2T operand rows, and a block's staging fits.
+extern "C" int omc_rf_eligible(const omc_layer_dev *L, int T, const omc_ws *ws) {
+    if (omc_router_exact == 1 || (omc_router_exact == 0 && L->E < OMC_RF_EMIN) || !L->rf_tab ||
+        L->family == OMC_FAMILY_GEMMA || T < OMC_RF_TMIN || !ws->rf_act ||
+        2 * T > ws->rf_R || (L->D % 8) || L->E > 1024 || L->D_pad > 32 * 256)
+        return 0;
+    const bool w8 = L->router_i8 && L->rf_q && (L->D % 16) == 0;
+    return rx_smem_bytes(L->E, w8 ? 1 : 0, L->has_shared && L->sh_gate ? 1 : 0) <= 200 * 1024;
+}
+
+// The bounded router's logits rows (exact for every expert that can be
+// selected and for the shared gate, bounded approximations otherwise), xh
+// (when non-NULL) the expert GEMMs' f16 token operand.  The caller checked
+// eligibility (rf_tab, T >= 16, the workspace's rf buffers).
+extern "C" int omc_launch_router_fast(const omc_layer_dev *L, const float *x, int T, const omc_ws *ws,
+                                      uint16_t *xh, cudaStream_t s) {
+    static int nsm = 0;
+    if (!nsm) {
+        int dev = 0;
+        if (cudaGetDevice(&dev) != cudaSuccess ||
+            cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+            return OMC_ECUDA;
+    }
+    const int E = L->E, D = L->D, M = L->rf_rows;
+    if (2 * T > ws->rf_R || (D % 8)) return OMC_EINVAL;
+    const int ntiles = (M + OMC_TM - 1) / OMC_TM;
+    const int ldl = E + 1;
+    // 1. prep
+    {
+        const long long nw = (long long)T * ((L->D_pad + 255) / 256);
+        const int blocks = (int)((nw + 7) / 8 < 4096 ? (nw + 7) / 8 : 4096);
+        rf_prep_kernel<<<blocks, 256, 0, s>>>(x, T, D, L->D_pad, ws->rf_R, ws->rf_act, xh, ws->rf_xn,
+                                              ws->rf_rowinfo, ws->rf_roww, reinterpret_cast<int4 *>(ws->rf_work),
+                                              ws->rf_ctl, ntiles, ws->err);
+    }
+    // 2. approximate products on the tensor cores
+    omc_layer_dev Ld;
+    memset(&Ld, 0, sizeof(Ld));
+    Ld.family = OMC_FAMILY_OLMOE;
+    Ld.D = M;
+    Ld.I = D;
+    Ld.E = 1;
+    Ld.k = 1;
+    Ld.D_pad = (M + OMC_KB - 1) / OMC_KB * OMC_KB;
+    Ld.I_pad = L->D_pad;
+    Ld.D_rows = ntiles * OMC_TM;
+    Ld.I_rows = L->D_rows;
+    Ld.experts = L->rf_tab;
+    int rc = omc_launch_gemm_dense_op(&Ld, ws->rf_act, ws->rf_R, ws->rf_rowinfo, ws->rf_roww, ws->rf_work,
+                                      ws->rf_ctl, ws->rf_y, ws->err, s);
+    if (rc) return rc;
+    // 3. candidates.  coef: see the file comment (u = 2^-24, kappa = 17)
+    const double u = 1.0 / 16777216.0;
+    const double gam = (double)D * u / (1.0 - (double)D * u);
+    double coef = gam + 1.0 / 2097152.0 + 17.0 * (2.0 * u) * ((double)L->D_pad / 16.0 + 1.0) * 1.003 + 4.0 * u;
+    coef *= 1.001;
+    const float coef_f = nextafterf((float)coef, INFINITY);
+    const float *Ws = L->router_i8 ? L->router_s : nullptr;
+    const int hs = L->has_shared && L->sh_gate ? 1 : 0;
+    const int nv = (E + 31) / 32;
+    const bool w8 = L->router_i8 && L->rf_q && (D % 16) == 0;
+    const int smem = rx_smem_bytes(E, w8 ? 1 : 0, hs);
+    const dim3 gx((T + RX_TB - 1) / RX_TB);
+    // 3.-4. candidates and their chains, the order check
+#define RFX(NV, W)                                                                                                   \
+    do {                                                                                                             \
+        static int attr = 0;                                                                                         \
+        if (attr < smem) {                                                                                           \
+            if (cudaFuncSetAttribute(rf_exact_kernel<NV, W>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=   \
+                cudaSuccess)                                                                                         \
+                return OMC_ECUDA;                                                                                    \
+            attr = smem;                                                                                             \
+        }                                                                                                            \
+        rf_exact_kernel<NV, W><<<gx, RX_NT, smem, s>>>(                                                              \
+            x, T, D, ws->rf_y, M, L->rf_split, coef_f, L->router, L->rf_q, Ws, L->sh_gate, E, L->k, hs, L->rbias,    \
+            L->rf_wn, ws->rf_xn, (L->D_pad + 255) / 256, ws->logits, ldl, reinterpret_cast<int2 *>(ws->rf_jobs2),     \
+            ws->rf_jcap, ws->rf_ctl,                                                                                 \
+            omc_rf_force_retry, ws->err);                                                                            \
+    } while (0)
+#define RFXW(NV) \
+    do {         \
+        if (w8) RFX(NV, true); \
+        else RFX(NV, false);   \
+    } while (0)
+    if (nv <= 1) RFXW(1);
+    else if (nv <= 2) RFXW(2);
+    else if (nv <= 4) RFXW(4);
+    else if (nv <= 8) RFXW(8);
+    else if (nv <= 16) RFXW(16);
+    else RFXW(32);
+#undef RFXW
+#undef RFX
+    // 5. tokens retried or taken whole: every row exact
+    const long long win_max = ((long long)T * ((E + 4) & ~3) + 31) / 32;
+    const int g2 = (int)(win_max < (long long)nsm * 2 ? win_max : (long long)nsm * 2);
+    rf_chain_kernel<<<g2, 32, RF_CHAIN_SMEM, s>>>(x, D, L->router, Ws, L->sh_gate, E,
+                                                  reinterpret_cast<const int2 *>(ws->rf_jobs2), ws->rf_ctl + 5,
+                                                  ws->logits, ldl, ws->rf_jcap);
+    omc_g_launches += 3;
+    return cudaGetLastError() == cudaSuccess ? 0 : OMC_ECUDA;
+}

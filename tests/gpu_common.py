@@ -50,6 +50,16 @@ GOLDEN_NAMES = ["olmoe_small", "olmoe_renorm", "olmoe_ties", "qwen_small", "qwen
 GEMMA_GOLDEN = ["gemma_small", "gemma_i8", "gemma_ties", "gemma_tiny_l0", "gemma_tiny_l5"]
 
 
+def routing_exact(gpu, L, T) -> bool:
+    """True when a forward of T tokens on layer L takes the exact router (its
+    weights bit-equal the reference's): exact mode, T < 16, a GEMMA layer, or
+    (in the default mode) fewer than 128 experts."""
+    import pyoracle
+    mode = gpu.router_mode()
+    return (mode == gpu.ROUTER_EXACT or T < 16 or L.family == pyoracle.FAMILY_GEMMA
+            or (mode == gpu.ROUTER_AUTO and L.E < 128))
+
+
 def route_dev(m, xd):
     """omc_moe_route_dev on device tensor xd [T, D]: (idx, w, shared gate or None)."""
     import ctypes as C

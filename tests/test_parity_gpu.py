@@ -15,8 +15,8 @@ GEMM) where the shape allows.
 import numpy as np
 import pytest
 
-from conftest import assert_close
-from gpu_common import golden, GOLDEN_NAMES, next_layer_id, olmoe_full, qwen_full
+from conftest import assert_close, assert_weights
+from gpu_common import golden, GOLDEN_NAMES, next_layer_id, olmoe_full, qwen_full, routing_exact
 
 pytestmark = pytest.mark.gpu
 
@@ -37,7 +37,7 @@ def test_golden_parity(gpu, path, name):
     m = gpu.MoELayer.from_oracle_layer(next_layer_id(), L)
     out, idx, w = m.forward(z["x"])
     assert np.array_equal(idx, z["idx_ref"])
-    assert np.array_equal(w.view(np.uint32), z["w_ref"].view(np.uint32))
+    assert_weights(w, z["w_ref"], routing_exact(gpu, L, z["x"].shape[0]))
     assert_close(out, z["out_ref"], what=f"{name}/{path}")
 
 

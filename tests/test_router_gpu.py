@@ -1,9 +1,11 @@
-"""GPU: the router is bit-exact with the reference (indices AND weights).
+"""GPU: the exact router is bit-exact with the reference (indices AND weights).
 
 The device computes the logits as one sequential fp32 chain per (token,
 expert), the softmax with a restatement of glibc expf and the reference's
 summation order, and top-k with the lower-id tie rule, so the routing is
-compared with ``==`` (no tolerance)."""
+compared with ``==`` (no tolerance).  Every test here runs with the exact
+router (omc_set_router_exact(1)); the bounded router, the default from
+T = 16, is checked in test_router_bounded_gpu.py."""
 import ctypes as C
 
 import numpy as np
@@ -12,6 +14,13 @@ import pytest
 from gpu_common import golden, GOLDEN_NAMES, next_layer_id, olmoe_full, qwen_full
 
 pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(autouse=True)
+def exact_router(gpu):
+    gpu.set_router_exact(True)
+    yield
+    gpu.set_router_exact(False)
 
 
 def test_device_expf_equals_glibc(gpu, oracle):
