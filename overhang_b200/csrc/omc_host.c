@@ -222,7 +222,7 @@ static int rf_setup(omc_layer *L, const void *router_w) {
     const int E = P->E, D = P->D;
     P->rf_tab = NULL;
     P->rf_wn = NULL;
-    P->rf_q = NULL;
+    P->rf_wc = NULL;
     P->rf_rows = 0;
     P->rf_split = 0;
     if (P->family == OMC_FAMILY_GEMMA || D % 8 || E <= 0) return OMC_OK;
@@ -250,7 +250,26 @@ static int rf_setup(omc_layer *L, const void *router_w) {
     const size_t tb = (omc_f16_tiles_bytes(M, D) + 255) & ~(size_t)255;
     const size_t ob = ((size_t)Mrows * 4 + 255) & ~(size_t)255;
     const size_t nb = ((size_t)E * 2 * 4 + 255) & ~(size_t)255;
-    const size_t qb = P->router_i8 ? (((size_t)E * D + 255) & ~(size_t)255) : 0;
+    /* chunk-major router rows (rf_wc): 64 bytes per row and chunk */
+    const int kce = P->router_i8 ? 64 : 16;
+    const size_t q1 = ((size_t)E * D * (P->router_i8 ? 1 : 4) + 255) & ~(size_t)255;   /* one copy */
+    const size_t qb = (D % kce) == 0 ? q1 * OMC_RF_NREP : 0;
+    unsigned char *hq = qb ? malloc(q1) : NULL;
+    if (qb && !hq) {
+        free(hn);
+        return omc_fail(OMC_ENOMEM, "omc_layer_init: host alloc");
+    }
+    if (hq) {
+        const int nchk = D / kce, esz = P->router_i8 ? 1 : 4;
+        for (int c = 0; c < nchk; ++c)
+            for (int e = 0; e < E; ++e)
+                for (int pc = 0; pc < 4; ++pc) {
+                    const int slot = pc ^ ((e >> 1) & 3);
+                    const unsigned char *src = (const unsigned char *)router_w +
+                                               ((size_t)e * D + (size_t)c * kce + (size_t)pc * (16 / esz)) * esz;
+                    memcpy(hq + ((size_t)c * E + e) * 64 + (size_t)slot * 16, src, 16);
+                }
+    }
     char *mem = NULL;
     float *tmp = NULL, *ones = malloc(sizeof(float) * (size_t)Mrows);
     int rc = OMC_OK;
@@ -273,10 +292,23 @@ static int rf_setup(omc_layer *L, const void *router_w) {
     if (cudaMemcpyAsync(d_ones, ones, sizeof(float) * (size_t)Mrows, cudaMemcpyHostToDevice, G.stream) ||
         cudaMemcpyAsync(d_wn, hn, sizeof(float) * 2 * (size_t)E, cudaMemcpyHostToDevice, G.stream) ||
         cudaMemcpyAsync(d_tab, &tab, sizeof(tab), cudaMemcpyHostToDevice, G.stream) ||
-        (qb && cudaMemcpyAsync(mem + tb + ob + nb + 256, router_w, (size_t)E * D, cudaMemcpyHostToDevice, G.stream)) ||
+        (qb && cudaMemcpyAsync(mem + tb + ob + nb + 256, hq, q1, cudaMemcpyHostToDevice, G.stream)) ||
         cudaStreamSynchronize(G.stream)) {
         cudaGetLastError();
         rc = omc_fail(OMC_ECUDA, "omc_layer_init: bounded router upload");
+        goto out;
+    }
+    /* the other copies of the chunk-major rows (see rf_wc) */
+    for (int r = 1; qb && r < OMC_RF_NREP; ++r)
+        if (cudaMemcpyAsync(mem + tb + ob + nb + 256 + (size_t)r * q1, mem + tb + ob + nb + 256, q1,
+                            cudaMemcpyDeviceToDevice, G.stream) != cudaSuccess) {
+            cudaGetLastError();
+            rc = omc_fail(OMC_ECUDA, "omc_layer_init: bounded router copies");
+            goto out;
+        }
+    if (qb && cudaStreamSynchronize(G.stream) != cudaSuccess) {
+        cudaGetLastError();
+        rc = omc_fail(OMC_ECUDA, "omc_layer_init: bounded router copies");
         goto out;
     }
     if ((rc = omc_check_device_error())) goto out;
@@ -286,12 +318,14 @@ static int rf_setup(omc_layer *L, const void *router_w) {
     P->rf_wn = d_wn;
     P->rf_rows = M;
     P->rf_split = P->router_i8 ? 0 : 1;
-    P->rf_q = qb ? (const int8_t *)((char *)L->rf_mem + tb + ob + nb + 256) : NULL;
+    P->rf_wc = qb ? (const unsigned char *)((char *)L->rf_mem + tb + ob + nb + 256) : NULL;
+    P->rf_wc_stride = q1;
 out:
     cudaFree(mem);
     cudaFree(tmp);
     free(ones);
     free(hn);
+    free(hq);
     return rc;
 }
 

@@ -114,7 +114,15 @@ typedef struct {
     const omc_expert_ptrs *rf_tab;
     int rf_rows, rf_split;
     const float *rf_wn;
-    const int8_t *rf_q;           /* int8 routers: the router's int8 values [E][D] (chain staging) */
+    const unsigned char *rf_wc;   /* the router rows chunk-major for the chains' staging: chunk c
+                                     (64 int8 or 16 f32 columns) of row e is 64 bytes at
+                                     (c * E + e) * 64, its 16-byte piece p at slot
+                                     p ^ ((e >> 1) & 3); NULL when D is not a multiple of the
+                                     chunk.  OMC_RF_NREP copies rf_wc_stride bytes apart: the
+                                     blocks of a pass walk the chunks in step (each chain's order
+                                     is fixed), and block b reading copy b % OMC_RF_NREP spreads
+                                     the same chunk's reads over more L2 slices */
+    size_t rf_wc_stride;
 } omc_layer_dev;
 
 #define OMC_NMAX 128              /* token rows per grouped-GEMM work item (MMA N) */
@@ -262,6 +270,7 @@ int omc_launch_router_fast(const omc_layer_dev *L, const float *x, int T, const 
  * token than the candidates' chains, each with its own router row. */
 #define OMC_RF_TMIN 16
 #define OMC_RF_EMIN 128
+#define OMC_RF_NREP 8
 /* router mode (omc_set_router_exact): 0 auto, 1 exact, 2 bounded */
 extern int omc_router_exact;
 /* test hook: 1 = every token of a bounded pass is retried whole */

@@ -145,6 +145,7 @@ __global__ void __launch_bounds__(256) rf_prep_kernel(const float *__restrict__ 
             *reinterpret_cast<uint4 *>(base + (size_t)t * 128 + ((c ^ (t & 7)) << 4)) = hi;
             *reinterpret_cast<uint4 *>(base + (size_t)(T + t) * 128 + ((c ^ ((T + t) & 7)) << 4)) = lo;
             if (xh && k0 < D) *reinterpret_cast<uint4 *>(xh + (size_t)t * D + k0) = hi;
+
         }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) {
@@ -189,15 +190,31 @@ __device__ __forceinline__ int rf_token_candidates(const float *__restrict__ y, 
                                                    const float *__restrict__ xn, int nseg, float coef,
                                                    float *__restrict__ lrow, int16_t *cand) {
     const int lane = threadIdx.x & 31;
+    const float *y0 = y + (size_t)t * M, *y1 = y + (size_t)(T + t) * M;
+    // every load first, at in-range indices (the experts past E of the last
+    // column are clamped and discarded), so that they are in flight together
+    float s2 = lane < nseg ? __ldcg(xn + 2 * (t * nseg + lane)) : 0.f;
+    float s1 = lane < nseg ? __ldcg(xn + 2 * (t * nseg + lane) + 1) : 0.f;
+    float v0[MAXV], v1[MAXV], v2[MAXV], v3[MAXV], n2[MAXV], n1[MAXV], sc[MAXV], bi[MAXV];
+#pragma unroll
+    for (int j = 0; j < MAXV; ++j) {
+        const int e = min(lane + 32 * j, E - 1);
+        v0[j] = __ldcg(y0 + e);
+        v1[j] = __ldcg(y1 + e);
+        v2[j] = split ? __ldcg(y0 + E + e) : 0.f;
+        v3[j] = split ? __ldcg(y1 + E + e) : 0.f;
+        n2[j] = __ldg(wn + e);
+        n1[j] = __ldg(wn + E + e);
+        sc[j] = Ws ? __ldg(Ws + e) : 1.f;
+        bi[j] = bias ? __ldg(bias + e) : 0.f;
+    }
     // ||x||_2 and ||x||_1 from the segments' sums, rounded up
-    float s2 = lane < nseg ? xn[2 * (t * nseg + lane)] : 0.f, s1 = lane < nseg ? xn[2 * (t * nseg + lane) + 1] : 0.f;
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
         s2 = __fadd_ru(s2, __shfl_xor_sync(0xffffffffu, s2, o));
         s1 = __fadd_ru(s1, __shfl_xor_sync(0xffffffffu, s1, o));
     }
     const float x2 = __fsqrt_ru(s2), x1 = split ? s1 : 0.f;
-    const float *y0 = y + (size_t)t * M, *y1 = y + (size_t)(T + t) * M;
     float hi[MAXV], lo[MAXV];
     bool bad = false;
 #pragma unroll
@@ -206,20 +223,20 @@ __device__ __forceinline__ int rf_token_candidates(const float *__restrict__ y, 
         hi[j] = -INFINITY;
         lo[j] = -INFINITY;
         if (e >= E) continue;
-        float a = __fadd_rn(y0[e], y1[e]);
-        if (split) a = __fadd_rn(__fadd_rn(a, y0[E + e]), y1[E + e]);
-        const float B = __fadd_ru(__fmul_ru(coef, __fmul_ru(x2, wn[e])),
-                                  __fmul_ru(1.1920928955078125e-7f, __fadd_ru(wn[E + e], x1)));
+        float a = __fadd_rn(v0[j], v1[j]);
+        if (split) a = __fadd_rn(__fadd_rn(a, v2[j]), v3[j]);
+        const float B = __fadd_ru(__fmul_ru(coef, __fmul_ru(x2, n2[j])),
+                                  __fmul_ru(1.1920928955078125e-7f, __fadd_ru(n1[j], x1)));
         const float cl = __fsub_rd(a, B), ch = __fadd_ru(a, B);
         float l1 = cl, h1 = ch, ap = a;
         if (Ws) {
-            const float s = Ws[e];
+            const float s = sc[j];
             l1 = s >= 0.f ? __fmul_rd(cl, s) : __fmul_rd(ch, s);
             h1 = s >= 0.f ? __fmul_ru(ch, s) : __fmul_ru(cl, s);
             ap = __fmul_rn(a, s);
         }
         if (bias) {
-            const float b = bias[e];
+            const float b = bi[j];
             l1 = __fadd_rd(l1, b);
             h1 = __fadd_ru(h1, b);
         }
@@ -279,85 +296,133 @@ __device__ __forceinline__ float rf_i8f(uint32_t u4, uint32_t sel) {
 }
 
 // ---- bounded pass: candidates and their exact chains, a block of RX_TB tokens
-// Every block stages, per RX_KC-column chunk, all E router rows (int8 routers
-// as int8, f32 routers as f32), the shared-gate row and its tokens' rows: the
-// router is streamed once per RX_TB tokens and shared by all their chains.
-// While the first chunks land, each warp finds the candidates of four tokens
-// (rf_token_candidates).  The chains (the reference's sequential fp32 order)
-// are dealt round-robin, up to RX_MAXJ a thread; the shared-gate chains are
-// the last 32 jobs, one warp's (f32 rows, no divergence from the int8 rows).
-// Then one warp per token checks the order-sensitive near-ties and appends the
-// token's retry chains.  Tokens taken whole go to the retry list at once.
-constexpr int RX_TB = 32;
+// Every block stages, per chunk (64 int8 or 16 f32 columns), all E router
+// rows (64 bytes each, from the chunk-major copy rf_wc: one 1-D bulk copy),
+// the shared-gate row and its tokens' rows (one bulk copy each) into a ring of
+// RX_ST stages completed on mbarriers: the router is streamed once per RX_TB
+// tokens and shared by all their chains, and bulk copies keep a chunk's bytes
+// in flight without per-thread requests.  While the first chunks land, each
+// warp finds the candidates of two tokens (rf_token_candidates).  Warps 0..6
+// then run the candidates' chains (the reference's sequential fp32 order), up
+// to RX_MAXJ a thread advanced element by element together so that their adds
+// overlap; warp 7 issues the copies and runs the shared-gate chains (an f32
+// row: no divergence from the int8 rows).  Last, one warp per token checks
+// the order-sensitive near-ties and appends the token's retry chains.  Tokens
+// taken whole go to the retry list at once.
+constexpr int RX_TB = 16;
 constexpr int RX_NT = 256;
-constexpr int RX_MAXJ = 4;
-constexpr int RX_KC = 64;
-constexpr int RX_ST = 3;
-constexpr int RX_FROW = 4 * RX_KC + 16;          // bytes of a staged f32 row (x, shared gate, f32 router)
-constexpr int RX_QROW = RX_KC + 16;              // bytes of a staged int8 router row
+constexpr int RX_RW = 7;                         // warps on the routed chains
+constexpr int RX_MAXJ = 2;                       // routed chains a thread: 7*32*2 >= RX_TB*RF_CAPC
+constexpr int RX_ST = 4;
+static_assert(RX_RW * 32 * RX_MAXJ >= RX_TB * RF_CAPC, "routed chain slots");
+static_assert(RX_TB <= 30, "one shared-gate chain a lane of warp 7; lanes 2.. copy the token rows");
 
+__host__ __device__ constexpr int rx_kc(int w8) { return w8 ? 64 : 16; }
+// a stage: the chunk of every router row, then the shared gate's chunk
 __host__ __device__ constexpr int rx_stage_bytes(int E, int w8, int has_shared) {
-    return E * (w8 ? RX_QROW : RX_FROW) + (has_shared ? RX_FROW : 0) + RX_TB * RX_FROW;
+    return E * 64 + (has_shared ? rx_kc(w8) * 4 : 0);
 }
-__host__ __device__ constexpr int rx_smem_bytes(int E, int w8, int has_shared) {
-    return RX_ST * rx_stage_bytes(E, w8, has_shared) + RX_TB * RF_CAPC * 2 + RX_TB * 8 + RX_NT * RX_MAXJ * 8 + 16;
+// the block's token rows stay resident (D f32 each, padded by 16 bytes so
+// that rows differ in bank), then the stages, barriers and job tables
+__host__ __device__ constexpr int rx_xrow(int D) { return D * 4 + 16; }
+__host__ __device__ constexpr int rx_smem_bytes(int E, int w8, int has_shared, int D) {
+    return RX_TB * rx_xrow(D) + RX_ST * rx_stage_bytes(E, w8, has_shared) + (RX_ST + 1) * 8 + RX_TB * RF_CAPC * 2 +
+           RX_TB * 8 + RX_RW * 32 * RX_MAXJ * 8 + 32;
+}
+
+// One chunk of one chain: the chunk's rounded products first (independent of
+// the chain, so they issue back to back), then their adds in column order
+// (the only dependent steps).  wrow: the row's 64-byte chunk (pieces at slot
+// p ^ sw), xr: the token's staged columns.
+template <bool W8>
+__device__ __forceinline__ float rx_chunk(float a, const unsigned char *wrow, int sw, const float *xr) {
+    constexpr int KC = W8 ? 64 : 16;
+    float p[KC];
+#pragma unroll
+    for (int pc = 0; pc < 4; ++pc) {
+        const uint4 q = *reinterpret_cast<const uint4 *>(wrow + ((pc ^ sw) << 4));
+        if (W8) {
+            const uint32_t u[4] = {q.x ^ 0x80808080u, q.y ^ 0x80808080u, q.z ^ 0x80808080u, q.w ^ 0x80808080u};
+#pragma unroll
+            for (int g = 0; g < 4; ++g) {
+                const float4 xv = *reinterpret_cast<const float4 *>(xr + pc * 16 + 4 * g);
+                p[pc * 16 + 4 * g + 0] = __fmul_rn(xv.x, rf_i8f(u[g], 0x7540u));
+                p[pc * 16 + 4 * g + 1] = __fmul_rn(xv.y, rf_i8f(u[g], 0x7541u));
+                p[pc * 16 + 4 * g + 2] = __fmul_rn(xv.z, rf_i8f(u[g], 0x7542u));
+                p[pc * 16 + 4 * g + 3] = __fmul_rn(xv.w, rf_i8f(u[g], 0x7543u));
+            }
+        } else {
+            const float4 wv = *reinterpret_cast<const float4 *>(&q);
+            const float4 xv = *reinterpret_cast<const float4 *>(xr + pc * 4);
+            p[pc * 4 + 0] = __fmul_rn(xv.x, wv.x);
+            p[pc * 4 + 1] = __fmul_rn(xv.y, wv.y);
+            p[pc * 4 + 2] = __fmul_rn(xv.z, wv.z);
+            p[pc * 4 + 3] = __fmul_rn(xv.w, wv.w);
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < KC; ++i) a = __fadd_rn(a, p[i]);
+    return a;
 }
 
 template <int MAXV, bool W8>
-__global__ void __launch_bounds__(RX_NT) rf_exact_kernel(const float *__restrict__ x, int T, int D,
-                                                         const float *__restrict__ y, int M, int split, float coef,
-                                                         const float *__restrict__ Wf, const int8_t *__restrict__ Wq,
-                                                         const float *__restrict__ Ws,
-                                                         const float *__restrict__ sh_gate, int E, int K, int has_shared,
-                                                         const float *__restrict__ bias, const float *__restrict__ wn,
-                                                         const float *__restrict__ xn, int nseg,
-                                                         float *__restrict__ logits, int ldl,
-                                                         int2 *__restrict__ jobs2, int jcap,
-                                                         int *__restrict__ ctl, int force_retry, int *err) {
-    extern __shared__ __align__(16) unsigned char xsm[];
+__global__ void __launch_bounds__(RX_NT, 1) rf_exact_kernel(const float *__restrict__ x, int T, int D,
+                                                            const float *__restrict__ y, int M, int split, float coef,
+                                                            const unsigned char *__restrict__ Wc, size_t wc_stride,
+                                                            const float *__restrict__ Ws,
+                                                            const float *__restrict__ sh_gate, int E, int K,
+                                                            int has_shared, const float *__restrict__ bias,
+                                                            const float *__restrict__ wn, const float *__restrict__ xn,
+                                                            int nseg, float *__restrict__ logits, int ldl,
+                                                            int2 *__restrict__ jobs2, int jcap,
+                                                            int *__restrict__ ctl, int force_retry, int *err) {
+    extern __shared__ __align__(128) unsigned char xsm[];
+    constexpr int KC = W8 ? 64 : 16;                                          // columns a chunk
+    const int XROW = rx_xrow(D);
+    const unsigned char *wcb = Wc + (size_t)(blockIdx.x % OMC_RF_NREP) * wc_stride;
+    constexpr int NJ = RX_RW * 32 * RX_MAXJ;                                  // routed chain slots
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int wrow = W8 ? RX_QROW : RX_FROW;
     const int sb = rx_stage_bytes(E, W8 ? 1 : 0, has_shared);
-    int16_t *s_cand = reinterpret_cast<int16_t *>(xsm + RX_ST * sb);          // [TB][CAPC]
+    unsigned char *xrows = xsm;                                               // [TB][XROW]
+    unsigned char *stages = xsm + RX_TB * XROW;                               // [ST][sb]
+    uint64_t *full = reinterpret_cast<uint64_t *>(stages + RX_ST * sb);       // [ST], then the rows' barrier
+    uint64_t *xbar = full + RX_ST;
+    int16_t *s_cand = reinterpret_cast<int16_t *>(xbar + 1);                  // [TB][CAPC]
     int *s_nc = reinterpret_cast<int *>(s_cand + RX_TB * RF_CAPC);            // [TB] (-1: whole)
-    int *s_off = s_nc + RX_TB;                                                // [TB] first job
-    int *s_job = s_off + RX_TB;                                               // [NT*MAXJ] tok << 16 | row, -1
-    float *s_val = reinterpret_cast<float *>(s_job + RX_NT * RX_MAXJ);       // [NT*MAXJ]
-    int *s_njob = reinterpret_cast<int *>(s_val + RX_NT * RX_MAXJ);
+    int *s_off = s_nc + RX_TB;                                                // [TB] first chain slot
+    int *s_job = s_off + RX_TB;                                               // [NJ] tok << 16 | row, -1
+    float *s_val = reinterpret_cast<float *>(s_job + NJ);                    // [NJ]
+    int *s_abort = reinterpret_cast<int *>(s_val + NJ);
     const int t0 = blockIdx.x * RX_TB;
     const int ntok = min(RX_TB, T - t0);
-    const int nch = (D + RX_KC - 1) / RX_KC;
-    auto stage = [&](int ch) {
-        unsigned char *st = xsm + (ch % RX_ST) * sb;
-        const int c0 = ch * RX_KC;
-        constexpr int PW = W8 ? RX_KC / 16 : RX_KC / 4;      // 16-byte pieces of a router row
-        for (int i = tid; i < E * PW; i += RX_NT) {
-            const int r = i / PW, p = i - r * PW, col = c0 + p * (W8 ? 16 : 4);
-            const bool ok = col < D;
-            const void *src = W8 ? static_cast<const void *>(Wq + (size_t)r * D + col)
-                                 : static_cast<const void *>(Wf + (size_t)r * D + col);
-            rf_cp16(st + r * wrow + p * 16, ok ? src : x, ok);
-        }
-        unsigned char *sg = st + E * wrow;
-        if (has_shared)
-            for (int i = tid; i < RX_KC / 4; i += RX_NT) {
-                const int col = c0 + i * 4;
-                const bool ok = col < D;
-                rf_cp16(sg + i * 16, ok ? sh_gate + col : x, ok);
-            }
-        unsigned char *xs = sg + (has_shared ? RX_FROW : 0);
-        for (int i = tid; i < RX_TB * (RX_KC / 4); i += RX_NT) {
-            const int r = i / (RX_KC / 4), p = i - r * (RX_KC / 4), col = c0 + p * 4;
-            const bool ok = r < ntok && col < D;
-            rf_cp16(xs + r * RX_FROW + p * 16, ok ? x + (size_t)(t0 + r) * D + col : x, ok);
-        }
-    };
-#pragma unroll
-    for (int s = 0; s < RX_ST - 1; ++s) {
-        if (s < nch) stage(s);
-        rf_commit();
+    const int nch = D / KC;
+    const int shb = has_shared ? KC * 4 : 0;
+    if (tid == 0) {
+        for (int i = 0; i < RX_ST + 1; ++i) mbar_init(&full[i], 1);
+        *s_abort = 0;
+        fence_barrier_init();
     }
-    // candidates, four tokens a warp, while the first chunks land
+    __syncthreads();
+    // warp 7: chunk ch into stage ch % ST (its previous chunk was read by every
+    // thread before the barrier that precedes this call): two bulk copies
+    auto issue = [&](int ch) {
+        unsigned char *st = stages + (ch % RX_ST) * sb;
+        if (lane == 0) {
+            fence_proxy_async_smem();
+            mbar_arrive_expect_tx(&full[ch % RX_ST], (uint32_t)(E * 64 + shb));
+        }
+        __syncwarp();
+        if (lane == 0) bulk_g2s(st, wcb + (size_t)ch * E * 64, (uint32_t)(E * 64), &full[ch % RX_ST]);
+        if (lane == 1 && has_shared) bulk_g2s(st + E * 64, sh_gate + (size_t)ch * KC, (uint32_t)(KC * 4), &full[ch % RX_ST]);
+    };
+    if (warp == RX_RW) {
+        // the token rows, once
+        if (lane == 0) mbar_arrive_expect_tx(xbar, (uint32_t)(ntok * D * 4));
+        __syncwarp();
+        if (lane < ntok) bulk_g2s(xrows + lane * XROW, x + (size_t)(t0 + lane) * D, (uint32_t)(D * 4), xbar);
+        for (int c = 0; c < RX_ST - 1 && c < nch; ++c) issue(c);
+    }
+    // candidates, two tokens a warp, while the first chunks land
     for (int tl = warp; tl < RX_TB; tl += RX_NT / 32) {
         int nc = 0;
         if (tl < ntok) {
@@ -379,10 +444,9 @@ __global__ void __launch_bounds__(RX_NT) rf_exact_kernel(const float *__restrict
         if (lane == 0) s_nc[tl] = nc;
     }
     __syncthreads();
-    // the block's chains: routed candidates token by token, padding to a
-    // multiple of 32, then the shared-gate chains (one warp)
+    // the routed chains, token by token, dealt to the routed warps' slots
     if (warp == 0) {
-        const int nc = s_nc[lane] > 0 ? s_nc[lane] : 0;
+        const int nc = lane < RX_TB && s_nc[lane] > 0 ? s_nc[lane] : 0;
         int inc = nc;
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
@@ -390,80 +454,76 @@ __global__ void __launch_bounds__(RX_NT) rf_exact_kernel(const float *__restrict
             if (lane >= o) inc += v;
         }
         const int off = inc - nc, total = __shfl_sync(0xffffffffu, inc, 31);
-        s_off[lane] = off;
+        if (lane < RX_TB) s_off[lane] = off;
         for (int j = 0; j < nc; ++j) s_job[off + j] = (lane << 16) | s_cand[lane * RF_CAPC + j];
-        const int p32 = (total + 31) & ~31;
-        if (total + lane < p32) s_job[total + lane] = -1;
-        int nj = p32;
-        if (has_shared) {
-            s_job[p32 + lane] = (lane < ntok && s_nc[lane] >= 0) ? ((lane << 16) | E) : -1;
-            nj += 32;
-        }
-        if (lane == 0) s_njob[0] = nj;
+        for (int j = total + lane; j < NJ; j += 32) s_job[j] = -1;
     }
-    __syncthreads();
-    const int njob = s_njob[0];
+    // slot q of routed thread u = tid (< 224) is chain u + 224 q
     int jt[RX_MAXJ], je[RX_MAXJ];
     float acc[RX_MAXJ];
+    const bool routed = warp < RX_RW;
+    __syncthreads();
+    const bool shared_lane = !routed && has_shared && lane < ntok && s_nc[lane] >= 0;
 #pragma unroll
     for (int q = 0; q < RX_MAXJ; ++q) {
-        const int j = tid + q * RX_NT;
-        const int code = j < njob ? s_job[j] : -1;
+        const int code = routed ? s_job[tid + q * RX_RW * 32] : -1;
         jt[q] = code >= 0 ? code >> 16 : 0;
         je[q] = code >= 0 ? code & 0xffff : -1;
         acc[q] = 0.f;
     }
+    // a routed warp advances two chains a lane only when some lane has two
+    const bool two = __any_sync(0xffffffffu, je[1] >= 0);
+    const bool busy = __any_sync(0xffffffffu, je[0] >= 0);
+    const int sw0 = ((je[0] > 0 ? je[0] : 0) >> 1) & 3, sw1 = ((je[1] > 0 ? je[1] : 0) >> 1) & 3;
+    if (!mbar_wait(xbar, 0, err, OMC_SITE_ROUTER)) atomicExch(s_abort, 1);
     for (int ch = 0; ch < nch; ++ch) {
-        rf_wait<RX_ST - 2>();
-        __syncthreads();      // chunk ch landed for every thread; chunk ch-1's stage is free
-        if (ch + RX_ST - 1 < nch) stage(ch + RX_ST - 1);
-        rf_commit();
-        const unsigned char *st = xsm + (ch % RX_ST) * sb;
-        const unsigned char *xs = st + E * wrow + (has_shared ? RX_FROW : 0);
+        if (ch > 0) __syncthreads();           // every thread is done with chunk ch-1's stage
+        if (warp == RX_RW && ch + RX_ST - 1 < nch) issue(ch + RX_ST - 1);
+        if (!*reinterpret_cast<volatile int *>(s_abort) &&
+            !mbar_wait(&full[ch % RX_ST], (uint32_t)((ch / RX_ST) & 1), err, OMC_SITE_ROUTER))
+            atomicExch(s_abort, 1);
+        if (*reinterpret_cast<volatile int *>(s_abort)) continue;
+        const unsigned char *st = stages + (ch % RX_ST) * sb;
+        const unsigned char *xs = xrows + ch * KC * 4;         // column ch*KC of token row 0
+        if (routed && busy) {
+            acc[0] = rx_chunk<W8>(acc[0], st + (je[0] >= 0 ? je[0] : 0) * 64, sw0,
+                                  reinterpret_cast<const float *>(xs + jt[0] * XROW));
+            if (two)
+                acc[1] = rx_chunk<W8>(acc[1], st + (je[1] >= 0 ? je[1] : 0) * 64, sw1,
+                                      reinterpret_cast<const float *>(xs + jt[1] * XROW));
+        } else if (shared_lane) {
+            // the shared gate of token `lane`: products first, then the adds
+            const float *xr = reinterpret_cast<const float *>(xs + lane * XROW);
+            const float *gr = reinterpret_cast<const float *>(st + E * 64);
+            float p[KC];
+#pragma unroll
+            for (int c = 0; c < KC; c += 4) {
+                const float4 xv = *reinterpret_cast<const float4 *>(xr + c);
+                const float4 gv = *reinterpret_cast<const float4 *>(gr + c);
+                p[c] = __fmul_rn(xv.x, gv.x);
+                p[c + 1] = __fmul_rn(xv.y, gv.y);
+                p[c + 2] = __fmul_rn(xv.z, gv.z);
+                p[c + 3] = __fmul_rn(xv.w, gv.w);
+            }
+            float a = acc[0];
+#pragma unroll
+            for (int c = 0; c < KC; ++c) a = __fadd_rn(a, p[c]);
+            acc[0] = a;
+        }
+    }
+    __syncthreads();
+    if (*reinterpret_cast<volatile int *>(s_abort)) return;   // a staged chunk never landed (reported)
+    if (routed) {
 #pragma unroll
         for (int q = 0; q < RX_MAXJ; ++q) {
             if (je[q] < 0) continue;
-            const float *xr = reinterpret_cast<const float *>(xs + jt[q] * RX_FROW);
-            float a = acc[q];
-            if (W8 && je[q] < E) {
-                const unsigned char *wr = st + je[q] * wrow;
-#pragma unroll
-                for (int c = 0; c < RX_KC; c += 16) {
-                    const uint4 qv = *reinterpret_cast<const uint4 *>(wr + c);
-                    const uint32_t u[4] = {qv.x ^ 0x80808080u, qv.y ^ 0x80808080u, qv.z ^ 0x80808080u,
-                                           qv.w ^ 0x80808080u};
-#pragma unroll
-                    for (int g = 0; g < 4; ++g) {
-                        const float4 xv = *reinterpret_cast<const float4 *>(xr + c + 4 * g);
-                        a = __fadd_rn(a, __fmul_rn(xv.x, rf_i8f(u[g], 0x7540u)));
-                        a = __fadd_rn(a, __fmul_rn(xv.y, rf_i8f(u[g], 0x7541u)));
-                        a = __fadd_rn(a, __fmul_rn(xv.z, rf_i8f(u[g], 0x7542u)));
-                        a = __fadd_rn(a, __fmul_rn(xv.w, rf_i8f(u[g], 0x7543u)));
-                    }
-                }
-            } else {
-                const float *wr = reinterpret_cast<const float *>(je[q] < E ? st + je[q] * wrow : st + E * wrow);
-#pragma unroll
-                for (int c = 0; c < RX_KC; c += 4) {
-                    const float4 xv = *reinterpret_cast<const float4 *>(xr + c);
-                    const float4 wv = *reinterpret_cast<const float4 *>(wr + c);
-                    a = __fadd_rn(a, __fmul_rn(xv.x, wv.x));
-                    a = __fadd_rn(a, __fmul_rn(xv.y, wv.y));
-                    a = __fadd_rn(a, __fmul_rn(xv.z, wv.z));
-                    a = __fadd_rn(a, __fmul_rn(xv.w, wv.w));
-                }
-            }
-            acc[q] = a;
+            const int t = t0 + jt[q];
+            const float v = Ws ? __fmul_rn(acc[q], Ws[je[q]]) : acc[q];
+            logits[(size_t)t * ldl + je[q]] = v;
+            s_val[tid + q * RX_RW * 32] = v;
         }
-    }
-    rf_wait<0>();
-#pragma unroll
-    for (int q = 0; q < RX_MAXJ; ++q) {
-        if (je[q] < 0) continue;
-        const int t = t0 + jt[q];
-        const float v = (Ws && je[q] < E) ? __fmul_rn(acc[q], Ws[je[q]]) : acc[q];
-        logits[(size_t)t * ldl + je[q]] = v;
-        s_val[tid + q * RX_NT] = v;
+    } else if (shared_lane) {
+        logits[(size_t)(t0 + lane) * ldl + E] = acc[0];
     }
     __syncthreads();
     // the order check, one warp per token: softmax numerators of the
@@ -639,8 +699,9 @@ extern "C" int omc_rf_eligible(const omc_layer_dev *L, int T, const omc_ws *ws) 
         L->family == OMC_FAMILY_GEMMA || T < OMC_RF_TMIN || !ws->rf_act ||
         2 * T > ws->rf_R || (L->D % 8) || L->E > 1024 || L->D_pad > 32 * 256)
         return 0;
-    const bool w8 = L->router_i8 && L->rf_q && (L->D % 16) == 0;
-    return rx_smem_bytes(L->E, w8 ? 1 : 0, L->has_shared && L->sh_gate ? 1 : 0) <= 200 * 1024;
+    const int w8 = L->router_i8 ? 1 : 0;
+    if (!L->rf_wc || (L->D % rx_kc(w8)) || (size_t)L->E * 64 > (1u << 20)) return 0;
+    return rx_smem_bytes(L->E, w8, L->has_shared && L->sh_gate ? 1 : 0, L->D) <= 220 * 1024;
 }
 
 // The bounded router's logits rows (exact for every expert that can be
@@ -693,8 +754,8 @@ extern "C" int omc_launch_router_fast(const omc_layer_dev *L, const float *x, in
     const float *Ws = L->router_i8 ? L->router_s : nullptr;
     const int hs = L->has_shared && L->sh_gate ? 1 : 0;
     const int nv = (E + 31) / 32;
-    const bool w8 = L->router_i8 && L->rf_q && (D % 16) == 0;
-    const int smem = rx_smem_bytes(E, w8 ? 1 : 0, hs);
+    const bool w8 = L->router_i8 != 0;
+    const int smem = rx_smem_bytes(E, w8 ? 1 : 0, hs, D);
     const dim3 gx((T + RX_TB - 1) / RX_TB);
     // 3.-4. candidates and their chains, the order check
 #define RFX(NV, W)                                                                                                   \
@@ -707,7 +768,8 @@ extern "C" int omc_launch_router_fast(const omc_layer_dev *L, const float *x, in
             attr = smem;                                                                                             \
         }                                                                                                            \
         rf_exact_kernel<NV, W><<<gx, RX_NT, smem, s>>>(                                                              \
-            x, T, D, ws->rf_y, M, L->rf_split, coef_f, L->router, L->rf_q, Ws, L->sh_gate, E, L->k, hs, L->rbias,    \
+            x, T, D, ws->rf_y, M, L->rf_split, coef_f, L->rf_wc, L->rf_wc_stride, Ws, L->sh_gate, E, L->k, hs,       \
+            L->rbias,                                                                                                \
             L->rf_wn, ws->rf_xn, (L->D_pad + 255) / 256, ws->logits, ldl, reinterpret_cast<int2 *>(ws->rf_jobs2),     \
             ws->rf_jcap, ws->rf_ctl,                                                                                 \
             omc_rf_force_retry, ws->err);                                                                            \
