@@ -176,6 +176,7 @@ void omc_shutdown(void) {
         free(G.layers[i].h_experts);
         cudaFree(G.layers[i].d_experts_tab);
         cudaFree(G.layers[i].rf_mem);
+        cudaFree(G.layers[i].rt_mem);
     }
     free(G.layers);
     G.layers = NULL;
@@ -358,6 +359,7 @@ int omc_layer_init(int layer, const omc_moe_desc *d, const void *router_w, const
         free(L->h_experts);
         cudaFree(L->d_experts_tab);
         cudaFree(L->rf_mem);
+        cudaFree(L->rt_mem);
         /* slab space of a re-initialised layer is not reclaimed (bump allocator) */
     }
     memset(L, 0, sizeof(*L));
@@ -406,6 +408,22 @@ int omc_layer_init(int layer, const omc_moe_desc *d, const void *router_w, const
     {
         int rc = rf_setup(L, router_w);
         if (rc) return rc;
+    }
+    /* the exact router's row blocks (the shared gate's row comes with omc_shared_set) */
+    P->rt_w = NULL;
+    P->rt_nrb = 0;
+    if (d->D % 128 == 0) {
+        const int nrb = (d->E + (d->has_shared ? 1 : 0) + 15) / 16;
+        const size_t bytes = (size_t)nrb * (d->D / 128) * 16 * 128 * 4;
+        if (cudaMalloc(&L->rt_mem, bytes) != cudaSuccess) {
+            cudaGetLastError();
+            return omc_fail(OMC_ENOMEM, "omc_layer_init: router row blocks");
+        }
+        CK(cudaMemsetAsync(L->rt_mem, 0, bytes, G.stream));
+        int rc = omc_launch_rt_blocks(router, 0, d->E, d->D, (float *)L->rt_mem, G.stream);
+        if (rc) return omc_fail(rc, "omc_layer_init: router row blocks");
+        P->rt_w = (const float *)L->rt_mem;
+        P->rt_nrb = nrb;
     }
     L->h_experts = calloc((size_t)d->E + 1, sizeof(omc_expert_ptrs));
     L->have = calloc((size_t)d->E + 1, 1);
@@ -604,6 +622,12 @@ int omc_shared_set(int layer, const int8_t *g, const float *gs, const int8_t *u,
     if (!sgv) return omc_fail(OMC_ENOMEM, "omc_shared_set: gate vector");
     CK(cudaMemcpy(sgv, sh_gate, (size_t)L->desc.D * sizeof(float), cudaMemcpyHostToDevice));
     L->dev.sh_gate = sgv;
+    if (L->dev.rt_w) {
+        /* row E of the exact router's row blocks */
+        int rc = omc_launch_rt_blocks(sgv, L->desc.E, 1, L->desc.D, (float *)L->rt_mem, G.stream);
+        if (rc) return omc_fail(rc, "omc_shared_set: router row blocks");
+        CK(cudaStreamSynchronize(G.stream));
+    }
     return set_expert_slot(L, L->desc.E, L->desc.Is, L->dev.Is_pad, L->dev.Is_rows, g, gs, u, us, d, ds);
 }
 

@@ -25,6 +25,7 @@ typedef struct {
     int gemma_ready;                /* GEMMA: omc_layer_gemma_norms called  */
     void *tier;                     /* tiered expert store (omc_tier.c)     */
     void *rf_mem;                   /* bounded router's tiles, table, norms */
+    void *rt_mem;                   /* exact router's row blocks (dev.rt_w)  */
 } omc_layer;
 
 typedef struct {

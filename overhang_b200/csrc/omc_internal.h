@@ -123,6 +123,13 @@ typedef struct {
                                      is fixed), and block b reading copy b % OMC_RF_NREP spreads
                                      the same chunk's reads over more L2 slices */
     size_t rf_wc_stride;
+    /* the exact router's rows in 16-row blocks (router.cu, router_tile2): block
+     * rb, 128-column chunk c is 16 rows x 128 f32 (8 KB) at ((rb * (D/128) + c)
+     * * 16 + r) * 128, the 16-byte unit u of row r at slot (u + r) % 32 (rows
+     * read together differ in bank); row E is the shared gate (written by
+     * omc_shared_set), rows past it zero; NULL when D % 128 != 0 */
+    const float *rt_w;
+    int rt_nrb;
 } omc_layer_dev;
 
 #define OMC_NMAX 128              /* token rows per grouped-GEMM work item (MMA N) */
@@ -258,6 +265,8 @@ int omc_launch_dense_f16(const omc_layer_dev *L, const float *x, int S, const om
 /* bounded router: per-layer tiles and norms (host side, at omc_layer_init),
  * the GEMM over a prepared operand (ffn_mma.cu), and the forward's launches */
 int omc_launch_rf_split_rows(const float *W, int E, int D, float *dst, cudaStream_t s);
+/* rows row0.. row0+nr-1 of the exact router's row blocks from W [nr][D] */
+int omc_launch_rt_blocks(const float *W, int row0, int nr, int D, float *dst, cudaStream_t s);
 int omc_launch_gemm_dense_op(const omc_layer_dev *Ld, const uint16_t *act, int R, const int *rowinfo,
                              const float *roww, const int *work, const int *nwork, float *y, int *err,
                              cudaStream_t s);

@@ -201,6 +201,126 @@ __global__ void __launch_bounds__(G * G, 2) router_tile_kernel(const float *__re
     }
 }
 
+// ---- logits, resident token rows ---------------------------------------------
+// Block = 16 tokens x 16 router rows, one chain a thread (thread tid: token
+// tid % 16, row tid / 16).  The block's 16 token rows are copied once into
+// shared memory by 1-D bulk copies (rows padded by 16 bytes, so that the 16
+// rows differ in bank) and its 16 router rows stream through a ring of
+// 128-column chunks, each one 8 KB bulk copy of the row-block-major copy rt_w
+// (rows rotated by a 16-byte unit each).  Each chunk's products are computed
+// ahead of its adds, which keep the reference's order.  Copies complete on
+// mbarriers; every wait is bounded.  (The staging of router_tile_kernel, per
+// thread cp.async, caps near 15 GB/s per SM on B200; bulk copies do not.)
+constexpr int R2_TB = 16, R2_RB = 16, R2_KC = 128, R2_ST = 6;
+constexpr int R2_WSTAGE = R2_RB * R2_KC * 4;    // 8 KB
+__host__ __device__ constexpr int r2_xrow(int D) { return D * 4 + 16; }
+__host__ __device__ constexpr int r2_smem(int D) { return R2_TB * r2_xrow(D) + R2_ST * R2_WSTAGE + (R2_ST + 1) * 8 + 16; }
+
+__global__ void __launch_bounds__(256, 1) router_tile2_kernel(const float *__restrict__ x, int T, int D,
+                                                              const float *__restrict__ Wt,
+                                                              const float *__restrict__ Ws, int E, int nrows,
+                                                              float *__restrict__ logits, int ldl,
+                                                              uint16_t *__restrict__ xh, int *err) {
+    extern __shared__ __align__(128) unsigned char r2sm[];
+    const int XROW = r2_xrow(D);
+    unsigned char *xrows = r2sm;
+    float *stages = reinterpret_cast<float *>(r2sm + R2_TB * XROW);
+    uint64_t *full = reinterpret_cast<uint64_t *>(reinterpret_cast<unsigned char *>(stages) + R2_ST * R2_WSTAGE);
+    uint64_t *xbar = full + R2_ST;
+    int *s_abort = reinterpret_cast<int *>(xbar + 1);
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int tg = tid & 15, rg = tid >> 4;
+    const int t0 = blockIdx.x * R2_TB, rb = blockIdx.y;
+    const int ntok = min(R2_TB, T - t0);
+    const int nch = D / R2_KC;
+    if (tid == 0) {
+        for (int i = 0; i < R2_ST + 1; ++i) mbar_init(&full[i], 1);
+        *s_abort = 0;
+        fence_barrier_init();
+    }
+    __syncthreads();
+    auto issue = [&](int c) {      // thread 0: chunk c into stage c % ST
+        fence_proxy_async_smem();
+        mbar_arrive_expect_tx(&full[c % R2_ST], (uint32_t)R2_WSTAGE);
+        bulk_g2s(reinterpret_cast<unsigned char *>(stages) + (c % R2_ST) * R2_WSTAGE,
+                 Wt + (size_t)(rb * nch + c) * R2_RB * R2_KC, (uint32_t)R2_WSTAGE, &full[c % R2_ST]);
+    };
+    if (warp == 0) {
+        if (lane == 0) mbar_arrive_expect_tx(xbar, (uint32_t)(ntok * D * 4));
+        __syncwarp();
+        if (lane < ntok) bulk_g2s(xrows + lane * XROW, x + (size_t)(t0 + lane) * D, (uint32_t)(D * 4), xbar);
+        if (lane == 0)
+            for (int c = 0; c < R2_ST - 1 && c < nch; ++c) issue(c);
+    }
+    if (!mbar_wait(xbar, 0, err, OMC_SITE_ROUTER)) atomicExch(s_abort, 1);
+    __syncthreads();
+    if (xh && rb == 0 && !*reinterpret_cast<volatile int *>(s_abort)) {
+        // the f16 token operand of the expert GEMMs (row t of xh = x[t]
+        // rounded to f16), from the resident rows; a value outside the f16
+        // range is reported, not clipped silently
+        const int n8 = D / 8;
+        for (int i = tid; i < ntok * n8; i += 256) {
+            const int r = i / n8, c8 = (i - r * n8) * 8;
+            const float *v = reinterpret_cast<const float *>(xrows + r * XROW) + c8;
+            const float4 a = *reinterpret_cast<const float4 *>(v), b = *reinterpret_cast<const float4 *>(v + 4);
+            if (omc_f16_outside(a.x) || omc_f16_outside(a.y) || omc_f16_outside(a.z) || omc_f16_outside(a.w) ||
+                omc_f16_outside(b.x) || omc_f16_outside(b.y) || omc_f16_outside(b.z) || omc_f16_outside(b.w))
+                omc_dev_error(err, OMC_DEVERR_RANGE, OMC_SITE_ROUTER, t0 + r);
+            uint4 o;
+            o.x = f32x2_to_f16x2_sat(a.x, a.y);
+            o.y = f32x2_to_f16x2_sat(a.z, a.w);
+            o.z = f32x2_to_f16x2_sat(b.x, b.y);
+            o.w = f32x2_to_f16x2_sat(b.z, b.w);
+            *reinterpret_cast<uint4 *>(xh + (size_t)(t0 + r) * D + c8) = o;
+        }
+    }
+    float acc = 0.f;
+    const float *xr = reinterpret_cast<const float *>(xrows + tg * XROW);
+    for (int c = 0; c < nch; ++c) {
+        if (c > 0) __syncthreads();                 // every thread is done with chunk c-1's stage
+        if (tid == 0 && c + R2_ST - 1 < nch) issue(c + R2_ST - 1);
+        if (!*reinterpret_cast<volatile int *>(s_abort) &&
+            !mbar_wait(&full[c % R2_ST], (uint32_t)((c / R2_ST) & 1), err, OMC_SITE_ROUTER))
+            atomicExch(s_abort, 1);
+        if (*reinterpret_cast<volatile int *>(s_abort)) continue;
+        const float *wr = stages + (c % R2_ST) * (R2_RB * R2_KC) + rg * R2_KC;
+        const float *xc = xr + c * R2_KC;
+#pragma unroll
+        for (int h = 0; h < R2_KC; h += 32) {
+            float p[32];
+#pragma unroll
+            for (int q = 0; q < 32; q += 4) {
+                const float4 xv = *reinterpret_cast<const float4 *>(xc + h + q);
+                const float4 wv = *reinterpret_cast<const float4 *>(wr + ((((h + q) >> 2) + rg) & 31) * 4);
+                p[q] = __fmul_rn(xv.x, wv.x);
+                p[q + 1] = __fmul_rn(xv.y, wv.y);
+                p[q + 2] = __fmul_rn(xv.z, wv.z);
+                p[q + 3] = __fmul_rn(xv.w, wv.w);
+            }
+#pragma unroll
+            for (int q = 0; q < 32; ++q) acc = __fadd_rn(acc, p[q]);
+        }
+    }
+    __syncthreads();
+    if (*reinterpret_cast<volatile int *>(s_abort)) return;   // a copy never landed (reported)
+    const int t = t0 + tg, r = rb * R2_RB + rg;
+    if (t < T && r < nrows) logits[(size_t)t * ldl + r] = (Ws && r < E) ? __fmul_rn(acc, Ws[r]) : acc;
+}
+
+// rows row0..row0+nr-1 of the row-block-major copy from W [nr][D]
+__global__ void __launch_bounds__(256) rt_blocks_kernel(const float *__restrict__ W, int row0, int nr, int D,
+                                                        float *__restrict__ dst) {
+    const int nch = D / R2_KC;
+    const long long n4 = (long long)nr * (D / 4);
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n4; i += (long long)gridDim.x * blockDim.x) {
+        const int rr = (int)(i / (D / 4)), u = (int)(i - (long long)rr * (D / 4));   // row, 16-byte unit
+        const int row = row0 + rr, c = u / (R2_KC / 4), uc = u - c * (R2_KC / 4);
+        const float4 v = *reinterpret_cast<const float4 *>(W + (size_t)rr * D + (size_t)u * 4);
+        float *blk = dst + ((size_t)((row / R2_RB) * nch + c) * R2_RB + (row % R2_RB)) * R2_KC;
+        *reinterpret_cast<float4 *>(blk + ((uc + row % R2_RB) & 31) * 4) = v;
+    }
+}
+
 // ---- logits, few tokens --------------------------------------------------------
 // Decode-sized batches (T <= 8): one block per 8 router rows stages all of D
 // for its rows and the T tokens at once (one memory latency instead of a
@@ -345,6 +465,20 @@ int launch_logits(const omc_layer_dev *L, const float *x, int T, int nrows, floa
         return (long long)((T + g * tt - 1) / (g * tt)) * ((nrows + g * rr - 1) / (g * rr));
     };
     const long long want = nsm;
+    if (!g_force_tile && L->rt_w && r2_smem(L->D) <= 220 * 1024 && nrows <= L->rt_nrb * R2_RB) {
+        static int attr2 = 0;
+        const int smem = r2_smem(L->D);
+        if (attr2 < smem) {
+            if (cudaFuncSetAttribute(router_tile2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
+                cudaSuccess)
+                return OMC_ECUDA;
+            attr2 = smem;
+        }
+        const dim3 g((T + R2_TB - 1) / R2_TB, (nrows + R2_RB - 1) / R2_RB);
+        router_tile2_kernel<<<g, 256, smem, s>>>(x, T, L->D, L->rt_w, L->router_i8 ? L->router_s : nullptr, L->E,
+                                                 nrows, logits, ldl, xh, err);
+        return 0;
+    }
     switch (g_force_tile) {
     case 1644: return launch_tile<16, 4, 4, 32>(L, x, T, nrows, logits, ldl, xh, err, s);
     case 1622: return launch_tile<16, 2, 2, 64>(L, x, T, nrows, logits, ldl, xh, err, s);
@@ -449,6 +583,14 @@ extern "C" int omc_launch_router(const omc_layer_dev *L, const float *x, int T, 
         omc_plan_fill_rows<<<(nfill + 255) / 256, 256, 0, s>>>(pa, topk_idx, topk_w);
         omc_g_launches += 1;
     }
+    return cudaGetLastError() == cudaSuccess ? 0 : OMC_ECUDA;
+}
+
+extern "C" int omc_launch_rt_blocks(const float *W, int row0, int nr, int D, float *dst, cudaStream_t s) {
+    if (nr <= 0 || D % R2_KC) return OMC_EINVAL;
+    const long long n4 = (long long)nr * (D / 4);
+    rt_blocks_kernel<<<(int)((n4 + 255) / 256 < 4096 ? (n4 + 255) / 256 : 4096), 256, 0, s>>>(W, row0, nr, D, dst);
+    omc_g_launches += 1;
     return cudaGetLastError() == cudaSuccess ? 0 : OMC_ECUDA;
 }
 
