@@ -92,6 +92,42 @@ def test_omm_moe_accumulates_and_follows_slot_reuse(gpu, oracle):
     assert_close(out2, exp, what="omm_moe after slot reuse")
 
 
+def test_omm_moe_slot_refill_with_equal_scales(gpu, oracle):
+    """A slot refilled in place with different int8 rows but bit-equal scales
+    (what a pointer-and-scales identity would miss): the content hash sees
+    the change and the next call uses the new rows."""
+    L = oracle.make_layer(oracle.FAMILY_OLMOE, 256, 128, 16, 4, seed=95)
+    a = L.arrays
+    x = oracle.normal(96, (16, 256))
+    slots = {e: tuple(np.array(a[n][e]) for n in ("g", "gs", "u", "us", "d", "ds")) for e in range(L.E)}
+    lib = gpu.lib()
+    out = np.zeros((16, 256), np.float32)
+    jobs, nj, keep = _jobs(gpu, L, x, slots)
+    assert lib.omm_moe(jobs, nj, x.ctypes.data_as(C.c_void_p), 16, 256, 128, out.ctypes.data_as(C.c_void_p)) == 0
+    # every routed expert's int8 rows negated in place, scales untouched: expert(x) changes
+    for e in range(L.E):
+        for i in (0, 2, 4):
+            slots[e][i][...] = -np.maximum(slots[e][i], -127)
+    L2 = oracle.make_layer(oracle.FAMILY_OLMOE, 256, 128, 16, 4, seed=95)
+    for e in range(L.E):
+        for i, n in ((0, "g"), (2, "u"), (4, "d")):
+            L2.arrays[n][e] = slots[e][i]
+    out2 = np.zeros((16, 256), np.float32)
+    jobs2, nj2, keep2 = _jobs(gpu, L, x, slots)
+    assert lib.omm_moe(jobs2, nj2, x.ctypes.data_as(C.c_void_p), 16, 256, 128, out2.ctypes.data_as(C.c_void_p)) == 0
+    import pyoracle as P
+    idx, w = P.oracle_route(L, x)
+    exp = np.zeros((16, 256), np.float32)
+    for e in range(L.E):
+        for s_ in range(16):
+            for kk in range(4):
+                if idx[s_, kk] == e:
+                    y = P.oracle_expert_rows(L2, x[s_:s_ + 1], np.array([e], np.int32))[0]
+                    exp[s_] = exp[s_] + (w[s_, kk] * y).astype(np.float32)
+    assert not np.allclose(out2, out), "the refilled rows were not used"
+    assert_close(out2, exp, what="omm_moe after an equal-scales refill")
+
+
 def test_omm_unsupported_shapes_fall_back(gpu):
     lib = gpu.lib()
     x = np.zeros((8, 96), np.float32)
@@ -142,6 +178,21 @@ def test_omm_dense_q_cache_follows_scales(gpu, oracle):
     sc[...] = sc2
     assert call() == 0
     assert_close(out, _dense_ref(x, q.astype(np.float32) * sc[:, None]), what="omm_dense_q after refill")
+
+
+def test_omm_dense_q_rows_change_scales_equal(gpu, oracle):
+    """The int8 rows change in place and the scales do not: copied again."""
+    N, K, S = 256, 512, 16
+    q, sc = oracle.quantize_py(oracle.normal(9210, (N, K), 0.02))
+    x = oracle.normal(9211, (S, K))
+    lib = gpu.lib()
+    out = np.zeros((S, N), np.float32)
+    call = lambda: lib.omm_dense_q(q.ctypes.data_as(C.c_void_p), sc.ctypes.data_as(C.c_void_p), N, K,  # noqa: E731
+                                   x.ctypes.data_as(C.c_void_p), S, out.ctypes.data_as(C.c_void_p))
+    assert call() == 0
+    q[...] = -np.maximum(q, -127)
+    assert call() == 0
+    assert_close(out, _dense_ref(x, q.astype(np.float32) * sc[:, None]), what="omm_dense_q after a rows-only refill")
 
 
 def test_omm_dense_q_unsupported(gpu):
