@@ -387,6 +387,15 @@ def run_ours(args):
         torch.cuda.synchronize()
         st.append(ob.stage_times())
     ob.set_profiling(False)
+    # which router the forward took, and the bounded router's counters for the
+    # last diagnostic forward (exact chains, retried tokens)
+    rstats = ob.router_stats()
+    bounded = (ob.router_mode() == ob.ROUTER_BOUNDED or
+               (ob.router_mode() == ob.ROUTER_AUTO and E >= 128)) and T >= 16 and FAMILY != "gemma"
+    router_info = {"mode": "bounded" if bounded else "exact"}
+    if bounded:
+        router_info.update({"exact_chains_per_token": rstats["jobs"] / T, "retried_tokens": rstats["retried_tokens"],
+                            "whole_tokens": rstats["whole_tokens"]})
     prof_misses = ((layer.tier_stats(tier)[5] - pmiss0) / 5) if tier else 0
     stage_names = [n for n, _ in st[-1]] if st and st[-1] else []
     stage_ms = np.array([[v for _, v in row] for row in st]).mean(axis=0).tolist() if stage_names else []
@@ -610,6 +619,7 @@ def run_ours(args):
             "gpu_launches": launches,
             "repeats": len(passes), "pass_ms": [round(p, 4) for p in passes],
             "stage_ms": stages,
+            "router": router_info,
             "roofline": dict(roof, **{
                          "kernel": dom, "peak_source": src, "alg_bytes_per_launch": alg_bytes,
                          "launch_ms": dom_ms, "launches_timed": dom_n,
