@@ -394,7 +394,9 @@ int omc_layer_init(int layer, const omc_moe_desc *d, const void *router_w, const
     if (P->router_i8) {
         int rc = staging_ensure((size_t)d->E * d->D);
         if (rc) return rc;
-        CK(cudaMemcpy(G.staging, router_w, (size_t)d->E * d->D, cudaMemcpyHostToDevice));
+        /* on the library's stream (non-blocking): a plain cudaMemcpy would not
+         * wait for an upload's relayout kernel that still reads the staging */
+        CK(cudaMemcpyAsync(G.staging, router_w, (size_t)d->E * d->D, cudaMemcpyHostToDevice, G.stream));
         rc = omc_launch_i8_to_f32((const int8_t *)G.staging, router, (long long)d->E * d->D, G.stream);
         if (rc) return omc_fail(rc, "omc_layer_init: router conversion launch");
         float *rs = omc_slab_alloc((size_t)d->E * sizeof(float), &on_host);

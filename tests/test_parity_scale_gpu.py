@@ -81,7 +81,13 @@ def test_zipf_skewed_routing(gpu, oracle, path, router, family):
     x = oracle.normal(9300 + L.E, (T, L.D))
     out, idx, w = m.forward(x)
     ridx, rw = oracle.oracle_route(L, x)
-    assert np.array_equal(idx, ridx)
+    if not np.array_equal(idx, ridx):
+        # say whether a second forward of the same input repeats the result
+        _, idx2, _ = m.forward(x)
+        bad = np.nonzero((idx != ridx).any(axis=1))[0]
+        pytest.fail(f"{len(bad)} of {T} rows differ from the oracle (first {bad[:8].tolist()}); "
+                    f"a second forward equals the first: {np.array_equal(idx2, idx)}, "
+                    f"equals the oracle: {np.array_equal(idx2, ridx)}")
     assert_weights(w, rw, router == "exact")
     counts = np.bincount(idx.ravel(), minlength=L.E)
     # the load is skewed: the hottest expert serves >= 90% of the tokens (a
