@@ -466,11 +466,17 @@ int omc_layer_gemma_norms(int layer, float eps, const float *router_scale, const
         free(h);
         return omc_fail(OMC_ENOMEM, "omc_layer_gemma_norms: slab");
     }
-    cudaError_t e1 = cudaMemcpy(s2, h, (size_t)D * sizeof(float), cudaMemcpyHostToDevice);
+    /* host-to-device copies go on the library's stream: a blocking
+     * cudaMemcpy from pageable memory may return before its transfer lands
+     * and is not ordered with that (non-blocking) stream's kernels */
+    cudaError_t e1 = cudaMemcpyAsync(s2, h, (size_t)D * sizeof(float), cudaMemcpyHostToDevice, G.stream);
+    if (e1 == cudaSuccess)
+        e1 = cudaMemcpyAsync(pes, per_expert_scale, (size_t)E * sizeof(float), cudaMemcpyHostToDevice, G.stream);
+    if (e1 == cudaSuccess && en)
+        e1 = cudaMemcpyAsync(en, expert_norm, (size_t)D * sizeof(float), cudaMemcpyHostToDevice, G.stream);
+    if (e1 == cudaSuccess) e1 = cudaStreamSynchronize(G.stream);   /* the sources are consumed at return */
     free(h);
     CK(e1);
-    CK(cudaMemcpy(pes, per_expert_scale, (size_t)E * sizeof(float), cudaMemcpyHostToDevice));
-    if (en) CK(cudaMemcpy(en, expert_norm, (size_t)D * sizeof(float), cudaMemcpyHostToDevice));
     graphs_invalidate();
     L->dev.eps = eps;
     L->dev.g_s2 = s2;
@@ -497,7 +503,8 @@ int omc_layer_router_bias(int layer, const float *bias) {
     int on_host;
     float *b = omc_slab_alloc((size_t)E * sizeof(float), &on_host);
     if (!b) return omc_fail(OMC_ENOMEM, "omc_layer_router_bias: slab");
-    CK(cudaMemcpy(b, bias, (size_t)E * sizeof(float), cudaMemcpyHostToDevice));
+    CK(cudaMemcpyAsync(b, bias, (size_t)E * sizeof(float), cudaMemcpyHostToDevice, G.stream));
+    CK(cudaStreamSynchronize(G.stream));
     L->dev.rbias = b;
     return OMC_OK;
 }
@@ -582,7 +589,8 @@ static int set_expert_slot(omc_layer *L, int slot, int I_, int I_pad, int I_rows
     if ((rc = omc_expert_upload(P->D, P->D_pad, P->D_rows, I_, I_pad, I_rows, g, gs, u, us, d, ds, &ep, 0))) return rc;
     L->h_experts[slot] = ep;
     L->have[slot] = 1;
-    CK(cudaMemcpy(L->d_experts_tab + slot, &ep, sizeof(ep), cudaMemcpyHostToDevice));
+    /* pageable source: staged by the runtime before the call returns */
+    CK(cudaMemcpyAsync(L->d_experts_tab + slot, &ep, sizeof(ep), cudaMemcpyHostToDevice, G.stream));
     return OMC_OK;
 }
 
@@ -622,14 +630,14 @@ int omc_shared_set(int layer, const int8_t *g, const float *gs, const int8_t *u,
     int on_host;
     float *sgv = omc_slab_alloc((size_t)L->desc.D * sizeof(float), &on_host);
     if (!sgv) return omc_fail(OMC_ENOMEM, "omc_shared_set: gate vector");
-    CK(cudaMemcpy(sgv, sh_gate, (size_t)L->desc.D * sizeof(float), cudaMemcpyHostToDevice));
+    CK(cudaMemcpyAsync(sgv, sh_gate, (size_t)L->desc.D * sizeof(float), cudaMemcpyHostToDevice, G.stream));
     L->dev.sh_gate = sgv;
     if (L->dev.rt_w) {
         /* row E of the exact router's row blocks */
         int rc = omc_launch_rt_blocks(sgv, L->desc.E, 1, L->desc.D, (float *)L->rt_mem, G.stream);
         if (rc) return omc_fail(rc, "omc_shared_set: router row blocks");
-        CK(cudaStreamSynchronize(G.stream));
     }
+    CK(cudaStreamSynchronize(G.stream));
     return set_expert_slot(L, L->desc.E, L->desc.Is, L->dev.Is_pad, L->dev.Is_rows, g, gs, u, us, d, ds);
 }
 
@@ -1497,7 +1505,7 @@ int omc_debug_expf(const float *x, float *y, long long n) {
     if (n <= 0) return OMC_OK;
     float *d = NULL;
     CK(cudaMalloc((void **)&d, (size_t)n * 8));
-    CK(cudaMemcpy(d, x, (size_t)n * 4, cudaMemcpyHostToDevice));
+    CK(cudaMemcpyAsync(d, x, (size_t)n * 4, cudaMemcpyHostToDevice, G.stream));
     int rc = omc_launch_expf_probe(d, d + n, n, G.stream);
     if (!rc) rc = cudaStreamSynchronize(G.stream) == cudaSuccess ? OMC_OK : OMC_ECUDA;
     if (!rc) rc = cudaMemcpy(y, d + n, (size_t)n * 4, cudaMemcpyDeviceToHost) == cudaSuccess ? OMC_OK : OMC_ECUDA;

@@ -241,7 +241,7 @@ int omc_tier_upload(omc_layer *L, int e, const int8_t *g, const float *gs, const
     }   /* else ep names the placeholder image until a forward routes e */
     L->h_experts[e] = ep;
     L->have[e] = 1;
-    CK(cudaMemcpy(L->d_experts_tab + e, &ep, sizeof(ep), cudaMemcpyHostToDevice));
+    CK(cudaMemcpyAsync(L->d_experts_tab + e, &ep, sizeof(ep), cudaMemcpyHostToDevice, omc_G.stream));
     return OMC_OK;
 }
 

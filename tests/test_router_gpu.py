@@ -68,6 +68,22 @@ def test_routing_qwen_full_bitexact(gpu, oracle, T):
     assert np.array_equal(w.view(np.uint32), rw.view(np.uint32))
 
 
+def test_int8_router_after_queued_uploads(gpu, oracle):
+    """Layers built back to back: each upload leaves expert copies and
+    relayouts queued on the library's stream while the next layer's int8
+    router goes through the same staging buffer.  The router must be the
+    layer's own (a router built from another upload's bytes routes nearly
+    every token differently)."""
+    L = qwen_full()
+    x = oracle.normal(9150, (64, L.D))
+    ridx, rw = oracle.oracle_route(L, x)
+    for _ in range(3):
+        m = gpu.MoELayer.from_oracle_layer(next_layer_id(), L)
+        _, idx, w = m.forward(x)
+        assert np.array_equal(idx, ridx)
+        assert np.array_equal(w.view(np.uint32), rw.view(np.uint32))
+
+
 def test_routing_ties_many(gpu, oracle):
     """Half of the router rows duplicate the other half: every token sees
     exactly tied probabilities; the reference keeps the lower expert id."""
