@@ -140,7 +140,8 @@ int omc_init(int device, size_t slab_bytes) {
     G.num_sms = prop.multiProcessorCount;
     CK(cudaStreamCreateWithFlags(&G.stream, cudaStreamNonBlocking));
     CK(cudaMalloc((void **)&G.d_err, 16 * sizeof(int)));
-    CK(cudaMemset(G.d_err, 0, 16 * sizeof(int)));
+    CK(cudaMemsetAsync(G.d_err, 0, 16 * sizeof(int), G.stream));
+    CK(cudaStreamSynchronize(G.stream));
     for (int i = 0; i < OMC_NSTAGE_EV; ++i) CK(cudaEventCreate(&G.ev[i]));
     if (slab_bytes == 0) {
         size_t fr = 0, tot = 0;
@@ -677,7 +678,10 @@ static int dec_ensure(const omc_layer_dev *P) {
         cudaGetLastError();
         return omc_fail(OMC_ENOMEM, "decode state: cudaMalloc(%zu ints, %zu floats) failed", ci, pf);
     }
-    CK(cudaMemset(G.dec_ctr, 0, ci * sizeof(int)));
+    /* a blocking cudaMemset is not ordered with the library's non-blocking
+     * stream: zero on it and wait, so that any stream's launch sees zeros */
+    CK(cudaMemsetAsync(G.dec_ctr, 0, ci * sizeof(int), G.stream));
+    CK(cudaStreamSynchronize(G.stream));
     G.dec_ctr_n = ci;
     G.dec_part_n = pf;
     return OMC_OK;
@@ -848,9 +852,10 @@ int omc_check_device_error(void) {
     cudaError_t e = cudaMemcpy(h, G.d_err, sizeof(h), cudaMemcpyDeviceToHost);
     if (e != cudaSuccess) return omc_fail(OMC_ECUDA, "reading device error word: %s", cudaGetErrorString(e));
     if (!h[0]) return OMC_OK;
-    cudaMemset(G.d_err, 0, sizeof(h));
+    cudaMemsetAsync(G.d_err, 0, sizeof(h), G.stream);
     /* a forward that stopped at a lost wait may leave decode counters set */
-    if (G.dec_ctr) cudaMemset(G.dec_ctr, 0, G.dec_ctr_n * sizeof(int));
+    if (G.dec_ctr) cudaMemsetAsync(G.dec_ctr, 0, G.dec_ctr_n * sizeof(int), G.stream);
+    cudaStreamSynchronize(G.stream);
     const int st = h[0] == OMC_DEVERR_TIMEOUT ? OMC_ETIMEOUT : h[0] == OMC_DEVERR_RANGE ? OMC_ERANGE : OMC_EDEVICE;
     return omc_fail(st, "device error code %d at site %d (detail %d)", h[0], h[1], h[2]);
 }

@@ -200,11 +200,12 @@ int omc_tier_enable(int layer, int hbm_slots, int interval, int decay_every) {
     if (ce == cudaSuccess) ce = cudaMalloc((void **)&t->spare, t->bytes);
     if (ce == cudaSuccess) ce = cudaMalloc((void **)&t->d_stats, sizeof(uint32_t) * (2 * (size_t)E + 1));
     if (ce == cudaSuccess) ce = cudaMalloc((void **)&t->d_list, sizeof(int) * ((size_t)E + 1));
-    if (ce == cudaSuccess) ce = cudaMemset(t->d_list, 0, sizeof(int) * ((size_t)E + 1));
+    if (ce == cudaSuccess) ce = cudaMemsetAsync(t->d_list, 0, sizeof(int) * ((size_t)E + 1), omc_G.stream);
     if (ce == cudaSuccess) ce = cudaMalloc((void **)&t->d_total, sizeof(unsigned long long));
-    if (ce == cudaSuccess) ce = cudaMemset(t->d_total, 0, sizeof(unsigned long long));
+    if (ce == cudaSuccess) ce = cudaMemsetAsync(t->d_total, 0, sizeof(unsigned long long), omc_G.stream);
     if (ce == cudaSuccess) ce = cudaEventCreateWithFlags(&t->ev, cudaEventDisableTiming);
-    if (ce == cudaSuccess) ce = cudaMemset(t->d_stats, 0, sizeof(uint32_t) * (2 * (size_t)E + 1));
+    if (ce == cudaSuccess) ce = cudaMemsetAsync(t->d_stats, 0, sizeof(uint32_t) * (2 * (size_t)E + 1), omc_G.stream);
+    if (ce == cudaSuccess) ce = cudaStreamSynchronize(omc_G.stream);   /* ordered with, and done before, any forward */
     if (ce != cudaSuccess) {
         cudaGetLastError();
         omc_tier_free(L);
