@@ -123,12 +123,13 @@ __device__ __forceinline__ void cp_async16(void *smem_dst, const void *gsrc) {
 // an error is already reported (the forward is lost either way).
 __device__ bool wait_value(const int *p, int want, int *err, int detail) {
     if (ld_acquire(p) == want) return true;
-    const uint64_t t0 = omc_globaltimer();
+    OmcDeadline dl;
+    dl.start();
     for (;;) {
         __nanosleep(64);
         if (ld_acquire(p) == want) return true;
         if (*(volatile int *)err != 0) return false;
-        if (omc_globaltimer() - t0 > OMC_WAIT_LIMIT_NS) {
+        if (dl.over()) {
             omc_dev_error(err, OMC_DEVERR_TIMEOUT, OMC_SITE_DECODE, detail);
             return false;
         }
@@ -139,9 +140,10 @@ __device__ bool wait_value(const int *p, int want, int *err, int detail) {
 // phase flips: waiting warps take no issue slots from working ones.
 __device__ __forceinline__ void mbar_wait_s(uint64_t *bar, uint32_t parity, int *err) {
     if (mbar_try_wait(bar, parity)) return;
-    const uint64_t t0 = omc_globaltimer();
+    OmcDeadline dl;
+    dl.start();
     while (!mbar_try_wait_sleep(bar, parity, 256u)) {   // short hint: wake-up latency stays small
-        if (omc_globaltimer() - t0 > OMC_WAIT_LIMIT_NS) {
+        if (dl.over()) {
             omc_dev_error(err, OMC_DEVERR_TIMEOUT, OMC_SITE_DECODE, (int)parity);
             return;
         }

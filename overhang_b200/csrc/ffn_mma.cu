@@ -123,12 +123,13 @@ struct GemmArgs {
 __device__ __forceinline__ bool wait_or_abort(uint64_t *bar, uint32_t parity, int *err, int site,
                                               volatile int *abort_flag) {
     if (mbar_try_wait(bar, parity)) return true;
-    const uint64_t t0 = omc_globaltimer();
+    OmcDeadline dl;
+    dl.start();
     for (;;) {
         for (int i = 0; i < 8; ++i)
             if (mbar_try_wait_sleep(bar, parity, 500000u)) return true;   // sleeps up to 0.5 ms per try
         if (*abort_flag) return false;
-        if (omc_globaltimer() - t0 > OMC_WAIT_LIMIT_NS) {
+        if (dl.over()) {
             omc_dev_error(err, OMC_DEVERR_TIMEOUT, site, (int)parity);
             *abort_flag = 1;
             return false;

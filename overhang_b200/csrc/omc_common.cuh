@@ -27,16 +27,33 @@ __device__ __forceinline__ void omc_dev_error(int *err, int code, int site, int 
     }
 }
 
-// Time limit for every mbarrier wait, measured on %globaltimer: any honest
-// wait here is microseconds (one tile); a lost wait ends after ~1 s, reports
-// OMC_DEVERR_TIMEOUT and the kernel unwinds instead of hanging.
+// Time limit for every wait on a barrier, flag or count: any honest wait
+// here is microseconds (one tile); a lost wait ends after ~1 s, reports
+// OMC_DEVERR_TIMEOUT and the kernel unwinds instead of hanging.  The limit
+// is over only when both clocks agree: %globaltimer (nanoseconds, kept by the
+// driver, which may step it) and the SM's own cycle counter (monotonic;
+// 1e9 cycles is 0.5 s at 1.965 GHz).  A step of one of them cannot end a
+// wait that is still honest.
 #define OMC_WAIT_LIMIT_NS 1000000000ull
+#define OMC_WAIT_LIMIT_CYCLES 1000000000ll
 
 __device__ __forceinline__ uint64_t omc_globaltimer() {
     uint64_t t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
     return t;
 }
+
+struct OmcDeadline {
+    uint64_t t0;
+    long long c0;
+    __device__ __forceinline__ void start() {
+        t0 = omc_globaltimer();
+        c0 = clock64();
+    }
+    __device__ __forceinline__ bool over() const {
+        return omc_globaltimer() - t0 > OMC_WAIT_LIMIT_NS && clock64() - c0 > OMC_WAIT_LIMIT_CYCLES;
+    }
+};
 
 // ------------------------------------------------------------- gelu_tanh --
 // engines/gemma.c:319-321, operation for operation: 0.5f*x*(1 + tanhf(c*(x +
@@ -155,11 +172,12 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t *bar, uint32_t pari
 // Bounded wait: returns false (after reporting) when the phase never flips.
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *err, int site) {
     if (mbar_try_wait(bar, parity)) return true;
-    const uint64_t t0 = omc_globaltimer();
+    OmcDeadline dl;
+    dl.start();
     for (;;) {
         for (int i = 0; i < 256; ++i)
             if (mbar_try_wait(bar, parity)) return true;
-        if (omc_globaltimer() - t0 > OMC_WAIT_LIMIT_NS) break;
+        if (dl.over()) break;
     }
     omc_dev_error(err, OMC_DEVERR_TIMEOUT, site, (int)parity);
     return false;

@@ -57,6 +57,7 @@
 #include <string.h>
 
 #include "omc_common.cuh"
+#include "omc_bounds.cuh"
 
 namespace {
 
@@ -166,15 +167,6 @@ __global__ void __launch_bounds__(256) rf_prep_kernel(const float *__restrict__ 
     }
 }
 
-// float -> unsigned key in the float order (NaN excluded by the caller)
-__device__ __forceinline__ uint32_t rf_ord(float f) {
-    const uint32_t b = __float_as_uint(f);
-    return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
-}
-__device__ __forceinline__ float rf_unord(uint32_t k) {
-    return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
-}
-
 // ---- candidates of one token (one warp) -------------------------------------
 // a_e = the sum of the GEMM's product parts; the interval [lo_e, hi_e] holds
 // the exact chain's logit (row scale and bias applied with directed rounding);
@@ -246,46 +238,7 @@ __device__ __forceinline__ int rf_token_candidates(const float *__restrict__ y, 
         lrow[e] = ap;
     }
     if (__any_sync(0xffffffffu, bad)) return -1;
-    // the k-th largest lower end: k passes of warp argmax with removal
-    uint32_t key[MAXV];
-#pragma unroll
-    for (int j = 0; j < MAXV; ++j) key[j] = lane + 32 * j < E ? rf_ord(lo[j]) : 0u;
-    uint32_t kmax = 0;
-    for (int kk = 0; kk < K; ++kk) {
-        uint32_t bk = 0;
-        int bj = 0;
-#pragma unroll
-        for (int j = 0; j < MAXV; ++j)
-            if (key[j] > bk) { bk = key[j]; bj = j; }
-        kmax = __reduce_max_sync(0xffffffffu, bk);
-        const uint32_t who = __reduce_min_sync(0xffffffffu, bk == kmax ? (uint32_t)lane : 32u);
-        if ((uint32_t)lane == who) {
-#pragma unroll
-            for (int j = 0; j < MAXV; ++j)
-                if (j == bj) key[j] = 0u;
-        }
-    }
-    float mh = -INFINITY;
-#pragma unroll
-    for (int j = 0; j < MAXV; ++j) mh = fmaxf(mh, hi[j]);
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) mh = fmaxf(mh, __shfl_xor_sync(0xffffffffu, mh, o));
-    const float kth = rf_unord(kmax);
-    // margin: a non-candidate's logit is below the k-th by more than two
-    // units in the last place of the softmax's differences plus 2^-20, so its
-    // exp value, and its probability, are strictly below the k-th
-    const float mu = __fadd_ru(1.9073486328125e-6f, __fmul_ru(4.76837158203125e-7f, __fadd_ru(fabsf(kth), fabsf(mh))));
-    const float thr = __fsub_rd(kth, mu);
-    if (kmax == 0u || __fsub_rd(kth, mh) < -60.f) return -1;
-    int nc = 0;
-#pragma unroll
-    for (int j = 0; j < MAXV; ++j) {
-        const bool c = lane + 32 * j < E && hi[j] >= thr;
-        const uint32_t m = __ballot_sync(0xffffffffu, c);
-        if (c && nc + __popc(m & ((1u << lane) - 1u)) < RF_CAPC)
-            cand[nc + __popc(m & ((1u << lane) - 1u))] = (int16_t)(lane + 32 * j);
-        nc += __popc(m);
-    }
+    const int nc = omc_topk_candidates<MAXV>(lo, hi, E, K, RF_CAPC, cand);
     return nc > RF_CAPC ? -1 : nc;
 }
 
