@@ -379,6 +379,7 @@ def run_ours(args):
 
     # per-stage device time, a diagnostic pass before the timed region
     # (profiling events between kernels, one synchronised forward at a time)
+    ob.decode_stats(reset=True)
     ob.set_profiling(True)
     st = []
     pmiss0 = layer.tier_stats(tier)[5] if tier else 0
@@ -393,6 +394,12 @@ def run_ours(args):
     bounded = (ob.router_mode() == ob.ROUTER_BOUNDED or
                (ob.router_mode() == ob.ROUTER_AUTO and E >= 128)) and T >= 16 and FAMILY != "gemma"
     router_info = {"mode": "bounded" if bounded else "exact"}
+    dstats = ob.decode_stats(reset=True)
+    if dstats["early"] + dstats["waited"]:
+        # the fused decode: forwards of the diagnostic pass whose top-k sets
+        # the logit intervals decided (streaming before the exact selection)
+        router_info["decode_sets_decided_early"] = f'{dstats["early"]}/{dstats["early"] + dstats["waited"]}'
+
     if bounded:
         router_info.update({"exact_chains_per_token": rstats["jobs"] / T, "retried_tokens": rstats["retried_tokens"],
                             "whole_tokens": rstats["whole_tokens"]})

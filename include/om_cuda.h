@@ -142,6 +142,15 @@ int omc_set_router_exact(int mode);
  * tokens retried.  Synchronises the library's stream. */
 int omc_router_stats(int *out);
 
+/* The fused decode forward (T <= 8 tokens, one launch) starts streaming the
+ * experts' weights as soon as intervals on the logits decide every token's
+ * top-k set; the exact chains, the selection's weights and order, and the
+ * combine follow.  out[0] = forwards the intervals decided, out[1] = forwards
+ * that waited for the exact selection (a near-tie at the k-th expert, a
+ * non-finite value), since the last reset; reset != 0 zeroes them.
+ * Synchronises the device. */
+int omc_decode_stats(int *out, int reset);
+
 /* Upload routed expert e of a layer into the HBM slab (re-tiled for the
  * kernels).  Row-major int8 container tensors as written by the converters
  * (tools/convert_olmoe.py:93-99): g,u [I,D], d [D,I], per-row f32 scales

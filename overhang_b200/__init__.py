@@ -97,6 +97,8 @@ SIGNATURES = {
     "omc_debug_plan_rows": (_i, [_i]),
     "omc_debug_router_tile": (_i, [_i, _i, _i]),
     "omc_debug_rf_force_retry": (_i, [_i]),
+    "omc_decode_stats": (_i, [C.POINTER(_i), _i]),
+    "omc_debug_decode_early": (_i, [_i]),
     "omc_debug_ws_copy": (_i, [_i, _vp, _sz]),
     "omc_debug_gemma_prenorm": (_i, [_i, _vp, _i, _vp, _vp, _vp]),
     "omc_debug_container_read": (C.c_longlong, [C.c_char_p, C.c_char_p, _vp, C.c_longlong]),
@@ -155,6 +157,20 @@ def router_stats() -> dict:
 def debug_rf_force_retry(on: bool) -> None:
     """Test hook: every token of a bounded pass is retried with every row exact."""
     check(lib().omc_debug_rf_force_retry(1 if on else 0), "omc_debug_rf_force_retry")
+
+
+def decode_stats(reset: bool = False) -> dict:
+    """Fused decode forwards whose top-k sets the logit intervals decided
+    ("early") and forwards that waited for the exact selection ("waited")."""
+    out = (C.c_int * 2)()
+    check(lib().omc_decode_stats(out, 1 if reset else 0), "omc_decode_stats")
+    return {"early": out[0], "waited": out[1]}
+
+
+def debug_decode_early(on: bool) -> None:
+    """Test hook: False = the fused decode waits for the exact selection
+    before streaming (the output is the same bit for bit)."""
+    check(lib().omc_debug_decode_early(1 if on else 0), "omc_debug_decode_early")
 
 
 _lib = None

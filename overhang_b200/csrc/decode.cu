@@ -2,18 +2,26 @@
 //
 // For T <= 8 tokens the block is HBM-bound on the selected experts' int8
 // weights (OLMoE T=1: 50 MB, 7.8 us at 6.4 TB/s) after a router whose exact
-// fp32 chain (D dependent adds, ~4.5 us) cannot be shortened.  One
-// cooperative launch of one CTA per SM does all of it:
+// fp32 chain (D dependent adds, ~4.5 us) cannot be shortened -- but only the
+// routing weights and order need the chain; the weight stream needs only the
+// set of selected experts.  One cooperative launch of one CTA per SM:
 //
-//  1. router: CTAs 0..nrc-1 each take rr = ceil((E + shared)/G) router rows,
-//     bulk-copy them and x in four column chunks and run the reference's
-//     chain for every (token, row) (engines/olmoe.c:74-85,
-//     engines/qwen.c:116-121: acc = RN(acc + RN(x*w)), i ascending), chunk
-//     by chunk as the copies land, then count themselves done.
-//  2. select: every CTA waits for that count and runs select_token for every
-//     token itself (softmax, top-k, renorm, shared gate: bit-exact,
-//     omc_select.cuh) into shared memory -- the same result in every CTA,
-//     with no publish hop.  CTA 0 writes the routing out.
+//  1. router: CTAs 0..nrc-1 each take rr = ceil((E + shared)/G) router rows
+//     and bulk-copy them in four column chunks.  Their select warp runs the
+//     reference's chain for every (token, row) (engines/olmoe.c:74-85,
+//     engines/qwen.c:116-121: acc = RN(acc + RN(x*w)), i ascending) as the
+//     chunks land, and counts itself done.  Meanwhile the other warps sum the
+//     same products in double, with their prefix sums, into an interval that
+//     provably holds the chain's logit (dec_interval), publish it and count.
+//  2. select: every CTA waits for the interval count and takes each token's
+//     top-k set from the intervals (omc_bounds.cuh).  When every set is
+//     decided (exactly k candidates) it plans and streams at once; the
+//     select warp then waits for the exact logits and runs select_token
+//     (softmax, top-k, renorm, shared gate: bit-exact, omc_select.cuh) beside
+//     the stream, for the combine.  A set that is not decided (a near tie at
+//     the k-th place, a non-finite value) makes every CTA wait for the exact
+//     logits and select first, as the reference does.  The select warp of
+//     CTA 0 writes the routing out.
 //  3. plan: one warp groups the routed slots by expert (ascending id, slot
 //     order inside a group: a bitmap and match masks), plus the shared expert
 //     with every token (engines/qwen.c:459-462).
@@ -37,7 +45,8 @@
 //               release flag for that tile;
 //       list B: y = sum * ds (matmul_q: acc * scale); when all of a token's
 //               k (+ shared) down segments of a row-tile pair are done, that
-//               CTA combines them in the reference's order:
+//               CTA combines them in the reference's order (the select
+//               warp's; slot positions map it onto the plan's):
 //               out = [sigmoid gate * shared] + sum_kk w_kk * y_kk
 //               (engines/olmoe.c:394-397, engines/qwen.c:486-492).
 //     A down block needs only the h tile of its 64 columns; down weights do
@@ -49,14 +58,18 @@
 // done and flags carry a per-launch tag kept in device memory, so the launch
 // can be replayed from a CUDA graph.  All CTAs are co-resident (cooperative
 // launch).
+#include "omc_bounds.cuh"
 #include "omc_select.cuh"
 #include "omc_rms.cuh"
 
 namespace {
 
 constexpr int DC_CW = 16;                       // consumer warps
-constexpr int DC_THREADS = 32 * (2 + DC_CW);    // warp 0: weight producer, warp 1: h tiles
+constexpr int DC_MT = 32 * (2 + DC_CW);         // warp 0: weight producer, warp 1: h tiles, consumers
+constexpr int DC_SELW = 2 + DC_CW;              // the select warp: exact chains and selection
+constexpr int DC_THREADS = DC_MT + 32;
 constexpr int DC_CT = 32 * DC_CW;               // consumer threads
+constexpr int DC_BW = 16;                       // warps that compute the logit intervals
 constexpr int DC_ROWS = 2 * OMC_TM;             // rows per block
 constexpr int DC_BLK = 2 * OMC_BLK_BYTES;       // one K block of a tile pair: 256 rows x 64 int8
 constexpr int DC_NCH = 4;                       // 16-column chunks of a block
@@ -72,14 +85,17 @@ constexpr int DC_HB = 4;                        // h tile ring
 // State words (ctr[]).  Flags hold launch tags and are never reset, so they
 // live at fixed places for every layer and T; the counters (zero between
 // forwards) follow at offsets that depend on the geometry.
-constexpr int CTR_EPOCH = 0, CTR_EXIT = 1, CTR_ROUTER = 2;
+constexpr int CTR_EPOCH = 0, CTR_EXIT = 1, CTR_ROUTER = 2, CTR_RFAST = 3;
+// forwards whose sets the intervals decided, and forwards that waited for the
+// exact selection (never reset by the kernel; omc_decode_stats reads them)
+constexpr int CTR_NEARLY = OMC_DEC_CTR_STATS, CTR_NFALL = OMC_DEC_CTR_STATS + 1;
+static_assert(CTR_NFALL < 8, "fixed state words");
 constexpr int CTR_HFLAG = 8;                                 // [DC_GMAX][DC_TILES_MAX] h tile published
 constexpr int CTR_FIXED = CTR_HFLAG + DC_GMAX * DC_TILES_MAX;
 
 struct DecArgs {
     omc_layer_dev L;
     const float *x;       // the input rows (GEMMA: the residual rows, normed here)
-    const float *xr;      // the rows the router CTAs stage (x)
     int T;
     int32_t *topk_idx;
     float *topk_w, *logits;
@@ -92,9 +108,13 @@ struct DecArgs {
     int *ctr;
     int offSA, offSB, offC;
     int *err;
-    int ns;               // ring stages
+    int ns;               // ring stages (the reserved router slots follow them)
     int ldx;              // smem stride of a token row of x (floats)
     int rr, nrc;          // router rows per router CTA, router CTAs
+    int nres;             // reserved slots: router rows (+ Gemma's router input), select scratch
+    float2 *rbnd;         // [T][E] interval of each routed logit (bias included)
+    int bnw;              // warps per interval team
+    int early;            // 1: stream as soon as the intervals decide every token's set
 };
 
 __device__ __forceinline__ int ld_acquire(const int *p) {
@@ -114,6 +134,8 @@ __device__ __forceinline__ void red_release_add(int *p, int v) {
 // the sequentially consistent fence of __threadfence().
 __device__ __forceinline__ void fence_acqrel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
 __device__ __forceinline__ void cons_bar() { asm volatile("bar.sync 1, %0;" ::"n"(DC_CT) : "memory"); }
+// every warp but the select warp
+__device__ __forceinline__ void main_bar() { asm volatile("bar.sync 2, %0;" ::"n"(DC_MT) : "memory"); }
 
 __device__ __forceinline__ void cp_async16(void *smem_dst, const void *gsrc) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)), "l"(gsrc) : "memory");
@@ -148,6 +170,52 @@ __device__ __forceinline__ void mbar_wait_s(uint64_t *bar, uint32_t parity, int 
             return;
         }
     }
+}
+
+// Bounded wait for a shared-memory flag another warp of the CTA sets.
+__device__ bool wait_smem_flag(volatile int *f, int *err, int detail) {
+    if (*f) return true;
+    OmcDeadline dl;
+    dl.start();
+    for (;;) {
+        __nanosleep(64);
+        if (*f) return true;
+        if (*(volatile int *)err != 0) return false;
+        if (dl.over()) {
+            omc_dev_error(err, OMC_DEVERR_TIMEOUT, OMC_SITE_DECODE, detail);
+            return false;
+        }
+    }
+}
+
+// The interval that holds the reference's chain acc = RN(acc + p_j), j = 0..D-1
+// (p_j = RN(x_j * w_j), the products the chain adds), from one pass of
+// double sums over the same products:
+//   c  ~ S_D, the exact sum of the p_j;   B ~ sum_j |S_j| (prefix sums);
+//   P >= sum_j |p_j| (float, rounded up).
+// Each chain add rounds with |err_j| <= u |acc_j| (u = 2^-24), so the chain
+// is within u * sum_j |acc_j| <= u B' / (1 - D u) of S_D, where B' bounds
+// sum_j |S_j|; every double partial sum here is within (D + 64) 2^-52 P of
+// its exact value, which bounds both |c - S_D| and B' - B / D.  A subnormal
+// partial sum adds at most 2^-150 per add.  The router's int8 row scale and
+// the bias then widen the ends with directed rounding.
+__device__ float2 dec_interval(double c, double B, float P, int D, const float *scale, const float *bias) {
+    const double u = 5.9604644775390625e-08, Dd = (double)D;
+    const double em = __dmul_ru(__dmul_ru(Dd + 64.0, 2.220446049250313e-16), (double)P);
+    const double Bp = __dadd_ru(B, __dmul_ru(Dd, em));
+    double beta = __dmul_ru(__dmul_ru(u, Bp), __dadd_ru(1.0, __dmul_ru(2.0 * Dd, u)));
+    beta = __dadd_ru(__dadd_ru(beta, em), __dmul_ru(Dd, 7.006492321624085e-46));
+    float lo = __double2float_rd(__dsub_rd(c, beta)), hi = __double2float_ru(__dadd_ru(c, beta));
+    if (scale) {
+        const float s = *scale, l = lo;
+        lo = s >= 0.f ? __fmul_rd(lo, s) : __fmul_rd(hi, s);
+        hi = s >= 0.f ? __fmul_ru(hi, s) : __fmul_ru(l, s);
+    }
+    if (bias) {
+        lo = __fadd_rd(lo, *bias);
+        hi = __fadd_ru(hi, *bias);
+    }
+    return make_float2(lo, hi);
 }
 
 // pointer words of the expert table in shared memory (5 per expert, even count)
@@ -251,7 +319,7 @@ __global__ void __launch_bounds__(DC_THREADS, 1) decode_moe_kernel(const DecArgs
     // dynamic shared memory: ring | x [T][ldx] | h tiles [HB][T][128] |
     // chunk partials [T][4][256] | own piece [T][256] | expert table | barriers
     uint8_t *ring = dsm;
-    float *xs = reinterpret_cast<float *>(dsm + (size_t)a.ns * DC_BLK);
+    float *xs = reinterpret_cast<float *>(dsm + (size_t)(a.ns + a.nres) * DC_BLK);
     float *hsm = xs + (size_t)T * a.ldx;
     float *xch = hsm + (size_t)DC_HB * T * OMC_TM;
     float *xown = xch + (size_t)T * DC_NCH * DC_ROWS;
@@ -271,12 +339,21 @@ __global__ void __launch_bounds__(DC_THREADS, 1) decode_moe_kernel(const DecArgs
     __shared__ int s_epoch, s_abort, s_ngr, s_np;
     __shared__ float s_r[DC_TMAX];                              // GEMMA: each token's rms factor
     __shared__ int s_comb[DC_TMAX];
+    // the reference's selection (the select warp): indices, weights, shared
+    // gates, and where each selected expert's y lies among the plan's slots
+    __shared__ int s_xidx[DC_SLOTS_MAX], s_pos[DC_SLOTS_MAX];
+    __shared__ float s_xw[DC_SLOTS_MAX], s_xsg[DC_TMAX];
+    __shared__ int s_det[DC_TMAX], s_planned, s_seldone;
+    __shared__ double s_bt[DC_BW], s_bb[DC_BW];                 // interval teams: warp totals, sum |S_j|
+    __shared__ float s_bp[DC_BW];                               // and sum |p_j|
     int *ctr = a.ctr;
     const bool router = c < a.nrc;
 
     if (tid == 0) {
         s_epoch = *(volatile int *)(ctr + CTR_EPOCH);
         s_abort = 0;
+        s_planned = 0;
+        s_seldone = 0;
         for (int i = 0; i < a.ns; ++i) {
             mbar_init(&full[i], 1);
             mbar_init(&empty[i], DC_CW);
@@ -289,29 +366,33 @@ __global__ void __launch_bounds__(DC_THREADS, 1) decode_moe_kernel(const DecArgs
         fence_barrier_init();
     }
     // ---- 1. x (every CTA) and the router rows (router CTAs) ---------------
-    const int rr = a.rr, r0 = c * rr, ldw = D_pad + 4, nrows = E + hsh;
-    float *wsm = reinterpret_cast<float *>(ring);
-    if (router) {
-        if (tid == 0) {   // (the barriers above are this thread's own: no sync needed)
-            const int cw = D / DC_RCH, nr = min(rr, nrows - r0);
-            for (int ch = 0; ch < DC_RCH; ++ch) {
-                mbar_arrive_expect_tx(&rbar[ch], (uint32_t)((T + nr) * cw * 4));
+    // A router CTA stages its rows (and, for Gemma, the token rows it scales
+    // into the router's input) in the reserved slots after the ring: its
+    // chains run on there while the ring streams the experts' weights.
+    const int rr = a.rr, r0 = c * rr, ldw = a.ldx, nrows = E + hsh;
+    const bool gemma = L.family == OMC_FAMILY_GEMMA;
+    float *rws = reinterpret_cast<float *>(ring + (size_t)a.ns * DC_BLK);     // [rr][ldw] router rows
+    float *rxs = gemma ? rws + (size_t)rr * ldw : xs;                          // [T][ldw] the router's input
+    float *selscr = rws + (size_t)(rr + (gemma ? T : 0)) * ldw;                // the select warp's scratch
+    if (router && tid == 0) {   // (the barriers above are this thread's own: no sync needed)
+        const int cw = D / DC_RCH, nr = min(rr, nrows - r0);
+        for (int ch = 0; ch < DC_RCH; ++ch) {
+            mbar_arrive_expect_tx(&rbar[ch], (uint32_t)(((gemma ? T : 0) + nr) * cw * 4));
+            if (gemma)
                 for (int t = 0; t < T; ++t)
-                    bulk_g2s(xs + (size_t)t * a.ldx + ch * cw, a.xr + (size_t)t * D + ch * cw, cw * 4, &rbar[ch]);
-                for (int r = 0; r < nr; ++r) {
-                    const int gr = r0 + r;
-                    const float *src = gr < E ? L.router + (size_t)gr * D : L.sh_gate;
-                    bulk_g2s(wsm + (size_t)r * ldw + ch * cw, src + ch * cw, cw * 4, &rbar[ch]);
-                }
+                    bulk_g2s(rxs + (size_t)t * ldw + ch * cw, a.x + (size_t)t * D + ch * cw, cw * 4, &rbar[ch]);
+            for (int r = 0; r < nr; ++r) {
+                const int gr = r0 + r;
+                const float *src = gr < E ? L.router + (size_t)gr * D : L.sh_gate;
+                bulk_g2s(rws + (size_t)r * ldw + ch * cw, src + ch * cw, cw * 4, &rbar[ch]);
             }
         }
-    } else {
-        for (int i = tid; i < T * (D / 4); i += DC_THREADS) {
-            const int t = i / (D / 4), col = (i - t * (D / 4)) * 4;
-            cp_async16(xs + (size_t)t * a.ldx + col, a.x + (size_t)t * D + col);
-        }
-        asm volatile("cp.async.commit_group;" ::: "memory");
     }
+    for (int i = tid; i < T * (D / 4); i += DC_THREADS) {
+        const int t = i / (D / 4), col = (i - t * (D / 4)) * 4;
+        cp_async16(xs + (size_t)t * a.ldx + col, a.x + (size_t)t * D + col);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
     for (int e = tid; e <= E; e += DC_THREADS) {
         const omc_expert_ptrs *P = L.experts + e;
         ptab[5 * e] = P->g;
@@ -326,87 +407,214 @@ __global__ void __launch_bounds__(DC_THREADS, 1) decode_moe_kernel(const DecArgs
         const int t = i / (D_pad - D), col = D + (i - t * (D_pad - D));
         xs[(size_t)t * a.ldx + col] = 0.f;
     }
-    const bool gemma = L.family == OMC_FAMILY_GEMMA;
-    // GEMMA: x is the residual row.  Each CTA takes every token's rms factor
-    // from its own copy (warp t, token t; omc_rms.cuh) and scales the copy
-    // into the router's input (router CTAs) or the experts' input.
-    auto gemma_factors = [&]() {
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    __syncthreads();   // every thread's copies of x have landed
+    if (gemma) {
+        // x is the residual row.  Each CTA takes every token's rms factor
+        // from its copy (warp t, token t; omc_rms.cuh); the router's input is
+        // (x*r)*router_scale*rroot (router CTAs), the experts' input
+        // (x*r)*pre_feedforward_layernorm_2
         if (warp < T) {
             const float r = omc_gemma_rms_factor(xs + (size_t)warp * a.ldx, D, L.eps);
             if (lane == 0) s_r[warp] = r;
         }
-    };
-    auto gemma_scale = [&](const float *__restrict__ w) {   // xs = (x*r)*w, x the staged rows
+        __syncthreads();
+        if (router) {
+            for (int ch = 0; ch < DC_RCH; ++ch) mbar_wait(&rbar[ch], 0, a.err, OMC_SITE_DECODE);
+            for (int i = tid; i < T * D; i += DC_THREADS) {
+                const int t = i / D, col = i - t * D;
+                float *v = rxs + (size_t)t * ldw + col;
+                *v = __fmul_rn(__fmul_rn(*v, s_r[t]), L.g_s2[col]);
+            }
+        }
         for (int i = tid; i < T * D; i += DC_THREADS) {
             const int t = i / D, col = i - t * D;
             float *v = xs + (size_t)t * a.ldx + col;
-            *v = __fmul_rn(__fmul_rn(*v, s_r[t]), w ? w[col] : 1.f);
+            *v = __fmul_rn(__fmul_rn(*v, s_r[t]), L.g_en ? L.g_en[col] : 1.f);
         }
-    };
-    if (router) {
-        if (gemma) {
-            // the chains need the scaled row: every chunk first
-            if (warp < T)
-                for (int ch = 0; ch < DC_RCH; ++ch) mbar_wait(&rbar[ch], 0, a.err, OMC_SITE_DECODE);
-            gemma_factors();
-            __syncthreads();
-            gemma_scale(L.g_s2);
-            __syncthreads();
-        }
-        if (tid < T * rr) {
-            // the chain (about 5.5 cycles an element: the add latency plus
-            // the loads and products it cannot hide)
-            const int t = tid / rr, r = tid - t * rr, gr = r0 + r;
-            const float *xr = xs + (size_t)t * a.ldx, *wr = wsm + (size_t)r * ldw;
-            const int cw = D / DC_RCH;
-            float acc = 0.f;
-            for (int ch = 0; ch < DC_RCH; ++ch) {
-                mbar_wait(&rbar[ch], 0, a.err, OMC_SITE_DECODE);
+        __syncthreads();
+    }
+
+    if (warp == DC_SELW) {
+        // ---- the select warp: this CTA's exact chains (the reference's
+        // order, engines/olmoe.c:74-85, engines/qwen.c:116-121; about 5.5
+        // cycles an element), then the reference's selection of every token
+        // from the exact logits, while the other warps stream.  The combine
+        // takes its weights, order and shared gates from here.
+        if (router) {
+            if (lane < T * rr) {
+                const int t = lane / rr, r = lane - t * rr, gr = r0 + r;
+                const float *xr = rxs + (size_t)t * ldw, *wr = rws + (size_t)r * ldw;
+                const int cw = D / DC_RCH;
+                float acc = 0.f;
+                for (int ch = 0; ch < DC_RCH; ++ch) {
+                    mbar_wait(&rbar[ch], 0, a.err, OMC_SITE_DECODE);
 #pragma unroll 8
-                for (int col = ch * cw; col < (ch + 1) * cw; col += 4) {
-                    const float4 xv = *reinterpret_cast<const float4 *>(xr + col);
-                    const float4 wv = *reinterpret_cast<const float4 *>(wr + col);
-                    acc = __fadd_rn(acc, __fmul_rn(xv.x, wv.x));
-                    acc = __fadd_rn(acc, __fmul_rn(xv.y, wv.y));
-                    acc = __fadd_rn(acc, __fmul_rn(xv.z, wv.z));
-                    acc = __fadd_rn(acc, __fmul_rn(xv.w, wv.w));
+                    for (int col = ch * cw; col < (ch + 1) * cw; col += 4) {
+                        const float4 xv = *reinterpret_cast<const float4 *>(xr + col);
+                        const float4 wv = *reinterpret_cast<const float4 *>(wr + col);
+                        acc = __fadd_rn(acc, __fmul_rn(xv.x, wv.x));
+                        acc = __fadd_rn(acc, __fmul_rn(xv.y, wv.y));
+                        acc = __fadd_rn(acc, __fmul_rn(xv.z, wv.z));
+                        acc = __fadd_rn(acc, __fmul_rn(xv.w, wv.w));
+                    }
+                }
+                if (gr < nrows)
+                    a.logits[(size_t)t * a.ldl + gr] = (L.router_i8 && gr < E) ? __fmul_rn(acc, L.router_s[gr]) : acc;
+            }
+            __syncwarp();
+            if (lane == 0) {
+                fence_acqrel_gpu();
+                red_release_add(ctr + CTR_ROUTER, 1);
+            }
+        }
+        int ok = 1;
+        if (lane == 0) ok = wait_value(ctr + CTR_ROUTER, a.nrc, a.err, -1);
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        if (ok)
+            for (int t = 0; t < T; ++t)
+                select_token<NV>(a.logits, a.ldl, t, E, K, L.family, L.renorm, L.has_shared, L.g_pes, L.rbias, s_xidx,
+                                 s_xw, s_xsg, a.err, selscr);
+        // the plan's slots: the interval sets (experts in ascending id) or
+        // these same indices; map each selected expert to its slot
+        if (lane == 0) wait_smem_flag(&s_planned, a.err, -3);
+        __syncwarp();
+        __threadfence_block();
+        const bool use = ok && !s_abort;
+        for (int i = lane; i < nslots; i += 32) {
+            const int t = i / K;
+            int pos = i - t * K;
+            if (use) {
+                int f = -1;
+                for (int j = 0; j < K; ++j)
+                    if (s_tidx[t * K + j] == s_xidx[i]) f = j;
+                if (f < 0) omc_dev_error(a.err, OMC_DEVERR_ROUTE, OMC_SITE_DECODE, i);
+                else pos = f;
+                if (c == 0) {
+                    a.topk_idx[i] = s_xidx[i];
+                    a.topk_w[i] = s_xw[i];
                 }
             }
-            if (gr < nrows)
-                a.logits[(size_t)t * a.ldl + gr] = (L.router_i8 && gr < E) ? __fmul_rn(acc, L.router_s[gr]) : acc;
+            s_pos[i] = pos;
         }
-        __syncthreads();   // this CTA's logits are written; x chunks have landed
+        __syncwarp();
+        __threadfence_block();
+        if (lane == 0) *(volatile int *)&s_seldone = 1;
+    } else {
+    if (router) {
+        // ---- intervals of this CTA's routed logits: teams of a.bnw warps, one
+        // (token, row) pair a team; a thread sums a contiguous run of the
+        // products in double, the team scans the runs (prefix sums S_j)
+        const int np = T * rr, nw = a.bnw, nteam = DC_BW / nw;
+        const int team = warp < DC_BW ? warp / nw : -1, wq = warp - (team < 0 ? 0 : team) * nw;
+        const int nq = 32 * nw, q = wq * 32 + lane;
+        bool landed = false;
+        for (int b0 = 0; b0 < np; b0 += nteam) {
+            const int b = b0 + team;
+            const bool act = team >= 0 && b < np;   // warp-uniform
+            const int t = act ? b / rr : 0, r = act ? b - t * rr : 0, gr = r0 + r;
+            const float *xv = rxs + (size_t)t * ldw, *wv = rws + (size_t)r * ldw;
+            const int j0 = (int)((long long)q * D / nq), j1 = (int)((long long)(q + 1) * D / nq);
+            if (act && !landed) {
+                for (int ch = 0; ch < DC_RCH; ++ch) mbar_wait(&rbar[ch], 0, a.err, OMC_SITE_DECODE);
+                landed = true;
+            }
+            double loc = 0.0;
+            float pab = 0.f;
+            if (act)
+                for (int j = j0; j < j1; ++j) {
+                    const float p = __fmul_rn(xv[j], wv[j]);
+                    loc = __dadd_rn(loc, (double)p);
+                    pab = __fadd_ru(pab, fabsf(p));
+                }
+            double inc = loc;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const double v = __shfl_up_sync(0xffffffffu, inc, o);
+                if (lane >= o) inc = __dadd_rn(inc, v);
+            }
+            if (act && lane == 31) s_bt[warp] = inc;
+            main_bar();
+            double babs = 0.0;
+            const double ex = __shfl_up_sync(0xffffffffu, inc, 1);
+            if (act) {
+                double sp = 0.0;
+                for (int w2 = team * nw; w2 < warp; ++w2) sp = __dadd_rn(sp, s_bt[w2]);
+                if (lane > 0) sp = __dadd_rn(sp, ex);
+                for (int j = j0; j < j1; ++j) {
+                    sp = __dadd_rn(sp, (double)__fmul_rn(xv[j], wv[j]));
+                    babs = __dadd_ru(babs, fabs(sp));
+                }
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                babs = __dadd_ru(babs, __shfl_xor_sync(0xffffffffu, babs, o));
+                pab = __fadd_ru(pab, __shfl_xor_sync(0xffffffffu, pab, o));
+            }
+            if (act && lane == 0) {
+                s_bb[warp] = babs;
+                s_bp[warp] = pab;
+            }
+            main_bar();
+            if (act && wq == 0 && lane == 0 && gr < E) {
+                double B = 0.0, cs = 0.0;
+                float P = 0.f;
+                for (int w2 = team * nw; w2 < team * nw + nw; ++w2) {
+                    B = __dadd_ru(B, s_bb[w2]);
+                    P = __fadd_ru(P, s_bp[w2]);
+                    cs = __dadd_rn(cs, s_bt[w2]);
+                }
+                a.rbnd[(size_t)t * E + gr] = dec_interval(cs, B, P, D, L.router_i8 ? L.router_s + gr : nullptr,
+                                                          L.rbias ? L.rbias + gr : nullptr);
+            }
+            main_bar();   // s_bt, s_bb are the next round's
+        }
         if (tid == 0) {
             fence_acqrel_gpu();
-            red_release_add(ctr + CTR_ROUTER, 1);
-        }
-        if (gemma) {
-            // the experts' input replaces the router's (columns D.. stay zero):
-            // (x*r)*pre_feedforward_layernorm_2 from the residual rows in HBM
-            for (int i = tid; i < T * D; i += DC_THREADS) {
-                const int t = i / D, col = i - t * D;
-                xs[(size_t)t * a.ldx + col] =
-                    __fmul_rn(__fmul_rn(__ldg(a.x + (size_t)t * D + col), s_r[t]), L.g_en ? L.g_en[col] : 1.f);
-            }
-        }
-    } else {
-        asm volatile("cp.async.wait_group 0;" ::: "memory");
-        if (gemma) {
-            __syncthreads();   // every thread's copies of the rows have landed
-            gemma_factors();
-            __syncthreads();
-            gemma_scale(L.g_en);
+            red_release_add(ctr + CTR_RFAST, 1);
         }
     }
 
-    // ---- 2. every router CTA done -> select, in every CTA ---------------------
-    if (tid == 0 && !wait_value(ctr + CTR_ROUTER, a.nrc, a.err, -1)) s_abort = 1;
-    __syncthreads();
-    if (!s_abort && warp < T)
-        select_token<NV>(a.logits, a.ldl, warp, E, K, L.family, L.renorm, L.has_shared, L.g_pes, L.rbias, s_tidx, s_tw,
-                         s_sg, a.err,
-                         reinterpret_cast<float *>(ring) + warp * NV * 32);
-    __syncthreads();
+    // ---- 2. every token's top-k set from the intervals, in every CTA: with
+    // exactly k candidates (omc_bounds.cuh) the set is the reference's, and
+    // the weights and order can wait for the select warp.  Otherwise the
+    // reference's selection from the exact logits, here, first.
+    if (tid == 0 && !wait_value(ctr + CTR_RFAST, a.nrc, a.err, -1)) s_abort = 1;
+    main_bar();
+    if (!s_abort && warp < T) {
+        float lo[NV], hi[NV];
+        bool bad = false;
+#pragma unroll
+        for (int j = 0; j < NV; ++j) {
+            const int e = lane + 32 * j;
+            lo[j] = hi[j] = -INFINITY;
+            if (e < E) {
+                const float2 v = __ldcg(a.rbnd + (size_t)warp * E + e);
+                lo[j] = v.x;
+                hi[j] = v.y;
+                bad |= !(fabsf(v.x) < 1e30f) || !(fabsf(v.y) < 1e30f);
+            }
+        }
+        int nc = -1;
+        if (!__any_sync(0xffffffffu, bad)) nc = omc_topk_candidates<NV>(lo, hi, E, K, K, s_tidx + warp * K);
+        if (lane == 0) s_det[warp] = nc == K;
+    }
+    main_bar();
+    bool early = a.early != 0;
+    for (int t = 0; t < T; ++t) early = early && s_det[t] != 0;
+    if (c == 0 && tid == 0 && !s_abort) atomicAdd(ctr + (early ? CTR_NEARLY : CTR_NFALL), 1);
+    if (!s_abort && !early) {
+        if (tid == 0 && !wait_value(ctr + CTR_ROUTER, a.nrc, a.err, -1)) s_abort = 1;
+        main_bar();
+        if (!s_abort && warp < T)
+            select_token<NV>(a.logits, a.ldl, warp, E, K, L.family, L.renorm, L.has_shared, L.g_pes, L.rbias, s_tidx,
+                             s_tw, s_sg, a.err, reinterpret_cast<float *>(ring) + warp * NV * 32);
+        main_bar();
+    }
+    if (tid == 0) {
+        __threadfence_block();
+        *(volatile int *)&s_planned = 1;   // s_tidx is final (the select warp maps onto it)
+    }
 
     // ---- 3. plan (one warp): groups in ascending expert id ---------------------
     if (warp == 0 && !s_abort) {
@@ -477,14 +685,8 @@ __global__ void __launch_bounds__(DC_THREADS, 1) decode_moe_kernel(const DecArgs
             }
         }
     }
-    if (c == 0 && warp == 1 && !s_abort) {
-        for (int i = lane; i < nslots; i += 32) {
-            a.topk_idx[i] = s_tidx[i];
-            a.topk_w[i] = s_tw[i];
-        }
-    }
-    fence_proxy_async_smem();   // router staging / select scratch (generic) before bulk copies into the ring
-    __syncthreads();
+    fence_proxy_async_smem();   // select scratch (generic) before bulk copies into the ring
+    main_bar();
 
     Lists W;
     W.ngr = s_ngr;
@@ -558,6 +760,7 @@ __global__ void __launch_bounds__(DC_THREADS, 1) decode_moe_kernel(const DecArgs
         const int ci = tid - 64, cw = ci >> 5, ch = cw >> 2, r = (cw & 3) * 32 + lane;
         float2 acc0[TM], acc1[TM];
         RingPos rp{0, 0}, hp{0, 0};
+        bool sel_seen = false;   // the select warp's results are in shared memory
 
         // rows r and r + 128 of chunk ch of the next block, dequantised; then
         // the slot is released (every loaded word is used before the arrive)
@@ -735,38 +938,49 @@ __global__ void __launch_bounds__(DC_THREADS, 1) decode_moe_kernel(const DecArgs
                 if (ci == 0) {
                     fence_acqrel_gpu();
                     const int nsl = K + hsh;
+                    bool any = false;
                     for (int j = 0; j < n; ++j) {
                         int *cc = ctr + a.offC + s_gtok[g * DC_TMAX + j] * W.npair + p;
                         const int old = atomicAdd(cc, 1);
                         s_comb[j] = old + 1 == nsl;
+                        any |= s_comb[j] != 0;
                         if (s_comb[j]) *cc = 0;
                     }
                     fence_acqrel_gpu();
+                    if (any && !sel_seen) {
+                        wait_smem_flag(&s_seldone, a.err, -4);
+                        __threadfence_block();
+                        sel_seen = true;
+                    }
                 }
                 cons_bar();
                 // tokens whose every y of these rows is written: combine in the
-                // reference's order
+                // reference's order (the select warp's order and weights; the
+                // y of selected expert kk is at the plan's slot s_pos)
                 for (int q = ci; q < n * DC_ROWS; q += DC_CT) {
                     const int j = q >> 8, rw = q & (DC_ROWS - 1), d = p * DC_ROWS + rw;
                     if (!s_comb[j] || d >= D) continue;
                     const int t = s_gtok[g * DC_TMAX + j];
                     const float *yt = a.ybuf + (size_t)t * (K + 1) * D + d;
                     float o = 0.f;
-                    if (L.has_shared) o = __fmul_rn(__ldcg(yt + (size_t)K * D), s_sg[t]);
-                    for (int kk = 0; kk < K; ++kk) o = __fadd_rn(o, __fmul_rn(s_tw[t * K + kk], __ldcg(yt + (size_t)kk * D)));
+                    if (L.has_shared) o = __fmul_rn(__ldcg(yt + (size_t)K * D), s_xsg[t]);
+                    for (int kk = 0; kk < K; ++kk)
+                        o = __fadd_rn(o, __fmul_rn(s_xw[t * K + kk], __ldcg(yt + (size_t)s_pos[t * K + kk] * D)));
                     a.out[(size_t)t * D + d] = o;
                 }
             }
         }
     }
+    }   // the main warps
 
-    // ---- exit: the last CTA resets the router count, advances the tag -----
+    // ---- exit: the last CTA resets the router counts, advances the tag ----
     __syncthreads();
     if (tid == 0) {
         fence_acqrel_gpu();
         if (atomicAdd(ctr + CTR_EXIT, 1) == G - 1) {
             atomicExch(ctr + CTR_EXIT, 0);
             atomicExch(ctr + CTR_ROUTER, 0);
+            atomicExch(ctr + CTR_RFAST, 0);
             fence_acqrel_gpu();
             atomicExch(ctr + CTR_EPOCH, tag);
         }
@@ -774,10 +988,17 @@ __global__ void __launch_bounds__(DC_THREADS, 1) decode_moe_kernel(const DecArgs
 }
 
 struct DecGeom {
-    int G, ns, ldx, rr, nrc;
+    int G, ns, nres, ldx, rr, nrc, bnw;
     int offSA, offSB, offC, nctr;
-    size_t smem, partA_floats, partB_floats;
+    size_t smem, partA_floats, partB_floats, rbnd_floats;
 };
+
+// ceil(E / 32) rounded up to a power of two: the select template's NV
+static int dec_nv(int E) {
+    int nv = 1;
+    while (nv * 32 < E) nv *= 2;
+    return nv;
+}
 
 constexpr size_t DC_SMEM_MAX = 216 * 1024;   // dynamic; the static plan needs the rest of 227 KiB
 
@@ -790,24 +1011,34 @@ static int dec_geometry(const omc_layer_dev *L, int T, int G, DecGeom *g) {
         return OMC_EUNSUPPORTED;   // (a segment has at most DC_NPMAX pieces: one K block each)
     g->G = G;
     g->ldx = L->D_pad + 4;
-    const size_t fixed = (size_t)T * g->ldx * 4 + (size_t)DC_HB * T * OMC_TM * 4 +
-                         (size_t)T * DC_NCH * DC_ROWS * 4 + (size_t)T * DC_ROWS * 4 + (size_t)dc_ptab_words(L->E) * 8 +
-                         (DC_RCH + 2 * DC_HB) * 8;
-    if (fixed + 4 * ((size_t)DC_BLK + 16) > DC_SMEM_MAX) return OMC_EUNSUPPORTED;
-    int ns = (int)((DC_SMEM_MAX - fixed) / (DC_BLK + 16));
-    if (ns > 12) ns = 12;
-    g->ns = ns;
-    g->smem = (size_t)ns * DC_BLK + fixed + (size_t)2 * ns * 8;
     const int nrows = L->E + (L->has_shared ? 1 : 0);
     g->rr = (nrows + G - 1) / G;
     g->nrc = (nrows + g->rr - 1) / g->rr;
-    if ((size_t)g->rr * (L->D_pad + 4) * 4 > (size_t)ns * DC_BLK) return OMC_EUNSUPPORTED;
+    if (T * g->rr > 32 || (L->D % 32)) return OMC_EUNSUPPORTED;   // chains: one select-warp lane each
+    const size_t fixed = (size_t)T * g->ldx * 4 + (size_t)DC_HB * T * OMC_TM * 4 +
+                         (size_t)T * DC_NCH * DC_ROWS * 4 + (size_t)T * DC_ROWS * 4 + (size_t)dc_ptab_words(L->E) * 8 +
+                         (DC_RCH + 2 * DC_HB) * 8;
+    // reserved slots after the ring: the router rows, Gemma's router input,
+    // the select warp's scratch
+    const size_t rbytes = ((size_t)g->rr + (L->family == OMC_FAMILY_GEMMA ? T : 0)) * g->ldx * 4 +
+                          (size_t)dec_nv(L->E) * 32 * 4;
+    g->nres = (int)((rbytes + DC_BLK - 1) / DC_BLK);
+    if (fixed + (size_t)g->nres * DC_BLK + 4 * ((size_t)DC_BLK + 16) > DC_SMEM_MAX) return OMC_EUNSUPPORTED;
+    int ns = (int)((DC_SMEM_MAX - fixed - (size_t)g->nres * DC_BLK) / (DC_BLK + 16));
+    if (ns > 12) ns = 12;
+    g->ns = ns;
+    g->smem = (size_t)(ns + g->nres) * DC_BLK + fixed + (size_t)2 * ns * 8;
+    // interval teams: DC_BW warps split over the T * rr (token, row) pairs
+    int p2 = 1;
+    while (p2 < T * g->rr) p2 *= 2;
+    g->bnw = p2 >= DC_BW ? 1 : DC_BW / p2;
     // worst-case lists: every slot its own expert
     const int gmax = (T * L->k < L->E ? T * L->k : L->E);
     const int ntr = L->I_rows / OMC_TM, nts = L->has_shared ? L->Is_rows / OMC_TM : 0;
     const int npair = (L->D_rows / OMC_TM + 1) / 2;
     g->partA_floats = (size_t)G * T * DC_ROWS;
     g->partB_floats = (size_t)G * T * DC_ROWS;
+    g->rbnd_floats = (size_t)2 * T * L->E;
     const int nsegA = gmax * ntr + nts, nsegB = (gmax + 1) * npair;
     g->offSA = CTR_FIXED;
     g->offSB = g->offSA + nsegA;
@@ -843,6 +1074,17 @@ static int launch_nv(const DecArgs &a, const DecGeom &g, cudaStream_t s) {
 
 }  // namespace
 
+int omc_decode_early = 1;
+
+// Test hook: 0 = the fused decode waits for the exact selection before it
+// streams, whatever the intervals decide (the output is the same bit for bit).
+extern "C" int omc_debug_decode_early(int on) {
+    if (on != 0 && on != 1) return OMC_EINVAL;
+    omc_decode_early = on;
+    omc_graphs_invalidate();
+    return 0;
+}
+
 // Sizes of the decode state (counters and pieces) that serve every T <= 8
 // for this layer on a grid of G CTAs.
 extern "C" int omc_decode_state_size(const omc_layer_dev *L, int G, size_t *ctr_ints, size_t *part_floats) {
@@ -853,7 +1095,7 @@ extern "C" int omc_decode_state_size(const omc_layer_dev *L, int G, size_t *ctr_
         if (dec_geometry(L, T, G, &g)) continue;
         any = 1;
         if ((size_t)g.nctr > ci) ci = (size_t)g.nctr;
-        if (g.partA_floats + g.partB_floats > pf) pf = g.partA_floats + g.partB_floats;
+        if (g.partA_floats + g.partB_floats + g.rbnd_floats > pf) pf = g.partA_floats + g.partB_floats + g.rbnd_floats;
     }
     *ctr_ints = ci;
     *part_floats = pf;
@@ -864,20 +1106,20 @@ extern "C" int omc_decode_state_size(const omc_layer_dev *L, int G, size_t *ctr_
 extern "C" int omc_decode_supported(const omc_layer_dev *L, int T, int G, size_t ctr_ints, size_t part_floats) {
     DecGeom g;
     if (dec_geometry(L, T, G, &g)) return 0;
-    return (size_t)g.nctr <= ctr_ints && g.partA_floats + g.partB_floats <= part_floats;
+    return (size_t)g.nctr <= ctr_ints && g.partA_floats + g.partB_floats + g.rbnd_floats <= part_floats;
 }
 
 extern "C" int omc_launch_decode(const omc_layer_dev *L, const float *x, const float *xr, int T, const omc_ws *ws,
                                  int G, int *ctr, float *part, int32_t *topk_idx, float *topk_w, float *out,
                                  cudaStream_t s) {
     if (T <= 0) return 0;
+    if (xr && xr != x) return OMC_EINVAL;   // the router's input is the experts' (Gemma: both from x)
     DecGeom g;
     int rc;
     if ((rc = dec_geometry(L, T, G, &g))) return rc;
     DecArgs a;
     a.L = *L;
     a.x = x;
-    a.xr = xr ? xr : x;
     a.T = T;
     a.topk_idx = topk_idx;
     a.topk_w = topk_w;
@@ -895,9 +1137,13 @@ extern "C" int omc_launch_decode(const omc_layer_dev *L, const float *x, const f
     a.offC = g.offC;
     a.err = ws->err;
     a.ns = g.ns;
+    a.nres = g.nres;
     a.ldx = g.ldx;
     a.rr = g.rr;
     a.nrc = g.nrc;
+    a.rbnd = reinterpret_cast<float2 *>(part + g.partA_floats + g.partB_floats);
+    a.bnw = g.bnw;
+    a.early = omc_decode_early;
     const int nv = (L->E + 31) / 32;
     if (nv <= 1) rc = launch_nv<1>(a, g, s);
     else if (nv <= 2) rc = launch_nv<2>(a, g, s);

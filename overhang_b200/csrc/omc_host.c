@@ -819,6 +819,20 @@ int omc_router_stats(int *out) {
     return OMC_OK;
 }
 
+int omc_decode_stats(int *out, int reset) {
+    if (!G.init) return omc_fail(OMC_ENOINIT, "omc_decode_stats: omc_init not called");
+    if (!out) return omc_fail(OMC_EINVAL, "omc_decode_stats: null pointer");
+    out[0] = out[1] = 0;
+    if (!G.dec_ctr) return OMC_OK;
+    CK(cudaDeviceSynchronize());   /* the decode may have run on a caller's stream */
+    CK(cudaMemcpy(out, G.dec_ctr + OMC_DEC_CTR_STATS, sizeof(int) * 2, cudaMemcpyDeviceToHost));
+    if (reset) {
+        CK(cudaMemsetAsync(G.dec_ctr + OMC_DEC_CTR_STATS, 0, sizeof(int) * 2, G.stream));
+        CK(cudaStreamSynchronize(G.stream));
+    }
+    return OMC_OK;
+}
+
 int omc_ws_ensure(const omc_layer *L, int T, int host_io) {
     const size_t Tz = (size_t)T;
     int rc = ws_ensure_in(L, Tz, Tz * (size_t)L->dev.k, L->dev.has_shared ? Tz : 0, host_io, &G.ws, &G.ws_ptrs,

@@ -284,6 +284,10 @@ int omc_launch_router_fast(const omc_layer_dev *L, const float *x, int T, const 
 extern int omc_router_exact;
 /* test hook: 1 = every token of a bounded pass is retried whole */
 extern int omc_rf_force_retry;
+/* fused decode: 1 = stream once the logit intervals decide the top-k sets */
+extern int omc_decode_early;
+/* decode state words: forwards the intervals decided, forwards that waited */
+#define OMC_DEC_CTR_STATS 4
 /* dst = f16(src), n % 8 == 0 */
 int omc_launch_f32_to_f16(const float *src, long long n, uint16_t *dst, cudaStream_t s);
 int omc_noalloc_setup(int device);

@@ -115,3 +115,72 @@ def test_decode_refuses_large_T(gpu, oracle, decode):
     m = gpu.MoELayer.from_oracle_layer(next_layer_id(), L)
     with pytest.raises(Exception):
         m.forward(oracle.normal(80, (9, 128)))
+
+
+def _early_vs_waiting(gpu, m, x):
+    gpu.decode_stats(reset=True)
+    gpu.debug_decode_early(False)
+    try:
+        waited = m.forward(x)
+        st_wait = gpu.decode_stats(reset=True)
+    finally:
+        gpu.debug_decode_early(True)
+    early = m.forward(x)
+    st_early = gpu.decode_stats(reset=True)
+    return waited, early, st_wait, st_early
+
+
+@pytest.mark.parametrize("kind", ["olmoe", "qwen"])
+@pytest.mark.parametrize("T", [1, 2, 8])
+def test_early_start_is_bit_identical(gpu, oracle, decode, kind, T):
+    """The kernel streams as soon as the logit intervals decide every
+    token's top-k set; the exact chains and the selection finish beside the
+    stream and the combine takes the reference's weights and order from
+    them.  So the forward equals the one that waits for the selection, bit
+    for bit, and the oracle's routing."""
+    L = olmoe_full() if kind == "olmoe" else qwen_full()
+    m = gpu.MoELayer.from_oracle_layer(next_layer_id(), L)
+    x = oracle.normal(8400 + T, (T, L.D))
+    (wo, wi, ww), (eo, ei, ew), st_wait, st_early = _early_vs_waiting(gpu, m, x)
+    assert st_wait == {"early": 0, "waited": 1}, st_wait
+    assert st_early["early"] + st_early["waited"] == 1, st_early
+    assert np.array_equal(ei, wi)
+    assert np.array_equal(ew.view(np.uint32), ww.view(np.uint32))
+    assert np.array_equal(eo.view(np.uint32), wo.view(np.uint32))
+    ro, ridx, rw = oracle.oracle_moe(L, x)
+    assert np.array_equal(ei, ridx)
+    assert np.array_equal(ew.view(np.uint32), rw.view(np.uint32))
+    assert_close(eo, ro, what=f"{kind} early decode T={T}")
+
+
+def test_early_start_decides_most_tokens(gpu, oracle, decode):
+    """Ordinary inputs: the intervals decide the set in nearly every forward."""
+    L = olmoe_full()
+    m = gpu.MoELayer.from_oracle_layer(next_layer_id(), L)
+    gpu.decode_stats(reset=True)
+    for i in range(40):
+        m.forward(oracle.normal(8500 + i, (1, L.D)))
+    st = gpu.decode_stats(reset=True)
+    assert st["early"] + st["waited"] == 40, st
+    assert st["early"] >= 36, st
+
+
+def test_tied_rows_wait_for_the_selection(gpu, oracle, decode):
+    """Router rows 8.. duplicate rows 0..: every expert is tied with another,
+    so whenever a tied pair straddles the k-th place the intervals cannot
+    decide and the kernel waits for the exact selection (lower id first).
+    Routing equals the oracle's either way."""
+    L = oracle.make_layer(oracle.FAMILY_OLMOE, 256, 64, 16, 5, seed=41)
+    r = L.arrays["router"]
+    r[8:] = r[:8]
+    m = gpu.MoELayer.from_oracle_layer(next_layer_id(), L)
+    gpu.decode_stats(reset=True)
+    for i in range(12):
+        x = oracle.normal(8600 + i, (1, 256))
+        out, idx, w = m.forward(x)
+        ro, ridx, rw = oracle.oracle_moe(L, x)
+        assert np.array_equal(idx, ridx)
+        assert np.array_equal(w.view(np.uint32), rw.view(np.uint32))
+        assert_close(out, ro, what=f"tied rows decode {i}")
+    st = gpu.decode_stats(reset=True)
+    assert st["waited"] == 12, st      # k = 5 is odd: a tied pair always straddles it
