@@ -111,7 +111,9 @@ struct DecArgs {
     int ns;               // ring stages (the reserved router slots follow them)
     int ldx;              // smem stride of a token row of x (floats)
     int rr, nrc;          // router rows per router CTA, router CTAs
-    int nres;             // reserved slots: router rows (+ Gemma's router input), select scratch
+    int rres;             // bytes reserved after the ring for the router rows (+ Gemma's router
+                          // input); 0: they are staged in the ring and the sets wait for the
+                          // exact selection (the ring is free only after it)
     float2 *rbnd;         // [T][E] interval of each routed logit (bias included)
     int bnw;              // warps per interval team
     int early;            // 1: stream as soon as the intervals decide every token's set
@@ -319,12 +321,13 @@ __global__ void __launch_bounds__(DC_THREADS, 1) decode_moe_kernel(const DecArgs
     // dynamic shared memory: ring | x [T][ldx] | h tiles [HB][T][128] |
     // chunk partials [T][4][256] | own piece [T][256] | expert table | barriers
     uint8_t *ring = dsm;
-    float *xs = reinterpret_cast<float *>(dsm + (size_t)(a.ns + a.nres) * DC_BLK);
+    float *xs = reinterpret_cast<float *>(dsm + (size_t)a.ns * DC_BLK + a.rres);
     float *hsm = xs + (size_t)T * a.ldx;
     float *xch = hsm + (size_t)DC_HB * T * OMC_TM;
     float *xown = xch + (size_t)T * DC_NCH * DC_ROWS;
+    float *selscr = xown + (size_t)T * DC_ROWS;                                // the select warp's scratch
     // every expert's matrices and scales (g, d, gs, us, ds), copied while the router runs
-    const void **ptab = reinterpret_cast<const void **>(xown + (size_t)T * DC_ROWS);
+    const void **ptab = reinterpret_cast<const void **>(selscr + (size_t)NV * 32);
     uint64_t *full = reinterpret_cast<uint64_t *>(ptab + dc_ptab_words(E));
     uint64_t *empty = full + a.ns, *rbar = empty + a.ns, *hfull = rbar + DC_RCH, *hempty = hfull + DC_HB;
     // the routing and the plan
@@ -367,13 +370,14 @@ __global__ void __launch_bounds__(DC_THREADS, 1) decode_moe_kernel(const DecArgs
     }
     // ---- 1. x (every CTA) and the router rows (router CTAs) ---------------
     // A router CTA stages its rows (and, for Gemma, the token rows it scales
-    // into the router's input) in the reserved slots after the ring: its
+    // into the router's input) in the reserved bytes after the ring: its
     // chains run on there while the ring streams the experts' weights.
+    // Without the reserve they go into the ring, which then streams only
+    // after every chain is done (the sets wait for the exact selection).
     const int rr = a.rr, r0 = c * rr, ldw = a.ldx, nrows = E + hsh;
     const bool gemma = L.family == OMC_FAMILY_GEMMA;
-    float *rws = reinterpret_cast<float *>(ring + (size_t)a.ns * DC_BLK);     // [rr][ldw] router rows
+    float *rws = reinterpret_cast<float *>(ring + (a.rres ? (size_t)a.ns * DC_BLK : 0));   // [rr][ldw] router rows
     float *rxs = gemma ? rws + (size_t)rr * ldw : xs;                          // [T][ldw] the router's input
-    float *selscr = rws + (size_t)(rr + (gemma ? T : 0)) * ldw;                // the select warp's scratch
     if (router && tid == 0) {   // (the barriers above are this thread's own: no sync needed)
         const int cw = D / DC_RCH, nr = min(rr, nrows - r0);
         for (int ch = 0; ch < DC_RCH; ++ch) {
@@ -600,7 +604,7 @@ __global__ void __launch_bounds__(DC_THREADS, 1) decode_moe_kernel(const DecArgs
         if (lane == 0) s_det[warp] = nc == K;
     }
     main_bar();
-    bool early = a.early != 0;
+    bool early = a.early != 0 && a.rres != 0;
     for (int t = 0; t < T; ++t) early = early && s_det[t] != 0;
     if (c == 0 && tid == 0 && !s_abort) atomicAdd(ctr + (early ? CTR_NEARLY : CTR_NFALL), 1);
     if (!s_abort && !early) {
@@ -988,7 +992,7 @@ __global__ void __launch_bounds__(DC_THREADS, 1) decode_moe_kernel(const DecArgs
 }
 
 struct DecGeom {
-    int G, ns, nres, ldx, rr, nrc, bnw;
+    int G, ns, rres, ldx, rr, nrc, bnw;
     int offSA, offSB, offC, nctr;
     size_t smem, partA_floats, partB_floats, rbnd_floats;
 };
@@ -1001,6 +1005,7 @@ static int dec_nv(int E) {
 }
 
 constexpr size_t DC_SMEM_MAX = 216 * 1024;   // dynamic; the static plan needs the rest of 227 KiB
+constexpr int DC_NS_EARLY = 4;                // ring stages left beside the reserved router rows
 
 // Everything about a launch that follows from the shapes (not the routing):
 // for T tokens, the worst case over routings.
@@ -1016,18 +1021,25 @@ static int dec_geometry(const omc_layer_dev *L, int T, int G, DecGeom *g) {
     g->nrc = (nrows + g->rr - 1) / g->rr;
     if (T * g->rr > 32 || (L->D % 32)) return OMC_EUNSUPPORTED;   // chains: one select-warp lane each
     const size_t fixed = (size_t)T * g->ldx * 4 + (size_t)DC_HB * T * OMC_TM * 4 +
-                         (size_t)T * DC_NCH * DC_ROWS * 4 + (size_t)T * DC_ROWS * 4 + (size_t)dc_ptab_words(L->E) * 8 +
-                         (DC_RCH + 2 * DC_HB) * 8;
-    // reserved slots after the ring: the router rows, Gemma's router input,
-    // the select warp's scratch
-    const size_t rbytes = ((size_t)g->rr + (L->family == OMC_FAMILY_GEMMA ? T : 0)) * g->ldx * 4 +
-                          (size_t)dec_nv(L->E) * 32 * 4;
-    g->nres = (int)((rbytes + DC_BLK - 1) / DC_BLK);
-    if (fixed + (size_t)g->nres * DC_BLK + 4 * ((size_t)DC_BLK + 16) > DC_SMEM_MAX) return OMC_EUNSUPPORTED;
-    int ns = (int)((DC_SMEM_MAX - fixed - (size_t)g->nres * DC_BLK) / (DC_BLK + 16));
+                         (size_t)T * DC_NCH * DC_ROWS * 4 + (size_t)T * DC_ROWS * 4 + (size_t)dec_nv(L->E) * 32 * 4 +
+                         (size_t)dc_ptab_words(L->E) * 8 + (DC_RCH + 2 * DC_HB) * 8;
+    // reserved bytes after the ring: the router rows and Gemma's router input
+    // (1 KiB granules), when a ring of at least DC_NS_EARLY stages remains;
+    // otherwise the rows go into the ring
+    const size_t rbytes = (((size_t)g->rr + (L->family == OMC_FAMILY_GEMMA ? T : 0)) * g->ldx * 4 + 1023) & ~(size_t)1023;
+    if (fixed + 4 * ((size_t)DC_BLK + 16) > DC_SMEM_MAX) return OMC_EUNSUPPORTED;
+    int ns;
+    if (fixed + rbytes + DC_NS_EARLY * ((size_t)DC_BLK + 16) <= DC_SMEM_MAX) {
+        g->rres = (int)rbytes;
+        ns = (int)((DC_SMEM_MAX - fixed - rbytes) / (DC_BLK + 16));
+    } else {
+        g->rres = 0;
+        ns = (int)((DC_SMEM_MAX - fixed) / (DC_BLK + 16));
+        if (rbytes > (size_t)ns * DC_BLK) return OMC_EUNSUPPORTED;
+    }
     if (ns > 12) ns = 12;
     g->ns = ns;
-    g->smem = (size_t)(ns + g->nres) * DC_BLK + fixed + (size_t)2 * ns * 8;
+    g->smem = (size_t)ns * DC_BLK + g->rres + fixed + (size_t)2 * ns * 8;
     // interval teams: DC_BW warps split over the T * rr (token, row) pairs
     int p2 = 1;
     while (p2 < T * g->rr) p2 *= 2;
@@ -1137,7 +1149,7 @@ extern "C" int omc_launch_decode(const omc_layer_dev *L, const float *x, const f
     a.offC = g.offC;
     a.err = ws->err;
     a.ns = g.ns;
-    a.nres = g.nres;
+    a.rres = g.rres;
     a.ldx = g.ldx;
     a.rr = g.rr;
     a.nrc = g.nrc;
