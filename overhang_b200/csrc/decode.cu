@@ -377,12 +377,17 @@ __global__ void __launch_bounds__(DC_THREADS, 1) decode_moe_kernel(const DecArgs
     const int rr = a.rr, r0 = c * rr, ldw = a.ldx, nrows = E + hsh;
     const bool gemma = L.family == OMC_FAMILY_GEMMA;
     float *rws = reinterpret_cast<float *>(ring + (a.rres ? (size_t)a.ns * DC_BLK : 0));   // [rr][ldw] router rows
-    float *rxs = gemma ? rws + (size_t)rr * ldw : xs;                          // [T][ldw] the router's input
+    // Gemma: the router's input is (x*r)*router scale, the experts' (x*r)*
+    // pre_feedforward_layernorm_2.  With the reserve the router's has its own
+    // copy; without it the router CTAs scale xs for the router and rebuild the
+    // experts' input once every chain is done (before the ring streams).
+    const bool gx = gemma && a.rres != 0, gx_late = gemma && !a.rres && router;
+    float *rxs = gx ? rws + (size_t)rr * ldw : xs;                             // [T][ldw] the router's input
     if (router && tid == 0) {   // (the barriers above are this thread's own: no sync needed)
         const int cw = D / DC_RCH, nr = min(rr, nrows - r0);
         for (int ch = 0; ch < DC_RCH; ++ch) {
-            mbar_arrive_expect_tx(&rbar[ch], (uint32_t)(((gemma ? T : 0) + nr) * cw * 4));
-            if (gemma)
+            mbar_arrive_expect_tx(&rbar[ch], (uint32_t)(((gx ? T : 0) + nr) * cw * 4));
+            if (gx)
                 for (int t = 0; t < T; ++t)
                     bulk_g2s(rxs + (size_t)t * ldw + ch * cw, a.x + (size_t)t * D + ch * cw, cw * 4, &rbar[ch]);
             for (int r = 0; r < nr; ++r) {
@@ -423,7 +428,7 @@ __global__ void __launch_bounds__(DC_THREADS, 1) decode_moe_kernel(const DecArgs
             if (lane == 0) s_r[warp] = r;
         }
         __syncthreads();
-        if (router) {
+        if (gx && router) {
             for (int ch = 0; ch < DC_RCH; ++ch) mbar_wait(&rbar[ch], 0, a.err, OMC_SITE_DECODE);
             for (int i = tid; i < T * D; i += DC_THREADS) {
                 const int t = i / D, col = i - t * D;
@@ -434,7 +439,7 @@ __global__ void __launch_bounds__(DC_THREADS, 1) decode_moe_kernel(const DecArgs
         for (int i = tid; i < T * D; i += DC_THREADS) {
             const int t = i / D, col = i - t * D;
             float *v = xs + (size_t)t * a.ldx + col;
-            *v = __fmul_rn(__fmul_rn(*v, s_r[t]), L.g_en ? L.g_en[col] : 1.f);
+            *v = __fmul_rn(__fmul_rn(*v, s_r[t]), gx_late ? L.g_s2[col] : (L.g_en ? L.g_en[col] : 1.f));
         }
         __syncthreads();
     }
@@ -610,6 +615,14 @@ __global__ void __launch_bounds__(DC_THREADS, 1) decode_moe_kernel(const DecArgs
     if (!s_abort && !early) {
         if (tid == 0 && !wait_value(ctr + CTR_ROUTER, a.nrc, a.err, -1)) s_abort = 1;
         main_bar();
+        if (gx_late) {   // every chain is done: the experts' input from the residual rows
+            for (int i = tid; i < T * D; i += DC_MT) {
+                const int t = i / D, col = i - t * D;
+                xs[(size_t)t * a.ldx + col] =
+                    __fmul_rn(__fmul_rn(__ldg(a.x + (size_t)t * D + col), s_r[t]), L.g_en ? L.g_en[col] : 1.f);
+            }
+            main_bar();
+        }
         if (!s_abort && warp < T)
             select_token<NV>(a.logits, a.ldl, warp, E, K, L.family, L.renorm, L.has_shared, L.g_pes, L.rbias, s_tidx,
                              s_tw, s_sg, a.err, reinterpret_cast<float *>(ring) + warp * NV * 32);
@@ -1026,16 +1039,17 @@ static int dec_geometry(const omc_layer_dev *L, int T, int G, DecGeom *g) {
     // reserved bytes after the ring: the router rows and Gemma's router input
     // (1 KiB granules), when a ring of at least DC_NS_EARLY stages remains;
     // otherwise the rows go into the ring
-    const size_t rbytes = (((size_t)g->rr + (L->family == OMC_FAMILY_GEMMA ? T : 0)) * g->ldx * 4 + 1023) & ~(size_t)1023;
+    const size_t rows = (size_t)g->rr * g->ldx * 4;
+    const size_t rbytes = (rows + (L->family == OMC_FAMILY_GEMMA ? (size_t)T * g->ldx * 4 : 0) + 1023) & ~(size_t)1023;
     if (fixed + 4 * ((size_t)DC_BLK + 16) > DC_SMEM_MAX) return OMC_EUNSUPPORTED;
     int ns;
     if (fixed + rbytes + DC_NS_EARLY * ((size_t)DC_BLK + 16) <= DC_SMEM_MAX) {
         g->rres = (int)rbytes;
         ns = (int)((DC_SMEM_MAX - fixed - rbytes) / (DC_BLK + 16));
-    } else {
+    } else {   // the rows in the ring (Gemma's router input in xs)
         g->rres = 0;
         ns = (int)((DC_SMEM_MAX - fixed) / (DC_BLK + 16));
-        if (rbytes > (size_t)ns * DC_BLK) return OMC_EUNSUPPORTED;
+        if (rows > (size_t)ns * DC_BLK) return OMC_EUNSUPPORTED;
     }
     if (ns > 12) ns = 12;
     g->ns = ns;
