@@ -565,18 +565,21 @@ __global__ void __launch_bounds__(DC_THREADS, 1) decode_moe_kernel(const DecArgs
                 s_bp[warp] = pab;
             }
             main_bar();
-            if (act && wq == 0 && lane == 0 && gr < E) {
-                double B = 0.0, cs = 0.0;
-                float P = 0.f;
-                for (int w2 = team * nw; w2 < team * nw + nw; ++w2) {
-                    B = __dadd_ru(B, s_bb[w2]);
-                    P = __fadd_ru(P, s_bp[w2]);
-                    cs = __dadd_rn(cs, s_bt[w2]);
+            if (act && wq == 0) {   // the team's first warp: the team's sums (lane w: warp w)
+                const int w2 = team * nw + lane;
+                double B = lane < nw ? s_bb[w2] : 0.0, cs = lane < nw ? s_bt[w2] : 0.0;
+                float P = lane < nw ? s_bp[w2] : 0.f;
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) {
+                    B = __dadd_ru(B, __shfl_xor_sync(0xffffffffu, B, o));
+                    P = __fadd_ru(P, __shfl_xor_sync(0xffffffffu, P, o));
+                    cs = __dadd_rn(cs, __shfl_xor_sync(0xffffffffu, cs, o));
                 }
-                a.rbnd[(size_t)t * E + gr] = dec_interval(cs, B, P, D, L.router_i8 ? L.router_s + gr : nullptr,
-                                                          L.rbias ? L.rbias + gr : nullptr);
+                if (lane == 0 && gr < E)
+                    a.rbnd[(size_t)t * E + gr] = dec_interval(cs, B, P, D, L.router_i8 ? L.router_s + gr : nullptr,
+                                                              L.rbias ? L.rbias + gr : nullptr);
             }
-            main_bar();   // s_bt, s_bb are the next round's
+            main_bar();   // the intervals are written before the count; s_bt, s_bb are the next round's
         }
         if (tid == 0) {
             fence_acqrel_gpu();
@@ -633,8 +636,13 @@ __global__ void __launch_bounds__(DC_THREADS, 1) decode_moe_kernel(const DecArgs
         *(volatile int *)&s_planned = 1;   // s_tidx is final (the select warp maps onto it)
     }
 
+    // With one token and a decided set the groups are the set itself (the
+    // candidates, ascending): the weight producer starts at once and warp 1
+    // plans beside it for the other warps.
+    const bool fast = early && T == 1 && !s_abort;
+
     // ---- 3. plan (one warp): groups in ascending expert id ---------------------
-    if (warp == 0 && !s_abort) {
+    if (warp == 1 && !s_abort) {
         const int nw = (E + 31) >> 5;
         for (int i = lane; i < nw; i += 32) s_bits[i] = 0u;
         for (int g = lane; g < DC_GMAX; g += 32) s_gn[g] = 0;
@@ -702,11 +710,16 @@ __global__ void __launch_bounds__(DC_THREADS, 1) decode_moe_kernel(const DecArgs
             }
         }
     }
-    fence_proxy_async_smem();   // select scratch (generic) before bulk copies into the ring
-    main_bar();
+    if (!fast) {
+        fence_proxy_async_smem();   // select scratch (generic) before bulk copies into the ring
+        main_bar();
+    } else if (warp != 0) {
+        // (the fast path wrote nothing generic to the ring: no proxy fence)
+        asm volatile("bar.sync 3, %0;" ::"n"(DC_MT - 32) : "memory");   // the plan, for warps 1..17
+    }
 
     Lists W;
-    W.ngr = s_ngr;
+    W.ngr = fast ? K : s_ngr;
     W.ntr = L.I_rows / OMC_TM;
     W.nts = L.has_shared ? L.Is_rows / OMC_TM : 0;
     W.nkbA = D_pad / OMC_KB;
@@ -735,17 +748,23 @@ __global__ void __launch_bounds__(DC_THREADS, 1) decode_moe_kernel(const DecArgs
                 rp.next(a.ns);
                 ++seq;
             };
+            // group g's matrices: the plan's, or (fast path) group g < K is the
+            // set's g-th expert and group K the shared expert
+            auto mat = [&](int g, int which) -> const int8_t * {
+                if (!fast) return which ? s_dp[g] : s_gp[g];
+                return static_cast<const int8_t *>(ptab[5 * (g < K ? s_tidx[g] : E) + which]);
+            };
             if (a0b < a1b) {
                 int S = W.segA(a0b), kb = (int)(a0b - W.segA_start(S));
                 for (long long b = a0b; b < a1b; ++S, kb = 0) {
                     int g, mt;
                     W.decA(S, g, mt);
-                    const int8_t *base = s_gp[g] + (size_t)mt * W.nkbA * DC_BLK;
+                    const int8_t *base = mat(g, 0) + (size_t)mt * W.nkbA * DC_BLK;
                     for (; kb < W.nkbA && b < a1b; ++kb, ++b) produce(base + (size_t)kb * DC_BLK);
                 }
             }
             walk_B(W, b0b, b1b, [&](int, int g, int p, int kb, int nkb) {
-                produce(s_dp[g] + ((size_t)p * nkb + kb) * DC_BLK);
+                produce(mat(g, 1) + ((size_t)p * nkb + kb) * DC_BLK);
             });
         }
         __syncwarp();
