@@ -302,8 +302,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_gemm_kernel(const GemmArgs a)
     uint64_t *accempty = accfull + 2;                                 // [2] accumulator slot drained
     uint64_t *stgfull = accempty + 2;                                 // h staging written (phase 1)
     uint64_t *stgfree = stgfull + 1;                                  // h staging read by its bulk store
-    uint64_t *fullA = stgfree + 1;                                    // [SA] phase 2: token tile landed
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(fullA + SA);
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(stgfree + 1);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -327,7 +326,6 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_gemm_kernel(const GemmArgs a)
         }
         mbar_init(stgfull, NEPI);
         mbar_init(stgfree, 1);
-        for (int i = 0; i < SA; ++i) mbar_init(&fullA[i], 1);
         *abort_flag = 0;
         fence_barrier_init();
     }
@@ -344,7 +342,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_gemm_kernel(const GemmArgs a)
         if (lane == 0) {
             StageIter<PHASE> it;
             it.init(c, blockIdx.x, nitems, gridDim.x);
-            const uint64_t stream = l2_policy_evict_first(), keep = l2_policy_evict_last();
+            const uint64_t stream = l2_policy_evict_first();
             for (uint32_t i = 0; it.valid && !*abort_flag; ++i) {
                 const int si = i % SI;
                 if (!wait_or_abort(&emptyI[si], ((i / SI) & 1) ^ 1, a.err, OMC_SITE_GEMM_PRODUCER, abort_flag))
@@ -354,19 +352,6 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_gemm_kernel(const GemmArgs a)
                 mbar_arrive_expect_tx(&fullI[si], bytes);
                 bulk_g2s_hint(smem + OFF_I8 + si * 2 * W_BYTES, it.w + (size_t)it.kb * OMC_PAIR_STRIDE, bytes,
                               &fullI[si], stream);
-                if (PHASE == 2) {
-                    // the K block's token tile right behind its weights in the
-                    // SM's copy queue: the h rows n0.. of the AOL operand are
-                    // one contiguous span, already in the swizzled layout
-                    const int sa = i % SA;
-                    if (!wait_or_abort(&emptyA[sa], ((i / SA) & 1) ^ 1, a.err, OMC_SITE_GEMM_PRODUCER, abort_flag))
-                        break;
-                    const uint32_t tb = (uint32_t)it.n * 128u;
-                    mbar_arrive_expect_tx(&fullA[sa], tb);
-                    bulk_g2s_hint(smem + OFF_A + sa * A_BYTES,
-                                  reinterpret_cast<const uint8_t *>(a.act) + ((size_t)it.kb * a.R + it.n0) * 128, tb,
-                                  &fullA[sa], keep);
-                }
                 it.step(c);
             }
         }
@@ -396,8 +381,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_gemm_kernel(const GemmArgs a)
             const uint32_t d0 = tmem + acc.col(0), d1 = tmem + acc.col(1);
             for (int kb = 0; kb < nkb; ++kb, ++i) {
                 const int sa = i % SA, st = i % ST;
-                if (!warp_wait(&fullT[st], (i / ST) & 1, a.err, OMC_SITE_GEMM_MMA, abort_flag) ||
-                    (PHASE == 2 && !warp_wait(&fullA[sa], (i / SA) & 1, a.err, OMC_SITE_GEMM_MMA, abort_flag))) {
+                if (!warp_wait(&fullT[st], (i / ST) & 1, a.err, OMC_SITE_GEMM_MMA, abort_flag)) {
                     ok = false;
                     break;
                 }
@@ -448,9 +432,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_gemm_kernel(const GemmArgs a)
             // token tile of this K block: per-lane cp.async (not a bulk copy, which would queue
             // behind the int8 stream's in the SM's copy engine), issued first so that its L2
             // latency overlaps the int8 wait and the conversion
-            if (PHASE == 1 && !warp_wait(&emptyA[sa], ((i / SA) & 1) ^ 1, a.err, OMC_SITE_GEMM_DEQUANT, abort_flag))
-                break;
-            if (PHASE == 1) {
+            if (!warp_wait(&emptyA[sa], ((i / SA) & 1) ^ 1, a.err, OMC_SITE_GEMM_DEQUANT, abort_flag)) break;
+            {
                 uint8_t *dst = smem + OFF_A + sa * A_BYTES;
                 if (PHASE == 1) {
                     // gather: operand row j of the item is token xrow[j] of xh (its
@@ -482,6 +465,11 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_gemm_kernel(const GemmArgs a)
                         const uint8_t *src = live ? xcol + (size_t)xrow[u] * (size_t)L.D * 2 : xcol;
                         cp_async16_zfill_hint(dst + j * 128 + ((c ^ (j & 7)) << 4), src, live, keep);
                     }
+                } else {
+                    const uint8_t *src = reinterpret_cast<const uint8_t *>(a.act) + (size_t)pr.kb * a.R * 128 +
+                                         (size_t)pr.n0 * 128;
+                    for (int ch = gt; ch < pr.n * 8; ch += GTHREADS)
+                        cp_async16_hint(dst + ch * 16, src + ch * 16, keep);
                 }
                 cp_async_commit();
             }
